@@ -1,0 +1,452 @@
+#!/usr/bin/env python
+"""Benchmark of the Dressi-AD per-iteration hot path on B200.
+
+Metric: fwd + bwd + Adam iterations/s of the silhouette
+optimisation with HardSoftRas (config C3: icosphere-5 = 10242 v / 20480 f,
+16 seeded views, 1024^2, sigma 1e-4, Adam lr 1e-3), seeded synthetic inputs
+(no dataset). One process per GPU; the 16 views are sharded over the ranks
+(strong scaling) and the position gradient is all-reduced with NCCL before
+the replicated Adam step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line (rank 0). See DESIGN.md for the byte model of the
+roofline and the definition of the end-to-end (e2e) step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fwd+bwd+Adam iterations/sec"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--res", type=int, default=1024)
+    ap.add_argument("--views", type=int, default=16)
+    ap.add_argument("--level", type=int, default=5)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def workload(args):
+    return {
+        "workload": "C3 silhouette HardSoftRas fwd+bwd+Adam",
+        "mesh": f"icosphere-{args.level}",
+        "views": args.views,
+        "res": args.res,
+        "sigma": 1e-4,
+        "lr": 1e-3,
+    }
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# --------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,"
+         "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "50"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [],
+                    "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                 "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4)
+                          if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------- byte model (roofline)
+
+def algorithmic_bytes(name: str, views: int, res: int, n_verts: int,
+                      n_faces: int) -> float:
+    """Logically necessary HBM bytes of ONE launch of a kernel of the fused
+    iteration (each tensor counted once per producer/consumer boundary that
+    must exist; fused-away intermediates are not counted)."""
+    px = views * res * res
+    rec = 176  # face record bytes
+    return {
+        # survivor state write (depth, face, dist, hard_z) + face records
+        "sweep1": px * 16 + views * n_faces * rec,
+        # survivor state + target reads; loss/gradient epilogue
+        "sweep2_sil": px * (16 + 4) + views * n_faces * rec,
+        # vertex clip reads (3 per face) + face indices + record write
+        "face_setup": views * n_faces * (3 * 16 + 12 + rec),
+        "transform": n_verts * 12 + views * n_verts * 16,
+        # g_clip read + clear, pos/m/v read + write, g_pos write
+        "gpos_adam": n_verts * (views * 32 + 36 + 36 + 12),
+    }.get(name, 0.0)
+
+
+# ------------------------------------------------------------- GPU arm
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from opendressi_b200 import _native as N
+    from opendressi_b200 import scene
+    from opendressi_b200.plans import SilhouettePlan
+
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local}"))
+    N.load()
+
+    sc = scene.silhouette_scene(level=args.level, n_views=args.views,
+                                res=args.res, seed=args.seed)
+    shard = np.array_split(np.arange(args.views), world)[rank]
+    plan = SilhouettePlan.from_scene(sc, views=shard, device=local)
+    plan.upload(N.SLOT_PARAM, sc.pos0)
+    plan.render_targets(sc.target_pos)
+    stream = torch.cuda.current_stream()
+
+    if world > 1:
+        grad = plan.grad_tensor()
+        loss_t = plan.loss_tensor()
+
+    def step():
+        if world == 1:
+            plan.step(1)
+        else:
+            plan.forward_backward()
+            dist.all_reduce(grad)
+            plan.apply_update()
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    sync_all()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    sync_all()
+    ms = t0.elapsed_time(t1)
+    clk = clocks.stop()
+    ms_t = torch.tensor([ms], device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+
+    # loss of the last iteration (all ranks' views)
+    if world > 1:
+        dist.all_reduce(loss_t)
+    loss = float(plan.loss())
+
+    # ---- end to end through the public API with host buffers ----------
+    e2e = None
+    if not args.no_e2e:
+        pos_pin = torch.empty(sc.n_verts * 3, dtype=torch.float32,
+                              pin_memory=True)
+        plan.download(N.SLOT_PARAM, out=pos_pin.numpy())
+        loss_pin = torch.empty(1, dtype=torch.float32, pin_memory=True)
+        h = plan._h
+        nb = sc.n_verts * 3 * 4
+        sp = stream.cuda_stream
+
+        def e2e_step():
+            N.call("dressi_plan_upload", h, N.SLOT_PARAM, pos_pin.data_ptr(),
+                   nb, 0, sp)
+            step()
+            N.call("dressi_plan_download", h, N.SLOT_PARAM,
+                   pos_pin.data_ptr(), nb, 0, sp)
+            N.call("dressi_plan_download", h, N.SLOT_LOSS,
+                   loss_pin.data_ptr(), 4, 0, sp)
+            stream.synchronize()
+
+        for _ in range(min(args.warmup, 5)):
+            e2e_step()
+        sync_all()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        n_e2e = args.steps
+        e0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        e1.record(stream)
+        sync_all()
+        ems = torch.tensor([e0.elapsed_time(e1)], device=f"cuda:{local}")
+        if world > 1:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        e2e = {"value": n_e2e / (float(ems.item()) / 1e3),
+               "unit": "iterations/s", "h2d_bytes_per_step": nb,
+               "d2h_bytes_per_step": nb + 4}
+
+    # ---- per-kernel timing (CUDA events, un-graphed) for the roofline ---
+    prof = plan.profile(n_iters=10)
+    per_iter = {p["name"]: p for p in prof}
+    launches_per_iter = sum(p["launches"] for p in prof) / 10.0
+    dom = max(prof, key=lambda p: p["total_ms"])
+    nvw = len(shard)
+    alg = algorithmic_bytes(dom["name"], nvw, args.res, sc.n_verts,
+                            sc.n_faces)
+    peak, peak_kind = peaks()
+    achieved = alg / (dom["avg_ms"] * 1e-3) / 1e9 if alg else None
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            tr = json.load(f).get(f"{dom['name']}@{nvw}x{args.res}")
+        if tr:
+            traffic = tr
+    roofline = {
+        "bound": "hbm", "kernel": dom["name"],
+        "achieved": achieved, "peak": peak, "unit": "GB/s",
+        "frac": (achieved / peak) if achieved else None,
+        "peak_source": peak_kind, "traffic": traffic,
+        "alg_bytes_per_launch": alg, "avg_ms": dom["avg_ms"],
+        "kernels_ms_per_iter": {k: round(v["total_ms"] / 10.0, 4)
+                                for k, v in per_iter.items()},
+    }
+
+    status = plan.status()
+    out = None
+    if rank == 0:
+        value = args.steps / (ms_max / 1e3)
+        out = {
+            "metric": METRIC, "value": value, "unit": "iterations/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded icosphere + SH-displaced target, "
+                    "seeded cameras; no dataset)",
+            "config": dict(workload(args), parallelism=f"views/{world} "
+                           "(view-sharded, NCCL all-reduce of the position "
+                           "gradient, replicated Adam)",
+                           l2="per-iteration working set > L2 (per-pixel "
+                              "survivor state 16 B/px = "
+                              f"{nvw * args.res * args.res * 16 / 1e6:.0f} MB "
+                              "per rank)"),
+            "gpu_launches": int(round(launches_per_iter * args.steps)),
+            "loss_last": loss, "device_status": status,
+            "clocks": clk, "e2e": e2e, "roofline": roofline,
+        }
+    if world > 1:
+        plan.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
+# -------------------------------------------------------- CPU baselines
+
+def cpu_reference_rate(args, max_seconds=40.0, min_iters=1, max_iters=2):
+    """The reference CPU implementation (oracle/_ref, else the C port) on the
+    same workload, view-parallel on the host cores."""
+    from oracle import pyoracle
+    from opendressi_b200 import scene
+
+    sc = scene.silhouette_scene(level=args.level, n_views=args.views,
+                                res=args.res, seed=args.seed)
+    port = pyoracle.Port()
+    targets = np.stack([(port.rasterize_face_id(
+        port.transform_clip(sc.target_pos, m), sc.faces_f, sc.res, sc.res)
+        > 0).astype(np.float32) for m in sc.mvps])
+    threads = max(1, min(os.cpu_count() or 1, args.views))
+    if pyoracle.ref_available():
+        ref = pyoracle.Ref()
+        vft = ref.vertex_faces_tex(sc.faces_f, sc.n_verts)
+        kind = "reference"
+
+        def run(n):
+            t0 = time.perf_counter()
+            ref.silhouette_run(sc.pos0, sc.faces_f, vft, sc.mvps, targets,
+                               sc.res, sc.radius_px, sc.sigma, sc.lr, n,
+                               threads=threads)
+            return time.perf_counter() - t0
+    else:
+        kind = "port"
+
+        def run(n):
+            t0 = time.perf_counter()
+            port.silhouette_run(sc.pos0, sc.faces_f, sc.mvps, targets, sc.res,
+                                sc.radius_px, sc.sigma, sc.lr, n,
+                                threads=threads)
+            return time.perf_counter() - t0
+    secs = run(min_iters)
+    iters = min_iters
+    if secs * (max_iters / min_iters) < max_seconds and max_iters > min_iters:
+        secs = run(max_iters)
+        iters = max_iters
+    return {"value": iters / secs, "unit": "iterations/s", "cores": threads,
+            "kind": kind,
+            "sample": f"{iters} full iteration(s) of the bench workload "
+                      f"({args.views} views at {args.res}^2, icosphere-"
+                      f"{args.level}), view-parallel on {threads} host "
+                      f"threads, {secs:.1f} s"}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path on the host cores."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return None
+    from oracle import pyoracle
+    from opendressi_b200 import scene
+
+    sc = scene.silhouette_scene(level=args.level, n_views=args.views,
+                                res=args.res, seed=args.seed)
+    port = pyoracle.Port()
+    targets = np.stack([(port.rasterize_face_id(
+        port.transform_clip(sc.target_pos, m), sc.faces_f, sc.res, sc.res)
+        > 0).astype(np.float32) for m in sc.mvps])
+    threads = max(1, min(os.cpu_count() or 1, args.views))
+    use_ref = pyoracle.ref_available()
+    if use_ref:
+        ref = pyoracle.Ref()
+        vft = ref.vertex_faces_tex(sc.faces_f, sc.n_verts)
+    # Each step is one full view-parallel iteration; the run is capped at
+    # ~170 s of timed work (steps beyond it are not run; `sample` says so).
+    budget = 170.0
+    times = []
+    pos = sc.pos0.copy()
+    done_w = 0
+    t_start = time.perf_counter()
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        if use_ref:
+            _, pos, _, _ = ref.silhouette_run(
+                pos, sc.faces_f, vft, sc.mvps, targets, sc.res,
+                sc.radius_px, sc.sigma, sc.lr, 1, threads=threads)
+        else:
+            _, pos = port.silhouette_run(pos, sc.faces_f, sc.mvps, targets,
+                                         sc.res, sc.radius_px, sc.sigma,
+                                         sc.lr, 1, threads=threads)
+        dt = time.perf_counter() - t0
+        if i < args.warmup:
+            done_w += 1
+            if time.perf_counter() - t_start > budget / 4:
+                break
+            continue
+        times.append(dt)
+        if time.perf_counter() - t_start > budget:
+            break
+    if not times:
+        times.append(dt)
+    value = len(times) / sum(times)
+    kind = "reference" if use_ref else "port"
+    sample = (f"{len(times)} of {args.steps} requested steps timed (each one "
+              f"full iteration: {args.views} views at {args.res}^2, view-"
+              f"parallel on {threads} threads), {done_w} warm-up")
+    return {
+        "metric": METRIC, "value": value, "unit": "iterations/s",
+        "n_gpus": world, "steps": len(times), "warmup": done_w,
+        "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload(args), "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "iterations/s",
+                         "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "iterations/s",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse()
+    world, rank, _ = dist_env()
+    if args.impl == "reference":
+        out = run_reference(args)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
+    out = run_ours(args)
+    if rank == 0 and out is not None:
+        if world == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_reference_rate(args)
+        else:
+            out["cpu_baseline"] = None
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,214 @@
+/*
+ * dressi_b200.h -- C ABI of libdressi_b200.so, the B200 (sm_100a) device
+ * layer of the Dressi-AD per-iteration hot path.
+ *
+ * Conventions
+ *  - Plain C: pointers, sizes and an int status. 0 = success; on failure
+ *    dressi_last_error() returns the message (thread-local), mirroring the
+ *    reference's DressiError text (include/dressi/types.h:110-123).
+ *  - Images are row-major with interleaved components and no VEC3 padding
+ *    (the reference's CpuImage layout, include/dressi/types.h:72-88).
+ *    Index images ("faces") are float-valued as in the reference's leaves.
+ *  - Op-level entry points take DEVICE pointers and enqueue on `stream`
+ *    (a cudaStream_t passed as void*; NULL = legacy default stream). Their
+ *    scratch memory is allocated stream-ordered (cudaMallocAsync) and freed
+ *    on the same stream.
+ *  - Kernels never trap. A condition the reference reports by throwing
+ *    (index out of range) sets a bit in a device status word instead; read it
+ *    with dressi_plan_status() or the `status` argument of op-level calls
+ *    (a device uint32_t the caller zeroes).
+ *
+ * Reference interfaces replaced (paths inside unclearness/opendressi):
+ *  - DressiAD::execStep / sendImg / recvImg    include/dressi/dressi_ad.h:95-131
+ *  - BuildGpuPlan / ExecuteGpuPlan             src/vk/executor.h:43-66
+ *  - F::SoftClip                               include/dressi/f.h:236-242
+ *  - F::RasterizeSoft (+ peel variant)         include/dressi/f.h:131-160
+ *  - F::RasterizeFaceId / F::Rasterize         include/dressi/f.h:162-169, 116-118
+ *  - RasterizeSoft backward (ColSum(GatherDistGrad))
+ *                                              src/core/f_ops.cpp:1218-1358
+ *  - dressi.torch.rasterize_soft / rasterize   python/dressi/torch/ops.py:682, 118
+ */
+#ifndef DRESSI_B200_H
+#define DRESSI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DRESSI_B200_ABI_VERSION 1
+
+/* status codes */
+#define DRESSI_OK 0
+#define DRESSI_ERR_INVALID 1  /* bad argument / shape (DressiError)        */
+#define DRESSI_ERR_CUDA 2     /* CUDA runtime error                         */
+#define DRESSI_ERR_OOM 3      /* device allocation failed                   */
+#define DRESSI_ERR_DEVICE 4   /* device status word reported an error       */
+
+/* device status word bits */
+#define DRESSI_STATUS_INDEX_RANGE 0x1u  /* face/vertex index out of range   */
+#define DRESSI_STATUS_BIN_OVERFLOW 0x2u /* tile list capacity exceeded; the */
+                                        /* exact fallback sweep was used     */
+
+/* ABI version of the loaded library (DRESSI_B200_ABI_VERSION). */
+int dressi_abi_version(void);
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated
+ * to len). Returns its full length. */
+int dressi_last_error(char* buf, size_t len);
+
+/* ------------------------------------------------------------------------
+ * Op-level entry points (device pointers)
+ * --------------------------------------------------------------------- */
+
+/* F::SoftClip (reference src/core/f_ops.cpp:1890-1981) for `views` stacked
+ * clip images: clip [views][n_verts][4], faces [n_faces][3] (shared),
+ * out [views][3*n_faces][4]. */
+int dressi_soft_clip(const float* clip, uint32_t n_verts, const float* faces,
+                     uint32_t n_faces, uint32_t views, uint32_t width,
+                     uint32_t height, float radius_px, float* out,
+                     uint32_t* status, void* stream);
+
+/* F::RasterizeSoft (reference src/core/cpu_raster.cpp:241-355), bit-exact.
+ *   soft_clip  [views][n_soft][4]   face_id [views][n_soft]
+ *   faces_soft [n_faces][3]         hard_clip [views][n_hard][4]
+ *   faces_tex  [n_faces][3]         prev_depth [views][H][W] or NULL
+ *   out        [views][H][W][4] = (signed_dist_px, face_id, hard_z, coverage)
+ * prev_depth != NULL selects the depth-peeling variant (f.h:149-160). */
+int dressi_rasterize_soft(const float* soft_clip, uint32_t n_soft,
+                          const float* face_id, const float* faces_soft,
+                          uint32_t n_faces, const float* hard_clip,
+                          uint32_t n_hard, const float* faces_tex,
+                          uint32_t views, uint32_t width, uint32_t height,
+                          float radius_px, const float* prev_depth,
+                          float* out, uint32_t* status, void* stream);
+
+/* RasterizeSoft's dist-channel backward, ColSum(GatherDistGrad(...))
+ * (reference src/core/f_ops.cpp:1248-1358): ADDS to grad [views][n_verts][4]
+ * the gradient of sum_px gy(px) * dist(px) w.r.t. the hard clip positions.
+ * gy [views][H][W] (the dist channel's incoming gradient), rs the forward
+ * output [views][H][W][4], clip [views][n_verts][4], faces [n_faces][3]. */
+int dressi_rasterize_soft_grad(const float* gy, const float* rs,
+                               const float* clip, uint32_t n_verts,
+                               const float* faces, uint32_t n_faces,
+                               uint32_t views, uint32_t width,
+                               uint32_t height, float* grad, uint32_t* status,
+                               void* stream);
+
+/* F::RasterizeFaceId (cpu_raster.cpp:357-369), bit-exact: out [views][H][W]
+ * = float(face)+1, 0 = background. depth_out (nullable) [views][H][W] gets
+ * the survivor's NDC depth (1 = background). */
+int dressi_rasterize_face_id(const float* clip, uint32_t n_verts,
+                             const float* faces, uint32_t n_faces,
+                             uint32_t views, uint32_t width, uint32_t height,
+                             float* out, float* depth_out, uint32_t* status,
+                             void* stream);
+
+/* F::Rasterize (cpu_raster.cpp:195-225), bit-exact: perspective-correct
+ * interpolation of attr [views][n_verts][n_comp] (n_comp 1..4);
+ * out [views][H][W][n_comp]; background 0. */
+int dressi_rasterize(const float* clip, uint32_t n_verts, const float* attr,
+                     uint32_t n_comp, const float* faces, uint32_t n_faces,
+                     uint32_t views, uint32_t width, uint32_t height,
+                     float* out, uint32_t* status, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Plans: one fused fwd + bwd + Adam iteration, resident on one device,
+ * replayed as a CUDA graph with no per-iteration host traffic
+ * (the reference's one pre-recorded command buffer per execStep,
+ * src/vk/executor.cpp:42-907, :1020-1026).
+ * --------------------------------------------------------------------- */
+
+typedef struct dressi_plan_s* dressi_plan;
+
+/* Buffer slots of a plan (upload / download / buffer address). */
+enum {
+    DRESSI_SLOT_PARAM = 0,   /* optimised parameter (pos [V][3] / image)   */
+    DRESSI_SLOT_ADAM_M = 1,  /* Adam first moment (same shape)             */
+    DRESSI_SLOT_ADAM_V = 2,  /* Adam second moment                         */
+    DRESSI_SLOT_ADAM_T = 3,  /* Adam counter t (1 float)                   */
+    DRESSI_SLOT_TARGET = 4,  /* target images                              */
+    DRESSI_SLOT_GRAD = 5,    /* last gradient of the parameter             */
+    DRESSI_SLOT_LOSS = 6,    /* loss of the last iteration (1 float)       */
+    DRESSI_SLOT_LOSS_HISTORY = 7, /* ring of per-iteration losses          */
+    DRESSI_SLOT_RASTER = 8,  /* silhouette: RasterizeSoft images of the    */
+                             /* last dressi_plan_render() [views][R][R][4] */
+    DRESSI_SLOT_MVP = 9      /* silhouette: view matrices [views][16]      */
+};
+
+/* Silhouette optimisation (configs C3/C4): HardSoftRas with RasterizeSoft's
+ * exact dist-channel backward. Per view v: clip = MVP_v (pos, 1);
+ * rs = RasterizeSoft(SoftClip(clip)); pred = max(cov*step(0,d),
+ * cov*sigmoid(d*|d|*k)), k = (2/R)^2/sigma; loss = sum (target - pred)^2/R^2;
+ * Adam on pos. faces/mvps are host arrays copied at creation. */
+typedef struct {
+    uint32_t struct_size;  /* sizeof(dressi_silhouette_desc) */
+    uint32_t n_verts, n_faces, n_views, res;
+    float radius_px, sigma, lr, beta1, beta2, eps;
+    const float* faces;    /* host [n_faces][3] */
+    const float* mvps;     /* host [n_views][16], column-major */
+    uint32_t loss_history; /* ring capacity (0 -> 4096) */
+    int device;            /* CUDA device ordinal */
+} dressi_silhouette_desc;
+
+int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
+                                  dressi_plan* out);
+
+/* 2-D image fitting (config C1): loss = Mean((param - target)^2) over a
+ * [h][w][4] image, Adam(lr, 0.9, 0.999, 1e-8) on param. */
+int dressi_image_fit_plan_create(uint32_t width, uint32_t height, float lr,
+                                 int device, dressi_plan* out);
+
+/* Host (or device, if src_is_device) -> slot copy on `stream`; `bytes` must
+ * equal the slot size (sizes in dressi_plan_slot_bytes). */
+int dressi_plan_upload(dressi_plan p, int slot, const void* src, size_t bytes,
+                       int src_is_device, void* stream);
+int dressi_plan_download(dressi_plan p, int slot, void* dst, size_t bytes,
+                         int dst_is_device, void* stream);
+int dressi_plan_slot_bytes(dressi_plan p, int slot, size_t* bytes);
+/* Device address of a slot (for zero-copy wrapping by bindings). */
+int dressi_plan_slot_ptr(dressi_plan p, int slot, void** ptr);
+
+/* Silhouette only: renders the hard silhouettes of target_pos (host
+ * [n_verts][3]) into the TARGET slot (setup, not part of the iteration). */
+int dressi_plan_render_targets(dressi_plan p, const float* target_pos_host,
+                               void* stream);
+
+/* Runs n_iters full iterations on `stream` (CUDA-graph replays; the graph
+ * is instantiated on first use). */
+int dressi_plan_exec(dressi_plan p, uint32_t n_iters, void* stream);
+
+/* Multi-device split of one iteration (view-sharded data parallelism):
+ *  phase 0: forward + backward, leaves the local gradient in the GRAD slot;
+ *  phase 1: Adam from the GRAD slot (after the caller all-reduced it). */
+int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream);
+
+/* Silhouette only: forward pass writing the RASTER slot (no update). */
+int dressi_plan_render(dressi_plan p, void* stream);
+
+/* Synchronises `stream`, returns the plan's device status word. */
+int dressi_plan_status(dressi_plan p, uint32_t* word, void* stream);
+
+/* Kernel launches one dressi_plan_exec iteration enqueues. */
+int dressi_plan_launches_per_iter(dressi_plan p, uint32_t* n);
+
+/* Debug timing outside the CUDA graph: runs n_iters iterations launching
+ * every kernel directly, each bracketed by a pair of CUDA events on
+ * `stream`. Fills up to max_kernels entries (one per distinct kernel, in
+ * launch order): names[i] (static strings owned by the library),
+ * total_ms[i] summed over its launches, launches[i]; *n_kernels = number of
+ * distinct kernels. Any output array may be NULL. */
+int dressi_plan_profile(dressi_plan p, uint32_t n_iters, void* stream,
+                        uint32_t max_kernels, const char** names,
+                        float* total_ms, uint32_t* launches,
+                        uint32_t* n_kernels);
+
+int dressi_plan_destroy(dressi_plan p);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DRESSI_B200_H */

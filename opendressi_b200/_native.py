@@ -1,0 +1,137 @@
+"""ctypes binding of libdressi_b200.so (include/dressi_b200.h).
+
+The library is built in-tree by ``opendressi_b200.build``; this module never
+falls back to anything else -- if the shared library is missing or fails to
+load, every entry point raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdressi_b200.so")
+
+ABI_VERSION = 1
+
+OK, ERR_INVALID, ERR_CUDA, ERR_OOM, ERR_DEVICE = 0, 1, 2, 3, 4
+STATUS_INDEX_RANGE = 0x1
+STATUS_BIN_OVERFLOW = 0x2
+
+SLOT_PARAM, SLOT_ADAM_M, SLOT_ADAM_V, SLOT_ADAM_T = 0, 1, 2, 3
+SLOT_TARGET, SLOT_GRAD, SLOT_LOSS, SLOT_LOSS_HISTORY = 4, 5, 6, 7
+SLOT_RASTER, SLOT_MVP = 8, 9
+
+_fp = C.POINTER(C.c_float)
+_u32 = C.c_uint32
+_vp = C.c_void_p
+
+
+class SilhouetteDesc(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("n_verts", C.c_uint32), ("n_faces", C.c_uint32),
+        ("n_views", C.c_uint32), ("res", C.c_uint32),
+        ("radius_px", C.c_float), ("sigma", C.c_float), ("lr", C.c_float),
+        ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float),
+        ("faces", _fp), ("mvps", _fp),
+        ("loss_history", C.c_uint32),
+        ("device", C.c_int),
+    ]
+
+
+# name -> (restype, argtypes); exactly the functions include/dressi_b200.h
+# declares.
+SIGNATURES = {
+    "dressi_abi_version": (C.c_int, []),
+    "dressi_last_error": (C.c_int, [C.c_char_p, C.c_size_t]),
+    "dressi_soft_clip": (C.c_int, [_vp, _u32, _vp, _u32, _u32, _u32, _u32,
+                                   C.c_float, _vp, _vp, _vp]),
+    "dressi_rasterize_soft": (C.c_int, [_vp, _u32, _vp, _vp, _u32, _vp, _u32,
+                                        _vp, _u32, _u32, _u32, C.c_float, _vp,
+                                        _vp, _vp, _vp]),
+    "dressi_rasterize_soft_grad": (C.c_int, [_vp, _vp, _vp, _u32, _vp, _u32,
+                                             _u32, _u32, _u32, _vp, _vp,
+                                             _vp]),
+    "dressi_rasterize_face_id": (C.c_int, [_vp, _u32, _vp, _u32, _u32, _u32,
+                                           _u32, _vp, _vp, _vp, _vp]),
+    "dressi_rasterize": (C.c_int, [_vp, _u32, _vp, _u32, _vp, _u32, _u32,
+                                   _u32, _u32, _vp, _vp, _vp]),
+    "dressi_silhouette_plan_create": (C.c_int, [C.POINTER(SilhouetteDesc),
+                                                C.POINTER(_vp)]),
+    "dressi_image_fit_plan_create": (C.c_int, [_u32, _u32, C.c_float, C.c_int,
+                                               C.POINTER(_vp)]),
+    "dressi_plan_upload": (C.c_int, [_vp, C.c_int, _vp, C.c_size_t, C.c_int,
+                                     _vp]),
+    "dressi_plan_download": (C.c_int, [_vp, C.c_int, _vp, C.c_size_t,
+                                       C.c_int, _vp]),
+    "dressi_plan_slot_bytes": (C.c_int, [_vp, C.c_int,
+                                         C.POINTER(C.c_size_t)]),
+    "dressi_plan_slot_ptr": (C.c_int, [_vp, C.c_int, C.POINTER(_vp)]),
+    "dressi_plan_render_targets": (C.c_int, [_vp, _fp, _vp]),
+    "dressi_plan_exec": (C.c_int, [_vp, _u32, _vp]),
+    "dressi_plan_exec_phase": (C.c_int, [_vp, C.c_int, _vp]),
+    "dressi_plan_render": (C.c_int, [_vp, _vp]),
+    "dressi_plan_status": (C.c_int, [_vp, C.POINTER(_u32), _vp]),
+    "dressi_plan_launches_per_iter": (C.c_int, [_vp, C.POINTER(_u32)]),
+    "dressi_plan_profile": (C.c_int, [_vp, _u32, _vp, _u32,
+                                      C.POINTER(C.c_char_p), _fp,
+                                      C.POINTER(_u32), C.POINTER(_u32)]),
+    "dressi_plan_destroy": (C.c_int, [_vp]),
+}
+
+
+class DressiError(RuntimeError):
+    """Error reported by libdressi_b200 (the reference's DressiError)."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg)
+        self.code = code
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load(path: str | None = None) -> C.CDLL:
+    """Loads (once) and returns the shared library; raises if absent."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise DressiError(
+                ERR_INVALID,
+                f"{p} is missing: build it with `python -m opendressi_b200."
+                "build` (there is no fallback implementation)")
+        lib = C.CDLL(p)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        ver = lib.dressi_abi_version()
+        if ver != ABI_VERSION:
+            raise DressiError(ERR_INVALID,
+                              f"ABI version {ver} != expected {ABI_VERSION}")
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    lib = load()
+    buf = C.create_string_buffer(4096)
+    lib.dressi_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != OK:
+        raise DressiError(rc, f"{what}: {last_error()}" if what
+                          else last_error())
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args), name)

@@ -1,0 +1,627 @@
+// C ABI of libdressi_b200.so (include/dressi_b200.h): argument checking,
+// device scratch, plan objects and their CUDA-graph replay.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/dressi_b200.h"
+#include "kernels.h"
+
+namespace dressi {
+
+static thread_local std::string g_last_error;
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+
+KernelProfiler*& current_profiler() {
+    static thread_local KernelProfiler* p = nullptr;
+    return p;
+}
+
+void KernelProfiler::begin(const char* name, cudaStream_t s) {
+    Rec r{name, nullptr, nullptr};
+    DRESSI_CUDA(cudaEventCreate(&r.a));
+    DRESSI_CUDA(cudaEventCreate(&r.b));
+    DRESSI_CUDA(cudaEventRecord(r.a, s));
+    recs.push_back(r);
+}
+
+void KernelProfiler::end(cudaStream_t s) {
+    if (!recs.empty()) cudaEventRecord(recs.back().b, s);
+}
+
+void KernelProfiler::collect(std::vector<const char*>* names,
+                             std::vector<double>* ms, std::vector<int>* count) {
+    for (auto& r : recs) {
+        DRESSI_CUDA(cudaEventSynchronize(r.b));
+        float t = 0.f;
+        DRESSI_CUDA(cudaEventElapsedTime(&t, r.a, r.b));
+        size_t i = 0;
+        while (i < names->size() && std::strcmp((*names)[i], r.name) != 0) i++;
+        if (i == names->size()) {
+            names->push_back(r.name);
+            ms->push_back(0.0);
+            count->push_back(0);
+        }
+        (*ms)[i] += t;
+        (*count)[i] += 1;
+    }
+}
+
+KernelProfiler::~KernelProfiler() {
+    for (auto& r : recs) {
+        if (r.a) cudaEventDestroy(r.a);
+        if (r.b) cudaEventDestroy(r.b);
+    }
+}
+
+namespace {
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// Selects a device for the duration of a call and restores the caller's.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        DRESSI_CUDA(cudaGetDevice(&prev));
+        if (prev != dev) DRESSI_CUDA(cudaSetDevice(dev));
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (cudaGetDevice(&cur) == cudaSuccess && cur != prev && prev >= 0)
+            cudaSetDevice(prev);
+    }
+};
+
+// Stream-ordered scratch for op-level calls.
+struct AsyncScratch {
+    void* p = nullptr;
+    cudaStream_t s;
+    AsyncScratch(size_t bytes, cudaStream_t st) : s(st) {
+        if (bytes) DRESSI_CUDA(cudaMallocAsync(&p, bytes, s));
+    }
+    ~AsyncScratch() {
+        if (p) cudaFreeAsync(p, s);
+    }
+};
+
+}  // namespace
+}  // namespace dressi
+
+using namespace dressi;
+
+struct dressi_plan_s {
+    enum Kind { kSil, kFit } kind = kSil;
+    int device = 0;
+    void* mem = nullptr;
+    size_t mem_bytes = 0;
+    struct Slot {
+        void* ptr = nullptr;
+        size_t bytes = 0;
+    } slots[10];
+    // silhouette
+    SoftDims d;
+    SilParams p{};
+    SilBuffers b{};
+    // image fit
+    size_t n = 0;
+    float lr = 0.f;
+    FitBuffers fb{};
+    // replay
+    cudaStream_t cap_stream = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    uint32_t kernels_per_iter = 0;
+
+    void set_slot(int i, void* ptr, size_t bytes) {
+        slots[i].ptr = ptr;
+        slots[i].bytes = bytes;
+    }
+
+    void record_iteration(cudaStream_t s) {
+        if (kind == kSil) {
+            sil_iteration(d, p, b, s);
+        } else {
+            fit_iteration(n, lr, fb, s);
+        }
+    }
+
+    void ensure_graph() {
+        if (exec) return;
+        if (!cap_stream)
+            DRESSI_CUDA(cudaStreamCreateWithFlags(&cap_stream,
+                                                  cudaStreamNonBlocking));
+        cudaGraph_t g = nullptr;
+        DRESSI_CUDA(cudaStreamBeginCapture(cap_stream,
+                                           cudaStreamCaptureModeThreadLocal));
+        try {
+            record_iteration(cap_stream);
+        } catch (...) {
+            cudaStreamEndCapture(cap_stream, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        DRESSI_CUDA(cudaStreamEndCapture(cap_stream, &g));
+        size_t n_nodes = 0;
+        DRESSI_CUDA(cudaGraphGetNodes(g, nullptr, &n_nodes));
+        std::vector<cudaGraphNode_t> nodes(n_nodes);
+        DRESSI_CUDA(cudaGraphGetNodes(g, nodes.data(), &n_nodes));
+        uint32_t k = 0;
+        for (auto nd : nodes) {
+            cudaGraphNodeType t;
+            DRESSI_CUDA(cudaGraphNodeGetType(nd, &t));
+            if (t == cudaGraphNodeTypeKernel) k++;
+        }
+        kernels_per_iter = k;
+        const cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+        cudaGraphDestroy(g);
+        DRESSI_CUDA(e);
+    }
+
+    ~dressi_plan_s() {
+        int prev = -1;
+        cudaGetDevice(&prev);
+        cudaSetDevice(device);
+        if (exec) cudaGraphExecDestroy(exec);
+        if (cap_stream) cudaStreamDestroy(cap_stream);
+        if (mem) cudaFree(mem);
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+extern "C" {
+
+int dressi_abi_version(void) { return DRESSI_B200_ABI_VERSION; }
+
+int dressi_last_error(char* buf, size_t len) {
+    const std::string& e = g_last_error;
+    if (buf && len) {
+        const size_t n = std::min(len - 1, e.size());
+        std::memcpy(buf, e.data(), n);
+        buf[n] = '\0';
+    }
+    return int(e.size());
+}
+
+int dressi_soft_clip(const float* clip, uint32_t n_verts, const float* faces,
+                     uint32_t n_faces, uint32_t views, uint32_t width,
+                     uint32_t height, float radius_px, float* out,
+                     uint32_t* status, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(clip && faces && out && status, "null pointer");
+        DRESSI_REQUIRE(views >= 1 && width >= 1 && height >= 1,
+                       "SoftClip: empty screen or no views");
+        DRESSI_REQUIRE(radius_px >= 0.f, "SoftClip: radius_px must be >= 0");
+        soft_clip_op(clip, faces, int(views), int(n_verts), int(n_faces),
+                     int(width), int(height), radius_px, out, status,
+                     as_stream(stream));
+    });
+}
+
+int dressi_rasterize_soft(const float* soft_clip, uint32_t n_soft,
+                          const float* face_id, const float* faces_soft,
+                          uint32_t n_faces, const float* hard_clip,
+                          uint32_t n_hard, const float* faces_tex,
+                          uint32_t views, uint32_t width, uint32_t height,
+                          float radius_px, const float* prev_depth,
+                          float* out, uint32_t* status, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(out && status, "null pointer");
+        DRESSI_REQUIRE(n_faces == 0 ||
+                               (soft_clip && face_id && faces_soft &&
+                                hard_clip && faces_tex),
+                       "null pointer");
+        DRESSI_REQUIRE(views >= 1 && width >= 1 && height >= 1,
+                       "RasterizeSoft: empty screen or no views");
+        DRESSI_REQUIRE(width <= 32768 && height <= 32768,
+                       "RasterizeSoft: screen larger than 32768");
+        DRESSI_REQUIRE(radius_px > 0.f, "RasterizeSoft: radius_px must be > 0");
+        DRESSI_REQUIRE(n_soft == 3 * n_faces,
+                       "RasterizeSoft: soft vertices must be unwelded "
+                       "(3 per face)");
+        cudaStream_t s = as_stream(stream);
+        SoftDims d;
+        d.W = int(width);
+        d.H = int(height);
+        d.views = int(views);
+        d.n_faces = int(n_faces);
+        d.n_verts = int(n_hard);
+        d.radius = radius_px;
+        d.finalize();
+        default_caps(&d);
+        Arena a;
+        SoftBuffers b;
+        carve_soft(a, d, &b);
+        AsyncScratch scratch(a.used + 256, s);
+        a = Arena{static_cast<char*>(scratch.p), a.used + 256, 0};
+        carve_soft(a, d, &b);
+        init_soft(d, b, s);  // zeroes the counters (and the scratch word)
+        b.status = status;   // report into the caller's word
+        SoftOpInputs in{soft_clip, face_id, faces_soft, hard_clip, faces_tex,
+                        prev_depth, int(n_soft), int(n_hard)};
+        soft_raster_op(d, b, in, out, s);
+    });
+}
+
+int dressi_rasterize_soft_grad(const float* gy, const float* rs,
+                               const float* clip, uint32_t n_verts,
+                               const float* faces, uint32_t n_faces,
+                               uint32_t views, uint32_t width,
+                               uint32_t height, float* grad, uint32_t* status,
+                               void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(gy && rs && clip && faces && grad && status,
+                       "null pointer");
+        DRESSI_REQUIRE(views >= 1 && width >= 1 && height >= 1,
+                       "RasterizeSoft grad: empty screen or no views");
+        dist_grad_op(gy, rs, clip, faces, int(views), int(n_verts),
+                     int(n_faces), int(width), int(height), grad, status,
+                     as_stream(stream));
+    });
+}
+
+static int hard_common(const float* clip, uint32_t n_verts, const float* attr,
+                       uint32_t n_comp, const float* faces, uint32_t n_faces,
+                       uint32_t views, uint32_t width, uint32_t height,
+                       float* out, float* depth_out, uint32_t* status,
+                       void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(clip && out && status && (faces || n_faces == 0),
+                       "null pointer");
+        DRESSI_REQUIRE(views >= 1 && width >= 1 && height >= 1,
+                       "Rasterize: empty screen or no views");
+        DRESSI_REQUIRE(width <= 32768 && height <= 32768,
+                       "Rasterize: screen larger than 32768");
+        DRESSI_REQUIRE(n_comp >= 1 && n_comp <= 4,
+                       "Rasterize: attribute must have 1..4 components");
+        cudaStream_t s = as_stream(stream);
+        HardDims d;
+        d.W = int(width);
+        d.H = int(height);
+        d.views = int(views);
+        d.n_faces = int(n_faces);
+        d.n_verts = int(n_verts);
+        d.n_comp = int(n_comp);
+        d.finalize();
+        AsyncScratch scratch(hard_workspace_bytes(d), s);
+        hard_raster_op(d, scratch.p, clip, attr, faces, out, depth_out,
+                       status, s);
+    });
+}
+
+int dressi_rasterize_face_id(const float* clip, uint32_t n_verts,
+                             const float* faces, uint32_t n_faces,
+                             uint32_t views, uint32_t width, uint32_t height,
+                             float* out, float* depth_out, uint32_t* status,
+                             void* stream) {
+    return hard_common(clip, n_verts, nullptr, 1, faces, n_faces, views,
+                       width, height, out, depth_out, status, stream);
+}
+
+int dressi_rasterize(const float* clip, uint32_t n_verts, const float* attr,
+                     uint32_t n_comp, const float* faces, uint32_t n_faces,
+                     uint32_t views, uint32_t width, uint32_t height,
+                     float* out, uint32_t* status, void* stream) {
+    if (!attr) {
+        set_last_error("Rasterize: null attribute");
+        return DRESSI_ERR_INVALID;
+    }
+    return hard_common(clip, n_verts, attr, n_comp, faces, n_faces, views,
+                       width, height, out, nullptr, status, stream);
+}
+
+int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
+                                  dressi_plan* out) {
+    return guarded([&] {
+        DRESSI_REQUIRE(desc && out, "null pointer");
+        DRESSI_REQUIRE(desc->struct_size == sizeof(dressi_silhouette_desc),
+                       "dressi_silhouette_desc: struct_size mismatch");
+        DRESSI_REQUIRE(desc->n_verts > 0 && desc->n_faces > 0 &&
+                               desc->n_views > 0 && desc->res > 0,
+                       "silhouette plan: empty mesh, views or screen");
+        DRESSI_REQUIRE(desc->res <= 32768, "silhouette plan: res > 32768");
+        DRESSI_REQUIRE(desc->faces && desc->mvps, "null pointer");
+        DRESSI_REQUIRE(desc->radius_px > 0.f && desc->sigma > 0.f,
+                       "silhouette plan: radius_px and sigma must be > 0");
+        *out = nullptr;
+        DeviceGuard dg(desc->device);
+        auto pl = std::make_unique<dressi_plan_s>();
+        pl->kind = dressi_plan_s::kSil;
+        pl->device = desc->device;
+        SoftDims& d = pl->d;
+        d.W = d.H = int(desc->res);
+        d.views = int(desc->n_views);
+        d.n_faces = int(desc->n_faces);
+        d.n_verts = int(desc->n_verts);
+        d.radius = desc->radius_px;
+        d.finalize();
+        default_caps(&d);
+        SilParams& p = pl->p;
+        p.n_verts = int(desc->n_verts);
+        p.n_faces = int(desc->n_faces);
+        p.views = int(desc->n_views);
+        p.res = int(desc->res);
+        p.radius = desc->radius_px;
+        p.sigma = desc->sigma;
+        p.lr = desc->lr;
+        p.b1 = desc->beta1;
+        p.b2 = desc->beta2;
+        p.eps = desc->eps;
+        p.k = (2.f / float(desc->res)) * (2.f / float(desc->res)) / desc->sigma;
+        p.c = 1.f / float(desc->res * desc->res);
+        const int hist = desc->loss_history ? int(desc->loss_history) : 4096;
+        const size_t V = desc->n_verts, F = desc->n_faces, NV = desc->n_views;
+        const size_t R2 = size_t(desc->res) * desc->res;
+        auto carve = [&](Arena& a) {
+            SilBuffers& b = pl->b;
+            b.pos = a.take<float>(V * 3);
+            b.adam_m = a.take<float>(V * 3);
+            b.adam_v = a.take<float>(V * 3);
+            b.scalars = a.take<float>(4);
+            b.faces = a.take<float>(F * 3);
+            b.mvps = a.take<float>(NV * 16);
+            b.targets = a.take<float>(NV * R2);
+            b.clip = a.take<float>(NV * V * 4);
+            b.gclip = a.take<float>(NV * V * 4);
+            b.gpos = a.take<float>(V * 3);
+            b.loss_slots = a.take<double>(kLossSlots);
+            b.loss_hist = a.take<float>(size_t(hist));
+            b.hist_cap = hist;
+            b.done = a.take<unsigned>(1);
+            carve_soft(a, d, &b.soft);
+        };
+        Arena dry;
+        carve(dry);
+        pl->mem_bytes = dry.used + 256;
+        DRESSI_CUDA(cudaMalloc(&pl->mem, pl->mem_bytes));
+        Arena a{static_cast<char*>(pl->mem), pl->mem_bytes, 0};
+        carve(a);
+        // Everything starts at zero: Adam state, counters, gradients.
+        DRESSI_CUDA(cudaMemset(pl->mem, 0, pl->mem_bytes));
+        DRESSI_CUDA(cudaMemcpy(pl->b.faces, desc->faces, F * 3 * sizeof(float),
+                               cudaMemcpyHostToDevice));
+        DRESSI_CUDA(cudaMemcpy(pl->b.mvps, desc->mvps, NV * 16 * sizeof(float),
+                               cudaMemcpyHostToDevice));
+        pl->set_slot(DRESSI_SLOT_PARAM, pl->b.pos, V * 3 * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_M, pl->b.adam_m, V * 3 * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_V, pl->b.adam_v, V * 3 * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_T, pl->b.scalars, 4);
+        pl->set_slot(DRESSI_SLOT_TARGET, pl->b.targets, NV * R2 * 4);
+        pl->set_slot(DRESSI_SLOT_GRAD, pl->b.gpos, V * 3 * 4);
+        pl->set_slot(DRESSI_SLOT_LOSS, pl->b.scalars + 3, 4);
+        pl->set_slot(DRESSI_SLOT_LOSS_HISTORY, pl->b.loss_hist, size_t(hist) * 4);
+        pl->set_slot(DRESSI_SLOT_RASTER, nullptr, NV * R2 * 16);
+        pl->set_slot(DRESSI_SLOT_MVP, pl->b.mvps, NV * 16 * 4);
+        *out = pl.release();
+    });
+}
+
+int dressi_image_fit_plan_create(uint32_t width, uint32_t height, float lr,
+                                 int device, dressi_plan* out) {
+    return guarded([&] {
+        DRESSI_REQUIRE(out, "null pointer");
+        DRESSI_REQUIRE(width > 0 && height > 0, "image fit: empty image");
+        *out = nullptr;
+        DeviceGuard dg(device);
+        auto pl = std::make_unique<dressi_plan_s>();
+        pl->kind = dressi_plan_s::kFit;
+        pl->device = device;
+        pl->n = size_t(width) * height * 4;
+        pl->lr = lr;
+        const size_t n = pl->n;
+        auto carve = [&](Arena& a) {
+            FitBuffers& f = pl->fb;
+            f.param = a.take<float>(n);
+            f.target = a.take<float>(n);
+            f.m = a.take<float>(n);
+            f.v = a.take<float>(n);
+            f.scalars = a.take<float>(4);
+            f.loss_acc = a.take<double>(1);
+            f.hist_cap = 4096;
+            f.loss_hist = a.take<float>(4096);
+            f.done = a.take<unsigned>(1);
+        };
+        Arena dry;
+        carve(dry);
+        pl->mem_bytes = dry.used + 256;
+        DRESSI_CUDA(cudaMalloc(&pl->mem, pl->mem_bytes));
+        Arena a{static_cast<char*>(pl->mem), pl->mem_bytes, 0};
+        carve(a);
+        DRESSI_CUDA(cudaMemset(pl->mem, 0, pl->mem_bytes));
+        pl->set_slot(DRESSI_SLOT_PARAM, pl->fb.param, n * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_M, pl->fb.m, n * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_V, pl->fb.v, n * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_T, pl->fb.scalars, 4);
+        pl->set_slot(DRESSI_SLOT_TARGET, pl->fb.target, n * 4);
+        pl->set_slot(DRESSI_SLOT_LOSS, pl->fb.scalars + 3, 4);
+        pl->set_slot(DRESSI_SLOT_LOSS_HISTORY, pl->fb.loss_hist, 4096 * 4);
+        *out = pl.release();
+    });
+}
+
+static dressi_plan_s::Slot& plan_slot(dressi_plan p, int slot) {
+    DRESSI_REQUIRE(p, "null plan");
+    DRESSI_REQUIRE(slot >= 0 && slot < 10 && p->slots[slot].bytes > 0,
+                   "plan has no such slot");
+    return p->slots[slot];
+}
+
+int dressi_plan_slot_bytes(dressi_plan p, int slot, size_t* bytes) {
+    return guarded([&] {
+        DRESSI_REQUIRE(bytes, "null pointer");
+        *bytes = plan_slot(p, slot).bytes;
+    });
+}
+
+int dressi_plan_slot_ptr(dressi_plan p, int slot, void** ptr) {
+    return guarded([&] {
+        DRESSI_REQUIRE(ptr, "null pointer");
+        auto& s = plan_slot(p, slot);
+        DRESSI_REQUIRE(s.ptr, "slot is not resident (render it first)");
+        *ptr = s.ptr;
+    });
+}
+
+int dressi_plan_upload(dressi_plan p, int slot, const void* src, size_t bytes,
+                       int src_is_device, void* stream) {
+    return guarded([&] {
+        auto& s = plan_slot(p, slot);
+        DRESSI_REQUIRE(src, "null pointer");
+        DRESSI_REQUIRE(s.ptr, "slot is not uploadable");
+        DRESSI_REQUIRE(bytes == s.bytes,
+                       "upload size " + std::to_string(bytes) +
+                               " != slot size " + std::to_string(s.bytes));
+        DeviceGuard dg(p->device);
+        DRESSI_CUDA(cudaMemcpyAsync(s.ptr, src, bytes,
+                                    src_is_device ? cudaMemcpyDeviceToDevice
+                                                  : cudaMemcpyHostToDevice,
+                                    as_stream(stream)));
+    });
+}
+
+int dressi_plan_download(dressi_plan p, int slot, void* dst, size_t bytes,
+                         int dst_is_device, void* stream) {
+    return guarded([&] {
+        auto& s = plan_slot(p, slot);
+        DRESSI_REQUIRE(dst, "null pointer");
+        DRESSI_REQUIRE(s.ptr, "slot is not resident (render it first)");
+        DRESSI_REQUIRE(bytes == s.bytes,
+                       "download size " + std::to_string(bytes) +
+                               " != slot size " + std::to_string(s.bytes));
+        DeviceGuard dg(p->device);
+        DRESSI_CUDA(cudaMemcpyAsync(dst, s.ptr, bytes,
+                                    dst_is_device ? cudaMemcpyDeviceToDevice
+                                                  : cudaMemcpyDeviceToHost,
+                                    as_stream(stream)));
+    });
+}
+
+int dressi_plan_render_targets(dressi_plan p, const float* target_pos_host,
+                               void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(p && target_pos_host, "null pointer");
+        DRESSI_REQUIRE(p->kind == dressi_plan_s::kSil,
+                       "render_targets: not a silhouette plan");
+        DeviceGuard dg(p->device);
+        cudaStream_t s = as_stream(stream);
+        const size_t bytes = size_t(p->p.n_verts) * 3 * sizeof(float);
+        AsyncScratch tp(bytes, s);
+        DRESSI_CUDA(cudaMemcpyAsync(tp.p, target_pos_host, bytes,
+                                    cudaMemcpyHostToDevice, s));
+        sil_render_targets(p->d, p->p, p->b, static_cast<float*>(tp.p), s);
+        // the host array must stay valid until the copy ran
+        DRESSI_CUDA(cudaStreamSynchronize(s));
+    });
+}
+
+int dressi_plan_exec(dressi_plan p, uint32_t n_iters, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(p, "null plan");
+        DeviceGuard dg(p->device);
+        p->ensure_graph();
+        for (uint32_t i = 0; i < n_iters; i++)
+            DRESSI_CUDA(cudaGraphLaunch(p->exec, as_stream(stream)));
+    });
+}
+
+int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(p, "null plan");
+        DRESSI_REQUIRE(p->kind == dressi_plan_s::kSil,
+                       "exec_phase: not a silhouette plan");
+        DRESSI_REQUIRE(phase == 0 || phase == 1, "exec_phase: phase is 0 or 1");
+        DeviceGuard dg(p->device);
+        cudaStream_t s = as_stream(stream);
+        if (phase == 0) {
+            sil_forward_backward(p->d, p->p, p->b, nullptr, s);
+            sil_grad_reduce(p->p, p->b, false, s);
+        } else {
+            sil_update(p->p, p->b, s);
+        }
+    });
+}
+
+int dressi_plan_render(dressi_plan p, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(p, "null plan");
+        DRESSI_REQUIRE(p->kind == dressi_plan_s::kSil,
+                       "render: not a silhouette plan");
+        DeviceGuard dg(p->device);
+        cudaStream_t s = as_stream(stream);
+        auto& slot = p->slots[DRESSI_SLOT_RASTER];
+        if (!slot.ptr) DRESSI_CUDA(cudaMalloc(&slot.ptr, slot.bytes));
+        // A forward/backward pass whose side effects are undone: the Adam
+        // counter advance is rolled back and the gradient buffers cleared.
+        float t_saved = 0.f;
+        DRESSI_CUDA(cudaMemcpyAsync(&t_saved, p->b.scalars, 4,
+                                    cudaMemcpyDeviceToHost, s));
+        DRESSI_CUDA(cudaStreamSynchronize(s));
+        sil_forward_backward(p->d, p->p, p->b, static_cast<float*>(slot.ptr),
+                             s);
+        sil_grad_reduce(p->p, p->b, false, s);
+        DRESSI_CUDA(cudaMemcpyAsync(p->b.scalars, &t_saved, 4,
+                                    cudaMemcpyHostToDevice, s));
+        DRESSI_CUDA(cudaStreamSynchronize(s));
+    });
+}
+
+int dressi_plan_status(dressi_plan p, uint32_t* word, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(p && word, "null pointer");
+        DeviceGuard dg(p->device);
+        cudaStream_t s = as_stream(stream);
+        *word = 0;
+        if (p->kind == dressi_plan_s::kSil) {
+            DRESSI_CUDA(cudaMemcpyAsync(word, p->b.soft.status, 4,
+                                        cudaMemcpyDeviceToHost, s));
+        }
+        DRESSI_CUDA(cudaStreamSynchronize(s));
+    });
+}
+
+int dressi_plan_launches_per_iter(dressi_plan p, uint32_t* n) {
+    return guarded([&] {
+        DRESSI_REQUIRE(p && n, "null pointer");
+        DeviceGuard dg(p->device);
+        p->ensure_graph();
+        *n = p->kernels_per_iter;
+    });
+}
+
+int dressi_plan_profile(dressi_plan p, uint32_t n_iters, void* stream,
+                        uint32_t max_kernels, const char** names,
+                        float* total_ms, uint32_t* launches,
+                        uint32_t* n_kernels) {
+    return guarded([&] {
+        DRESSI_REQUIRE(p && n_kernels, "null pointer");
+        DeviceGuard dg(p->device);
+        cudaStream_t s = as_stream(stream);
+        KernelProfiler prof;
+        current_profiler() = &prof;
+        try {
+            for (uint32_t i = 0; i < n_iters; i++) p->record_iteration(s);
+        } catch (...) {
+            current_profiler() = nullptr;
+            throw;
+        }
+        current_profiler() = nullptr;
+        std::vector<const char*> nm;
+        std::vector<double> ms;
+        std::vector<int> cnt;
+        prof.collect(&nm, &ms, &cnt);
+        *n_kernels = uint32_t(nm.size());
+        for (size_t i = 0; i < nm.size() && i < max_kernels; i++) {
+            if (names) names[i] = nm[i];  // launch-site string literals
+            if (total_ms) total_ms[i] = float(ms[i]);
+            if (launches) launches[i] = uint32_t(cnt[i]);
+        }
+    });
+}
+
+int dressi_plan_destroy(dressi_plan p) {
+    return guarded([&] { delete p; });
+}
+
+}  // extern "C"

@@ -1,0 +1,291 @@
+// Hard rasterizer (F::RasterizeFaceId / F::Rasterize): tile-binned and
+// bit-exact with the reference's RasterizeCore (cpu_raster.cpp:31-110).
+//
+// The reference keeps, per pixel, the fragment with the smallest NDC z and
+// the latest face on ties (`if (z > zb) continue;`). Each thread owns one
+// pixel and folds every fragment of its tile's face list into that key, so
+// list order does not matter. The survivor's barycentrics are recomputed
+// once at the end for the attribute interpolation, with the reference's
+// expressions (shade lambda, cpu_raster.cpp:205-223).
+#include <algorithm>
+
+#include "kernels.h"
+
+namespace dressi {
+
+struct __align__(16) HardRec {
+    float x0, y0, x1, y1;   // screen px
+    float x2, y2, inv_area, pad;
+    float z0, z1, z2, pad2;  // NDC depth
+    float iw0, iw1, iw2, pad3;  // 1 / clip.w
+    int bx0, bx1, by0, by1;  // pixel range (inclusive)
+    uint32_t flags, i0, i1, i2;
+};
+static_assert(sizeof(HardRec) == 96, "HardRec layout");
+constexpr int kHardVec4 = sizeof(HardRec) / 16;
+
+struct HardBuffers {
+    HardRec* recs;
+    BinSet bin;
+    uint32_t* status;
+};
+
+static void carve_hard(Arena& a, const HardDims& d, HardBuffers* b) {
+    const size_t vt = size_t(d.views) * d.n_tiles;
+    b->recs = a.take<HardRec>(size_t(d.views) * std::max(d.n_faces, 1));
+    b->bin.count = a.take<int>(vt);
+    b->bin.offset = a.take<int>(vt);
+    b->bin.cursor = a.take<int>(vt);
+    b->bin.overflow = a.take<int>(d.views);
+    b->bin.cap = d.cap;
+    b->bin.list = a.take<int>(size_t(d.views) * d.cap);
+}
+
+static HardDims with_cap(HardDims d) {
+    d.finalize();
+    if (d.cap <= 0) {
+        const long long f = d.n_faces, t = d.n_tiles;
+        d.cap = int(std::min<long long>(std::max<long long>(16 * f, 4 * t) + 4096,
+                                        1ll << 30));
+    }
+    return d;
+}
+
+size_t hard_workspace_bytes(const HardDims& d0) {
+    const HardDims d = with_cap(d0);
+    Arena a;
+    HardBuffers b;
+    carve_hard(a, d, &b);
+    return a.used + 256;
+}
+
+// RasterizeCore's per-face prologue (cpu_raster.cpp:43-78).
+__global__ void k_hard_setup(HardDims d, const float4* clip,
+                             const float* faces, HardBuffers b) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    const int v = blockIdx.y;
+    if (f >= d.n_faces) return;
+    HardRec r;
+    r.flags = 0;
+    uint32_t idx[3];
+    float sx[3], sy[3], sz[3], iw[3];
+    bool ok = true;
+    for (int k = 0; k < 3; k++) {
+        idx[k] = x86_u32_via_i64(faces[size_t(f) * 3 + k]);
+        if (idx[k] >= uint32_t(d.n_verts)) {
+            atomicOr(b.status, kStatusIndexRange);
+            ok = false;
+            break;
+        }
+        const float4 c = clip[size_t(v) * d.n_verts + idx[k]];
+        if (fabsf(c.w) <= 1e-6f || c.w < 0.f) {
+            ok = false;
+            break;
+        }
+        const float inv_w = 1.f / c.w;
+        sx[k] = (c.x * inv_w * 0.5f + 0.5f) * float(d.W);
+        sy[k] = (c.y * inv_w * 0.5f + 0.5f) * float(d.H);
+        sz[k] = c.z * inv_w;
+        iw[k] = inv_w;
+    }
+    if (ok) {
+        const float area = (sx[1] - sx[0]) * (sy[2] - sy[0]) -
+                           (sy[1] - sy[0]) * (sx[2] - sx[0]);
+        if (!(fabsf(area) < 1e-6f)) {
+            r.x0 = sx[0]; r.y0 = sy[0]; r.x1 = sx[1]; r.y1 = sy[1];
+            r.x2 = sx[2]; r.y2 = sy[2];
+            r.inv_area = 1.f / area;
+            r.z0 = sz[0]; r.z1 = sz[1]; r.z2 = sz[2];
+            r.iw0 = iw[0]; r.iw1 = iw[1]; r.iw2 = iw[2];
+            r.pad = r.pad2 = r.pad3 = 0.f;
+            bbox_range(std_min(std_min(sx[0], sx[1]), sx[2]),
+                       std_max(std_max(sx[0], sx[1]), sx[2]), d.W, &r.bx0,
+                       &r.bx1);
+            bbox_range(std_min(std_min(sy[0], sy[1]), sy[2]),
+                       std_max(std_max(sy[0], sy[1]), sy[2]), d.H, &r.by0,
+                       &r.by1);
+            r.i0 = idx[0]; r.i1 = idx[1]; r.i2 = idx[2];
+            if (r.bx0 <= r.bx1 && r.by0 <= r.by1) r.flags = kFaceValid;
+        }
+    }
+    b.recs[size_t(v) * d.n_faces + f] = r;
+    if (!(r.flags & kFaceValid)) return;
+    int tx0, tx1, ty0, ty1;
+    tile_range(r.bx0, r.bx1, r.by0, r.by1, &tx0, &tx1, &ty0, &ty1);
+    int* cnt = b.bin.count + size_t(v) * d.n_tiles;
+    for (int ty = ty0; ty <= ty1; ty++)
+        for (int tx = tx0; tx <= tx1; tx++) atomicAdd(&cnt[ty * d.tiles_x + tx], 1);
+}
+
+__global__ void k_hard_fill(HardDims d, HardBuffers b) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    const int v = blockIdx.y;
+    if (f >= d.n_faces) return;
+    const HardRec& r = b.recs[size_t(v) * d.n_faces + f];
+    if (!(r.flags & kFaceValid)) return;
+    const bool of = b.bin.overflow[v] != 0;
+    int tx0, tx1, ty0, ty1;
+    tile_range(r.bx0, r.bx1, r.by0, r.by1, &tx0, &tx1, &ty0, &ty1);
+    int* cur = b.bin.cursor + size_t(v) * d.n_tiles;
+    int* list = b.bin.list + size_t(v) * b.bin.cap;
+    for (int ty = ty0; ty <= ty1; ty++)
+        for (int tx = tx0; tx <= tx1; tx++) {
+            const int slot = atomicAdd(&cur[ty * d.tiles_x + tx], 1);
+            if (!of && slot < b.bin.cap) list[slot] = f;
+        }
+}
+
+// Screen barycentrics of RasterizeCore (cpu_raster.cpp:82-90).
+__device__ __forceinline__ void hard_bary(const HardRec& r, float px, float py,
+                                          float* l0, float* l1, float* l2) {
+    *l0 = ((r.x1 - px) * (r.y2 - py) - (r.y1 - py) * (r.x2 - px)) * r.inv_area;
+    *l1 = ((r.x2 - px) * (r.y0 - py) - (r.y2 - py) * (r.x0 - px)) * r.inv_area;
+    *l2 = 1.f - *l0 - *l1;
+}
+
+constexpr int kHardChunk = 128;
+
+// attr == nullptr: writes float(face)+1 / 0 into out[v][H][W].
+// Otherwise writes the perspective-correct attribute (n_comp channels).
+__global__ void __launch_bounds__(kTileThreads)
+        k_hard_sweep(HardDims d, HardBuffers b, const float* attr, float* out,
+                     float* depth_out) {
+    __shared__ HardRec sh[kHardChunk];
+    const int v = blockIdx.y, tile = blockIdx.x;
+    const int tx = tile % d.tiles_x, ty = tile / d.tiles_x;
+    const int x = tx * kTile + (threadIdx.x % kTile);
+    const int y = ty * kTile + (threadIdx.x / kTile);
+    const bool in = x < d.W && y < d.H;
+    const float px = float(x) + 0.5f, py = float(y) + 0.5f;
+    const HardRec* recs = b.recs + size_t(v) * d.n_faces;
+    const bool identity = b.bin.overflow[v] != 0;
+    const int tl = v * d.n_tiles + tile;
+    const int beg = identity ? 0 : b.bin.offset[tl];
+    const int end = identity ? d.n_faces : b.bin.cursor[tl];
+    const int* list = b.bin.list + size_t(v) * b.bin.cap;
+    float best_z = 1.f;
+    int best_f = -1;
+    for (int base = beg; base < end; base += kHardChunk) {
+        const int n = imin_(kHardChunk, end - base);
+        __syncthreads();
+        const float4* src = reinterpret_cast<const float4*>(recs);
+        float4* dst = reinterpret_cast<float4*>(sh);
+        for (int i = threadIdx.x; i < n * kHardVec4; i += blockDim.x) {
+            const int j = i / kHardVec4, w = i % kHardVec4;
+            const int f = identity ? base + j : list[base + j];
+            dst[i] = src[size_t(f) * kHardVec4 + w];
+        }
+        __syncthreads();
+        if (!in) continue;
+        for (int i = 0; i < n; i++) {
+            const HardRec& r = sh[i];
+            if (!(r.flags & kFaceValid)) continue;
+            if (x < r.bx0 || x > r.bx1 || y < r.by0 || y > r.by1) continue;
+            float l0, l1, l2;
+            hard_bary(r, px, py, &l0, &l1, &l2);
+            if (l0 < 0.f || l1 < 0.f || l2 < 0.f) continue;
+            const float z = l0 * r.z0 + l1 * r.z1 + l2 * r.z2;
+            if (z < 0.f || z > 1.f) continue;
+            const int f = identity ? base + i : list[base + i];
+            if (beats(z, f, best_z, best_f)) {
+                best_z = z;
+                best_f = f;
+            }
+        }
+    }
+    if (!in) return;
+    const size_t pix = size_t(v) * d.W * d.H + size_t(y) * d.W + x;
+    if (depth_out) depth_out[pix] = best_f >= 0 ? best_z : 1.f;
+    if (!attr) {
+        out[pix] = best_f >= 0 ? float(best_f) + 1.f : 0.f;
+        return;
+    }
+    float* o = out + pix * d.n_comp;
+    if (best_f < 0) {
+        for (int c = 0; c < d.n_comp; c++) o[c] = 0.f;
+        return;
+    }
+    const HardRec& r = recs[best_f];
+    float l[3];
+    hard_bary(r, px, py, &l[0], &l[1], &l[2]);
+    const float iw[3] = {r.iw0, r.iw1, r.iw2};
+    const uint32_t idx[3] = {r.i0, r.i1, r.i2};
+    const float denom = l[0] * iw[0] + l[1] * iw[1] + l[2] * iw[2];
+    const float* av = attr + size_t(v) * d.n_verts * d.n_comp;
+    for (int c = 0; c < d.n_comp; c++) {
+        float num = 0.f;
+        for (int k = 0; k < 3; k++) num += l[k] * iw[k] * av[size_t(idx[k]) * d.n_comp + c];
+        o[c] = num / denom;
+    }
+}
+
+static void check_launch() { DRESSI_CUDA(cudaGetLastError()); }
+
+void hard_raster_op(const HardDims& d0, void* workspace, const float* clip,
+                    const float* attr, const float* faces, float* out,
+                    float* depth_out, uint32_t* status, cudaStream_t s) {
+    const HardDims d = with_cap(d0);
+    Arena a;
+    a.base = static_cast<char*>(workspace);
+    a.size = hard_workspace_bytes(d0);
+    HardBuffers b;
+    carve_hard(a, d, &b);
+    b.status = status;
+    const size_t vt = size_t(d.views) * d.n_tiles;
+    DRESSI_CUDA(cudaMemsetAsync(b.bin.count, 0, vt * sizeof(int), s));
+    if (d.n_faces > 0) {
+        const dim3 fg((d.n_faces + 127) / 128, d.views);
+        k_hard_setup<<<fg, 128, 0, s>>>(d, reinterpret_cast<const float4*>(clip),
+                                        faces, b);
+        k_bin_scan<<<d.views, 1024, 0, s>>>(b.bin, d.n_tiles, status);
+        k_hard_fill<<<fg, 128, 0, s>>>(d, b);
+    } else {
+        k_bin_scan<<<d.views, 1024, 0, s>>>(b.bin, d.n_tiles, status);
+    }
+    k_hard_sweep<<<dim3(d.n_tiles, d.views), kTileThreads, 0, s>>>(
+            d, b, attr, out, depth_out);
+    check_launch();
+}
+
+// ------------------------------------------------- silhouette targets
+
+__global__ void k_transform_plain(const float* pos, const float* mvps,
+                                  int n_verts, float4* clip) {
+    const int v = blockIdx.y;
+    const int u = blockIdx.x * blockDim.x + threadIdx.x;
+    if (u >= n_verts) return;
+    clip[size_t(v) * n_verts + u] = transform_clip(
+            pos[u * 3 + 0], pos[u * 3 + 1], pos[u * 3 + 2], mvps + v * 16);
+}
+
+__global__ void k_mask_from_id(float* img, size_t n) {
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += size_t(gridDim.x) * blockDim.x)
+        img[i] = img[i] > 0.5f ? 1.f : 0.f;
+}
+
+void sil_render_targets(const SoftDims& d, const SilParams& p,
+                        const SilBuffers& b, const float* target_pos,
+                        cudaStream_t s) {
+    HardDims hd;
+    hd.W = hd.H = p.res;
+    hd.views = p.views;
+    hd.n_faces = p.n_faces;
+    hd.n_verts = p.n_verts;
+    const size_t ws = hard_workspace_bytes(hd);
+    void* mem = nullptr;
+    DRESSI_CUDA(cudaMallocAsync(&mem, ws, s));
+    // target clip positions go through b.clip (overwritten every iteration)
+    k_transform_plain<<<dim3((p.n_verts + 255) / 256, p.views), 256, 0, s>>>(
+            target_pos, b.mvps, p.n_verts, reinterpret_cast<float4*>(b.clip));
+    hard_raster_op(hd, mem, b.clip, nullptr, b.faces, b.targets, nullptr,
+                   b.soft.status, s);
+    const size_t n = size_t(p.views) * p.res * p.res;
+    k_mask_from_id<<<int(std::min<size_t>((n + 255) / 256, 8192)), 256, 0, s>>>(
+            b.targets, n);
+    check_launch();
+    DRESSI_CUDA(cudaFreeAsync(mem, s));
+    (void)d;
+}
+
+}  // namespace dressi

@@ -1,0 +1,157 @@
+// Internal host-side interface between the C ABI (capi.cu) and the kernel
+// translation units. Not installed; the public surface is
+// include/dressi_b200.h.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "common.h"
+#include "raster_soft.cuh"
+
+namespace dressi {
+
+// Shape of one soft-raster launch (all views share W, H and the face count).
+struct SoftDims {
+    int W = 0, H = 0, views = 1, n_faces = 0, n_verts = 0;
+    float radius = 1.f;
+    int tiles_x = 0, tiles_y = 0, n_tiles = 0;
+    int cap1 = 0, cap2 = 0;  // tile-list capacity per view (entries)
+
+    void finalize() {
+        tiles_x = (W + kTile - 1) / kTile;
+        tiles_y = (H + kTile - 1) / kTile;
+        n_tiles = tiles_x * tiles_y;
+    }
+};
+
+// Device scratch of the soft rasterizer, carved from one allocation.
+struct SoftBuffers {
+    FaceRec* recs = nullptr;   // [views * n_faces]
+    BinSet bin1{}, bin2{};
+    PixState* state = nullptr; // [views * W * H]
+    int* active = nullptr;     // [views * n_tiles]
+    uint32_t* status = nullptr;
+};
+
+// Carves SoftBuffers out of `a` (a dry run with a.base == nullptr measures
+// the size). The count arrays must be zero before the first use; the scan
+// re-zeroes them after every use.
+void carve_soft(Arena& a, const SoftDims& d, SoftBuffers* b);
+// Zeroes the persistent counters of freshly carved buffers.
+void init_soft(const SoftDims& d, const SoftBuffers& b, cudaStream_t s);
+
+// Default tile-list capacities for a scene (entries per view).
+void default_caps(SoftDims* d);
+
+// Enqueues sweep-1 binning, sweep 1 and sweep-2 binning (records and the
+// sweep-1 tile counts must already be written by a face-setup kernel).
+void soft_bin_and_sweep1(const SoftDims& d, const SoftBuffers& b,
+                         const float* prev_depth, cudaStream_t s);
+
+// --- op-level soft raster (explicit soft geometry, one or more views) ---
+struct SoftOpInputs {
+    const float* soft_clip;   // [views][n_soft][4]
+    const float* face_id;     // [views][n_soft]
+    const float* faces_soft;  // [n_faces][3]  (shared by all views)
+    const float* hard_clip;   // [views][n_hard][4]
+    const float* faces_tex;   // [n_faces][3]  (shared)
+    const float* prev_depth;  // [views][H][W] or null
+    int n_soft, n_hard;
+};
+// Enqueues face setup, binning and both sweeps; writes out[views][H][W][4].
+void soft_raster_op(const SoftDims& d, const SoftBuffers& b,
+                    const SoftOpInputs& in, float* out, cudaStream_t s);
+
+// --- exact GatherDistGrad + ColSum (op level) ---
+// grad[views][n_verts][4] += d/d clip of sum_px gy * dist.
+void dist_grad_op(const float* gy, const float* rs, const float* clip,
+                  const float* faces, int views, int n_verts, int n_faces,
+                  int W, int H, float* grad, uint32_t* status,
+                  cudaStream_t s);
+
+// --- SoftClip (op level) ---
+void soft_clip_op(const float* clip, const float* faces, int views,
+                  int n_verts, int n_faces, int W, int H, float radius,
+                  float* out, uint32_t* status, cudaStream_t s);
+
+// --- silhouette iteration (plan level) ---
+struct SilParams {
+    int n_verts, n_faces, views, res;
+    float radius, sigma, lr, b1, b2, eps;
+    float k;  // (2/R)^2 / sigma
+    float c;  // 1 / R^2
+};
+struct SilBuffers {
+    float* pos;       // [V*3]
+    float* adam_m;    // [V*3]
+    float* adam_v;    // [V*3]
+    float* scalars;   // [0]=t  [1]=bc1 [2]=bc2 [3]=last loss
+    float* faces;     // [F*3]
+    float* mvps;      // [views*16]
+    float* targets;   // [views*R*R]
+    float* clip;      // [views*V*4]
+    float* gclip;     // [views*V*4]  zeroed by the Adam step
+    float* gpos;      // [V*3]        last gradient (for inspection)
+    double* loss_slots;  // [kLossSlots] zeroed by the Adam step
+    float* loss_hist;    // [hist_cap]
+    int hist_cap;
+    unsigned* done;      // block-completion counter of the Adam step
+    SoftBuffers soft;
+};
+constexpr int kLossSlots = 1024;
+// Transform, raster, loss and per-view clip gradients (advances the Adam
+// counter). rs_out (nullable) receives the RasterizeSoft images.
+void sil_forward_backward(const SoftDims& d, const SilParams& p,
+                          const SilBuffers& b, float* rs_out, cudaStream_t s);
+// g_pos = sum_v MVP_v^T g_clip_v, the loss of the iteration, and (update)
+// the Adam step.
+void sil_grad_reduce(const SilParams& p, const SilBuffers& b, bool update,
+                     cudaStream_t s);
+// Adam step from an externally reduced g_pos (multi-GPU: after the
+// all-reduce).
+void sil_update(const SilParams& p, const SilBuffers& b, cudaStream_t s);
+// One full single-device iteration.
+void sil_iteration(const SoftDims& d, const SilParams& p,
+                   const SilBuffers& b, cudaStream_t s);
+// Renders hard silhouettes (face id > 0) of pos into targets (setup only).
+void sil_render_targets(const SoftDims& d, const SilParams& p,
+                        const SilBuffers& b, const float* target_pos,
+                        cudaStream_t s);
+
+// --- hard rasterizer (face id / attribute interpolation) ---
+struct HardDims {
+    int W = 0, H = 0, views = 1, n_faces = 0, n_verts = 0, n_comp = 1;
+    int tiles_x = 0, tiles_y = 0, n_tiles = 0, cap = 0;
+    void finalize() {
+        tiles_x = (W + kTile - 1) / kTile;
+        tiles_y = (H + kTile - 1) / kTile;
+        n_tiles = tiles_x * tiles_y;
+    }
+};
+size_t hard_workspace_bytes(const HardDims& d);
+// clip [views][V][4]; attr [views][V][n_comp] (null for face id); faces
+// [F][3] shared. out: face id image [views][H][W] (attr == null) or the
+// interpolated attribute [views][H][W][n_comp]. tri_out (nullable) gets the
+// face-id image as well.
+void hard_raster_op(const HardDims& d, void* workspace, const float* clip,
+                    const float* attr, const float* faces, float* out,
+                    float* depth_out, uint32_t* status, cudaStream_t s);
+
+// --- image fitting (C1) ---
+struct FitBuffers {
+    float* param;   // [n]
+    float* target;  // [n]
+    float* m;       // [n]
+    float* v;       // [n]
+    float* scalars; // [0]=t [3]=last loss
+    double* loss_acc;  // [1]
+    float* loss_hist;
+    int hist_cap;
+    unsigned* done;
+};
+void fit_iteration(size_t n, float lr, const FitBuffers& b, cudaStream_t s);
+
+}  // namespace dressi

@@ -1,0 +1,310 @@
+// The fused silhouette iteration (configs C3/C4, HardSoftRas path):
+//
+//   per view:  clip = MVP_v (pos, 1)                       k_transform
+//              soft = SoftClip(clip); face records          k_face_setup_sil
+//              RasterizeSoft sweeps 1/2 (exact survivor)    raster_soft.cuh
+//              loss image + dL/d dist + GatherDistGrad      k_sweep2_sil
+//   all views: g_pos = sum_v MVP_v^T g_clip_v               k_gpos_adam
+//              in-graph Adam                                k_gpos_adam
+//
+// It computes what the reference's DressiAD::execStep computes for the graph
+// built in oracle/ref_driver.cpp (SilViewLoss + in-graph Adam of
+// examples/silhouette_optimization/run.cpp:421-436), with the RasterizeSoft
+// output, the loss image and the per-view clip gradients kept on chip
+// instead of round-tripping through HBM between passes.
+#include <algorithm>
+
+#include "kernels.h"
+
+namespace dressi {
+
+// Per-pixel loss and dL/d dist of the silhouette graph, in the operation
+// order of the reference autodiff (see oracle.c sil_pixel for the
+// derivation): pred = max(cov*step(0,d), cov*sigmoid(d*|d|*k)),
+// loss = (target - pred)^2 * c.
+__device__ __forceinline__ float sil_pixel(float dist, float cov, float target,
+                                           float k, float c, float* g_dist) {
+    const float step = dist < 0.f ? 0.f : 1.f;
+    const float hard = cov * step;
+    const float a = fabsf(dist);
+    const float m1 = dist * a;
+    const float m2 = m1 * k;
+    const float s = 1.f / (1.f + expf(-m2));
+    const float soft = cov * s;
+    const float pred = std_max(hard, soft);
+    const float diff = target - pred;
+    const float lv = diff * diff * c;
+    const float g_m4 = 1.f * c;
+    const float g_diff = g_m4 * diff + g_m4 * diff;
+    const float g_pred = -g_diff;
+    const float mask = hard < soft ? 0.f : 1.f;
+    const float g_m3 = g_pred * (1.f - mask);
+    const float g_sg = g_m3 * cov;
+    const float g_m2 = g_sg * (s * (1.f - s));
+    const float g_m1 = g_m2 * k;
+    const float sgn = float((dist > 0.f) - (dist < 0.f));
+    *g_dist = g_m1 * a + (g_m1 * dist) * sgn;
+    return lv;
+}
+
+// clip[v][u] = MVP_v (pos_u, 1). Block (0,0) also advances the Adam
+// counter and the bias corrections of this iteration (the {1,1} part of
+// the in-graph Adam: t_new = t + 1, bc = 1 - pow(beta, t_new)).
+__global__ void k_transform(const float* pos, const float* mvps, int n_verts,
+                            float4* clip, float* scalars, float b1, float b2,
+                            int advance) {
+    const int v = blockIdx.y;
+    const int u = blockIdx.x * blockDim.x + threadIdx.x;
+    if (advance && v == 0 && blockIdx.x == 0 && threadIdx.x == 0) {
+        const float t_new = scalars[0] + 1.f;
+        scalars[0] = t_new;
+        scalars[1] = 1.f - powf(b1, t_new);
+        scalars[2] = 1.f - powf(b2, t_new);
+    }
+    __shared__ float m[16];
+    if (threadIdx.x < 16) m[threadIdx.x] = mvps[v * 16 + threadIdx.x];
+    __syncthreads();
+    if (u >= n_verts) return;
+    clip[size_t(v) * n_verts + u] =
+            transform_clip(pos[u * 3 + 0], pos[u * 3 + 1], pos[u * 3 + 2], m);
+}
+
+// Face records of the standard soft geometry (sequential soft faces,
+// face_id = f; examples/silhouette_optimization/run.cpp:456-466).
+__global__ void k_face_setup_sil(SoftDims d, const float4* clip,
+                                 const float* faces, SoftBuffers b) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    const int v = blockIdx.y;
+    if (f >= d.n_faces) return;
+    FaceRec* out = b.recs + size_t(v) * d.n_faces + f;
+    const float W = float(d.W), H = float(d.H);
+    uint32_t idx[3];
+    float4 c[3];
+    for (int k = 0; k < 3; k++) {
+        idx[k] = x86_u32_via_i64(faces[size_t(f) * 3 + k] + 0.5f);
+        if (idx[k] >= uint32_t(d.n_verts)) {
+            atomicOr(b.status, kStatusIndexRange);
+            out->flags = 0;
+            return;
+        }
+        c[k] = clip[size_t(v) * d.n_verts + idx[k]];
+    }
+    float4 sc[3];
+    soft_clip_face(c, W, H, d.radius, sc);
+    float ss[3][2], sz[3], hs[3][2], hz[3];
+    bool valid = true;
+    for (int k = 0; k < 3 && valid; k++) {
+        valid = project_clip(sc[k].x, sc[k].y, sc[k].z, sc[k].w, W, H,
+                             &ss[k][0], &ss[k][1], &sz[k]);
+    }
+    for (int k = 0; k < 3 && valid; k++) {
+        valid = project_clip(c[k].x, c[k].y, c[k].z, c[k].w, W, H, &hs[k][0],
+                             &hs[k][1], &hz[k]);
+    }
+    FaceRec r;
+    if (!valid || !build_record(ss, sz, hs, hz, float(f), idx, d.W, d.H, &r)) {
+        out->flags = 0;
+        return;
+    }
+    *out = r;
+    if (r.rx0 > r.rx1 || r.ry0 > r.ry1) return;
+    int tx0, tx1, ty0, ty1;
+    tile_range(r.rx0, r.rx1, r.ry0, r.ry1, &tx0, &tx1, &ty0, &ty1);
+    int* cnt = b.bin1.count + size_t(v) * d.n_tiles;
+    for (int ty = ty0; ty <= ty1; ty++)
+        for (int tx = tx0; tx <= tx1; tx++) atomicAdd(&cnt[ty * d.tiles_x + tx], 1);
+}
+
+__device__ __forceinline__ void sil_scatter(float px, float py, float g,
+                                            const FaceRec& r,
+                                            const float4* clip_v, float W,
+                                            float H, float* gclip_v) {
+    const float hs[3][2] = {{r.h0x, r.h0y}, {r.h1x, r.h1y}, {r.h2x, r.h2y}};
+    const uint32_t idx[3] = {r.i0, r.i1, r.i2};
+    const float4 c[3] = {clip_v[r.i0], clip_v[r.i1], clip_v[r.i2]};
+    // SignedDistToTri + SignedDistGradToTri (cpu_raster.cpp:114-175) on the
+    // survivor's hard triangle, then GatherDistGrad's chain to clip
+    // (f_ops.cpp:1335-1349).
+    const TriDist td = signed_dist(px, py, r);
+    const float d = fabsf(td.dist);
+    if (d < 1e-6f) return;
+    const int ia = td.edge, ib = (td.edge + 1) % 3;
+    const float qx = hs[ia][0] + td.t * (hs[ib][0] - hs[ia][0]);
+    const float qy = hs[ia][1] + td.t * (hs[ib][1] - hs[ia][1]);
+    const float sgn = td.dist >= 0.f ? 1.f : -1.f;
+    const float nx = (px - qx) / d;
+    const float ny = (py - qy) / d;
+    const float ga[2] = {-sgn * (1.f - td.t) * nx, -sgn * (1.f - td.t) * ny};
+    const float gb[2] = {-sgn * td.t * nx, -sgn * td.t * ny};
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const int k = j == 0 ? ia : ib;
+        const float* gk = j == 0 ? ga : gb;
+        const float gsx = g * gk[0];
+        const float gsy = g * gk[1];
+        if (gsx == 0.f && gsy == 0.f) continue;
+        float* dst = gclip_v + size_t(idx[k]) * 4;
+        atomicAdd(dst + 0, gsx * 0.5f * W / c[k].w);
+        atomicAdd(dst + 1, gsy * 0.5f * H / c[k].w);
+        atomicAdd(dst + 3, -(gsx * 0.5f * W * c[k].x + gsy * 0.5f * H * c[k].y) /
+                                   (c[k].w * c[k].w));
+    }
+}
+
+// Sweep 2 + the silhouette loss epilogue: loss partials and the per-view
+// clip gradient (GatherDistGrad summed over pixels = its ColSum).
+__global__ void __launch_bounds__(kTileThreads)
+        k_sweep2_sil(SoftDims d, SoftBuffers b, SilParams p,
+                     const float4* clip, const float* targets, float* gclip,
+                     double* loss_slots, float4* rs_out) {
+    const int v = blockIdx.y;
+    SweepView sv{b.recs + size_t(v) * d.n_faces, d.n_faces, d.W, d.H,
+                 d.tiles_x, d.n_tiles, d.radius};
+    int x, y;
+    bool in;
+    const PixState s = sweep2_tile(sv, b.bin2, v, blockIdx.x, nullptr,
+                                   b.state, b.active, &x, &y, &in);
+    double lv = 0.0;
+    if (in) {
+        const size_t pix = size_t(v) * d.W * d.H + size_t(y) * d.W + x;
+        const bool cov = s.face >= 0;
+        const float dist = cov ? s.dist : 0.f;
+        float g;
+        lv = sil_pixel(dist, cov ? 1.f : 0.f, targets[pix], p.k, p.c, &g);
+        if (rs_out) {
+            rs_out[pix] = cov ? make_float4(s.dist, sv.recs[s.face].fid,
+                                            s.hard_z, 1.f)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (cov && g != 0.f) {
+            sil_scatter(float(x) + 0.5f, float(y) + 0.5f, g, sv.recs[s.face],
+                        clip + size_t(v) * d.n_verts, float(d.W), float(d.H),
+                        gclip + size_t(v) * d.n_verts * 4);
+        }
+    }
+    // block sum of the loss image
+    __shared__ double red[kTileThreads / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lv += __shfl_down_sync(0xffffffffu, lv, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = lv;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double sum = 0.0;
+        for (int i = 0; i < kTileThreads / 32; i++) sum += red[i];
+        atomicAdd(&loss_slots[(size_t(v) * d.n_tiles + blockIdx.x) % kLossSlots],
+                  sum);
+    }
+}
+
+// g_pos = sum_v MVP_v^T g_clip_v (TransformToClipVar's backward); zeroes
+// g_clip for the next iteration. With `update`, also applies the in-graph
+// Adam and (block 0) publishes the loss of this iteration.
+__global__ void k_gpos_adam(SilParams p, SilBuffers b, float omb1, float omb2,
+                            int do_grad, int update) {
+    const int u = blockIdx.x * blockDim.x + threadIdx.x;
+    if (blockIdx.x == 0) {
+        // reduce + clear the loss slots (written by k_sweep2_sil)
+        __shared__ double red[256];
+        double acc = 0.0;
+        for (int i = threadIdx.x; i < kLossSlots; i += blockDim.x) {
+            acc += b.loss_slots[i];
+            b.loss_slots[i] = 0.0;
+        }
+        red[threadIdx.x] = acc;
+        __syncthreads();
+        for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+            if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+            __syncthreads();
+        }
+        if (threadIdx.x == 0 && do_grad) {
+            const float loss = float(red[0]);
+            b.scalars[3] = loss;
+            const int it = int(b.scalars[0]) - 1;
+            if (b.hist_cap > 0 && it >= 0) b.loss_hist[it % b.hist_cap] = loss;
+        }
+    }
+    if (u >= p.n_verts) return;
+    float g0, g1, g2;
+    if (do_grad) {
+        g0 = g1 = g2 = 0.f;
+        for (int v = 0; v < p.views; v++) {
+            float4* gcp = reinterpret_cast<float4*>(b.gclip) + size_t(v) * p.n_verts + u;
+            const float4 gc = *gcp;
+            *gcp = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float* m = b.mvps + v * 16;
+            g0 += gc.x * m[0] + gc.y * m[1] + gc.z * m[2] + gc.w * m[3];
+            g1 += gc.x * m[4] + gc.y * m[5] + gc.z * m[6] + gc.w * m[7];
+            g2 += gc.x * m[8] + gc.y * m[9] + gc.z * m[10] + gc.w * m[11];
+        }
+        b.gpos[u * 3 + 0] = g0;
+        b.gpos[u * 3 + 1] = g1;
+        b.gpos[u * 3 + 2] = g2;
+    } else {
+        g0 = b.gpos[u * 3 + 0];
+        g1 = b.gpos[u * 3 + 1];
+        g2 = b.gpos[u * 3 + 2];
+    }
+    if (!update) return;
+    const float bc1 = b.scalars[1], bc2 = b.scalars[2];
+    const float g[3] = {g0, g1, g2};
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+        const int i = u * 3 + j;
+        const float m_new = b.adam_m[i] * p.b1 + g[j] * omb1;
+        const float v_new = b.adam_v[i] * p.b2 + g[j] * g[j] * omb2;
+        const float step = (m_new / bc1) / (sqrtf(v_new / bc2) + p.eps) * p.lr;
+        b.pos[i] = b.pos[i] - step;
+        b.adam_m[i] = m_new;
+        b.adam_v[i] = v_new;
+    }
+}
+
+static void check_launch() { DRESSI_CUDA(cudaGetLastError()); }
+
+void sil_forward_backward(const SoftDims& d, const SilParams& p,
+                          const SilBuffers& b, float* rs_out,
+                          cudaStream_t s) {
+    const dim3 vg((p.n_verts + 255) / 256, p.views);
+    {
+    ProfScope ps("transform", s);
+    k_transform<<<vg, 256, 0, s>>>(b.pos, b.mvps, p.n_verts,
+                                   reinterpret_cast<float4*>(b.clip),
+                                   b.scalars, p.b1, p.b2, 1);
+    }
+    const dim3 fg((d.n_faces + 127) / 128, d.views);
+    {
+        ProfScope ps("face_setup", s);
+        k_face_setup_sil<<<fg, 128, 0, s>>>(
+                d, reinterpret_cast<const float4*>(b.clip), b.faces, b.soft);
+    }
+    check_launch();
+    soft_bin_and_sweep1(d, b.soft, nullptr, s);
+    ProfScope ps("sweep2_sil", s);
+    k_sweep2_sil<<<dim3(d.n_tiles, d.views), kTileThreads, 0, s>>>(
+            d, b.soft, p, reinterpret_cast<const float4*>(b.clip), b.targets,
+            b.gclip, b.loss_slots, reinterpret_cast<float4*>(rs_out));
+    check_launch();
+}
+
+void sil_grad_reduce(const SilParams& p, const SilBuffers& b, bool update,
+                     cudaStream_t s) {
+    ProfScope ps("gpos_adam", s);
+    k_gpos_adam<<<(p.n_verts + 255) / 256, 256, 0, s>>>(
+            p, b, 1.f - p.b1, 1.f - p.b2, 1, update ? 1 : 0);
+    check_launch();
+}
+
+void sil_update(const SilParams& p, const SilBuffers& b, cudaStream_t s) {
+    ProfScope ps("adam", s);
+    k_gpos_adam<<<(p.n_verts + 255) / 256, 256, 0, s>>>(
+            p, b, 1.f - p.b1, 1.f - p.b2, 0, 1);
+    check_launch();
+}
+
+void sil_iteration(const SoftDims& d, const SilParams& p, const SilBuffers& b,
+                   cudaStream_t s) {
+    sil_forward_backward(d, p, b, nullptr, s);
+    sil_grad_reduce(p, b, true, s);
+}
+
+}  // namespace dressi

@@ -1,0 +1,402 @@
+// Soft rasterizer kernels (face setup, binning, sweeps) and the op-level
+// launchers for F::SoftClip, F::RasterizeSoft and its dist-channel backward.
+// See raster_soft.cuh for the exactness argument.
+#include <algorithm>
+
+#include "kernels.h"
+
+namespace dressi {
+
+// ------------------------------------------------------------- buffers
+
+void default_caps(SoftDims* d) {
+    // Sweep 1 bins each face into the tiles of its hard bbox + margin
+    // (a few tiles for the meshes of the configs); sweep 2 only into active
+    // (silhouette) tiles. Overflow is detected on the device and falls back
+    // to an exhaustive, still exact, sweep.
+    const long long f = d->n_faces;
+    const long long t = d->n_tiles;
+    d->cap1 = int(std::min<long long>(std::max<long long>(16 * f, 4 * t) + 4096,
+                                      1ll << 30));
+    d->cap2 = d->cap1;
+}
+
+void carve_soft(Arena& a, const SoftDims& d, SoftBuffers* b) {
+    const size_t vt = size_t(d.views) * d.n_tiles;
+    b->recs = a.take<FaceRec>(size_t(d.views) * std::max(d.n_faces, 1));
+    for (BinSet* bs : {&b->bin1, &b->bin2}) {
+        bs->count = a.take<int>(vt);
+        bs->offset = a.take<int>(vt);
+        bs->cursor = a.take<int>(vt);
+        bs->overflow = a.take<int>(d.views);
+    }
+    b->bin1.cap = d.cap1;
+    b->bin2.cap = d.cap2;
+    b->bin1.list = a.take<int>(size_t(d.views) * d.cap1);
+    b->bin2.list = a.take<int>(size_t(d.views) * d.cap2);
+    b->state = a.take<PixState>(size_t(d.views) * d.W * d.H);
+    b->active = a.take<int>(vt);
+    b->status = a.take<uint32_t>(4);
+}
+
+void init_soft(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
+    const size_t vt = size_t(d.views) * d.n_tiles;
+    DRESSI_CUDA(cudaMemsetAsync(b.bin1.count, 0, vt * sizeof(int), s));
+    DRESSI_CUDA(cudaMemsetAsync(b.bin2.count, 0, vt * sizeof(int), s));
+    DRESSI_CUDA(cudaMemsetAsync(b.status, 0, 4 * sizeof(uint32_t), s));
+}
+
+// ---------------------------------------------------------- face setup
+
+__device__ __forceinline__ void count_tiles(const FaceRec& r, int x0, int x1,
+                                            int y0, int y1, int* count,
+                                            int tiles_x) {
+    if (x0 > x1 || y0 > y1) return;
+    int tx0, tx1, ty0, ty1;
+    tile_range(x0, x1, y0, y1, &tx0, &tx1, &ty0, &ty1);
+    for (int ty = ty0; ty <= ty1; ty++)
+        for (int tx = tx0; tx <= tx1; tx++)
+            atomicAdd(&count[ty * tiles_x + tx], 1);
+}
+
+// Op-level face setup: explicit soft clip / face ids / faces
+// (RasterizeSoftCpu's per-face prologue, cpu_raster.cpp:260-298).
+__global__ void k_face_setup_op(SoftDims d, SoftOpInputs in, SoftBuffers b) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    const int v = blockIdx.y;
+    if (f >= d.n_faces) return;
+    FaceRec* out = b.recs + size_t(v) * d.n_faces + f;
+    const float* sc = in.soft_clip + size_t(v) * in.n_soft * 4;
+    const float* fidv = in.face_id + size_t(v) * in.n_soft;
+    const float* hc = in.hard_clip + size_t(v) * in.n_hard * 4;
+    const float W = float(d.W), H = float(d.H);
+    float ss[3][2], sz[3], fid = 0.f;
+    bool valid = true;
+    for (int k = 0; k < 3; k++) {
+        const uint32_t vi = x86_u32_via_i64(in.faces_soft[size_t(f) * 3 + k]);
+        if (vi >= uint32_t(in.n_soft)) {
+            atomicOr(b.status, kStatusIndexRange);
+            valid = false;
+            break;
+        }
+        const float* c = sc + size_t(vi) * 4;
+        if (!project_clip(c[0], c[1], c[2], c[3], W, H, &ss[k][0], &ss[k][1],
+                          &sz[k])) {
+            valid = false;
+            break;
+        }
+        fid = fidv[vi];
+    }
+    float hs[3][2], hz[3];
+    uint32_t hidx[3] = {0, 0, 0};
+    if (valid) {
+        const uint32_t hf = x86_u32_via_i64(fid + 0.5f);
+        if (hf >= uint32_t(d.n_faces)) {
+            atomicOr(b.status, kStatusIndexRange);
+            valid = false;
+        } else {
+            for (int k = 0; k < 3; k++) {
+                hidx[k] = x86_u32_via_i64(in.faces_tex[size_t(hf) * 3 + k] +
+                                          0.5f);
+                if (hidx[k] >= uint32_t(in.n_hard)) {
+                    atomicOr(b.status, kStatusIndexRange);
+                    valid = false;
+                    break;
+                }
+                const float* c = hc + size_t(hidx[k]) * 4;
+                if (!project_clip(c[0], c[1], c[2], c[3], W, H, &hs[k][0],
+                                  &hs[k][1], &hz[k])) {
+                    valid = false;
+                    break;
+                }
+            }
+        }
+    }
+    FaceRec r;
+    if (!valid || !build_record(ss, sz, hs, hz, fid, hidx, d.W, d.H, &r)) {
+        r.flags = 0;
+        *out = r;
+        return;
+    }
+    *out = r;
+    count_tiles(r, r.rx0, r.rx1, r.ry0, r.ry1,
+                b.bin1.count + size_t(v) * d.n_tiles, d.tiles_x);
+}
+
+// Sweep-1 list fill (after k_bin_scan).
+__global__ void k_bin1_fill(SoftDims d, SoftBuffers b) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    const int v = blockIdx.y;
+    if (f >= d.n_faces) return;
+    const FaceRec& r = b.recs[size_t(v) * d.n_faces + f];
+    if (!(r.flags & kFaceValid) || r.rx0 > r.rx1 || r.ry0 > r.ry1) return;
+    const bool of = b.bin1.overflow[v] != 0;
+    int tx0, tx1, ty0, ty1;
+    tile_range(r.rx0, r.rx1, r.ry0, r.ry1, &tx0, &tx1, &ty0, &ty1);
+    int* cur = b.bin1.cursor + size_t(v) * d.n_tiles;
+    int* list = b.bin1.list + size_t(v) * b.bin1.cap;
+    for (int ty = ty0; ty <= ty1; ty++)
+        for (int tx = tx0; tx <= tx1; tx++) {
+            const int slot = atomicAdd(&cur[ty * d.tiles_x + tx], 1);
+            if (!of && slot < b.bin1.cap) list[slot] = f;
+        }
+}
+
+// Does tile (tx, ty) hold a pixel of face r's soft bbox outside its sweep-1
+// region?
+__device__ __forceinline__ bool tile_has_rim(const FaceRec& r, int tx,
+                                             int ty) {
+    const int x0 = imax_(tx * kTile, r.bx0), x1 = imin_(tx * kTile + kTile - 1, r.bx1);
+    const int y0 = imax_(ty * kTile, r.by0), y1 = imin_(ty * kTile + kTile - 1, r.by1);
+    if (x0 > x1 || y0 > y1) return false;
+    const bool inside = x0 >= r.rx0 && x1 <= r.rx1 && y0 >= r.ry0 && y1 <= r.ry1;
+    return !inside;
+}
+
+template <bool kFill>
+__global__ void k_bin2(SoftDims d, SoftBuffers b) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    const int v = blockIdx.y;
+    if (f >= d.n_faces) return;
+    const FaceRec& r = b.recs[size_t(v) * d.n_faces + f];
+    const uint32_t need = kFaceValid | kFaceSafe;
+    if ((r.flags & need) != need) return;
+    int tx0, tx1, ty0, ty1;
+    tile_range(r.bx0, r.bx1, r.by0, r.by1, &tx0, &tx1, &ty0, &ty1);
+    const int* act = b.active + size_t(v) * d.n_tiles;
+    int* cnt = b.bin2.count + size_t(v) * d.n_tiles;
+    int* cur = b.bin2.cursor + size_t(v) * d.n_tiles;
+    int* list = b.bin2.list + size_t(v) * b.bin2.cap;
+    const bool of = kFill && b.bin2.overflow[v] != 0;
+    for (int ty = ty0; ty <= ty1; ty++)
+        for (int tx = tx0; tx <= tx1; tx++) {
+            const int t = ty * d.tiles_x + tx;
+            if (!act[t] || !tile_has_rim(r, tx, ty)) continue;
+            if (kFill) {
+                const int slot = atomicAdd(&cur[t], 1);
+                if (!of && slot < b.bin2.cap) list[slot] = f;
+            } else {
+                atomicAdd(&cnt[t], 1);
+            }
+        }
+}
+
+__global__ void __launch_bounds__(kTileThreads)
+        k_sweep1(SoftDims d, SoftBuffers b, const float* prev_depth) {
+    const int v = blockIdx.y;
+    SweepView sv{b.recs + size_t(v) * d.n_faces, d.n_faces, d.W, d.H,
+                 d.tiles_x, d.n_tiles, d.radius};
+    sweep1_tile(sv, b.bin1, v, blockIdx.x,
+                prev_depth ? prev_depth + size_t(v) * d.W * d.H : nullptr,
+                b.state, b.active);
+}
+
+// Sweep 2 with the plain epilogue: out = (dist, face_id, hard_z, coverage).
+__global__ void __launch_bounds__(kTileThreads)
+        k_sweep2_rs(SoftDims d, SoftBuffers b, const float* prev_depth,
+                    float4* out) {
+    const int v = blockIdx.y;
+    SweepView sv{b.recs + size_t(v) * d.n_faces, d.n_faces, d.W, d.H,
+                 d.tiles_x, d.n_tiles, d.radius};
+    int x, y;
+    bool in;
+    const PixState s = sweep2_tile(
+            sv, b.bin2, v, blockIdx.x,
+            prev_depth ? prev_depth + size_t(v) * d.W * d.H : nullptr,
+            b.state, b.active, &x, &y, &in);
+    if (!in) return;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (s.face >= 0) {
+        o.x = s.dist;
+        o.y = sv.recs[s.face].fid;
+        o.z = s.hard_z;
+        o.w = 1.f;
+    }
+    out[size_t(v) * d.W * d.H + size_t(y) * d.W + x] = o;
+}
+
+static void check_launch() { DRESSI_CUDA(cudaGetLastError()); }
+
+void soft_bin_and_sweep1(const SoftDims& d, const SoftBuffers& b,
+                         const float* prev_depth, cudaStream_t s) {
+    const dim3 fg((d.n_faces + 127) / 128, d.views);
+    {
+        ProfScope ps("bin_scan", s);
+        k_bin_scan<<<d.views, 1024, 0, s>>>(b.bin1, d.n_tiles, b.status);
+    }
+    {
+        ProfScope ps("bin1_fill", s);
+        k_bin1_fill<<<fg, 128, 0, s>>>(d, b);
+    }
+    {
+        ProfScope ps("sweep1", s);
+        k_sweep1<<<dim3(d.n_tiles, d.views), kTileThreads, 0, s>>>(
+                d, b, prev_depth);
+    }
+    {
+        ProfScope ps("bin2_count", s);
+        k_bin2<false><<<fg, 128, 0, s>>>(d, b);
+    }
+    {
+        ProfScope ps("bin_scan", s);
+        k_bin_scan<<<d.views, 1024, 0, s>>>(b.bin2, d.n_tiles, b.status);
+    }
+    {
+        ProfScope ps("bin2_fill", s);
+        k_bin2<true><<<fg, 128, 0, s>>>(d, b);
+    }
+    check_launch();
+}
+
+void soft_raster_op(const SoftDims& d, const SoftBuffers& b,
+                    const SoftOpInputs& in, float* out, cudaStream_t s) {
+    if (d.n_faces > 0) {
+        const dim3 fg((d.n_faces + 127) / 128, d.views);
+        ProfScope ps("face_setup_op", s);
+        k_face_setup_op<<<fg, 128, 0, s>>>(d, in, b);
+        check_launch();
+    }
+    soft_bin_and_sweep1(d, b, in.prev_depth, s);
+    ProfScope ps("sweep2_rs", s);
+    k_sweep2_rs<<<dim3(d.n_tiles, d.views), kTileThreads, 0, s>>>(
+            d, b, in.prev_depth, reinterpret_cast<float4*>(out));
+    check_launch();
+}
+
+// ------------------------------------------------- dist-channel backward
+
+// SignedDistGradToTri (cpu_raster.cpp:153-175) + GatherDistGrad's
+// screen->clip chain (f_ops.cpp:1335-1349). `c` are the clip vertices.
+__device__ __forceinline__ void dist_grad_scatter(
+        float px, float py, float g, const float hs[3][2], const float4 c[3],
+        const uint32_t idx[3], float W, float H, float* grad /*[V][4]*/) {
+    // SignedDistToTri over the hard triangle, then the envelope gradient.
+    FaceRec r;
+    r.h0x = hs[0][0]; r.h0y = hs[0][1];
+    r.h1x = hs[1][0]; r.h1y = hs[1][1];
+    r.h2x = hs[2][0]; r.h2y = hs[2][1];
+    r.ex0 = hs[1][0] - hs[0][0]; r.ey0 = hs[1][1] - hs[0][1];
+    r.ex1 = hs[2][0] - hs[1][0]; r.ey1 = hs[2][1] - hs[1][1];
+    r.ex2 = hs[0][0] - hs[2][0]; r.ey2 = hs[0][1] - hs[2][1];
+    r.len2_0 = r.ex0 * r.ex0 + r.ey0 * r.ey0;
+    r.len2_1 = r.ex1 * r.ex1 + r.ey1 * r.ey1;
+    r.len2_2 = r.ex2 * r.ex2 + r.ey2 * r.ey2;
+    const TriDist td = signed_dist(px, py, r);
+    const float d = fabsf(td.dist);
+    if (d < 1e-6f) return;
+    const int ia = td.edge, ib = (td.edge + 1) % 3;
+    const float qx = hs[ia][0] + td.t * (hs[ib][0] - hs[ia][0]);
+    const float qy = hs[ia][1] + td.t * (hs[ib][1] - hs[ia][1]);
+    const float sgn = td.dist >= 0.f ? 1.f : -1.f;
+    const float nx = (px - qx) / d;
+    const float ny = (py - qy) / d;
+    float gs[3][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+    gs[ia][0] = -sgn * (1.f - td.t) * nx;
+    gs[ia][1] = -sgn * (1.f - td.t) * ny;
+    gs[ib][0] = -sgn * td.t * nx;
+    gs[ib][1] = -sgn * td.t * ny;
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        const float gsx = g * gs[k][0];
+        const float gsy = g * gs[k][1];
+        if (gsx == 0.f && gsy == 0.f) continue;
+        float* dst = grad + size_t(idx[k]) * 4;
+        atomicAdd(dst + 0, gsx * 0.5f * W / c[k].w);
+        atomicAdd(dst + 1, gsy * 0.5f * H / c[k].w);
+        atomicAdd(dst + 3, -(gsx * 0.5f * W * c[k].x + gsy * 0.5f * H * c[k].y) /
+                                   (c[k].w * c[k].w));
+    }
+}
+
+__global__ void k_dist_grad(const float* gy, const float4* rs,
+                            const float4* clip, const float* faces,
+                            int n_verts, int n_faces, int W, int H,
+                            float* grad, uint32_t* status) {
+    const int v = blockIdx.y;
+    const size_t npx = size_t(W) * H;
+    for (size_t p = size_t(blockIdx.x) * blockDim.x + threadIdx.x; p < npx;
+         p += size_t(gridDim.x) * blockDim.x) {
+        const float4 o = rs[v * npx + p];
+        if (o.w < 0.5f) continue;
+        const float g = gy[v * npx + p];
+        if (g == 0.f) continue;
+        const uint32_t f = x86_u32_via_i64(o.y + 0.5f);
+        if (f >= uint32_t(n_faces)) {
+            atomicOr(status, kStatusIndexRange);
+            continue;
+        }
+        uint32_t idx[3];
+        float hs[3][2];
+        float4 c[3];
+        bool valid = true;
+        for (int k = 0; k < 3; k++) {
+            idx[k] = x86_u32_via_i64(faces[size_t(f) * 3 + k] + 0.5f);
+            if (idx[k] >= uint32_t(n_verts)) {
+                atomicOr(status, kStatusIndexRange);
+                valid = false;
+                break;
+            }
+            c[k] = clip[size_t(v) * n_verts + idx[k]];
+            float z;
+            if (!project_clip(c[k].x, c[k].y, c[k].z, c[k].w, float(W),
+                              float(H), &hs[k][0], &hs[k][1], &z)) {
+                valid = false;
+                break;
+            }
+        }
+        if (!valid) continue;
+        const int y = int(p / W), x = int(p % W);
+        dist_grad_scatter(float(x) + 0.5f, float(y) + 0.5f, g, hs, c, idx,
+                          float(W), float(H),
+                          grad + size_t(v) * n_verts * 4);
+    }
+}
+
+void dist_grad_op(const float* gy, const float* rs, const float* clip,
+                  const float* faces, int views, int n_verts, int n_faces,
+                  int W, int H, float* grad, uint32_t* status,
+                  cudaStream_t s) {
+    const size_t npx = size_t(W) * H;
+    const int blocks = int(std::min<size_t>((npx + 255) / 256, 4096));
+    k_dist_grad<<<dim3(blocks, views), 256, 0, s>>>(
+            gy, reinterpret_cast<const float4*>(rs),
+            reinterpret_cast<const float4*>(clip), faces, n_verts, n_faces, W,
+            H, grad, status);
+    check_launch();
+}
+
+// ----------------------------------------------------------- SoftClip op
+
+__global__ void k_soft_clip(const float4* clip, const float* faces, int views,
+                            int n_verts, int n_faces, float W, float H,
+                            float radius, float4* out, uint32_t* status) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    const int v = blockIdx.y;
+    if (f >= n_faces) return;
+    float4 c[3], o[3];
+    for (int k = 0; k < 3; k++) {
+        const uint32_t i = x86_u32_via_i64(faces[size_t(f) * 3 + k] + 0.5f);
+        if (i >= uint32_t(n_verts)) {
+            atomicOr(status, kStatusIndexRange);
+            for (int j = 0; j < 3; j++)
+                out[(size_t(v) * n_faces + f) * 3 + j] = make_float4(0, 0, 0, 0);
+            return;
+        }
+        c[k] = clip[size_t(v) * n_verts + i];
+    }
+    soft_clip_face(c, W, H, radius, o);
+    for (int k = 0; k < 3; k++) out[(size_t(v) * n_faces + f) * 3 + k] = o[k];
+}
+
+void soft_clip_op(const float* clip, const float* faces, int views,
+                  int n_verts, int n_faces, int W, int H, float radius,
+                  float* out, uint32_t* status, cudaStream_t s) {
+    if (n_faces == 0) return;
+    k_soft_clip<<<dim3((n_faces + 127) / 128, views), 128, 0, s>>>(
+            reinterpret_cast<const float4*>(clip), faces, views, n_verts,
+            n_faces, float(W), float(H), radius, reinterpret_cast<float4*>(out),
+            status);
+    check_launch();
+}
+
+}  // namespace dressi

@@ -1,0 +1,199 @@
+"""Op-level entry points on torch CUDA tensors (zero-copy; current stream).
+
+Each function mirrors one reference op (src/core/f_ops.cpp) and calls the
+C ABI with raw device pointers. Inputs are float32 CUDA tensors in the
+reference layouts; views are stacked along a leading dimension.
+
+Errors the reference raises as DressiError (bad shapes, and -- through the
+device status word -- out-of-range indices) raise DressiError here.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _native as N
+
+__all__ = [
+    "soft_clip",
+    "rasterize_soft",
+    "rasterize_soft_grad",
+    "rasterize_face_id",
+    "rasterize",
+    "check_status",
+]
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dev(t: torch.Tensor, name: str, ndim: int | None = None) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise N.DressiError(N.ERR_INVALID, f"{name} must be a CUDA tensor")
+    if t.dtype != torch.float32:
+        raise N.DressiError(N.ERR_INVALID, f"{name} must be float32")
+    if ndim is not None and t.dim() != ndim:
+        raise N.DressiError(N.ERR_INVALID,
+                            f"{name} must have {ndim} dims, got {t.dim()}")
+    return t.contiguous()
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _new_status(device):
+    return torch.zeros(1, dtype=torch.int32, device=device)
+
+
+def check_status(status: torch.Tensor) -> int:
+    """Synchronises and raises if a kernel reported an index error."""
+    word = int(status.item()) & 0xFFFFFFFF
+    if word & N.STATUS_INDEX_RANGE:
+        raise N.DressiError(N.ERR_DEVICE,
+                            "index out of range (face or vertex id)")
+    return word
+
+
+def _views(t: torch.Tensor, base_dims: int) -> tuple[torch.Tensor, int]:
+    """Adds a leading view dimension when absent."""
+    if t.dim() == base_dims:
+        return t.unsqueeze(0), 1
+    return t, t.shape[0]
+
+
+def _match_views(t: torch.Tensor, views: int, name: str) -> torch.Tensor:
+    """Broadcasts a single-view input over `views`; rejects other counts."""
+    if t.shape[0] == views:
+        return t
+    if t.shape[0] == 1:
+        return t.expand(views, *t.shape[1:]).contiguous()
+    raise N.DressiError(N.ERR_INVALID, f"{name}: {t.shape[0]} views, "
+                        f"expected {views}")
+
+
+def soft_clip(clip, faces, width: int, height: int, radius_px: float,
+              check: bool = True):
+    """F::SoftClip: clip [(views,) V, 4], faces [F, 3] -> [(views,) 3F, 4]."""
+    squeeze = clip.dim() == 2
+    clip = _dev(clip, "clip")
+    faces = _dev(faces, "faces", 2)
+    clip, views = _views(clip, 2)
+    n_faces = faces.shape[0]
+    out = torch.empty((views, 3 * n_faces, 4), dtype=torch.float32,
+                      device=clip.device)
+    st = _new_status(clip.device)
+    N.call("dressi_soft_clip", clip.data_ptr(), clip.shape[1],
+           faces.data_ptr(), n_faces, views, width, height, float(radius_px),
+           out.data_ptr(), st.data_ptr(), _stream())
+    if check:
+        check_status(st)
+    return out[0] if squeeze else out
+
+
+def rasterize_soft(soft_clip, face_id, faces_soft, hard_clip, faces_tex,
+                   width: int, height: int, radius_px: float,
+                   prev_depth=None, check: bool = True):
+    """F::RasterizeSoft -> [(views,) H, W, 4] (dist, face_id, hard_z, cov).
+
+    soft_clip [(views,) 3F, 4], face_id [(views,) 3F], faces_soft [F, 3],
+    hard_clip [(views,) V, 4], faces_tex [F, 3], prev_depth [(views,) H, W]
+    (depth-peeling variant) or None."""
+    squeeze = soft_clip.dim() == 2
+    soft_clip = _dev(soft_clip, "soft_clip")
+    face_id = _dev(face_id, "face_id")
+    hard_clip = _dev(hard_clip, "hard_clip")
+    faces_soft = _dev(faces_soft, "faces_soft", 2)
+    faces_tex = _dev(faces_tex, "faces_tex", 2)
+    soft_clip, views = _views(soft_clip, 2)
+    face_id, _ = _views(face_id, 1)
+    hard_clip, _ = _views(hard_clip, 2)
+    if prev_depth is not None:
+        prev_depth = _dev(prev_depth, "prev_depth")
+        prev_depth, _ = _views(prev_depth, 2)
+    n_faces = faces_soft.shape[0]
+    face_id = _match_views(face_id, views, "face_id")
+    hard_clip = _match_views(hard_clip, views, "hard_clip")
+    if prev_depth is not None:
+        prev_depth = _match_views(prev_depth, views, "prev_depth")
+    out = torch.empty((views, height, width, 4), dtype=torch.float32,
+                      device=soft_clip.device)
+    st = _new_status(soft_clip.device)
+    N.call("dressi_rasterize_soft", soft_clip.data_ptr(), soft_clip.shape[1],
+           face_id.data_ptr(), faces_soft.data_ptr(), n_faces,
+           hard_clip.data_ptr(), hard_clip.shape[1], faces_tex.data_ptr(),
+           views, width, height, float(radius_px), _ptr(prev_depth),
+           out.data_ptr(), st.data_ptr(), _stream())
+    if check:
+        check_status(st)
+    return out[0] if squeeze else out
+
+
+def rasterize_soft_grad(gy, rs, clip, faces, check: bool = True):
+    """ColSum(GatherDistGrad): d(sum gy*dist)/d clip -> [(views,) V, 4]."""
+    squeeze = clip.dim() == 2
+    gy = _dev(gy, "gy")
+    rs = _dev(rs, "rs")
+    clip = _dev(clip, "clip")
+    faces = _dev(faces, "faces", 2)
+    gy, views = _views(gy, 2)
+    rs, _ = _views(rs, 3)
+    clip, _ = _views(clip, 2)
+    rs = _match_views(rs, views, "rs")
+    clip = _match_views(clip, views, "clip")
+    h, w = gy.shape[1], gy.shape[2]
+    grad = torch.zeros((views, clip.shape[1], 4), dtype=torch.float32,
+                       device=clip.device)
+    st = _new_status(clip.device)
+    N.call("dressi_rasterize_soft_grad", gy.data_ptr(), rs.data_ptr(),
+           clip.data_ptr(), clip.shape[1], faces.data_ptr(), faces.shape[0],
+           views, w, h, grad.data_ptr(), st.data_ptr(), _stream())
+    if check:
+        check_status(st)
+    return grad[0] if squeeze else grad
+
+
+def rasterize_face_id(clip, faces, width: int, height: int,
+                      with_depth: bool = False, check: bool = True):
+    """F::RasterizeFaceId -> [(views,) H, W] float(face)+1, 0 background."""
+    squeeze = clip.dim() == 2
+    clip = _dev(clip, "clip")
+    faces = _dev(faces, "faces", 2)
+    clip, views = _views(clip, 2)
+    out = torch.empty((views, height, width), dtype=torch.float32,
+                      device=clip.device)
+    depth = torch.empty_like(out) if with_depth else None
+    st = _new_status(clip.device)
+    N.call("dressi_rasterize_face_id", clip.data_ptr(), clip.shape[1],
+           faces.data_ptr(), faces.shape[0], views, width, height,
+           out.data_ptr(), _ptr(depth), st.data_ptr(), _stream())
+    if check:
+        check_status(st)
+    if squeeze:
+        out = out[0]
+        depth = depth[0] if depth is not None else None
+    return (out, depth) if with_depth else out
+
+
+def rasterize(clip, attr, faces, width: int, height: int, check: bool = True):
+    """F::Rasterize -> [(views,) H, W, C] perspective-correct attribute."""
+    squeeze = clip.dim() == 2
+    clip = _dev(clip, "clip")
+    attr = _dev(attr, "attr")
+    faces = _dev(faces, "faces", 2)
+    clip, views = _views(clip, 2)
+    if attr.dim() == 1:
+        attr = attr.unsqueeze(-1)
+    attr, _ = _views(attr, 2)
+    attr = _match_views(attr, views, "attr")
+    n_comp = attr.shape[-1]
+    out = torch.empty((views, height, width, n_comp), dtype=torch.float32,
+                      device=clip.device)
+    st = _new_status(clip.device)
+    N.call("dressi_rasterize", clip.data_ptr(), clip.shape[1],
+           attr.data_ptr(), n_comp, faces.data_ptr(), faces.shape[0], views,
+           width, height, out.data_ptr(), st.data_ptr(), _stream())
+    if check:
+        check_status(st)
+    return out[0] if squeeze else out

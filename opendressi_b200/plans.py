@@ -1,0 +1,210 @@
+"""Fused fwd + bwd + Adam iterations resident on one device (CUDA graphs).
+
+``SilhouettePlan`` is the HardSoftRas silhouette optimisation (configs
+C3/C4), ``ImageFitPlan`` the 2-D image fit (C1). Both hold every buffer of
+the iteration on the device; ``step(n)`` replays the captured iteration n
+times with no host traffic, like the reference's DressiAD::execStep replaying
+one recorded command buffer (src/dressi_ad.cpp:461-480).
+
+State access mirrors DressiAD::sendImg / recvImg (include/dressi/
+dressi_ad.h:114-131): ``upload(slot, array)`` / ``download(slot)`` take host
+numpy arrays or CUDA tensors.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import _native as N
+
+__all__ = ["Plan", "SilhouettePlan", "ImageFitPlan"]
+
+
+def _stream_ptr(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+class Plan:
+    """Owns a dressi_plan handle."""
+
+    def __init__(self, handle, device: int):
+        self._h = handle
+        self.device = device
+
+    # -- lifetime -----------------------------------------------------------
+    def close(self):
+        if self._h:
+            N.call("dressi_plan_destroy", self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # -- slots --------------------------------------------------------------
+    def slot_bytes(self, slot: int) -> int:
+        n = C.c_size_t(0)
+        N.call("dressi_plan_slot_bytes", self._h, slot, C.byref(n))
+        return n.value
+
+    def slot_tensor(self, slot: int, shape=None) -> torch.Tensor:
+        """Zero-copy CUDA tensor view of a resident slot (float32)."""
+        ptr = C.c_void_p(0)
+        N.call("dressi_plan_slot_ptr", self._h, slot, C.byref(ptr))
+        n = self.slot_bytes(slot) // 4
+        shape = tuple(shape) if shape is not None else (n,)
+
+        class _Iface:
+            __cuda_array_interface__ = {
+                "shape": shape, "typestr": "<f4",
+                "data": (ptr.value, False), "version": 3, "strides": None,
+            }
+
+        with torch.cuda.device(self.device):
+            return torch.as_tensor(_Iface(), device=f"cuda:{self.device}")
+
+    def upload(self, slot: int, data, stream=None):
+        if isinstance(data, torch.Tensor) and data.is_cuda:
+            t = data.detach().to(torch.float32).contiguous()
+            N.call("dressi_plan_upload", self._h, slot, t.data_ptr(),
+                   t.numel() * 4, 1, _stream_ptr(stream))
+            return
+        a = np.ascontiguousarray(
+            data.cpu().numpy() if isinstance(data, torch.Tensor) else data,
+            dtype=np.float32)
+        N.call("dressi_plan_upload", self._h, slot, a.ctypes.data, a.nbytes,
+               0, _stream_ptr(stream))
+        torch.cuda.current_stream().synchronize() if stream is None else \
+            stream.synchronize()
+
+    def download(self, slot: int, out=None, stream=None):
+        n = self.slot_bytes(slot)
+        if isinstance(out, torch.Tensor) and out.is_cuda:
+            N.call("dressi_plan_download", self._h, slot, out.data_ptr(), n,
+                   1, _stream_ptr(stream))
+            return out
+        a = out if out is not None else np.empty(n // 4, np.float32)
+        N.call("dressi_plan_download", self._h, slot, a.ctypes.data, n, 0,
+               _stream_ptr(stream))
+        (stream or torch.cuda.current_stream()).synchronize()
+        return a
+
+    # -- execution ----------------------------------------------------------
+    def step(self, n_iters: int = 1, stream=None):
+        N.call("dressi_plan_exec", self._h, int(n_iters), _stream_ptr(stream))
+
+    def status(self, stream=None) -> int:
+        w = C.c_uint32(0)
+        N.call("dressi_plan_status", self._h, C.byref(w), _stream_ptr(stream))
+        return w.value
+
+    def launches_per_iter(self) -> int:
+        n = C.c_uint32(0)
+        N.call("dressi_plan_launches_per_iter", self._h, C.byref(n))
+        return n.value
+
+    def profile(self, n_iters: int = 5, stream=None) -> list[dict]:
+        """Per-kernel CUDA-event timing of n_iters un-graphed iterations:
+        [{"name", "total_ms", "launches", "avg_ms"}] in launch order."""
+        cap = 64
+        names = (C.c_char_p * cap)()
+        ms = (C.c_float * cap)()
+        cnt = (C.c_uint32 * cap)()
+        n = C.c_uint32(0)
+        N.call("dressi_plan_profile", self._h, int(n_iters),
+               _stream_ptr(stream), cap, names, ms, cnt, C.byref(n))
+        out = []
+        for i in range(min(n.value, cap)):
+            out.append({"name": names[i].decode(), "total_ms": float(ms[i]),
+                        "launches": int(cnt[i]),
+                        "avg_ms": float(ms[i]) / max(1, int(cnt[i]))})
+        return out
+
+    def loss(self) -> float:
+        return float(self.download(N.SLOT_LOSS)[0])
+
+    def loss_history(self, n: int) -> np.ndarray:
+        """Losses of the first n iterations (ring of 4096 by default)."""
+        return self.download(N.SLOT_LOSS_HISTORY)[:n].copy()
+
+
+class SilhouettePlan(Plan):
+    """C3/C4 silhouette optimisation of vertex positions (HardSoftRas)."""
+
+    def __init__(self, faces, mvps, n_verts: int, res: int, radius_px: float,
+                 sigma: float = 1e-4, lr: float = 1e-3, beta1: float = 0.9,
+                 beta2: float = 0.999, eps: float = 1e-8, device: int = 0,
+                 loss_history: int = 4096):
+        faces = np.ascontiguousarray(faces, np.float32).reshape(-1, 3)
+        mvps = np.ascontiguousarray(mvps, np.float32).reshape(-1, 16)
+        self.n_verts, self.n_faces = int(n_verts), faces.shape[0]
+        self.n_views, self.res = mvps.shape[0], int(res)
+        d = N.SilhouetteDesc()
+        d.struct_size = C.sizeof(N.SilhouetteDesc)
+        d.n_verts, d.n_faces = self.n_verts, self.n_faces
+        d.n_views, d.res = self.n_views, self.res
+        d.radius_px, d.sigma, d.lr = radius_px, sigma, lr
+        d.beta1, d.beta2, d.eps = beta1, beta2, eps
+        d.faces = faces.ctypes.data_as(C.POINTER(C.c_float))
+        d.mvps = mvps.ctypes.data_as(C.POINTER(C.c_float))
+        d.loss_history = loss_history
+        d.device = device
+        h = C.c_void_p(0)
+        N.call("dressi_silhouette_plan_create", C.byref(d), C.byref(h))
+        super().__init__(h, device)
+
+    @classmethod
+    def from_scene(cls, scene, device: int = 0, views=None, **kw):
+        mvps = scene.mvps if views is None else scene.mvps[views]
+        return cls(scene.faces_f, mvps, scene.n_verts, scene.res,
+                   scene.radius_px, sigma=scene.sigma, lr=scene.lr,
+                   device=device, **kw)
+
+    def render_targets(self, target_pos, stream=None):
+        tp = np.ascontiguousarray(target_pos, np.float32)
+        N.call("dressi_plan_render_targets", self._h,
+               tp.ctypes.data_as(C.POINTER(C.c_float)), _stream_ptr(stream))
+
+    def render(self, stream=None) -> torch.Tensor:
+        """RasterizeSoft images of the current positions [views, R, R, 4]."""
+        N.call("dressi_plan_render", self._h, _stream_ptr(stream))
+        return self.slot_tensor(N.SLOT_RASTER,
+                                (self.n_views, self.res, self.res, 4)).clone()
+
+    def forward_backward(self, stream=None):
+        """Phase 0 of a sharded iteration: local gradient into GRAD."""
+        N.call("dressi_plan_exec_phase", self._h, 0, _stream_ptr(stream))
+
+    def apply_update(self, stream=None):
+        """Phase 1: Adam from the (all-reduced) GRAD slot."""
+        N.call("dressi_plan_exec_phase", self._h, 1, _stream_ptr(stream))
+
+    def grad_tensor(self) -> torch.Tensor:
+        return self.slot_tensor(N.SLOT_GRAD, (self.n_verts, 3))
+
+    def loss_tensor(self) -> torch.Tensor:
+        return self.slot_tensor(N.SLOT_LOSS, (1,))
+
+
+class ImageFitPlan(Plan):
+    """C1 image fitting: Mean((param - target)^2) + Adam, one fused pass."""
+
+    def __init__(self, width: int, height: int, lr: float = 1e-2,
+                 device: int = 0):
+        h = C.c_void_p(0)
+        N.call("dressi_image_fit_plan_create", width, height, float(lr),
+               device, C.byref(h))
+        self.width, self.height = width, height
+        super().__init__(h, device)

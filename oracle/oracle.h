@@ -1,0 +1,112 @@
+/*
+ * TEST INFRASTRUCTURE ONLY -- the CPU checker for opendressi_b200.
+ *
+ * A plain-C restatement of the reference (unclearness/opendressi) CPU
+ * algorithms on the Dressi-AD silhouette hot path. Each function cites the
+ * reference file:line it follows. Only tests/, __graft_entry__.smoke() and
+ * bench.py's cpu_baseline / reference arm may load liboracle.so; the product
+ * path never calls it.
+ *
+ * Pinned against: (1) the reference's own known-answer tests, re-expressed
+ * in tests/test_oracle.py (tests/test_softras.cpp:92-137,
+ * tests/test_cpu_eval.cpp:310-474 of the reference), and (2) the compiled
+ * reference itself (oracle/_ref, ref_driver.cpp) on seeded random scenes,
+ * bit-exact for raster outputs; see tests/golden/make_golden.py.
+ *
+ * Conventions (reference src/core/cpu_raster.h:8-13): screen =
+ * (clip.xy / clip.w * 0.5 + 0.5) * (W, H), row 0 on top, pixel centres at
+ * +0.5, depth = clip.z / clip.w in [0, 1]. Images are row-major with
+ * interleaved components. Index arrays ("faces") are float-valued, as in
+ * the reference's image leaves.
+ */
+#ifndef DRESSI_ORACLE_H
+#define DRESSI_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Error text of the last failing call on this thread. */
+const char* orc_last_error(void);
+
+/* F::SoftClip -> out[3F*4] (f_ops.cpp:1890-1981). */
+int orc_soft_clip(const float* clip, uint32_t n_verts, const float* faces,
+                  uint32_t n_faces, uint32_t w, uint32_t h, float radius,
+                  float* out);
+
+/* RasterizeSoftCpu -> out[W*H*4] = (dist_px, face_id, hard_z, coverage)
+ * (cpu_raster.cpp:241-355). prev_depth (nullable) = depth-peeling input. */
+int orc_rasterize_soft(const float* soft_clip, uint32_t n_soft,
+                       const float* face_id, const float* faces_soft,
+                       uint32_t n_faces, const float* hard_clip,
+                       uint32_t n_hard, const float* faces_tex, uint32_t w,
+                       uint32_t h, float radius, const float* prev_depth,
+                       float* out);
+
+/* RasterizeFaceIdCpu -> out[W*H] (cpu_raster.cpp:357-369). */
+int orc_rasterize_face_id(const float* clip, uint32_t n_verts,
+                          const float* faces, uint32_t n_faces, uint32_t w,
+                          uint32_t h, float* out);
+
+/* RasterizeHardCpu -> out[W*H*n_comp] (cpu_raster.cpp:195-225). */
+int orc_rasterize_hard(const float* clip, uint32_t n_verts, const float* attr,
+                       uint32_t n_comp, const float* faces, uint32_t n_faces,
+                       uint32_t w, uint32_t h, float* out);
+
+/* ColSum(GatherDistGrad(gy, rs, clip, faces, vft)) -> grad[V*4]: the
+ * gradient of sum_px gy(px)*dist(px) w.r.t. the hard clip positions
+ * (f_ops.cpp:1248-1358 with ColSum 1218-1246). gy is W*H (the dist
+ * channel's incoming gradient), rs the RasterizeSoft output. */
+int orc_dist_grad(const float* gy, const float* rs, const float* clip,
+                  uint32_t n_verts, const float* faces, uint32_t n_faces,
+                  uint32_t w, uint32_t h, float* grad);
+
+/* Clip transform (examples/common/geometry_utils.cpp:391-402):
+ * clip[V*4] = rows x*m[r] + y*m[4+r] + z*m[8+r] + m[12+r]. */
+void orc_transform_clip(const float* pos, uint32_t n_verts, const float* mvp,
+                        float* clip);
+
+/* One silhouette iteration's loss and position gradient (no update): the
+ * graph of ref_driver.cpp's SilViewLoss summed over views. Returns the loss
+ * (sum over pixels and views) in *loss; grad[V*3]. rs_out (nullable) gets
+ * n_views*W*W*4 raster outputs. */
+int orc_silhouette_loss_grad(const float* pos, uint32_t n_verts,
+                             const float* faces, uint32_t n_faces,
+                             uint32_t n_views, uint32_t res, float radius,
+                             float sigma, const float* mvps,
+                             const float* targets, double* loss, float* grad,
+                             float* rs_out);
+
+/* In-graph Adam of examples/silhouette_optimization/run.cpp:421-436, one
+ * step over n params; t is the counter BEFORE the step (updated in place). */
+void orc_adam(float* param, float* m, float* v, float* t, const float* grad,
+              uint32_t n, float lr, float b1, float b2, float eps);
+
+/* Full silhouette run: n_iters of loss/grad + Adam (lr, 0.9, 0.999, 1e-8).
+ * loss_trace[n_iters]; pos updated in place. threads > 1 evaluates views
+ * on that many threads (gradients summed in view order). */
+int orc_silhouette_run(float* pos, uint32_t n_verts, const float* faces,
+                       uint32_t n_faces, uint32_t n_views, uint32_t res,
+                       float radius, float sigma, float lr, const float* mvps,
+                       const float* targets, uint32_t n_iters,
+                       uint32_t threads, float* loss_trace);
+
+/* 2-D image fitting (C1): loss = Mean((p - t)^2) over W*H*4, Adam on p.
+ * loss_trace[n_iters] = loss at the start of each iteration. */
+int orc_image_fit_run(float* param, const float* target, uint32_t w,
+                      uint32_t h, float lr, uint32_t n_iters,
+                      float* loss_trace);
+
+/* VertexFacesTex (mesh_utils.cpp:53-69): out[V*cap] row-major {V,max_deg},
+ * -1 padding; *max_deg set. Nonzero if cap is too small. */
+int orc_vertex_faces_tex(const float* faces, uint32_t n_faces,
+                         uint32_t n_verts, uint32_t cap, float* out,
+                         uint32_t* max_deg);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DRESSI_ORACLE_H */

@@ -1,0 +1,290 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes bindings of the CPU checkers.
+
+``Port`` wraps liboracle.so (this repository's C restatement, oracle.c);
+``Ref`` wraps _ref/libdressi_ref.so (the unmodified reference CPU code built
+in place by oracle/Makefile plus ref_driver.cpp). Only tests/,
+__graft_entry__.smoke() and bench.py's CPU-baseline / reference arm import
+this module.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PORT_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libdressi_ref.so")
+
+_f32p = C.POINTER(C.c_float)
+_u32 = C.c_uint32
+
+
+def _fp(a):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_f32p)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def build_port() -> str:
+    subprocess.run(["make", "-s", "-C", HERE, "port"], check=True)
+    return PORT_SO
+
+
+def build_ref(ref_dir: str = "/root/reference") -> str | None:
+    """Builds _ref/libdressi_ref.so when the reference checkout exists."""
+    if not os.path.isdir(os.path.join(ref_dir, "src", "core")):
+        return REF_SO if os.path.exists(REF_SO) else None
+    subprocess.run(["make", "-s", "-j8", "-C", HERE, "ref",
+                    f"REF_DIR={ref_dir}"], check=True)
+    return REF_SO
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+class _Lib:
+    prefix = ""
+
+    def __init__(self, path):
+        self.lib = C.CDLL(path)
+        p = self.prefix
+        L = self.lib
+        getattr(L, p + "last_error").restype = C.c_char_p
+
+    def _err(self, rc, what):
+        if rc != 0:
+            msg = getattr(self.lib, self.prefix + "last_error")().decode()
+            raise RuntimeError(f"{what}: {msg}")
+
+
+class Port(_Lib):
+    """liboracle.so -- the C restatement."""
+
+    prefix = "orc_"
+
+    def __init__(self, path=None):
+        if path is None:
+            path = PORT_SO
+            if not os.path.exists(path):
+                build_port()
+        super().__init__(path)
+
+    def soft_clip(self, clip, faces, w, h, radius):
+        clip, faces = _f32(clip), _f32(faces)
+        out = np.zeros((faces.shape[0] * 3, 4), np.float32)
+        self._err(self.lib.orc_soft_clip(_fp(clip), _u32(clip.shape[0]),
+                                         _fp(faces), _u32(faces.shape[0]),
+                                         _u32(w), _u32(h), C.c_float(radius),
+                                         _fp(out)), "soft_clip")
+        return out
+
+    def rasterize_soft(self, soft_clip, face_id, faces_soft, hard_clip,
+                       faces_tex, w, h, radius, prev_depth=None):
+        soft_clip, face_id, faces_soft = map(_f32, (soft_clip, face_id,
+                                                    faces_soft))
+        hard_clip, faces_tex = _f32(hard_clip), _f32(faces_tex)
+        pd = None if prev_depth is None else _f32(prev_depth)
+        out = np.zeros((h, w, 4), np.float32)
+        self._err(self.lib.orc_rasterize_soft(
+            _fp(soft_clip), _u32(soft_clip.shape[0]), _fp(face_id),
+            _fp(faces_soft), _u32(faces_soft.shape[0]), _fp(hard_clip),
+            _u32(hard_clip.shape[0]), _fp(faces_tex), _u32(w), _u32(h),
+            C.c_float(radius), _fp(pd), _fp(out)), "rasterize_soft")
+        return out
+
+    def rasterize_face_id(self, clip, faces, w, h):
+        clip, faces = _f32(clip), _f32(faces)
+        out = np.zeros((h, w), np.float32)
+        self._err(self.lib.orc_rasterize_face_id(
+            _fp(clip), _u32(clip.shape[0]), _fp(faces), _u32(faces.shape[0]),
+            _u32(w), _u32(h), _fp(out)), "rasterize_face_id")
+        return out
+
+    def rasterize_hard(self, clip, attr, faces, w, h):
+        clip, faces = _f32(clip), _f32(faces)
+        attr = _f32(attr)
+        nc = 1 if attr.ndim == 1 else attr.shape[1]
+        out = np.zeros((h, w, nc), np.float32)
+        self._err(self.lib.orc_rasterize_hard(
+            _fp(clip), _u32(clip.shape[0]), _fp(attr), _u32(nc), _fp(faces),
+            _u32(faces.shape[0]), _u32(w), _u32(h), _fp(out)),
+            "rasterize_hard")
+        return out
+
+    def dist_grad(self, gy, rs, clip, faces, w, h):
+        gy, rs, clip, faces = map(_f32, (gy, rs, clip, faces))
+        out = np.zeros((clip.shape[0], 4), np.float32)
+        self._err(self.lib.orc_dist_grad(
+            _fp(gy), _fp(rs), _fp(clip), _u32(clip.shape[0]), _fp(faces),
+            _u32(faces.shape[0]), _u32(w), _u32(h), _fp(out)), "dist_grad")
+        return out
+
+    def transform_clip(self, pos, mvp):
+        pos, mvp = _f32(pos), _f32(mvp)
+        out = np.zeros((pos.shape[0], 4), np.float32)
+        self.lib.orc_transform_clip(_fp(pos), _u32(pos.shape[0]), _fp(mvp),
+                                    _fp(out))
+        return out
+
+    def silhouette_loss_grad(self, pos, faces, mvps, targets, res, radius,
+                             sigma, want_rs=False):
+        pos, faces, mvps, targets = map(_f32, (pos, faces, mvps, targets))
+        nv = mvps.shape[0]
+        grad = np.zeros_like(pos)
+        loss = C.c_double(0.0)
+        rs = np.zeros((nv, res, res, 4), np.float32) if want_rs else None
+        self._err(self.lib.orc_silhouette_loss_grad(
+            _fp(pos), _u32(pos.shape[0]), _fp(faces), _u32(faces.shape[0]),
+            _u32(nv), _u32(res), C.c_float(radius), C.c_float(sigma),
+            _fp(mvps), _fp(targets), C.byref(loss), _fp(grad), _fp(rs)),
+            "silhouette_loss_grad")
+        return loss.value, grad, rs
+
+    def silhouette_run(self, pos, faces, mvps, targets, res, radius, sigma,
+                       lr, n_iters, threads=1):
+        pos = _f32(pos).copy()
+        faces, mvps, targets = map(_f32, (faces, mvps, targets))
+        trace = np.zeros(n_iters, np.float32)
+        self._err(self.lib.orc_silhouette_run(
+            _fp(pos), _u32(pos.shape[0]), _fp(faces), _u32(faces.shape[0]),
+            _u32(mvps.shape[0]), _u32(res), C.c_float(radius),
+            C.c_float(sigma), C.c_float(lr), _fp(mvps), _fp(targets),
+            _u32(n_iters), _u32(threads), _fp(trace)), "silhouette_run")
+        return trace, pos
+
+    def image_fit_run(self, param, target, lr, n_iters):
+        param = _f32(param).copy()
+        target = _f32(target)
+        h, w = param.shape[:2]
+        trace = np.zeros(n_iters, np.float32)
+        self._err(self.lib.orc_image_fit_run(
+            _fp(param), _fp(target), _u32(w), _u32(h), C.c_float(lr),
+            _u32(n_iters), _fp(trace)), "image_fit_run")
+        return trace, param
+
+    def vertex_faces_tex(self, faces, n_verts, cap=64):
+        faces = _f32(faces)
+        out = np.zeros(n_verts * cap, np.float32)
+        md = _u32(0)
+        self._err(self.lib.orc_vertex_faces_tex(
+            _fp(faces), _u32(faces.shape[0]), _u32(n_verts), _u32(cap),
+            _fp(out), C.byref(md)), "vertex_faces_tex")
+        return out[: n_verts * md.value].reshape(md.value, n_verts)
+
+
+class Ref(_Lib):
+    """_ref/libdressi_ref.so -- the reference CPU implementation."""
+
+    prefix = "ref_"
+
+    def __init__(self, path=None):
+        super().__init__(path or REF_SO)
+
+    def soft_clip(self, clip, faces, w, h, radius):
+        clip, faces = _f32(clip), _f32(faces)
+        out = np.zeros((faces.shape[0] * 3, 4), np.float32)
+        self._err(self.lib.ref_soft_clip(_fp(clip), _u32(clip.shape[0]),
+                                         _fp(faces), _u32(faces.shape[0]),
+                                         _u32(w), _u32(h), C.c_float(radius),
+                                         _fp(out)), "soft_clip")
+        return out
+
+    def rasterize_soft(self, soft_clip, face_id, faces_soft, hard_clip,
+                       faces_tex, vft, w, h, radius, prev_depth=None):
+        soft_clip, face_id, faces_soft = map(_f32, (soft_clip, face_id,
+                                                    faces_soft))
+        hard_clip, faces_tex, vft = map(_f32, (hard_clip, faces_tex, vft))
+        pd = None if prev_depth is None else _f32(prev_depth)
+        out = np.zeros((h, w, 4), np.float32)
+        self._err(self.lib.ref_rasterize_soft(
+            _fp(soft_clip), _fp(face_id), _fp(faces_soft),
+            _u32(faces_soft.shape[0]), _fp(hard_clip), _u32(hard_clip.shape[0]),
+            _fp(faces_tex), _fp(vft), _u32(vft.shape[0]), _u32(w), _u32(h),
+            C.c_float(radius), _fp(pd), _fp(out)), "rasterize_soft")
+        return out
+
+    def rasterize_face_id(self, clip, faces, w, h):
+        clip, faces = _f32(clip), _f32(faces)
+        out = np.zeros((h, w), np.float32)
+        self._err(self.lib.ref_rasterize_face_id(
+            _fp(clip), _u32(clip.shape[0]), _fp(faces), _u32(faces.shape[0]),
+            _u32(w), _u32(h), _fp(out)), "rasterize_face_id")
+        return out
+
+    def rasterize_hard(self, clip, attr, faces, w, h):
+        clip, faces, attr = _f32(clip), _f32(faces), _f32(attr)
+        nc = 1 if attr.ndim == 1 else attr.shape[1]
+        out = np.zeros((h, w, nc), np.float32)
+        self._err(self.lib.ref_rasterize_hard(
+            _fp(clip), _u32(clip.shape[0]), _fp(attr), _u32(nc), _fp(faces),
+            _u32(faces.shape[0]), _u32(w), _u32(h), _fp(out)),
+            "rasterize_hard")
+        return out
+
+    def dist_grad(self, soft_clip, face_id, faces_soft, hard_clip, faces_tex,
+                  vft, w, h, radius, gy):
+        args = list(map(_f32, (soft_clip, face_id, faces_soft, hard_clip,
+                               faces_tex, vft, gy)))
+        soft_clip, face_id, faces_soft, hard_clip, faces_tex, vft, gy = args
+        grad = np.zeros((hard_clip.shape[0], 4), np.float32)
+        rs = np.zeros((h, w, 4), np.float32)
+        self._err(self.lib.ref_dist_grad(
+            _fp(soft_clip), _fp(face_id), _fp(faces_soft),
+            _u32(faces_soft.shape[0]), _fp(hard_clip), _u32(hard_clip.shape[0]),
+            _fp(faces_tex), _fp(vft), _u32(vft.shape[0]), _u32(w), _u32(h),
+            C.c_float(radius), _fp(gy), _fp(grad), _fp(rs)), "dist_grad")
+        return grad, rs
+
+    def silhouette_run(self, pos, faces, vft, mvps, targets, res, radius,
+                       sigma, lr, n_iters, threads=1, want_grad0=False):
+        pos, faces, vft, mvps, targets = map(_f32, (pos, faces, vft, mvps,
+                                                    targets))
+        trace = np.zeros(n_iters, np.float32)
+        pos_out = np.zeros_like(pos)
+        grad0 = np.zeros_like(pos) if want_grad0 else None
+        secs = C.c_double(0.0)
+        self._err(self.lib.ref_silhouette_run(
+            _u32(pos.shape[0]), _u32(faces.shape[0]), _u32(mvps.shape[0]),
+            _u32(res), C.c_float(radius), C.c_float(sigma), C.c_float(lr),
+            _fp(pos), _fp(faces), _fp(vft), _u32(vft.shape[0]), _fp(mvps),
+            _fp(targets), _u32(n_iters), _u32(threads), _fp(trace),
+            _fp(pos_out), _fp(grad0), C.byref(secs)), "silhouette_run")
+        return trace, pos_out, grad0, secs.value
+
+    def image_fit_run(self, param, target, lr, n_iters):
+        param, target = _f32(param), _f32(target)
+        h, w = param.shape[:2]
+        trace = np.zeros(n_iters, np.float32)
+        out = np.zeros_like(param)
+        secs = C.c_double(0.0)
+        self._err(self.lib.ref_image_fit_run(
+            _u32(w), _u32(h), _fp(param), _fp(target), C.c_float(lr),
+            _u32(n_iters), _fp(trace), _fp(out), C.byref(secs)),
+            "image_fit_run")
+        return trace, out, secs.value
+
+    def vertex_faces_tex(self, faces, n_verts, cap=64):
+        faces = _f32(faces)
+        out = np.zeros(n_verts * cap, np.float32)
+        md = _u32(0)
+        self._err(self.lib.ref_vertex_faces_tex(
+            _fp(faces), _u32(faces.shape[0]), _u32(n_verts), _u32(cap),
+            _fp(out), C.byref(md)), "vertex_faces_tex")
+        return out[: n_verts * md.value].reshape(md.value, n_verts)
+
+
+def soft_inputs(n_faces: int):
+    """face_id {3F} and sequential faces_soft {F,3} (run.cpp:456-466)."""
+    fid = np.repeat(np.arange(n_faces, dtype=np.float32), 3)
+    fs = np.arange(n_faces * 3, dtype=np.float32).reshape(n_faces, 3)
+    return fid, fs

@@ -1,0 +1,476 @@
+// Test infrastructure only: a C entry-point shim over the UNMODIFIED
+// reference implementation (unclearness/opendressi), compiled in place from
+// the reference checkout by oracle/Makefile into oracle/_ref/. Nothing in the
+// product links this file; tests/ and bench.py's reference arm load it via
+// ctypes as the checker / CPU baseline.
+//
+// Every graph here is built with the reference's public graph API
+// (include/dressi/f.h) and evaluated by its CPU interpreter
+// (src/core/cpu_eval.cpp:25-63) after its autodiff
+// (src/core/build_backward.cpp:62-149) -- i.e. exactly what the reference's
+// Vulkan executor computes per execStep (src/dressi_ad.cpp:280-530), minus
+// the graphics API.
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "core/build_backward.h"
+#include "core/cpu_eval.h"
+#include "core/cpu_raster.h"
+#include "dressi/dressi.h"
+#include "dressi/mesh_utils.h"
+
+using namespace dressi;
+
+namespace {
+
+thread_local std::string g_err;
+
+CpuTensor Tensor(VType vt, ImgSize sz, const float* data) {
+    CpuTensor t;
+    t.vtype = vt;
+    t.size = sz;
+    t.data.assign(data, data + size_t(sz.w) * sz.h * NumComponents(vt));
+    return t;
+}
+
+void CopyOut(const CpuTensor& t, float* out) {
+    std::memcpy(out, t.data.data(), t.data.size() * sizeof(float));
+}
+
+template <typename Fn>
+int Guard(Fn&& fn) {
+    try {
+        fn();
+        return 0;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return 1;
+    }
+}
+
+// Clip transform of examples/common/geometry_utils.cpp:391-402 rebuilt with
+// the public ops: row r = x*m[r] + y*m[4+r] + z*m[8+r] + m[12+r].
+Variable ClipOf(const Variable& pos, const float* m) {
+    Variable x = F::GetX(pos), y = F::GetY(pos), z = F::GetZ(pos);
+    auto row = [&](int r) {
+        return x * m[0 * 4 + r] + y * m[1 * 4 + r] + z * m[2 * 4 + r] +
+               m[3 * 4 + r];
+    };
+    return F::Vec4(row(0), row(1), row(2), row(3));
+}
+
+struct SilInputs {
+    uint32_t n_verts, n_faces, res, max_deg;
+    float radius_px, sigma;
+};
+
+// The silhouette prediction of one view (HardSoftRas, RasterizeSoft's own
+// exact dist-channel backward):
+//   rs    = RasterizeSoft(SoftClip(clip), ..., clip, ...)
+//   hard  = cov * step(0, dist)
+//   soft  = cov * sigmoid(dist * |dist| * k),  k = (2/R)^2 / sigma
+//   pred  = max(hard, soft)                    (examples/silhouette_
+//                                               optimization/run.cpp:339-342)
+//   loss  = (target - pred)^2 / R^2
+struct SilGraph {
+    Variable faces_f, vft, face_id, faces_soft;
+    std::vector<Variable> targets;
+    Variables view_losses;
+};
+
+Variable SilViewLoss(const Variable& clip, const SilGraph& g,
+                     const Variable& target, const SilInputs& in) {
+    const ImgSize screen = {in.res, in.res};
+    Variable soft_clip = F::SoftClip(clip, g.faces_f, screen, in.radius_px);
+    Variable rs = F::RasterizeSoft(soft_clip, g.face_id, g.faces_soft, clip,
+                                   g.faces_f, g.vft, screen, in.radius_px);
+    Variable dist = F::GetX(rs);
+    Variable cov = F::GetW(rs);
+    Variable zero = F::Float(0.f);
+    const float k = (2.f / float(in.res)) * (2.f / float(in.res)) / in.sigma;
+    Variable hard = cov * F::Step(zero, dist);
+    Variable soft = cov * F::Sigmoid(dist * F::Abs(dist) * k);
+    Variable pred = F::Max(hard, soft);
+    Variable diff = F::StopGradient(target) - pred;
+    return diff * diff * (1.f / float(in.res * in.res));
+}
+
+double SumAll(const CpuTensor& t) {
+    double s = 0.0;
+    for (float v : t.data) s += v;
+    return s;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ref_last_error() { return g_err.c_str(); }
+
+// F::RasterizeSoft forward (src/core/f_ops.cpp:1362-1420 ->
+// src/core/cpu_raster.cpp:241-355); out = W*H*4.
+int ref_rasterize_soft(const float* soft_clip, const float* face_id,
+                       const float* faces_soft, uint32_t n_faces,
+                       const float* hard_clip, uint32_t n_hard,
+                       const float* faces_tex, const float* vft,
+                       uint32_t max_deg, uint32_t w, uint32_t h,
+                       float radius, const float* prev_depth, float* out) {
+    return Guard([&] {
+        Variable sc(VEC4, {n_faces * 3, 1}), fid(FLOAT, {n_faces * 3, 1}),
+                fs(IVEC3, {n_faces, 1}), hc(VEC4, {n_hard, 1}),
+                ft(VEC3, {n_faces, 1}), vf(FLOAT, {n_hard, max_deg}),
+                pd(FLOAT, {w, h});
+        Variable rs = prev_depth
+                              ? F::RasterizeSoft(sc, fid, fs, hc, ft, vf, pd,
+                                                 {w, h}, radius)
+                              : F::RasterizeSoft(sc, fid, fs, hc, ft, vf,
+                                                 {w, h}, radius);
+        CpuEvaluator ev;
+        ev.bind(sc, Tensor(VEC4, {n_faces * 3, 1}, soft_clip));
+        ev.bind(fid, Tensor(FLOAT, {n_faces * 3, 1}, face_id));
+        ev.bind(fs, Tensor(IVEC3, {n_faces, 1}, faces_soft));
+        ev.bind(hc, Tensor(VEC4, {n_hard, 1}, hard_clip));
+        ev.bind(ft, Tensor(VEC3, {n_faces, 1}, faces_tex));
+        ev.bind(vf, Tensor(FLOAT, {n_hard, max_deg}, vft));
+        if (prev_depth) ev.bind(pd, Tensor(FLOAT, {w, h}, prev_depth));
+        CopyOut(ev.eval(rs), out);
+    });
+}
+
+// F::SoftClip (src/core/f_ops.cpp:1890-1981); out = 3F*4.
+int ref_soft_clip(const float* clip, uint32_t n_verts, const float* faces,
+                  uint32_t n_faces, uint32_t w, uint32_t h, float radius,
+                  float* out) {
+    return Guard([&] {
+        Variable c(VEC4, {n_verts, 1}), f(VEC3, {n_faces, 1});
+        Variable y = F::SoftClip(c, f, {w, h}, radius);
+        CpuEvaluator ev;
+        ev.bind(c, Tensor(VEC4, {n_verts, 1}, clip));
+        ev.bind(f, Tensor(VEC3, {n_faces, 1}, faces));
+        CopyOut(ev.eval(y), out);
+    });
+}
+
+// F::RasterizeFaceId (src/core/f_ops.cpp:2183-2209); out = W*H.
+int ref_rasterize_face_id(const float* clip, uint32_t n_verts,
+                          const float* faces, uint32_t n_faces, uint32_t w,
+                          uint32_t h, float* out) {
+    return Guard([&] {
+        Variable c(VEC4, {n_verts, 1}), a(FLOAT, {n_verts, 1}),
+                f(IVEC3, {n_faces, 1});
+        Variable y = F::RasterizeFaceId(c, a, f, {w, h});
+        CpuEvaluator ev;
+        std::vector<float> ones(n_verts, 1.f);
+        ev.bind(c, Tensor(VEC4, {n_verts, 1}, clip));
+        ev.bind(a, Tensor(FLOAT, {n_verts, 1}, ones.data()));
+        ev.bind(f, Tensor(IVEC3, {n_faces, 1}, faces));
+        CopyOut(ev.eval(y), out);
+    });
+}
+
+// F::Rasterize (src/core/f_ops.cpp:1182-1207); attr has n_comp (1..4)
+// components; out = W*H*n_comp.
+int ref_rasterize_hard(const float* clip, uint32_t n_verts, const float* attr,
+                       uint32_t n_comp, const float* faces, uint32_t n_faces,
+                       uint32_t w, uint32_t h, float* out) {
+    return Guard([&] {
+        const VType at = VecVTypeOf(n_comp);
+        Variable c(VEC4, {n_verts, 1}), a(at, {n_verts, 1}),
+                f(IVEC3, {n_faces, 1});
+        Variable y = F::Rasterize(c, a, f, {w, h});
+        CpuEvaluator ev;
+        ev.bind(c, Tensor(VEC4, {n_verts, 1}, clip));
+        ev.bind(a, Tensor(at, {n_verts, 1}, attr));
+        ev.bind(f, Tensor(IVEC3, {n_faces, 1}, faces));
+        CopyOut(ev.eval(y), out);
+    });
+}
+
+// Gradient of sum_px gy(px) * dist(px) w.r.t. the hard clip positions via
+// the reference autodiff: RasterizeSoft's backward is
+// ColSum(GatherDistGrad(...)) (src/core/f_ops.cpp:1407-1416, 1248-1358).
+// out_grad = n_hard*4; out_rs (optional) = W*H*4.
+int ref_dist_grad(const float* soft_clip, const float* face_id,
+                  const float* faces_soft, uint32_t n_faces,
+                  const float* hard_clip, uint32_t n_hard,
+                  const float* faces_tex, const float* vft, uint32_t max_deg,
+                  uint32_t w, uint32_t h, float radius, const float* gy,
+                  float* out_grad, float* out_rs) {
+    return Guard([&] {
+        Variable sc(VEC4, {n_faces * 3, 1}), fid(FLOAT, {n_faces * 3, 1}),
+                fs(IVEC3, {n_faces, 1}), hc(VEC4, {n_hard, 1}),
+                ft(VEC3, {n_faces, 1}), vf(FLOAT, {n_hard, max_deg}),
+                g(FLOAT, {w, h});
+        Variable rs =
+                F::RasterizeSoft(sc, fid, fs, hc, ft, vf, {w, h}, radius);
+        Variable loss = F::GetX(rs) * F::StopGradient(g);
+        Variable hc_mut = hc;
+        hc_mut.setRequiresGradRecursively();
+        auto [xs, gxs] = BuildBackward(loss);
+        Variable grad(nullptr);
+        for (size_t i = 0; i < xs.size(); i++) {
+            if (xs[i] == hc) grad = gxs[i];
+        }
+        DRESSI_CHECK(grad, "no gradient reached the hard clip leaf");
+        CpuEvaluator ev;
+        ev.bind(sc, Tensor(VEC4, {n_faces * 3, 1}, soft_clip));
+        ev.bind(fid, Tensor(FLOAT, {n_faces * 3, 1}, face_id));
+        ev.bind(fs, Tensor(IVEC3, {n_faces, 1}, faces_soft));
+        ev.bind(hc, Tensor(VEC4, {n_hard, 1}, hard_clip));
+        ev.bind(ft, Tensor(VEC3, {n_faces, 1}, faces_tex));
+        ev.bind(vf, Tensor(FLOAT, {n_hard, max_deg}, vft));
+        ev.bind(g, Tensor(FLOAT, {w, h}, gy));
+        CopyOut(ev.eval(grad), out_grad);
+        if (out_rs) CopyOut(ev.eval(rs), out_rs);
+    });
+}
+
+// Full silhouette optimisation (fwd + bwd + in-graph Adam) exactly as the
+// reference's DressiAD runs it: one graph over all views whose per-view loss
+// images are summed with SumPixelWise (examples/silhouette_optimization/
+// run.cpp:386-396), BuildBackward on the image loss (per-pixel seed 1), and
+// the in-graph Adam of run.cpp:421-436 (no regularisers). Each iteration
+// evaluates the updated leaves on one evaluator and re-binds them
+// (the copy-backs of src/vk/executor.cpp:883-898).
+//
+// loss_trace[i] = sum over pixels of the loss image at the START of
+// iteration i. grad0 (optional, V*3) = the position gradient of iteration 0.
+// threads > 1 evaluates views on separate threads (one graph per view,
+// gradients summed in view order, then the same Adam arithmetic).
+int ref_silhouette_run(uint32_t n_verts, uint32_t n_faces, uint32_t n_views,
+                       uint32_t res, float radius_px, float sigma, float lr,
+                       const float* pos0, const float* faces,
+                       const float* vft, uint32_t max_deg,
+                       const float* mvps, const float* targets,
+                       uint32_t n_iters, uint32_t threads, float* loss_trace,
+                       float* pos_out, float* grad0, double* seconds) {
+    return Guard([&] {
+        SilInputs in{n_verts, n_faces, res, max_deg, radius_px, sigma};
+        const float b1 = 0.9f, b2 = 0.999f, eps = 1e-8f;
+        std::vector<float> face_id(size_t(n_faces) * 3),
+                faces_soft(size_t(n_faces) * 3);
+        for (uint32_t f = 0; f < n_faces; f++) {
+            for (uint32_t k = 0; k < 3; k++) {
+                face_id[f * 3 + k] = float(f);
+                faces_soft[f * 3 + k] = float(f * 3 + k);
+            }
+        }
+        const size_t px = size_t(res) * res;
+        CpuTensor t_faces = Tensor(VEC3, {n_faces, 1}, faces);
+        CpuTensor t_vft = Tensor(FLOAT, {n_verts, max_deg}, vft);
+        CpuTensor t_fid = Tensor(FLOAT, {n_faces * 3, 1}, face_id.data());
+        CpuTensor t_fs = Tensor(IVEC3, {n_faces, 1}, faces_soft.data());
+
+        auto make_graph = [&](SilGraph& g) {
+            g.faces_f = Variable(VEC3, {n_faces, 1});
+            g.vft = Variable(FLOAT, {n_verts, max_deg});
+            g.face_id = Variable(FLOAT, {n_faces * 3, 1});
+            g.faces_soft = Variable(IVEC3, {n_faces, 1});
+        };
+        auto bind_static = [&](CpuEvaluator& ev, const SilGraph& g) {
+            ev.bind(g.faces_f, t_faces);
+            ev.bind(g.vft, t_vft);
+            ev.bind(g.face_id, t_fid);
+            ev.bind(g.faces_soft, t_fs);
+        };
+
+        std::vector<float> pos(pos0, pos0 + size_t(n_verts) * 3);
+        const auto t0 = std::chrono::steady_clock::now();
+
+        if (threads <= 1) {
+            SilGraph g;
+            make_graph(g);
+            Variable vpos(VEC3, {n_verts, 1}), am(VEC3, {n_verts, 1}),
+                    av(VEC3, {n_verts, 1}), at(FLOAT, {1, 1});
+            Variables losses;
+            for (uint32_t v = 0; v < n_views; v++) {
+                g.targets.emplace_back(FLOAT, ImgSize{res, res});
+                losses.push_back(SilViewLoss(ClipOf(vpos, mvps + v * 16), g,
+                                             g.targets.back(), in));
+            }
+            Variable loss = F::SumPixelWise(losses);
+            vpos.setRequiresGradRecursively();
+            auto [xs, gxs] = BuildBackward(loss);
+            DRESSI_CHECK(xs.size() == 1 && xs[0] == vpos,
+                         "expected pos as the only gradient leaf");
+            Variable gp = gxs[0];
+            Variable t_new = at + 1.f;
+            Variable m_new = am * b1 + gp * (1.f - b1);
+            Variable v_new = av * b2 + gp * gp * (1.f - b2);
+            Variable bc1 = 1.f - F::Pow(F::Float(b1), t_new);
+            Variable bc2 = 1.f - F::Pow(F::Float(b2), t_new);
+            Variable step = (m_new / bc1) / (F::Sqrt(v_new / bc2) + eps) * lr;
+            Variable pos_new = vpos - step;
+            CpuTensor tm = Tensor(VEC3, {n_verts, 1},
+                                  std::vector<float>(n_verts * 3, 0.f).data());
+            CpuTensor tv = tm;
+            float tt = 0.f;
+            for (uint32_t it = 0; it < n_iters; it++) {
+                CpuEvaluator ev;
+                bind_static(ev, g);
+                for (uint32_t v = 0; v < n_views; v++) {
+                    ev.bind(g.targets[v],
+                            Tensor(FLOAT, {res, res}, targets + v * px));
+                }
+                ev.bind(vpos, Tensor(VEC3, {n_verts, 1}, pos.data()));
+                ev.bind(am, tm);
+                ev.bind(av, tv);
+                ev.bind(at, Tensor(FLOAT, {1, 1}, &tt));
+                loss_trace[it] = float(SumAll(ev.eval(loss)));
+                if (it == 0 && grad0) CopyOut(ev.eval(gp), grad0);
+                CpuTensor np = ev.eval(pos_new);
+                tm = ev.eval(m_new);
+                tv = ev.eval(v_new);
+                tt = ev.eval(t_new).data[0];
+                pos = np.data;
+            }
+        } else {
+            // View-parallel: one graph per view, evaluated concurrently
+            struct ViewG {
+                SilGraph g;
+                Variable vpos, target, loss, grad;
+            };
+            std::vector<ViewG> vg(n_views);
+            for (uint32_t v = 0; v < n_views; v++) {
+                make_graph(vg[v].g);
+                vg[v].vpos = Variable(VEC3, {n_verts, 1});
+                vg[v].target = Variable(FLOAT, {res, res});
+                vg[v].loss = SilViewLoss(ClipOf(vg[v].vpos, mvps + v * 16),
+                                         vg[v].g, vg[v].target, in);
+                vg[v].vpos.setRequiresGradRecursively();
+                auto [xs, gxs] = BuildBackward(vg[v].loss);
+                DRESSI_CHECK(xs.size() == 1, "expected one gradient leaf");
+                vg[v].grad = gxs[0];
+            }
+            std::vector<float> m(size_t(n_verts) * 3, 0.f), vv = m;
+            float t = 0.f;
+            std::vector<std::vector<float>> grads(n_views);
+            std::vector<double> vloss(n_views);
+            for (uint32_t it = 0; it < n_iters; it++) {
+                std::atomic<uint32_t> next{0};
+                std::vector<std::string> errs(threads);
+                auto work = [&](uint32_t tid) {
+                    try {
+                        for (uint32_t v; (v = next++) < n_views;) {
+                            CpuEvaluator ev;
+                            bind_static(ev, vg[v].g);
+                            ev.bind(vg[v].target,
+                                    Tensor(FLOAT, {res, res},
+                                           targets + v * px));
+                            ev.bind(vg[v].vpos,
+                                    Tensor(VEC3, {n_verts, 1}, pos.data()));
+                            vloss[v] = SumAll(ev.eval(vg[v].loss));
+                            grads[v] = ev.eval(vg[v].grad).data;
+                        }
+                    } catch (const std::exception& e) {
+                        errs[tid] = e.what();
+                    }
+                };
+                std::vector<std::thread> pool;
+                for (uint32_t i = 0; i < threads; i++) pool.emplace_back(work, i);
+                for (auto& th : pool) th.join();
+                for (auto& e : errs) DRESSI_CHECK(e.empty(), e);
+                double ls = 0.0;
+                for (double l : vloss) ls += l;
+                loss_trace[it] = float(ls);
+                std::vector<float> g(size_t(n_verts) * 3, 0.f);
+                for (uint32_t v = 0; v < n_views; v++) {
+                    for (size_t i = 0; i < g.size(); i++) g[i] += grads[v][i];
+                }
+                if (it == 0 && grad0) std::copy(g.begin(), g.end(), grad0);
+                t = t + 1.f;
+                const float bc1 = 1.f - std::pow(b1, t);
+                const float bc2 = 1.f - std::pow(b2, t);
+                for (size_t i = 0; i < g.size(); i++) {
+                    m[i] = m[i] * b1 + g[i] * (1.f - b1);
+                    vv[i] = vv[i] * b2 + g[i] * g[i] * (1.f - b2);
+                    pos[i] = pos[i] - (m[i] / bc1) /
+                                              (std::sqrt(vv[i] / bc2) + eps) *
+                                              lr;
+                }
+            }
+        }
+        const auto t1 = std::chrono::steady_clock::now();
+        if (seconds) *seconds = std::chrono::duration<double>(t1 - t0).count();
+        std::copy(pos.begin(), pos.end(), pos_out);
+    });
+}
+
+// 2-D image fitting (examples/image_fitting/run.cpp:40-63 with the in-graph
+// Adam of the silhouette example): loss = Mean((param - target)^2) over a
+// VEC4 image; Adam lr on param. loss_trace[i] is the Mean loss at the start
+// of iteration i.
+int ref_image_fit_run(uint32_t w, uint32_t h, const float* param0,
+                      const float* target, float lr, uint32_t n_iters,
+                      float* loss_trace, float* param_out, double* seconds) {
+    return Guard([&] {
+        const float b1 = 0.9f, b2 = 0.999f, eps = 1e-8f;
+        Variable p(VEC4, {w, h}), tg(VEC4, {w, h}), am(VEC4, {w, h}),
+                av(VEC4, {w, h}), at(FLOAT, {1, 1});
+        Variable diff = p - F::StopGradient(tg);
+        Variable loss = F::Mean(diff * diff);
+        p.setRequiresGradRecursively();
+        auto [xs, gxs] = BuildBackward(loss);
+        DRESSI_CHECK(xs.size() == 1 && xs[0] == p, "expected param leaf");
+        Variable g = gxs[0];
+        Variable t_new = at + 1.f;
+        Variable m_new = am * b1 + g * (1.f - b1);
+        Variable v_new = av * b2 + g * g * (1.f - b2);
+        Variable bc1 = 1.f - F::Pow(F::Float(b1), t_new);
+        Variable bc2 = 1.f - F::Pow(F::Float(b2), t_new);
+        Variable step = (m_new / bc1) / (F::Sqrt(v_new / bc2) + eps) * lr;
+        Variable p_new = p - step;
+        const size_t n = size_t(w) * h * 4;
+        CpuTensor tp = Tensor(VEC4, {w, h}, param0);
+        CpuTensor tt = Tensor(VEC4, {w, h}, target);
+        std::vector<float> zeros(n, 0.f);
+        CpuTensor tm = Tensor(VEC4, {w, h}, zeros.data()), tv = tm;
+        float t = 0.f;
+        const auto t0 = std::chrono::steady_clock::now();
+        for (uint32_t it = 0; it < n_iters; it++) {
+            CpuEvaluator ev;
+            ev.bind(p, tp);
+            ev.bind(tg, tt);
+            ev.bind(am, tm);
+            ev.bind(av, tv);
+            ev.bind(at, Tensor(FLOAT, {1, 1}, &t));
+            loss_trace[it] = ev.eval(loss).data[0];
+            CpuTensor np = ev.eval(p_new);
+            tm = ev.eval(m_new);
+            tv = ev.eval(v_new);
+            t = ev.eval(t_new).data[0];
+            tp = np;
+        }
+        const auto t1 = std::chrono::steady_clock::now();
+        if (seconds) *seconds = std::chrono::duration<double>(t1 - t0).count();
+        CopyOut(tp, param_out);
+    });
+}
+
+// Vertex -> incident-face adjacency (src/core/mesh_utils.cpp:53-69).
+// Returns max_deg via *max_deg; out must hold n_verts*cap floats and is
+// written row-major {V, max_deg} (-1 padding). Returns nonzero if cap is
+// too small.
+int ref_vertex_faces_tex(const float* faces, uint32_t n_faces,
+                         uint32_t n_verts, uint32_t cap, float* out,
+                         uint32_t* max_deg) {
+    return Guard([&] {
+        CpuImage fi(n_faces, 1, 3);
+        std::copy(faces, faces + size_t(n_faces) * 3, fi.data.begin());
+        CpuImage t = VertexFacesTex(fi, n_verts);
+        DRESSI_CHECK(t.height <= cap, "vertex_faces_tex: capacity");
+        *max_deg = t.height;
+        std::copy(t.data.begin(), t.data.end(), out);
+    });
+}
+
+}  // extern "C"
