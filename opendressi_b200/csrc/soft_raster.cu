@@ -219,7 +219,9 @@ static void check_launch() { DRESSI_CUDA(cudaGetLastError()); }
 
 void soft_bin_and_sweep1(const SoftDims& d, const SoftBuffers& b,
                          const float* prev_depth, cudaStream_t s) {
-    const dim3 fg((d.n_faces + 127) / 128, d.views);
+    // zero faces: the scan still runs (clears the tile lists); the per-face
+    // passes have nothing to launch
+    const dim3 fg((std::max(d.n_faces, 1) + 127) / 128, d.views);
     {
         ProfScope ps("bin_scan", s);
         k_bin_scan<<<d.views, 1024, 0, s>>>(b.bin1, d.n_tiles, b.status);

@@ -168,9 +168,10 @@ class SilhouettePlan(Plan):
     @classmethod
     def from_scene(cls, scene, device: int = 0, views=None, **kw):
         mvps = scene.mvps if views is None else scene.mvps[views]
+        kw.setdefault("lr", scene.lr)
+        kw.setdefault("sigma", scene.sigma)
         return cls(scene.faces_f, mvps, scene.n_verts, scene.res,
-                   scene.radius_px, sigma=scene.sigma, lr=scene.lr,
-                   device=device, **kw)
+                   scene.radius_px, device=device, **kw)
 
     def render_targets(self, target_pos, stream=None):
         tp = np.ascontiguousarray(target_pos, np.float32)
