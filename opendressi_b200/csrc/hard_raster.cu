@@ -8,6 +8,7 @@
 // once at the end for the attribute interpolation, with the reference's
 // expressions (shade lambda, cpu_raster.cpp:205-223).
 #include <algorithm>
+#include <cstdlib>
 
 #include "kernels.h"
 
@@ -47,6 +48,11 @@ static HardDims with_cap(HardDims d) {
         const long long f = d.n_faces, t = d.n_tiles;
         d.cap = int(std::min<long long>(std::max<long long>(16 * f, 4 * t) + 4096,
                                         1ll << 30));
+        // test hook shared with the soft rasterizer (exercises the fallback)
+        if (const char* e = std::getenv("DRESSI_B200_BIN_CAP")) {
+            const long long c = std::atoll(e);
+            if (c > 0) d.cap = int(std::min<long long>(c, 1ll << 30));
+        }
     }
     return d;
 }

@@ -18,21 +18,45 @@ struct SoftDims {
     int W = 0, H = 0, views = 1, n_faces = 0, n_verts = 0;
     float radius = 1.f;
     int tiles_x = 0, tiles_y = 0, n_tiles = 0;
-    int cap1 = 0, cap2 = 0;  // tile-list capacity per view (entries)
+    int rim_cells_x = 0, rim_cells = 0;
+    int cap1 = 0, cap2 = 0;  // entries per sweep-1 tile / rim block bin
 
     void finalize() {
         tiles_x = (W + kTile - 1) / kTile;
         tiles_y = (H + kTile - 1) / kTile;
         n_tiles = tiles_x * tiles_y;
+        rim_cells_x = (W + kRimCell - 1) / kRimCell;
+        rim_cells = rim_cells_x * ((H + kRimCell - 1) / kRimCell);
+    }
+
+    // Sweep arguments of view 0 (the kernels offset them per view).
+    SweepArgs args(const FaceRec* recs, const int* rim, const float* prev,
+                   uint32_t* status) const {
+        SweepArgs a;
+        a.recs = recs;
+        a.n_faces = n_faces;
+        a.W = W;
+        a.H = H;
+        a.tiles_x = tiles_x;
+        a.n_tiles = n_tiles;
+        a.v = 0;
+        a.radius = radius;
+        a.prev = prev;
+        a.rim_cells_x = rim_cells_x;
+        a.rim = rim;
+        a.status = status;
+        return a;
     }
 };
 
 // Device scratch of the soft rasterizer, carved from one allocation.
 struct SoftBuffers {
     FaceRec* recs = nullptr;   // [views * n_faces]
-    BinSet bin1{}, bin2{};
-    PixState* state = nullptr; // [views * W * H]
-    int* active = nullptr;     // [views * n_tiles]
+    FixedBins bin1{};          // sweep-1 bins per 16x16 tile
+    FixedBins bin2{};          // rim-phase bins per 8x4 block
+    int2* state = nullptr;     // packed survivors [views * W * H]
+    int* active = nullptr;     // open-block mask per tile [views * n_tiles]
+    int* rim = nullptr;        // rim-possible flags [views * rim_cells]
     uint32_t* status = nullptr;
 };
 
@@ -46,10 +70,32 @@ void init_soft(const SoftDims& d, const SoftBuffers& b, cudaStream_t s);
 // Default tile-list capacities for a scene (entries per view).
 void default_caps(SoftDims* d);
 
-// Enqueues sweep-1 binning, sweep 1 and sweep-2 binning (records and the
-// sweep-1 tile counts must already be written by a face-setup kernel).
-void soft_bin_and_sweep1(const SoftDims& d, const SoftBuffers& b,
-                         const float* prev_depth, cudaStream_t s);
+// The face-setup kernels fill the sweep-1 bins; after sweep 1 the rim
+// binning fills the per-block bins of the open blocks.
+void soft_rim_bins(const SoftDims& d, const SoftBuffers& b, cudaStream_t s);
+
+// Launches sweep 1, the rim binning and the rim phase with an epilogue.
+template <class Epi>
+void launch_sweeps(const SoftDims& d, const SoftBuffers& b,
+                   const float* prev_depth, const Epi& epi, cudaStream_t s) {
+    const SweepArgs a = d.args(b.recs, b.rim, prev_depth, b.status);
+    const dim3 grid(d.n_tiles, d.views);
+    const size_t sr = size_t(d.n_faces), sp = size_t(d.W) * d.H,
+                 sm = size_t(d.rim_cells);
+    {
+        ProfScope ps("sweep1", s);
+        k_sweep1<Epi><<<grid, kTileThreads, 0, s>>>(a, b.bin1, b.state,
+                                                    b.active, sr, sp, sm, epi);
+    }
+    DRESSI_CUDA(cudaGetLastError());
+    soft_rim_bins(d, b, s);
+    {
+        ProfScope ps("rim", s);
+        k_rim<Epi><<<grid, kTileThreads, 0, s>>>(a, b.bin2, b.state, b.active,
+                                                 sr, sp, sm, epi);
+    }
+    DRESSI_CUDA(cudaGetLastError());
+}
 
 // --- op-level soft raster (explicit soft geometry, one or more views) ---
 struct SoftOpInputs {
@@ -101,7 +147,7 @@ struct SilBuffers {
     unsigned* done;      // block-completion counter of the Adam step
     SoftBuffers soft;
 };
-constexpr int kLossSlots = 1024;
+constexpr int kLossSlots = 4096;
 // Transform, raster, loss and per-view clip gradients (advances the Adam
 // counter). rs_out (nullable) receives the RasterizeSoft images.
 void sil_forward_backward(const SoftDims& d, const SilParams& p,

@@ -8,23 +8,27 @@
 // Each thread here owns one pixel and folds fragments into that key in any
 // order, which gives the same survivor (for finite depths).
 //
-// Work split (per view, 16x16-pixel tiles, one CTA per tile):
-//  sweep 1: every fragment inside a face's *sweep-1 region* -- the hard
-//           triangle's bbox grown by kHardMargin pixels (or the whole soft
-//           bbox for faces flagged unsafe) -- is evaluated in full.
-//  sweep 2: only tiles that still hold a pixel whose best depth is > 0.5
-//           (not covered by a hard fragment) see the remaining soft-rim
-//           fragments of safe faces (soft bbox minus sweep-1 region).
+// Work split per view:
+//  sweep 1 (16x16-pixel tiles, one CTA each): the faces whose *sweep-1
+//           region* -- the hard triangle's bbox grown by kHardMargin pixels,
+//           or the whole soft bbox for faces flagged unsafe -- touches the
+//           tile. Inside (hard) and boundary fragments are folded; fragments
+//           provably more than 0.008 px outside (see classify) are rim
+//           fragments with depth > 0.5 and are deferred.
+//  rim phase (8x4-pixel blocks, one warp each): only blocks that still hold
+//           a pixel whose best depth is > 0.5 (no hard fragment) see the
+//           rim fragments of safe faces: the deferred ones and those outside
+//           the sweep-1 region.
 // A fragment outside the hard bbox + margin of a *safe* face is provably a
 // rim fragment with dist <= -kHardMargin, hence depth > 0.5, so it can never
-// beat a hard fragment: skipping it for tiles whose pixels all have
-// depth <= 0.5 cannot change any output. "Safe" bounds the sign-test
-// rounding error: every angle of the hard triangle must satisfy
-// sin(theta/2) > kSafeSlope * L, L the largest pixel distance the face's
-// soft bbox reaches from a hard vertex (the rounding error of the edge
-// function is <= ~5u*|e|*L, its exact value outside the margin is
-// >= 2*sin(theta/2)*|e| * kHardMargin/2); faces failing it, or with huge
-// coordinates, are evaluated exhaustively in sweep 1.
+// beat a hard fragment: leaving it out for pixels whose depth is <= 0.5
+// cannot change any output. "Safe" bounds the sign-test rounding error:
+// every angle of the hard triangle must satisfy sin(theta/2) > kSafeSlope *
+// L, L the largest pixel distance the face's soft bbox reaches from a hard
+// vertex (the rounding error of the edge function is <= ~5u*|e|*L, its
+// exact value outside the margin is >= 2*sin(theta/2)*|e| * kHardMargin/2);
+// faces failing it, or with huge coordinates, are evaluated exhaustively in
+// sweep 1.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -50,33 +54,52 @@ enum FaceFlags : uint32_t {
     kFaceValid = 1u,     // produces fragments
     kFaceHardBary = 2u,  // hard ScreenBarycentric succeeds
     kFaceSafe = 4u,      // sweep-2 skipping is exact for this face
+    kFaceFast = 8u,      // the "far" classification is exact for this face
+    kFaceSoftInside = 16u,  // an inside fragment is always soft-covered
 };
+
+constexpr float kMaxFastRadius = 1e4f;  // rim depth stays > 0.5 below it
 
 // Per-(view, face) constants hoisted out of the per-pixel loop. Every value
 // is computed with the reference's own expression, so hoisting is exact.
 struct __align__(16) FaceRec {
     float s0x, s0y, s1x, s1y;  // soft triangle, screen px
     float s2x, s2y, s_inv_area, fid;
-    float sz0, sz1, sz2, pad0;  // soft vertex NDC depth
-    float h0x, h0y, h1x, h1y;   // hard triangle, screen px
+    float sz0, sz1, sz2, orient;  // soft vertex NDC depth; sign of hard area
+    float h0x, h0y, h1x, h1y;     // hard triangle, screen px
     float h2x, h2y, h_inv_area, hz0;
-    float hz1, hz2, ex0, ey0;   // hard edges e_k = h[k+1] - h[k]
+    float hz1, hz2, ex0, ey0;     // hard edges e_k = h[k+1] - h[k]
     float ex1, ey1, ex2, ey2;
     float len2_0, len2_1, len2_2, pad1;
+    float lbx0, lbx1, lby0, lby1;  // hard bbox grown by rounding slack
     int bx0, bx1, by0, by1;  // soft bbox pixel range (inclusive)
     int rx0, rx1, ry0, ry1;  // sweep-1 region pixel range (inclusive)
     uint32_t flags, i0, i1, i2;  // flags + hard vertex indices
 };
-static_assert(sizeof(FaceRec) == 176, "FaceRec layout");
+static_assert(sizeof(FaceRec) == 192, "FaceRec layout");
 constexpr int kRecVec4 = sizeof(FaceRec) / 16;
 
-// Per-pixel survivor carried from sweep 1 to sweep 2.
-struct __align__(16) PixState {
-    float depth;  // Eq.3 shifted depth of the survivor (1 = clear)
-    int face;     // soft face index of the survivor (-1 = none)
-    float dist;   // signed distance to its hard triangle
-    float hard_z; // unclamped hard depth
+// Survivor of a pixel: Eq.3 depth, soft face index (-1 = none) and whether
+// its signed distance is >= 0 (a "hard" fragment). The distance and hard
+// depth themselves are recomputed once, for the survivor only, from its
+// record -- the same expressions, hence the same values.
+struct Survivor {
+    float depth;
+    int face;
+    bool hard;
 };
+// Packed form kept in HBM between the sweeps (8 B / pixel).
+__device__ __forceinline__ int2 pack(const Survivor& s) {
+    return make_int2(__float_as_int(s.depth),
+                     s.face < 0 ? -1 : (s.face | (s.hard ? int(0x80000000u) : 0)));
+}
+__device__ __forceinline__ Survivor unpack(int2 p) {
+    Survivor s;
+    s.depth = __int_as_float(p.x);
+    s.face = p.y == -1 ? -1 : (p.y & 0x7fffffff);
+    s.hard = p.y != -1 && (p.y & int(0x80000000u)) != 0;
+    return s;
+}
 
 struct TriDist {
     float dist;
@@ -121,6 +144,44 @@ __device__ __forceinline__ TriDist signed_dist(float px, float py,
     const float sgn = (n_pos == 3 || n_neg == 3) ? 1.f : -1.f;
     best.dist = sgn * sqrtf(std_max(best_d2, 0.f));
     return best;
+}
+
+// Fragment classes of the two-pass sweep.
+enum FragClass : int {
+    kInside = 0,    // SignedDistToTri's sign test says inside: dist >= 0
+    kFar = 1,       // provably dist <= -0.008 px: a rim fragment, depth > 0.5
+    kBoundary = 2,  // anything else: evaluate in full
+};
+
+// The inside test is SignedDistToTri's own sign test (same expressions).
+// "Far" needs kFaceFast (well-conditioned, |coords| < 4096, see
+// build_record): some edge function has the outside sign with
+// cr^2 > 1e-4 |e|^2, i.e. the pixel centre is > 0.01 px beyond that edge's
+// line while the rounding error of cr is < 0.001 |e| -- so every edge's
+// closest point is > 0.008 px away and the reference's distance is negative.
+__device__ __forceinline__ int classify(float px, float py, const FaceRec& r) {
+    const float cr0 = r.ex0 * (py - r.h0y) - r.ey0 * (px - r.h0x);
+    const float cr1 = r.ex1 * (py - r.h1y) - r.ey1 * (px - r.h1x);
+    const float cr2 = r.ex2 * (py - r.h2y) - r.ey2 * (px - r.h2x);
+    const int n_pos = (cr0 >= 0.f) + (cr1 >= 0.f) + (cr2 >= 0.f);
+    const int n_neg = (cr0 <= 0.f) + (cr1 <= 0.f) + (cr2 <= 0.f);
+    if (n_pos == 3 || n_neg == 3) return kInside;
+    if (!(r.flags & 8u /* kFaceFast */)) return kBoundary;
+    const float o = r.orient;
+    const bool far = (o * cr0 < 0.f && cr0 * cr0 > 1e-4f * r.len2_0) ||
+                     (o * cr1 < 0.f && cr1 * cr1 > 1e-4f * r.len2_1) ||
+                     (o * cr2 < 0.f && cr2 * cr2 > 1e-4f * r.len2_2);
+    return far ? kFar : kBoundary;
+}
+
+// Lower bound of a rim fragment's depth from the distance to the face's
+// (slack-grown) hard bbox; never above the reference's depth (monotone).
+__device__ __forceinline__ float rim_depth_lb(float px, float py,
+                                              const FaceRec& r, float radius) {
+    const float dx = fmaxf(fmaxf(r.lbx0 - px, px - r.lbx1), 0.f);
+    const float dy = fmaxf(fmaxf(r.lby0 - py, py - r.lby1), 0.f);
+    const float d = sqrtf(dx * dx + dy * dy) * 0.999f;
+    return 0.5f + 0.5f * std_min(d / radius, 1.f);
 }
 
 // Unclamped hard depth: ScreenBarycentric on the hard triangle, 0.5 when it
@@ -194,7 +255,7 @@ __device__ __forceinline__ bool build_record(
     r.s_inv_area = 1.f / s_area;
     r.fid = fid;
     r.sz0 = sz[0]; r.sz1 = sz[1]; r.sz2 = sz[2];
-    r.pad0 = 0.f;
+    r.orient = 0.f;
     r.h0x = hs[0][0]; r.h0y = hs[0][1];
     r.h1x = hs[1][0]; r.h1y = hs[1][1];
     r.h2x = hs[2][0]; r.h2y = hs[2][1];
@@ -216,46 +277,111 @@ __device__ __forceinline__ bool build_record(
     r.len2_0 = l2s[0]; r.len2_1 = l2s[1]; r.len2_2 = l2s[2];
     r.pad1 = 0.f;
     r.i0 = hidx[0]; r.i1 = hidx[1]; r.i2 = hidx[2];
-
-    // Safety classification (all in double; only decides how much work is
-    // done, never a result).
-    bool safe = true;
-    double hmnx = 1e300, hmxx = -1e300, hmny = 1e300, hmxy = -1e300;
-    for (int k = 0; k < 3; k++) {
-        const double x = hs[k][0], y = hs[k][1];
-        if (!(fabs(x) < kCoordLimit && fabs(y) < kCoordLimit)) safe = false;
-        hmnx = fmin(hmnx, x); hmxx = fmax(hmxx, x);
-        hmny = fmin(hmny, y); hmxy = fmax(hmxy, y);
+    {
+        // bbox of the segments a_k + t e_k the distance is measured to,
+        // grown by their rounding slack
+        float mnx = hs[0][0], mxx = hs[0][0], mny = hs[0][1], mxy = hs[0][1];
+        float amax = 0.f;
+        for (int k = 0; k < 3; k++) {
+            const float ax = hs[k][0], ay = hs[k][1];
+            const float bx = ax + exs[k], by = ay + eys[k];
+            mnx = fminf(mnx, fminf(ax, bx)); mxx = fmaxf(mxx, fmaxf(ax, bx));
+            mny = fminf(mny, fminf(ay, by)); mxy = fmaxf(mxy, fmaxf(ay, by));
+            amax = fmaxf(amax, fmaxf(fabsf(ax), fabsf(ay)));
+        }
+        const float slack = 1e-3f + 4e-7f * amax;
+        r.lbx0 = mnx - slack; r.lbx1 = mxx + slack;
+        r.lby0 = mny - slack; r.lby1 = mxy + slack;
     }
+
+    // Safety classification. Float arithmetic with explicit rounding
+    // allowances (u = 2^-24); it only decides how much work is done, the
+    // results never depend on it beyond the guarantees stated per flag.
+    constexpr float kU = 5.9604645e-8f;
+    bool safe = true;
+    float hmnx = hs[0][0], hmxx = hs[0][0], hmny = hs[0][1], hmxy = hs[0][1];
+    float cmax = 0.f, emax = 0.f;
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        const float x = hs[k][0], y = hs[k][1];
+        if (!(fabsf(x) < kCoordLimit && fabsf(y) < kCoordLimit)) safe = false;
+        hmnx = fminf(hmnx, x); hmxx = fmaxf(hmxx, x);
+        hmny = fminf(hmny, y); hmxy = fmaxf(hmxy, y);
+        cmax = fmaxf(cmax, fmaxf(fabsf(x), fabsf(y)));
+        emax = fmaxf(emax, sqrtf(l2s[k]));
+    }
+    // L: largest distance from a hard vertex to a (grown) soft-bbox corner,
+    // rounded up
+    float L = 0.f;
     if (safe) {
-        double L = 0.0;
-        const double cx[2] = {double(r.bx0) - 1.0, double(r.bx1) + 2.0};
-        const double cy[2] = {double(r.by0) - 1.0, double(r.by1) + 2.0};
+        const float cx[2] = {float(r.bx0) - 1.f, float(r.bx1) + 2.f};
+        const float cy[2] = {float(r.by0) - 1.f, float(r.by1) + 2.f};
+#pragma unroll
         for (int k = 0; k < 3; k++)
+#pragma unroll
             for (int a = 0; a < 2; a++)
+#pragma unroll
                 for (int b = 0; b < 2; b++) {
-                    const double dx = cx[a] - hs[k][0], dy = cy[b] - hs[k][1];
-                    L = fmax(L, sqrt(dx * dx + dy * dy));
+                    const float dx = cx[a] - hs[k][0], dy = cy[b] - hs[k][1];
+                    L = fmaxf(L, sqrtf(dx * dx + dy * dy));
                 }
-        for (int k = 0; k < 3 && safe; k++) {
+        L *= 1.001f;
+        // every angle: sin(theta/2) >= sin(theta)/2 = |u x v| / (2|u||v|),
+        // with the cross product's rounding subtracted
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
             const int k1 = (k + 1) % 3, k2 = (k + 2) % 3;
-            const double ux = hs[k1][0] - hs[k][0], uy = hs[k1][1] - hs[k][1];
-            const double vx = hs[k2][0] - hs[k][0], vy = hs[k2][1] - hs[k][1];
-            const double nu = sqrt(ux * ux + uy * uy), nv = sqrt(vx * vx + vy * vy);
-            if (!(nu > 1e-3 && nv > 1e-3)) { safe = false; break; }
-            const double cs = (ux * vx + uy * vy) / (nu * nv);
-            // sin(theta/2) = sqrt((1 - cos theta) / 2)
-            const double sh = sqrt(fmax(0.0, (1.0 - cs) * 0.5));
-            if (!(sh > double(kSafeSlope) * L)) safe = false;
+            const float ux = hs[k1][0] - hs[k][0], uy = hs[k1][1] - hs[k][1];
+            const float vx = hs[k2][0] - hs[k][0], vy = hs[k2][1] - hs[k][1];
+            const float nu = sqrtf(ux * ux + uy * uy), nv = sqrtf(vx * vx + vy * vy);
+            const float p1 = ux * vy, p2 = uy * vx;
+            const float cross = fabsf(p1 - p2) - 8.f * kU * (fabsf(p1) + fabsf(p2));
+            const float sh = cross / (2.f * nu * nv * 1.001f);
+            if (!(nu > 1e-3f && nv > 1e-3f && sh > kSafeSlope * L)) safe = false;
+        }
+    }
+    if (safe && (flags & kFaceHardBary)) {
+        // "far" classification (classify()): coordinates < 4096 keep the
+        // edge endpoints within 2.5e-4 px of the next vertex; the reach L
+        // of the soft bbox bounds the edge-function rounding error by
+        // 4u|e|L < 0.001|e|; the area keeps the three edge functions from
+        // all taking the outside sign.
+        if (cmax < 4096.f && L < 4000.f &&
+            fabsf(h_area) >= fmaxf(1.f, 1e-4f * emax * L * 1.001f)) {
+            flags |= kFaceFast;
+            r.orient = h_area > 0.f ? 1.f : -1.f;
+            // Soft coverage of inside fragments: if every hard vertex has
+            // soft barycentrics >= 0.01 (convexity extends that to the whole
+            // hard triangle, and an inside-classified pixel is within 1e-3
+            // px of it) and the vertex depths stay 1e-5 inside [0, 1], the
+            // reference's soft test passes for every inside fragment. The
+            // barycentrics here carry a rounding allowance of 1e-5 times
+            // the magnitude of their terms.
+            bool si = !(fabsf(s_area) < 1e-6f);
+            const float ia = fabsf(1.f / s_area);
+#pragma unroll
+            for (int k = 0; k < 3; k++) {
+                const float px = hs[k][0], py = hs[k][1];
+                const float a0 = (ss[1][0] - px) * (ss[2][1] - py),
+                            b0 = (ss[1][1] - py) * (ss[2][0] - px);
+                const float a1 = (ss[2][0] - px) * (ss[0][1] - py),
+                            b1 = (ss[2][1] - py) * (ss[0][0] - px);
+                const float l0 = (a0 - b0) / s_area, l1 = (a1 - b1) / s_area;
+                const float tol = 0.01f + 1e-5f * (1.f + (fabsf(a0) + fabsf(b0) +
+                                                          fabsf(a1) + fabsf(b1)) * ia);
+                si = si && l0 >= tol && l1 >= tol && 1.f - l0 - l1 >= tol;
+                si = si && sz[k] > 1e-5f && sz[k] < 1.f - 1e-5f;
+            }
+            if (si) flags |= kFaceSoftInside;
         }
     }
     if (safe) {
         flags |= kFaceSafe;
-        int hx0, hx1, hy0, hy1;
-        hx0 = int(floor(hmnx - 0.5)) - kHardMargin;
-        hx1 = int(ceil(hmxx - 0.5)) + kHardMargin;
-        hy0 = int(floor(hmny - 0.5)) - kHardMargin;
-        hy1 = int(ceil(hmxy - 0.5)) + kHardMargin;
+        // |coords| < 2^20: floorf/ceilf of x - 0.5 are exact
+        const int hx0 = int(floorf(hmnx - 0.5f)) - kHardMargin;
+        const int hx1 = int(ceilf(hmxx - 0.5f)) + kHardMargin;
+        const int hy0 = int(floorf(hmny - 0.5f)) - kHardMargin;
+        const int hy1 = int(ceilf(hmxy - 0.5f)) + kHardMargin;
         r.rx0 = imax_(r.bx0, hx0);
         r.rx1 = imin_(r.bx1, hx1);
         r.ry0 = imax_(r.by0, hy0);
@@ -389,137 +515,356 @@ static __global__ void k_bin_scan(BinSet b, int n_tiles, uint32_t* status) {
 
 // ------------------------------------------------------------ tile sweeps
 
-// Cooperative load of `n` records into shared memory.
-__device__ __forceinline__ void load_recs(FaceRec* sh, const FaceRec* recs,
-                                          const int* list, int base, int n,
-                                          bool identity) {
-    const float4* src = reinterpret_cast<const float4*>(recs);
-    float4* dst = reinterpret_cast<float4*>(sh);
-    for (int i = threadIdx.x; i < n * kRecVec4; i += blockDim.x) {
-        const int j = i / kRecVec4, w = i % kRecVec4;
-        const int f = identity ? base + j : list[base + j];
-        dst[i] = src[size_t(f) * kRecVec4 + w];
-    }
-}
-
 constexpr int kRecChunk = 64;
+constexpr int kRimCell = 64;     // pixels per side of a rim-flag cell
+constexpr int kRimChunk = 16;    // records staged per warp in the rim phase
 
-struct SweepView {
-    const FaceRec* recs;  // this view's records [n_faces]
-    int n_faces;
-    int W, H, tiles_x, n_tiles;
-    float radius;
+// Fixed-capacity bins filled in one pass: entry i of bin k lives at
+// list[k * cap + i]; the bin's cursor counts every append (also those past
+// the capacity, which are dropped -- the consumer then falls back to
+// scanning all faces, still exact). The consumer resets the cursor.
+struct FixedBins {
+    int* cursor;  // [views * bins]
+    int* list;    // [views * bins * cap]
+    int cap;
 };
 
-// Sweep 1: full evaluation inside each face's sweep-1 region.
-// State out: PixState per pixel, active flag per tile.
-static __device__ void sweep1_tile(const SweepView& sv, const BinSet& b, int v,
-                            int tile, const float* prev_depth,
-                            PixState* state, int* active) {
-    __shared__ FaceRec sh[kRecChunk];
-    const int tx = tile % sv.tiles_x, ty = tile / sv.tiles_x;
-    const int x = tx * kTile + (threadIdx.x % kTile);
-    const int y = ty * kTile + (threadIdx.x / kTile);
-    const bool in = x < sv.W && y < sv.H;
-    const float px = float(x) + 0.5f, py = float(y) + 0.5f;
-    const size_t pix = size_t(y) * sv.W + x;
-    const float prev = (in && prev_depth) ? prev_depth[pix] : 0.f;
-
-    float best_depth = 1.f, best_dist = 0.f, best_hz = 0.f;
-    int best_face = -1;
-
-    const bool identity = b.overflow[v] != 0;
-    const int tl = v * sv.n_tiles + tile;
-    const int beg = identity ? 0 : b.offset[tl];
-    const int end = identity ? sv.n_faces : b.cursor[tl];
-    const int* list = b.list + size_t(v) * b.cap;
-    for (int base = beg; base < end; base += kRecChunk) {
-        const int n = imin_(kRecChunk, end - base);
-        __syncthreads();
-        load_recs(sh, sv.recs, list, base, n, identity);
-        __syncthreads();
-        if (!in) continue;
-        for (int i = 0; i < n; i++) {
-            const FaceRec& r = sh[i];
-            if (!(r.flags & kFaceValid)) continue;
-            if (x < r.rx0 || x > r.rx1 || y < r.ry0 || y > r.ry1) continue;
-            if (!soft_covers(px, py, r)) continue;
-            const TriDist td = signed_dist(px, py, r);
-            const float hz = hard_depth(px, py, r);
-            const float depth = shifted_depth(td.dist, hz, sv.radius);
-            if (prev_depth && depth <= prev + 1e-4f) continue;
-            const int f = identity ? base + i : list[base + i];
-            if (beats(depth, f, best_depth, best_face)) {
-                best_depth = depth;
-                best_face = f;
-                best_dist = td.dist;
-                best_hz = hz;
-            }
-        }
-    }
-    if (in) {
-        state[size_t(v) * sv.W * sv.H + pix] =
-                PixState{best_depth, best_face, best_dist, best_hz};
-    }
-    const int act = __syncthreads_or(in && best_depth > 0.5f);
-    if (threadIdx.x == 0) active[tl] = act;
+// Thread -> pixel of a 16x16 tile: 8 warps of 8x4 pixels (2-D warp
+// footprints keep more lanes inside a small triangle's bbox).
+__device__ __forceinline__ void tile_xy(int tile, int tiles_x, int* x,
+                                        int* y) {
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    *x = (tile % tiles_x) * kTile + (w & 1) * 8 + (l & 7);
+    *y = (tile / tiles_x) * kTile + (w >> 1) * 4 + (l >> 3);
 }
 
-// Sweep 2: soft-rim fragments of safe faces outside their sweep-1 region,
-// for pixels still uncovered by a hard fragment. Returns the survivor.
-static __device__ PixState sweep2_tile(const SweepView& sv, const BinSet& b, int v,
-                                int tile, const float* prev_depth,
-                                const PixState* state, const int* active,
-                                int* out_x, int* out_y, bool* out_in) {
+// 8-bit mask of the 8x4 blocks of tile (tx, ty) that a pixel rectangle
+// touches (bit w = warp w of tile_xy).
+__device__ __forceinline__ int block_mask(int tx, int ty, int x0, int x1,
+                                          int y0, int y1) {
+    int m = 0;
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+        const int bx0 = tx * kTile + (w & 1) * 8, by0 = ty * kTile + (w >> 1) * 4;
+        if (x0 <= bx0 + 7 && x1 >= bx0 && y0 <= by0 + 3 && y1 >= by0) m |= 1 << w;
+    }
+    return m;
+}
+
+struct SweepArgs {
+    const FaceRec* recs;  // this view's records [n_faces]
+    int n_faces, W, H, tiles_x, n_tiles, v;
+    float radius;
+    const float* prev;    // this view's peeling depth [H][W] or null
+    int rim_cells_x;
+    const int* rim;       // this view's rim-possible flags per cell
+    uint32_t* status;     // device status word
+};
+
+__device__ __forceinline__ void fold(Survivor& s, float depth, int f,
+                                     bool hard) {
+    if (beats(depth, f, s.depth, s.face)) {
+        s.depth = depth;
+        s.face = f;
+        s.hard = hard;
+    }
+}
+
+// Full evaluation of a fragment the way RasterizeSoftCpu does it (the
+// caller has checked soft coverage).
+__device__ __forceinline__ void eval_full(Survivor& s, float px, float py,
+                                          const FaceRec& r, int f,
+                                          float radius, bool peel,
+                                          float prev) {
+    const TriDist td = signed_dist(px, py, r);
+    const float hz = td.dist >= 0.f ? hard_depth(px, py, r) : 0.f;
+    const float depth = shifted_depth(td.dist, hz, radius);
+    if (peel && depth <= prev + 1e-4f) return;
+    fold(s, depth, f, td.dist >= 0.f);
+}
+
+// Appends face f to the sweep-1 bins of the tiles its region touches; the
+// entry carries the 8-bit block mask so untouched warps skip it.
+__device__ __forceinline__ void bin_sweep1(const FaceRec& r, int f,
+                                           int tiles_x, FixedBins b1,
+                                           size_t view_bin0) {
+    if (r.rx0 > r.rx1 || r.ry0 > r.ry1) return;
+    for (int ty = r.ry0 / kTile; ty <= r.ry1 / kTile; ty++)
+        for (int tx = r.rx0 / kTile; tx <= r.rx1 / kTile; tx++) {
+            const size_t bin = view_bin0 + size_t(ty) * tiles_x + tx;
+            const int slot = atomicAdd(&b1.cursor[bin], 1);
+            if (slot < b1.cap)
+                b1.list[bin * b1.cap + slot] =
+                        (f << 8) | block_mask(tx, ty, r.rx0, r.rx1, r.ry0, r.ry1);
+        }
+}
+
+// Sweep 1 over the tile's bin: inside and boundary fragments are folded;
+// far (rim) fragments are left to the rim phase. At the end each warp (an
+// 8x4-pixel block) reports whether it still holds an open pixel
+// (depth > 0.5) inside some face's soft reach. Tiles without such blocks
+// finish here through the epilogue; the others store their survivors and
+// the open-block mask for the rim phase.
+template <class Epi>
+static __device__ void sweep1_tile(const SweepArgs& a, FixedBins b1,
+                                   int tile, int2* state, int* mask_out,
+                                   Epi& epi) {
     __shared__ FaceRec sh[kRecChunk];
-    const int tx = tile % sv.tiles_x, ty = tile / sv.tiles_x;
-    const int x = tx * kTile + (threadIdx.x % kTile);
-    const int y = ty * kTile + (threadIdx.x / kTile);
-    const bool in = x < sv.W && y < sv.H;
+    __shared__ int ids[kRecChunk];
+    __shared__ int warp_open[8];
+    __shared__ int n_entries;
+    int x, y;
+    tile_xy(tile, a.tiles_x, &x, &y);
+    const int w = threadIdx.x >> 5;
+    const bool in = x < a.W && y < a.H;
     const float px = float(x) + 0.5f, py = float(y) + 0.5f;
-    const size_t pix = size_t(y) * sv.W + x;
-    *out_x = x;
-    *out_y = y;
-    *out_in = in;
-    PixState s{1.f, -1, 0.f, 0.f};
-    if (in) s = state[size_t(v) * sv.W * sv.H + pix];
-    const int tl = v * sv.n_tiles + tile;
-    if (!active[tl]) return s;
-    const float prev = (in && prev_depth) ? prev_depth[pix] : 0.f;
-    const bool identity = b.overflow[v] != 0;
-    const int beg = identity ? 0 : b.offset[tl];
-    const int end = identity ? sv.n_faces : b.cursor[tl];
-    const int* list = b.list + size_t(v) * b.cap;
-    const bool open = in && s.depth > 0.5f;
-    for (int base = beg; base < end; base += kRecChunk) {
+    const size_t pix = size_t(y) * a.W + x;
+    const bool peel = a.prev != nullptr;
+    const float prev = (in && peel) ? a.prev[pix] : 0.f;
+    const bool fast_ok = a.radius < kMaxFastRadius;
+    const size_t bin = size_t(a.v) * a.n_tiles + tile;
+    if (threadIdx.x == 0) {
+        n_entries = b1.cursor[bin];
+        b1.cursor[bin] = 0;  // ready for the next use
+    }
+    __syncthreads();
+    const bool identity = n_entries > b1.cap;  // overflow: all faces
+    if (identity && threadIdx.x == 0) atomicOr(a.status, kStatusBinOverflow);
+    const int end = identity ? a.n_faces : n_entries;
+    const int* list = b1.list + bin * b1.cap;
+
+    Survivor s{1.f, -1, false};
+    for (int base = 0; base < end; base += kRecChunk) {
         const int n = imin_(kRecChunk, end - base);
         __syncthreads();
-        load_recs(sh, sv.recs, list, base, n, identity);
+        if (threadIdx.x < n)
+            ids[threadIdx.x] = identity ? ((base + threadIdx.x) << 8) | 0xff
+                                        : list[base + threadIdx.x];
         __syncthreads();
-        if (!open) continue;
+        {
+            const float4* src = reinterpret_cast<const float4*>(a.recs);
+            float4* dst = reinterpret_cast<float4*>(sh);
+            for (int i = threadIdx.x; i < n * kRecVec4; i += blockDim.x) {
+                const int j = i / kRecVec4, q = i % kRecVec4;
+                dst[i] = src[size_t(ids[j] >> 8) * kRecVec4 + q];
+            }
+        }
+        __syncthreads();
         for (int i = 0; i < n; i++) {
+            const int ent = ids[i];
+            if (!((ent >> w) & 1)) continue;  // region misses this warp
+            if (!in) continue;
             const FaceRec& r = sh[i];
-            const uint32_t need = kFaceValid | kFaceSafe;
-            if ((r.flags & need) != need) continue;
-            if (x < r.bx0 || x > r.bx1 || y < r.by0 || y > r.by1) continue;
-            if (x >= r.rx0 && x <= r.rx1 && y >= r.ry0 && y <= r.ry1) continue;
-            if (!soft_covers(px, py, r)) continue;
-            const TriDist td = signed_dist(px, py, r);
-            // dist < 0 here for safe faces; the hard-type branch is kept so
-            // the expression is the reference's in every case.
-            const float hz = td.dist >= 0.f ? hard_depth(px, py, r) : 0.f;
-            const float depth = shifted_depth(td.dist, hz, sv.radius);
-            if (prev_depth && depth <= prev + 1e-4f) continue;
-            const int f = identity ? base + i : list[base + i];
-            if (beats(depth, f, s.depth, s.face)) {
-                s.depth = depth;
-                s.face = f;
-                s.dist = td.dist;
-                s.hard_z = td.dist >= 0.f ? hz : hard_depth(px, py, r);
+            if (x < r.rx0 || x > r.rx1 || y < r.ry0 || y > r.ry1) continue;
+            if (!(r.flags & kFaceValid)) continue;
+            const int f = ent >> 8;
+            int c = classify(px, py, r);
+            if (c == kFar && !fast_ok) c = kBoundary;
+            if (c == kInside) {
+                if (!(r.flags & kFaceSoftInside) && !soft_covers(px, py, r))
+                    continue;
+                const float depth =
+                        0.5f * std_min(std_max(hard_depth(px, py, r), 0.f), 1.f);
+                if (peel && depth <= prev + 1e-4f) continue;
+                fold(s, depth, f, true);
+            } else if (c == kBoundary) {
+                if (!soft_covers(px, py, r)) continue;
+                eval_full(s, px, py, r, f, a.radius, peel, prev);
             }
         }
     }
-    return s;
+    const int cell = (y / kRimCell) * a.rim_cells_x + (x / kRimCell);
+    const unsigned ob = __ballot_sync(0xffffffffu, in && s.depth > 0.5f &&
+                                                           a.rim[cell] != 0);
+    if ((threadIdx.x & 31) == 0) warp_open[w] = ob != 0u;
+    __syncthreads();
+    int m = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) m |= warp_open[k] << k;
+    if (m == 0) {
+        if (threadIdx.x == 0) mask_out[bin] = 0;
+        epi(a, x, y, in, s);
+    } else {
+        if (threadIdx.x == 0) mask_out[bin] = m;
+        if (in) state[size_t(a.v) * a.W * a.H + pix] = pack(s);
+    }
+}
+
+// Conservative test whether the soft triangle can cover a pixel centre of
+// 8x4 block (bx, by): false only if, for one barycentric coordinate, all
+// four corner centres are below -margin. The coordinates are affine in the
+// pixel centre; the margin (~170 float ulps of the terms' magnitude) bounds
+// the rounding of this float evaluation and of soft_covers' own.
+__device__ __forceinline__ bool tri_touches_block(const FaceRec& r, int bx,
+                                                  int by) {
+    const float xs[2] = {float(bx * 8) + 0.5f, float(bx * 8) + 7.5f};
+    const float ys[2] = {float(by * 4) + 0.5f, float(by * 4) + 3.5f};
+    const float ia = fabsf(r.s_inv_area);
+    float mx0 = -3e38f, mx1 = -3e38f, mx2 = -3e38f, mag = 0.f;
+#pragma unroll
+    for (int i = 0; i < 2; i++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const float px = xs[i], py = ys[j];
+            const float a0 = (r.s1x - px) * (r.s2y - py), b0 = (r.s1y - py) * (r.s2x - px);
+            const float a1 = (r.s2x - px) * (r.s0y - py), b1 = (r.s2y - py) * (r.s0x - px);
+            const float l0 = (a0 - b0) * r.s_inv_area;
+            const float l1 = (a1 - b1) * r.s_inv_area;
+            mx0 = fmaxf(mx0, l0);
+            mx1 = fmaxf(mx1, l1);
+            mx2 = fmaxf(mx2, 1.f - l0 - l1);
+            mag = fmaxf(mag, (fabsf(a0) + fabsf(b0) + fabsf(a1) + fabsf(b1)) * ia);
+        }
+    const float margin = 1e-5f * (1.f + mag);
+    return !(mx0 < -margin || mx1 < -margin || mx2 < -margin);
+}
+
+// Rim-phase binning: a safe face enters the bin of every open 8x4 block its
+// soft triangle may touch. One warp per face, lanes striding over the
+// blocks of its soft bbox.
+static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
+                          const FaceRec* recs_all, const int* mask,
+                          FixedBins b2) {
+    const int f = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int v = blockIdx.y;
+    if (f >= n_faces) return;
+    const FaceRec& r = recs_all[size_t(v) * n_faces + f];
+    const uint32_t need = kFaceValid | kFaceSafe;
+    if ((r.flags & need) != need) return;
+    const int blocks_x = tiles_x * 2;
+    const int* mk = mask + size_t(v) * n_tiles;
+    const size_t bin0 = size_t(v) * n_tiles * 8;
+    const int bx0 = r.bx0 >> 3, by0 = r.by0 >> 2;
+    const int nbx = (r.bx1 >> 3) - bx0 + 1;
+    const int nb = nbx * ((r.by1 >> 2) - by0 + 1);
+    for (int i = lane; i < nb; i += 32) {
+        const int bx = bx0 + i % nbx, by = by0 + i / nbx;
+        const int m = mk[(by >> 2) * tiles_x + (bx >> 1)];
+        if (!((m >> ((by & 3) * 2 + (bx & 1))) & 1)) continue;
+        if (!tri_touches_block(r, bx, by)) continue;
+        const size_t bin = bin0 + size_t(by) * blocks_x + bx;
+        const int slot = atomicAdd(&b2.cursor[bin], 1);
+        if (slot < b2.cap) b2.list[bin * b2.cap + slot] = f;
+    }
+}
+
+// Rim phase for the open pixels of an open 8x4 block: folds every fragment
+// of the faces in the block's bin (records staged per warp in shared
+// memory), pruned by the bbox depth bound. Fragments at |dist| >= radius
+// all have depth exactly 1, where the latest covering face wins: once a
+// pixel holds such a survivor, older faces at depth 1 are skipped without a
+// coverage test (in list order this costs ~ln(n) tests, as for a running
+// maximum).
+template <class Epi>
+static __device__ void rim_tile(const SweepArgs& a, FixedBins b2, int tile,
+                                const int2* state, const int* mask,
+                                Epi& epi) {
+    __shared__ FaceRec recs_sh[8][kRimChunk];
+    __shared__ int ids_sh[8][kRimChunk];
+    const size_t tbin = size_t(a.v) * a.n_tiles + tile;
+    const int m = mask[tbin];
+    if (m == 0) return;  // finished in sweep 1
+    int x, y;
+    tile_xy(tile, a.tiles_x, &x, &y);
+    const bool in = x < a.W && y < a.H;
+    const float px = float(x) + 0.5f, py = float(y) + 0.5f;
+    const size_t pix = size_t(y) * a.W + x;
+    const bool peel = a.prev != nullptr;
+    const float prev = (in && peel) ? a.prev[pix] : 0.f;
+    Survivor s{1.f, -1, false};
+    if (in) s = unpack(state[size_t(a.v) * a.W * a.H + pix]);
+    const bool open = in && s.depth > 0.5f;
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if ((m >> w) & 1) {
+        const int bx = (tile % a.tiles_x) * 2 + (w & 1);
+        const int by = (tile / a.tiles_x) * 4 + (w >> 1);
+        const size_t bin = size_t(a.v) * a.n_tiles * 8 +
+                           size_t(by) * (a.tiles_x * 2) + bx;
+        int n = 0;
+        if (lane == 0) {
+            n = b2.cursor[bin];
+            b2.cursor[bin] = 0;  // ready for the next use
+        }
+        n = __shfl_sync(0xffffffffu, n, 0);
+        const bool identity = n > b2.cap;  // overflow: all faces
+        if (identity && lane == 0) atomicOr(a.status, kStatusBinOverflow);
+        const int end = identity ? a.n_faces : n;
+        const int* lst = b2.list + bin * b2.cap;
+        const float4* src = reinterpret_cast<const float4*>(a.recs);
+        for (int base = 0; base < end; base += kRimChunk) {
+            const int cn = imin_(kRimChunk, end - base);
+            __syncwarp();
+            if (lane < cn)
+                ids_sh[w][lane] = identity ? a.n_faces - 1 - (base + lane)
+                                           : lst[base + lane];
+            __syncwarp();
+            float4* dst = reinterpret_cast<float4*>(recs_sh[w]);
+            for (int i = lane; i < cn * kRecVec4; i += 32) {
+                const int j = i / kRecVec4, q = i % kRecVec4;
+                dst[i] = src[size_t(ids_sh[w][j]) * kRecVec4 + q];
+            }
+            __syncwarp();
+            if (!open) continue;
+            for (int j = 0; j < cn; j++) {
+                const int f = ids_sh[w][j];
+                const FaceRec& r = recs_sh[w][j];
+                const uint32_t need = kFaceValid | kFaceSafe;
+                if ((r.flags & need) != need) continue;
+                if (x < r.bx0 || x > r.bx1 || y < r.by0 || y > r.by1) continue;
+                const float lb = rim_depth_lb(px, py, r, a.radius);
+                if (lb > s.depth) continue;
+                if (lb == 1.f && f < s.face) continue;  // 1.0 tie, older face
+                if (!soft_covers(px, py, r)) continue;
+                if (lb == 1.f) {
+                    // |dist| >= radius: the Eq.3 depth is exactly 1
+                    if (peel && 1.f <= prev + 1e-4f) continue;
+                    fold(s, 1.f, f, false);
+                } else {
+                    eval_full(s, px, py, r, f, a.radius, peel, prev);
+                }
+            }
+        }
+    }
+    epi(a, x, y, in, s);
+}
+
+template <class Epi>
+__global__ void __launch_bounds__(kTileThreads)
+        k_sweep1(SweepArgs a0, FixedBins b1, int2* state, int* mask,
+                 size_t view_stride_recs, size_t view_stride_px,
+                 size_t view_stride_rim, Epi epi) {
+    SweepArgs a = a0;
+    a.v = blockIdx.y;
+    a.recs = a0.recs + a.v * view_stride_recs;
+    a.rim = a0.rim + a.v * view_stride_rim;
+    if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
+    sweep1_tile(a, b1, blockIdx.x, state, mask, epi);
+}
+
+template <class Epi>
+__global__ void __launch_bounds__(kTileThreads)
+        k_rim(SweepArgs a0, FixedBins b2, const int2* state, const int* mask,
+              size_t view_stride_recs, size_t view_stride_px,
+              size_t view_stride_rim, Epi epi) {
+    SweepArgs a = a0;
+    a.v = blockIdx.y;
+    a.recs = a0.recs + a.v * view_stride_recs;
+    a.rim = a0.rim + a.v * view_stride_rim;
+    if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
+    rim_tile(a, b2, blockIdx.x, state, mask, epi);
+}
+
+// Marks the rim-flag cells a safe face's soft bbox reaches: a superset of
+// where the rim phase can find fragments (those outside the sweep-1 region
+// and the deferred far ones inside it).
+__device__ __forceinline__ void mark_rim_cells(const FaceRec& r, int* rim,
+                                               int cells_x) {
+    const uint32_t need = kFaceValid | kFaceSafe;
+    if ((r.flags & need) != need) return;
+    for (int cy = r.by0 / kRimCell; cy <= r.by1 / kRimCell; cy++)
+        for (int cx = r.bx0 / kRimCell; cx <= r.bx1 / kRimCell; cx++)
+            rim[cy * cells_x + cx] = 1;
 }
 
 }  // namespace dressi

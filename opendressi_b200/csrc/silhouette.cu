@@ -52,9 +52,14 @@ __device__ __forceinline__ float sil_pixel(float dist, float cov, float target,
 // the in-graph Adam: t_new = t + 1, bc = 1 - pow(beta, t_new)).
 __global__ void k_transform(const float* pos, const float* mvps, int n_verts,
                             float4* clip, float* scalars, float b1, float b2,
-                            int advance) {
+                            int advance, int* rim, int rim_cells) {
     const int v = blockIdx.y;
     const int u = blockIdx.x * blockDim.x + threadIdx.x;
+    if (blockIdx.x == 0) {
+        // this iteration's face setup re-marks the rim cells
+        for (int i = threadIdx.x; i < rim_cells; i += blockDim.x)
+            rim[size_t(v) * rim_cells + i] = 0;
+    }
     if (advance && v == 0 && blockIdx.x == 0 && threadIdx.x == 0) {
         const float t_new = scalars[0] + 1.f;
         scalars[0] = t_new;
@@ -107,30 +112,26 @@ __global__ void k_face_setup_sil(SoftDims d, const float4* clip,
         return;
     }
     *out = r;
-    if (r.rx0 > r.rx1 || r.ry0 > r.ry1) return;
-    int tx0, tx1, ty0, ty1;
-    tile_range(r.rx0, r.rx1, r.ry0, r.ry1, &tx0, &tx1, &ty0, &ty1);
-    int* cnt = b.bin1.count + size_t(v) * d.n_tiles;
-    for (int ty = ty0; ty <= ty1; ty++)
-        for (int tx = tx0; tx <= tx1; tx++) atomicAdd(&cnt[ty * d.tiles_x + tx], 1);
+    mark_rim_cells(r, b.rim + size_t(v) * d.rim_cells, d.rim_cells_x);
+    bin_sweep1(r, f, d.tiles_x, b.bin1, size_t(v) * d.n_tiles);
 }
 
+// SignedDistGradToTri (cpu_raster.cpp:153-175) for the survivor's hard
+// triangle, then GatherDistGrad's screen->clip chain (f_ops.cpp:1335-1349),
+// accumulated straight into the view's clip gradient (its ColSum).
 __device__ __forceinline__ void sil_scatter(float px, float py, float g,
+                                            const TriDist& td,
                                             const FaceRec& r,
                                             const float4* clip_v, float W,
                                             float H, float* gclip_v) {
-    const float hs[3][2] = {{r.h0x, r.h0y}, {r.h1x, r.h1y}, {r.h2x, r.h2y}};
-    const uint32_t idx[3] = {r.i0, r.i1, r.i2};
-    const float4 c[3] = {clip_v[r.i0], clip_v[r.i1], clip_v[r.i2]};
-    // SignedDistToTri + SignedDistGradToTri (cpu_raster.cpp:114-175) on the
-    // survivor's hard triangle, then GatherDistGrad's chain to clip
-    // (f_ops.cpp:1335-1349).
-    const TriDist td = signed_dist(px, py, r);
     const float d = fabsf(td.dist);
     if (d < 1e-6f) return;
+    const float hx[3] = {r.h0x, r.h1x, r.h2x};
+    const float hy[3] = {r.h0y, r.h1y, r.h2y};
+    const uint32_t idx[3] = {r.i0, r.i1, r.i2};
     const int ia = td.edge, ib = (td.edge + 1) % 3;
-    const float qx = hs[ia][0] + td.t * (hs[ib][0] - hs[ia][0]);
-    const float qy = hs[ia][1] + td.t * (hs[ib][1] - hs[ia][1]);
+    const float qx = hx[ia] + td.t * (hx[ib] - hx[ia]);
+    const float qy = hy[ia] + td.t * (hy[ib] - hy[ia]);
     const float sgn = td.dist >= 0.f ? 1.f : -1.f;
     const float nx = (px - qx) / d;
     const float ny = (py - qy) / d;
@@ -143,58 +144,70 @@ __device__ __forceinline__ void sil_scatter(float px, float py, float g,
         const float gsx = g * gk[0];
         const float gsy = g * gk[1];
         if (gsx == 0.f && gsy == 0.f) continue;
+        const float4 c = clip_v[idx[k]];
         float* dst = gclip_v + size_t(idx[k]) * 4;
-        atomicAdd(dst + 0, gsx * 0.5f * W / c[k].w);
-        atomicAdd(dst + 1, gsy * 0.5f * H / c[k].w);
-        atomicAdd(dst + 3, -(gsx * 0.5f * W * c[k].x + gsy * 0.5f * H * c[k].y) /
-                                   (c[k].w * c[k].w));
+        atomicAdd(dst + 0, gsx * 0.5f * W / c.w);
+        atomicAdd(dst + 1, gsy * 0.5f * H / c.w);
+        atomicAdd(dst + 3, -(gsx * 0.5f * W * c.x + gsy * 0.5f * H * c.y) /
+                                   (c.w * c.w));
     }
 }
 
-// Sweep 2 + the silhouette loss epilogue: loss partials and the per-view
-// clip gradient (GatherDistGrad summed over pixels = its ColSum).
-__global__ void __launch_bounds__(kTileThreads)
-        k_sweep2_sil(SoftDims d, SoftBuffers b, SilParams p,
-                     const float4* clip, const float* targets, float* gclip,
-                     double* loss_slots, float4* rs_out) {
-    const int v = blockIdx.y;
-    SweepView sv{b.recs + size_t(v) * d.n_faces, d.n_faces, d.W, d.H,
-                 d.tiles_x, d.n_tiles, d.radius};
-    int x, y;
-    bool in;
-    const PixState s = sweep2_tile(sv, b.bin2, v, blockIdx.x, nullptr,
-                                   b.state, b.active, &x, &y, &in);
-    double lv = 0.0;
-    if (in) {
-        const size_t pix = size_t(v) * d.W * d.H + size_t(y) * d.W + x;
-        const bool cov = s.face >= 0;
-        const float dist = cov ? s.dist : 0.f;
-        float g;
-        lv = sil_pixel(dist, cov ? 1.f : 0.f, targets[pix], p.k, p.c, &g);
-        if (rs_out) {
-            rs_out[pix] = cov ? make_float4(s.dist, sv.recs[s.face].fid,
-                                            s.hard_z, 1.f)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
+// Epilogue of the fused iteration: the loss image (block-summed into the
+// loss slots) and, for the rim pixels that carry a gradient, the per-view
+// clip gradient. A pixel whose survivor is a hard fragment (dist >= 0) has
+// pred = max(1, sigmoid(.)) = 1 exactly and a zero gradient, so its
+// distance is never needed.
+struct EpiSil {
+    const float* targets;   // [views][R][R]
+    const float4* clip;     // [views][V]
+    float* gclip;           // [views][V][4]
+    double* loss_slots;
+    float4* rs_out;         // optional RasterizeSoft images
+    float k, c;
+    int n_verts;
+    __device__ void operator()(const SweepArgs& a, int x, int y, bool in,
+                               const Survivor& s) const {
+        double lv = 0.0;
+        if (in) {
+            const size_t pix = size_t(a.v) * a.W * a.H + size_t(y) * a.W + x;
+            const float t = targets[pix];
+            const float px = float(x) + 0.5f, py = float(y) + 0.5f;
+            float g = 0.f;
+            if (s.face < 0) {
+                lv = sil_pixel(0.f, 0.f, t, k, c, &g);
+                if (rs_out) rs_out[pix] = make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {
+                const FaceRec& r = a.recs[s.face];
+                if (s.hard && !rs_out) {
+                    const float diff = t - 1.f;
+                    lv = diff * diff * c;
+                } else {
+                    const TriDist td = signed_dist(px, py, r);
+                    lv = sil_pixel(td.dist, 1.f, t, k, c, &g);
+                    if (rs_out)
+                        rs_out[pix] = make_float4(td.dist, r.fid,
+                                                  hard_depth(px, py, r), 1.f);
+                    if (g != 0.f)
+                        sil_scatter(px, py, g, td, r,
+                                    clip + size_t(a.v) * n_verts, float(a.W),
+                                    float(a.H),
+                                    gclip + size_t(a.v) * n_verts * 4);
+                }
+            }
         }
-        if (cov && g != 0.f) {
-            sil_scatter(float(x) + 0.5f, float(y) + 0.5f, g, sv.recs[s.face],
-                        clip + size_t(v) * d.n_verts, float(d.W), float(d.H),
-                        gclip + size_t(v) * d.n_verts * 4);
-        }
-    }
-    // block sum of the loss image
-    __shared__ double red[kTileThreads / 32];
+        // warp sum of the loss image (no block barrier: the warps of a
+        // tile finish independently)
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lv += __shfl_down_sync(0xffffffffu, lv, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = lv;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        double sum = 0.0;
-        for (int i = 0; i < kTileThreads / 32; i++) sum += red[i];
-        atomicAdd(&loss_slots[(size_t(v) * d.n_tiles + blockIdx.x) % kLossSlots],
-                  sum);
+        for (int o = 16; o > 0; o >>= 1)
+            lv += __shfl_down_sync(0xffffffffu, lv, o);
+        if ((threadIdx.x & 31) == 0) {
+            const size_t slot = ((size_t(a.v) * a.n_tiles + blockIdx.x) * 8 +
+                                 (threadIdx.x >> 5)) % kLossSlots;
+            atomicAdd(&loss_slots[slot], lv);
+        }
     }
-}
+};
 
 // g_pos = sum_v MVP_v^T g_clip_v (TransformToClipVar's backward); zeroes
 // g_clip for the next iteration. With `update`, also applies the in-graph
@@ -266,10 +279,11 @@ void sil_forward_backward(const SoftDims& d, const SilParams& p,
                           cudaStream_t s) {
     const dim3 vg((p.n_verts + 255) / 256, p.views);
     {
-    ProfScope ps("transform", s);
-    k_transform<<<vg, 256, 0, s>>>(b.pos, b.mvps, p.n_verts,
-                                   reinterpret_cast<float4*>(b.clip),
-                                   b.scalars, p.b1, p.b2, 1);
+        ProfScope ps("transform", s);
+        k_transform<<<vg, 256, 0, s>>>(b.pos, b.mvps, p.n_verts,
+                                       reinterpret_cast<float4*>(b.clip),
+                                       b.scalars, p.b1, p.b2, 1, b.soft.rim,
+                                       d.rim_cells);
     }
     const dim3 fg((d.n_faces + 127) / 128, d.views);
     {
@@ -278,12 +292,10 @@ void sil_forward_backward(const SoftDims& d, const SilParams& p,
                 d, reinterpret_cast<const float4*>(b.clip), b.faces, b.soft);
     }
     check_launch();
-    soft_bin_and_sweep1(d, b.soft, nullptr, s);
-    ProfScope ps("sweep2_sil", s);
-    k_sweep2_sil<<<dim3(d.n_tiles, d.views), kTileThreads, 0, s>>>(
-            d, b.soft, p, reinterpret_cast<const float4*>(b.clip), b.targets,
-            b.gclip, b.loss_slots, reinterpret_cast<float4*>(rs_out));
-    check_launch();
+    EpiSil epi{b.targets, reinterpret_cast<const float4*>(b.clip), b.gclip,
+               b.loss_slots, reinterpret_cast<float4*>(rs_out), p.k, p.c,
+               p.n_verts};
+    launch_sweeps(d, b.soft, nullptr, epi, s);
 }
 
 void sil_grad_reduce(const SilParams& p, const SilBuffers& b, bool update,

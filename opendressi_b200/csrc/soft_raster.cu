@@ -2,6 +2,7 @@
 // launchers for F::SoftClip, F::RasterizeSoft and its dist-channel backward.
 // See raster_soft.cuh for the exactness argument.
 #include <algorithm>
+#include <cstdlib>
 
 #include "kernels.h"
 
@@ -10,54 +11,48 @@ namespace dressi {
 // ------------------------------------------------------------- buffers
 
 void default_caps(SoftDims* d) {
-    // Sweep 1 bins each face into the tiles of its hard bbox + margin
-    // (a few tiles for the meshes of the configs); sweep 2 only into active
-    // (silhouette) tiles. Overflow is detected on the device and falls back
-    // to an exhaustive, still exact, sweep.
-    const long long f = d->n_faces;
-    const long long t = d->n_tiles;
-    d->cap1 = int(std::min<long long>(std::max<long long>(16 * f, 4 * t) + 4096,
-                                      1ll << 30));
-    d->cap2 = d->cap1;
+    // Sweep-1 bins hold the faces whose hard bbox (+ margin) touches a tile
+    // (~4 tiles per face on the configs' meshes); rim bins hold the soft
+    // triangles touching an open 8x4 block. An overflowing bin falls back to
+    // an exhaustive, still exact, scan of all faces.
+    const long long f = d->n_faces, t = std::max(d->n_tiles, 1);
+    d->cap1 = int(std::min<long long>(std::max<long long>(256, 8 * ((4 * f + t - 1) / t)),
+                                      1 << 16));
+    d->cap2 = 1024;
+    // Test hook: DRESSI_B200_BIN_CAP forces a (small) capacity so the
+    // overflow fallback can be exercised.
+    if (const char* e = std::getenv("DRESSI_B200_BIN_CAP")) {
+        const long long c = std::atoll(e);
+        if (c > 0) d->cap1 = d->cap2 = int(std::min<long long>(c, 1 << 16));
+    }
 }
 
 void carve_soft(Arena& a, const SoftDims& d, SoftBuffers* b) {
     const size_t vt = size_t(d.views) * d.n_tiles;
+    const size_t vb = vt * 8;  // 8x4-pixel blocks of the rim phase
     b->recs = a.take<FaceRec>(size_t(d.views) * std::max(d.n_faces, 1));
-    for (BinSet* bs : {&b->bin1, &b->bin2}) {
-        bs->count = a.take<int>(vt);
-        bs->offset = a.take<int>(vt);
-        bs->cursor = a.take<int>(vt);
-        bs->overflow = a.take<int>(d.views);
-    }
     b->bin1.cap = d.cap1;
+    b->bin1.cursor = a.take<int>(vt);
+    b->bin1.list = a.take<int>(vt * d.cap1);
     b->bin2.cap = d.cap2;
-    b->bin1.list = a.take<int>(size_t(d.views) * d.cap1);
-    b->bin2.list = a.take<int>(size_t(d.views) * d.cap2);
-    b->state = a.take<PixState>(size_t(d.views) * d.W * d.H);
+    b->bin2.cursor = a.take<int>(vb);
+    b->bin2.list = a.take<int>(vb * d.cap2);
+    b->state = a.take<int2>(size_t(d.views) * d.W * d.H);
     b->active = a.take<int>(vt);
+    b->rim = a.take<int>(size_t(d.views) * std::max(d.rim_cells, 1));
     b->status = a.take<uint32_t>(4);
 }
 
 void init_soft(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
     const size_t vt = size_t(d.views) * d.n_tiles;
-    DRESSI_CUDA(cudaMemsetAsync(b.bin1.count, 0, vt * sizeof(int), s));
-    DRESSI_CUDA(cudaMemsetAsync(b.bin2.count, 0, vt * sizeof(int), s));
+    DRESSI_CUDA(cudaMemsetAsync(b.bin1.cursor, 0, vt * sizeof(int), s));
+    DRESSI_CUDA(cudaMemsetAsync(b.bin2.cursor, 0, vt * 8 * sizeof(int), s));
     DRESSI_CUDA(cudaMemsetAsync(b.status, 0, 4 * sizeof(uint32_t), s));
+    DRESSI_CUDA(cudaMemsetAsync(b.rim, 0,
+                                size_t(d.views) * d.rim_cells * sizeof(int), s));
 }
 
 // ---------------------------------------------------------- face setup
-
-__device__ __forceinline__ void count_tiles(const FaceRec& r, int x0, int x1,
-                                            int y0, int y1, int* count,
-                                            int tiles_x) {
-    if (x0 > x1 || y0 > y1) return;
-    int tx0, tx1, ty0, ty1;
-    tile_range(x0, x1, y0, y1, &tx0, &tx1, &ty0, &ty1);
-    for (int ty = ty0; ty <= ty1; ty++)
-        for (int tx = tx0; tx <= tx1; tx++)
-            atomicAdd(&count[ty * tiles_x + tx], 1);
-}
 
 // Op-level face setup: explicit soft clip / face ids / faces
 // (RasterizeSoftCpu's per-face prologue, cpu_raster.cpp:260-298).
@@ -119,136 +114,40 @@ __global__ void k_face_setup_op(SoftDims d, SoftOpInputs in, SoftBuffers b) {
         return;
     }
     *out = r;
-    count_tiles(r, r.rx0, r.rx1, r.ry0, r.ry1,
-                b.bin1.count + size_t(v) * d.n_tiles, d.tiles_x);
-}
-
-// Sweep-1 list fill (after k_bin_scan).
-__global__ void k_bin1_fill(SoftDims d, SoftBuffers b) {
-    const int f = blockIdx.x * blockDim.x + threadIdx.x;
-    const int v = blockIdx.y;
-    if (f >= d.n_faces) return;
-    const FaceRec& r = b.recs[size_t(v) * d.n_faces + f];
-    if (!(r.flags & kFaceValid) || r.rx0 > r.rx1 || r.ry0 > r.ry1) return;
-    const bool of = b.bin1.overflow[v] != 0;
-    int tx0, tx1, ty0, ty1;
-    tile_range(r.rx0, r.rx1, r.ry0, r.ry1, &tx0, &tx1, &ty0, &ty1);
-    int* cur = b.bin1.cursor + size_t(v) * d.n_tiles;
-    int* list = b.bin1.list + size_t(v) * b.bin1.cap;
-    for (int ty = ty0; ty <= ty1; ty++)
-        for (int tx = tx0; tx <= tx1; tx++) {
-            const int slot = atomicAdd(&cur[ty * d.tiles_x + tx], 1);
-            if (!of && slot < b.bin1.cap) list[slot] = f;
-        }
-}
-
-// Does tile (tx, ty) hold a pixel of face r's soft bbox outside its sweep-1
-// region?
-__device__ __forceinline__ bool tile_has_rim(const FaceRec& r, int tx,
-                                             int ty) {
-    const int x0 = imax_(tx * kTile, r.bx0), x1 = imin_(tx * kTile + kTile - 1, r.bx1);
-    const int y0 = imax_(ty * kTile, r.by0), y1 = imin_(ty * kTile + kTile - 1, r.by1);
-    if (x0 > x1 || y0 > y1) return false;
-    const bool inside = x0 >= r.rx0 && x1 <= r.rx1 && y0 >= r.ry0 && y1 <= r.ry1;
-    return !inside;
-}
-
-template <bool kFill>
-__global__ void k_bin2(SoftDims d, SoftBuffers b) {
-    const int f = blockIdx.x * blockDim.x + threadIdx.x;
-    const int v = blockIdx.y;
-    if (f >= d.n_faces) return;
-    const FaceRec& r = b.recs[size_t(v) * d.n_faces + f];
-    const uint32_t need = kFaceValid | kFaceSafe;
-    if ((r.flags & need) != need) return;
-    int tx0, tx1, ty0, ty1;
-    tile_range(r.bx0, r.bx1, r.by0, r.by1, &tx0, &tx1, &ty0, &ty1);
-    const int* act = b.active + size_t(v) * d.n_tiles;
-    int* cnt = b.bin2.count + size_t(v) * d.n_tiles;
-    int* cur = b.bin2.cursor + size_t(v) * d.n_tiles;
-    int* list = b.bin2.list + size_t(v) * b.bin2.cap;
-    const bool of = kFill && b.bin2.overflow[v] != 0;
-    for (int ty = ty0; ty <= ty1; ty++)
-        for (int tx = tx0; tx <= tx1; tx++) {
-            const int t = ty * d.tiles_x + tx;
-            if (!act[t] || !tile_has_rim(r, tx, ty)) continue;
-            if (kFill) {
-                const int slot = atomicAdd(&cur[t], 1);
-                if (!of && slot < b.bin2.cap) list[slot] = f;
-            } else {
-                atomicAdd(&cnt[t], 1);
-            }
-        }
-}
-
-__global__ void __launch_bounds__(kTileThreads)
-        k_sweep1(SoftDims d, SoftBuffers b, const float* prev_depth) {
-    const int v = blockIdx.y;
-    SweepView sv{b.recs + size_t(v) * d.n_faces, d.n_faces, d.W, d.H,
-                 d.tiles_x, d.n_tiles, d.radius};
-    sweep1_tile(sv, b.bin1, v, blockIdx.x,
-                prev_depth ? prev_depth + size_t(v) * d.W * d.H : nullptr,
-                b.state, b.active);
-}
-
-// Sweep 2 with the plain epilogue: out = (dist, face_id, hard_z, coverage).
-__global__ void __launch_bounds__(kTileThreads)
-        k_sweep2_rs(SoftDims d, SoftBuffers b, const float* prev_depth,
-                    float4* out) {
-    const int v = blockIdx.y;
-    SweepView sv{b.recs + size_t(v) * d.n_faces, d.n_faces, d.W, d.H,
-                 d.tiles_x, d.n_tiles, d.radius};
-    int x, y;
-    bool in;
-    const PixState s = sweep2_tile(
-            sv, b.bin2, v, blockIdx.x,
-            prev_depth ? prev_depth + size_t(v) * d.W * d.H : nullptr,
-            b.state, b.active, &x, &y, &in);
-    if (!in) return;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (s.face >= 0) {
-        o.x = s.dist;
-        o.y = sv.recs[s.face].fid;
-        o.z = s.hard_z;
-        o.w = 1.f;
-    }
-    out[size_t(v) * d.W * d.H + size_t(y) * d.W + x] = o;
+    bin_sweep1(r, f, d.tiles_x, b.bin1, size_t(v) * d.n_tiles);
+    mark_rim_cells(r, b.rim + size_t(v) * d.rim_cells, d.rim_cells_x);
 }
 
 static void check_launch() { DRESSI_CUDA(cudaGetLastError()); }
 
-void soft_bin_and_sweep1(const SoftDims& d, const SoftBuffers& b,
-                         const float* prev_depth, cudaStream_t s) {
-    // zero faces: the scan still runs (clears the tile lists); the per-face
-    // passes have nothing to launch
-    const dim3 fg((std::max(d.n_faces, 1) + 127) / 128, d.views);
-    {
-        ProfScope ps("bin_scan", s);
-        k_bin_scan<<<d.views, 1024, 0, s>>>(b.bin1, d.n_tiles, b.status);
-    }
-    {
-        ProfScope ps("bin1_fill", s);
-        k_bin1_fill<<<fg, 128, 0, s>>>(d, b);
-    }
-    {
-        ProfScope ps("sweep1", s);
-        k_sweep1<<<dim3(d.n_tiles, d.views), kTileThreads, 0, s>>>(
-                d, b, prev_depth);
-    }
-    {
-        ProfScope ps("bin2_count", s);
-        k_bin2<false><<<fg, 128, 0, s>>>(d, b);
-    }
-    {
-        ProfScope ps("bin_scan", s);
-        k_bin_scan<<<d.views, 1024, 0, s>>>(b.bin2, d.n_tiles, b.status);
-    }
-    {
-        ProfScope ps("bin2_fill", s);
-        k_bin2<true><<<fg, 128, 0, s>>>(d, b);
-    }
+void soft_rim_bins(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
+    if (d.n_faces == 0) return;
+    const dim3 fg((d.n_faces + 7) / 8, d.views);  // one warp per face
+    ProfScope ps("rim_bin", s);
+    k_rim_bin<<<fg, 256, 0, s>>>(d.n_faces, d.n_tiles, d.tiles_x, b.recs,
+                                 b.active, b.bin2);
     check_launch();
 }
+
+// Epilogue of the op-level RasterizeSoft: the reference's output channels
+// (dist, face_id, hard_z, coverage) recomputed for the survivor.
+struct EpiRS {
+    float4* out;  // [views][H][W]
+    __device__ void operator()(const SweepArgs& a, int x, int y, bool in,
+                               const Survivor& s) const {
+        if (!in) return;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (s.face >= 0) {
+            const FaceRec& r = a.recs[s.face];
+            const float px = float(x) + 0.5f, py = float(y) + 0.5f;
+            o.x = signed_dist(px, py, r).dist;
+            o.y = r.fid;
+            o.z = hard_depth(px, py, r);
+            o.w = 1.f;
+        }
+        out[size_t(a.v) * a.W * a.H + size_t(y) * a.W + x] = o;
+    }
+};
 
 void soft_raster_op(const SoftDims& d, const SoftBuffers& b,
                     const SoftOpInputs& in, float* out, cudaStream_t s) {
@@ -258,11 +157,8 @@ void soft_raster_op(const SoftDims& d, const SoftBuffers& b,
         k_face_setup_op<<<fg, 128, 0, s>>>(d, in, b);
         check_launch();
     }
-    soft_bin_and_sweep1(d, b, in.prev_depth, s);
-    ProfScope ps("sweep2_rs", s);
-    k_sweep2_rs<<<dim3(d.n_tiles, d.views), kTileThreads, 0, s>>>(
-            d, b, in.prev_depth, reinterpret_cast<float4*>(out));
-    check_launch();
+    launch_sweeps(d, b, in.prev_depth, EpiRS{reinterpret_cast<float4*>(out)},
+                  s);
 }
 
 // ------------------------------------------------- dist-channel backward

@@ -164,3 +164,36 @@ def test_empty_mesh_and_index_errors(cuda, port):
         ops.rasterize_face_id(T(clip, cuda), T(bad, cuda), 16, 16)
     with pytest.raises(DressiError):
         ops.soft_clip(T(clip, cuda), T(bad, cuda), 16, 16, 2.0)
+
+
+def test_bin_overflow_fallback_is_exact(cuda, port, monkeypatch):
+    """A tile-list capacity too small for the scene makes the device fall
+    back to exhaustive (all-faces) sweeps: still bit-exact, and flagged in
+    the status word."""
+    from opendressi_b200 import ops
+    from opendressi_b200 import _native as N
+
+    monkeypatch.setenv("DRESSI_B200_BIN_CAP", "64")
+    sc = scene.silhouette_scene(level=3, n_views=1, res=128, seed=9)
+    clip = port.transform_clip(sc.pos0, sc.mvps[0])
+    soft = port.soft_clip(clip, sc.faces_f, 128, 128, sc.radius_px)
+    fid, fs = pyoracle.soft_inputs(sc.n_faces)
+    cpu = port.rasterize_soft(soft, fid, fs, clip, sc.faces_f, 128, 128,
+                              sc.radius_px)
+    import torch
+
+    st = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = torch.empty((1, 128, 128, 4), device=cuda)
+    args = [T(soft, cuda), T(fid, cuda), T(fs, cuda), T(clip, cuda),
+            T(sc.faces_f, cuda)]
+    N.call("dressi_rasterize_soft", args[0].data_ptr(), soft.shape[0],
+           args[1].data_ptr(), args[2].data_ptr(), sc.n_faces,
+           args[3].data_ptr(), clip.shape[0], args[4].data_ptr(), 1, 128, 128,
+           float(sc.radius_px), None, out.data_ptr(), st.data_ptr(),
+           torch.cuda.current_stream().cuda_stream)
+    assert int(st.item()) & N.STATUS_BIN_OVERFLOW
+    assert_bitexact(npy(out[0]), cpu, "RasterizeSoft (overflow fallback)")
+    fi = ops.rasterize_face_id(T(clip, cuda), T(sc.faces_f, cuda), 128, 128,
+                               check=False)
+    assert_bitexact(npy(fi), port.rasterize_face_id(clip, sc.faces_f, 128,
+                                                    128), "FaceId fallback")
