@@ -114,6 +114,52 @@ struct dressi_plan_s {
     cudaStream_t cap_stream = nullptr;
     cudaGraphExec_t exec = nullptr;
     uint32_t kernels_per_iter = 0;
+    // silhouette bins live in their own allocation so they can grow
+    void* bins_mem = nullptr;
+    uint32_t* ovf_host = nullptr;  // pinned: overflow bits of the last
+                                   // replayed iteration (written by the graph)
+
+    void alloc_bins() {
+        Arena dry;
+        carve_soft_bins(dry, d, &b.soft);
+        const size_t bytes = dry.used + 256;
+        DRESSI_CUDA(cudaMalloc(&bins_mem, bytes));
+        Arena a{static_cast<char*>(bins_mem), bytes, 0};
+        carve_soft_bins(a, d, &b.soft);
+        const size_t vt = size_t(d.views) * d.n_tiles;
+        DRESSI_CUDA(cudaMemset(b.soft.bin1.cursor, 0, vt * sizeof(int)));
+        DRESSI_CUDA(cudaMemset(b.soft.bin2.cursor, 0, vt * 8 * sizeof(int)));
+    }
+
+    // Reactive growth: a bin set that overflowed in the last replayed
+    // iteration (its exact fallback is slow) doubles its capacity, within
+    // half of the free device memory; the graph is then re-instantiated.
+    void grow_bins_if_needed(cudaStream_t s) {
+        if (kind != kSil || !ovf_host) return;
+        const uint32_t bits = *reinterpret_cast<volatile uint32_t*>(ovf_host);
+        if (!bits) return;
+        DRESSI_CUDA(cudaStreamSynchronize(s));
+        DRESSI_CUDA(cudaDeviceSynchronize());
+        SoftDims nd = d;
+        if (bits & 1u) nd.cap1 = std::min(nd.cap1 * 2, 1 << 16);
+        if (bits & 2u) nd.cap2 = std::min(nd.cap2 * 2, 1 << 16);
+        *ovf_host = 0;
+        if (nd.cap1 == d.cap1 && nd.cap2 == d.cap2) return;
+        Arena dry;
+        SoftBuffers tmp = b.soft;
+        carve_soft_bins(dry, nd, &tmp);
+        size_t free_b = 0, total_b = 0;
+        DRESSI_CUDA(cudaMemGetInfo(&free_b, &total_b));
+        if (dry.used > free_b / 2) return;  // keep the (exact) fallback
+        if (exec) {
+            cudaGraphExecDestroy(exec);
+            exec = nullptr;
+        }
+        DRESSI_CUDA(cudaFree(bins_mem));
+        bins_mem = nullptr;
+        d = nd;
+        alloc_bins();
+    }
 
     void set_slot(int i, void* ptr, size_t bytes) {
         slots[i].ptr = ptr;
@@ -123,6 +169,9 @@ struct dressi_plan_s {
     void record_iteration(cudaStream_t s) {
         if (kind == kSil) {
             sil_iteration(d, p, b, s);
+            if (ovf_host)
+                DRESSI_CUDA(cudaMemcpyAsync(ovf_host, b.soft.status + 1, 4,
+                                            cudaMemcpyDeviceToHost, s));
         } else {
             fit_iteration(n, lr, fb, s);
         }
@@ -167,6 +216,8 @@ struct dressi_plan_s {
         if (exec) cudaGraphExecDestroy(exec);
         if (cap_stream) cudaStreamDestroy(cap_stream);
         if (mem) cudaFree(mem);
+        if (bins_mem) cudaFree(bins_mem);
+        if (ovf_host) cudaFreeHost(ovf_host);
         if (prev >= 0) cudaSetDevice(prev);
     }
 };
@@ -370,7 +421,7 @@ int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
             b.loss_hist = a.take<float>(size_t(hist));
             b.hist_cap = hist;
             b.done = a.take<unsigned>(1);
-            carve_soft(a, d, &b.soft);
+            carve_soft_main(a, d, &b.soft);
         };
         Arena dry;
         carve(dry);
@@ -384,6 +435,10 @@ int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
                                cudaMemcpyHostToDevice));
         DRESSI_CUDA(cudaMemcpy(pl->b.mvps, desc->mvps, NV * 16 * sizeof(float),
                                cudaMemcpyHostToDevice));
+        pl->alloc_bins();
+        DRESSI_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&pl->ovf_host), 4,
+                                  cudaHostAllocDefault));
+        *pl->ovf_host = 0;
         pl->set_slot(DRESSI_SLOT_PARAM, pl->b.pos, V * 3 * 4);
         pl->set_slot(DRESSI_SLOT_ADAM_M, pl->b.adam_m, V * 3 * 4);
         pl->set_slot(DRESSI_SLOT_ADAM_V, pl->b.adam_v, V * 3 * 4);
@@ -520,6 +575,7 @@ int dressi_plan_exec(dressi_plan p, uint32_t n_iters, void* stream) {
     return guarded([&] {
         DRESSI_REQUIRE(p, "null plan");
         DeviceGuard dg(p->device);
+        p->grow_bins_if_needed(as_stream(stream));
         p->ensure_graph();
         for (uint32_t i = 0; i < n_iters; i++)
             DRESSI_CUDA(cudaGraphLaunch(p->exec, as_stream(stream)));
@@ -535,8 +591,11 @@ int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream) {
         DeviceGuard dg(p->device);
         cudaStream_t s = as_stream(stream);
         if (phase == 0) {
+            p->grow_bins_if_needed(s);
             sil_forward_backward(p->d, p->p, p->b, nullptr, s);
             sil_grad_reduce(p->p, p->b, false, s);
+            DRESSI_CUDA(cudaMemcpyAsync(p->ovf_host, p->b.soft.status + 1, 4,
+                                        cudaMemcpyDeviceToHost, s));
         } else {
             sil_update(p->p, p->b, s);
         }

@@ -52,7 +52,7 @@ struct SoftDims {
 // Device scratch of the soft rasterizer, carved from one allocation.
 struct SoftBuffers {
     FaceRec* recs = nullptr;   // [views * n_faces]
-    FixedBins bin1{};          // sweep-1 bins per 16x16 tile
+    FixedBins1 bin1{};         // sweep-1 bins per 16x16 tile
     FixedBins bin2{};          // rim-phase bins per 8x4 block
     int2* state = nullptr;     // packed survivors [views * W * H]
     int* active = nullptr;     // open-block mask per tile [views * n_tiles]
@@ -64,6 +64,10 @@ struct SoftBuffers {
 // the size). The count arrays must be zero before the first use; the scan
 // re-zeroes them after every use.
 void carve_soft(Arena& a, const SoftDims& d, SoftBuffers* b);
+// The same split in two: everything but the bins / the two bin sets (so a
+// plan can grow its bins alone).
+void carve_soft_main(Arena& a, const SoftDims& d, SoftBuffers* b);
+void carve_soft_bins(Arena& a, const SoftDims& d, SoftBuffers* b);
 // Zeroes the persistent counters of freshly carved buffers.
 void init_soft(const SoftDims& d, const SoftBuffers& b, cudaStream_t s);
 

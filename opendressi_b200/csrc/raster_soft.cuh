@@ -529,6 +529,17 @@ struct FixedBins {
     int cap;
 };
 
+// Sweep-1 bins: 64-bit entries, high word = a lower bound of the depth of
+// every fragment of the face (float bits, >= 0), low word = face << 8 |
+// 8-bit block mask. Sorting them front to back lets a pixel stop at the
+// first face whose bound exceeds its survivor's depth.
+struct FixedBins1 {
+    int* cursor;                 // [views * tiles]
+    unsigned long long* list;    // [views * tiles * cap]
+    int cap;
+};
+constexpr int kSortMax = 256;    // longest sweep-1 list sorted per tile
+
 // Thread -> pixel of a 16x16 tile: 8 warps of 8x4 pixels (2-D warp
 // footprints keep more lanes inside a small triangle's bbox).
 __device__ __forceinline__ void tile_xy(int tile, int tiles_x, int* x,
@@ -558,7 +569,8 @@ struct SweepArgs {
     const float* prev;    // this view's peeling depth [H][W] or null
     int rim_cells_x;
     const int* rim;       // this view's rim-possible flags per cell
-    uint32_t* status;     // device status word
+    uint32_t* status;     // [0] sticky status word, [1] per-iteration
+                          // overflow bits (1: sweep-1 bins, 2: rim bins)
 };
 
 __device__ __forceinline__ void fold(Survivor& s, float depth, int f,
@@ -583,20 +595,61 @@ __device__ __forceinline__ void eval_full(Survivor& s, float px, float py,
     fold(s, depth, f, td.dist >= 0.f);
 }
 
+// Lower bound of the Eq.3 depth of every fragment of a face: inside (and
+// distance-zero) fragments of a kFaceFast face lie within 1.2e-3 of the
+// triangle in barycentric units (the area criterion of build_record), so
+// their hard depth is >= zmin - 3.6e-3 (zmax - zmin) less rounding; rim
+// fragments are >= 0.5. Faces without the guarantees get 0.
+__device__ __forceinline__ float face_depth_lb(const FaceRec& r) {
+    if (!(r.flags & kFaceFast)) return 0.f;
+    const float zmin = fminf(fminf(r.hz0, r.hz1), r.hz2);
+    const float zmax = fmaxf(fmaxf(r.hz0, r.hz1), r.hz2);
+    const float zlb = zmin - 0.1f * (zmax - zmin) - 1e-6f;
+    return 0.5f * fminf(fmaxf(zlb, 0.f), 1.f) * 0.99999f;
+}
+
 // Appends face f to the sweep-1 bins of the tiles its region touches; the
-// entry carries the 8-bit block mask so untouched warps skip it.
+// entry carries the face's depth bound and the 8-bit block mask.
 __device__ __forceinline__ void bin_sweep1(const FaceRec& r, int f,
-                                           int tiles_x, FixedBins b1,
+                                           int tiles_x, FixedBins1 b1,
                                            size_t view_bin0) {
     if (r.rx0 > r.rx1 || r.ry0 > r.ry1) return;
+    const unsigned long long hi =
+            (unsigned long long)__float_as_uint(face_depth_lb(r)) << 32;
     for (int ty = r.ry0 / kTile; ty <= r.ry1 / kTile; ty++)
         for (int tx = r.rx0 / kTile; tx <= r.rx1 / kTile; tx++) {
             const size_t bin = view_bin0 + size_t(ty) * tiles_x + tx;
             const int slot = atomicAdd(&b1.cursor[bin], 1);
             if (slot < b1.cap)
                 b1.list[bin * b1.cap + slot] =
-                        (f << 8) | block_mask(tx, ty, r.rx0, r.rx1, r.ry0, r.ry1);
+                        hi | uint32_t((f << 8) |
+                                      block_mask(tx, ty, r.rx0, r.rx1, r.ry0, r.ry1));
         }
+}
+
+// Block-wide ascending bitonic sort of n <= kSortMax 64-bit keys in shared
+// memory (padded with ~0).
+__device__ __forceinline__ void block_sort_asc(unsigned long long* k, int n) {
+    int p = 2;
+    while (p < n) p <<= 1;
+    for (int i = n + threadIdx.x; i < p; i += blockDim.x) k[i] = ~0ull;
+    __syncthreads();
+    for (int size = 2; size <= p; size <<= 1) {
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < p; i += blockDim.x) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long a = k[i], b = k[ixj];
+                    const bool up = (i & size) == 0;
+                    if (up ? a > b : a < b) {
+                        k[i] = b;
+                        k[ixj] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
 }
 
 // Sweep 1 over the tile's bin: inside and boundary fragments are folded;
@@ -606,11 +659,11 @@ __device__ __forceinline__ void bin_sweep1(const FaceRec& r, int f,
 // finish here through the epilogue; the others store their survivors and
 // the open-block mask for the rim phase.
 template <class Epi>
-static __device__ void sweep1_tile(const SweepArgs& a, FixedBins b1,
+static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
                                    int tile, int2* state, int* mask_out,
                                    Epi& epi) {
     __shared__ FaceRec sh[kRecChunk];
-    __shared__ int ids[kRecChunk];
+    __shared__ unsigned long long keys[kSortMax];
     __shared__ int warp_open[8];
     __shared__ int n_entries;
     int x, y;
@@ -628,32 +681,53 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins b1,
         b1.cursor[bin] = 0;  // ready for the next use
     }
     __syncthreads();
-    const bool identity = n_entries > b1.cap;  // overflow: all faces
-    if (identity && threadIdx.x == 0) atomicOr(a.status, kStatusBinOverflow);
-    const int end = identity ? a.n_faces : n_entries;
-    const int* list = b1.list + bin * b1.cap;
+    const int nent = n_entries;
+    const bool identity = nent > b1.cap;  // overflow: all faces
+    if (identity && threadIdx.x == 0) {
+        atomicOr(&a.status[0], kStatusBinOverflow);  // sticky report
+        atomicOr(&a.status[1], 1u);  // this iteration: grow the sweep-1 bins
+    }
+    const int end = identity ? a.n_faces : nent;
+    const unsigned long long* list = b1.list + bin * b1.cap;
+    // front-to-back order when the list fits the sort buffer
+    const bool sorted = !identity && end <= kSortMax;
+    if (sorted) {
+        for (int i = threadIdx.x; i < end; i += blockDim.x) keys[i] = list[i];
+        block_sort_asc(keys, end);
+    }
 
     Survivor s{1.f, -1, false};
+    bool done = !in;  // sorted lists: every later face is behind the survivor
     for (int base = 0; base < end; base += kRecChunk) {
         const int n = imin_(kRecChunk, end - base);
         __syncthreads();
-        if (threadIdx.x < n)
-            ids[threadIdx.x] = identity ? ((base + threadIdx.x) << 8) | 0xff
-                                        : list[base + threadIdx.x];
+        if (!sorted && threadIdx.x < n) {
+            keys[threadIdx.x] =
+                    identity ? (unsigned long long)(((base + threadIdx.x) << 8) | 0xff)
+                             : list[base + threadIdx.x];
+        }
         __syncthreads();
+        const int kofs = sorted ? base : 0;
         {
             const float4* src = reinterpret_cast<const float4*>(a.recs);
             float4* dst = reinterpret_cast<float4*>(sh);
             for (int i = threadIdx.x; i < n * kRecVec4; i += blockDim.x) {
                 const int j = i / kRecVec4, q = i % kRecVec4;
-                dst[i] = src[size_t(ids[j] >> 8) * kRecVec4 + q];
+                const int f = int(uint32_t(keys[kofs + j])) >> 8;
+                dst[i] = src[size_t(f) * kRecVec4 + q];
             }
         }
         __syncthreads();
+        if (__all_sync(0xffffffffu, done)) continue;
         for (int i = 0; i < n; i++) {
-            const int ent = ids[i];
+            const unsigned long long key = keys[kofs + i];
+            const int ent = int(uint32_t(key));
             if (!((ent >> w) & 1)) continue;  // region misses this warp
-            if (!in) continue;
+            if (done) continue;
+            if (sorted && s.depth < __uint_as_float(uint32_t(key >> 32))) {
+                done = true;  // this face and all later ones lose
+                continue;
+            }
             const FaceRec& r = sh[i];
             if (x < r.rx0 || x > r.rx1 || y < r.ry0 || y > r.ry1) continue;
             if (!(r.flags & kFaceValid)) continue;
@@ -735,17 +809,17 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
     const int blocks_x = tiles_x * 2;
     const int* mk = mask + size_t(v) * n_tiles;
     const size_t bin0 = size_t(v) * n_tiles * 8;
-    const int bx0 = r.bx0 >> 3, by0 = r.by0 >> 2;
-    const int nbx = (r.bx1 >> 3) - bx0 + 1;
-    const int nb = nbx * ((r.by1 >> 2) - by0 + 1);
-    for (int i = lane; i < nb; i += 32) {
-        const int bx = bx0 + i % nbx, by = by0 + i / nbx;
-        const int m = mk[(by >> 2) * tiles_x + (bx >> 1)];
-        if (!((m >> ((by & 3) * 2 + (bx & 1))) & 1)) continue;
-        if (!tri_touches_block(r, bx, by)) continue;
-        const size_t bin = bin0 + size_t(by) * blocks_x + bx;
-        const int slot = atomicAdd(&b2.cursor[bin], 1);
-        if (slot < b2.cap) b2.list[bin * b2.cap + slot] = f;
+    // lanes tile the block range 8 wide x 4 tall (no integer division)
+    const int lx = lane & 7, ly = lane >> 3;
+    for (int by = (r.by0 >> 2) + ly; by <= (r.by1 >> 2); by += 4) {
+        for (int bx = (r.bx0 >> 3) + lx; bx <= (r.bx1 >> 3); bx += 8) {
+            const int m = mk[(by >> 2) * tiles_x + (bx >> 1)];
+            if (!((m >> ((by & 3) * 2 + (bx & 1))) & 1)) continue;
+            if (!tri_touches_block(r, bx, by)) continue;
+            const size_t bin = bin0 + size_t(by) * blocks_x + bx;
+            const int slot = atomicAdd(&b2.cursor[bin], 1);
+            if (slot < b2.cap) b2.list[bin * b2.cap + slot] = f;
+        }
     }
 }
 
@@ -788,7 +862,10 @@ static __device__ void rim_tile(const SweepArgs& a, FixedBins b2, int tile,
         }
         n = __shfl_sync(0xffffffffu, n, 0);
         const bool identity = n > b2.cap;  // overflow: all faces
-        if (identity && lane == 0) atomicOr(a.status, kStatusBinOverflow);
+        if (identity && lane == 0) {
+            atomicOr(&a.status[0], kStatusBinOverflow);  // sticky report
+            atomicOr(&a.status[1], 2u);  // this iteration: grow the rim bins
+        }
         const int end = identity ? a.n_faces : n;
         const int* lst = b2.list + bin * b2.cap;
         const float4* src = reinterpret_cast<const float4*>(a.recs);
@@ -831,7 +908,7 @@ static __device__ void rim_tile(const SweepArgs& a, FixedBins b2, int tile,
 
 template <class Epi>
 __global__ void __launch_bounds__(kTileThreads)
-        k_sweep1(SweepArgs a0, FixedBins b1, int2* state, int* mask,
+        k_sweep1(SweepArgs a0, FixedBins1 b1, int2* state, int* mask,
                  size_t view_stride_recs, size_t view_stride_px,
                  size_t view_stride_rim, Epi epi) {
     SweepArgs a = a0;

@@ -52,9 +52,11 @@ __device__ __forceinline__ float sil_pixel(float dist, float cov, float target,
 // the in-graph Adam: t_new = t + 1, bc = 1 - pow(beta, t_new)).
 __global__ void k_transform(const float* pos, const float* mvps, int n_verts,
                             float4* clip, float* scalars, float b1, float b2,
-                            int advance, int* rim, int rim_cells) {
+                            int advance, int* rim, int rim_cells,
+                            uint32_t* status) {
     const int v = blockIdx.y;
     const int u = blockIdx.x * blockDim.x + threadIdx.x;
+    if (v == 0 && blockIdx.x == 0 && threadIdx.x == 0) status[1] = 0u;
     if (blockIdx.x == 0) {
         // this iteration's face setup re-marks the rim cells
         for (int i = threadIdx.x; i < rim_cells; i += blockDim.x)
@@ -283,7 +285,7 @@ void sil_forward_backward(const SoftDims& d, const SilParams& p,
         k_transform<<<vg, 256, 0, s>>>(b.pos, b.mvps, p.n_verts,
                                        reinterpret_cast<float4*>(b.clip),
                                        b.scalars, p.b1, p.b2, 1, b.soft.rim,
-                                       d.rim_cells);
+                                       d.rim_cells, b.soft.status);
     }
     const dim3 fg((d.n_faces + 127) / 128, d.views);
     {

@@ -27,20 +27,29 @@ void default_caps(SoftDims* d) {
     }
 }
 
-void carve_soft(Arena& a, const SoftDims& d, SoftBuffers* b) {
+void carve_soft_main(Arena& a, const SoftDims& d, SoftBuffers* b) {
     const size_t vt = size_t(d.views) * d.n_tiles;
-    const size_t vb = vt * 8;  // 8x4-pixel blocks of the rim phase
     b->recs = a.take<FaceRec>(size_t(d.views) * std::max(d.n_faces, 1));
-    b->bin1.cap = d.cap1;
-    b->bin1.cursor = a.take<int>(vt);
-    b->bin1.list = a.take<int>(vt * d.cap1);
-    b->bin2.cap = d.cap2;
-    b->bin2.cursor = a.take<int>(vb);
-    b->bin2.list = a.take<int>(vb * d.cap2);
     b->state = a.take<int2>(size_t(d.views) * d.W * d.H);
     b->active = a.take<int>(vt);
     b->rim = a.take<int>(size_t(d.views) * std::max(d.rim_cells, 1));
     b->status = a.take<uint32_t>(4);
+}
+
+void carve_soft_bins(Arena& a, const SoftDims& d, SoftBuffers* b) {
+    const size_t vt = size_t(d.views) * d.n_tiles;
+    const size_t vb = vt * 8;  // 8x4-pixel blocks of the rim phase
+    b->bin1.cap = d.cap1;
+    b->bin1.cursor = a.take<int>(vt);
+    b->bin1.list = a.take<unsigned long long>(vt * d.cap1);
+    b->bin2.cap = d.cap2;
+    b->bin2.cursor = a.take<int>(vb);
+    b->bin2.list = a.take<int>(vb * d.cap2);
+}
+
+void carve_soft(Arena& a, const SoftDims& d, SoftBuffers* b) {
+    carve_soft_main(a, d, b);
+    carve_soft_bins(a, d, b);
 }
 
 void init_soft(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {

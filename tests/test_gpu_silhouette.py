@@ -177,3 +177,26 @@ def test_image_fit_golden_and_full(cuda, port):
     tr = plan.loss_history(500)
     assert tr[-1] == pytest.approx(trace_cpu[-1], rel=1e-3)
     np.testing.assert_allclose(tr, trace_cpu, rtol=1e-3)
+
+
+def test_bins_grow_after_overflow(cuda, port, monkeypatch):
+    """Tiny initial bin capacities: the first iterations overflow and use
+    the exact fallback, the plan then grows its bins and re-instantiates its
+    graph; the loss trace matches the C restatement throughout."""
+    from opendressi_b200.plans import SilhouettePlan
+    from opendressi_b200 import _native as N
+
+    monkeypatch.setenv("DRESSI_B200_BIN_CAP", "8")
+    sc = scene.silhouette_scene(level=3, n_views=2, res=128, seed=6)
+    targets = _targets(port, sc)
+    plan = SilhouettePlan.from_scene(sc, lr=1e-2)
+    monkeypatch.delenv("DRESSI_B200_BIN_CAP")
+    plan.upload(N.SLOT_PARAM, sc.pos0)
+    plan.upload(N.SLOT_TARGET, targets)
+    for _ in range(8):
+        plan.step(1)
+    trace_cpu, pos_cpu = port.silhouette_run(sc.pos0, sc.faces_f, sc.mvps,
+                                             targets, 128, sc.radius_px,
+                                             sc.sigma, 1e-2, 8)
+    np.testing.assert_allclose(plan.loss_history(8), trace_cpu, rtol=1e-3)
+    assert plan.status() & N.STATUS_BIN_OVERFLOW
