@@ -58,7 +58,7 @@ enum FaceFlags : uint32_t {
     kFaceSoftInside = 16u,  // an inside fragment is always soft-covered
 };
 
-constexpr float kMaxFastRadius = 1e4f;  // rim depth stays > 0.5 below it
+constexpr float kMaxFastRadius = 1e3f;  // rim depth stays > 0.5 below it
 
 // Per-(view, face) constants hoisted out of the per-pixel loop. Every value
 // is computed with the reference's own expression, so hoisting is exact.
@@ -70,7 +70,7 @@ struct __align__(16) FaceRec {
     float h2x, h2y, h_inv_area, hz0;
     float hz1, hz2, ex0, ey0;     // hard edges e_k = h[k+1] - h[k]
     float ex1, ey1, ex2, ey2;
-    float len2_0, len2_1, len2_2, pad1;
+    float len2_0, len2_1, len2_2, near2;  // near2: tau^2 of classify()
     float lbx0, lbx1, lby0, lby1;  // hard bbox grown by rounding slack
     int bx0, bx1, by0, by1;  // soft bbox pixel range (inclusive)
     int rx0, rx1, ry0, ry1;  // sweep-1 region pixel range (inclusive)
@@ -149,16 +149,19 @@ __device__ __forceinline__ TriDist signed_dist(float px, float py,
 // Fragment classes of the two-pass sweep.
 enum FragClass : int {
     kInside = 0,    // SignedDistToTri's sign test says inside: dist >= 0
-    kFar = 1,       // provably dist <= -0.008 px: a rim fragment, depth > 0.5
+    kFar = 1,       // provably dist < 0 with depth > 0.5: a rim fragment
     kBoundary = 2,  // anything else: evaluate in full
 };
 
 // The inside test is SignedDistToTri's own sign test (same expressions).
-// "Far" needs kFaceFast (well-conditioned, |coords| < 4096, see
-// build_record): some edge function has the outside sign with
-// cr^2 > 1e-4 |e|^2, i.e. the pixel centre is > 0.01 px beyond that edge's
-// line while the rounding error of cr is < 0.001 |e| -- so every edge's
-// closest point is > 0.008 px away and the reference's distance is negative.
+// Otherwise the reference's distance is -sqrt(best_d2), which is -0 -- a
+// hard-type fragment -- only when some closest point q_k = a_k + t e_k
+// rounds exactly onto the pixel centre. That puts the centre within
+// |q rounding| + |cr rounding| / |e_k| of edge k's line, a bound tau the
+// record stores as near2 = tau^2 (kFaceFast faces only, see build_record).
+// A centre farther than tau from all three lines therefore has d2 > 0 and
+// |dist| > 1.2e-4 px, so with radius < kMaxFastRadius its Eq.3 depth
+// 0.5 + 0.5 |dist| / radius rounds strictly above 0.5.
 __device__ __forceinline__ int classify(float px, float py, const FaceRec& r) {
     const float cr0 = r.ex0 * (py - r.h0y) - r.ey0 * (px - r.h0x);
     const float cr1 = r.ex1 * (py - r.h1y) - r.ey1 * (px - r.h1x);
@@ -167,11 +170,10 @@ __device__ __forceinline__ int classify(float px, float py, const FaceRec& r) {
     const int n_neg = (cr0 <= 0.f) + (cr1 <= 0.f) + (cr2 <= 0.f);
     if (n_pos == 3 || n_neg == 3) return kInside;
     if (!(r.flags & 8u /* kFaceFast */)) return kBoundary;
-    const float o = r.orient;
-    const bool far = (o * cr0 < 0.f && cr0 * cr0 > 1e-4f * r.len2_0) ||
-                     (o * cr1 < 0.f && cr1 * cr1 > 1e-4f * r.len2_1) ||
-                     (o * cr2 < 0.f && cr2 * cr2 > 1e-4f * r.len2_2);
-    return far ? kFar : kBoundary;
+    const bool near = cr0 * cr0 <= r.near2 * r.len2_0 ||
+                      cr1 * cr1 <= r.near2 * r.len2_1 ||
+                      cr2 * cr2 <= r.near2 * r.len2_2;
+    return near ? kBoundary : kFar;
 }
 
 // Lower bound of a rim fragment's depth from the distance to the face's
@@ -275,7 +277,7 @@ __device__ __forceinline__ bool build_record(
     r.ex0 = exs[0]; r.ey0 = eys[0]; r.ex1 = exs[1]; r.ey1 = eys[1];
     r.ex2 = exs[2]; r.ey2 = eys[2];
     r.len2_0 = l2s[0]; r.len2_1 = l2s[1]; r.len2_2 = l2s[2];
-    r.pad1 = 0.f;
+    r.near2 = 0.f;
     r.i0 = hidx[0]; r.i1 = hidx[1]; r.i2 = hidx[2];
     {
         // bbox of the segments a_k + t e_k the distance is measured to,
@@ -350,6 +352,12 @@ __device__ __forceinline__ bool build_record(
             fabsf(h_area) >= fmaxf(1.f, 1e-4f * emax * L * 1.001f)) {
             flags |= kFaceFast;
             r.orient = h_area > 0.f ? 1.f : -1.f;
+            // tau (classify): rounding of q = a + t e (<= 4u|coords|) plus
+            // that of the edge function over the reach L (4u L), doubled,
+            // plus 2.5e-4 px, which keeps |dist| >= 2^-23 * kMaxFastRadius
+            // so the Eq.3 depth of a deferred fragment rounds above 0.5
+            const float tau = 2.f * (4.f * kU * L + 4.f * kU * cmax) + 2.5e-4f;
+            r.near2 = tau * tau;
             // Soft coverage of inside fragments: if every hard vertex has
             // soft barycentrics >= 0.01 (convexity extends that to the whole
             // hard triangle, and an inside-classified pixel is within 1e-3
@@ -691,7 +699,26 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
     const unsigned long long* list = b1.list + bin * b1.cap;
     // front-to-back order when the list fits the sort buffer
     const bool sorted = !identity && end <= kSortMax;
-    if (sorted) {
+    if (sorted && end <= 32) {
+        // one warp, register bitonic network (no block barriers)
+        if (w == 0) {
+            const int lane = threadIdx.x & 31;
+            unsigned long long k = lane < end ? list[lane] : ~0ull;
+#pragma unroll
+            for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+                for (int j = size >> 1; j > 0; j >>= 1) {
+                    const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, j);
+                    const bool up = (lane & size) == 0;
+                    const bool lower = (lane & j) == 0;
+                    const unsigned long long lo = k < o ? k : o;
+                    const unsigned long long hi = k < o ? o : k;
+                    k = (lower == up) ? lo : hi;
+                }
+            }
+            keys[lane] = k;
+        }
+    } else if (sorted) {
         for (int i = threadIdx.x; i < end; i += blockDim.x) keys[i] = list[i];
         block_sort_asc(keys, end);
     }
