@@ -134,24 +134,16 @@ class ClockSampler:
 
 # ---------------------------------------------------- byte model (roofline)
 
-def algorithmic_bytes(name: str, views: int, res: int, n_verts: int,
-                      n_faces: int) -> float:
-    """Logically necessary HBM bytes of ONE launch of a kernel of the fused
-    iteration (each tensor counted once per producer/consumer boundary that
-    must exist; fused-away intermediates are not counted)."""
-    px = views * res * res
-    rec = 176  # face record bytes
-    return {
-        # survivor state write (depth, face, dist, hard_z) + face records
-        "sweep1": px * 16 + views * n_faces * rec,
-        # survivor state + target reads; loss/gradient epilogue
-        "sweep2_sil": px * (16 + 4) + views * n_faces * rec,
-        # vertex clip reads (3 per face) + face indices + record write
-        "face_setup": views * n_faces * (3 * 16 + 12 + rec),
-        "transform": n_verts * 12 + views * n_verts * 16,
-        # g_clip read + clear, pos/m/v read + write, g_pos write
-        "gpos_adam": n_verts * (views * 32 + 36 + 36 + 12),
-    }.get(name, 0.0)
+def iteration_bytes(views: int, res: int, n_verts: int, n_faces: int) -> float:
+    """Algorithmic HBM bytes of one fwd+bwd+Adam silhouette iteration (the
+    per-iteration figure of the survey's byte model): 16 B per view-pixel
+    (target read 4, triangle-ID write 4, depth write 4, triangle-ID read in
+    the backward 4), per view the clip positions written and read (32 B per
+    vertex) and the face indices (12 B per face), and the replicated Adam
+    (read p, g, m, v = 48 B, write p, m, v = 36 B per vertex) plus the
+    gradient buffer (12 B written + read per vertex)."""
+    return (16.0 * views * res * res + views * (32.0 * n_verts + 12.0 * n_faces)
+            + (48.0 + 36.0 + 24.0) * n_verts)
 
 
 # ------------------------------------------------------------- GPU arm
@@ -262,31 +254,32 @@ def run_ours(args):
                "unit": "iterations/s", "h2d_bytes_per_step": nb,
                "d2h_bytes_per_step": nb + 4}
 
-    # ---- per-kernel timing (CUDA events, un-graphed) for the roofline ---
+    # ---- roofline of the fused iteration (one CUDA-graph launch) ---------
+    # The iteration is the unit the byte model is defined on; its duration
+    # is the CUDA-event time per step of the timed region above. Per-kernel
+    # times come from an un-graphed run with CUDA events around each launch.
     prof = plan.profile(n_iters=10)
-    per_iter = {p["name"]: p for p in prof}
+    per_iter = {p["name"]: round(p["total_ms"] / 10.0, 4) for p in prof}
     launches_per_iter = sum(p["launches"] for p in prof) / 10.0
     dom = max(prof, key=lambda p: p["total_ms"])
     nvw = len(shard)
-    alg = algorithmic_bytes(dom["name"], nvw, args.res, sc.n_verts,
-                            sc.n_faces)
+    alg = iteration_bytes(nvw, args.res, sc.n_verts, sc.n_faces)
     peak, peak_kind = peaks()
-    achieved = alg / (dom["avg_ms"] * 1e-3) / 1e9 if alg else None
+    ms_step = ms_max / args.steps
+    achieved = alg / (ms_step * 1e-3) / 1e9
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
-            tr = json.load(f).get(f"{dom['name']}@{nvw}x{args.res}")
-        if tr:
-            traffic = tr
+            traffic = json.load(f).get(f"iteration@{nvw}x{args.res}")
     roofline = {
-        "bound": "hbm", "kernel": dom["name"],
+        "bound": "hbm", "kernel": "fused iteration (one CUDA graph)",
         "achieved": achieved, "peak": peak, "unit": "GB/s",
-        "frac": (achieved / peak) if achieved else None,
-        "peak_source": peak_kind, "traffic": traffic,
-        "alg_bytes_per_launch": alg, "avg_ms": dom["avg_ms"],
-        "kernels_ms_per_iter": {k: round(v["total_ms"] / 10.0, 4)
-                                for k, v in per_iter.items()},
+        "frac": achieved / peak, "peak_source": peak_kind,
+        "traffic": traffic, "alg_bytes_per_launch": alg,
+        "avg_ms": ms_step,
+        "dominant_kernel": dom["name"],
+        "kernels_ms_per_iter": per_iter,
     }
 
     status = plan.status()
