@@ -106,6 +106,25 @@ int dressi_rasterize_face_id(const float* clip, uint32_t n_verts,
                              float* out, float* depth_out, uint32_t* status,
                              void* stream);
 
+/* dressi_rasterize_face_id on a fixed scratch area; no counterpart in the
+ * reference. Same arguments and output as dressi_rasterize_face_id, but it
+ * allocates no device memory: its scratch is a 16 MiB file-scope device
+ * array that every device loading the library holds until process exit.
+ * For callers that cannot allocate during a call (a host framework's
+ * allocator owns the free memory; latency-critical loops). A call whose
+ * scratch need exceeds 16 MiB fails with DRESSI_ERR_INVALID; the need is
+ * about views * (96 F + 12 T + 4 max(16 F, 4 T) + 16 K) bytes for F faces
+ * and T 16x16-pixel tiles (one 1024x1024 view of 20480 faces: 3.4 MB).
+ * The first call on a device looks up the scratch address (and may load the
+ * module): make it outside any stream capture. Calls that overlap in time
+ * on one device share the scratch and race. */
+int dressi_rasterize_face_id_noalloc(const float* clip, uint32_t n_verts,
+                                     const float* faces, uint32_t n_faces,
+                                     uint32_t views, uint32_t width,
+                                     uint32_t height, float* out,
+                                     float* depth_out, uint32_t* status,
+                                     void* stream);
+
 /* F::Rasterize (cpu_raster.cpp:195-225), bit-exact: perspective-correct
  * interpolation of attr [views][n_verts][n_comp] (n_comp 1..4);
  * out [views][H][W][n_comp]; background 0. */

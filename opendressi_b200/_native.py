@@ -57,6 +57,9 @@ SIGNATURES = {
                                              _vp]),
     "dressi_rasterize_face_id": (C.c_int, [_vp, _u32, _vp, _u32, _u32, _u32,
                                            _u32, _vp, _vp, _vp, _vp]),
+    "dressi_rasterize_face_id_noalloc": (C.c_int, [_vp, _u32, _vp, _u32, _u32,
+                                                   _u32, _u32, _vp, _vp, _vp,
+                                                   _vp]),
     "dressi_rasterize": (C.c_int, [_vp, _u32, _vp, _u32, _vp, _u32, _u32,
                                    _u32, _u32, _vp, _vp, _vp]),
     "dressi_silhouette_plan_create": (C.c_int, [C.POINTER(SilhouetteDesc),
