@@ -50,7 +50,8 @@ extern "C" {
 /* device status word bits */
 #define DRESSI_STATUS_INDEX_RANGE 0x1u  /* face/vertex index out of range   */
 #define DRESSI_STATUS_BIN_OVERFLOW 0x2u /* tile list capacity exceeded; the */
-                                        /* exact fallback sweep was used     */
+                                        /* excess went to the spill lists   */
+                                        /* (results stay exact)             */
 
 /* ABI version of the loaded library (DRESSI_B200_ABI_VERSION). */
 int dressi_abi_version(void);

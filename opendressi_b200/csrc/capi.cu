@@ -129,6 +129,9 @@ struct dressi_plan_s {
         const size_t vt = size_t(d.views) * d.n_tiles;
         DRESSI_CUDA(cudaMemset(b.soft.bin1.cursor, 0, vt * sizeof(int)));
         DRESSI_CUDA(cudaMemset(b.soft.bin2.cursor, 0, vt * 8 * sizeof(int)));
+        DRESSI_CUDA(cudaMemset(b.soft.bin1.spill_n, 0, sizeof(int)));
+        DRESSI_CUDA(cudaMemset(b.soft.bin1.parked_n, 0, sizeof(int)));
+        DRESSI_CUDA(cudaMemset(b.soft.bin2.spill_n, 0, sizeof(int)));
     }
 
     // Reactive growth: a bin set that overflowed in the last replayed

@@ -20,6 +20,7 @@ struct SoftDims {
     int tiles_x = 0, tiles_y = 0, n_tiles = 0;
     int rim_cells_x = 0, rim_cells = 0;
     int cap1 = 0, cap2 = 0;  // entries per sweep-1 tile / rim block bin
+    int spill1 = 0, spill2 = 0;  // spill-list entries (all bins of a set)
 
     void finalize() {
         tiles_x = (W + kTile - 1) / kTile;
@@ -90,6 +91,13 @@ void launch_sweeps(const SoftDims& d, const SoftBuffers& b,
         ProfScope ps("sweep1", s);
         k_sweep1<Epi><<<grid, kTileThreads, 0, s>>>(a, b.bin1, b.state,
                                                     b.active, sr, sp, sm, epi);
+    }
+    DRESSI_CUDA(cudaGetLastError());
+    {
+        // tiles whose bins overflowed into the spill list (usually none)
+        ProfScope ps("sweep1_spill", s);
+        k_sweep1_spill<Epi><<<kSpillBlocks, kTileThreads, 0, s>>>(
+                a, b.bin1, b.state, b.active, sr, sp, sm, epi);
     }
     DRESSI_CUDA(cudaGetLastError());
     soft_rim_bins(d, b, s);

@@ -528,13 +528,19 @@ constexpr int kRimCell = 64;     // pixels per side of a rim-flag cell
 constexpr int kRimChunk = 16;    // records staged per warp in the rim phase
 
 // Fixed-capacity bins filled in one pass: entry i of bin k lives at
-// list[k * cap + i]; the bin's cursor counts every append (also those past
-// the capacity, which are dropped -- the consumer then falls back to
-// scanning all faces, still exact). The consumer resets the cursor.
+// list[k * cap + i]; the bin's cursor counts every append. Appends past the
+// capacity go to one shared spill list, tagged with their bin; the consumer
+// of an overflowed bin reads its own entries and then scans the spill list
+// for its tag. Only when the spill list itself overflows does the consumer
+// fall back to scanning all faces (still exact). The consumer resets the
+// cursor; the spill counter is reset by the kernel after the consumer.
 struct FixedBins {
     int* cursor;  // [views * bins]
     int* list;    // [views * bins * cap]
     int cap;
+    int* spill_n;     // [1] appends past the capacity (all bins)
+    int2* spill;      // [spill_cap] (global bin, face)
+    int spill_cap;
 };
 
 // Sweep-1 bins: 64-bit entries, high word = a lower bound of the depth of
@@ -545,8 +551,16 @@ struct FixedBins1 {
     int* cursor;                 // [views * tiles]
     unsigned long long* list;    // [views * tiles * cap]
     int cap;
+    int* spill_n;                     // [1]
+    unsigned long long* spill_key;    // [spill_cap]
+    int* spill_bin;                   // [spill_cap] global bin of each key
+    int spill_cap;
+    int* parked_n;                    // [1] overflowed tiles left to finish
+    int* parked;                      // [views * tiles] their global bins
 };
 constexpr int kSortMax = 256;    // longest sweep-1 list sorted per tile
+constexpr int kSpillBlocks = 296;  // grid of k_sweep1_spill (2 per SM)
+static_assert(kSortMax >= kTileThreads, "spill gathers need blockDim keys");
 
 // Thread -> pixel of a 16x16 tile: 8 warps of 8x4 pixels (2-D warp
 // footprints keep more lanes inside a small triangle's bbox).
@@ -627,11 +641,19 @@ __device__ __forceinline__ void bin_sweep1(const FaceRec& r, int f,
     for (int ty = r.ry0 / kTile; ty <= r.ry1 / kTile; ty++)
         for (int tx = r.rx0 / kTile; tx <= r.rx1 / kTile; tx++) {
             const size_t bin = view_bin0 + size_t(ty) * tiles_x + tx;
+            const unsigned long long key =
+                    hi | uint32_t((f << 8) |
+                                  block_mask(tx, ty, r.rx0, r.rx1, r.ry0, r.ry1));
             const int slot = atomicAdd(&b1.cursor[bin], 1);
-            if (slot < b1.cap)
-                b1.list[bin * b1.cap + slot] =
-                        hi | uint32_t((f << 8) |
-                                      block_mask(tx, ty, r.rx0, r.rx1, r.ry0, r.ry1));
+            if (slot < b1.cap) {
+                b1.list[bin * b1.cap + slot] = key;
+            } else {
+                const int sp = atomicAdd(b1.spill_n, 1);
+                if (sp < b1.spill_cap) {
+                    b1.spill_key[sp] = key;
+                    b1.spill_bin[sp] = int(bin);
+                }
+            }
         }
 }
 
@@ -660,12 +682,105 @@ __device__ __forceinline__ void block_sort_asc(unsigned long long* k, int n) {
     }
 }
 
+// Folds the spilled entries of an overflowed sweep-1 bin (gathered from the
+// spill list blockDim at a time) into the pixel's survivor -- or, when the
+// spill list itself overflowed (all_faces), every face. Faces already folded
+// by sweep 1 fold again to the same survivor. Called by every thread of the
+// block (it has barriers); used only by k_sweep1_spill.
+__device__ __forceinline__ void sweep1_spilled(
+        const SweepArgs& a, const FixedBins1& b1, int bin, int ns,
+        bool all_faces, int x, int y, bool in, bool peel, float prev,
+        bool fast_ok, FaceRec* sh, unsigned long long* keys, int* n_match,
+        Survivor& s) {
+    const int w = threadIdx.x >> 5;
+    const float px = float(x) + 0.5f, py = float(y) + 0.5f;
+    const int total = all_faces ? a.n_faces : ns;
+    for (int sb = 0; sb < total; sb += blockDim.x) {
+        __syncthreads();
+        if (threadIdx.x == 0) *n_match = 0;
+        __syncthreads();
+        const int i = sb + threadIdx.x;
+        if (all_faces) {
+            if (i < total) keys[threadIdx.x] = (unsigned long long)((i << 8) | 0xff);
+            if (threadIdx.x == 0) *n_match = imin_(int(blockDim.x), total - sb);
+        } else if (i < ns && b1.spill_bin[i] == bin) {
+            keys[atomicAdd(n_match, 1)] = b1.spill_key[i];
+        }
+        __syncthreads();
+        const int m = *n_match;
+        for (int c = 0; c < m; c += kRecChunk) {
+            const int n = imin_(kRecChunk, m - c);
+            __syncthreads();
+            const float4* src = reinterpret_cast<const float4*>(a.recs);
+            float4* dst = reinterpret_cast<float4*>(sh);
+            for (int t = threadIdx.x; t < n * kRecVec4; t += blockDim.x) {
+                const int j = t / kRecVec4, q = t % kRecVec4;
+                const int f = int(uint32_t(keys[c + j])) >> 8;
+                dst[t] = src[size_t(f) * kRecVec4 + q];
+            }
+            __syncthreads();
+            if (!in) continue;
+            for (int j = 0; j < n; j++) {
+                const int ent = int(uint32_t(keys[c + j]));
+                if (!((ent >> w) & 1)) continue;
+                const FaceRec& r = sh[j];
+                if (x < r.rx0 || x > r.rx1 || y < r.ry0 || y > r.ry1) continue;
+                if (!(r.flags & kFaceValid)) continue;
+                const int f = ent >> 8;
+                int cl = classify(px, py, r);
+                if (cl == kFar && !fast_ok) cl = kBoundary;
+                if (cl == kInside) {
+                    if (!(r.flags & kFaceSoftInside) && !soft_covers(px, py, r))
+                        continue;
+                    const float depth =
+                            0.5f * std_min(std_max(hard_depth(px, py, r), 0.f), 1.f);
+                    if (peel && depth <= prev + 1e-4f) continue;
+                    fold(s, depth, f, true);
+                } else if (cl == kBoundary) {
+                    if (!soft_covers(px, py, r)) continue;
+                    eval_full(s, px, py, r, f, a.radius, peel, prev);
+                }
+            }
+        }
+    }
+}
+
+// End of a sweep-1 tile: each warp (an 8x4-pixel block) reports whether it
+// still holds an open pixel (depth > 0.5) inside some face's soft reach.
+// Tiles without such blocks finish through the epilogue; the others store
+// their survivors and the open-block mask for the rim phase.
+template <class Epi>
+__device__ __forceinline__ void sweep1_finish(const SweepArgs& a, size_t bin,
+                                              int x, int y, bool in,
+                                              const Survivor& s, int2* state,
+                                              int* mask_out, int* warp_open,
+                                              Epi& epi) {
+    const int w = threadIdx.x >> 5;
+    const int cell = (y / kRimCell) * a.rim_cells_x + (x / kRimCell);
+    const unsigned ob = __ballot_sync(0xffffffffu, in && s.depth > 0.5f &&
+                                                           a.rim[cell] != 0);
+    if ((threadIdx.x & 31) == 0) warp_open[w] = ob != 0u;
+    __syncthreads();
+    int m = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) m |= warp_open[k] << k;
+    if (m == 0) {
+        if (threadIdx.x == 0) mask_out[bin] = 0;
+        epi(a, x, y, in, s);
+    } else {
+        if (threadIdx.x == 0) mask_out[bin] = m;
+        if (in) state[size_t(a.v) * a.W * a.H + size_t(y) * a.W + x] = pack(s);
+    }
+}
+
 // Sweep 1 over the tile's bin: inside and boundary fragments are folded;
 // far (rim) fragments are left to the rim phase. At the end each warp (an
 // 8x4-pixel block) reports whether it still holds an open pixel
 // (depth > 0.5) inside some face's soft reach. Tiles without such blocks
 // finish here through the epilogue; the others store their survivors and
-// the open-block mask for the rim phase.
+// the open-block mask for the rim phase. A tile whose bin overflowed folds
+// the entries it holds and is parked for k_sweep1_spill (this kernel keeps
+// no spill code: compiled in, it slowed the common path).
 template <class Epi>
 static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
                                    int tile, int2* state, int* mask_out,
@@ -690,15 +805,18 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
     }
     __syncthreads();
     const int nent = n_entries;
-    const bool identity = nent > b1.cap;  // overflow: all faces
-    if (identity && threadIdx.x == 0) {
+    // overflow: the own list's entries are folded here, the tile is then
+    // parked for k_sweep1_spill (spilled entries, or all faces)
+    const bool over = nent > b1.cap;
+    if (over && threadIdx.x == 0) {
         atomicOr(&a.status[0], kStatusBinOverflow);  // sticky report
         atomicOr(&a.status[1], 1u);  // this iteration: grow the sweep-1 bins
+        b1.parked[atomicAdd(b1.parked_n, 1)] = int(bin);
     }
-    const int end = identity ? a.n_faces : nent;
+    const int end = over ? b1.cap : nent;
     const unsigned long long* list = b1.list + bin * b1.cap;
     // front-to-back order when the list fits the sort buffer
-    const bool sorted = !identity && end <= kSortMax;
+    const bool sorted = !over && end <= kSortMax;
     if (sorted && end <= 32) {
         // one warp, register bitonic network (no block barriers)
         if (w == 0) {
@@ -729,9 +847,7 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
         const int n = imin_(kRecChunk, end - base);
         __syncthreads();
         if (!sorted && threadIdx.x < n) {
-            keys[threadIdx.x] =
-                    identity ? (unsigned long long)(((base + threadIdx.x) << 8) | 0xff)
-                             : list[base + threadIdx.x];
+            keys[threadIdx.x] = list[base + threadIdx.x];
         }
         __syncthreads();
         const int kofs = sorted ? base : 0;
@@ -775,8 +891,10 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
         }
     }
     const int cell = (y / kRimCell) * a.rim_cells_x + (x / kRimCell);
-    const unsigned ob = __ballot_sync(0xffffffffu, in && s.depth > 0.5f &&
-                                                           a.rim[cell] != 0);
+    // a parked tile reports every block open, so its survivors are stored
+    const unsigned ob = __ballot_sync(0xffffffffu, (in && s.depth > 0.5f &&
+                                                            a.rim[cell] != 0) ||
+                                                           over);
     if ((threadIdx.x & 31) == 0) warp_open[w] = ob != 0u;
     __syncthreads();
     int m = 0;
@@ -825,7 +943,12 @@ __device__ __forceinline__ bool tri_touches_block(const FaceRec& r, int bx,
 // blocks of its soft bbox.
 static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
                           const FaceRec* recs_all, const int* mask,
-                          FixedBins b2) {
+                          FixedBins b2, FixedBins1 b1) {
+    // sweep 1 has consumed the sweep-1 spill list and the parked tiles
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+        *b1.spill_n = 0;
+        *b1.parked_n = 0;
+    }
     const int f = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     const int v = blockIdx.y;
@@ -845,7 +968,12 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
             if (!tri_touches_block(r, bx, by)) continue;
             const size_t bin = bin0 + size_t(by) * blocks_x + bx;
             const int slot = atomicAdd(&b2.cursor[bin], 1);
-            if (slot < b2.cap) b2.list[bin * b2.cap + slot] = f;
+            if (slot < b2.cap) {
+                b2.list[bin * b2.cap + slot] = f;
+            } else {
+                const int sp = atomicAdd(b2.spill_n, 1);
+                if (sp < b2.spill_cap) b2.spill[sp] = make_int2(int(bin), f);
+            }
         }
     }
 }
@@ -882,26 +1010,25 @@ static __device__ void rim_tile(const SweepArgs& a, FixedBins b2, int tile,
         const int by = (tile / a.tiles_x) * 4 + (w >> 1);
         const size_t bin = size_t(a.v) * a.n_tiles * 8 +
                            size_t(by) * (a.tiles_x * 2) + bx;
-        int n = 0;
+        int n = 0, ns = 0;
         if (lane == 0) {
             n = b2.cursor[bin];
             b2.cursor[bin] = 0;  // ready for the next use
+            if (n > b2.cap) ns = *b2.spill_n;
         }
         n = __shfl_sync(0xffffffffu, n, 0);
-        const bool identity = n > b2.cap;  // overflow: all faces
-        if (identity && lane == 0) {
+        ns = __shfl_sync(0xffffffffu, ns, 0);
+        const bool over = n > b2.cap;  // the rest of the list is spilled
+        const bool identity = over && ns > b2.spill_cap;  // spill lost
+        if (over && lane == 0) {
             atomicOr(&a.status[0], kStatusBinOverflow);  // sticky report
             atomicOr(&a.status[1], 2u);  // this iteration: grow the rim bins
         }
-        const int end = identity ? a.n_faces : n;
+        const int end = identity ? a.n_faces : (over ? b2.cap : n);
         const int* lst = b2.list + bin * b2.cap;
         const float4* src = reinterpret_cast<const float4*>(a.recs);
-        for (int base = 0; base < end; base += kRimChunk) {
-            const int cn = imin_(kRimChunk, end - base);
-            __syncwarp();
-            if (lane < cn)
-                ids_sh[w][lane] = identity ? a.n_faces - 1 - (base + lane)
-                                           : lst[base + lane];
+        // Stages the records of ids_sh[w][0..cn) and folds their fragments.
+        auto run = [&](int cn) {
             __syncwarp();
             float4* dst = reinterpret_cast<float4*>(recs_sh[w]);
             for (int i = lane; i < cn * kRecVec4; i += 32) {
@@ -909,7 +1036,7 @@ static __device__ void rim_tile(const SweepArgs& a, FixedBins b2, int tile,
                 dst[i] = src[size_t(ids_sh[w][j]) * kRecVec4 + q];
             }
             __syncwarp();
-            if (!open) continue;
+            if (!open) return;
             for (int j = 0; j < cn; j++) {
                 const int f = ids_sh[w][j];
                 const FaceRec& r = recs_sh[w][j];
@@ -928,6 +1055,28 @@ static __device__ void rim_tile(const SweepArgs& a, FixedBins b2, int tile,
                     eval_full(s, px, py, r, f, a.radius, peel, prev);
                 }
             }
+        };
+        for (int base = 0; base < end; base += kRimChunk) {
+            const int cn = imin_(kRimChunk, end - base);
+            __syncwarp();
+            if (lane < cn)
+                ids_sh[w][lane] = identity ? a.n_faces - 1 - (base + lane)
+                                           : lst[base + lane];
+            run(cn);
+        }
+        if (over && !identity) {
+            // this block's spilled entries, kRimChunk scanned per step
+            for (int sb = 0; sb < ns; sb += kRimChunk) {
+                const int i = sb + lane;
+                int2 e = make_int2(-1, 0);
+                if (lane < kRimChunk && i < ns) e = b2.spill[i];
+                const bool match = e.x == int(bin);
+                const unsigned mm = __ballot_sync(0xffffffffu, match);
+                if (mm == 0u) continue;
+                __syncwarp();
+                if (match) ids_sh[w][__popc(mm & ((1u << lane) - 1u))] = e.y;
+                run(__popc(mm));
+            }
         }
     }
     epi(a, x, y, in, s);
@@ -944,6 +1093,46 @@ __global__ void __launch_bounds__(kTileThreads)
     a.rim = a0.rim + a.v * view_stride_rim;
     if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
     sweep1_tile(a, b1, blockIdx.x, state, mask, epi);
+}
+
+// Finishes the sweep-1 tiles whose bins overflowed into the spill list:
+// their survivors over the own-list entries were stored by sweep 1; the
+// spilled entries are folded here, then the tile ends as in sweep 1. A grid
+// of any size strides over the parked tiles (none: every block exits).
+template <class Epi>
+__global__ void __launch_bounds__(kTileThreads)
+        k_sweep1_spill(SweepArgs a0, FixedBins1 b1, int2* state, int* mask,
+                       size_t view_stride_recs, size_t view_stride_px,
+                       size_t view_stride_rim, Epi epi) {
+    __shared__ FaceRec sh[kRecChunk];
+    __shared__ unsigned long long keys[kSortMax];
+    __shared__ int warp_open[8];
+    __shared__ int n_match;
+    const int n_parked = *b1.parked_n;
+    const int ns_all = *b1.spill_n;
+    const bool all_faces = ns_all > b1.spill_cap;  // spill entries were lost
+    const int ns = imin_(ns_all, b1.spill_cap);
+    for (int k = blockIdx.x; k < n_parked; k += gridDim.x) {
+        const int bin = b1.parked[k];
+        SweepArgs a = a0;
+        a.v = bin / a0.n_tiles;
+        const int tile = bin - a.v * a0.n_tiles;
+        a.recs = a0.recs + a.v * view_stride_recs;
+        a.rim = a0.rim + a.v * view_stride_rim;
+        if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
+        int x, y;
+        tile_xy(tile, a.tiles_x, &x, &y);
+        const bool in = x < a.W && y < a.H;
+        const size_t pix = size_t(y) * a.W + x;
+        const bool peel = a.prev != nullptr;
+        const float prev = (in && peel) ? a.prev[pix] : 0.f;
+        Survivor s{1.f, -1, false};
+        if (in) s = unpack(state[size_t(a.v) * a.W * a.H + pix]);
+        sweep1_spilled(a, b1, bin, ns, all_faces, x, y, in, peel, prev,
+                       a.radius < kMaxFastRadius, sh, keys, &n_match, s);
+        sweep1_finish(a, size_t(bin), x, y, in, s, state, mask, warp_open, epi);
+        __syncthreads();  // warp_open / sh reuse by the next parked tile
+    }
 }
 
 template <class Epi>

@@ -13,17 +13,27 @@ namespace dressi {
 void default_caps(SoftDims* d) {
     // Sweep-1 bins hold the faces whose hard bbox (+ margin) touches a tile
     // (~4 tiles per face on the configs' meshes); rim bins hold the soft
-    // triangles touching an open 8x4 block. An overflowing bin falls back to
-    // an exhaustive, still exact, scan of all faces.
+    // triangles touching an open 8x4 block. Entries past a bin's capacity go
+    // to its set's spill list; only a full spill list makes the bin's
+    // consumer scan all faces (every path is exact).
     const long long f = d->n_faces, t = std::max(d->n_tiles, 1);
     d->cap1 = int(std::min<long long>(std::max<long long>(256, 8 * ((4 * f + t - 1) / t)),
                                       1 << 16));
     d->cap2 = 1024;
-    // Test hook: DRESSI_B200_BIN_CAP forces a (small) capacity so the
-    // overflow fallback can be exercised.
+    // Spill lists: room for a few overflowing bins per view.
+    const long long sp = std::min<long long>(
+            std::max<long long>(1 << 16, 4ll * d->views * t), 1 << 24);
+    d->spill1 = d->spill2 = int(sp);
+    // Test hooks: DRESSI_B200_BIN_CAP forces a (small) bin capacity so the
+    // spill path can be exercised, DRESSI_B200_SPILL_CAP a small spill list
+    // so the all-faces fallback can be.
     if (const char* e = std::getenv("DRESSI_B200_BIN_CAP")) {
         const long long c = std::atoll(e);
         if (c > 0) d->cap1 = d->cap2 = int(std::min<long long>(c, 1 << 16));
+    }
+    if (const char* e = std::getenv("DRESSI_B200_SPILL_CAP")) {
+        const long long c = std::atoll(e);
+        if (c >= 0) d->spill1 = d->spill2 = int(std::min<long long>(c, 1 << 24));
     }
 }
 
@@ -42,9 +52,18 @@ void carve_soft_bins(Arena& a, const SoftDims& d, SoftBuffers* b) {
     b->bin1.cap = d.cap1;
     b->bin1.cursor = a.take<int>(vt);
     b->bin1.list = a.take<unsigned long long>(vt * d.cap1);
+    b->bin1.spill_cap = d.spill1;
+    b->bin1.spill_n = a.take<int>(1);
+    b->bin1.spill_key = a.take<unsigned long long>(std::max(d.spill1, 1));
+    b->bin1.spill_bin = a.take<int>(std::max(d.spill1, 1));
+    b->bin1.parked_n = a.take<int>(1);
+    b->bin1.parked = a.take<int>(std::max<size_t>(vt, 1));
     b->bin2.cap = d.cap2;
     b->bin2.cursor = a.take<int>(vb);
     b->bin2.list = a.take<int>(vb * d.cap2);
+    b->bin2.spill_cap = d.spill2;
+    b->bin2.spill_n = a.take<int>(1);
+    b->bin2.spill = a.take<int2>(std::max(d.spill2, 1));
 }
 
 void carve_soft(Arena& a, const SoftDims& d, SoftBuffers* b) {
@@ -56,6 +75,9 @@ void init_soft(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
     const size_t vt = size_t(d.views) * d.n_tiles;
     DRESSI_CUDA(cudaMemsetAsync(b.bin1.cursor, 0, vt * sizeof(int), s));
     DRESSI_CUDA(cudaMemsetAsync(b.bin2.cursor, 0, vt * 8 * sizeof(int), s));
+    DRESSI_CUDA(cudaMemsetAsync(b.bin1.spill_n, 0, sizeof(int), s));
+    DRESSI_CUDA(cudaMemsetAsync(b.bin1.parked_n, 0, sizeof(int), s));
+    DRESSI_CUDA(cudaMemsetAsync(b.bin2.spill_n, 0, sizeof(int), s));
     DRESSI_CUDA(cudaMemsetAsync(b.status, 0, 4 * sizeof(uint32_t), s));
     DRESSI_CUDA(cudaMemsetAsync(b.rim, 0,
                                 size_t(d.views) * d.rim_cells * sizeof(int), s));
@@ -66,6 +88,8 @@ void init_soft(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
 // Op-level face setup: explicit soft clip / face ids / faces
 // (RasterizeSoftCpu's per-face prologue, cpu_raster.cpp:260-298).
 __global__ void k_face_setup_op(SoftDims d, SoftOpInputs in, SoftBuffers b) {
+    // the previous rim phase has consumed the rim spill list
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *b.bin2.spill_n = 0;
     const int f = blockIdx.x * blockDim.x + threadIdx.x;
     const int v = blockIdx.y;
     if (f >= d.n_faces) return;
@@ -134,7 +158,7 @@ void soft_rim_bins(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
     const dim3 fg((d.n_faces + 7) / 8, d.views);  // one warp per face
     ProfScope ps("rim_bin", s);
     k_rim_bin<<<fg, 256, 0, s>>>(d.n_faces, d.n_tiles, d.tiles_x, b.recs,
-                                 b.active, b.bin2);
+                                 b.active, b.bin2, b.bin1);
     check_launch();
 }
 

@@ -166,14 +166,18 @@ def test_empty_mesh_and_index_errors(cuda, port):
         ops.soft_clip(T(clip, cuda), T(bad, cuda), 16, 16, 2.0)
 
 
-def test_bin_overflow_fallback_is_exact(cuda, port, monkeypatch):
-    """A tile-list capacity too small for the scene makes the device fall
-    back to exhaustive (all-faces) sweeps: still bit-exact, and flagged in
-    the status word."""
+@pytest.mark.parametrize("spill_cap", [None, "0"])
+def test_bin_overflow_fallback_is_exact(cuda, port, monkeypatch, spill_cap):
+    """A tile-list capacity too small for the scene sends the excess entries
+    to the spill lists (spill_cap None) or, with no spill room, makes the
+    device fall back to exhaustive (all-faces) sweeps: bit-exact either way,
+    and flagged in the status word."""
     from opendressi_b200 import ops
     from opendressi_b200 import _native as N
 
     monkeypatch.setenv("DRESSI_B200_BIN_CAP", "64")
+    if spill_cap is not None:
+        monkeypatch.setenv("DRESSI_B200_SPILL_CAP", spill_cap)
     sc = scene.silhouette_scene(level=3, n_views=1, res=128, seed=9)
     clip = port.transform_clip(sc.pos0, sc.mvps[0])
     soft = port.soft_clip(clip, sc.faces_f, 128, 128, sc.radius_px)
