@@ -715,6 +715,515 @@ int orc_silhouette_run(float* pos, uint32_t n_verts, const float* faces,
     return rc;
 }
 
+/* ------------------------------------------------------ screen-space AA */
+
+typedef struct {
+    float r;
+    uint32_t ia, ib;     /* vertex ids of the chosen edge */
+    float qa[2], qb[2];  /* its screen endpoints */
+    float es, len;       /* edge function at s's centre, edge length */
+} aa_pair_t;
+
+static const int kAaOffs[8][2] = {{-1, -1}, {0, -1}, {1, -1}, {-1, 0},
+                                  {1, 0},   {-1, 1}, {0, 1},  {1, 1}};
+
+/* EvalAaPair (cpu_raster.cpp:371-454): the silhouette edge crossed between
+ * pixel s and its neighbour n, taken from the owner triangle (n's first,
+ * then s's), with r = min(|e(s)| / |edge|, 1). */
+static int aa_pair(const float* tri, const float* clip, uint32_t n_verts,
+                   const float* faces, uint32_t n_faces, uint32_t w,
+                   uint32_t h, int sx, int sy, int nx, int ny,
+                   aa_pair_t* out) {
+    const int its = to_i32(tri[(size_t)sy * w + sx] + 0.5f);
+    const int itn = to_i32(tri[(size_t)ny * w + nx] + 0.5f);
+    if (its == itn) return 0;
+    const float ps[2] = {(float)sx + 0.5f, (float)sy + 0.5f};
+    const float pn[2] = {(float)nx + 0.5f, (float)ny + 0.5f};
+    for (int o = 0; o < 2; o++) {
+        const int owner = o == 0 ? itn : its;
+        if (owner == 0) continue;
+        const uint32_t f = (uint32_t)owner - 1u;
+        if (f >= n_faces) continue;
+        uint32_t vi[3];
+        float q[3][2];
+        int ok = 1;
+        for (int k = 0; k < 3; k++) {
+            vi[k] = to_u32_via_i64(faces[(size_t)f * 3 + k] + 0.5f);
+            if (vi[k] >= n_verts ||
+                !project_ok(&clip[(size_t)vi[k] * 4], w, h, q[k], NULL)) {
+                ok = 0;
+                break;
+            }
+        }
+        if (!ok) continue;
+        int best_j = -1;
+        float best_t = 0.f;
+        for (int j = 0; j < 3; j++) {
+            const float* a = q[j];
+            const float* b = q[(j + 1) % 3];
+            const float es = (b[0] - a[0]) * (ps[1] - a[1]) -
+                             (b[1] - a[1]) * (ps[0] - a[0]);
+            const float en = (b[0] - a[0]) * (pn[1] - a[1]) -
+                             (b[1] - a[1]) * (pn[0] - a[0]);
+            if (es * en >= 0.f) continue;
+            const float t = es / (es - en);
+            if (best_j < 0 || (o == 0 ? t > best_t : t < best_t)) {
+                best_t = t;
+                best_j = j;
+            }
+        }
+        if (best_j < 0) continue;
+        const float* a = q[best_j];
+        const float* b = q[(best_j + 1) % 3];
+        const float ex = b[0] - a[0];
+        const float ey = b[1] - a[1];
+        const float len = sqrtf(ex * ex + ey * ey);
+        if (len < 1e-6f) continue;
+        const float es = ex * (ps[1] - a[1]) - ey * (ps[0] - a[0]);
+        out->r = smin(fabsf(es) / len, 1.f);
+        out->ia = vi[best_j];
+        out->ib = vi[(best_j + 1) % 3];
+        out->qa[0] = a[0];
+        out->qa[1] = a[1];
+        out->qb[0] = b[0];
+        out->qb[1] = b[1];
+        out->es = es;
+        out->len = len;
+        return 1;
+    }
+    return 0;
+}
+
+static inline int aa_inside(int x, int y, uint32_t w, uint32_t h) {
+    return x >= 0 && y >= 0 && x < (int)w && y < (int)h;
+}
+
+int orc_antialias(const float* img, uint32_t n_comp, const float* tri,
+                  const float* clip, uint32_t n_verts, const float* faces,
+                  uint32_t n_faces, uint32_t w, uint32_t h, float* out) {
+    if (n_comp < 1 || n_comp > 4) return fail("antialias: n_comp 1..4");
+    for (int y = 0; y < (int)h; y++) {
+        for (int x = 0; x < (int)w; x++) {
+            const size_t so = ((size_t)y * w + x) * n_comp;
+            const float* cs = &img[so];
+            float* dst = &out[so];
+            for (uint32_t c = 0; c < n_comp; c++) dst[c] = cs[c];
+            for (int k = 0; k < 8; k++) {
+                const int nx = x + kAaOffs[k][0], ny = y + kAaOffs[k][1];
+                aa_pair_t pr;
+                if (!aa_inside(nx, ny, w, h) ||
+                    !aa_pair(tri, clip, n_verts, faces, n_faces, w, h, x, y,
+                             nx, ny, &pr)) {
+                    for (uint32_t c = 0; c < n_comp; c++) dst[c] += cs[c];
+                    continue;
+                }
+                const float* cn = &img[((size_t)ny * w + nx) * n_comp];
+                for (uint32_t c = 0; c < n_comp; c++)
+                    dst[c] += pr.r * cs[c] + (1.f - pr.r) * cn[c];
+            }
+            for (uint32_t c = 0; c < n_comp; c++) dst[c] /= 9.f;
+        }
+    }
+    return 0;
+}
+
+int orc_antialias_bwd_img(const float* gy, uint32_t n_comp, const float* tri,
+                          const float* clip, uint32_t n_verts,
+                          const float* faces, uint32_t n_faces, uint32_t w,
+                          uint32_t h, float* out) {
+    if (n_comp < 1 || n_comp > 4) return fail("antialias: n_comp 1..4");
+    for (int y = 0; y < (int)h; y++) {
+        for (int x = 0; x < (int)w; x++) {
+            const size_t so = ((size_t)y * w + x) * n_comp;
+            float alpha_sum = 0.f;
+            float* dst = &out[so];
+            for (uint32_t c = 0; c < n_comp; c++) dst[c] = 0.f;
+            for (int k = 0; k < 8; k++) {
+                const int nx = x + kAaOffs[k][0], ny = y + kAaOffs[k][1];
+                if (!aa_inside(nx, ny, w, h)) {
+                    alpha_sum += 1.f;
+                    continue;
+                }
+                aa_pair_t pr, pr2;
+                alpha_sum += aa_pair(tri, clip, n_verts, faces, n_faces, w, h,
+                                     x, y, nx, ny, &pr)
+                                     ? pr.r
+                                     : 1.f;
+                if (aa_pair(tri, clip, n_verts, faces, n_faces, w, h, nx, ny,
+                            x, y, &pr2)) {
+                    const size_t no = ((size_t)ny * w + nx) * n_comp;
+                    for (uint32_t c = 0; c < n_comp; c++)
+                        dst[c] += (1.f - pr2.r) * gy[no + c];
+                }
+            }
+            for (uint32_t c = 0; c < n_comp; c++) {
+                dst[c] += gy[so + c] * (1.f + alpha_sum);
+                dst[c] /= 9.f;
+            }
+        }
+    }
+    return 0;
+}
+
+/* Wang's integer hash and its [0,1) mapping (f_ops.cpp:1473-1487) */
+static inline uint32_t wang_hash(uint32_t x) {
+    x = (x ^ 61u) ^ (x >> 16);
+    x *= 9u;
+    x ^= x >> 4;
+    x *= 0x27d4eb2du;
+    x ^= x >> 15;
+    return x;
+}
+
+static inline float hash_to_unit(uint32_t f, uint32_t s, uint32_t seed,
+                                 uint32_t salt) {
+    const uint32_t hsh = wang_hash(f * 9781u ^ s * 6151u ^ seed * 26699u ^
+                                   salt * 42589u);
+    return (float)(hsh & 0xFFFFFFu) / 16777216.f;
+}
+
+float orc_hash_to_unit(uint32_t f, uint32_t s, uint32_t seed, uint32_t salt) {
+    return hash_to_unit(f, s, seed, salt);
+}
+
+/* One active pair's vertex gradient (AntiAliasBwdVtx's accumulate lambda,
+ * f_ops.cpp:2329-2372): into dst_v for vertex v only (only_v), else into
+ * both endpoint rows of out. */
+static void aa_accumulate(const float* gy, const float* img, uint32_t n_comp,
+                          const float* clip, uint32_t w, uint32_t h,
+                          uint32_t v, int x, int y, int nx, int ny,
+                          const aa_pair_t* pr, int only_v, float* dst_v,
+                          float* out) {
+    const size_t so = ((size_t)y * w + x) * n_comp;
+    const size_t no = ((size_t)ny * w + nx) * n_comp;
+    const float w_scr = (float)w, h_scr = (float)h;
+    float gr = 0.f;
+    for (uint32_t c = 0; c < n_comp; c++)
+        gr += gy[so + c] * (img[so + c] - img[no + c]);
+    gr /= 9.f;
+    if (gr == 0.f) return;
+    const float ps[2] = {(float)x + 0.5f, (float)y + 0.5f};
+    const float sgn = pr->es >= 0.f ? 1.f : -1.f;
+    const float inv_l = 1.f / pr->len;
+    const float l3 = fabsf(pr->es) * inv_l * inv_l * inv_l;
+    const float ex = pr->qb[0] - pr->qa[0];
+    const float ey = pr->qb[1] - pr->qa[1];
+    const float dqa[2] = {sgn * inv_l * (pr->qb[1] - ps[1]) + l3 * ex,
+                          sgn * inv_l * (ps[0] - pr->qb[0]) + l3 * ey};
+    const float dqb[2] = {sgn * inv_l * (ps[1] - pr->qa[1]) - l3 * ex,
+                          sgn * inv_l * (pr->qa[0] - ps[0]) - l3 * ey};
+    const uint32_t ids[2] = {pr->ia, pr->ib};
+    const float* dqs[2] = {dqa, dqb};
+    for (int e = 0; e < 2; e++) {
+        if (only_v && ids[e] != v) continue;
+        const float gqx = gr * dqs[e][0];
+        const float gqy = gr * dqs[e][1];
+        const float* c = &clip[(size_t)ids[e] * 4];
+        float* dst = only_v ? dst_v : &out[(size_t)ids[e] * 4];
+        dst[0] += gqx * 0.5f * w_scr / c[3];
+        dst[1] += gqy * 0.5f * h_scr / c[3];
+        dst[3] += -(gqx * 0.5f * w_scr * c[0] + gqy * 0.5f * h_scr * c[1]) /
+                  (c[3] * c[3]);
+    }
+}
+
+int orc_antialias_bwd_vtx(const float* gy, const float* img, uint32_t n_comp,
+                          const float* tri, const float* clip,
+                          uint32_t n_verts, const float* faces,
+                          uint32_t n_faces, const float* vft,
+                          uint32_t max_deg, float seed, uint32_t n_samples,
+                          uint32_t w, uint32_t h, float* grad) {
+    if (n_comp < 1 || n_comp > 4) return fail("antialias: n_comp 1..4");
+    memset(grad, 0, sizeof(float) * (size_t)n_verts * 4);
+    if (n_samples == 0) {
+        /* exact: every boundary pixel pair (f_ops.cpp:2373-2396) */
+        for (int y = 0; y < (int)h; y++)
+            for (int x = 0; x < (int)w; x++)
+                for (int k = 0; k < 8; k++) {
+                    const int nx = x + kAaOffs[k][0], ny = y + kAaOffs[k][1];
+                    if (!aa_inside(nx, ny, w, h)) continue;
+                    aa_pair_t pr;
+                    if (!aa_pair(tri, clip, n_verts, faces, n_faces, w, h, x,
+                                 y, nx, ny, &pr) ||
+                        pr.r >= 1.f)
+                        continue;
+                    aa_accumulate(gy, img, n_comp, clip, w, h, 0, x, y, nx,
+                                  ny, &pr, 0, NULL, grad);
+                }
+        return 0;
+    }
+    /* stochastic, wide layout {V, max_deg} + ColSum (f_ops.cpp:2397-2470,
+     * 2567-2572; ColSum 1218-1246: rows summed in order) */
+    float* part = (float*)calloc((size_t)n_verts * max_deg * 4, sizeof(float));
+    if (!part) return fail("oom");
+    const uint32_t seed_u = to_u32_via_i64(seed + 0.5f);
+    const float w_scr = (float)w, h_scr = (float)h;
+    for (uint32_t v = 0; v < n_verts; v++) {
+        for (uint32_t d = 0; d < max_deg; d++) {
+            float* dst_v = &part[((size_t)d * n_verts + v) * 4];
+            const float fv = vft[(size_t)d * n_verts + v];
+            if (fv < -0.5f) continue;
+            const uint32_t f = to_u32_via_i64(fv + 0.5f);
+            if (f >= n_faces) continue; /* the reference reads out of range */
+            float s3[3][2];
+            int ok = 1;
+            for (int k = 0; k < 3; k++) {
+                const uint32_t vi = to_u32_via_i64(faces[(size_t)f * 3 + k] + 0.5f);
+                if (vi >= n_verts) { ok = 0; break; }
+                const float* c = &clip[(size_t)vi * 4];
+                if (c[3] <= 1e-6f) { ok = 0; break; }
+                s3[k][0] = (c[0] / c[3] * 0.5f + 0.5f) * w_scr;
+                s3[k][1] = (c[1] / c[3] * 0.5f + 0.5f) * h_scr;
+            }
+            if (!ok) continue;
+            for (uint32_t smp = 0; smp < n_samples; smp++) {
+                const int e = (int)(smp % 3);
+                const float* a = s3[e];
+                const float* b = s3[(e + 1) % 3];
+                const float ex = b[0] - a[0];
+                const float ey = b[1] - a[1];
+                const float len = sqrtf(ex * ex + ey * ey);
+                if (len < 1e-6f) continue;
+                const float u = hash_to_unit(f, smp, seed_u, 2);
+                const float o = (hash_to_unit(f, smp, seed_u, 3) * 2.f - 1.f) * 2.f;
+                const int x = to_i32(floorf(a[0] + u * ex - o * (ey / len)));
+                const int y = to_i32(floorf(a[1] + u * ey + o * (ex / len)));
+                if (!aa_inside(x, y, w, h)) continue;
+                for (int k = 0; k < 8; k++) {
+                    const int nx = x + kAaOffs[k][0], ny = y + kAaOffs[k][1];
+                    if (!aa_inside(nx, ny, w, h)) continue;
+                    aa_pair_t pr;
+                    if (!aa_pair(tri, clip, n_verts, faces, n_faces, w, h, x,
+                                 y, nx, ny, &pr) ||
+                        pr.r >= 1.f)
+                        continue;
+                    if (pr.ia != v && pr.ib != v) continue;
+                    aa_accumulate(gy, img, n_comp, clip, w, h, v, x, y, nx,
+                                  ny, &pr, 1, dst_v, NULL);
+                }
+            }
+        }
+    }
+    for (uint32_t d = 0; d < max_deg; d++)
+        for (size_t i = 0; i < (size_t)n_verts * 4; i++)
+            grad[i] += part[(size_t)d * n_verts * 4 + i];
+    free(part);
+    return 0;
+}
+
+/* ------------------------------------------- AA silhouette iteration (C4) */
+
+/* Hard mask, triangle ids and their anti-aliased image of one view
+ * (examples/silhouette_optimization/run.cpp:230-238): mask =
+ * Rasterize(clip, ones), tri = RasterizeFaceId(clip), aa = AntiAlias(mask,
+ * tri, clip). Buffers are W*W. */
+static int aa_view_fwd(const float* clip, uint32_t n_verts, const float* faces,
+                       uint32_t n_faces, uint32_t res, float* mask,
+                       float* tri, float* aa) {
+    float* ones = (float*)malloc(sizeof(float) * n_verts);
+    if (!ones) return fail("oom");
+    for (uint32_t i = 0; i < n_verts; i++) ones[i] = 1.f;
+    int rc = orc_rasterize_hard(clip, n_verts, ones, 1, faces, n_faces, res,
+                                res, mask);
+    free(ones);
+    if (rc) return rc;
+    rc = orc_rasterize_face_id(clip, n_verts, faces, n_faces, res, res, tri);
+    if (rc) return rc;
+    return orc_antialias(mask, 1, tri, clip, n_verts, faces, n_faces, res,
+                         res, aa);
+}
+
+int orc_aa_targets(const float* target_pos, uint32_t n_verts,
+                   const float* faces, uint32_t n_faces, uint32_t n_views,
+                   uint32_t res, const float* mvps, float* out) {
+    const size_t npx = (size_t)res * res;
+    float* clip = (float*)malloc(sizeof(float) * n_verts * 4);
+    float* mask = (float*)malloc(sizeof(float) * npx);
+    float* tri = (float*)malloc(sizeof(float) * npx);
+    int rc = (!clip || !mask || !tri) ? fail("oom") : 0;
+    for (uint32_t v = 0; v < n_views && !rc; v++) {
+        orc_transform_clip(target_pos, n_verts, mvps + (size_t)v * 16, clip);
+        rc = aa_view_fwd(clip, n_verts, faces, n_faces, res, mask, tri,
+                         out + (size_t)v * npx);
+    }
+    free(clip);
+    free(mask);
+    free(tri);
+    return rc;
+}
+
+/* One view of the C4 graph: loss = sum_px (t - aa)^2 / R^2, the backward
+ * of (t - pred)^2 * c in the reference AD's operation order (as sil_pixel),
+ * the AntiAlias vertex backward (n_samples, seed) and the clip transform's
+ * backward. */
+static int aa_view(const float* pos, uint32_t n_verts, const float* faces,
+                   uint32_t n_faces, const float* vft, uint32_t max_deg,
+                   uint32_t res, uint32_t n_samples, float seed,
+                   const float* mvp, const float* target, double* loss,
+                   float* gpos, float* pred_out) {
+    const size_t npx = (size_t)res * res;
+    int rc = 1;
+    float* clip = (float*)malloc(sizeof(float) * n_verts * 4);
+    float* mask = (float*)malloc(sizeof(float) * npx);
+    float* tri = (float*)malloc(sizeof(float) * npx);
+    float* pred = pred_out ? pred_out : (float*)malloc(sizeof(float) * npx);
+    float* gy = (float*)malloc(sizeof(float) * npx);
+    float* gc = (float*)malloc(sizeof(float) * n_verts * 4);
+    if (!clip || !mask || !tri || !pred || !gy || !gc) {
+        fail("oom");
+        goto done;
+    }
+    orc_transform_clip(pos, n_verts, mvp, clip);
+    if (aa_view_fwd(clip, n_verts, faces, n_faces, res, mask, tri, pred))
+        goto done;
+    const float c = 1.f / (float)(res * res);
+    double l = 0.0;
+    for (size_t i = 0; i < npx; i++) {
+        const float diff = target[i] - pred[i];
+        l += diff * diff * c;
+        const float g_m4 = 1.f * c;
+        gy[i] = -(g_m4 * diff + g_m4 * diff);
+    }
+    *loss = l;
+    if (orc_antialias_bwd_vtx(gy, mask, 1, tri, clip, n_verts, faces, n_faces,
+                              vft, max_deg, seed, n_samples, res, res, gc))
+        goto done;
+    for (uint32_t i = 0; i < n_verts; i++) {
+        const float* g = &gc[i * 4];
+        for (int j = 0; j < 3; j++) {
+            gpos[i * 3 + j] = g[0] * mvp[j * 4 + 0] + g[1] * mvp[j * 4 + 1] +
+                              g[2] * mvp[j * 4 + 2] + g[3] * mvp[j * 4 + 3];
+        }
+    }
+    rc = 0;
+done:
+    free(clip);
+    free(mask);
+    free(tri);
+    if (!pred_out) free(pred);
+    free(gy);
+    free(gc);
+    return rc;
+}
+
+typedef struct {
+    const float* pos;
+    uint32_t n_verts, n_faces, n_views, res, max_deg, n_samples;
+    const float* faces;
+    const float* vft;
+    float seed;
+    const float* mvps;
+    const float* targets;
+    double* vloss;
+    float* vgrad;
+    float* pred_out;
+    int next, err;
+    pthread_mutex_t mu;
+} aa_job;
+
+static void* aa_worker(void* arg) {
+    aa_job* j = (aa_job*)arg;
+    for (;;) {
+        pthread_mutex_lock(&j->mu);
+        const int v = j->next++;
+        pthread_mutex_unlock(&j->mu);
+        if (v >= (int)j->n_views) break;
+        const size_t npx = (size_t)j->res * j->res;
+        if (aa_view(j->pos, j->n_verts, j->faces, j->n_faces, j->vft,
+                    j->max_deg, j->res, j->n_samples, j->seed,
+                    j->mvps + (size_t)v * 16, j->targets + (size_t)v * npx,
+                    &j->vloss[v], j->vgrad + (size_t)v * j->n_verts * 3,
+                    j->pred_out ? j->pred_out + (size_t)v * npx : NULL))
+            j->err = 1;
+    }
+    return NULL;
+}
+
+int orc_aa_silhouette_loss_grad(const float* pos, uint32_t n_verts,
+                                const float* faces, uint32_t n_faces,
+                                const float* vft, uint32_t max_deg,
+                                uint32_t n_views, uint32_t res,
+                                uint32_t n_samples, float seed,
+                                const float* mvps, const float* targets,
+                                uint32_t threads, double* loss, float* grad,
+                                float* pred_out) {
+    aa_job j;
+    memset(&j, 0, sizeof(j));
+    j.pos = pos;
+    j.n_verts = n_verts;
+    j.n_faces = n_faces;
+    j.n_views = n_views;
+    j.res = res;
+    j.max_deg = max_deg;
+    j.n_samples = n_samples;
+    j.faces = faces;
+    j.vft = vft;
+    j.seed = seed;
+    j.mvps = mvps;
+    j.targets = targets;
+    j.pred_out = pred_out;
+    j.vloss = (double*)calloc(n_views, sizeof(double));
+    j.vgrad = (float*)calloc((size_t)n_views * n_verts * 3, sizeof(float));
+    if (!j.vloss || !j.vgrad) {
+        free(j.vloss);
+        free(j.vgrad);
+        return fail("oom");
+    }
+    pthread_mutex_init(&j.mu, NULL);
+    if (threads < 1) threads = 1;
+    if (threads > n_views) threads = n_views;
+    pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * threads);
+    for (uint32_t i = 1; i < threads; i++)
+        pthread_create(&th[i], NULL, aa_worker, &j);
+    aa_worker(&j);
+    for (uint32_t i = 1; i < threads; i++) pthread_join(th[i], NULL);
+    free(th);
+    pthread_mutex_destroy(&j.mu);
+    int rc = j.err;
+    if (!rc) {
+        double l = 0.0;
+        memset(grad, 0, sizeof(float) * n_verts * 3);
+        for (uint32_t v = 0; v < n_views; v++) {
+            l += j.vloss[v];
+            const float* g = j.vgrad + (size_t)v * n_verts * 3;
+            for (size_t i = 0; i < (size_t)n_verts * 3; i++) grad[i] += g[i];
+        }
+        *loss = l;
+    }
+    free(j.vloss);
+    free(j.vgrad);
+    return rc;
+}
+
+int orc_aa_silhouette_run(float* pos, uint32_t n_verts, const float* faces,
+                          uint32_t n_faces, const float* vft,
+                          uint32_t max_deg, uint32_t n_views, uint32_t res,
+                          uint32_t n_samples, float lr, const float* mvps,
+                          const float* targets, uint32_t n_iters,
+                          uint32_t threads, float* loss_trace) {
+    const size_t n = (size_t)n_verts * 3;
+    float* m = (float*)calloc(n, sizeof(float));
+    float* v = (float*)calloc(n, sizeof(float));
+    float* g = (float*)calloc(n, sizeof(float));
+    float t = 0.f;
+    int rc = 0;
+    if (!m || !v || !g) rc = fail("oom");
+    for (uint32_t it = 0; it < n_iters && !rc; it++) {
+        double l = 0.0;
+        /* the in-graph counter (before its update) seeds the sampling */
+        rc = orc_aa_silhouette_loss_grad(pos, n_verts, faces, n_faces, vft,
+                                         max_deg, n_views, res, n_samples, t,
+                                         mvps, targets, threads, &l, g, NULL);
+        if (rc) break;
+        loss_trace[it] = (float)l;
+        orc_adam(pos, m, v, &t, g, (uint32_t)n, lr, 0.9f, 0.999f, 1e-8f);
+    }
+    free(m);
+    free(v);
+    free(g);
+    return rc;
+}
+
 /* --------------------------------------------------------- image fitting */
 
 /* Sum (f_ops.cpp:1037-1043, the Reduce2x2Sum chain 998-1033) followed by

@@ -93,6 +93,59 @@ int orc_silhouette_run(float* pos, uint32_t n_verts, const float* faces,
                        const float* targets, uint32_t n_iters,
                        uint32_t threads, float* loss_trace);
 
+/* F::AntiAlias forward (f_ops.cpp:2543-2575 over EvalAaPair,
+ * cpu_raster.cpp:371-454): img/out W*H*n_comp, tri W*H (face id + 1). */
+int orc_antialias(const float* img, uint32_t n_comp, const float* tri,
+                  const float* clip, uint32_t n_verts, const float* faces,
+                  uint32_t n_faces, uint32_t w, uint32_t h, float* out);
+
+/* AntiAliasBwdImg (f_ops.cpp:2220-2278): out = d(sum gy*aa)/d img. */
+int orc_antialias_bwd_img(const float* gy, uint32_t n_comp, const float* tri,
+                          const float* clip, uint32_t n_verts,
+                          const float* faces, uint32_t n_faces, uint32_t w,
+                          uint32_t h, float* out);
+
+/* AntiAliasBwdVtx (f_ops.cpp:2284-2476): grad[V*4] = d(sum gy*aa)/d clip.
+ * n_samples == 0: the exact scan; > 0: the stochastic edge samples seeded
+ * by `seed` (the {V,max_deg} partials summed in row order, as ColSum).
+ * vft = VertexFacesTex {V,max_deg} (row d at vft[d*V]). */
+int orc_antialias_bwd_vtx(const float* gy, const float* img, uint32_t n_comp,
+                          const float* tri, const float* clip,
+                          uint32_t n_verts, const float* faces,
+                          uint32_t n_faces, const float* vft,
+                          uint32_t max_deg, float seed, uint32_t n_samples,
+                          uint32_t w, uint32_t h, float* grad);
+
+/* HashToUnit (f_ops.cpp:1481-1486) over Wang's integer hash. */
+float orc_hash_to_unit(uint32_t f, uint32_t s, uint32_t seed, uint32_t salt);
+
+/* Anti-aliased target masks of a mesh (run.cpp:352-362 with seed 0 and the
+ * exact backward): out[n_views*W*W]. */
+int orc_aa_targets(const float* target_pos, uint32_t n_verts,
+                   const float* faces, uint32_t n_faces, uint32_t n_views,
+                   uint32_t res, const float* mvps, float* out);
+
+/* One AA-silhouette iteration (C4; run.cpp:230-238 + 386-396): loss and
+ * position gradient, views on `threads` threads. pred_out (nullable) gets
+ * the n_views*W*W anti-aliased predictions. */
+int orc_aa_silhouette_loss_grad(const float* pos, uint32_t n_verts,
+                                const float* faces, uint32_t n_faces,
+                                const float* vft, uint32_t max_deg,
+                                uint32_t n_views, uint32_t res,
+                                uint32_t n_samples, float seed,
+                                const float* mvps, const float* targets,
+                                uint32_t threads, double* loss, float* grad,
+                                float* pred_out);
+
+/* Full AA-silhouette run: n_iters of loss/grad (sampling seeded by the
+ * in-graph Adam counter) + Adam (lr, 0.9, 0.999, 1e-8). */
+int orc_aa_silhouette_run(float* pos, uint32_t n_verts, const float* faces,
+                          uint32_t n_faces, const float* vft,
+                          uint32_t max_deg, uint32_t n_views, uint32_t res,
+                          uint32_t n_samples, float lr, const float* mvps,
+                          const float* targets, uint32_t n_iters,
+                          uint32_t threads, float* loss_trace);
+
 /* 2-D image fitting (C1): loss = Mean((p - t)^2) over W*H*4, Adam on p.
  * loss_trace[n_iters] = loss at the start of each iteration. */
 int orc_image_fit_run(float* param, const float* target, uint32_t w,

@@ -172,6 +172,84 @@ class Port(_Lib):
             _u32(n_iters), _fp(trace)), "image_fit_run")
         return trace, param
 
+    def antialias(self, img, tri, clip, faces):
+        img, tri, clip, faces = map(_f32, (img, tri, clip, faces))
+        h, w = tri.shape
+        nc = 1 if img.ndim == 2 else img.shape[2]
+        out = np.zeros_like(img)
+        self._err(self.lib.orc_antialias(
+            _fp(img), _u32(nc), _fp(tri), _fp(clip), _u32(clip.shape[0]),
+            _fp(faces), _u32(faces.shape[0]), _u32(w), _u32(h), _fp(out)),
+            "antialias")
+        return out
+
+    def antialias_bwd_img(self, gy, tri, clip, faces):
+        gy, tri, clip, faces = map(_f32, (gy, tri, clip, faces))
+        h, w = tri.shape
+        nc = 1 if gy.ndim == 2 else gy.shape[2]
+        out = np.zeros_like(gy)
+        self._err(self.lib.orc_antialias_bwd_img(
+            _fp(gy), _u32(nc), _fp(tri), _fp(clip), _u32(clip.shape[0]),
+            _fp(faces), _u32(faces.shape[0]), _u32(w), _u32(h), _fp(out)),
+            "antialias_bwd_img")
+        return out
+
+    def antialias_bwd_vtx(self, gy, img, tri, clip, faces, vft, seed,
+                          n_samples):
+        gy, img, tri, clip, faces, vft = map(_f32, (gy, img, tri, clip,
+                                                    faces, vft))
+        h, w = tri.shape
+        nc = 1 if gy.ndim == 2 else gy.shape[2]
+        out = np.zeros((clip.shape[0], 4), np.float32)
+        self._err(self.lib.orc_antialias_bwd_vtx(
+            _fp(gy), _fp(img), _u32(nc), _fp(tri), _fp(clip),
+            _u32(clip.shape[0]), _fp(faces), _u32(faces.shape[0]), _fp(vft),
+            _u32(vft.shape[0]), C.c_float(seed), _u32(n_samples), _u32(w),
+            _u32(h), _fp(out)), "antialias_bwd_vtx")
+        return out
+
+    def hash_to_unit(self, f, s, seed, salt):
+        self.lib.orc_hash_to_unit.restype = C.c_float
+        return float(self.lib.orc_hash_to_unit(_u32(f), _u32(s), _u32(seed),
+                                               _u32(salt)))
+
+    def aa_targets(self, target_pos, faces, mvps, res):
+        target_pos, faces, mvps = map(_f32, (target_pos, faces, mvps))
+        out = np.zeros((mvps.shape[0], res, res), np.float32)
+        self._err(self.lib.orc_aa_targets(
+            _fp(target_pos), _u32(target_pos.shape[0]), _fp(faces),
+            _u32(faces.shape[0]), _u32(mvps.shape[0]), _u32(res), _fp(mvps),
+            _fp(out)), "aa_targets")
+        return out
+
+    def aa_silhouette_loss_grad(self, pos, faces, vft, mvps, targets, res,
+                                n_samples, seed, threads=1, want_pred=False):
+        pos, faces, vft, mvps, targets = map(_f32, (pos, faces, vft, mvps,
+                                                    targets))
+        nv = mvps.shape[0]
+        grad = np.zeros_like(pos)
+        loss = C.c_double(0.0)
+        pred = np.zeros((nv, res, res), np.float32) if want_pred else None
+        self._err(self.lib.orc_aa_silhouette_loss_grad(
+            _fp(pos), _u32(pos.shape[0]), _fp(faces), _u32(faces.shape[0]),
+            _fp(vft), _u32(vft.shape[0]), _u32(nv), _u32(res),
+            _u32(n_samples), C.c_float(seed), _fp(mvps), _fp(targets),
+            _u32(threads), C.byref(loss), _fp(grad), _fp(pred)),
+            "aa_silhouette_loss_grad")
+        return loss.value, grad, pred
+
+    def aa_silhouette_run(self, pos, faces, vft, mvps, targets, res,
+                          n_samples, lr, n_iters, threads=1):
+        pos = _f32(pos).copy()
+        faces, vft, mvps, targets = map(_f32, (faces, vft, mvps, targets))
+        trace = np.zeros(n_iters, np.float32)
+        self._err(self.lib.orc_aa_silhouette_run(
+            _fp(pos), _u32(pos.shape[0]), _fp(faces), _u32(faces.shape[0]),
+            _fp(vft), _u32(vft.shape[0]), _u32(mvps.shape[0]), _u32(res),
+            _u32(n_samples), C.c_float(lr), _fp(mvps), _fp(targets),
+            _u32(n_iters), _u32(threads), _fp(trace)), "aa_silhouette_run")
+        return trace, pos
+
     def vertex_faces_tex(self, faces, n_verts, cap=64):
         faces = _f32(faces)
         out = np.zeros(n_verts * cap, np.float32)
@@ -259,6 +337,42 @@ class Ref(_Lib):
             _fp(pos), _fp(faces), _fp(vft), _u32(vft.shape[0]), _fp(mvps),
             _fp(targets), _u32(n_iters), _u32(threads), _fp(trace),
             _fp(pos_out), _fp(grad0), C.byref(secs)), "silhouette_run")
+        return trace, pos_out, grad0, secs.value
+
+    def antialias(self, img, tri, clip, faces, vft, seed=0.0, n_samples=0,
+                  gy=None):
+        """AntiAlias forward; with gy also (image grad, clip grad)."""
+        img, tri, clip, faces, vft = map(_f32, (img, tri, clip, faces, vft))
+        h, w = tri.shape
+        nc = 1 if img.ndim == 2 else img.shape[2]
+        out = np.zeros_like(img)
+        gi = gc = None
+        if gy is not None:
+            gy = _f32(gy)
+            gi = np.zeros_like(img)
+            gc = np.zeros((clip.shape[0], 4), np.float32)
+        self._err(self.lib.ref_antialias(
+            _fp(img), _u32(nc), _fp(tri), _fp(clip), _u32(clip.shape[0]),
+            _fp(faces), _u32(faces.shape[0]), _fp(vft), _u32(vft.shape[0]),
+            C.c_float(seed), _u32(n_samples), _u32(w), _u32(h), _fp(gy),
+            _fp(out), _fp(gi), _fp(gc)), "antialias")
+        return out if gy is None else (out, gi, gc)
+
+    def aa_silhouette_run(self, pos, faces, vft, mvps, targets, res,
+                          n_samples, lr, n_iters, threads=1,
+                          want_grad0=False):
+        pos, faces, vft, mvps, targets = map(_f32, (pos, faces, vft, mvps,
+                                                    targets))
+        trace = np.zeros(n_iters, np.float32)
+        pos_out = np.zeros_like(pos)
+        grad0 = np.zeros_like(pos) if want_grad0 else None
+        secs = C.c_double(0.0)
+        self._err(self.lib.ref_aa_silhouette_run(
+            _u32(pos.shape[0]), _u32(faces.shape[0]), _u32(mvps.shape[0]),
+            _u32(res), _u32(n_samples), C.c_float(lr), _fp(pos), _fp(faces),
+            _fp(vft), _u32(vft.shape[0]), _fp(mvps), _fp(targets),
+            _u32(n_iters), _u32(threads), _fp(trace), _fp(pos_out),
+            _fp(grad0), C.byref(secs)), "aa_silhouette_run")
         return trace, pos_out, grad0, secs.value
 
     def image_fit_run(self, param, target, lr, n_iters):

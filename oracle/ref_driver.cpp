@@ -405,6 +405,197 @@ int ref_silhouette_run(uint32_t n_verts, uint32_t n_faces, uint32_t n_views,
     });
 }
 
+// F::AntiAlias on fixed leaves (img/tri/clip/faces/vertex-faces/seed), its
+// image gradient and clip gradient for an incoming gradient gy: both from
+// BuildBackward on sum(StopGradient(gy) * AntiAlias(...)). out_img_grad /
+// out_clip_grad are nullable.
+int ref_antialias(const float* img, uint32_t n_comp, const float* tri,
+                  const float* clip, uint32_t n_verts, const float* faces,
+                  uint32_t n_faces, const float* vft, uint32_t max_deg,
+                  float seed, uint32_t n_samples, uint32_t w, uint32_t h,
+                  const float* gy, float* out, float* out_img_grad,
+                  float* out_clip_grad) {
+    return Guard([&] {
+        DRESSI_CHECK(n_comp >= 1 && n_comp <= 4, "n_comp 1..4");
+        const VType it = n_comp == 1 ? FLOAT : n_comp == 2 ? VEC2
+                                         : n_comp == 3   ? VEC3
+                                                         : VEC4;
+        Variable vimg(it, {w, h}), vtri(FLOAT, {w, h}), vclip(VEC4, {n_verts, 1}),
+                vfaces(VEC3, {n_faces, 1}), vvf(FLOAT, {n_verts, max_deg}),
+                vseed(FLOAT, {1, 1}), vgy(it, {w, h});
+        Variable aa = F::AntiAlias(vimg, vtri, vclip, vfaces, vvf, vseed,
+                                   n_samples);
+        CpuEvaluator ev;
+        ev.bind(vimg, Tensor(it, {w, h}, img));
+        ev.bind(vtri, Tensor(FLOAT, {w, h}, tri));
+        ev.bind(vclip, Tensor(VEC4, {n_verts, 1}, clip));
+        ev.bind(vfaces, Tensor(VEC3, {n_faces, 1}, faces));
+        ev.bind(vvf, Tensor(FLOAT, {n_verts, max_deg}, vft));
+        ev.bind(vseed, Tensor(FLOAT, {1, 1}, &seed));
+        CopyOut(ev.eval(aa), out);
+        if (!out_img_grad && !out_clip_grad) return;
+        ev.bind(vgy, Tensor(it, {w, h}, gy));
+        Variable loss = F::StopGradient(vgy) * aa;
+        Variable vimg_mut = vimg, vclip_mut = vclip;
+        vimg_mut.setRequiresGradRecursively();
+        vclip_mut.setRequiresGradRecursively();
+        auto [xs, gxs] = BuildBackward(loss);
+        for (size_t i = 0; i < xs.size(); i++) {
+            if (xs[i] == vimg && out_img_grad) CopyOut(ev.eval(gxs[i]), out_img_grad);
+            if (xs[i] == vclip && out_clip_grad) CopyOut(ev.eval(gxs[i]), out_clip_grad);
+        }
+    });
+}
+
+// The AA silhouette prediction of one view (C4; examples/silhouette_
+// optimization/run.cpp:230-238): mask = Rasterize(clip, ones), tri =
+// RasterizeFaceId(clip), pred = AntiAlias(mask, tri, clip, faces,
+// vertex-faces, seed, n_samples); loss = (target - pred)^2 / R^2.
+struct AaGraph {
+    Variable ones, faces_i, faces_f, vft, seed;
+};
+
+Variable AaViewLoss(const Variable& clip, const AaGraph& g,
+                    const Variable& target, uint32_t res, uint32_t n_samples) {
+    const ImgSize screen = {res, res};
+    Variable mask = F::Rasterize(clip, g.ones, g.faces_i, screen);
+    Variable tri = F::RasterizeFaceId(clip, g.ones, g.faces_i, screen);
+    Variable pred = F::AntiAlias(mask, tri, clip, g.faces_f, g.vft, g.seed,
+                                 n_samples);
+    Variable diff = F::StopGradient(target) - pred;
+    return diff * diff * (1.f / float(res * res));
+}
+
+// Full AA-silhouette optimisation: the graph of AaViewLoss over all views
+// (SumPixelWise), BuildBackward, and the in-graph Adam whose counter is also
+// the sampling seed (run.cpp:238, 421-436). threads > 1: one graph per view
+// on separate threads, gradients summed in view order, then the same Adam
+// arithmetic (as ref_silhouette_run).
+int ref_aa_silhouette_run(uint32_t n_verts, uint32_t n_faces, uint32_t n_views,
+                          uint32_t res, uint32_t n_samples, float lr,
+                          const float* pos0, const float* faces,
+                          const float* vft, uint32_t max_deg,
+                          const float* mvps, const float* targets,
+                          uint32_t n_iters, uint32_t threads,
+                          float* loss_trace, float* pos_out, float* grad0,
+                          double* seconds) {
+    return Guard([&] {
+        const float b1 = 0.9f, b2 = 0.999f, eps = 1e-8f;
+        const size_t px = size_t(res) * res;
+        CpuTensor t_faces = Tensor(VEC3, {n_faces, 1}, faces);
+        CpuTensor t_faces_i = t_faces;
+        t_faces_i.vtype = IVEC3;
+        CpuTensor t_vft = Tensor(FLOAT, {n_verts, max_deg}, vft);
+        std::vector<float> ones(n_verts, 1.f);
+        CpuTensor t_ones = Tensor(FLOAT, {n_verts, 1}, ones.data());
+        auto make_graph = [&](AaGraph& g) {
+            g.ones = Variable(FLOAT, {n_verts, 1});
+            g.faces_i = Variable(IVEC3, {n_faces, 1});
+            g.faces_f = Variable(VEC3, {n_faces, 1});
+            g.vft = Variable(FLOAT, {n_verts, max_deg});
+            g.seed = Variable(FLOAT, {1, 1});
+        };
+        auto bind_static = [&](CpuEvaluator& ev, const AaGraph& g) {
+            ev.bind(g.ones, t_ones);
+            ev.bind(g.faces_i, t_faces_i);
+            ev.bind(g.faces_f, t_faces);
+            ev.bind(g.vft, t_vft);
+        };
+        std::vector<float> pos(pos0, pos0 + size_t(n_verts) * 3);
+        const auto t0 = std::chrono::steady_clock::now();
+        struct ViewG {
+            AaGraph g;
+            Variable vpos, target, loss, grad;
+        };
+        const uint32_t n_graphs = threads <= 1 ? 1 : n_views;
+        std::vector<ViewG> vg(n_graphs);
+        Variables all_losses;
+        std::vector<Variable> all_targets;
+        if (threads <= 1) {
+            // one graph over every view: SumPixelWise of the view losses
+            make_graph(vg[0].g);
+            vg[0].vpos = Variable(VEC3, {n_verts, 1});
+            for (uint32_t v = 0; v < n_views; v++) {
+                all_targets.emplace_back(FLOAT, ImgSize{res, res});
+                all_losses.push_back(AaViewLoss(ClipOf(vg[0].vpos, mvps + v * 16),
+                                                vg[0].g, all_targets.back(),
+                                                res, n_samples));
+            }
+            vg[0].loss = F::SumPixelWise(all_losses);
+            vg[0].vpos.setRequiresGradRecursively();
+            auto [xs, gxs] = BuildBackward(vg[0].loss);
+            DRESSI_CHECK(xs.size() == 1, "expected one gradient leaf");
+            vg[0].grad = gxs[0];
+        } else {
+            for (uint32_t v = 0; v < n_views; v++) {
+                make_graph(vg[v].g);
+                vg[v].vpos = Variable(VEC3, {n_verts, 1});
+                vg[v].target = Variable(FLOAT, {res, res});
+                vg[v].loss = AaViewLoss(ClipOf(vg[v].vpos, mvps + v * 16),
+                                        vg[v].g, vg[v].target, res, n_samples);
+                vg[v].vpos.setRequiresGradRecursively();
+                auto [xs, gxs] = BuildBackward(vg[v].loss);
+                DRESSI_CHECK(xs.size() == 1, "expected one gradient leaf");
+                vg[v].grad = gxs[0];
+            }
+        }
+        std::vector<float> m(size_t(n_verts) * 3, 0.f), vv = m;
+        float t = 0.f;
+        std::vector<std::vector<float>> grads(n_graphs);
+        std::vector<double> vloss(n_graphs);
+        for (uint32_t it = 0; it < n_iters; it++) {
+            std::atomic<uint32_t> next{0};
+            const uint32_t nt = std::max(1u, std::min(threads, n_graphs));
+            std::vector<std::string> errs(nt);
+            auto work = [&](uint32_t tid) {
+                try {
+                    for (uint32_t v; (v = next++) < n_graphs;) {
+                        CpuEvaluator ev;
+                        bind_static(ev, vg[v].g);
+                        ev.bind(vg[v].g.seed, Tensor(FLOAT, {1, 1}, &t));
+                        if (n_graphs == 1) {
+                            for (uint32_t k = 0; k < n_views; k++)
+                                ev.bind(all_targets[k],
+                                        Tensor(FLOAT, {res, res}, targets + k * px));
+                        } else {
+                            ev.bind(vg[v].target,
+                                    Tensor(FLOAT, {res, res}, targets + v * px));
+                        }
+                        ev.bind(vg[v].vpos, Tensor(VEC3, {n_verts, 1}, pos.data()));
+                        vloss[v] = SumAll(ev.eval(vg[v].loss));
+                        grads[v] = ev.eval(vg[v].grad).data;
+                    }
+                } catch (const std::exception& e) {
+                    errs[tid] = e.what();
+                }
+            };
+            std::vector<std::thread> pool;
+            for (uint32_t i = 1; i < nt; i++) pool.emplace_back(work, i);
+            work(0);
+            for (auto& th : pool) th.join();
+            for (auto& e : errs) DRESSI_CHECK(e.empty(), e);
+            double ls = 0.0;
+            for (double l : vloss) ls += l;
+            loss_trace[it] = float(ls);
+            std::vector<float> g(size_t(n_verts) * 3, 0.f);
+            for (uint32_t v = 0; v < n_graphs; v++)
+                for (size_t i = 0; i < g.size(); i++) g[i] += grads[v][i];
+            if (it == 0 && grad0) std::copy(g.begin(), g.end(), grad0);
+            t = t + 1.f;
+            const float bc1 = 1.f - std::pow(b1, t);
+            const float bc2 = 1.f - std::pow(b2, t);
+            for (size_t i = 0; i < g.size(); i++) {
+                m[i] = m[i] * b1 + g[i] * (1.f - b1);
+                vv[i] = vv[i] * b2 + g[i] * g[i] * (1.f - b2);
+                pos[i] = pos[i] - (m[i] / bc1) / (std::sqrt(vv[i] / bc2) + eps) * lr;
+            }
+        }
+        const auto t1 = std::chrono::steady_clock::now();
+        if (seconds) *seconds = std::chrono::duration<double>(t1 - t0).count();
+        std::copy(pos.begin(), pos.end(), pos_out);
+    });
+}
+
 // 2-D image fitting (examples/image_fitting/run.cpp:40-63 with the in-graph
 // Adam of the silhouette example): loss = Mean((param - target)^2) over a
 // VEC4 image; Adam lr on param. loss_trace[i] is the Mean loss at the start
