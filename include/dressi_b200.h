@@ -134,6 +134,33 @@ int dressi_rasterize(const float* clip, uint32_t n_verts, const float* attr,
                      uint32_t views, uint32_t width, uint32_t height,
                      float* out, uint32_t* status, void* stream);
 
+/* F::AntiAlias (f_ops.cpp:2480-2579 over EvalAaPair, cpu_raster.cpp:
+ * 371-454), bit-exact: Dr.Hair screen-space anti-aliasing of img
+ * [views][H][W][n_comp] (n_comp 1..4) given the triangle-id image tri
+ * [views][H][W] (float(face)+1, 0 = background), clip [views][n_verts][4]
+ * and faces [n_faces][3]; out like img. */
+int dressi_antialias(const float* img, uint32_t n_comp, const float* tri,
+                     const float* clip, uint32_t n_verts, const float* faces,
+                     uint32_t n_faces, uint32_t views, uint32_t width,
+                     uint32_t height, float* out, uint32_t* status,
+                     void* stream);
+
+/* AntiAlias backward for an incoming gradient gy (like img):
+ * grad_img (nullable, like img) = AntiAliasBwdImg (f_ops.cpp:2220-2278),
+ * bit-exact; grad_clip (nullable) [views][n_verts][4] += AntiAliasBwdVtx
+ * (f_ops.cpp:2284-2476): n_samples == 0 the exact scan of every boundary
+ * pair, else n_samples stochastic edge samples per incident face, seeded
+ * by `seed` (the graph's seed value) over the vertex -> face table vft
+ * [max_deg][n_verts] (VertexFacesTex, mesh_utils.cpp:53-69; -1 padding). */
+int dressi_antialias_grad(const float* gy, const float* img, uint32_t n_comp,
+                          const float* tri, const float* clip,
+                          uint32_t n_verts, const float* faces,
+                          uint32_t n_faces, const float* vft,
+                          uint32_t max_deg, float seed, uint32_t n_samples,
+                          uint32_t views, uint32_t width, uint32_t height,
+                          float* grad_img, float* grad_clip, uint32_t* status,
+                          void* stream);
+
 /* ------------------------------------------------------------------------
  * Plans: one fused fwd + bwd + Adam iteration, resident on one device,
  * replayed as a CUDA graph with no per-iteration host traffic

@@ -62,6 +62,12 @@ SIGNATURES = {
                                                    _vp]),
     "dressi_rasterize": (C.c_int, [_vp, _u32, _vp, _u32, _vp, _u32, _u32,
                                    _u32, _u32, _vp, _vp, _vp]),
+    "dressi_antialias": (C.c_int, [_vp, _u32, _vp, _vp, _u32, _vp, _u32,
+                                   _u32, _u32, _u32, _vp, _vp, _vp]),
+    "dressi_antialias_grad": (C.c_int, [_vp, _vp, _u32, _vp, _vp, _u32, _vp,
+                                        _u32, _vp, _u32, C.c_float, _u32,
+                                        _u32, _u32, _u32, _vp, _vp, _vp,
+                                        _vp]),
     "dressi_silhouette_plan_create": (C.c_int, [C.POINTER(SilhouetteDesc),
                                                 C.POINTER(_vp)]),
     "dressi_image_fit_plan_create": (C.c_int, [_u32, _u32, C.c_float, C.c_int,

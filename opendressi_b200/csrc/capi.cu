@@ -366,6 +366,81 @@ int dressi_rasterize(const float* clip, uint32_t n_verts, const float* attr,
                        width, height, out, nullptr, status, stream);
 }
 
+static void aa_common_checks(const float* tri, const float* clip,
+                             uint32_t n_comp, const float* faces,
+                             uint32_t n_faces, uint32_t views, uint32_t width,
+                             uint32_t height, uint32_t* status) {
+    DRESSI_REQUIRE(tri && clip && status && (faces || n_faces == 0),
+                   "null pointer");
+    DRESSI_REQUIRE(n_comp >= 1 && n_comp <= 4,
+                   "AntiAlias: img must have 1..4 components");
+    DRESSI_REQUIRE(views >= 1 && width >= 1 && height >= 1,
+                   "AntiAlias: empty screen or no views");
+    DRESSI_REQUIRE(width <= 32768 && height <= 32768,
+                   "AntiAlias: screen larger than 32768");
+}
+
+static AaDims aa_dims(uint32_t n_comp, uint32_t n_verts, uint32_t n_faces,
+                      uint32_t views, uint32_t width, uint32_t height) {
+    AaDims d;
+    d.W = int(width);
+    d.H = int(height);
+    d.views = int(views);
+    d.n_faces = int(n_faces);
+    d.n_verts = int(n_verts);
+    d.n_comp = int(n_comp);
+    return d;
+}
+
+int dressi_antialias(const float* img, uint32_t n_comp, const float* tri,
+                     const float* clip, uint32_t n_verts, const float* faces,
+                     uint32_t n_faces, uint32_t views, uint32_t width,
+                     uint32_t height, float* out, uint32_t* status,
+                     void* stream) {
+    return guarded([&] {
+        aa_common_checks(tri, clip, n_comp, faces, n_faces, views, width,
+                         height, status);
+        DRESSI_REQUIRE(img && out, "null pointer");
+        cudaStream_t s = as_stream(stream);
+        const AaDims d = aa_dims(n_comp, n_verts, n_faces, views, width, height);
+        AsyncScratch fr(size_t(views) * std::max<uint32_t>(n_faces, 1) *
+                                sizeof(AaFace), s);
+        AaFace* recs = static_cast<AaFace*>(fr.p);
+        aa_face_setup(d, clip, faces, recs, status, s);
+        aa_forward_op(d, recs, img, tri, out, s);
+    });
+}
+
+int dressi_antialias_grad(const float* gy, const float* img, uint32_t n_comp,
+                          const float* tri, const float* clip,
+                          uint32_t n_verts, const float* faces,
+                          uint32_t n_faces, const float* vft,
+                          uint32_t max_deg, float seed, uint32_t n_samples,
+                          uint32_t views, uint32_t width, uint32_t height,
+                          float* grad_img, float* grad_clip, uint32_t* status,
+                          void* stream) {
+    return guarded([&] {
+        aa_common_checks(tri, clip, n_comp, faces, n_faces, views, width,
+                         height, status);
+        DRESSI_REQUIRE(gy, "null pointer");
+        DRESSI_REQUIRE(!grad_clip || img, "AntiAlias grad: img is required "
+                                          "for the vertex gradient");
+        DRESSI_REQUIRE(!grad_clip || n_samples == 0 || (vft && max_deg >= 1),
+                       "AntiAlias grad: stochastic samples need the vertex "
+                       "-> face table");
+        cudaStream_t s = as_stream(stream);
+        const AaDims d = aa_dims(n_comp, n_verts, n_faces, views, width, height);
+        AsyncScratch fr(size_t(views) * std::max<uint32_t>(n_faces, 1) *
+                                sizeof(AaFace), s);
+        AaFace* recs = static_cast<AaFace*>(fr.p);
+        aa_face_setup(d, clip, faces, recs, status, s);
+        if (grad_img) aa_bwd_img_op(d, recs, gy, tri, grad_img, s);
+        if (grad_clip)
+            aa_bwd_vtx_op(d, recs, gy, img, tri, clip, vft, int(max_deg),
+                          seed, int(n_samples), grad_clip, s);
+    });
+}
+
 int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
                                   dressi_plan* out) {
     return guarded([&] {

@@ -198,6 +198,36 @@ void hard_raster_op(const HardDims& d, void* workspace, const float* clip,
                     const float* attr, const float* faces, float* out,
                     float* depth_out, uint32_t* status, cudaStream_t s);
 
+// --- screen-space AA (F::AntiAlias and its backward) ---
+// Per (view, face): screen vertices in both projections the reference uses
+// and the vertex ids (64 B).
+struct __align__(16) AaFace {
+    float qx0, qy0, qx1, qy1;  // ProjectToScreen (1/w product): pair tests
+    float qx2, qy2;
+    uint32_t i0, i1;
+    float sx0, sy0, sx1, sy1;  // (c / w * 0.5 + 0.5) * size: sample placement
+    float sx2, sy2;
+    uint32_t i2, flags;        // 1: pair data valid, 2: sample data valid
+};
+static_assert(sizeof(AaFace) == 64, "AaFace layout");
+struct AaDims {
+    int W = 0, H = 0, views = 1, n_faces = 0, n_verts = 0, n_comp = 1;
+};
+// clip [views][V][4], faces [F][3] -> out [views][F].
+void aa_face_setup(const AaDims& d, const float* clip, const float* faces,
+                   AaFace* out, uint32_t* status, cudaStream_t s);
+// img / out [views][H][W][n_comp], tri [views][H][W] (face id + 1).
+void aa_forward_op(const AaDims& d, const AaFace* fr, const float* img,
+                   const float* tri, float* out, cudaStream_t s);
+void aa_bwd_img_op(const AaDims& d, const AaFace* fr, const float* gy,
+                   const float* tri, float* out, cudaStream_t s);
+// grad [views][V][4] += d(sum gy * aa)/d clip; n_samples 0 = exact scan,
+// else stochastic over vft [max_deg][V] seeded by `seed`.
+void aa_bwd_vtx_op(const AaDims& d, const AaFace* fr, const float* gy,
+                   const float* img, const float* tri, const float* clip,
+                   const float* vft, int max_deg, float seed, int n_samples,
+                   float* grad, cudaStream_t s);
+
 // --- image fitting (C1) ---
 struct FitBuffers {
     float* param;   // [n]

@@ -20,6 +20,8 @@ __all__ = [
     "rasterize_soft_grad",
     "rasterize_face_id",
     "rasterize",
+    "antialias",
+    "antialias_grad",
     "check_status",
 ]
 
@@ -197,3 +199,79 @@ def rasterize(clip, attr, faces, width: int, height: int, check: bool = True):
     if check:
         check_status(st)
     return out[0] if squeeze else out
+
+
+def _aa_inputs(img_like, tri, clip, faces, name):
+    """Normalises AntiAlias inputs: img_like [(views,) H, W(, C)], tri
+    [(views,) H, W], clip [(views,) V, 4], faces [F, 3]."""
+    tri = _dev(tri, "tri")
+    squeeze = tri.dim() == 2
+    tri, views = _views(tri, 2)
+    h, w = tri.shape[1], tri.shape[2]
+    x = _dev(img_like, name)
+    if x.dim() == (2 if squeeze else 3):
+        x = x.unsqueeze(-1)
+    x, _ = _views(x, 3)
+    x = _match_views(x, views, name)
+    if x.shape[1] != h or x.shape[2] != w:
+        raise N.DressiError(N.ERR_INVALID, f"{name} must match tri's size")
+    clip = _dev(clip, "clip")
+    clip, _ = _views(clip, 2)
+    clip = _match_views(clip, views, "clip")
+    faces = _dev(faces, "faces", 2)
+    return x, tri, clip, faces, views, h, w, squeeze
+
+
+def antialias(img, tri, clip, faces, check: bool = True):
+    """F::AntiAlias (Dr.Hair screen-space AA): img [(views,) H, W(, C)],
+    tri [(views,) H, W] = float(face)+1, clip [(views,) V, 4], faces [F, 3]
+    -> an image shaped like img."""
+    shape = img.shape
+    x, tri, clip, faces, views, h, w, _ = _aa_inputs(img, tri, clip, faces,
+                                                      "img")
+    out = torch.empty_like(x)
+    st = _new_status(x.device)
+    N.call("dressi_antialias", x.data_ptr(), x.shape[-1], tri.data_ptr(),
+           clip.data_ptr(), clip.shape[1], faces.data_ptr(), faces.shape[0],
+           views, w, h, out.data_ptr(), st.data_ptr(), _stream())
+    if check:
+        check_status(st)
+    return out.reshape(shape)
+
+
+def antialias_grad(gy, img, tri, clip, faces, vft=None, seed: float = 0.0,
+                   n_samples: int = 0, want_img: bool = True,
+                   want_clip: bool = True, check: bool = True):
+    """AntiAlias backward: (d img, d clip) of sum(gy * AntiAlias(img)).
+    n_samples == 0 gives the exact vertex gradient; > 0 the reference's
+    stochastic edge samples seeded by `seed` over vft [max_deg, V]
+    (VertexFacesTex). Returns (grad_img or None, grad_clip or None)."""
+    shape = gy.shape
+    x = None
+    if want_clip:
+        x = _aa_inputs(img, tri, clip, faces, "img")[0]
+    g, tri, clip, faces, views, h, w, squeeze = _aa_inputs(gy, tri, clip,
+                                                            faces, "gy")
+    vft_t = None
+    max_deg = 0
+    if want_clip and n_samples > 0:
+        if vft is None:
+            raise N.DressiError(N.ERR_INVALID,
+                                "stochastic samples need vft (VertexFacesTex)")
+        vft_t = _dev(vft, "vft", 2)
+        max_deg = vft_t.shape[0]
+    gi = torch.empty_like(g) if want_img else None
+    gc = (torch.zeros((views, clip.shape[1], 4), dtype=torch.float32,
+                      device=g.device) if want_clip else None)
+    st = _new_status(g.device)
+    N.call("dressi_antialias_grad", g.data_ptr(), _ptr(x), g.shape[-1],
+           tri.data_ptr(), clip.data_ptr(), clip.shape[1], faces.data_ptr(),
+           faces.shape[0], _ptr(vft_t), max_deg, float(seed), int(n_samples),
+           views, w, h, _ptr(gi), _ptr(gc), st.data_ptr(), _stream())
+    if check:
+        check_status(st)
+    if gi is not None:
+        gi = gi.reshape(shape)
+    if gc is not None and squeeze:
+        gc = gc[0]
+    return gi, gc
