@@ -180,8 +180,9 @@ enum {
     DRESSI_SLOT_GRAD = 5,    /* last gradient of the parameter             */
     DRESSI_SLOT_LOSS = 6,    /* loss of the last iteration (1 float)       */
     DRESSI_SLOT_LOSS_HISTORY = 7, /* ring of per-iteration losses          */
-    DRESSI_SLOT_RASTER = 8,  /* silhouette: RasterizeSoft images of the    */
-                             /* last dressi_plan_render() [views][R][R][4] */
+    DRESSI_SLOT_RASTER = 8,  /* silhouette: images of the last             */
+                             /* dressi_plan_render(): RasterizeSoft        */
+                             /* [views][R][R][4], AA predictions [views][R][R] */
     DRESSI_SLOT_MVP = 9      /* silhouette: view matrices [views][16]      */
 };
 
@@ -203,6 +204,27 @@ typedef struct {
 int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
                                   dressi_plan* out);
 
+/* AA silhouette optimisation (config C4; examples/silhouette_optimization/
+ * run.cpp:230-238): per view v, clip = MVP_v (pos, 1); mask =
+ * Rasterize(clip, ones); tri = RasterizeFaceId(clip); pred =
+ * AntiAlias(mask, tri, clip) with the vertex gradient from n_samples
+ * stochastic edge samples per face seeded by the Adam counter (0: the
+ * exact scan); loss = sum (target - pred)^2 / R^2; Adam on pos. Targets
+ * (dressi_plan_render_targets) are the anti-aliased target masks. */
+typedef struct {
+    uint32_t struct_size;  /* sizeof(dressi_aa_silhouette_desc) */
+    uint32_t n_verts, n_faces, n_views, res;
+    uint32_t n_samples;    /* 8 in the reference example; 0 = exact */
+    float lr, beta1, beta2, eps;
+    const float* faces;    /* host [n_faces][3] */
+    const float* mvps;     /* host [n_views][16], column-major */
+    uint32_t loss_history; /* ring capacity (0 -> 4096) */
+    int device;            /* CUDA device ordinal */
+} dressi_aa_silhouette_desc;
+
+int dressi_aa_silhouette_plan_create(const dressi_aa_silhouette_desc* desc,
+                                     dressi_plan* out);
+
 /* 2-D image fitting (config C1): loss = Mean((param - target)^2) over a
  * [h][w][4] image, Adam(lr, 0.9, 0.999, 1e-8) on param. */
 int dressi_image_fit_plan_create(uint32_t width, uint32_t height, float lr,
@@ -218,8 +240,9 @@ int dressi_plan_slot_bytes(dressi_plan p, int slot, size_t* bytes);
 /* Device address of a slot (for zero-copy wrapping by bindings). */
 int dressi_plan_slot_ptr(dressi_plan p, int slot, void** ptr);
 
-/* Silhouette only: renders the hard silhouettes of target_pos (host
- * [n_verts][3]) into the TARGET slot (setup, not part of the iteration). */
+/* Silhouette plans: renders the targets of target_pos (host [n_verts][3])
+ * into the TARGET slot -- hard silhouettes (HardSoftRas plans) or
+ * anti-aliased masks (AA plans); setup, not part of the iteration. */
 int dressi_plan_render_targets(dressi_plan p, const float* target_pos_host,
                                void* stream);
 
@@ -232,7 +255,7 @@ int dressi_plan_exec(dressi_plan p, uint32_t n_iters, void* stream);
  *  phase 1: Adam from the GRAD slot (after the caller all-reduced it). */
 int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream);
 
-/* Silhouette only: forward pass writing the RASTER slot (no update). */
+/* Silhouette plans: forward pass writing the RASTER slot (no update). */
 int dressi_plan_render(dressi_plan p, void* stream);
 
 /* Synchronises `stream`, returns the plan's device status word. */

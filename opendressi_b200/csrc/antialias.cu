@@ -164,32 +164,37 @@ __global__ void __launch_bounds__(256)
     __syncthreads();
     const int lx = threadIdx.x & 15, ly = threadIdx.x >> 4;
     const int x = x0 + lx, y = y0 + ly;
-    if (x >= d.W || y >= d.H) return;
-    const AaFace* fr = frs + size_t(v) * d.n_faces;
-    const int nc = d.n_comp;
-    const float* im = img + px0 * nc;
-    float cs[4], dst[4];
-    for (int c = 0; c < nc; c++) {
-        cs[c] = im[(size_t(y) * d.W + x) * nc + c];
-        dst[c] = cs[c];
-    }
-    const int its = ids[ly + 1][lx + 1];
-    const float psx = float(x) + 0.5f, psy = float(y) + 0.5f;
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const int nx = x + kAaOffX[k], ny = y + kAaOffY[k];
-        AaPairD pr;
-        if (nx < 0 || ny < 0 || nx >= d.W || ny >= d.H ||
-            !aa_pair(fr, d.n_faces, its, ids[ly + 1 + kAaOffY[k]][lx + 1 + kAaOffX[k]],
-                     psx, psy, float(nx) + 0.5f, float(ny) + 0.5f, &pr)) {
-            for (int c = 0; c < nc; c++) dst[c] += cs[c];
-            continue;
+    const bool in = x < d.W && y < d.H;
+    float dst[4] = {0.f, 0.f, 0.f, 0.f};
+    if (in) {
+        const AaFace* fr = frs + size_t(v) * d.n_faces;
+        const int nc = d.n_comp;
+        const float* im = img + px0 * nc;
+        float cs[4];
+        for (int c = 0; c < nc; c++) {
+            cs[c] = im[(size_t(y) * d.W + x) * nc + c];
+            dst[c] = cs[c];
         }
-        const float* cn = im + (size_t(ny) * d.W + nx) * nc;
-        for (int c = 0; c < nc; c++) dst[c] += pr.r * cs[c] + (1.f - pr.r) * cn[c];
+        const int its = ids[ly + 1][lx + 1];
+        const float psx = float(x) + 0.5f, psy = float(y) + 0.5f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int nx = x + kAaOffX[k], ny = y + kAaOffY[k];
+            AaPairD pr;
+            if (nx < 0 || ny < 0 || nx >= d.W || ny >= d.H ||
+                !aa_pair(fr, d.n_faces, its,
+                         ids[ly + 1 + kAaOffY[k]][lx + 1 + kAaOffX[k]], psx,
+                         psy, float(nx) + 0.5f, float(ny) + 0.5f, &pr)) {
+                for (int c = 0; c < nc; c++) dst[c] += cs[c];
+                continue;
+            }
+            const float* cn = im + (size_t(ny) * d.W + nx) * nc;
+            for (int c = 0; c < nc; c++)
+                dst[c] += pr.r * cs[c] + (1.f - pr.r) * cn[c];
+        }
+        for (int c = 0; c < nc; c++) dst[c] /= 9.f;
     }
-    for (int c = 0; c < nc; c++) dst[c] /= 9.f;
-    epi(d, v, x, y, dst);
+    epi(d, v, x, y, in, dst);  // every thread (epilogues may reduce a warp)
 }
 
 // Image transpose (AntiAliasBwdImg, f_ops.cpp:2220-2278).
@@ -416,8 +421,8 @@ __global__ void k_aa_bwd_vtx_vft(AaDims d, const AaFace* frs, const float* gy,
 __global__ void k_aa_bwd_vtx_faces(AaDims d, const AaFace* frs,
                                    const float* gy, const float* img,
                                    const float* tri, const float4* clip,
-                                   const float* seed, int n_samples,
-                                   float* grad) {
+                                   const float* t_ptr, float t_add,
+                                   int n_samples, float* grad) {
     const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     const int v = blockIdx.y;
     if (i >= (long long)d.n_faces * n_samples) return;
@@ -426,7 +431,7 @@ __global__ void k_aa_bwd_vtx_faces(AaDims d, const AaFace* frs,
     const AaFace* fr = frs + size_t(v) * d.n_faces;
     const AaFace r = fr[f];
     if (!(r.flags & kAaSValid)) return;
-    const uint32_t seed_u = x86_u32_via_i64(seed[0] + 0.5f);
+    const uint32_t seed_u = x86_u32_via_i64((t_ptr[0] + t_add) + 0.5f);
     aa_sample(d, v, fr, r, f, smp, seed_u, -1, gy, img, tri, clip, grad);
 }
 
@@ -434,8 +439,9 @@ namespace {
 
 struct EpiAaOut {
     float* out;
-    __device__ void operator()(const AaDims& d, int v, int x, int y,
+    __device__ void operator()(const AaDims& d, int v, int x, int y, bool in,
                                const float* val) const {
+        if (!in) return;
         float* o = out + (size_t(v) * d.W * d.H + size_t(y) * d.W + x) * d.n_comp;
         for (int c = 0; c < d.n_comp; c++) o[c] = val[c];
     }
@@ -491,6 +497,129 @@ void aa_bwd_vtx_op(const AaDims& d, const AaFace* fr, const float* gy,
                                    seed_u, n_samples, grad);
     }
     check_launch();
+}
+
+// ------------------------------------------------ AA silhouette (C4)
+
+namespace {
+
+// Per-pixel loss and its gradient w.r.t. the anti-aliased prediction, in
+// the reference autodiff's operation order for (t - pred)^2 * c with seed 1
+// (as the HardSoftRas iteration): gy = -(c*diff + c*diff). The loss is
+// reduced per warp into one of kLossSlots double slots.
+struct EpiAaSil {
+    const float* targets;
+    float* gy;
+    double* loss_slots;
+    float c;
+    __device__ void operator()(const AaDims& d, int v, int x, int y, bool in,
+                               const float* val) const {
+        float lv = 0.f;
+        if (in) {
+            const size_t pix = size_t(v) * d.W * d.H + size_t(y) * d.W + x;
+            const float diff = targets[pix] - val[0];
+            lv = diff * diff * c;
+            const float g_m4 = 1.f * c;
+            gy[pix] = -(g_m4 * diff + g_m4 * diff);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lv += __shfl_down_sync(0xffffffffu, lv, o);
+        if ((threadIdx.x & 31) == 0 && lv != 0.f) {
+            const unsigned slot = (unsigned(blockIdx.y) * gridDim.x + blockIdx.x) * 8u +
+                                  (threadIdx.x >> 5);
+            atomicAdd(&loss_slots[slot % kLossSlots], double(lv));
+        }
+    }
+};
+
+}  // namespace
+
+// Hard mask + triangle ids (one raster sweep), the per-face AA records and
+// the anti-aliased image of the plan's current clip positions; epi
+// receives the AA value of every pixel.
+template <class Epi>
+static void aa_sil_render(const SilParams& p, const AaSilBuffers& b,
+                          const Epi& epi, cudaStream_t s) {
+    HardDims hd;
+    hd.W = hd.H = p.res;
+    hd.views = p.views;
+    hd.n_faces = p.n_faces;
+    hd.n_verts = p.n_verts;
+    hd.attr_ones = 1;
+    hard_raster_op(hd, b.hard_ws, b.sil.clip, nullptr, b.sil.faces, b.mask,
+                   nullptr, b.status, s, b.tri);
+    AaDims d;
+    d.W = d.H = p.res;
+    d.views = p.views;
+    d.n_faces = p.n_faces;
+    d.n_verts = p.n_verts;
+    d.n_comp = 1;
+    aa_face_setup(d, b.sil.clip, b.sil.faces, b.frs, b.status, s);
+    {
+        ProfScope ps("aa_forward", s);
+        k_aa_forward<Epi><<<tile_grid(d), 256, 0, s>>>(d, b.frs, b.mask,
+                                                       b.tri, epi);
+    }
+    check_launch();
+}
+
+size_t aa_sil_workspace_bytes(const SilParams& p) {
+    HardDims hd;
+    hd.W = hd.H = p.res;
+    hd.views = p.views;
+    hd.n_faces = p.n_faces;
+    hd.n_verts = p.n_verts;
+    hd.attr_ones = 1;
+    return hard_workspace_bytes(hd);
+}
+
+void aa_sil_forward_backward(const SilParams& p, const AaSilBuffers& b,
+                             cudaStream_t s) {
+    sil_transform(p, b.sil, 1, nullptr, 0, b.status, s);
+    aa_sil_render(p, b, EpiAaSil{b.sil.targets, b.gy, b.sil.loss_slots, p.c},
+                  s);
+    AaDims d;
+    d.W = d.H = p.res;
+    d.views = p.views;
+    d.n_faces = p.n_faces;
+    d.n_verts = p.n_verts;
+    d.n_comp = 1;
+    const float4* c4 = reinterpret_cast<const float4*>(b.sil.clip);
+    ProfScope ps("aa_bwd_vtx", s);
+    if (p.n_samples == 0) {
+        k_aa_bwd_vtx_exact<<<tile_grid(d), 256, 0, s>>>(d, b.frs, b.gy, b.mask,
+                                                        b.tri, c4, b.sil.gclip);
+    } else {
+        // the sampling seed is the Adam counter before this iteration's
+        // update: scalars[0] - 1 once the transform has advanced it (exact
+        // for counters below 2^24)
+        const long long n = (long long)p.n_faces * p.n_samples;
+        k_aa_bwd_vtx_faces<<<dim3(unsigned((n + 255) / 256), p.views), 256,
+                             0, s>>>(d, b.frs, b.gy, b.mask, b.tri, c4,
+                                     b.sil.scalars, -1.f, p.n_samples,
+                                     b.sil.gclip);
+    }
+    check_launch();
+}
+
+void aa_sil_iteration(const SilParams& p, const AaSilBuffers& b,
+                      cudaStream_t s) {
+    aa_sil_forward_backward(p, b, s);
+    sil_grad_reduce(p, b.sil, true, s);
+}
+
+void aa_sil_predict(const SilParams& p, const AaSilBuffers& b, float* out,
+                    cudaStream_t s) {
+    sil_transform(p, b.sil, 0, nullptr, 0, b.status, s);
+    aa_sil_render(p, b, EpiAaOut{out}, s);
+}
+
+void aa_render_targets(const SilParams& p, const AaSilBuffers& b,
+                       const float* target_pos, cudaStream_t s) {
+    // target clip positions go through the plan's clip buffer (overwritten
+    // by every iteration's transform)
+    sil_transform_plain(p, b.sil, target_pos, s);
+    aa_sil_render(p, b, EpiAaOut{b.sil.targets}, s);
 }
 
 }  // namespace dressi

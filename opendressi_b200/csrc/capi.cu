@@ -94,7 +94,7 @@ struct AsyncScratch {
 using namespace dressi;
 
 struct dressi_plan_s {
-    enum Kind { kSil, kFit } kind = kSil;
+    enum Kind { kSil, kFit, kAa } kind = kSil;
     int device = 0;
     void* mem = nullptr;
     size_t mem_bytes = 0;
@@ -106,6 +106,7 @@ struct dressi_plan_s {
     SoftDims d;
     SilParams p{};
     SilBuffers b{};
+    AaSilBuffers ab{};  // AA plans (ab.sil aliases b)
     // image fit
     size_t n = 0;
     float lr = 0.f;
@@ -175,6 +176,8 @@ struct dressi_plan_s {
             if (ovf_host)
                 DRESSI_CUDA(cudaMemcpyAsync(ovf_host, b.soft.status + 1, 4,
                                             cudaMemcpyDeviceToHost, s));
+        } else if (kind == kAa) {
+            aa_sil_iteration(p, ab, s);
         } else {
             fit_iteration(n, lr, fb, s);
         }
@@ -220,6 +223,8 @@ struct dressi_plan_s {
         if (cap_stream) cudaStreamDestroy(cap_stream);
         if (mem) cudaFree(mem);
         if (bins_mem) cudaFree(bins_mem);
+        // the render slot is allocated on first use
+        if (slots[DRESSI_SLOT_RASTER].ptr) cudaFree(slots[DRESSI_SLOT_RASTER].ptr);
         if (ovf_host) cudaFreeHost(ovf_host);
         if (prev >= 0) cudaSetDevice(prev);
     }
@@ -531,6 +536,90 @@ int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
     });
 }
 
+int dressi_aa_silhouette_plan_create(const dressi_aa_silhouette_desc* desc,
+                                     dressi_plan* out) {
+    return guarded([&] {
+        DRESSI_REQUIRE(desc && out, "null pointer");
+        DRESSI_REQUIRE(desc->struct_size == sizeof(dressi_aa_silhouette_desc),
+                       "dressi_aa_silhouette_desc: struct_size mismatch");
+        DRESSI_REQUIRE(desc->n_verts > 0 && desc->n_faces > 0 &&
+                               desc->n_views > 0 && desc->res > 0,
+                       "AA silhouette plan: empty mesh, views or screen");
+        DRESSI_REQUIRE(desc->res <= 32768, "AA silhouette plan: res > 32768");
+        DRESSI_REQUIRE(desc->faces && desc->mvps, "null pointer");
+        DRESSI_REQUIRE(desc->n_samples <= 4096,
+                       "AA silhouette plan: n_samples > 4096");
+        *out = nullptr;
+        DeviceGuard dg(desc->device);
+        auto pl = std::make_unique<dressi_plan_s>();
+        pl->kind = dressi_plan_s::kAa;
+        pl->device = desc->device;
+        SilParams& p = pl->p;
+        p.n_verts = int(desc->n_verts);
+        p.n_faces = int(desc->n_faces);
+        p.views = int(desc->n_views);
+        p.res = int(desc->res);
+        p.lr = desc->lr;
+        p.b1 = desc->beta1;
+        p.b2 = desc->beta2;
+        p.eps = desc->eps;
+        p.c = 1.f / float(desc->res * desc->res);
+        p.n_samples = int(desc->n_samples);
+        const int hist = desc->loss_history ? int(desc->loss_history) : 4096;
+        const size_t V = desc->n_verts, F = desc->n_faces, NV = desc->n_views;
+        const size_t R2 = size_t(desc->res) * desc->res;
+        const size_t ws = aa_sil_workspace_bytes(p);
+        auto carve = [&](Arena& a) {
+            SilBuffers& b = pl->b;
+            b.pos = a.take<float>(V * 3);
+            b.adam_m = a.take<float>(V * 3);
+            b.adam_v = a.take<float>(V * 3);
+            b.scalars = a.take<float>(4);
+            b.faces = a.take<float>(F * 3);
+            b.mvps = a.take<float>(NV * 16);
+            b.targets = a.take<float>(NV * R2);
+            b.clip = a.take<float>(NV * V * 4);
+            b.gclip = a.take<float>(NV * V * 4);
+            b.gpos = a.take<float>(V * 3);
+            b.loss_slots = a.take<double>(kLossSlots);
+            b.loss_hist = a.take<float>(size_t(hist));
+            b.hist_cap = hist;
+            b.done = a.take<unsigned>(1);
+            AaSilBuffers& ab = pl->ab;
+            ab.tri = a.take<float>(NV * R2);
+            ab.mask = a.take<float>(NV * R2);
+            ab.gy = a.take<float>(NV * R2);
+            ab.frs = a.take<AaFace>(NV * F);
+            ab.status = a.take<uint32_t>(4);
+            ab.hard_ws = a.take<char>(ws);
+        };
+        Arena dry;
+        carve(dry);
+        pl->mem_bytes = dry.used + 256;
+        DRESSI_CUDA(cudaMalloc(&pl->mem, pl->mem_bytes));
+        Arena a{static_cast<char*>(pl->mem), pl->mem_bytes, 0};
+        carve(a);
+        pl->ab.sil = pl->b;
+        // Everything starts at zero: Adam state, counters, gradients.
+        DRESSI_CUDA(cudaMemset(pl->mem, 0, pl->mem_bytes));
+        DRESSI_CUDA(cudaMemcpy(pl->b.faces, desc->faces, F * 3 * sizeof(float),
+                               cudaMemcpyHostToDevice));
+        DRESSI_CUDA(cudaMemcpy(pl->b.mvps, desc->mvps, NV * 16 * sizeof(float),
+                               cudaMemcpyHostToDevice));
+        pl->set_slot(DRESSI_SLOT_PARAM, pl->b.pos, V * 3 * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_M, pl->b.adam_m, V * 3 * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_V, pl->b.adam_v, V * 3 * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_T, pl->b.scalars, 4);
+        pl->set_slot(DRESSI_SLOT_TARGET, pl->b.targets, NV * R2 * 4);
+        pl->set_slot(DRESSI_SLOT_GRAD, pl->b.gpos, V * 3 * 4);
+        pl->set_slot(DRESSI_SLOT_LOSS, pl->b.scalars + 3, 4);
+        pl->set_slot(DRESSI_SLOT_LOSS_HISTORY, pl->b.loss_hist, size_t(hist) * 4);
+        pl->set_slot(DRESSI_SLOT_RASTER, nullptr, NV * R2 * 4);
+        pl->set_slot(DRESSI_SLOT_MVP, pl->b.mvps, NV * 16 * 4);
+        *out = pl.release();
+    });
+}
+
 int dressi_image_fit_plan_create(uint32_t width, uint32_t height, float lr,
                                  int device, dressi_plan* out) {
     return guarded([&] {
@@ -635,7 +724,8 @@ int dressi_plan_render_targets(dressi_plan p, const float* target_pos_host,
                                void* stream) {
     return guarded([&] {
         DRESSI_REQUIRE(p && target_pos_host, "null pointer");
-        DRESSI_REQUIRE(p->kind == dressi_plan_s::kSil,
+        DRESSI_REQUIRE(p->kind == dressi_plan_s::kSil ||
+                               p->kind == dressi_plan_s::kAa,
                        "render_targets: not a silhouette plan");
         DeviceGuard dg(p->device);
         cudaStream_t s = as_stream(stream);
@@ -643,7 +733,10 @@ int dressi_plan_render_targets(dressi_plan p, const float* target_pos_host,
         AsyncScratch tp(bytes, s);
         DRESSI_CUDA(cudaMemcpyAsync(tp.p, target_pos_host, bytes,
                                     cudaMemcpyHostToDevice, s));
-        sil_render_targets(p->d, p->p, p->b, static_cast<float*>(tp.p), s);
+        if (p->kind == dressi_plan_s::kAa)
+            aa_render_targets(p->p, p->ab, static_cast<float*>(tp.p), s);
+        else
+            sil_render_targets(p->d, p->p, p->b, static_cast<float*>(tp.p), s);
         // the host array must stay valid until the copy ran
         DRESSI_CUDA(cudaStreamSynchronize(s));
     });
@@ -663,11 +756,21 @@ int dressi_plan_exec(dressi_plan p, uint32_t n_iters, void* stream) {
 int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream) {
     return guarded([&] {
         DRESSI_REQUIRE(p, "null plan");
-        DRESSI_REQUIRE(p->kind == dressi_plan_s::kSil,
+        DRESSI_REQUIRE(p->kind == dressi_plan_s::kSil ||
+                               p->kind == dressi_plan_s::kAa,
                        "exec_phase: not a silhouette plan");
         DRESSI_REQUIRE(phase == 0 || phase == 1, "exec_phase: phase is 0 or 1");
         DeviceGuard dg(p->device);
         cudaStream_t s = as_stream(stream);
+        if (p->kind == dressi_plan_s::kAa) {
+            if (phase == 0) {
+                aa_sil_forward_backward(p->p, p->ab, s);
+                sil_grad_reduce(p->p, p->b, false, s);
+            } else {
+                sil_update(p->p, p->b, s);
+            }
+            return;
+        }
         if (phase == 0) {
             p->grow_bins_if_needed(s);
             sil_forward_backward(p->d, p->p, p->b, nullptr, s);
@@ -683,12 +786,18 @@ int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream) {
 int dressi_plan_render(dressi_plan p, void* stream) {
     return guarded([&] {
         DRESSI_REQUIRE(p, "null plan");
-        DRESSI_REQUIRE(p->kind == dressi_plan_s::kSil,
+        DRESSI_REQUIRE(p->kind == dressi_plan_s::kSil ||
+                               p->kind == dressi_plan_s::kAa,
                        "render: not a silhouette plan");
         DeviceGuard dg(p->device);
         cudaStream_t s = as_stream(stream);
         auto& slot = p->slots[DRESSI_SLOT_RASTER];
         if (!slot.ptr) DRESSI_CUDA(cudaMalloc(&slot.ptr, slot.bytes));
+        if (p->kind == dressi_plan_s::kAa) {
+            aa_sil_predict(p->p, p->ab, static_cast<float*>(slot.ptr), s);
+            DRESSI_CUDA(cudaStreamSynchronize(s));
+            return;
+        }
         // A forward/backward pass whose side effects are undone: the Adam
         // counter advance is rolled back and the gradient buffers cleared.
         float t_saved = 0.f;
@@ -712,6 +821,9 @@ int dressi_plan_status(dressi_plan p, uint32_t* word, void* stream) {
         *word = 0;
         if (p->kind == dressi_plan_s::kSil) {
             DRESSI_CUDA(cudaMemcpyAsync(word, p->b.soft.status, 4,
+                                        cudaMemcpyDeviceToHost, s));
+        } else if (p->kind == dressi_plan_s::kAa) {
+            DRESSI_CUDA(cudaMemcpyAsync(word, p->ab.status, 4,
                                         cudaMemcpyDeviceToHost, s));
         }
         DRESSI_CUDA(cudaStreamSynchronize(s));

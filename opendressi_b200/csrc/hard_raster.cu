@@ -155,7 +155,7 @@ constexpr int kHardChunk = 128;
 // Otherwise writes the perspective-correct attribute (n_comp channels).
 __global__ void __launch_bounds__(kTileThreads)
         k_hard_sweep(HardDims d, HardBuffers b, const float* attr, float* out,
-                     float* depth_out) {
+                     float* depth_out, float* id_out) {
     __shared__ HardRec sh[kHardChunk];
     const int v = blockIdx.y, tile = blockIdx.x;
     const int tx = tile % d.tiles_x, ty = tile / d.tiles_x;
@@ -202,7 +202,8 @@ __global__ void __launch_bounds__(kTileThreads)
     if (!in) return;
     const size_t pix = size_t(v) * d.W * d.H + size_t(y) * d.W + x;
     if (depth_out) depth_out[pix] = best_f >= 0 ? best_z : 1.f;
-    if (!attr) {
+    if (id_out) id_out[pix] = best_f >= 0 ? float(best_f) + 1.f : 0.f;
+    if (!attr && !d.attr_ones) {
         out[pix] = best_f >= 0 ? float(best_f) + 1.f : 0.f;
         return;
     }
@@ -217,10 +218,11 @@ __global__ void __launch_bounds__(kTileThreads)
     const float iw[3] = {r.iw0, r.iw1, r.iw2};
     const uint32_t idx[3] = {r.i0, r.i1, r.i2};
     const float denom = l[0] * iw[0] + l[1] * iw[1] + l[2] * iw[2];
-    const float* av = attr + size_t(v) * d.n_verts * d.n_comp;
+    const float* av = d.attr_ones ? nullptr : attr + size_t(v) * d.n_verts * d.n_comp;
     for (int c = 0; c < d.n_comp; c++) {
         float num = 0.f;
-        for (int k = 0; k < 3; k++) num += l[k] * iw[k] * av[size_t(idx[k]) * d.n_comp + c];
+        for (int k = 0; k < 3; k++)
+            num += l[k] * iw[k] * (av ? av[size_t(idx[k]) * d.n_comp + c] : 1.f);
         o[c] = num / denom;
     }
 }
@@ -229,7 +231,8 @@ static void check_launch() { DRESSI_CUDA(cudaGetLastError()); }
 
 void hard_raster_op(const HardDims& d0, void* workspace, const float* clip,
                     const float* attr, const float* faces, float* out,
-                    float* depth_out, uint32_t* status, cudaStream_t s) {
+                    float* depth_out, uint32_t* status, cudaStream_t s,
+                    float* id_out) {
     const HardDims d = with_cap(d0);
     Arena a;
     a.base = static_cast<char*>(workspace);
@@ -239,17 +242,23 @@ void hard_raster_op(const HardDims& d0, void* workspace, const float* clip,
     b.status = status;
     const size_t vt = size_t(d.views) * d.n_tiles;
     DRESSI_CUDA(cudaMemsetAsync(b.bin.count, 0, vt * sizeof(int), s));
-    if (d.n_faces > 0) {
-        const dim3 fg((d.n_faces + 127) / 128, d.views);
-        k_hard_setup<<<fg, 128, 0, s>>>(d, reinterpret_cast<const float4*>(clip),
-                                        faces, b);
-        k_bin_scan<<<d.views, 1024, 0, s>>>(b.bin, d.n_tiles, status);
-        k_hard_fill<<<fg, 128, 0, s>>>(d, b);
-    } else {
-        k_bin_scan<<<d.views, 1024, 0, s>>>(b.bin, d.n_tiles, status);
+    {
+        ProfScope ps("hard_bin", s);
+        if (d.n_faces > 0) {
+            const dim3 fg((d.n_faces + 127) / 128, d.views);
+            k_hard_setup<<<fg, 128, 0, s>>>(
+                    d, reinterpret_cast<const float4*>(clip), faces, b);
+            k_bin_scan<<<d.views, 1024, 0, s>>>(b.bin, d.n_tiles, status);
+            k_hard_fill<<<fg, 128, 0, s>>>(d, b);
+        } else {
+            k_bin_scan<<<d.views, 1024, 0, s>>>(b.bin, d.n_tiles, status);
+        }
     }
-    k_hard_sweep<<<dim3(d.n_tiles, d.views), kTileThreads, 0, s>>>(
-            d, b, attr, out, depth_out);
+    {
+        ProfScope ps("hard_sweep", s);
+        k_hard_sweep<<<dim3(d.n_tiles, d.views), kTileThreads, 0, s>>>(
+                d, b, attr, out, depth_out, id_out);
+    }
     check_launch();
 }
 
@@ -268,6 +277,13 @@ __global__ void k_mask_from_id(float* img, size_t n) {
     for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += size_t(gridDim.x) * blockDim.x)
         img[i] = img[i] > 0.5f ? 1.f : 0.f;
+}
+
+void sil_transform_plain(const SilParams& p, const SilBuffers& b,
+                         const float* target_pos, cudaStream_t s) {
+    k_transform_plain<<<dim3((p.n_verts + 255) / 256, p.views), 256, 0, s>>>(
+            target_pos, b.mvps, p.n_verts, reinterpret_cast<float4*>(b.clip));
+    check_launch();
 }
 
 void sil_render_targets(const SoftDims& d, const SilParams& p,

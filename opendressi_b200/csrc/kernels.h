@@ -141,6 +141,7 @@ struct SilParams {
     float radius, sigma, lr, b1, b2, eps;
     float k;  // (2/R)^2 / sigma
     float c;  // 1 / R^2
+    int n_samples;  // AA plans: stochastic edge samples (0: exact)
 };
 struct SilBuffers {
     float* pos;       // [V*3]
@@ -171,6 +172,14 @@ void sil_grad_reduce(const SilParams& p, const SilBuffers& b, bool update,
 // Adam step from an externally reduced g_pos (multi-GPU: after the
 // all-reduce).
 void sil_update(const SilParams& p, const SilBuffers& b, cudaStream_t s);
+// clip = MVP (pos, 1) for every view; with `advance` also the Adam
+// counter / bias corrections of the iteration. rim (nullable) rim flags to
+// clear; status[1] is reset.
+void sil_transform(const SilParams& p, const SilBuffers& b, int advance,
+                   int* rim, int rim_cells, uint32_t* status, cudaStream_t s);
+// clip = MVP (target_pos, 1) into b.clip (target rendering).
+void sil_transform_plain(const SilParams& p, const SilBuffers& b,
+                         const float* target_pos, cudaStream_t s);
 // One full single-device iteration.
 void sil_iteration(const SoftDims& d, const SilParams& p,
                    const SilBuffers& b, cudaStream_t s);
@@ -182,6 +191,7 @@ void sil_render_targets(const SoftDims& d, const SilParams& p,
 // --- hard rasterizer (face id / attribute interpolation) ---
 struct HardDims {
     int W = 0, H = 0, views = 1, n_faces = 0, n_verts = 0, n_comp = 1;
+    int attr_ones = 0;  // the attribute is 1 at every vertex (a mask)
     int tiles_x = 0, tiles_y = 0, n_tiles = 0, cap = 0;
     void finalize() {
         tiles_x = (W + kTile - 1) / kTile;
@@ -190,13 +200,15 @@ struct HardDims {
     }
 };
 size_t hard_workspace_bytes(const HardDims& d);
-// clip [views][V][4]; attr [views][V][n_comp] (null for face id); faces
-// [F][3] shared. out: face id image [views][H][W] (attr == null) or the
-// interpolated attribute [views][H][W][n_comp]. tri_out (nullable) gets the
-// face-id image as well.
+// clip [views][V][4]; attr [views][V][n_comp] (null for face id, or with
+// d.attr_ones for a constant 1); faces [F][3] shared. out: face id image
+// [views][H][W] (no attribute) or the interpolated attribute
+// [views][H][W][n_comp]. depth_out / id_out (nullable) also get the
+// survivor's depth / the face-id image.
 void hard_raster_op(const HardDims& d, void* workspace, const float* clip,
                     const float* attr, const float* faces, float* out,
-                    float* depth_out, uint32_t* status, cudaStream_t s);
+                    float* depth_out, uint32_t* status, cudaStream_t s,
+                    float* id_out = nullptr);
 
 // --- screen-space AA (F::AntiAlias and its backward) ---
 // Per (view, face): screen vertices in both projections the reference uses
@@ -227,6 +239,31 @@ void aa_bwd_vtx_op(const AaDims& d, const AaFace* fr, const float* gy,
                    const float* img, const float* tri, const float* clip,
                    const float* vft, int max_deg, float seed, int n_samples,
                    float* grad, cudaStream_t s);
+
+// --- AA silhouette (C4): hard raster + AntiAlias + stochastic vertex
+// gradient, sharing the HardSoftRas plan's transform, gradient reduction
+// and Adam.
+struct AaSilBuffers {
+    SilBuffers sil;     // pos / Adam / targets / clip / gclip / loss ...
+    float* tri;         // [views][R][R] face id + 1
+    float* mask;        // [views][R][R] Rasterize(clip, ones)
+    float* gy;          // [views][R][R] dL / d pred
+    AaFace* frs;        // [views][F]
+    void* hard_ws;      // hard raster workspace (aa_sil_workspace_bytes)
+    uint32_t* status;   // [4]
+};
+size_t aa_sil_workspace_bytes(const SilParams& p);
+void aa_sil_forward_backward(const SilParams& p, const AaSilBuffers& b,
+                             cudaStream_t s);
+void aa_sil_iteration(const SilParams& p, const AaSilBuffers& b,
+                      cudaStream_t s);
+// The anti-aliased predictions of the current positions into out
+// [views][R][R] (no gradient, counter unchanged).
+void aa_sil_predict(const SilParams& p, const AaSilBuffers& b, float* out,
+                    cudaStream_t s);
+// targets = AntiAlias of the target mesh's mask (seed 0, forward only).
+void aa_render_targets(const SilParams& p, const AaSilBuffers& b,
+                       const float* target_pos, cudaStream_t s);
 
 // --- image fitting (C1) ---
 struct FitBuffers {

@@ -278,17 +278,21 @@ __global__ void k_gpos_adam(SilParams p, SilBuffers b, float omb1, float omb2,
 
 static void check_launch() { DRESSI_CUDA(cudaGetLastError()); }
 
+void sil_transform(const SilParams& p, const SilBuffers& b, int advance,
+                   int* rim, int rim_cells, uint32_t* status, cudaStream_t s) {
+    ProfScope ps("transform", s);
+    const dim3 vg((p.n_verts + 255) / 256, p.views);
+    k_transform<<<vg, 256, 0, s>>>(b.pos, b.mvps, p.n_verts,
+                                   reinterpret_cast<float4*>(b.clip),
+                                   b.scalars, p.b1, p.b2, advance, rim,
+                                   rim_cells, status);
+    check_launch();
+}
+
 void sil_forward_backward(const SoftDims& d, const SilParams& p,
                           const SilBuffers& b, float* rs_out,
                           cudaStream_t s) {
-    const dim3 vg((p.n_verts + 255) / 256, p.views);
-    {
-        ProfScope ps("transform", s);
-        k_transform<<<vg, 256, 0, s>>>(b.pos, b.mvps, p.n_verts,
-                                       reinterpret_cast<float4*>(b.clip),
-                                       b.scalars, p.b1, p.b2, 1, b.soft.rim,
-                                       d.rim_cells, b.soft.status);
-    }
+    sil_transform(p, b, 1, b.soft.rim, d.rim_cells, b.soft.status, s);
     const dim3 fg((d.n_faces + 127) / 128, d.views);
     {
         ProfScope ps("face_setup", s);

@@ -1,7 +1,8 @@
 """Fused fwd + bwd + Adam iterations resident on one device (CUDA graphs).
 
-``SilhouettePlan`` is the HardSoftRas silhouette optimisation (configs
-C3/C4), ``ImageFitPlan`` the 2-D image fit (C1). Both hold every buffer of
+``SilhouettePlan`` is the HardSoftRas silhouette optimisation (config C3),
+``AaSilhouettePlan`` the screen-space-AA one (C4), ``ImageFitPlan`` the 2-D
+image fit (C1). All hold every buffer of
 the iteration on the device; ``step(n)`` replays the captured iteration n
 times with no host traffic, like the reference's DressiAD::execStep replaying
 one recorded command buffer (src/dressi_ad.cpp:461-480).
@@ -20,7 +21,7 @@ import torch
 
 from . import _native as N
 
-__all__ = ["Plan", "SilhouettePlan", "ImageFitPlan"]
+__all__ = ["Plan", "SilhouettePlan", "AaSilhouettePlan", "ImageFitPlan"]
 
 
 def _stream_ptr(stream=None):
@@ -197,6 +198,49 @@ class SilhouettePlan(Plan):
 
     def loss_tensor(self) -> torch.Tensor:
         return self.slot_tensor(N.SLOT_LOSS, (1,))
+
+
+class AaSilhouettePlan(SilhouettePlan):
+    """C4 silhouette optimisation with screen-space AA (Dr.Hair): hard
+    raster + AntiAlias, vertex gradient from n_samples stochastic edge
+    samples per face (0: the exact scan)."""
+
+    def __init__(self, faces, mvps, n_verts: int, res: int,
+                 n_samples: int = 8, lr: float = 1e-3, beta1: float = 0.9,
+                 beta2: float = 0.999, eps: float = 1e-8, device: int = 0,
+                 loss_history: int = 4096):
+        faces = np.ascontiguousarray(faces, np.float32).reshape(-1, 3)
+        mvps = np.ascontiguousarray(mvps, np.float32).reshape(-1, 16)
+        self.n_verts, self.n_faces = int(n_verts), faces.shape[0]
+        self.n_views, self.res = mvps.shape[0], int(res)
+        self.n_samples = int(n_samples)
+        d = N.AaSilhouetteDesc()
+        d.struct_size = C.sizeof(N.AaSilhouetteDesc)
+        d.n_verts, d.n_faces = self.n_verts, self.n_faces
+        d.n_views, d.res = self.n_views, self.res
+        d.n_samples = self.n_samples
+        d.lr, d.beta1, d.beta2, d.eps = lr, beta1, beta2, eps
+        d.faces = faces.ctypes.data_as(C.POINTER(C.c_float))
+        d.mvps = mvps.ctypes.data_as(C.POINTER(C.c_float))
+        d.loss_history = loss_history
+        d.device = device
+        h = C.c_void_p(0)
+        N.call("dressi_aa_silhouette_plan_create", C.byref(d), C.byref(h))
+        Plan.__init__(self, h, device)
+
+    @classmethod
+    def from_scene(cls, scene, device: int = 0, views=None, n_samples=8,
+                   **kw):
+        mvps = scene.mvps if views is None else scene.mvps[views]
+        kw.setdefault("lr", scene.lr)
+        return cls(scene.faces_f, mvps, scene.n_verts, scene.res,
+                   n_samples=n_samples, device=device, **kw)
+
+    def render(self, stream=None) -> torch.Tensor:
+        """Anti-aliased predictions of the current positions [views, R, R]."""
+        N.call("dressi_plan_render", self._h, _stream_ptr(stream))
+        return self.slot_tensor(N.SLOT_RASTER,
+                                (self.n_views, self.res, self.res)).clone()
 
 
 class ImageFitPlan(Plan):
