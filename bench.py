@@ -2,13 +2,16 @@
 """Benchmark of the Dressi-AD per-iteration hot path on B200.
 
 Metric: fwd + bwd + Adam iterations/s of the silhouette
-optimisation with HardSoftRas (config C3: icosphere-5 = 10242 v / 20480 f,
-16 seeded views, 1024^2, sigma 1e-4, Adam lr 1e-3), seeded synthetic inputs
-(no dataset). One process per GPU; the 16 views are sharded over the ranks
+optimisation. Default workload: HardSoftRas (config C3: icosphere-5 =
+10242 v / 20480 f, 16 seeded views, 1024^2, sigma 1e-4, Adam lr 1e-3).
+--config c4: screen-space AA (Dr.Hair) on the same mesh, 64 views at
+1024^2, 8 stochastic edge samples per face. Seeded synthetic inputs (no
+dataset). One process per GPU; the views are sharded over the ranks
 (strong scaling) and the position gradient is all-reduced with NCCL before
 the replicated Adam step.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3|c4]
+                    [--impl reference]
 
 Prints one JSON line (rank 0). See DESIGN.md for the byte model of the
 roofline and the definition of the end-to-end (e2e) step.
@@ -41,13 +44,20 @@ def parse():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["c3", "c4"], default="c3")
     ap.add_argument("--res", type=int, default=1024)
-    ap.add_argument("--views", type=int, default=16)
+    ap.add_argument("--views", type=int, default=None,
+                    help="default: 16 (c3), 64 (c4)")
+    ap.add_argument("--samples", type=int, default=8,
+                    help="c4: stochastic edge samples per face (0: exact)")
     ap.add_argument("--level", type=int, default=5)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.views is None:
+        args.views = 16 if args.config == "c3" else 64
+    return args
 
 
 def dist_env():
@@ -58,6 +68,15 @@ def dist_env():
 
 
 def workload(args):
+    if args.config == "c4":
+        return {
+            "workload": "C4 silhouette screen-space AA (Dr.Hair) fwd+bwd+Adam",
+            "mesh": f"icosphere-{args.level}",
+            "views": args.views,
+            "res": args.res,
+            "edge_samples": args.samples,
+            "lr": 1e-3,
+        }
     return {
         "workload": "C3 silhouette HardSoftRas fwd+bwd+Adam",
         "mesh": f"icosphere-{args.level}",
@@ -66,6 +85,53 @@ def workload(args):
         "sigma": 1e-4,
         "lr": 1e-3,
     }
+
+
+def cpu_targets(args, sc, ref, port, threads):
+    """Targets of the CPU arms, computed by the CPU code itself (hard
+    silhouettes for c3; the reference's anti-aliased masks for c4, views on
+    a thread pool)."""
+    if args.config == "c3":
+        return np.stack([(port.rasterize_face_id(
+            port.transform_clip(sc.target_pos, m), sc.faces_f, sc.res, sc.res)
+            > 0).astype(np.float32) for m in sc.mvps])
+    from concurrent.futures import ThreadPoolExecutor
+
+    lib = ref if ref is not None else port
+    vft = (ref.vertex_faces_tex(sc.faces_f, sc.n_verts) if ref is not None
+           else None)
+
+    def one(m):
+        clip = port.transform_clip(sc.target_pos, m)
+        mask = lib.rasterize_hard(clip, np.ones(sc.n_verts, np.float32),
+                                  sc.faces_f, sc.res, sc.res)[..., 0]
+        tri = lib.rasterize_face_id(clip, sc.faces_f, sc.res, sc.res)
+        if ref is not None:
+            return ref.antialias(mask, tri, clip, sc.faces_f, vft)
+        return port.antialias(mask, tri, clip, sc.faces_f)
+
+    with ThreadPoolExecutor(threads) as ex:
+        return np.stack(list(ex.map(one, list(sc.mvps))))
+
+
+def cpu_run(args, sc, ref, port, vft, targets, pos, n, threads):
+    """n iterations of the CPU implementation (reference if built, else the
+    C port) from pos; returns the final positions."""
+    if args.config == "c4":
+        if ref is not None:
+            return ref.aa_silhouette_run(pos, sc.faces_f, vft, sc.mvps,
+                                         targets, sc.res, args.samples,
+                                         sc.lr, n, threads=threads)[1]
+        return port.aa_silhouette_run(pos, sc.faces_f, vft, sc.mvps, targets,
+                                      sc.res, args.samples, sc.lr, n,
+                                      threads=threads)[1]
+    if ref is not None:
+        return ref.silhouette_run(pos, sc.faces_f, vft, sc.mvps, targets,
+                                  sc.res, sc.radius_px, sc.sigma, sc.lr, n,
+                                  threads=threads)[1]
+    return port.silhouette_run(pos, sc.faces_f, sc.mvps, targets, sc.res,
+                               sc.radius_px, sc.sigma, sc.lr, n,
+                               threads=threads)[1]
 
 
 def peaks():
@@ -154,7 +220,7 @@ def run_ours(args):
 
     from opendressi_b200 import _native as N
     from opendressi_b200 import scene
-    from opendressi_b200.plans import SilhouettePlan
+    from opendressi_b200.plans import AaSilhouettePlan, SilhouettePlan
 
     world, rank, local = dist_env()
     if world != args.gpus:
@@ -168,7 +234,11 @@ def run_ours(args):
     sc = scene.silhouette_scene(level=args.level, n_views=args.views,
                                 res=args.res, seed=args.seed)
     shard = np.array_split(np.arange(args.views), world)[rank]
-    plan = SilhouettePlan.from_scene(sc, views=shard, device=local)
+    if args.config == "c4":
+        plan = AaSilhouettePlan.from_scene(sc, views=shard, device=local,
+                                           n_samples=args.samples)
+    else:
+        plan = SilhouettePlan.from_scene(sc, views=shard, device=local)
     plan.upload(N.SLOT_PARAM, sc.pos0)
     plan.render_targets(sc.target_pos)
     stream = torch.cuda.current_stream()
@@ -271,7 +341,10 @@ def run_ours(args):
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
-            traffic = json.load(f).get(f"iteration@{nvw}x{args.res}")
+            key = f"iteration@{nvw}x{args.res}"
+            if args.config != "c3":
+                key = f"{args.config}:{key}"
+            traffic = json.load(f).get(key)
     roofline = {
         "bound": "hbm", "kernel": "fused iteration (one CUDA graph)",
         "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -297,7 +370,7 @@ def run_ours(args):
                            "(view-sharded, NCCL all-reduce of the position "
                            "gradient, replicated Adam)",
                            l2="per-iteration working set > L2 (per-pixel "
-                              "survivor state 16 B/px = "
+                              "state 16 B/px = "
                               f"{nvw * args.res * args.res * 16 / 1e6:.0f} MB "
                               "per rank)"),
             "gpu_launches": int(round(launches_per_iter * args.steps)),
@@ -313,39 +386,32 @@ def run_ours(args):
 
 # -------------------------------------------------------- CPU baselines
 
-def cpu_reference_rate(args, max_seconds=40.0, min_iters=1, max_iters=2):
-    """The reference CPU implementation (oracle/_ref, else the C port) on the
-    same workload, view-parallel on the host cores."""
+def _cpu_setup(args):
     from oracle import pyoracle
     from opendressi_b200 import scene
 
     sc = scene.silhouette_scene(level=args.level, n_views=args.views,
                                 res=args.res, seed=args.seed)
     port = pyoracle.Port()
-    targets = np.stack([(port.rasterize_face_id(
-        port.transform_clip(sc.target_pos, m), sc.faces_f, sc.res, sc.res)
-        > 0).astype(np.float32) for m in sc.mvps])
+    ref = pyoracle.Ref() if pyoracle.ref_available() else None
     threads = max(1, min(os.cpu_count() or 1, args.views))
-    if pyoracle.ref_available():
-        ref = pyoracle.Ref()
-        vft = ref.vertex_faces_tex(sc.faces_f, sc.n_verts)
-        kind = "reference"
+    vft = (ref if ref is not None else port).vertex_faces_tex(sc.faces_f,
+                                                              sc.n_verts)
+    targets = cpu_targets(args, sc, ref, port, threads)
+    return sc, ref, port, vft, targets, threads
 
-        def run(n):
-            t0 = time.perf_counter()
-            ref.silhouette_run(sc.pos0, sc.faces_f, vft, sc.mvps, targets,
-                               sc.res, sc.radius_px, sc.sigma, sc.lr, n,
-                               threads=threads)
-            return time.perf_counter() - t0
-    else:
-        kind = "port"
 
-        def run(n):
-            t0 = time.perf_counter()
-            port.silhouette_run(sc.pos0, sc.faces_f, sc.mvps, targets, sc.res,
-                                sc.radius_px, sc.sigma, sc.lr, n,
-                                threads=threads)
-            return time.perf_counter() - t0
+def cpu_reference_rate(args, max_seconds=40.0, min_iters=1, max_iters=2):
+    """The reference CPU implementation (oracle/_ref, else the C port) on the
+    same workload, view-parallel on the host cores."""
+    sc, ref, port, vft, targets, threads = _cpu_setup(args)
+    kind = "reference" if ref is not None else "port"
+
+    def run(n):
+        t0 = time.perf_counter()
+        cpu_run(args, sc, ref, port, vft, targets, sc.pos0, n, threads)
+        return time.perf_counter() - t0
+
     secs = run(min_iters)
     iters = min_iters
     if secs * (max_iters / min_iters) < max_seconds and max_iters > min_iters:
@@ -354,9 +420,9 @@ def cpu_reference_rate(args, max_seconds=40.0, min_iters=1, max_iters=2):
     return {"value": iters / secs, "unit": "iterations/s", "cores": threads,
             "kind": kind,
             "sample": f"{iters} full iteration(s) of the bench workload "
-                      f"({args.views} views at {args.res}^2, icosphere-"
-                      f"{args.level}), view-parallel on {threads} host "
-                      f"threads, {secs:.1f} s"}
+                      f"({args.config}: {args.views} views at {args.res}^2, "
+                      f"icosphere-{args.level}), view-parallel on {threads} "
+                      f"host threads, {secs:.1f} s"}
 
 
 def run_reference(args):
@@ -364,20 +430,7 @@ def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return None
-    from oracle import pyoracle
-    from opendressi_b200 import scene
-
-    sc = scene.silhouette_scene(level=args.level, n_views=args.views,
-                                res=args.res, seed=args.seed)
-    port = pyoracle.Port()
-    targets = np.stack([(port.rasterize_face_id(
-        port.transform_clip(sc.target_pos, m), sc.faces_f, sc.res, sc.res)
-        > 0).astype(np.float32) for m in sc.mvps])
-    threads = max(1, min(os.cpu_count() or 1, args.views))
-    use_ref = pyoracle.ref_available()
-    if use_ref:
-        ref = pyoracle.Ref()
-        vft = ref.vertex_faces_tex(sc.faces_f, sc.n_verts)
+    sc, ref, port, vft, targets, threads = _cpu_setup(args)
     # Each step is one full view-parallel iteration; the run is capped at
     # ~170 s of timed work (steps beyond it are not run; `sample` says so).
     budget = 170.0
@@ -387,14 +440,7 @@ def run_reference(args):
     t_start = time.perf_counter()
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
-        if use_ref:
-            _, pos, _, _ = ref.silhouette_run(
-                pos, sc.faces_f, vft, sc.mvps, targets, sc.res,
-                sc.radius_px, sc.sigma, sc.lr, 1, threads=threads)
-        else:
-            _, pos = port.silhouette_run(pos, sc.faces_f, sc.mvps, targets,
-                                         sc.res, sc.radius_px, sc.sigma,
-                                         sc.lr, 1, threads=threads)
+        pos = cpu_run(args, sc, ref, port, vft, targets, pos, 1, threads)
         dt = time.perf_counter() - t0
         if i < args.warmup:
             done_w += 1
@@ -407,10 +453,11 @@ def run_reference(args):
     if not times:
         times.append(dt)
     value = len(times) / sum(times)
-    kind = "reference" if use_ref else "port"
+    kind = "reference" if ref is not None else "port"
     sample = (f"{len(times)} of {args.steps} requested steps timed (each one "
-              f"full iteration: {args.views} views at {args.res}^2, view-"
-              f"parallel on {threads} threads), {done_w} warm-up")
+              f"full iteration: {args.config}, {args.views} views at "
+              f"{args.res}^2, view-parallel on {threads} threads), {done_w} "
+              "warm-up")
     return {
         "metric": METRIC, "value": value, "unit": "iterations/s",
         "n_gpus": world, "steps": len(times), "warmup": done_w,

@@ -21,6 +21,7 @@ namespace {
 
 constexpr int kAaQValid = 1;  // all 3 vertices in range and projectable
 constexpr int kAaSValid = 2;  // all 3 vertices in range and w > 1e-6
+constexpr int kAaViewWild = 1;  // a face of the view has |screen| >= 1e18
 
 __constant__ int kAaOffX[8] = {-1, 0, 1, -1, 1, -1, 0, 1};
 __constant__ int kAaOffY[8] = {-1, -1, -1, 0, 0, 1, 1, 1};
@@ -38,7 +39,7 @@ struct AaPairD {
 // placement of AntiAliasBwdVtx.
 __global__ void k_aa_face_setup(AaDims d, const float4* clip,
                                 const float* faces, AaFace* out,
-                                uint32_t* status) {
+                                int* view_flags, uint32_t* status) {
     const int f = blockIdx.x * blockDim.x + threadIdx.x;
     const int v = blockIdx.y;
     if (f >= d.n_faces) return;
@@ -78,6 +79,13 @@ __global__ void k_aa_face_setup(AaDims d, const float4* clip,
     r.i0 = vi[0]; r.i1 = vi[1]; r.i2 = vi[2];
     r.flags = uint32_t(flags);
     out[size_t(v) * d.n_faces + f] = r;
+    // Screen coordinates below 1e18 keep every product of the pair test
+    // finite, so r is a number in [0, 1] (see k_aa_forward's shortcut).
+    if (flags & kAaQValid) {
+        bool tame = true;
+        for (int i = 0; i < 6; i++) tame = tame && fabsf(q[i]) < 1e18f;
+        if (!tame) atomicOr(&view_flags[v], kAaViewWild);
+    }
 }
 
 // EvalAaPair over the face records of one view.
@@ -151,47 +159,114 @@ __device__ __forceinline__ void aa_load_ids(const float* tri, int W, int H,
 }
 
 // Forward: out = AntiAlias(img) (f_ops.cpp:2543-2575). Grid (tiles, views).
-template <class Epi>
+// The neighbour loops are not unrolled: one copy of the pair test keeps
+// the kernels inside the instruction cache.
+//
+// Shortcut (exact): when c(s) and c(n) have the same bits and are 0 or 1
+// in every channel, r * c + (1 - r) * c == c for any r in [0, 1] (for
+// c = 1, r + fl(1 - r) rounds to exactly 1), which is what an inactive
+// pair adds; such pairs skip the pair test. r is in [0, 1] unless a face
+// of the view has wild screen coordinates (view flag), where the shortcut
+// is off. On silhouette masks only pixels next to an edge of the mask run
+// pair tests.
+// r of the pair (s, n), or -1 when the pair is inactive (r itself is >= 0
+// or NaN). Out of line: it runs only where the shortcut does not apply, and
+// keeps the forward kernel's common path small.
+static __device__ __noinline__ float aa_pair_r(const AaFace* fr, int n_faces,
+                                               const float* tri_v, int W,
+                                               int x, int y, int nx, int ny) {
+    AaPairD pr;
+    if (!aa_pair(fr, n_faces, aa_tri_id(tri_v[size_t(y) * W + x]),
+                 aa_tri_id(tri_v[size_t(ny) * W + nx]), float(x) + 0.5f,
+                 float(y) + 0.5f, float(nx) + 0.5f, float(ny) + 0.5f, &pr))
+        return -1.f;
+    return pr.r;
+}
+
+template <class Epi, int NC>
 __global__ void __launch_bounds__(256)
         k_aa_forward(AaDims d, const AaFace* frs, const float* img,
-                     const float* tri, Epi epi) {
-    __shared__ int ids[18][18];
+                     const float* tri, const int* view_flags, Epi epi) {
+    __shared__ float vals[18][18];  // n_comp == 1: the image tile + halo
     const int v = blockIdx.y;
     const int tiles_x = (d.W + 15) / 16;
     const int x0 = (blockIdx.x % tiles_x) * 16, y0 = (blockIdx.x / tiles_x) * 16;
     const size_t px0 = size_t(v) * d.W * d.H;
-    aa_load_ids(tri + px0, d.W, d.H, x0, y0, ids);
+    constexpr int nc = NC;
+    const float* im = img + px0 * nc;
+    if (nc == 1) {
+        for (int i = threadIdx.x; i < 18 * 18; i += blockDim.x) {
+            const int hx = x0 - 1 + i % 18, hy = y0 - 1 + i / 18;
+            vals[i / 18][i % 18] = (hx >= 0 && hy >= 0 && hx < d.W && hy < d.H)
+                                           ? im[size_t(hy) * d.W + hx]
+                                           : 0.f;
+        }
+    }
     __syncthreads();
+    const bool quick = !(view_flags[v] & kAaViewWild);
     const int lx = threadIdx.x & 15, ly = threadIdx.x >> 4;
     const int x = x0 + lx, y = y0 + ly;
     const bool in = x < d.W && y < d.H;
     float dst[4] = {0.f, 0.f, 0.f, 0.f};
-    if (in) {
-        const AaFace* fr = frs + size_t(v) * d.n_faces;
-        const int nc = d.n_comp;
-        const float* im = img + px0 * nc;
-        float cs[4];
-        for (int c = 0; c < nc; c++) {
-            cs[c] = im[(size_t(y) * d.W + x) * nc + c];
-            dst[c] = cs[c];
-        }
-        const int its = ids[ly + 1][lx + 1];
-        const float psx = float(x) + 0.5f, psy = float(y) + 0.5f;
+    bool flat = false;
+    if (in && nc == 1 && quick) {
+        // all 8 neighbours (off-screen ones add c too) equal a 0/1 c:
+        // c + 8c = 9c is exact and 9c / 9 == c
+        const float c0 = vals[ly + 1][lx + 1];
+        const uint32_t b0 = __float_as_uint(c0);
+        flat = c0 == 0.f || c0 == 1.f;
 #pragma unroll
         for (int k = 0; k < 8; k++) {
             const int nx = x + kAaOffX[k], ny = y + kAaOffY[k];
-            AaPairD pr;
-            if (nx < 0 || ny < 0 || nx >= d.W || ny >= d.H ||
-                !aa_pair(fr, d.n_faces, its,
-                         ids[ly + 1 + kAaOffY[k]][lx + 1 + kAaOffX[k]], psx,
-                         psy, float(nx) + 0.5f, float(ny) + 0.5f, &pr)) {
+            const bool on = nx >= 0 && ny >= 0 && nx < d.W && ny < d.H;
+            flat = flat && (!on || __float_as_uint(vals[ly + 1 + kAaOffY[k]][lx + 1 + kAaOffX[k]]) == b0);
+        }
+        if (flat) dst[0] = c0;
+    }
+    if (in && !flat) {
+        const AaFace* fr = frs + size_t(v) * d.n_faces;
+        float cs[NC];
+#pragma unroll
+        for (int c = 0; c < nc; c++) {
+            cs[c] = nc == 1 ? vals[ly + 1][lx + 1]
+                            : im[(size_t(y) * d.W + x) * nc + c];
+            dst[c] = cs[c];
+        }
+#pragma unroll 1
+        for (int k = 0; k < 8; k++) {
+            const int nx = x + kAaOffX[k], ny = y + kAaOffY[k];
+            if (nx < 0 || ny < 0 || nx >= d.W || ny >= d.H) {
+#pragma unroll
                 for (int c = 0; c < nc; c++) dst[c] += cs[c];
                 continue;
             }
-            const float* cn = im + (size_t(ny) * d.W + nx) * nc;
+            float cn[NC];
+#pragma unroll
             for (int c = 0; c < nc; c++)
-                dst[c] += pr.r * cs[c] + (1.f - pr.r) * cn[c];
+                cn[c] = nc == 1 ? vals[ly + 1 + kAaOffY[k]][lx + 1 + kAaOffX[k]]
+                                : im[(size_t(ny) * d.W + nx) * nc + c];
+            if (quick) {
+                bool same = true;
+#pragma unroll
+                for (int c = 0; c < nc; c++)
+                    same = same && __float_as_uint(cs[c]) == __float_as_uint(cn[c]) &&
+                           (cs[c] == 0.f || cs[c] == 1.f);
+                if (same) {
+#pragma unroll
+                    for (int c = 0; c < nc; c++) dst[c] += cs[c];
+                    continue;
+                }
+            }
+            const float r = aa_pair_r(fr, d.n_faces, tri + px0, d.W, x, y, nx, ny);
+            if (r == -1.f) {
+#pragma unroll
+                for (int c = 0; c < nc; c++) dst[c] += cs[c];
+                continue;
+            }
+#pragma unroll
+            for (int c = 0; c < nc; c++) dst[c] += r * cs[c] + (1.f - r) * cn[c];
         }
+#pragma unroll
         for (int c = 0; c < nc; c++) dst[c] /= 9.f;
     }
     epi(d, v, x, y, in, dst);  // every thread (epilogues may reduce a warp)
@@ -218,7 +293,7 @@ __global__ void __launch_bounds__(256)
     float alpha_sum = 0.f;
     const int its = ids[ly + 1][lx + 1];
     const float psx = float(x) + 0.5f, psy = float(y) + 0.5f;
-#pragma unroll
+#pragma unroll 1
     for (int k = 0; k < 8; k++) {
         const int nx = x + kAaOffX[k], ny = y + kAaOffY[k];
         if (nx < 0 || ny < 0 || nx >= d.W || ny >= d.H) {
@@ -246,21 +321,26 @@ __global__ void __launch_bounds__(256)
 
 // One active pair's vertex gradient (AntiAliasBwdVtx's accumulate,
 // f_ops.cpp:2329-2372) added `mult_a` / `mult_b` times to the endpoints.
-__device__ __forceinline__ void aa_accumulate(const AaDims& d, int v,
-                                              const float* gy,
-                                              const float* img,
-                                              const float4* clip, int x,
-                                              int y, int nx, int ny,
-                                              const AaPairD& pr, int mult_a,
-                                              int mult_b, float* grad) {
+// (1/9) dot(gy(s), c(s) - c(n)): the pair's weight. Zero -- the pair adds
+// nothing -- needs no pair test (the reference returns at this point).
+__device__ __forceinline__ float aa_pair_weight(const AaDims& d, int v,
+                                                const float* gy,
+                                                const float* img, int x, int y,
+                                                int nx, int ny) {
     const int nc = d.n_comp;
     const size_t px0 = size_t(v) * d.W * d.H;
     const size_t so = (px0 + size_t(y) * d.W + x) * nc;
     const size_t no = (px0 + size_t(ny) * d.W + nx) * nc;
     float gr = 0.f;
     for (int c = 0; c < nc; c++) gr += gy[so + c] * (img[so + c] - img[no + c]);
-    gr /= 9.f;
-    if (gr == 0.f) return;
+    return gr / 9.f;
+}
+
+__device__ __forceinline__ void aa_accumulate(const AaDims& d, int v,
+                                              float gr, const float4* clip,
+                                              int x, int y,
+                                              const AaPairD& pr, int mult_a,
+                                              int mult_b, float* grad) {
     const float psx = float(x) + 0.5f, psy = float(y) + 0.5f;
     const float sgn = pr.es >= 0.f ? 1.f : -1.f;
     const float inv_l = 1.f / pr.len;
@@ -311,15 +391,18 @@ __global__ void __launch_bounds__(256)
     const AaFace* fr = frs + size_t(v) * d.n_faces;
     const int its = ids[ly + 1][lx + 1];
     const float psx = float(x) + 0.5f, psy = float(y) + 0.5f;
+    #pragma unroll 1
     for (int k = 0; k < 8; k++) {
         const int nx = x + kAaOffX[k], ny = y + kAaOffY[k];
         if (nx < 0 || ny < 0 || nx >= d.W || ny >= d.H) continue;
+        const float gr = aa_pair_weight(d, v, gy, img, x, y, nx, ny);
+        if (gr == 0.f) continue;
         AaPairD pr;
         if (!aa_pair(fr, d.n_faces, its, ids[ly + 1 + kAaOffY[k]][lx + 1 + kAaOffX[k]],
                      psx, psy, float(nx) + 0.5f, float(ny) + 0.5f, &pr) ||
             pr.r >= 1.f)
             continue;
-        aa_accumulate(d, v, gy, img, clip, x, y, nx, ny, pr, 1, 1, grad);
+        aa_accumulate(d, v, gr, clip, x, y, pr, 1, 1, grad);
     }
 }
 
@@ -367,9 +450,12 @@ __device__ __forceinline__ void aa_sample(const AaDims& d, int v,
     const float* tv = tri + size_t(v) * d.W * d.H;
     const int its = aa_tri_id(tv[size_t(y) * d.W + x]);
     const float psx = float(x) + 0.5f, psy = float(y) + 0.5f;
+    #pragma unroll 1
     for (int k = 0; k < 8; k++) {
         const int nx = x + kAaOffX[k], ny = y + kAaOffY[k];
         if (nx < 0 || ny < 0 || nx >= d.W || ny >= d.H) continue;
+        const float gr = aa_pair_weight(d, v, gy, img, x, y, nx, ny);
+        if (gr == 0.f) continue;
         AaPairD pr;
         if (!aa_pair(fr, d.n_faces, its, aa_tri_id(tv[size_t(ny) * d.W + nx]),
                      psx, psy, float(nx) + 0.5f, float(ny) + 0.5f, &pr) ||
@@ -384,7 +470,7 @@ __device__ __forceinline__ void aa_sample(const AaDims& d, int v,
             mb = (r.i0 == pr.ib) + (r.i1 == pr.ib) + (r.i2 == pr.ib);
         }
         if (ma == 0 && mb == 0) continue;
-        aa_accumulate(d, v, gy, img, clip, x, y, nx, ny, pr, ma, mb, grad);
+        aa_accumulate(d, v, gr, clip, x, y, pr, ma, mb, grad);
     }
 }
 
@@ -456,19 +542,28 @@ dim3 tile_grid(const AaDims& d) {
 }  // namespace
 
 void aa_face_setup(const AaDims& d, const float* clip, const float* faces,
-                   AaFace* out, uint32_t* status, cudaStream_t s) {
-    if (d.n_faces == 0) return;
+                   AaFace* out, int* view_flags, uint32_t* status,
+                   cudaStream_t s) {
     ProfScope ps("aa_face_setup", s);
+    DRESSI_CUDA(cudaMemsetAsync(view_flags, 0, sizeof(int) * d.views, s));
+    if (d.n_faces == 0) return;
     k_aa_face_setup<<<dim3((d.n_faces + 127) / 128, d.views), 128, 0, s>>>(
-            d, reinterpret_cast<const float4*>(clip), faces, out, status);
+            d, reinterpret_cast<const float4*>(clip), faces, out, view_flags,
+            status);
     check_launch();
 }
 
-void aa_forward_op(const AaDims& d, const AaFace* fr, const float* img,
-                   const float* tri, float* out, cudaStream_t s) {
+void aa_forward_op(const AaDims& d, const AaFace* fr, const int* view_flags,
+                   const float* img, const float* tri, float* out,
+                   cudaStream_t s) {
     ProfScope ps("aa_forward", s);
-    k_aa_forward<EpiAaOut><<<tile_grid(d), 256, 0, s>>>(d, fr, img, tri,
-                                                        EpiAaOut{out});
+    const EpiAaOut epi{out};
+    switch (d.n_comp) {
+    case 1: k_aa_forward<EpiAaOut, 1><<<tile_grid(d), 256, 0, s>>>(d, fr, img, tri, view_flags, epi); break;
+    case 2: k_aa_forward<EpiAaOut, 2><<<tile_grid(d), 256, 0, s>>>(d, fr, img, tri, view_flags, epi); break;
+    case 3: k_aa_forward<EpiAaOut, 3><<<tile_grid(d), 256, 0, s>>>(d, fr, img, tri, view_flags, epi); break;
+    default: k_aa_forward<EpiAaOut, 4><<<tile_grid(d), 256, 0, s>>>(d, fr, img, tri, view_flags, epi); break;
+    }
     check_launch();
 }
 
@@ -554,11 +649,13 @@ static void aa_sil_render(const SilParams& p, const AaSilBuffers& b,
     d.n_faces = p.n_faces;
     d.n_verts = p.n_verts;
     d.n_comp = 1;
-    aa_face_setup(d, b.sil.clip, b.sil.faces, b.frs, b.status, s);
+    aa_face_setup(d, b.sil.clip, b.sil.faces, b.frs, b.view_flags, b.status,
+                  s);
     {
         ProfScope ps("aa_forward", s);
-        k_aa_forward<Epi><<<tile_grid(d), 256, 0, s>>>(d, b.frs, b.mask,
-                                                       b.tri, epi);
+        k_aa_forward<Epi, 1><<<tile_grid(d), 256, 0, s>>>(d, b.frs, b.mask,
+                                                          b.tri, b.view_flags,
+                                                          epi);
     }
     check_launch();
 }

@@ -408,11 +408,13 @@ int dressi_antialias(const float* img, uint32_t n_comp, const float* tri,
         DRESSI_REQUIRE(img && out, "null pointer");
         cudaStream_t s = as_stream(stream);
         const AaDims d = aa_dims(n_comp, n_verts, n_faces, views, width, height);
-        AsyncScratch fr(size_t(views) * std::max<uint32_t>(n_faces, 1) *
-                                sizeof(AaFace), s);
+        const size_t rec_bytes = size_t(views) * std::max<uint32_t>(n_faces, 1) *
+                                 sizeof(AaFace);
+        AsyncScratch fr(rec_bytes + sizeof(int) * views, s);
         AaFace* recs = static_cast<AaFace*>(fr.p);
-        aa_face_setup(d, clip, faces, recs, status, s);
-        aa_forward_op(d, recs, img, tri, out, s);
+        int* vflags = reinterpret_cast<int*>(static_cast<char*>(fr.p) + rec_bytes);
+        aa_face_setup(d, clip, faces, recs, vflags, status, s);
+        aa_forward_op(d, recs, vflags, img, tri, out, s);
     });
 }
 
@@ -435,10 +437,12 @@ int dressi_antialias_grad(const float* gy, const float* img, uint32_t n_comp,
                        "-> face table");
         cudaStream_t s = as_stream(stream);
         const AaDims d = aa_dims(n_comp, n_verts, n_faces, views, width, height);
-        AsyncScratch fr(size_t(views) * std::max<uint32_t>(n_faces, 1) *
-                                sizeof(AaFace), s);
+        const size_t rec_bytes = size_t(views) * std::max<uint32_t>(n_faces, 1) *
+                                 sizeof(AaFace);
+        AsyncScratch fr(rec_bytes + sizeof(int) * views, s);
         AaFace* recs = static_cast<AaFace*>(fr.p);
-        aa_face_setup(d, clip, faces, recs, status, s);
+        int* vflags = reinterpret_cast<int*>(static_cast<char*>(fr.p) + rec_bytes);
+        aa_face_setup(d, clip, faces, recs, vflags, status, s);
         if (grad_img) aa_bwd_img_op(d, recs, gy, tri, grad_img, s);
         if (grad_clip)
             aa_bwd_vtx_op(d, recs, gy, img, tri, clip, vft, int(max_deg),
@@ -590,6 +594,7 @@ int dressi_aa_silhouette_plan_create(const dressi_aa_silhouette_desc* desc,
             ab.mask = a.take<float>(NV * R2);
             ab.gy = a.take<float>(NV * R2);
             ab.frs = a.take<AaFace>(NV * F);
+            ab.view_flags = a.take<int>(NV);
             ab.status = a.take<uint32_t>(4);
             ab.hard_ws = a.take<char>(ws);
         };

@@ -16,7 +16,7 @@ namespace dressi {
 
 struct __align__(16) HardRec {
     float x0, y0, x1, y1;   // screen px
-    float x2, y2, inv_area, pad;
+    float x2, y2, inv_area, zlb;  // zlb: lower bound of every fragment depth
     float z0, z1, z2, pad2;  // NDC depth
     float iw0, iw1, iw2, pad3;  // 1 / clip.w
     int bx0, bx1, by0, by1;  // pixel range (inclusive)
@@ -103,7 +103,16 @@ __global__ void k_hard_setup(HardDims d, const float4* clip,
             r.inv_area = 1.f / area;
             r.z0 = sz[0]; r.z1 = sz[1]; r.z2 = sz[2];
             r.iw0 = iw[0]; r.iw1 = iw[1]; r.iw2 = iw[2];
-            r.pad = r.pad2 = r.pad3 = 0.f;
+            r.pad2 = r.pad3 = 0.f;
+            // A covered pixel has computed l_k >= 0 whose sum is within
+            // 3u of 1 (u = 2^-24; l2 = 1 - l0 - l1 takes two roundings), so
+            // sum(l_k z_k) >= zmin - 3u max|z_k|, and evaluating it takes 5
+            // more roundings (<= 5u (1 + 3u) max|z_k|): the fragment depth is
+            // at least zmin - 8u max|z_k|; 1e-6 (~16.8u) covers it.
+            const float zmin = std_min(std_min(sz[0], sz[1]), sz[2]);
+            const float zabs = fmaxf(fmaxf(fabsf(sz[0]), fabsf(sz[1])), fabsf(sz[2]));
+            r.zlb = zmin - 1e-6f * zabs;
+            if (!(r.zlb == r.zlb)) r.zlb = -INFINITY;  // NaN: never skipped
             bbox_range(std_min(std_min(sx[0], sx[1]), sx[2]),
                        std_max(std_max(sx[0], sx[1]), sx[2]), d.W, &r.bx0,
                        &r.bx1);
@@ -150,6 +159,13 @@ __device__ __forceinline__ void hard_bary(const HardRec& r, float px, float py,
 }
 
 constexpr int kHardChunk = 128;
+static_assert(kHardChunk <= kSortMax, "a chunk must fit the sort buffer");
+
+// Order-preserving key of a float (ascending floats -> ascending keys).
+__device__ __forceinline__ unsigned long long zlb_key(float z) {
+    const uint32_t u = __float_as_uint(z);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
 
 // attr == nullptr: writes float(face)+1 / 0 into out[v][H][W].
 // Otherwise writes the perspective-correct attribute (n_comp channels).
@@ -157,10 +173,15 @@ __global__ void __launch_bounds__(kTileThreads)
         k_hard_sweep(HardDims d, HardBuffers b, const float* attr, float* out,
                      float* depth_out, float* id_out) {
     __shared__ HardRec sh[kHardChunk];
+    __shared__ int fid_sh[kHardChunk];
+    __shared__ unsigned long long order[kSortMax];  // (zlb key, record index)
+    __shared__ unsigned char wlist[8][kHardChunk];  // per-warp sorted faces
     const int v = blockIdx.y, tile = blockIdx.x;
     const int tx = tile % d.tiles_x, ty = tile / d.tiles_x;
-    const int x = tx * kTile + (threadIdx.x % kTile);
-    const int y = ty * kTile + (threadIdx.x / kTile);
+    int x, y;
+    tile_xy(tile, d.tiles_x, &x, &y);  // 8 warps of 8x4 pixels
+    const int w = threadIdx.x >> 5;
+    const int wx0 = tx * kTile + (w & 1) * 8, wy0 = ty * kTile + (w >> 1) * 4;
     const bool in = x < d.W && y < d.H;
     const float px = float(x) + 0.5f, py = float(y) + 0.5f;
     const HardRec* recs = b.recs + size_t(v) * d.n_faces;
@@ -177,22 +198,64 @@ __global__ void __launch_bounds__(kTileThreads)
         const float4* src = reinterpret_cast<const float4*>(recs);
         float4* dst = reinterpret_cast<float4*>(sh);
         for (int i = threadIdx.x; i < n * kHardVec4; i += blockDim.x) {
-            const int j = i / kHardVec4, w = i % kHardVec4;
+            const int j = i / kHardVec4, q = i % kHardVec4;
             const int f = identity ? base + j : list[base + j];
-            dst[i] = src[size_t(f) * kHardVec4 + w];
+            dst[i] = src[size_t(f) * kHardVec4 + q];
+            if (q == 0) fid_sh[j] = f;
         }
         __syncthreads();
-        if (!in) continue;
-        for (int i = 0; i < n; i++) {
+        // front to back by the depth lower bound
+        if (n <= 32) {
+            if (threadIdx.x < 32) {
+                const int lane = threadIdx.x;
+                unsigned long long k =
+                        lane < n ? (zlb_key(sh[lane].zlb) << 32) | unsigned(lane)
+                                 : ~0ull;
+                k = warp_sort_asc(k);
+                order[lane] = k;
+            }
+        } else {
+            for (int j = threadIdx.x; j < n; j += blockDim.x)
+                order[j] = (zlb_key(sh[j].zlb) << 32) | unsigned(j);
+            block_sort_asc(order, n);
+        }
+        __syncthreads();
+        // this warp's list: the valid faces whose pixel range meets its 8x4
+        // block, kept in front-to-back order
+        const int lane = threadIdx.x & 31;
+        int cnt = 0;
+        for (int o0 = 0; o0 < n; o0 += 32) {
+            const int o = o0 + lane;
+            int j = 0;
+            bool hit = false;
+            if (o < n) {
+                j = int(uint32_t(order[o]));
+                const HardRec& r = sh[j];
+                hit = (r.flags & kFaceValid) && !(r.bx1 < wx0 || r.bx0 > wx0 + 7 ||
+                                                  r.by1 < wy0 || r.by0 > wy0 + 3);
+            }
+            const unsigned m = __ballot_sync(0xffffffffu, hit);
+            if (hit) wlist[w][cnt + __popc(m & ((1u << lane) - 1u))] = (unsigned char)j;
+            cnt += __popc(m);
+        }
+        __syncwarp();
+        for (int t = 0; t < cnt; t++) {
+            const int i = wlist[w][t];
             const HardRec& r = sh[i];
-            if (!(r.flags & kFaceValid)) continue;
+            // the warp leaves the chunk once every pixel holds a survivor in
+            // front of this face (and so of all later ones)
+            if (__all_sync(0xffffffffu, !in || (best_f >= 0 && best_z < r.zlb)))
+                break;
+            if (!in) continue;
             if (x < r.bx0 || x > r.bx1 || y < r.by0 || y > r.by1) continue;
+            // every fragment of this face lies behind the survivor (no tie)
+            if (best_f >= 0 && r.zlb > best_z) continue;
             float l0, l1, l2;
             hard_bary(r, px, py, &l0, &l1, &l2);
             if (l0 < 0.f || l1 < 0.f || l2 < 0.f) continue;
             const float z = l0 * r.z0 + l1 * r.z1 + l2 * r.z2;
             if (z < 0.f || z > 1.f) continue;
-            const int f = identity ? base + i : list[base + i];
+            const int f = fid_sh[i];
             if (beats(z, f, best_z, best_f)) {
                 best_z = z;
                 best_f = f;

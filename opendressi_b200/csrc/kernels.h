@@ -225,12 +225,15 @@ static_assert(sizeof(AaFace) == 64, "AaFace layout");
 struct AaDims {
     int W = 0, H = 0, views = 1, n_faces = 0, n_verts = 0, n_comp = 1;
 };
-// clip [views][V][4], faces [F][3] -> out [views][F].
+// clip [views][V][4], faces [F][3] -> out [views][F]; view_flags
+// [views] (zeroed here) marks views with wild screen coordinates.
 void aa_face_setup(const AaDims& d, const float* clip, const float* faces,
-                   AaFace* out, uint32_t* status, cudaStream_t s);
+                   AaFace* out, int* view_flags, uint32_t* status,
+                   cudaStream_t s);
 // img / out [views][H][W][n_comp], tri [views][H][W] (face id + 1).
-void aa_forward_op(const AaDims& d, const AaFace* fr, const float* img,
-                   const float* tri, float* out, cudaStream_t s);
+void aa_forward_op(const AaDims& d, const AaFace* fr, const int* view_flags,
+                   const float* img, const float* tri, float* out,
+                   cudaStream_t s);
 void aa_bwd_img_op(const AaDims& d, const AaFace* fr, const float* gy,
                    const float* tri, float* out, cudaStream_t s);
 // grad [views][V][4] += d(sum gy * aa)/d clip; n_samples 0 = exact scan,
@@ -249,6 +252,7 @@ struct AaSilBuffers {
     float* mask;        // [views][R][R] Rasterize(clip, ones)
     float* gy;          // [views][R][R] dL / d pred
     AaFace* frs;        // [views][F]
+    int* view_flags;    // [views]
     void* hard_ws;      // hard raster workspace (aa_sil_workspace_bytes)
     uint32_t* status;   // [4]
 };

@@ -657,6 +657,25 @@ __device__ __forceinline__ void bin_sweep1(const FaceRec& r, int f,
         }
 }
 
+// Ascending bitonic sort of one key per lane across a full warp.
+__device__ __forceinline__ unsigned long long warp_sort_asc(
+        unsigned long long k) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, j);
+            const bool up = (lane & size) == 0;
+            const bool lower = (lane & j) == 0;
+            const unsigned long long lo = k < o ? k : o;
+            const unsigned long long hi = k < o ? o : k;
+            k = (lower == up) ? lo : hi;
+        }
+    }
+    return k;
+}
+
 // Block-wide ascending bitonic sort of n <= kSortMax 64-bit keys in shared
 // memory (padded with ~0).
 __device__ __forceinline__ void block_sort_asc(unsigned long long* k, int n) {

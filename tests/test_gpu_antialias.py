@@ -137,3 +137,24 @@ def test_antialias_index_error(cuda):
     with pytest.raises(DressiError):
         ops.antialias(torch.zeros((16, 16), device=cuda), tri,
                       T(clip, cuda), T(bad, cuda))
+
+
+@pytest.mark.parametrize("wild", [False, True])
+def test_antialias_mask_matches_port(cuda, port, wild):
+    """0/1 masks take the equal-value shortcut; a view with a face whose
+    screen coordinates are huge turns it off. Bit-exact either way."""
+    from opendressi_b200 import ops
+
+    w, h = 70, 50
+    clip, faces = S.random_triangles(77, 80, max(w, h), spread=1.0,
+                                     w_range=(0.5, 2.0))
+    if wild:
+        clip[0, 0] = 1e30 * clip[0, 3]
+    nv = clip.shape[0]
+    mask = port.rasterize_hard(clip, np.ones(nv, np.float32), faces, w,
+                               h)[..., 0]
+    tri = port.rasterize_face_id(clip, faces, w, h)
+    out = ops.antialias(T(mask, cuda), T(tri, cuda), T(clip, cuda),
+                        T(faces, cuda))
+    assert_bitexact(npy(out), port.antialias(mask, tri, clip, faces),
+                    "AntiAlias mask")
