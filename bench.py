@@ -220,6 +220,7 @@ def run_ours(args):
 
     from opendressi_b200 import _native as N
     from opendressi_b200 import scene
+    from opendressi_b200.distributed import ShardedStep, shard_views
     from opendressi_b200.plans import AaSilhouettePlan, SilhouettePlan
 
     world, rank, local = dist_env()
@@ -233,7 +234,7 @@ def run_ours(args):
 
     sc = scene.silhouette_scene(level=args.level, n_views=args.views,
                                 res=args.res, seed=args.seed)
-    shard = np.array_split(np.arange(args.views), world)[rank]
+    shard = shard_views(args.views, world, rank)
     if args.config == "c4":
         plan = AaSilhouettePlan.from_scene(sc, views=shard, device=local,
                                            n_samples=args.samples)
@@ -243,17 +244,13 @@ def run_ours(args):
     plan.render_targets(sc.target_pos)
     stream = torch.cuda.current_stream()
 
-    if world > 1:
-        grad = plan.grad_tensor()
-        loss_t = plan.loss_tensor()
+    sharded = ShardedStep(plan) if world > 1 else None
 
     def step():
         if world == 1:
-            plan.step(1)
+            plan.step(1)  # the fused iteration, one CUDA-graph replay
         else:
-            plan.forward_backward()
-            dist.all_reduce(grad)
-            plan.apply_update()
+            sharded()
 
     def sync_all():
         torch.cuda.synchronize()
@@ -281,9 +278,7 @@ def run_ours(args):
     ms_max = float(ms_t.item())
 
     # loss of the last iteration (all ranks' views)
-    if world > 1:
-        dist.all_reduce(loss_t)
-    loss = float(plan.loss())
+    loss = sharded.loss() if world > 1 else float(plan.loss())
 
     # ---- end to end through the public API with host buffers ----------
     e2e = None

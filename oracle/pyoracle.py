@@ -162,6 +162,16 @@ class Port(_Lib):
             _u32(n_iters), _u32(threads), _fp(trace)), "silhouette_run")
         return trace, pos
 
+    def adam(self, param, m, v, t, grad, lr, b1=0.9, b2=0.999, eps=1e-8):
+        """One in-graph Adam step in place (orc_adam); returns the new t."""
+        for a in (param, m, v, grad):
+            assert a.dtype == np.float32 and a.flags.c_contiguous
+        tt = C.c_float(t)
+        self.lib.orc_adam(_fp(param), _fp(m), _fp(v), C.byref(tt), _fp(grad),
+                          _u32(param.size), C.c_float(lr), C.c_float(b1),
+                          C.c_float(b2), C.c_float(eps))
+        return tt.value
+
     def image_fit_run(self, param, target, lr, n_iters):
         param = _f32(param).copy()
         target = _f32(target)
