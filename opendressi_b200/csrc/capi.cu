@@ -133,6 +133,8 @@ struct dressi_plan_s {
         DRESSI_CUDA(cudaMemset(b.soft.bin1.spill_n, 0, sizeof(int)));
         DRESSI_CUDA(cudaMemset(b.soft.bin1.parked_n, 0, sizeof(int)));
         DRESSI_CUDA(cudaMemset(b.soft.bin2.spill_n, 0, sizeof(int)));
+        DRESSI_CUDA(cudaMemset(b.soft.bin2.open_n, 0, sizeof(int)));
+        DRESSI_CUDA(cudaMemset(b.soft.bin2.take, 0, sizeof(int)));
     }
 
     // Reactive growth: a bin set that overflowed in the last replayed

@@ -89,7 +89,7 @@ void launch_sweeps(const SoftDims& d, const SoftBuffers& b,
                  sm = size_t(d.rim_cells);
     {
         ProfScope ps("sweep1", s);
-        k_sweep1<Epi><<<grid, kTileThreads, 0, s>>>(a, b.bin1, b.state,
+        k_sweep1<Epi><<<grid, kTileThreads, 0, s>>>(a, b.bin1, b.bin2, b.state,
                                                     b.active, sr, sp, sm, epi);
     }
     DRESSI_CUDA(cudaGetLastError());
@@ -97,14 +97,14 @@ void launch_sweeps(const SoftDims& d, const SoftBuffers& b,
         // tiles whose bins overflowed into the spill list (usually none)
         ProfScope ps("sweep1_spill", s);
         k_sweep1_spill<Epi><<<kSpillBlocks, kTileThreads, 0, s>>>(
-                a, b.bin1, b.state, b.active, sr, sp, sm, epi);
+                a, b.bin1, b.bin2, b.state, b.active, sr, sp, sm, epi);
     }
     DRESSI_CUDA(cudaGetLastError());
     soft_rim_bins(d, b, s);
     {
         ProfScope ps("rim", s);
-        k_rim<Epi><<<grid, kTileThreads, 0, s>>>(a, b.bin2, b.state, b.active,
-                                                 sr, sp, sm, epi);
+        k_rim<Epi><<<kRimCtas, kTileThreads, 0, s>>>(a, b.bin2, b.state, sr,
+                                                     sp, sm, epi);
     }
     DRESSI_CUDA(cudaGetLastError());
 }

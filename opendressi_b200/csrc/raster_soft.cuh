@@ -541,6 +541,11 @@ struct FixedBins {
     int* spill_n;     // [1] appends past the capacity (all bins)
     int2* spill;      // [spill_cap] (global bin, face)
     int spill_cap;
+    // work list of the rim phase: the open 8x4 blocks (global tile * 8 +
+    // block), appended by sweep 1, taken by the rim warps through `take`
+    int* open_n;      // [1]
+    int* open;        // [views * tiles * 8]
+    int* take;        // [1]
 };
 
 // Sweep-1 bins: 64-bit entries, high word = a lower bound of the depth of
@@ -773,7 +778,7 @@ __device__ __forceinline__ void sweep1_finish(const SweepArgs& a, size_t bin,
                                               int x, int y, bool in,
                                               const Survivor& s, int2* state,
                                               int* mask_out, int* warp_open,
-                                              Epi& epi) {
+                                              const FixedBins& b2, Epi& epi) {
     const int w = threadIdx.x >> 5;
     const int cell = (y / kRimCell) * a.rim_cells_x + (x / kRimCell);
     const unsigned ob = __ballot_sync(0xffffffffu, in && s.depth > 0.5f &&
@@ -783,12 +788,14 @@ __device__ __forceinline__ void sweep1_finish(const SweepArgs& a, size_t bin,
     int m = 0;
 #pragma unroll
     for (int k = 0; k < 8; k++) m |= warp_open[k] << k;
-    if (m == 0) {
-        if (threadIdx.x == 0) mask_out[bin] = 0;
-        epi(a, x, y, in, s);
-    } else {
-        if (threadIdx.x == 0) mask_out[bin] = m;
+    if (threadIdx.x == 0) mask_out[bin] = m;
+    if ((m >> w) & 1) {
+        // open block: survivors stored, the block queued for the rim phase
         if (in) state[size_t(a.v) * a.W * a.H + size_t(y) * a.W + x] = pack(s);
+        if ((threadIdx.x & 31) == 0)
+            b2.open[atomicAdd(b2.open_n, 1)] = int(bin) * 8 + w;
+    } else {
+        epi(a, x, y, in, s);
     }
 }
 
@@ -802,8 +809,8 @@ __device__ __forceinline__ void sweep1_finish(const SweepArgs& a, size_t bin,
 // no spill code: compiled in, it slowed the common path).
 template <class Epi>
 static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
-                                   int tile, int2* state, int* mask_out,
-                                   Epi& epi) {
+                                   const FixedBins& b2, int tile, int2* state,
+                                   int* mask_out, Epi& epi) {
     __shared__ FaceRec sh[kRecChunk];
     __shared__ unsigned long long keys[kSortMax];
     __shared__ int warp_open[8];
@@ -924,7 +931,15 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
         epi(a, x, y, in, s);
     } else {
         if (threadIdx.x == 0) mask_out[bin] = m;
-        if (in) state[size_t(a.v) * a.W * a.H + pix] = pack(s);
+        if ((m >> w) & 1) {
+            // open block (or a parked tile): survivors stored; an open block
+            // of an unparked tile is queued for the rim phase
+            if (in) state[size_t(a.v) * a.W * a.H + pix] = pack(s);
+            if (!over && (threadIdx.x & 31) == 0)
+                b2.open[atomicAdd(b2.open_n, 1)] = int(bin) * 8 + w;
+        } else {
+            epi(a, x, y, in, s);
+        }
     }
 }
 
@@ -1005,16 +1020,12 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
 // coverage test (in list order this costs ~ln(n) tests, as for a running
 // maximum).
 template <class Epi>
-static __device__ void rim_tile(const SweepArgs& a, FixedBins b2, int tile,
-                                const int2* state, const int* mask,
-                                Epi& epi) {
-    __shared__ FaceRec recs_sh[8][kRimChunk];
-    __shared__ int ids_sh[8][kRimChunk];
-    const size_t tbin = size_t(a.v) * a.n_tiles + tile;
-    const int m = mask[tbin];
-    if (m == 0) return;  // finished in sweep 1
-    int x, y;
-    tile_xy(tile, a.tiles_x, &x, &y);
+static __device__ void rim_block(const SweepArgs& a, FixedBins b2, int tile,
+                                 int w, const int2* state, FaceRec* recs_w,
+                                 int* ids_w, Epi& epi) {
+    const int lane = threadIdx.x & 31;
+    const int x = (tile % a.tiles_x) * kTile + (w & 1) * 8 + (lane & 7);
+    const int y = (tile / a.tiles_x) * kTile + (w >> 1) * 4 + (lane >> 3);
     const bool in = x < a.W && y < a.H;
     const float px = float(x) + 0.5f, py = float(y) + 0.5f;
     const size_t pix = size_t(y) * a.W + x;
@@ -1023,95 +1034,93 @@ static __device__ void rim_tile(const SweepArgs& a, FixedBins b2, int tile,
     Survivor s{1.f, -1, false};
     if (in) s = unpack(state[size_t(a.v) * a.W * a.H + pix]);
     const bool open = in && s.depth > 0.5f;
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if ((m >> w) & 1) {
-        const int bx = (tile % a.tiles_x) * 2 + (w & 1);
-        const int by = (tile / a.tiles_x) * 4 + (w >> 1);
-        const size_t bin = size_t(a.v) * a.n_tiles * 8 +
-                           size_t(by) * (a.tiles_x * 2) + bx;
-        int n = 0, ns = 0;
-        if (lane == 0) {
-            n = b2.cursor[bin];
-            b2.cursor[bin] = 0;  // ready for the next use
-            if (n > b2.cap) ns = *b2.spill_n;
+    const int bx = (tile % a.tiles_x) * 2 + (w & 1);
+    const int by = (tile / a.tiles_x) * 4 + (w >> 1);
+    const size_t bin = size_t(a.v) * a.n_tiles * 8 +
+                       size_t(by) * (a.tiles_x * 2) + bx;
+    int n = 0, ns = 0;
+    if (lane == 0) {
+        n = b2.cursor[bin];
+        b2.cursor[bin] = 0;  // ready for the next use
+        if (n > b2.cap) ns = *b2.spill_n;
+    }
+    n = __shfl_sync(0xffffffffu, n, 0);
+    ns = __shfl_sync(0xffffffffu, ns, 0);
+    const bool over = n > b2.cap;  // the rest of the list is spilled
+    const bool identity = over && ns > b2.spill_cap;  // spill lost
+    if (over && lane == 0) {
+        atomicOr(&a.status[0], kStatusBinOverflow);  // sticky report
+        atomicOr(&a.status[1], 2u);  // this iteration: grow the rim bins
+    }
+    const int end = identity ? a.n_faces : (over ? b2.cap : n);
+    const int* lst = b2.list + bin * b2.cap;
+    const float4* src = reinterpret_cast<const float4*>(a.recs);
+    // Stages the records of ids_w[0..cn) and folds their fragments.
+    auto run = [&](int cn) {
+        __syncwarp();
+        float4* dst = reinterpret_cast<float4*>(recs_w);
+        for (int i = lane; i < cn * kRecVec4; i += 32) {
+            const int j = i / kRecVec4, q = i % kRecVec4;
+            dst[i] = src[size_t(ids_w[j]) * kRecVec4 + q];
         }
-        n = __shfl_sync(0xffffffffu, n, 0);
-        ns = __shfl_sync(0xffffffffu, ns, 0);
-        const bool over = n > b2.cap;  // the rest of the list is spilled
-        const bool identity = over && ns > b2.spill_cap;  // spill lost
-        if (over && lane == 0) {
-            atomicOr(&a.status[0], kStatusBinOverflow);  // sticky report
-            atomicOr(&a.status[1], 2u);  // this iteration: grow the rim bins
+        __syncwarp();
+        if (!open) return;
+        for (int j = 0; j < cn; j++) {
+            const int f = ids_w[j];
+            const FaceRec& r = recs_w[j];
+            const uint32_t need = kFaceValid | kFaceSafe;
+            if ((r.flags & need) != need) continue;
+            if (x < r.bx0 || x > r.bx1 || y < r.by0 || y > r.by1) continue;
+            const float lb = rim_depth_lb(px, py, r, a.radius);
+            if (lb > s.depth) continue;
+            if (lb == 1.f && f < s.face) continue;  // 1.0 tie, older face
+            if (!soft_covers(px, py, r)) continue;
+            if (lb == 1.f) {
+                // |dist| >= radius: the Eq.3 depth is exactly 1
+                if (peel && 1.f <= prev + 1e-4f) continue;
+                fold(s, 1.f, f, false);
+            } else {
+                eval_full(s, px, py, r, f, a.radius, peel, prev);
+            }
         }
-        const int end = identity ? a.n_faces : (over ? b2.cap : n);
-        const int* lst = b2.list + bin * b2.cap;
-        const float4* src = reinterpret_cast<const float4*>(a.recs);
-        // Stages the records of ids_sh[w][0..cn) and folds their fragments.
-        auto run = [&](int cn) {
+    };
+    for (int base = 0; base < end; base += kRimChunk) {
+        const int cn = imin_(kRimChunk, end - base);
+        __syncwarp();
+        if (lane < cn)
+            ids_w[lane] = identity ? a.n_faces - 1 - (base + lane)
+                                   : lst[base + lane];
+        run(cn);
+    }
+    if (over && !identity) {
+        // this block's spilled entries, kRimChunk scanned per step
+        for (int sb = 0; sb < ns; sb += kRimChunk) {
+            const int i = sb + lane;
+            int2 e = make_int2(-1, 0);
+            if (lane < kRimChunk && i < ns) e = b2.spill[i];
+            const bool match = e.x == int(bin);
+            const unsigned mm = __ballot_sync(0xffffffffu, match);
+            if (mm == 0u) continue;
             __syncwarp();
-            float4* dst = reinterpret_cast<float4*>(recs_sh[w]);
-            for (int i = lane; i < cn * kRecVec4; i += 32) {
-                const int j = i / kRecVec4, q = i % kRecVec4;
-                dst[i] = src[size_t(ids_sh[w][j]) * kRecVec4 + q];
-            }
-            __syncwarp();
-            if (!open) return;
-            for (int j = 0; j < cn; j++) {
-                const int f = ids_sh[w][j];
-                const FaceRec& r = recs_sh[w][j];
-                const uint32_t need = kFaceValid | kFaceSafe;
-                if ((r.flags & need) != need) continue;
-                if (x < r.bx0 || x > r.bx1 || y < r.by0 || y > r.by1) continue;
-                const float lb = rim_depth_lb(px, py, r, a.radius);
-                if (lb > s.depth) continue;
-                if (lb == 1.f && f < s.face) continue;  // 1.0 tie, older face
-                if (!soft_covers(px, py, r)) continue;
-                if (lb == 1.f) {
-                    // |dist| >= radius: the Eq.3 depth is exactly 1
-                    if (peel && 1.f <= prev + 1e-4f) continue;
-                    fold(s, 1.f, f, false);
-                } else {
-                    eval_full(s, px, py, r, f, a.radius, peel, prev);
-                }
-            }
-        };
-        for (int base = 0; base < end; base += kRimChunk) {
-            const int cn = imin_(kRimChunk, end - base);
-            __syncwarp();
-            if (lane < cn)
-                ids_sh[w][lane] = identity ? a.n_faces - 1 - (base + lane)
-                                           : lst[base + lane];
-            run(cn);
-        }
-        if (over && !identity) {
-            // this block's spilled entries, kRimChunk scanned per step
-            for (int sb = 0; sb < ns; sb += kRimChunk) {
-                const int i = sb + lane;
-                int2 e = make_int2(-1, 0);
-                if (lane < kRimChunk && i < ns) e = b2.spill[i];
-                const bool match = e.x == int(bin);
-                const unsigned mm = __ballot_sync(0xffffffffu, match);
-                if (mm == 0u) continue;
-                __syncwarp();
-                if (match) ids_sh[w][__popc(mm & ((1u << lane) - 1u))] = e.y;
-                run(__popc(mm));
-            }
+            if (match) ids_w[__popc(mm & ((1u << lane) - 1u))] = e.y;
+            run(__popc(mm));
         }
     }
     epi(a, x, y, in, s);
+    __syncwarp();  // recs_w / ids_w reuse by the warp's next block
 }
 
 template <class Epi>
 __global__ void __launch_bounds__(kTileThreads)
-        k_sweep1(SweepArgs a0, FixedBins1 b1, int2* state, int* mask,
-                 size_t view_stride_recs, size_t view_stride_px,
+        k_sweep1(SweepArgs a0, FixedBins1 b1, FixedBins b2, int2* state,
+                 int* mask, size_t view_stride_recs, size_t view_stride_px,
                  size_t view_stride_rim, Epi epi) {
     SweepArgs a = a0;
     a.v = blockIdx.y;
     a.recs = a0.recs + a.v * view_stride_recs;
     a.rim = a0.rim + a.v * view_stride_rim;
     if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
-    sweep1_tile(a, b1, blockIdx.x, state, mask, epi);
+    sweep1_tile(a, b1, b2, blockIdx.x, state, mask, epi);
 }
 
 // Finishes the sweep-1 tiles whose bins overflowed into the spill list:
@@ -1120,9 +1129,10 @@ __global__ void __launch_bounds__(kTileThreads)
 // of any size strides over the parked tiles (none: every block exits).
 template <class Epi>
 __global__ void __launch_bounds__(kTileThreads)
-        k_sweep1_spill(SweepArgs a0, FixedBins1 b1, int2* state, int* mask,
-                       size_t view_stride_recs, size_t view_stride_px,
-                       size_t view_stride_rim, Epi epi) {
+        k_sweep1_spill(SweepArgs a0, FixedBins1 b1, FixedBins b2, int2* state,
+                       int* mask, size_t view_stride_recs,
+                       size_t view_stride_px, size_t view_stride_rim,
+                       Epi epi) {
     __shared__ FaceRec sh[kRecChunk];
     __shared__ unsigned long long keys[kSortMax];
     __shared__ int warp_open[8];
@@ -1149,23 +1159,41 @@ __global__ void __launch_bounds__(kTileThreads)
         if (in) s = unpack(state[size_t(a.v) * a.W * a.H + pix]);
         sweep1_spilled(a, b1, bin, ns, all_faces, x, y, in, peel, prev,
                        a.radius < kMaxFastRadius, sh, keys, &n_match, s);
-        sweep1_finish(a, size_t(bin), x, y, in, s, state, mask, warp_open, epi);
+        sweep1_finish(a, size_t(bin), x, y, in, s, state, mask, warp_open, b2,
+                      epi);
         __syncthreads();  // warp_open / sh reuse by the next parked tile
     }
 }
 
+// The rim phase: persistent warps take the open 8x4 blocks queued by sweep
+// 1 from the work list (an atomic cursor balances blocks of very different
+// cost), so every resident warp has work.
 template <class Epi>
 __global__ void __launch_bounds__(kTileThreads)
-        k_rim(SweepArgs a0, FixedBins b2, const int2* state, const int* mask,
+        k_rim(SweepArgs a0, FixedBins b2, const int2* state,
               size_t view_stride_recs, size_t view_stride_px,
               size_t view_stride_rim, Epi epi) {
-    SweepArgs a = a0;
-    a.v = blockIdx.y;
-    a.recs = a0.recs + a.v * view_stride_recs;
-    a.rim = a0.rim + a.v * view_stride_rim;
-    if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
-    rim_tile(a, b2, blockIdx.x, state, mask, epi);
+    __shared__ FaceRec recs_sh[8][kRimChunk];
+    __shared__ int ids_sh[8][kRimChunk];
+    const int wc = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_open = *b2.open_n;
+    for (;;) {
+        int item = 0;
+        if (lane == 0) item = atomicAdd(b2.take, 1);
+        item = __shfl_sync(0xffffffffu, item, 0);
+        if (item >= n_open) break;
+        const int e = b2.open[item];
+        const int tbin = e >> 3, w = e & 7;
+        SweepArgs a = a0;
+        a.v = tbin / a0.n_tiles;
+        const int tile = tbin - a.v * a0.n_tiles;
+        a.recs = a0.recs + a.v * view_stride_recs;
+        a.rim = a0.rim + a.v * view_stride_rim;
+        if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
+        rim_block(a, b2, tile, w, state, recs_sh[wc], ids_sh[wc], epi);
+    }
 }
+constexpr int kRimCtas = 148 * 4;  // persistent grid of k_rim
 
 // Marks the rim-flag cells a safe face's soft bbox reaches: a superset of
 // where the rim phase can find fragments (those outside the sweep-1 region

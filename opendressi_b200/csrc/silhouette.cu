@@ -80,8 +80,12 @@ __global__ void k_transform(const float* pos, const float* mvps, int n_verts,
 // face_id = f; examples/silhouette_optimization/run.cpp:456-466).
 __global__ void k_face_setup_sil(SoftDims d, const float4* clip,
                                  const float* faces, SoftBuffers b) {
-    // the previous rim phase has consumed the rim spill list
-    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *b.bin2.spill_n = 0;
+    // the previous rim phase has consumed the rim spill list and work list
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+        *b.bin2.spill_n = 0;
+        *b.bin2.open_n = 0;
+        *b.bin2.take = 0;
+    }
     const int f = blockIdx.x * blockDim.x + threadIdx.x;
     const int v = blockIdx.y;
     if (f >= d.n_faces) return;

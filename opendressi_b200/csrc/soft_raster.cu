@@ -64,6 +64,9 @@ void carve_soft_bins(Arena& a, const SoftDims& d, SoftBuffers* b) {
     b->bin2.spill_cap = d.spill2;
     b->bin2.spill_n = a.take<int>(1);
     b->bin2.spill = a.take<int2>(std::max(d.spill2, 1));
+    b->bin2.open_n = a.take<int>(1);
+    b->bin2.take = a.take<int>(1);
+    b->bin2.open = a.take<int>(std::max<size_t>(vb, 1));
 }
 
 void carve_soft(Arena& a, const SoftDims& d, SoftBuffers* b) {
@@ -78,6 +81,8 @@ void init_soft(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
     DRESSI_CUDA(cudaMemsetAsync(b.bin1.spill_n, 0, sizeof(int), s));
     DRESSI_CUDA(cudaMemsetAsync(b.bin1.parked_n, 0, sizeof(int), s));
     DRESSI_CUDA(cudaMemsetAsync(b.bin2.spill_n, 0, sizeof(int), s));
+    DRESSI_CUDA(cudaMemsetAsync(b.bin2.open_n, 0, sizeof(int), s));
+    DRESSI_CUDA(cudaMemsetAsync(b.bin2.take, 0, sizeof(int), s));
     DRESSI_CUDA(cudaMemsetAsync(b.status, 0, 4 * sizeof(uint32_t), s));
     DRESSI_CUDA(cudaMemsetAsync(b.rim, 0,
                                 size_t(d.views) * d.rim_cells * sizeof(int), s));
@@ -88,8 +93,12 @@ void init_soft(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
 // Op-level face setup: explicit soft clip / face ids / faces
 // (RasterizeSoftCpu's per-face prologue, cpu_raster.cpp:260-298).
 __global__ void k_face_setup_op(SoftDims d, SoftOpInputs in, SoftBuffers b) {
-    // the previous rim phase has consumed the rim spill list
-    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *b.bin2.spill_n = 0;
+    // the previous rim phase has consumed the rim spill list and work list
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+        *b.bin2.spill_n = 0;
+        *b.bin2.open_n = 0;
+        *b.bin2.take = 0;
+    }
     const int f = blockIdx.x * blockDim.x + threadIdx.x;
     const int v = blockIdx.y;
     if (f >= d.n_faces) return;
