@@ -161,6 +161,25 @@ int dressi_antialias_grad(const float* gy, const float* img, uint32_t n_comp,
                           float* grad_img, float* grad_clip, uint32_t* status,
                           void* stream);
 
+/* F::Texture (filter 0: nearest, the reference's clamp-to-edge nearest
+ * sampler, f_ops.cpp:2605-2639) / F::TextureBilinear (filter 1: BilerpClamp,
+ * f_ops.cpp:2736-2780, bit-exact): tex [th][tw][n_comp] (n_comp 1..4)
+ * sampled at uv [n_px][2] -> out [n_px][n_comp]. */
+int dressi_texture(const float* tex, uint32_t tw, uint32_t th,
+                   uint32_t n_comp, const float* uv, uint32_t n_px,
+                   uint32_t filter, float* out, void* stream);
+
+/* The texture gradient of dressi_texture through the inverse-UV table:
+ * filter 0 GatherByInverseUV (restated from glsl_codegen.cpp:658-709),
+ * filter 1 GatherByInverseUVBilinear (f_ops.cpp:2650-2732, bit-exact).
+ * gy [sh][sw][n_comp], inv_uv [th][tw][4] (Rasterize(UvAsClip(uv),
+ * ScreenAttr(clip)), mesh_utils.cpp:180-203), uv_screen [sh][sw][2] ->
+ * grad_tex [th][tw][n_comp] (written). */
+int dressi_texture_grad(const float* gy, uint32_t sw, uint32_t sh,
+                        uint32_t n_comp, const float* inv_uv, uint32_t tw,
+                        uint32_t th, const float* uv_screen, uint32_t filter,
+                        float* grad_tex, void* stream);
+
 /* ------------------------------------------------------------------------
  * Plans: one fused fwd + bwd + Adam iteration, resident on one device,
  * replayed as a CUDA graph with no per-iteration host traffic
@@ -224,6 +243,32 @@ typedef struct {
 
 int dressi_aa_silhouette_plan_create(const dressi_aa_silhouette_desc* desc,
                                      dressi_plan* out);
+
+/* Texture optimisation (config C2): a fixed UV-mapped mesh seen from
+ * n_views cameras; per view the G-buffer (uv, mask) = Rasterize(clip,
+ * (u, v, 1)), pred = mask * trilinear(mips(tex), uv) with `levels` box-
+ * filtered mip levels and a per-pixel lod from the uv differences, loss =
+ * sum_v Mean((target - pred)^2); Adam on the [tex_size][tex_size][3]
+ * texture (PARAM slot). The mip path has no counterpart in the reference
+ * (which samples one level); its definition is in oracle.c. Targets:
+ * dressi_plan_render_targets with the target TEXTURE (host
+ * [tex_size][tex_size][3]). */
+typedef struct {
+    uint32_t struct_size;  /* sizeof(dressi_texture_desc) */
+    uint32_t n_verts, n_faces, n_views, res;
+    uint32_t tex_size;     /* square, power of two */
+    uint32_t levels;       /* mip levels (1 = level 0 only) */
+    float lr, beta1, beta2, eps;
+    const float* pos;      /* host [n_verts][3] */
+    const float* uv;       /* host [n_verts][2] */
+    const float* faces;    /* host [n_faces][3] */
+    const float* mvps;     /* host [n_views][16], column-major */
+    uint32_t loss_history; /* ring capacity (0 -> 4096) */
+    int device;
+} dressi_texture_desc;
+
+int dressi_texture_plan_create(const dressi_texture_desc* desc,
+                               dressi_plan* out);
 
 /* 2-D image fitting (config C1): loss = Mean((param - target)^2) over a
  * [h][w][4] image, Adam(lr, 0.9, 0.999, 1e-8) on param. */

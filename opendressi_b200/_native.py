@@ -56,6 +56,20 @@ class AaSilhouetteDesc(C.Structure):
     ]
 
 
+class TextureDesc(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("n_verts", C.c_uint32), ("n_faces", C.c_uint32),
+        ("n_views", C.c_uint32), ("res", C.c_uint32),
+        ("tex_size", C.c_uint32), ("levels", C.c_uint32),
+        ("lr", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float),
+        ("eps", C.c_float),
+        ("pos", _fp), ("uv", _fp), ("faces", _fp), ("mvps", _fp),
+        ("loss_history", C.c_uint32),
+        ("device", C.c_int),
+    ]
+
+
 # name -> (restype, argtypes); exactly the functions include/dressi_b200.h
 # declares.
 SIGNATURES = {
@@ -86,6 +100,12 @@ SIGNATURES = {
                                                 C.POINTER(_vp)]),
     "dressi_aa_silhouette_plan_create": (C.c_int, [C.POINTER(AaSilhouetteDesc),
                                                    C.POINTER(_vp)]),
+    "dressi_texture": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _u32, _u32, _vp,
+                                 _vp]),
+    "dressi_texture_grad": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _u32, _u32,
+                                      _vp, _u32, _vp, _vp]),
+    "dressi_texture_plan_create": (C.c_int, [C.POINTER(TextureDesc),
+                                             C.POINTER(_vp)]),
     "dressi_image_fit_plan_create": (C.c_int, [_u32, _u32, C.c_float, C.c_int,
                                                C.POINTER(_vp)]),
     "dressi_plan_upload": (C.c_int, [_vp, C.c_int, _vp, C.c_size_t, C.c_int,

@@ -94,7 +94,7 @@ struct AsyncScratch {
 using namespace dressi;
 
 struct dressi_plan_s {
-    enum Kind { kSil, kFit, kAa } kind = kSil;
+    enum Kind { kSil, kFit, kAa, kTex } kind = kSil;
     int device = 0;
     void* mem = nullptr;
     size_t mem_bytes = 0;
@@ -107,6 +107,9 @@ struct dressi_plan_s {
     SilParams p{};
     SilBuffers b{};
     AaSilBuffers ab{};  // AA plans (ab.sil aliases b)
+    // texture plans
+    TexParams tp{};
+    TexBuffers tb{};
     // image fit
     size_t n = 0;
     float lr = 0.f;
@@ -180,6 +183,8 @@ struct dressi_plan_s {
                                             cudaMemcpyDeviceToHost, s));
         } else if (kind == kAa) {
             aa_sil_iteration(p, ab, s);
+        } else if (kind == kTex) {
+            tex_iteration(tp, tb, s);
         } else {
             fit_iteration(n, lr, fb, s);
         }
@@ -627,6 +632,145 @@ int dressi_aa_silhouette_plan_create(const dressi_aa_silhouette_desc* desc,
     });
 }
 
+int dressi_texture(const float* tex, uint32_t tw, uint32_t th,
+                   uint32_t n_comp, const float* uv, uint32_t n_px,
+                   uint32_t filter, float* out, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(tex && uv && out, "null pointer");
+        DRESSI_REQUIRE(tw >= 1 && th >= 1, "Texture: empty texture");
+        DRESSI_REQUIRE(n_comp >= 1 && n_comp <= 4,
+                       "Texture: texture must have 1..4 components");
+        DRESSI_REQUIRE(filter <= 1, "Texture: filter is 0 (nearest) or 1 "
+                                    "(bilinear)");
+        texture_sample_op(tex, int(tw), int(th), int(n_comp), int(filter), uv,
+                          n_px, out, as_stream(stream));
+    });
+}
+
+int dressi_texture_grad(const float* gy, uint32_t sw, uint32_t sh,
+                        uint32_t n_comp, const float* inv_uv, uint32_t tw,
+                        uint32_t th, const float* uv_screen, uint32_t filter,
+                        float* grad_tex, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(gy && inv_uv && uv_screen && grad_tex, "null pointer");
+        DRESSI_REQUIRE(tw >= 1 && th >= 1 && sw >= 1 && sh >= 1,
+                       "Texture grad: empty texture or screen");
+        DRESSI_REQUIRE(n_comp >= 1 && n_comp <= 4,
+                       "Texture grad: 1..4 components");
+        DRESSI_REQUIRE(filter <= 1, "Texture grad: filter is 0 or 1");
+        texture_gather_op(gy, int(sw), int(sh), int(n_comp), int(filter),
+                          inv_uv, int(tw), int(th), uv_screen, grad_tex,
+                          as_stream(stream));
+    });
+}
+
+int dressi_texture_plan_create(const dressi_texture_desc* desc,
+                               dressi_plan* out) {
+    return guarded([&] {
+        DRESSI_REQUIRE(desc && out, "null pointer");
+        DRESSI_REQUIRE(desc->struct_size == sizeof(dressi_texture_desc),
+                       "dressi_texture_desc: struct_size mismatch");
+        DRESSI_REQUIRE(desc->n_verts > 0 && desc->n_faces > 0 &&
+                               desc->n_views > 0 && desc->res > 0,
+                       "texture plan: empty mesh, views or screen");
+        DRESSI_REQUIRE(desc->res <= 32768, "texture plan: res > 32768");
+        const uint32_t w = desc->tex_size;
+        DRESSI_REQUIRE(w >= 1 && (w & (w - 1)) == 0 && w <= 16384,
+                       "texture plan: tex_size must be a power of two <= 16384");
+        DRESSI_REQUIRE(desc->levels >= 1 && (w >> (desc->levels - 1)) >= 1,
+                       "texture plan: more mip levels than the texture has");
+        DRESSI_REQUIRE(desc->pos && desc->uv && desc->faces && desc->mvps,
+                       "null pointer");
+        *out = nullptr;
+        DeviceGuard dg(desc->device);
+        auto pl = std::make_unique<dressi_plan_s>();
+        pl->kind = dressi_plan_s::kTex;
+        pl->device = desc->device;
+        TexParams& p = pl->tp;
+        p.w_tex = int(w);
+        p.levels = int(desc->levels);
+        p.views = int(desc->n_views);
+        p.res = int(desc->res);
+        p.n_verts = int(desc->n_verts);
+        p.n_faces = int(desc->n_faces);
+        p.lr = desc->lr;
+        p.b1 = desc->beta1;
+        p.b2 = desc->beta2;
+        p.eps = desc->eps;
+        p.inv_n = 1.f / (float(desc->res) * float(desc->res) * 3.f);
+        const int hist = desc->loss_history ? int(desc->loss_history) : 4096;
+        const size_t V = desc->n_verts, F = desc->n_faces, NV = desc->n_views;
+        const size_t R2 = size_t(desc->res) * desc->res;
+        const size_t T0 = size_t(w) * w * 3;
+        const size_t nmip = tex_mip_floats(int(w), p.levels);
+        const size_t ws = tex_workspace_bytes(p);
+        auto carve = [&](Arena& a) {
+            TexBuffers& b = pl->tb;
+            b.pyr = a.take<float>(nmip);
+            b.gpyr = a.take<float>(nmip);
+            b.grad = a.take<float>(T0);
+            b.adam_m = a.take<float>(T0);
+            b.adam_v = a.take<float>(T0);
+            b.scalars = a.take<float>(4);
+            b.clip = a.take<float>(NV * V * 4);
+            b.attr = a.take<float>(V * 3);
+            b.faces = a.take<float>(F * 3);
+            b.gbuf = a.take<float>(NV * R2 * 3);
+            b.targets = a.take<float>(NV * R2 * 3);
+            b.loss_slots = a.take<double>(kLossSlots);
+            b.loss_hist = a.take<float>(size_t(hist));
+            b.hist_cap = hist;
+            b.status = a.take<uint32_t>(4);
+            b.hard_ws = a.take<char>(ws);
+        };
+        Arena dry;
+        carve(dry);
+        pl->mem_bytes = dry.used + 256;
+        DRESSI_CUDA(cudaMalloc(&pl->mem, pl->mem_bytes));
+        Arena a{static_cast<char*>(pl->mem), pl->mem_bytes, 0};
+        carve(a);
+        DRESSI_CUDA(cudaMemset(pl->mem, 0, pl->mem_bytes));
+        // static inputs: faces, the (u, v, 1) attribute, the clip positions
+        std::vector<float> attr(V * 3), clip(NV * V * 4);
+        for (size_t i = 0; i < V; i++) {
+            attr[i * 3 + 0] = desc->uv[i * 2 + 0];
+            attr[i * 3 + 1] = desc->uv[i * 2 + 1];
+            attr[i * 3 + 2] = 1.f;
+        }
+        for (size_t v = 0; v < NV; v++) {
+            const float* m = desc->mvps + v * 16;
+            for (size_t i = 0; i < V; i++) {
+                const float4 c = transform_clip(desc->pos[i * 3 + 0],
+                                                desc->pos[i * 3 + 1],
+                                                desc->pos[i * 3 + 2], m);
+                float* o = &clip[(v * V + i) * 4];
+                o[0] = c.x;
+                o[1] = c.y;
+                o[2] = c.z;
+                o[3] = c.w;
+            }
+        }
+        DRESSI_CUDA(cudaMemcpy(pl->tb.faces, desc->faces, F * 3 * sizeof(float),
+                               cudaMemcpyHostToDevice));
+        DRESSI_CUDA(cudaMemcpy(pl->tb.attr, attr.data(), V * 3 * sizeof(float),
+                               cudaMemcpyHostToDevice));
+        DRESSI_CUDA(cudaMemcpy(pl->tb.clip, clip.data(),
+                               clip.size() * sizeof(float),
+                               cudaMemcpyHostToDevice));
+        pl->set_slot(DRESSI_SLOT_PARAM, pl->tb.pyr, T0 * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_M, pl->tb.adam_m, T0 * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_V, pl->tb.adam_v, T0 * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_T, pl->tb.scalars, 4);
+        pl->set_slot(DRESSI_SLOT_TARGET, pl->tb.targets, NV * R2 * 3 * 4);
+        pl->set_slot(DRESSI_SLOT_GRAD, pl->tb.grad, T0 * 4);
+        pl->set_slot(DRESSI_SLOT_LOSS, pl->tb.scalars + 3, 4);
+        pl->set_slot(DRESSI_SLOT_LOSS_HISTORY, pl->tb.loss_hist, size_t(hist) * 4);
+        pl->set_slot(DRESSI_SLOT_RASTER, nullptr, NV * R2 * 3 * 4);
+        pl->set_slot(DRESSI_SLOT_MVP, nullptr, NV * 16 * 4);
+        *out = pl.release();
+    });
+}
+
 int dressi_image_fit_plan_create(uint32_t width, uint32_t height, float lr,
                                  int device, dressi_plan* out) {
     return guarded([&] {
@@ -731,11 +875,19 @@ int dressi_plan_render_targets(dressi_plan p, const float* target_pos_host,
                                void* stream) {
     return guarded([&] {
         DRESSI_REQUIRE(p && target_pos_host, "null pointer");
-        DRESSI_REQUIRE(p->kind == dressi_plan_s::kSil ||
-                               p->kind == dressi_plan_s::kAa,
-                       "render_targets: not a silhouette plan");
+        DRESSI_REQUIRE(p->kind != dressi_plan_s::kFit,
+                       "render_targets: not a silhouette or texture plan");
         DeviceGuard dg(p->device);
         cudaStream_t s = as_stream(stream);
+        if (p->kind == dressi_plan_s::kTex) {
+            const size_t tb = size_t(p->tp.w_tex) * p->tp.w_tex * 3 * sizeof(float);
+            AsyncScratch gt(tb, s);
+            DRESSI_CUDA(cudaMemcpyAsync(gt.p, target_pos_host, tb,
+                                        cudaMemcpyHostToDevice, s));
+            tex_render_targets(p->tp, p->tb, static_cast<float*>(gt.p), s);
+            DRESSI_CUDA(cudaStreamSynchronize(s));
+            return;
+        }
         const size_t bytes = size_t(p->p.n_verts) * 3 * sizeof(float);
         AsyncScratch tp(bytes, s);
         DRESSI_CUDA(cudaMemcpyAsync(tp.p, target_pos_host, bytes,
@@ -763,12 +915,18 @@ int dressi_plan_exec(dressi_plan p, uint32_t n_iters, void* stream) {
 int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream) {
     return guarded([&] {
         DRESSI_REQUIRE(p, "null plan");
-        DRESSI_REQUIRE(p->kind == dressi_plan_s::kSil ||
-                               p->kind == dressi_plan_s::kAa,
-                       "exec_phase: not a silhouette plan");
+        DRESSI_REQUIRE(p->kind != dressi_plan_s::kFit,
+                       "exec_phase: not a silhouette or texture plan");
         DRESSI_REQUIRE(phase == 0 || phase == 1, "exec_phase: phase is 0 or 1");
         DeviceGuard dg(p->device);
         cudaStream_t s = as_stream(stream);
+        if (p->kind == dressi_plan_s::kTex) {
+            if (phase == 0)
+                tex_forward_backward(p->tp, p->tb, nullptr, s);
+            else
+                tex_update(p->tp, p->tb, s);
+            return;
+        }
         if (p->kind == dressi_plan_s::kAa) {
             if (phase == 0) {
                 aa_sil_forward_backward(p->p, p->ab, s);
@@ -793,13 +951,17 @@ int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream) {
 int dressi_plan_render(dressi_plan p, void* stream) {
     return guarded([&] {
         DRESSI_REQUIRE(p, "null plan");
-        DRESSI_REQUIRE(p->kind == dressi_plan_s::kSil ||
-                               p->kind == dressi_plan_s::kAa,
-                       "render: not a silhouette plan");
+        DRESSI_REQUIRE(p->kind != dressi_plan_s::kFit,
+                       "render: not a silhouette or texture plan");
         DeviceGuard dg(p->device);
         cudaStream_t s = as_stream(stream);
         auto& slot = p->slots[DRESSI_SLOT_RASTER];
         if (!slot.ptr) DRESSI_CUDA(cudaMalloc(&slot.ptr, slot.bytes));
+        if (p->kind == dressi_plan_s::kTex) {
+            tex_predict(p->tp, p->tb, static_cast<float*>(slot.ptr), s);
+            DRESSI_CUDA(cudaStreamSynchronize(s));
+            return;
+        }
         if (p->kind == dressi_plan_s::kAa) {
             aa_sil_predict(p->p, p->ab, static_cast<float*>(slot.ptr), s);
             DRESSI_CUDA(cudaStreamSynchronize(s));
@@ -831,6 +993,9 @@ int dressi_plan_status(dressi_plan p, uint32_t* word, void* stream) {
                                         cudaMemcpyDeviceToHost, s));
         } else if (p->kind == dressi_plan_s::kAa) {
             DRESSI_CUDA(cudaMemcpyAsync(word, p->ab.status, 4,
+                                        cudaMemcpyDeviceToHost, s));
+        } else if (p->kind == dressi_plan_s::kTex) {
+            DRESSI_CUDA(cudaMemcpyAsync(word, p->tb.status, 4,
                                         cudaMemcpyDeviceToHost, s));
         }
         DRESSI_CUDA(cudaStreamSynchronize(s));

@@ -281,7 +281,8 @@ __global__ void __launch_bounds__(kTileThreads)
     const float iw[3] = {r.iw0, r.iw1, r.iw2};
     const uint32_t idx[3] = {r.i0, r.i1, r.i2};
     const float denom = l[0] * iw[0] + l[1] * iw[1] + l[2] * iw[2];
-    const float* av = d.attr_ones ? nullptr : attr + size_t(v) * d.n_verts * d.n_comp;
+    const float* av = d.attr_ones ? nullptr
+                      : attr + (d.attr_shared ? 0 : size_t(v) * d.n_verts * d.n_comp);
     for (int c = 0; c < d.n_comp; c++) {
         float num = 0.f;
         for (int k = 0; k < 3; k++)

@@ -192,6 +192,7 @@ void sil_render_targets(const SoftDims& d, const SilParams& p,
 struct HardDims {
     int W = 0, H = 0, views = 1, n_faces = 0, n_verts = 0, n_comp = 1;
     int attr_ones = 0;  // the attribute is 1 at every vertex (a mask)
+    int attr_shared = 0;  // one attribute array [V][n_comp] for all views
     int tiles_x = 0, tiles_y = 0, n_tiles = 0, cap = 0;
     void finalize() {
         tiles_x = (W + kTile - 1) / kTile;
@@ -268,6 +269,59 @@ void aa_sil_predict(const SilParams& p, const AaSilBuffers& b, float* out,
 // targets = AntiAlias of the target mesh's mask (seed 0, forward only).
 void aa_render_targets(const SilParams& p, const AaSilBuffers& b,
                        const float* target_pos, cudaStream_t s);
+
+// --- texturing: op-level sampling and inverse-UV gathers ---
+// filter: 0 nearest (GLSL texture() of a clamp-to-edge nearest sampler),
+// 1 bilinear (BilerpClamp). tex [th][tw][n]; uv / out per pixel.
+void texture_sample_op(const float* tex, int tw, int th, int n, int filter,
+                       const float* uv, size_t npx, float* out,
+                       cudaStream_t s);
+// GatherByInverseUV (filter 0) / GatherByInverseUVBilinear (1): gy
+// [sh][sw][n], inv_uv [th][tw][4], uv_screen [sh][sw][2] -> out [th][tw][n].
+void texture_gather_op(const float* gy, int sw, int sh, int n, int filter,
+                       const float* inv_uv, int tw, int th,
+                       const float* uv_screen, float* out, cudaStream_t s);
+
+// --- C2 texture optimisation (first principles: box mips, trilinear
+// sampling, exact scatter transpose, Adam on level 0) ---
+struct TexParams {
+    int w_tex, levels, views, res, n_verts, n_faces;
+    float lr, b1, b2, eps;
+    float inv_n;  // 1 / (R * R * 3): the per-view Mean
+};
+struct TexBuffers {
+    float* pyr;       // mip pyramid, level 0 = the optimised texture
+    float* gpyr;      // its gradient (levels > 0 zeroed by the mip build)
+    float* grad;      // d loss / d level 0 [w][w][3]
+    float* adam_m;    // [w][w][3]
+    float* adam_v;
+    float* scalars;   // [0]=t [1]=bc1 [2]=bc2 [3]=last loss
+    float* clip;      // [views][V][4] (static)
+    float* attr;      // [V][3] = (u, v, 1)
+    float* faces;     // [F][3]
+    float* gbuf;      // [views][R][R][3] = (u, v, mask)
+    float* targets;   // [views][R][R][3]
+    double* loss_slots;
+    float* loss_hist;
+    int hist_cap;
+    void* hard_ws;
+    uint32_t* status;
+};
+size_t tex_mip_floats(int w, int levels);
+size_t tex_workspace_bytes(const TexParams& p);
+// Forward + loss + d loss / d level 0 into grad (advances the Adam counter).
+void tex_forward_backward(const TexParams& p, const TexBuffers& b,
+                          float* pred_out, cudaStream_t s);
+// Adam on level 0 from grad (and the loss of the iteration).
+void tex_update(const TexParams& p, const TexBuffers& b, cudaStream_t s);
+void tex_iteration(const TexParams& p, const TexBuffers& b, cudaStream_t s);
+// out [views][R][R][3] = mask * trilinear(mips(texture)) of the current
+// texture (no gradient, counter unchanged).
+void tex_predict(const TexParams& p, const TexBuffers& b, float* out,
+                 cudaStream_t s);
+// targets = mask * trilinear(mips(gt_tex)) per view (gt_tex on the device).
+void tex_render_targets(const TexParams& p, const TexBuffers& b,
+                        const float* gt_tex, cudaStream_t s);
 
 // --- image fitting (C1) ---
 struct FitBuffers {

@@ -22,6 +22,8 @@ __all__ = [
     "rasterize",
     "antialias",
     "antialias_grad",
+    "texture",
+    "texture_grad",
     "check_status",
 ]
 
@@ -275,3 +277,39 @@ def antialias_grad(gy, img, tri, clip, faces, vft=None, seed: float = 0.0,
     if gc is not None and squeeze:
         gc = gc[0]
     return gi, gc
+
+
+_FILTERS = {"nearest": 0, "linear": 1, "bilinear": 1}
+
+
+def texture(tex, uv, filter_mode: str = "nearest"):
+    """F::Texture (nearest) / F::TextureBilinear ("linear"): tex [H, W, C]
+    (C 1..4) sampled at uv [..., 2] -> [..., C]."""
+    tex = _dev(tex, "tex", 3)
+    uv = _dev(uv, "uv")
+    if uv.shape[-1] != 2:
+        raise N.DressiError(N.ERR_INVALID, "uv must end with 2 components")
+    n = tex.shape[2]
+    out = torch.empty(uv.shape[:-1] + (n,), dtype=torch.float32,
+                      device=tex.device)
+    N.call("dressi_texture", tex.data_ptr(), tex.shape[1], tex.shape[0], n,
+           uv.data_ptr(), uv.numel() // 2, _FILTERS[filter_mode],
+           out.data_ptr(), _stream())
+    return out
+
+
+def texture_grad(gy, inv_uv, uv_screen, filter_mode: str = "nearest"):
+    """The texture gradient of `texture` through the inverse-UV table
+    (GatherByInverseUV / GatherByInverseUVBilinear): gy [H, W, C], inv_uv
+    [TH, TW, 4], uv_screen [H, W, 2] -> [TH, TW, C]."""
+    gy = _dev(gy, "gy", 3)
+    inv_uv = _dev(inv_uv, "inv_uv", 3)
+    uv_screen = _dev(uv_screen, "uv_screen", 3)
+    n = gy.shape[2]
+    out = torch.empty((inv_uv.shape[0], inv_uv.shape[1], n),
+                      dtype=torch.float32, device=gy.device)
+    N.call("dressi_texture_grad", gy.data_ptr(), gy.shape[1], gy.shape[0], n,
+           inv_uv.data_ptr(), inv_uv.shape[1], inv_uv.shape[0],
+           uv_screen.data_ptr(), _FILTERS[filter_mode], out.data_ptr(),
+           _stream())
+    return out

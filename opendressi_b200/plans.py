@@ -21,7 +21,8 @@ import torch
 
 from . import _native as N
 
-__all__ = ["Plan", "SilhouettePlan", "AaSilhouettePlan", "ImageFitPlan"]
+__all__ = ["Plan", "SilhouettePlan", "AaSilhouettePlan", "TexturePlan",
+           "ImageFitPlan"]
 
 
 def _stream_ptr(stream=None):
@@ -241,6 +242,71 @@ class AaSilhouettePlan(SilhouettePlan):
         N.call("dressi_plan_render", self._h, _stream_ptr(stream))
         return self.slot_tensor(N.SLOT_RASTER,
                                 (self.n_views, self.res, self.res)).clone()
+
+
+class TexturePlan(Plan):
+    """C2 texture optimisation: trilinear sampling of a box-filtered mip
+    pyramid of the optimised texture on a fixed UV-mapped mesh, per-view
+    Mean L2 loss, Adam on the texture."""
+
+    def __init__(self, pos, uv, faces, mvps, res: int, tex_size: int,
+                 levels: int, lr: float = 1e-2, beta1: float = 0.9,
+                 beta2: float = 0.999, eps: float = 1e-8, device: int = 0,
+                 loss_history: int = 4096):
+        pos = np.ascontiguousarray(pos, np.float32).reshape(-1, 3)
+        uv = np.ascontiguousarray(uv, np.float32).reshape(-1, 2)
+        faces = np.ascontiguousarray(faces, np.float32).reshape(-1, 3)
+        mvps = np.ascontiguousarray(mvps, np.float32).reshape(-1, 16)
+        self.n_views, self.res = mvps.shape[0], int(res)
+        self.tex_size, self.levels = int(tex_size), int(levels)
+        d = N.TextureDesc()
+        d.struct_size = C.sizeof(N.TextureDesc)
+        d.n_verts, d.n_faces = pos.shape[0], faces.shape[0]
+        d.n_views, d.res = self.n_views, self.res
+        d.tex_size, d.levels = self.tex_size, self.levels
+        d.lr, d.beta1, d.beta2, d.eps = lr, beta1, beta2, eps
+        fp = C.POINTER(C.c_float)
+        d.pos = pos.ctypes.data_as(fp)
+        d.uv = uv.ctypes.data_as(fp)
+        d.faces = faces.ctypes.data_as(fp)
+        d.mvps = mvps.ctypes.data_as(fp)
+        d.loss_history = loss_history
+        d.device = device
+        h = C.c_void_p(0)
+        N.call("dressi_texture_plan_create", C.byref(d), C.byref(h))
+        super().__init__(h, device)
+
+    @classmethod
+    def from_scene(cls, scene, device: int = 0, views=None, **kw):
+        mvps = scene.mvps if views is None else scene.mvps[views]
+        kw.setdefault("lr", scene.lr)
+        return cls(scene.pos, scene.uv, scene.faces_f, mvps, scene.res,
+                   scene.tex_size, scene.levels, device=device, **kw)
+
+    def render_targets(self, target_tex, stream=None):
+        """Targets = the renders of `target_tex` [T, T, 3] (host)."""
+        tt = np.ascontiguousarray(target_tex, np.float32)
+        N.call("dressi_plan_render_targets", self._h,
+               tt.ctypes.data_as(C.POINTER(C.c_float)), _stream_ptr(stream))
+
+    def render(self, stream=None) -> torch.Tensor:
+        """Renders of the current texture [views, R, R, 3]."""
+        N.call("dressi_plan_render", self._h, _stream_ptr(stream))
+        return self.slot_tensor(N.SLOT_RASTER,
+                                (self.n_views, self.res, self.res, 3)).clone()
+
+    def forward_backward(self, stream=None):
+        N.call("dressi_plan_exec_phase", self._h, 0, _stream_ptr(stream))
+
+    def apply_update(self, stream=None):
+        N.call("dressi_plan_exec_phase", self._h, 1, _stream_ptr(stream))
+
+    def grad_tensor(self) -> torch.Tensor:
+        return self.slot_tensor(N.SLOT_GRAD,
+                                (self.tex_size, self.tex_size, 3))
+
+    def loss_tensor(self) -> torch.Tensor:
+        return self.slot_tensor(N.SLOT_LOSS, (1,))
 
 
 class ImageFitPlan(Plan):

@@ -259,3 +259,68 @@ def silhouette_scene(level: int = 5, n_views: int = 16, res: int = 1024,
     mvps = orbit_cameras(n_views, seed=seed + 2)
     return SilhouetteScene(pos, target, faces, mvps, res, sigma,
                            silhouette_radius_px(res, sigma), lr)
+
+
+# ------------------------------------------------------------------ C2
+
+def sphere_uv(pos: np.ndarray) -> np.ndarray:
+    """Spherical uv of unit-sphere positions: (atan2(z, x) / 2pi + 0.5,
+    acos(y) / pi). Triangles across the u seam interpolate through the whole
+    texture (the config's spherical mapping has no seam split)."""
+    p = pos / np.linalg.norm(pos, axis=1, keepdims=True)
+    u = np.arctan2(p[:, 2], p[:, 0]) / (2.0 * math.pi) + 0.5
+    v = np.arccos(np.clip(p[:, 1], -1.0, 1.0)) / math.pi
+    return np.stack([u, v], 1).astype(np.float32)
+
+
+def checker_texture(seed: int, size: int = 1024, cells: int = 32) -> np.ndarray:
+    """Seeded cells x cells checkerboard with a random RGB per cell, float32
+    [size, size, 3]."""
+    rng = np.random.default_rng(seed)
+    colors = rng.random((cells, cells, 3)).astype(np.float32)
+    idx = (np.arange(size) * cells) // size
+    return np.ascontiguousarray(colors[idx[:, None], idx[None, :]])
+
+
+class TextureScene:
+    """C2 texture optimisation: a UV-mapped icosphere rendered from seeded
+    orbit cameras; the optimised texture starts at 0.5."""
+
+    def __init__(self, pos, faces, uv, mvps, res, tex_size, levels, gt_tex,
+                 lr):
+        self.pos = pos
+        self.faces = faces
+        self.faces_f = faces.astype(np.float32)
+        self.uv = uv
+        self.mvps = mvps
+        self.res = res
+        self.tex_size = tex_size
+        self.levels = levels
+        self.gt_tex = gt_tex
+        self.tex0 = np.full((tex_size, tex_size, 3), 0.5, np.float32)
+        self.lr = lr
+
+    @property
+    def n_verts(self):
+        return self.pos.shape[0]
+
+    @property
+    def n_faces(self):
+        return self.faces.shape[0]
+
+    @property
+    def n_views(self):
+        return self.mvps.shape[0]
+
+
+def texture_scene(level: int = 4, n_views: int = 8, res: int = 512,
+                  tex_size: int = 1024, levels: int = 10, seed: int = 0,
+                  lr: float = 1e-2) -> TextureScene:
+    """Config C2: icosphere-4 (2562 v / 5120 f) with spherical uv, 8 seeded
+    cameras on a radius-3 orbit (fov 45 deg) at 512^2, a 1024^2 x 3 texture
+    with 10 mip levels (1024 .. 2), a seeded 32x32 checkerboard target,
+    Adam lr 1e-2."""
+    pos, faces = icosphere(level)
+    return TextureScene(pos.astype(np.float32), faces, sphere_uv(pos),
+                        orbit_cameras(n_views, seed), res, tex_size, levels,
+                        checker_texture(seed + 1, tex_size), lr)

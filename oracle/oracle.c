@@ -1224,6 +1224,463 @@ int orc_aa_silhouette_run(float* pos, uint32_t n_verts, const float* faces,
     return rc;
 }
 
+/* ---------------------------------------------------------- texturing */
+
+static inline int iclamp(int x, int lo, int hi) {
+    return x < lo ? lo : (x > hi ? hi : x);
+}
+
+/* BilerpClamp (ibl_math.h:91-115): 4-tap, clamp-to-edge */
+static void bilerp_clamp(const float* data, uint32_t w, uint32_t h,
+                         uint32_t n, float u, float v, float* out) {
+    const float sx = u * (float)w - 0.5f;
+    const float sy = v * (float)h - 0.5f;
+    const int ix = to_i32(floorf(sx));
+    const int iy = to_i32(floorf(sy));
+    const float fx = sx - (float)ix;
+    const float fy = sy - (float)iy;
+    for (uint32_t c = 0; c < n; c++) out[c] = 0.f;
+    for (int dy = 0; dy <= 1; dy++) {
+        for (int dx = 0; dx <= 1; dx++) {
+            const int x = iclamp(ix + dx, 0, (int)w - 1);
+            const int y = iclamp(iy + dy, 0, (int)h - 1);
+            const float wgt = (dx == 0 ? 1.f - fx : fx) * (dy == 0 ? 1.f - fy : fy);
+            const float* p = data + ((size_t)y * w + (size_t)x) * n;
+            for (uint32_t c = 0; c < n; c++) out[c] += wgt * p[c];
+        }
+    }
+}
+
+int orc_texture_bilinear(const float* tex, uint32_t tw, uint32_t th,
+                         uint32_t n, const float* uv, uint32_t npx,
+                         float* out) {
+    if (n < 1 || n > 4) return fail("texture: n_comp 1..4");
+    for (uint32_t p = 0; p < npx; p++)
+        bilerp_clamp(tex, tw, th, n, uv[(size_t)p * 2], uv[(size_t)p * 2 + 1],
+                     out + (size_t)p * n);
+    return 0;
+}
+
+/* The inverse-UV anchor of texel (tx, ty): its table entry, else the first
+ * valid entry of the 9x9 neighbourhood in row order (f_ops.cpp:2681-2702;
+ * glsl_codegen.cpp:674-690). Returns 0 when none is valid. */
+static int inv_uv_anchor(const float* iv_t, int tw, int th, int tx, int ty,
+                         float iv[4]) {
+    const float* iv0 = &iv_t[((size_t)ty * tw + tx) * 4];
+    for (int k = 0; k < 4; k++) iv[k] = iv0[k];
+    for (int ny = -4; ny <= 4 && iv[2] < 0.5f; ny++) {
+        for (int nx = -4; nx <= 4; nx++) {
+            const int px = tx + nx, py = ty + ny;
+            if (px < 0 || py < 0 || px >= tw || py >= th) continue;
+            const float* q = &iv_t[((size_t)py * tw + px) * 4];
+            for (int k = 0; k < 4; k++) iv[k] = q[k];
+            if (iv[2] > 0.5f) break;
+        }
+    }
+    return iv[2] > 0.5f;
+}
+
+/* GatherByInverseUVBilinear (f_ops.cpp:2650-2732) */
+int orc_gather_inv_uv_bilinear(const float* gy, uint32_t sw, uint32_t sh,
+                               uint32_t n, const float* inv_uv, uint32_t tw,
+                               uint32_t th, const float* uv_screen,
+                               float* out) {
+    if (n < 1 || n > 4) return fail("gather: n_comp 1..4");
+    memset(out, 0, sizeof(float) * (size_t)tw * th * n);
+    for (int ty = 0; ty < (int)th; ty++) {
+        for (int tx = 0; tx < (int)tw; tx++) {
+            float iv[4];
+            if (!inv_uv_anchor(inv_uv, (int)tw, (int)th, tx, ty, iv)) continue;
+            const int scx = to_i32(iv[0]), scy = to_i32(iv[1]);
+            float* o = &out[((size_t)ty * tw + tx) * n];
+            for (int dy = -3; dy <= 3; dy++) {
+                for (int dx = -3; dx <= 3; dx++) {
+                    const int spx = scx + dx, spy = scy + dy;
+                    if (spx < 0 || spy < 0 || spx >= (int)sw || spy >= (int)sh)
+                        continue;
+                    const float* suv = &uv_screen[((size_t)spy * sw + spx) * 2];
+                    const float stx = suv[0] * (float)tw - 0.5f;
+                    const float sty = suv[1] * (float)th - 0.5f;
+                    const float w = smax(0.f, 1.f - fabsf(stx - (float)tx)) *
+                                    smax(0.f, 1.f - fabsf(sty - (float)ty));
+                    if (w > 0.f) {
+                        const float* g = &gy[((size_t)spy * sw + spx) * n];
+                        for (uint32_t c = 0; c < n; c++) o[c] += g[c] * w;
+                    }
+                }
+            }
+        }
+    }
+    return 0;
+}
+
+/* Nearest texture() of a clamp-to-edge nearest sampler (the reference's
+ * Texture on its Vulkan path, f_ops.cpp:2605-2639, executor.cpp:193-202):
+ * texel (clamp(floor(u*W)), clamp(floor(v*H))). Restated from the GLSL /
+ * Vulkan sampling rules; the reference has no CPU kernel for it. */
+int orc_texture_nearest(const float* tex, uint32_t tw, uint32_t th,
+                        uint32_t n, const float* uv, uint32_t npx,
+                        float* out) {
+    if (n < 1 || n > 4) return fail("texture: n_comp 1..4");
+    for (uint32_t p = 0; p < npx; p++) {
+        const int x = iclamp(to_i32(floorf(uv[(size_t)p * 2] * (float)tw)), 0,
+                             (int)tw - 1);
+        const int y = iclamp(to_i32(floorf(uv[(size_t)p * 2 + 1] * (float)th)),
+                             0, (int)th - 1);
+        const float* q = tex + ((size_t)y * tw + x) * n;
+        for (uint32_t c = 0; c < n; c++) out[(size_t)p * n + c] = q[c];
+    }
+    return 0;
+}
+
+/* GatherByInverseUV, restated from its GLSL (glsl_codegen.cpp:658-709):
+ * the gradient of the first screen pixel of the anchor's 7x7 window (row
+ * order) whose uv truncates to this texel. */
+int orc_gather_inv_uv(const float* gy, uint32_t sw, uint32_t sh, uint32_t n,
+                      const float* inv_uv, uint32_t tw, uint32_t th,
+                      const float* uv_screen, float* out) {
+    if (n < 1 || n > 4) return fail("gather: n_comp 1..4");
+    memset(out, 0, sizeof(float) * (size_t)tw * th * n);
+    for (int ty = 0; ty < (int)th; ty++) {
+        for (int tx = 0; tx < (int)tw; tx++) {
+            float iv[4];
+            if (!inv_uv_anchor(inv_uv, (int)tw, (int)th, tx, ty, iv)) continue;
+            const int scx = to_i32(iv[0]), scy = to_i32(iv[1]);
+            float* o = &out[((size_t)ty * tw + tx) * n];
+            int found = 0;
+            for (int dy = -3; dy <= 3 && !found; dy++) {
+                for (int dx = -3; dx <= 3; dx++) {
+                    const int spx = scx + dx, spy = scy + dy;
+                    if (spx < 0 || spy < 0 || spx >= (int)sw || spy >= (int)sh)
+                        continue;
+                    const float* suv = &uv_screen[((size_t)spy * sw + spx) * 2];
+                    const int stx = to_i32(suv[0] * (float)tw);
+                    const int sty = to_i32(suv[1] * (float)th);
+                    if (stx == tx && sty == ty) {
+                        const float* g = &gy[((size_t)spy * sw + spx) * n];
+                        for (uint32_t c = 0; c < n; c++) o[c] = g[c];
+                        found = 1;
+                        break;
+                    }
+                }
+            }
+        }
+    }
+    return 0;
+}
+
+/* UvAsClip / ScreenAttr (mesh_utils.cpp:180-203): the inverse-UV table is
+ * Rasterize(UvAsClip(uv), ScreenAttr(clip), faces, tex_size). */
+void orc_uv_as_clip(const float* uv, uint32_t n_verts, float* out) {
+    for (uint32_t i = 0; i < n_verts; i++) {
+        out[i * 4 + 0] = uv[i * 2 + 0] * 2.f - 1.f;
+        out[i * 4 + 1] = uv[i * 2 + 1] * 2.f - 1.f;
+        out[i * 4 + 2] = 0.5f;
+        out[i * 4 + 3] = 1.f;
+    }
+}
+
+void orc_screen_attr(const float* clip, uint32_t n_verts, uint32_t sw,
+                     uint32_t sh, float* out) {
+    for (uint32_t i = 0; i < n_verts; i++) {
+        const float w = clip[i * 4 + 3];
+        const float ndc_x = clip[i * 4 + 0] / w;
+        const float ndc_y = clip[i * 4 + 1] / w;
+        out[i * 4 + 0] = (ndc_x * 0.5f + 0.5f) * (float)sw;
+        out[i * 4 + 1] = (ndc_y * 0.5f + 0.5f) * (float)sh;
+        out[i * 4 + 2] = 1.f;
+        out[i * 4 + 3] = 0.f;
+    }
+}
+
+/* ---- C2: mip pyramid, trilinear sampling, exact transpose -------------
+ * No reference implementation (the reference samples one level); defined
+ * here from first principles and documented as such:
+ *  - level l+1 texel = 0.25 * (((a + b) + c) + d) of its 2x2 children
+ *    (row-major order), square power-of-two textures;
+ *  - per pixel, rho = max(|d uv/dx|, |d uv/dy|) in level-0 texels from the
+ *    G-buffer's forward differences (backward at the right / bottom edge or
+ *    next to background; 0 when neither neighbour is covered);
+ *  - lod = e + (m - 1) for rho = m * 2^e, m in [1, 2) (piecewise-linear
+ *    log2, exact in float), clamped to [0, levels - 1];
+ *  - trilinear = (1 - f) * bilerp(level l) + f * bilerp(level l + 1). */
+
+static inline size_t mip_offset(uint32_t w, uint32_t level, uint32_t n) {
+    size_t off = 0;
+    for (uint32_t l = 0; l < level; l++) {
+        const size_t s = w >> l;
+        off += s * s * n;
+    }
+    return off;
+}
+
+int orc_mip_build(const float* tex0, uint32_t w, uint32_t n, uint32_t levels,
+                  float* pyr) {
+    if ((w & (w - 1)) || (w >> (levels - 1)) < 1) return fail("mip: size");
+    memcpy(pyr, tex0, sizeof(float) * (size_t)w * w * n);
+    for (uint32_t l = 0; l + 1 < levels; l++) {
+        const uint32_t s = w >> l, t = s >> 1;
+        const float* src = pyr + mip_offset(w, l, n);
+        float* dst = pyr + mip_offset(w, l + 1, n);
+        for (uint32_t y = 0; y < t; y++)
+            for (uint32_t x = 0; x < t; x++)
+                for (uint32_t c = 0; c < n; c++) {
+                    const float a = src[((size_t)(2 * y) * s + 2 * x) * n + c];
+                    const float b = src[((size_t)(2 * y) * s + 2 * x + 1) * n + c];
+                    const float cc = src[((size_t)(2 * y + 1) * s + 2 * x) * n + c];
+                    const float d = src[((size_t)(2 * y + 1) * s + 2 * x + 1) * n + c];
+                    dst[((size_t)y * t + x) * n + c] = 0.25f * (((a + b) + cc) + d);
+                }
+    }
+    return 0;
+}
+
+/* lod of a pixel from its level-0 footprint rho (texels per pixel) */
+static inline float lod_of(float rho, uint32_t levels) {
+    if (!(rho > 1.f)) return 0.f;
+    int e;
+    const float m2 = frexpf(rho, &e);      /* rho = m2 * 2^e, m2 in [0.5,1) */
+    const float lod = (float)(e - 1) + (m2 * 2.f - 1.f);
+    const float top = (float)(levels - 1);
+    return lod < top ? lod : top;
+}
+
+/* rho of pixel (x, y): uv [H][W][2], mask [H][W] (>0.5 covered), w_tex =
+ * level-0 size */
+static float pixel_rho(const float* uv, const float* mask, int W, int H,
+                       int x, int y, float w_tex) {
+    float du[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    for (int axis = 0; axis < 2; axis++) {
+        const int ax = axis == 0 ? 1 : 0, ay = axis == 0 ? 0 : 1;
+        const int x1 = x + ax, y1 = y + ay, x0 = x - ax, y0 = y - ay;
+        const float* c = &uv[((size_t)y * W + x) * 2];
+        if (x1 < W && y1 < H && mask[(size_t)y1 * W + x1] > 0.5f) {
+            const float* q = &uv[((size_t)y1 * W + x1) * 2];
+            du[axis][0] = q[0] - c[0];
+            du[axis][1] = q[1] - c[1];
+        } else if (x0 >= 0 && y0 >= 0 && mask[(size_t)y0 * W + x0] > 0.5f) {
+            const float* q = &uv[((size_t)y0 * W + x0) * 2];
+            du[axis][0] = c[0] - q[0];
+            du[axis][1] = c[1] - q[1];
+        }
+    }
+    const float ax_ = du[0][0] * w_tex, ay_ = du[0][1] * w_tex;
+    const float bx_ = du[1][0] * w_tex, by_ = du[1][1] * w_tex;
+    const float rx = sqrtf(ax_ * ax_ + ay_ * ay_);
+    const float ry = sqrtf(bx_ * bx_ + by_ * by_);
+    return smax(rx, ry);
+}
+
+int orc_texture_lod(const float* uv, const float* mask, uint32_t W,
+                    uint32_t H, uint32_t w_tex, uint32_t levels, float* lod) {
+    for (int y = 0; y < (int)H; y++)
+        for (int x = 0; x < (int)W; x++)
+            lod[(size_t)y * W + x] =
+                    mask[(size_t)y * W + x] > 0.5f
+                            ? lod_of(pixel_rho(uv, mask, (int)W, (int)H, x, y,
+                                               (float)w_tex), levels)
+                            : 0.f;
+    return 0;
+}
+
+int orc_texture_trilinear(const float* pyr, uint32_t w, uint32_t n,
+                          uint32_t levels, const float* uv, const float* lod,
+                          uint32_t npx, float* out) {
+    float s0[4], s1[4];
+    for (uint32_t p = 0; p < npx; p++) {
+        const float l = lod[p];
+        const int l0 = to_i32(floorf(l));
+        const float f = l - (float)l0;
+        const float u = uv[(size_t)p * 2], v = uv[(size_t)p * 2 + 1];
+        const uint32_t s = w >> l0;
+        bilerp_clamp(pyr + mip_offset(w, (uint32_t)l0, n), s, s, n, u, v, s0);
+        float* o = out + (size_t)p * n;
+        if (f > 0.f && (uint32_t)l0 + 1 < levels) {
+            bilerp_clamp(pyr + mip_offset(w, (uint32_t)l0 + 1, n), s >> 1,
+                         s >> 1, n, u, v, s1);
+            for (uint32_t c = 0; c < n; c++) o[c] = s0[c] * (1.f - f) + s1[c] * f;
+        } else {
+            for (uint32_t c = 0; c < n; c++) o[c] = s0[c];
+        }
+    }
+    return 0;
+}
+
+/* The bilinear taps of (u, v) on an s x s level: texel indices + weights */
+static void bilerp_taps(uint32_t s, float u, float v, int tx[4], int ty[4],
+                        float tw_[4]) {
+    const float sx = u * (float)s - 0.5f;
+    const float sy = v * (float)s - 0.5f;
+    const int ix = to_i32(floorf(sx));
+    const int iy = to_i32(floorf(sy));
+    const float fx = sx - (float)ix;
+    const float fy = sy - (float)iy;
+    int k = 0;
+    for (int dy = 0; dy <= 1; dy++)
+        for (int dx = 0; dx <= 1; dx++, k++) {
+            tx[k] = iclamp(ix + dx, 0, (int)s - 1);
+            ty[k] = iclamp(iy + dy, 0, (int)s - 1);
+            tw_[k] = (dx == 0 ? 1.f - fx : fx) * (dy == 0 ? 1.f - fy : fy);
+        }
+}
+
+/* Exact transpose of orc_texture_trilinear: adds g [npx][n] into the
+ * pyramid gradient gpyr. */
+int orc_texture_trilinear_grad(const float* g, uint32_t w, uint32_t n,
+                               uint32_t levels, const float* uv,
+                               const float* lod, uint32_t npx, float* gpyr) {
+    for (uint32_t p = 0; p < npx; p++) {
+        const float l = lod[p];
+        const int l0 = to_i32(floorf(l));
+        const float f = l - (float)l0;
+        const float u = uv[(size_t)p * 2], v = uv[(size_t)p * 2 + 1];
+        const int two = f > 0.f && (uint32_t)l0 + 1 < levels;
+        for (int lv = 0; lv < 1 + two; lv++) {
+            const uint32_t level = (uint32_t)l0 + (uint32_t)lv;
+            const float lw = two ? (lv == 0 ? 1.f - f : f) : 1.f;
+            const uint32_t s = w >> level;
+            int tx[4], ty[4];
+            float wt[4];
+            bilerp_taps(s, u, v, tx, ty, wt);
+            float* gl = gpyr + mip_offset(w, level, n);
+            for (int k = 0; k < 4; k++)
+                for (uint32_t c = 0; c < n; c++)
+                    gl[((size_t)ty[k] * s + tx[k]) * n + c] +=
+                            g[(size_t)p * n + c] * lw * wt[k];
+        }
+    }
+    return 0;
+}
+
+/* Transpose of orc_mip_build: level l texel += 0.25 * its parent's
+ * gradient, from the top level down; gpyr level 0 then holds d/d tex0. */
+void orc_mip_fold(float* gpyr, uint32_t w, uint32_t n, uint32_t levels) {
+    for (int l = (int)levels - 2; l >= 0; l--) {
+        const uint32_t s = w >> l, t = s >> 1;
+        float* dst = gpyr + mip_offset(w, (uint32_t)l, n);
+        const float* src = gpyr + mip_offset(w, (uint32_t)l + 1, n);
+        for (uint32_t y = 0; y < s; y++)
+            for (uint32_t x = 0; x < s; x++)
+                for (uint32_t c = 0; c < n; c++)
+                    dst[((size_t)y * s + x) * n + c] +=
+                            0.25f * src[((size_t)(y / 2) * t + x / 2) * n + c];
+    }
+}
+
+size_t orc_mip_floats(uint32_t w, uint32_t n, uint32_t levels) {
+    return mip_offset(w, levels, n);
+}
+
+/* One C2 iteration (first principles on the reference's graph shape,
+ * examples/texture_optimization/run.cpp:115-126 with trilinear sampling):
+ * per view, G-buffer (uv, mask) = Rasterize(clip, (u, v, 1)); pred = mask *
+ * trilinear(mips(tex), uv); loss_v = Mean((target - pred)^2) over W*H*3;
+ * loss = sum_v loss_v; grad = d loss / d tex (level 0). gbuf (nullable)
+ * [views][R][R][3] receives the G-buffers, pred_out (nullable) the
+ * predictions. */
+int orc_c2_loss_grad(const float* tex, uint32_t w_tex, uint32_t levels,
+                     const float* pos, const float* uv_v, uint32_t n_verts,
+                     const float* faces, uint32_t n_faces, const float* mvps,
+                     uint32_t n_views, uint32_t res, const float* targets,
+                     double* loss, float* grad, float* pred_out) {
+    const uint32_t n = 3;
+    const size_t npx = (size_t)res * res;
+    const size_t nmip = orc_mip_floats(w_tex, n, levels);
+    float* pyr = (float*)malloc(sizeof(float) * nmip);
+    float* gpyr = (float*)calloc(nmip, sizeof(float));
+    float* clip = (float*)malloc(sizeof(float) * n_verts * 4);
+    float* attr = (float*)malloc(sizeof(float) * n_verts * 3);
+    float* gb = (float*)malloc(sizeof(float) * npx * 3);
+    float* uv = (float*)malloc(sizeof(float) * npx * 2);
+    float* mask = (float*)malloc(sizeof(float) * npx);
+    float* lod = (float*)malloc(sizeof(float) * npx);
+    float* smp = (float*)malloc(sizeof(float) * npx * n);
+    float* g = (float*)malloc(sizeof(float) * npx * n);
+    int rc = 1;
+    if (!pyr || !gpyr || !clip || !attr || !gb || !uv || !mask || !lod ||
+        !smp || !g) {
+        fail("oom");
+        goto done;
+    }
+    orc_mip_build(tex, w_tex, n, levels, pyr);
+    for (uint32_t i = 0; i < n_verts; i++) {
+        attr[i * 3 + 0] = uv_v[i * 2 + 0];
+        attr[i * 3 + 1] = uv_v[i * 2 + 1];
+        attr[i * 3 + 2] = 1.f;
+    }
+    const float inv_n = 1.f / ((float)res * (float)res * (float)n);
+    double l = 0.0;
+    for (uint32_t v = 0; v < n_views; v++) {
+        orc_transform_clip(pos, n_verts, mvps + (size_t)v * 16, clip);
+        if (orc_rasterize_hard(clip, n_verts, attr, 3, faces, n_faces, res, res,
+                               gb))
+            goto done;
+        for (size_t i = 0; i < npx; i++) {
+            uv[i * 2] = gb[i * 3];
+            uv[i * 2 + 1] = gb[i * 3 + 1];
+            mask[i] = gb[i * 3 + 2];
+        }
+        orc_texture_lod(uv, mask, res, res, w_tex, levels, lod);
+        orc_texture_trilinear(pyr, w_tex, n, levels, uv, lod, (uint32_t)npx, smp);
+        const float* t = targets + (size_t)v * npx * n;
+        for (size_t i = 0; i < npx; i++) {
+            for (uint32_t c = 0; c < n; c++) {
+                const float pred = mask[i] * smp[i * n + c];
+                if (pred_out) pred_out[((size_t)v * npx + i) * n + c] = pred;
+                const float diff = t[i * n + c] - pred;
+                l += (double)(diff * diff * inv_n);
+                const float g_m = 1.f * inv_n;
+                const float g_pred = -(g_m * diff + g_m * diff);
+                g[i * n + c] = g_pred * mask[i];
+            }
+        }
+        orc_texture_trilinear_grad(g, w_tex, n, levels, uv, lod, (uint32_t)npx,
+                                   gpyr);
+    }
+    orc_mip_fold(gpyr, w_tex, n, levels);
+    memcpy(grad, gpyr, sizeof(float) * (size_t)w_tex * w_tex * n);
+    *loss = l;
+    rc = 0;
+done:
+    free(pyr);
+    free(gpyr);
+    free(clip);
+    free(attr);
+    free(gb);
+    free(uv);
+    free(mask);
+    free(lod);
+    free(smp);
+    free(g);
+    return rc;
+}
+
+int orc_c2_run(float* tex, uint32_t w_tex, uint32_t levels, const float* pos,
+               const float* uv_v, uint32_t n_verts, const float* faces,
+               uint32_t n_faces, const float* mvps, uint32_t n_views,
+               uint32_t res, const float* targets, float lr, uint32_t n_iters,
+               float* loss_trace) {
+    const size_t nt = (size_t)w_tex * w_tex * 3;
+    float* m = (float*)calloc(nt, sizeof(float));
+    float* v = (float*)calloc(nt, sizeof(float));
+    float* g = (float*)calloc(nt, sizeof(float));
+    float t = 0.f;
+    int rc = (!m || !v || !g) ? fail("oom") : 0;
+    for (uint32_t it = 0; it < n_iters && !rc; it++) {
+        double l = 0.0;
+        rc = orc_c2_loss_grad(tex, w_tex, levels, pos, uv_v, n_verts, faces,
+                              n_faces, mvps, n_views, res, targets, &l, g,
+                              NULL);
+        if (rc) break;
+        loss_trace[it] = (float)l;
+        orc_adam(tex, m, v, &t, g, (uint32_t)nt, lr, 0.9f, 0.999f, 1e-8f);
+    }
+    free(m);
+    free(v);
+    free(g);
+    return rc;
+}
+
 /* --------------------------------------------------------- image fitting */
 
 /* Sum (f_ops.cpp:1037-1043, the Reduce2x2Sum chain 998-1033) followed by

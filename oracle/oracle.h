@@ -22,6 +22,7 @@
 #ifndef DRESSI_ORACLE_H
 #define DRESSI_ORACLE_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -145,6 +146,58 @@ int orc_aa_silhouette_run(float* pos, uint32_t n_verts, const float* faces,
                           uint32_t n_samples, float lr, const float* mvps,
                           const float* targets, uint32_t n_iters,
                           uint32_t threads, float* loss_trace);
+
+/* F::TextureBilinear forward (f_ops.cpp:2767-2778 over BilerpClamp,
+ * ibl_math.h:91-115): tex [th][tw][n], uv [npx][2] -> out [npx][n]. */
+int orc_texture_bilinear(const float* tex, uint32_t tw, uint32_t th,
+                         uint32_t n, const float* uv, uint32_t npx,
+                         float* out);
+/* GatherByInverseUVBilinear (f_ops.cpp:2650-2732): gy [sh][sw][n], inv_uv
+ * [th][tw][4], uv_screen [sh][sw][2] -> out [th][tw][n]. */
+int orc_gather_inv_uv_bilinear(const float* gy, uint32_t sw, uint32_t sh,
+                               uint32_t n, const float* inv_uv, uint32_t tw,
+                               uint32_t th, const float* uv_screen,
+                               float* out);
+/* Nearest Texture / GatherByInverseUV: restated from the reference's GLSL
+ * and sampler (no CPU kernel there; unpinned by reference outputs). */
+int orc_texture_nearest(const float* tex, uint32_t tw, uint32_t th,
+                        uint32_t n, const float* uv, uint32_t npx,
+                        float* out);
+int orc_gather_inv_uv(const float* gy, uint32_t sw, uint32_t sh, uint32_t n,
+                      const float* inv_uv, uint32_t tw, uint32_t th,
+                      const float* uv_screen, float* out);
+/* UvAsClip / ScreenAttr (mesh_utils.cpp:180-203). */
+void orc_uv_as_clip(const float* uv, uint32_t n_verts, float* out);
+void orc_screen_attr(const float* clip, uint32_t n_verts, uint32_t sw,
+                     uint32_t sh, float* out);
+
+/* C2 texture path, first principles (no reference implementation): box
+ * mip pyramid of a square power-of-two texture (levels concatenated,
+ * orc_mip_floats floats), per-pixel lod from the G-buffer, trilinear
+ * sampling and its exact transpose, and the mip-chain fold. */
+size_t orc_mip_floats(uint32_t w, uint32_t n, uint32_t levels);
+int orc_mip_build(const float* tex0, uint32_t w, uint32_t n, uint32_t levels,
+                  float* pyr);
+int orc_texture_lod(const float* uv, const float* mask, uint32_t W,
+                    uint32_t H, uint32_t w_tex, uint32_t levels, float* lod);
+int orc_texture_trilinear(const float* pyr, uint32_t w, uint32_t n,
+                          uint32_t levels, const float* uv, const float* lod,
+                          uint32_t npx, float* out);
+int orc_texture_trilinear_grad(const float* g, uint32_t w, uint32_t n,
+                               uint32_t levels, const float* uv,
+                               const float* lod, uint32_t npx, float* gpyr);
+void orc_mip_fold(float* gpyr, uint32_t w, uint32_t n, uint32_t levels);
+/* One C2 iteration (loss, d loss / d tex) and a full Adam run. */
+int orc_c2_loss_grad(const float* tex, uint32_t w_tex, uint32_t levels,
+                     const float* pos, const float* uv_v, uint32_t n_verts,
+                     const float* faces, uint32_t n_faces, const float* mvps,
+                     uint32_t n_views, uint32_t res, const float* targets,
+                     double* loss, float* grad, float* pred_out);
+int orc_c2_run(float* tex, uint32_t w_tex, uint32_t levels, const float* pos,
+               const float* uv_v, uint32_t n_verts, const float* faces,
+               uint32_t n_faces, const float* mvps, uint32_t n_views,
+               uint32_t res, const float* targets, float lr, uint32_t n_iters,
+               float* loss_trace);
 
 /* 2-D image fitting (C1): loss = Mean((p - t)^2) over W*H*4, Adam on p.
  * loss_trace[n_iters] = loss at the start of each iteration. */

@@ -260,6 +260,130 @@ class Port(_Lib):
             _u32(n_iters), _u32(threads), _fp(trace)), "aa_silhouette_run")
         return trace, pos
 
+    # ---- texturing
+    def texture_bilinear(self, tex, uv):
+        tex, uv = _f32(tex), _f32(uv)
+        th, tw = tex.shape[:2]
+        n = 1 if tex.ndim == 2 else tex.shape[2]
+        out = np.zeros(uv.shape[:-1] + ((n,) if tex.ndim == 3 else ()),
+                       np.float32)
+        self._err(self.lib.orc_texture_bilinear(
+            _fp(tex), _u32(tw), _u32(th), _u32(n), _fp(uv),
+            _u32(uv.size // 2), _fp(out)), "texture_bilinear")
+        return out
+
+    def texture_nearest(self, tex, uv):
+        tex, uv = _f32(tex), _f32(uv)
+        th, tw = tex.shape[:2]
+        n = 1 if tex.ndim == 2 else tex.shape[2]
+        out = np.zeros(uv.shape[:-1] + ((n,) if tex.ndim == 3 else ()),
+                       np.float32)
+        self._err(self.lib.orc_texture_nearest(
+            _fp(tex), _u32(tw), _u32(th), _u32(n), _fp(uv),
+            _u32(uv.size // 2), _fp(out)), "texture_nearest")
+        return out
+
+    def _gather(self, fn, gy, inv_uv, uv_screen):
+        gy, inv_uv, uv_screen = map(_f32, (gy, inv_uv, uv_screen))
+        sh, sw = uv_screen.shape[:2]
+        th, tw = inv_uv.shape[:2]
+        n = 1 if gy.ndim == 2 else gy.shape[2]
+        out = np.zeros((th, tw) + ((n,) if gy.ndim == 3 else ()), np.float32)
+        self._err(getattr(self.lib, fn)(
+            _fp(gy), _u32(sw), _u32(sh), _u32(n), _fp(inv_uv), _u32(tw),
+            _u32(th), _fp(uv_screen), _fp(out)), fn)
+        return out
+
+    def gather_inv_uv_bilinear(self, gy, inv_uv, uv_screen):
+        return self._gather("orc_gather_inv_uv_bilinear", gy, inv_uv,
+                            uv_screen)
+
+    def gather_inv_uv(self, gy, inv_uv, uv_screen):
+        return self._gather("orc_gather_inv_uv", gy, inv_uv, uv_screen)
+
+    def uv_as_clip(self, uv):
+        uv = _f32(uv)
+        out = np.zeros((uv.shape[0], 4), np.float32)
+        self.lib.orc_uv_as_clip(_fp(uv), _u32(uv.shape[0]), _fp(out))
+        return out
+
+    def screen_attr(self, clip, sw, sh):
+        clip = _f32(clip)
+        out = np.zeros((clip.shape[0], 4), np.float32)
+        self.lib.orc_screen_attr(_fp(clip), _u32(clip.shape[0]), _u32(sw),
+                                 _u32(sh), _fp(out))
+        return out
+
+    def mip_floats(self, w, n, levels):
+        self.lib.orc_mip_floats.restype = C.c_size_t
+        return int(self.lib.orc_mip_floats(_u32(w), _u32(n), _u32(levels)))
+
+    def mip_build(self, tex0, levels):
+        tex0 = _f32(tex0)
+        w, n = tex0.shape[0], tex0.shape[2]
+        pyr = np.zeros(self.mip_floats(w, n, levels), np.float32)
+        self._err(self.lib.orc_mip_build(_fp(tex0), _u32(w), _u32(n),
+                                         _u32(levels), _fp(pyr)), "mip_build")
+        return pyr
+
+    def texture_lod(self, uv, mask, w_tex, levels):
+        uv, mask = _f32(uv), _f32(mask)
+        h, w = mask.shape
+        lod = np.zeros((h, w), np.float32)
+        self.lib.orc_texture_lod(_fp(uv), _fp(mask), _u32(w), _u32(h),
+                                 _u32(w_tex), _u32(levels), _fp(lod))
+        return lod
+
+    def texture_trilinear(self, pyr, w, n, levels, uv, lod):
+        pyr, uv, lod = map(_f32, (pyr, uv, lod))
+        out = np.zeros(lod.shape + (n,), np.float32)
+        self._err(self.lib.orc_texture_trilinear(
+            _fp(pyr), _u32(w), _u32(n), _u32(levels), _fp(uv), _fp(lod),
+            _u32(lod.size), _fp(out)), "texture_trilinear")
+        return out
+
+    def texture_trilinear_grad(self, g, w, n, levels, uv, lod):
+        g, uv, lod = map(_f32, (g, uv, lod))
+        gpyr = np.zeros(self.mip_floats(w, n, levels), np.float32)
+        self._err(self.lib.orc_texture_trilinear_grad(
+            _fp(g), _u32(w), _u32(n), _u32(levels), _fp(uv), _fp(lod),
+            _u32(lod.size), _fp(gpyr)), "texture_trilinear_grad")
+        return gpyr
+
+    def mip_fold(self, gpyr, w, n, levels):
+        gpyr = _f32(gpyr).copy()
+        self.lib.orc_mip_fold(_fp(gpyr), _u32(w), _u32(n), _u32(levels))
+        return gpyr
+
+    def c2_loss_grad(self, tex, levels, pos, uv_v, faces, mvps, targets, res,
+                     want_pred=False):
+        tex, pos, uv_v, faces, mvps, targets = map(
+            _f32, (tex, pos, uv_v, faces, mvps, targets))
+        w = tex.shape[0]
+        grad = np.zeros_like(tex)
+        loss = C.c_double(0.0)
+        pred = (np.zeros((mvps.shape[0], res, res, 3), np.float32)
+                if want_pred else None)
+        self._err(self.lib.orc_c2_loss_grad(
+            _fp(tex), _u32(w), _u32(levels), _fp(pos), _fp(uv_v),
+            _u32(pos.shape[0]), _fp(faces), _u32(faces.shape[0]), _fp(mvps),
+            _u32(mvps.shape[0]), _u32(res), _fp(targets), C.byref(loss),
+            _fp(grad), _fp(pred)), "c2_loss_grad")
+        return loss.value, grad, pred
+
+    def c2_run(self, tex, levels, pos, uv_v, faces, mvps, targets, res, lr,
+               n_iters):
+        tex = _f32(tex).copy()
+        pos, uv_v, faces, mvps, targets = map(_f32, (pos, uv_v, faces, mvps,
+                                                     targets))
+        trace = np.zeros(n_iters, np.float32)
+        self._err(self.lib.orc_c2_run(
+            _fp(tex), _u32(tex.shape[0]), _u32(levels), _fp(pos), _fp(uv_v),
+            _u32(pos.shape[0]), _fp(faces), _u32(faces.shape[0]), _fp(mvps),
+            _u32(mvps.shape[0]), _u32(res), _fp(targets), C.c_float(lr),
+            _u32(n_iters), _fp(trace)), "c2_run")
+        return trace, tex
+
     def vertex_faces_tex(self, faces, n_verts, cap=64):
         faces = _f32(faces)
         out = np.zeros(n_verts * cap, np.float32)
@@ -367,6 +491,23 @@ class Ref(_Lib):
             C.c_float(seed), _u32(n_samples), _u32(w), _u32(h), _fp(gy),
             _fp(out), _fp(gi), _fp(gc)), "antialias")
         return out if gy is None else (out, gi, gc)
+
+    def texture_bilinear(self, tex, uv, inv_uv, gy=None):
+        """TextureBilinear forward; with gy also its texture gradient."""
+        tex, uv, inv_uv = map(_f32, (tex, uv, inv_uv))
+        th, tw = tex.shape[:2]
+        sh, sw = uv.shape[:2]
+        n = 1 if tex.ndim == 2 else tex.shape[2]
+        out = np.zeros((sh, sw) + ((n,) if tex.ndim == 3 else ()), np.float32)
+        g = None
+        if gy is not None:
+            gy = _f32(gy)
+            g = np.zeros_like(tex)
+        self._err(self.lib.ref_texture_bilinear(
+            _fp(tex), _u32(tw), _u32(th), _u32(n), _fp(uv), _u32(sw),
+            _u32(sh), _fp(inv_uv), _fp(gy), _fp(out), _fp(g)),
+            "texture_bilinear")
+        return out if gy is None else (out, g)
 
     def aa_silhouette_run(self, pos, faces, vft, mvps, targets, res,
                           n_samples, lr, n_iters, threads=1,

@@ -596,6 +596,36 @@ int ref_aa_silhouette_run(uint32_t n_verts, uint32_t n_faces, uint32_t n_views,
     });
 }
 
+// F::TextureBilinear on fixed leaves: out = TextureBilinear(tex, uv, inv_uv)
+// [sh][sw][n]; out_grad (nullable) = d(sum gy * out)/d tex through
+// BuildBackward (GatherByInverseUVBilinear).
+int ref_texture_bilinear(const float* tex, uint32_t tw, uint32_t th,
+                         uint32_t n, const float* uv, uint32_t sw, uint32_t sh,
+                         const float* inv_uv, const float* gy, float* out,
+                         float* out_grad) {
+    return Guard([&] {
+        DRESSI_CHECK(n >= 1 && n <= 4, "n_comp 1..4");
+        const VType vt = n == 1 ? FLOAT : n == 2 ? VEC2 : n == 3 ? VEC3 : VEC4;
+        Variable vtex(vt, {tw, th}), vuv(VEC2, {sw, sh}),
+                viv(VEC4, {tw, th}), vgy(vt, {sw, sh});
+        Variable y = F::TextureBilinear(vtex, vuv, viv);
+        CpuEvaluator ev;
+        ev.bind(vtex, Tensor(vt, {tw, th}, tex));
+        ev.bind(vuv, Tensor(VEC2, {sw, sh}, uv));
+        ev.bind(viv, Tensor(VEC4, {tw, th}, inv_uv));
+        CopyOut(ev.eval(y), out);
+        if (!out_grad) return;
+        ev.bind(vgy, Tensor(vt, {sw, sh}, gy));
+        Variable loss = F::StopGradient(vgy) * y;
+        Variable vtex_mut = vtex;
+        vtex_mut.setRequiresGradRecursively();
+        auto [xs, gxs] = BuildBackward(loss);
+        for (size_t i = 0; i < xs.size(); i++) {
+            if (xs[i] == vtex) CopyOut(ev.eval(gxs[i]), out_grad);
+        }
+    });
+}
+
 // 2-D image fitting (examples/image_fitting/run.cpp:40-63 with the in-graph
 // Adam of the silhouette example): loss = Mean((param - target)^2) over a
 // VEC4 image; Adam lr on param. loss_trace[i] is the Mean loss at the start
