@@ -44,10 +44,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c3", "c4"], default="c3")
-    ap.add_argument("--res", type=int, default=1024)
+    ap.add_argument("--config", choices=["c2", "c3", "c4"], default="c3")
+    ap.add_argument("--res", type=int, default=None,
+                    help="default: 512 (c2), 1024 (c3, c4)")
     ap.add_argument("--views", type=int, default=None,
-                    help="default: 16 (c3), 64 (c4)")
+                    help="default: 8 (c2), 16 (c3), 64 (c4)")
     ap.add_argument("--samples", type=int, default=8,
                     help="c4: stochastic edge samples per face (0: exact)")
     ap.add_argument("--level", type=int, default=5)
@@ -56,7 +57,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     if args.views is None:
-        args.views = 16 if args.config == "c3" else 64
+        args.views = {"c2": 8, "c3": 16, "c4": 64}[args.config]
+    if args.res is None:
+        args.res = 512 if args.config == "c2" else 1024
+    if args.config == "c2" and args.level == 5:
+        args.level = 4  # C2's mesh is icosphere-4
     return args
 
 
@@ -68,6 +73,16 @@ def dist_env():
 
 
 def workload(args):
+    if args.config == "c2":
+        return {
+            "workload": "C2 texture optimisation (trilinear, 10 mips) "
+                        "fwd+bwd+Adam",
+            "mesh": f"icosphere-{args.level}",
+            "views": args.views,
+            "res": args.res,
+            "texture": "1024x1024x3, 10 mip levels",
+            "lr": 1e-2,
+        }
     if args.config == "c4":
         return {
             "workload": "C4 silhouette screen-space AA (Dr.Hair) fwd+bwd+Adam",
@@ -85,6 +100,13 @@ def workload(args):
         "sigma": 1e-4,
         "lr": 1e-3,
     }
+
+
+def c2_targets(sc, port):
+    """C2 targets: the renders of the target texture (C restatement)."""
+    zeros = np.zeros((sc.n_views, sc.res, sc.res, 3), np.float32)
+    return port.c2_loss_grad(sc.gt_tex, sc.levels, sc.pos, sc.uv, sc.faces_f,
+                             sc.mvps, zeros, sc.res, want_pred=True)[2]
 
 
 def cpu_targets(args, sc, ref, port, threads):
@@ -117,6 +139,10 @@ def cpu_targets(args, sc, ref, port, threads):
 def cpu_run(args, sc, ref, port, vft, targets, pos, n, threads):
     """n iterations of the CPU implementation (reference if built, else the
     C port) from pos; returns the final positions."""
+    if args.config == "c2":
+        # no reference implementation of the mip path: the C port
+        return port.c2_run(pos, sc.levels, sc.pos, sc.uv, sc.faces_f, sc.mvps,
+                           targets, sc.res, sc.lr, n)[1]
     if args.config == "c4":
         if ref is not None:
             return ref.aa_silhouette_run(pos, sc.faces_f, vft, sc.mvps,
@@ -212,6 +238,17 @@ def iteration_bytes(views: int, res: int, n_verts: int, n_faces: int) -> float:
             + (48.0 + 36.0 + 24.0) * n_verts)
 
 
+def texture_iteration_bytes(views: int, res: int, tex: int) -> float:
+    """Algorithmic HBM bytes of one C2 iteration (the survey's byte model):
+    per view-pixel the uv (8), target (12) and triangle-id (4) reads and
+    two reads of the output gradient (24); the mip chain (1.33 x the level-0
+    texels, 12 B each) read by the sampling and written by the gradient
+    scatter; Adam over the texels (read p, g, m, v = 48 B, write p, m, v =
+    36 B per RGB texel)."""
+    return (48.0 * views * res * res + 2.0 * 1.33 * tex * tex * 12.0
+            + 84.0 * tex * tex)
+
+
 # ------------------------------------------------------------- GPU arm
 
 def run_ours(args):
@@ -221,7 +258,8 @@ def run_ours(args):
     from opendressi_b200 import _native as N
     from opendressi_b200 import scene
     from opendressi_b200.distributed import ShardedStep, shard_views
-    from opendressi_b200.plans import AaSilhouettePlan, SilhouettePlan
+    from opendressi_b200.plans import (AaSilhouettePlan, SilhouettePlan,
+                                       TexturePlan)
 
     world, rank, local = dist_env()
     if world != args.gpus:
@@ -232,16 +270,28 @@ def run_ours(args):
                                 device_id=torch.device(f"cuda:{local}"))
     N.load()
 
-    sc = scene.silhouette_scene(level=args.level, n_views=args.views,
-                                res=args.res, seed=args.seed)
+    if args.config == "c2":
+        sc = scene.texture_scene(level=args.level, n_views=args.views,
+                                 res=args.res, seed=args.seed)
+    else:
+        sc = scene.silhouette_scene(level=args.level, n_views=args.views,
+                                    res=args.res, seed=args.seed)
     shard = shard_views(args.views, world, rank)
-    if args.config == "c4":
+    if args.config == "c2":
+        plan = TexturePlan.from_scene(sc, views=shard, device=local)
+    elif args.config == "c4":
         plan = AaSilhouettePlan.from_scene(sc, views=shard, device=local,
                                            n_samples=args.samples)
     else:
         plan = SilhouettePlan.from_scene(sc, views=shard, device=local)
-    plan.upload(N.SLOT_PARAM, sc.pos0)
-    plan.render_targets(sc.target_pos)
+    if args.config == "c2":
+        plan.upload(N.SLOT_PARAM, sc.tex0)
+        plan.render_targets(sc.gt_tex)
+        param0, n_param = sc.tex0, sc.tex0.size
+    else:
+        plan.upload(N.SLOT_PARAM, sc.pos0)
+        plan.render_targets(sc.target_pos)
+        param0, n_param = sc.pos0, sc.n_verts * 3
     stream = torch.cuda.current_stream()
 
     sharded = ShardedStep(plan) if world > 1 else None
@@ -283,12 +333,11 @@ def run_ours(args):
     # ---- end to end through the public API with host buffers ----------
     e2e = None
     if not args.no_e2e:
-        pos_pin = torch.empty(sc.n_verts * 3, dtype=torch.float32,
-                              pin_memory=True)
+        pos_pin = torch.empty(n_param, dtype=torch.float32, pin_memory=True)
         plan.download(N.SLOT_PARAM, out=pos_pin.numpy())
         loss_pin = torch.empty(1, dtype=torch.float32, pin_memory=True)
         h = plan._h
-        nb = sc.n_verts * 3 * 4
+        nb = n_param * 4
         sp = stream.cuda_stream
 
         def e2e_step():
@@ -328,7 +377,10 @@ def run_ours(args):
     launches_per_iter = sum(p["launches"] for p in prof) / 10.0
     dom = max(prof, key=lambda p: p["total_ms"])
     nvw = len(shard)
-    alg = iteration_bytes(nvw, args.res, sc.n_verts, sc.n_faces)
+    if args.config == "c2":
+        alg = texture_iteration_bytes(nvw, args.res, sc.tex_size)
+    else:
+        alg = iteration_bytes(nvw, args.res, sc.n_verts, sc.n_faces)
     peak, peak_kind = peaks()
     ms_step = ms_max / args.steps
     achieved = alg / (ms_step * 1e-3) / 1e9
@@ -385,9 +437,14 @@ def _cpu_setup(args):
     from oracle import pyoracle
     from opendressi_b200 import scene
 
+    port = pyoracle.Port()
+    if args.config == "c2":
+        sc = scene.texture_scene(level=args.level, n_views=args.views,
+                                 res=args.res, seed=args.seed)
+        sc.pos0 = sc.tex0  # the optimised parameter
+        return sc, None, port, None, c2_targets(sc, port), 1
     sc = scene.silhouette_scene(level=args.level, n_views=args.views,
                                 res=args.res, seed=args.seed)
-    port = pyoracle.Port()
     ref = pyoracle.Ref() if pyoracle.ref_available() else None
     threads = max(1, min(os.cpu_count() or 1, args.views))
     vft = (ref if ref is not None else port).vertex_faces_tex(sc.faces_f,
@@ -401,6 +458,8 @@ def cpu_reference_rate(args, max_seconds=40.0, min_iters=1, max_iters=2):
     same workload, view-parallel on the host cores."""
     sc, ref, port, vft, targets, threads = _cpu_setup(args)
     kind = "reference" if ref is not None else "port"
+    if args.config == "c2":
+        max_iters = min_iters  # ~1 s single-threaded per iteration
 
     def run(n):
         t0 = time.perf_counter()
