@@ -161,6 +161,38 @@ int dressi_antialias_grad(const float* gy, const float* img, uint32_t n_comp,
                           float* grad_img, float* grad_clip, uint32_t* status,
                           void* stream);
 
+/* dressi.torch rasterize (python/dressi/torch/ops.py:96-163): out
+ * [views][H][W][4] = (u, v, z/w, face + 1), 0 = background, computed as
+ * the reference does it -- Rasterize of the unwelded corner attributes
+ * (1,0,z,w), (0,1,z,w), (0,0,z,w) with clip_vk, RasterizeFaceId, and
+ * z/w = g.z / (g.w + (1 - mask)) -- bit-exact. clip_vk [views][V][4] is the
+ * Vulkan-depth clip position (z_vk = 0.5 (z_gl + w)), pos_gl [views][V][4]
+ * the GL one whose z, w are interpolated. */
+int dressi_rasterize_uvzw(const float* clip_vk, const float* pos_gl,
+                          uint32_t n_verts, const float* faces,
+                          uint32_t n_faces, uint32_t views, uint32_t width,
+                          uint32_t height, float* out, uint32_t* status,
+                          void* stream);
+
+/* dressi.torch interpolate (ops.py:169-298): per pixel of a rasterize
+ * output, u a0 + v a1 + (1 - u - v) a2 of the face's vertex attributes
+ * (LookupFaces + FaceFetch, f_ops.cpp:1568-1799), bit-exact. attr
+ * [attr_views][n_verts][n_comp] (attr_views 1: shared by the views). */
+int dressi_interpolate(const float* attr, uint32_t n_comp, uint32_t n_verts,
+                       uint32_t attr_views, const float* rast,
+                       const float* faces, uint32_t n_faces, uint32_t views,
+                       uint32_t width, uint32_t height, float* out,
+                       uint32_t* status, void* stream);
+
+/* Its exact VJP w.r.t. attr (FaceFetchBwd n=0 + LookupFacesBwd):
+ * grad_attr [attr_views][n_verts][n_comp] += ..., gy like out. */
+int dressi_interpolate_grad(const float* gy, uint32_t n_comp,
+                            uint32_t n_verts, uint32_t attr_views,
+                            const float* rast, const float* faces,
+                            uint32_t n_faces, uint32_t views, uint32_t width,
+                            uint32_t height, float* grad_attr,
+                            uint32_t* status, void* stream);
+
 /* F::Texture (filter 0: nearest, the reference's clamp-to-edge nearest
  * sampler, f_ops.cpp:2605-2639) / F::TextureBilinear (filter 1: BilerpClamp,
  * f_ops.cpp:2736-2780, bit-exact): tex [th][tw][n_comp] (n_comp 1..4)

@@ -100,6 +100,13 @@ SIGNATURES = {
                                                 C.POINTER(_vp)]),
     "dressi_aa_silhouette_plan_create": (C.c_int, [C.POINTER(AaSilhouetteDesc),
                                                    C.POINTER(_vp)]),
+    "dressi_rasterize_uvzw": (C.c_int, [_vp, _vp, _u32, _vp, _u32, _u32, _u32,
+                                        _u32, _vp, _vp, _vp]),
+    "dressi_interpolate": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp, _u32,
+                                     _u32, _u32, _u32, _vp, _vp, _vp]),
+    "dressi_interpolate_grad": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp,
+                                          _u32, _u32, _u32, _u32, _vp, _vp,
+                                          _vp]),
     "dressi_texture": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _u32, _u32, _vp,
                                  _vp]),
     "dressi_texture_grad": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _u32, _u32,

@@ -632,6 +632,73 @@ int dressi_aa_silhouette_plan_create(const dressi_aa_silhouette_desc* desc,
     });
 }
 
+int dressi_rasterize_uvzw(const float* clip_vk, const float* pos_gl,
+                          uint32_t n_verts, const float* faces,
+                          uint32_t n_faces, uint32_t views, uint32_t width,
+                          uint32_t height, float* out, uint32_t* status,
+                          void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(clip_vk && pos_gl && out && status &&
+                               (faces || n_faces == 0),
+                       "null pointer");
+        DRESSI_REQUIRE(views >= 1 && width >= 1 && height >= 1,
+                       "rasterize: empty screen or no views");
+        DRESSI_REQUIRE(width <= 32768 && height <= 32768,
+                       "rasterize: screen larger than 32768");
+        cudaStream_t s = as_stream(stream);
+        HardDims d;
+        d.W = int(width);
+        d.H = int(height);
+        d.views = int(views);
+        d.n_faces = int(n_faces);
+        d.n_verts = int(n_verts);
+        d.n_comp = 4;
+        d.uvzw = 1;
+        d.finalize();
+        AsyncScratch scratch(hard_workspace_bytes(d), s);
+        hard_raster_op(d, scratch.p, clip_vk, pos_gl, faces, out, nullptr,
+                       status, s);
+    });
+}
+
+int dressi_interpolate(const float* attr, uint32_t n_comp, uint32_t n_verts,
+                       uint32_t attr_views, const float* rast,
+                       const float* faces, uint32_t n_faces, uint32_t views,
+                       uint32_t width, uint32_t height, float* out,
+                       uint32_t* status, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(attr && rast && out && status && (faces || n_faces == 0),
+                       "null pointer");
+        DRESSI_REQUIRE(n_comp >= 1, "interpolate: attr has no components");
+        DRESSI_REQUIRE(attr_views == 1 || attr_views == views,
+                       "interpolate: attr views must be 1 or the rast views");
+        interpolate_op(attr, int(n_comp), int(n_verts), int(attr_views), rast,
+                       faces, int(n_faces), int(views), int(width),
+                       int(height), out, status, as_stream(stream));
+    });
+}
+
+int dressi_interpolate_grad(const float* gy, uint32_t n_comp,
+                            uint32_t n_verts, uint32_t attr_views,
+                            const float* rast, const float* faces,
+                            uint32_t n_faces, uint32_t views, uint32_t width,
+                            uint32_t height, float* grad_attr,
+                            uint32_t* status, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(gy && rast && grad_attr && status &&
+                               (faces || n_faces == 0),
+                       "null pointer");
+        DRESSI_REQUIRE(n_comp >= 1, "interpolate grad: no components");
+        DRESSI_REQUIRE(attr_views == 1 || attr_views == views,
+                       "interpolate grad: attr views must be 1 or the rast "
+                       "views");
+        interpolate_grad_op(gy, int(n_comp), int(n_verts), int(attr_views),
+                            rast, faces, int(n_faces), int(views),
+                            int(width), int(height), grad_attr, status,
+                            as_stream(stream));
+    });
+}
+
 int dressi_texture(const float* tex, uint32_t tw, uint32_t th,
                    uint32_t n_comp, const float* uv, uint32_t n_px,
                    uint32_t filter, float* out, void* stream) {

@@ -266,6 +266,33 @@ __global__ void __launch_bounds__(kTileThreads)
     const size_t pix = size_t(v) * d.W * d.H + size_t(y) * d.W + x;
     if (depth_out) depth_out[pix] = best_f >= 0 ? best_z : 1.f;
     if (id_out) id_out[pix] = best_f >= 0 ? float(best_f) + 1.f : 0.f;
+    if (d.uvzw) {
+        // The reference's rasterize (python/dressi/torch/ops.py:96-110):
+        // g = Rasterize(unwelded clip, corner attributes), tid =
+        // RasterizeFaceId, z/w = g.z / (g.w + (1 - mask)).
+        float4* o4 = reinterpret_cast<float4*>(out) + pix;
+        if (best_f < 0) {
+            *o4 = make_float4(0.f, 0.f, 0.f / (0.f + 1.f), 0.f);
+            return;
+        }
+        const HardRec& r = recs[best_f];
+        float l[3];
+        hard_bary(r, px, py, &l[0], &l[1], &l[2]);
+        const float iw[3] = {r.iw0, r.iw1, r.iw2};
+        const uint32_t idx[3] = {r.i0, r.i1, r.i2};
+        const float denom = l[0] * iw[0] + l[1] * iw[1] + l[2] * iw[2];
+        const float4* pg = reinterpret_cast<const float4*>(attr) + size_t(v) * d.n_verts;
+        float num[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int k = 0; k < 3; k++) {
+            const float4 a = pg[idx[k]];
+            const float ak[4] = {k == 0 ? 1.f : 0.f, k == 1 ? 1.f : 0.f, a.z, a.w};
+            for (int c = 0; c < 4; c++) num[c] += l[k] * iw[k] * ak[c];
+        }
+        const float gz = num[2] / denom, gw = num[3] / denom;
+        *o4 = make_float4(num[0] / denom, num[1] / denom, gz / (gw + (1.f - 1.f)),
+                          float(best_f) + 1.f);
+        return;
+    }
     if (!attr && !d.attr_ones) {
         out[pix] = best_f >= 0 ? float(best_f) + 1.f : 0.f;
         return;

@@ -193,6 +193,10 @@ struct HardDims {
     int W = 0, H = 0, views = 1, n_faces = 0, n_verts = 0, n_comp = 1;
     int attr_ones = 0;  // the attribute is 1 at every vertex (a mask)
     int attr_shared = 0;  // one attribute array [V][n_comp] for all views
+    // nvdiffrast-style output (dressi.torch rasterize): out [views][H][W][4]
+    // = (u, v, z/w, face + 1) from the corner attributes (1,0,z,w), (0,1,
+    // z,w), (0,0,z,w) with z, w = attr[views][V][4] (the GL clip position)
+    int uvzw = 0;
     int tiles_x = 0, tiles_y = 0, n_tiles = 0, cap = 0;
     void finalize() {
         tiles_x = (W + kTile - 1) / kTile;
@@ -322,6 +326,19 @@ void tex_predict(const TexParams& p, const TexBuffers& b, float* out,
 // targets = mask * trilinear(mips(gt_tex)) per view (gt_tex on the device).
 void tex_render_targets(const TexParams& p, const TexBuffers& b,
                         const float* gt_tex, cudaStream_t s);
+
+// --- dressi.torch-style interpolation (interp.cu) ---
+// attr [attr_views][V][n_comp] (attr_views 1: shared), rast
+// [views][H][W][4] -> out [views][H][W][n_comp]; the grad ADDS into
+// grad [attr_views][V][n_comp].
+void interpolate_op(const float* attr, int n_comp, int n_verts,
+                    int attr_views, const float* rast, const float* faces,
+                    int n_faces, int views, int W, int H, float* out,
+                    uint32_t* status, cudaStream_t s);
+void interpolate_grad_op(const float* gy, int n_comp, int n_verts,
+                         int attr_views, const float* rast, const float* faces,
+                         int n_faces, int views, int W, int H, float* grad,
+                         uint32_t* status, cudaStream_t s);
 
 // --- image fitting (C1) ---
 struct FitBuffers {
