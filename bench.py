@@ -51,6 +51,12 @@ def parse():
                     help="default: 8 (c2), 16 (c3), 64 (c4)")
     ap.add_argument("--samples", type=int, default=8,
                     help="c4: stochastic edge samples per face (0: exact)")
+    ap.add_argument("--laplacian", type=float, default=None,
+                    help="optimizer-side regulariser weights relative to the "
+                         "data-gradient RMS (run.cpp:407-420); default: the "
+                         "reference example's, 0.15/0.4 (c3), 0.5/0.5 (c4); "
+                         "0 0 = none")
+    ap.add_argument("--normal", type=float, default=None)
     ap.add_argument("--level", type=int, default=5)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -62,6 +68,13 @@ def parse():
         args.res = 512 if args.config == "c2" else 1024
     if args.config == "c2" and args.level == 5:
         args.level = 4  # C2's mesh is icosphere-4
+    # the silhouette example's per-technique defaults (run.cpp:127-132)
+    lap0, nrm0 = {"c3": (0.15, 0.4), "c4": (0.5, 0.5)}.get(args.config,
+                                                          (0.0, 0.0))
+    if args.laplacian is None:
+        args.laplacian = lap0
+    if args.normal is None:
+        args.normal = nrm0
     return args
 
 
@@ -91,6 +104,8 @@ def workload(args):
             "res": args.res,
             "edge_samples": args.samples,
             "lr": 1e-3,
+            "regularizer": {"laplacian": args.laplacian,
+                            "normal": args.normal},
         }
     return {
         "workload": "C3 silhouette HardSoftRas fwd+bwd+Adam",
@@ -99,6 +114,7 @@ def workload(args):
         "res": args.res,
         "sigma": 1e-4,
         "lr": 1e-3,
+        "regularizer": {"laplacian": args.laplacian, "normal": args.normal},
     }
 
 
@@ -143,21 +159,22 @@ def cpu_run(args, sc, ref, port, vft, targets, pos, n, threads):
         # no reference implementation of the mip path: the C port
         return port.c2_run(pos, sc.levels, sc.pos, sc.uv, sc.faces_f, sc.mvps,
                            targets, sc.res, sc.lr, n)[1]
+    reg = dict(laplacian=args.laplacian, normal=args.normal)
     if args.config == "c4":
         if ref is not None:
             return ref.aa_silhouette_run(pos, sc.faces_f, vft, sc.mvps,
                                          targets, sc.res, args.samples,
-                                         sc.lr, n, threads=threads)[1]
+                                         sc.lr, n, threads=threads, **reg)[1]
         return port.aa_silhouette_run(pos, sc.faces_f, vft, sc.mvps, targets,
                                       sc.res, args.samples, sc.lr, n,
-                                      threads=threads)[1]
+                                      threads=threads, **reg)[1]
     if ref is not None:
         return ref.silhouette_run(pos, sc.faces_f, vft, sc.mvps, targets,
                                   sc.res, sc.radius_px, sc.sigma, sc.lr, n,
-                                  threads=threads)[1]
+                                  threads=threads, **reg)[1]
     return port.silhouette_run(pos, sc.faces_f, sc.mvps, targets, sc.res,
                                sc.radius_px, sc.sigma, sc.lr, n,
-                               threads=threads)[1]
+                               threads=threads, **reg)[1]
 
 
 def peaks():
@@ -281,9 +298,13 @@ def run_ours(args):
         plan = TexturePlan.from_scene(sc, views=shard, device=local)
     elif args.config == "c4":
         plan = AaSilhouettePlan.from_scene(sc, views=shard, device=local,
-                                           n_samples=args.samples)
+                                           n_samples=args.samples,
+                                           laplacian=args.laplacian,
+                                           normal=args.normal)
     else:
-        plan = SilhouettePlan.from_scene(sc, views=shard, device=local)
+        plan = SilhouettePlan.from_scene(sc, views=shard, device=local,
+                                         laplacian=args.laplacian,
+                                         normal=args.normal)
     if args.config == "c2":
         plan.upload(N.SLOT_PARAM, sc.tex0)
         plan.render_targets(sc.gt_tex)

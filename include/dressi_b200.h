@@ -27,6 +27,9 @@
  *  - RasterizeSoft backward (ColSum(GatherDistGrad))
  *                                              src/core/f_ops.cpp:1218-1358
  *  - dressi.torch.rasterize_soft / rasterize   python/dressi/torch/ops.py:682, 118
+ *  - F::VertexNeighborMean / NormalConsistency* / SumAll and the mesh
+ *    tables of the silhouette optimizer         include/dressi/f.h:97, 240-255;
+ *                                              include/dressi/mesh_utils.h:26-34
  */
 #ifndef DRESSI_B200_H
 #define DRESSI_B200_H
@@ -212,6 +215,67 @@ int dressi_texture_grad(const float* gy, uint32_t sw, uint32_t sh,
                         uint32_t th, const float* uv_screen, uint32_t filter,
                         float* grad_tex, void* stream);
 
+/* Optimizer-side regulariser ops of the silhouette example
+ * (examples/silhouette_optimization/run.cpp:407-420). Tables keep the
+ * reference's layout: ids as float, -1 padding, {V, deg} tables row-major
+ * with row d at [d * n_verts].
+ *
+ * VertexFacesTex / VertexNeighborsTex / FaceNeighborsTex (mesh_utils.cpp:
+ * 53-101; HOST pointers, no device work): out holds cap * n_verts floats
+ * ({V, deg} tables; *deg receives the table height, an error when above
+ * cap) or 3 * n_faces floats (face neighbours). */
+int dressi_vertex_faces_tex(const float* faces, uint32_t n_faces,
+                            uint32_t n_verts, uint32_t cap, float* out,
+                            uint32_t* deg);
+int dressi_vertex_neighbors_tex(const float* faces, uint32_t n_faces,
+                                uint32_t n_verts, uint32_t cap, float* out,
+                                uint32_t* deg);
+int dressi_face_neighbors_tex(const float* faces, uint32_t n_faces,
+                              float* out);
+
+/* F::VertexNeighborMean (f_ops.cpp:1983-2029): out [V][3] = mean of the
+ * listed neighbours of each vertex (pos itself when it has none). In these
+ * ops a table id out of range sets DRESSI_STATUS_INDEX_RANGE in `status`
+ * (a device word, nullable) and is skipped. */
+int dressi_vertex_neighbor_mean(const float* pos, uint32_t n_verts,
+                                const float* nbrs, uint32_t nbr_deg,
+                                float* out, uint32_t* status, void* stream);
+
+/* F::NormalConsistencyFaceTerm (f_ops.cpp:2031-2098): out [F][3] from pos
+ * [V][3], faces [F][3] and face_adj [F][3]. */
+int dressi_normal_consistency_face_term(const float* pos, uint32_t n_verts,
+                                        const float* faces, uint32_t n_faces,
+                                        const float* face_adj, float* out,
+                                        uint32_t* status, void* stream);
+
+/* F::NormalConsistencyVertexGrad (f_ops.cpp:2100-2181): out [V][3] from
+ * the face term [F][3], pos, faces and vtx_faces {V, vf_deg}. */
+int dressi_normal_consistency_vertex_grad(const float* term, const float* pos,
+                                          uint32_t n_verts, const float* faces,
+                                          uint32_t n_faces,
+                                          const float* vtx_faces,
+                                          uint32_t vf_deg, float* out,
+                                          uint32_t* status, void* stream);
+
+/* F::SumAll (f_ops.cpp:1119-1149, with SumPartial's 64 strided double
+ * partials above 256 pixels): out (1 device float) = the sum of x
+ * [n_px][n_comp], bit-identical to the reference's CPU evaluator. */
+int dressi_sum_all(const float* x, uint32_t n_px, uint32_t n_comp, float* out,
+                   void* stream);
+
+/* The whole regulariser: out [V][3] = g + g_lap (rms(g) / rms(g_lap)
+ * laplacian) + g_nrm (rms(g) / rms(g_nrm) normal), g_lap = pos -
+ * VertexNeighborMean(pos), g_nrm = NormalConsistencyVertexGrad(
+ * NormalConsistencyFaceTerm(pos)), rms(x) = sqrt(SumAll(x*x) / (3V) +
+ * 1e-24); out may alias g. */
+int dressi_regularized_grad(const float* pos, uint32_t n_verts,
+                            const float* faces, uint32_t n_faces,
+                            const float* nbrs, uint32_t nbr_deg,
+                            const float* face_adj, const float* vtx_faces,
+                            uint32_t vf_deg, const float* g, float laplacian,
+                            float normal, float* out, uint32_t* status,
+                            void* stream);
+
 /* ------------------------------------------------------------------------
  * Plans: one fused fwd + bwd + Adam iteration, resident on one device,
  * replayed as a CUDA graph with no per-iteration host traffic
@@ -250,6 +314,10 @@ typedef struct {
     const float* mvps;     /* host [n_views][16], column-major */
     uint32_t loss_history; /* ring capacity (0 -> 4096) */
     int device;            /* CUDA device ordinal */
+    /* optimizer-side regulariser weights relative to the data-gradient RMS
+     * (run.cpp:407-420; the example's defaults are 0.15 / 0.4); 0 / 0 =
+     * none */
+    float laplacian, normal;
 } dressi_silhouette_desc;
 
 int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
@@ -271,6 +339,9 @@ typedef struct {
     const float* mvps;     /* host [n_views][16], column-major */
     uint32_t loss_history; /* ring capacity (0 -> 4096) */
     int device;            /* CUDA device ordinal */
+    /* regulariser weights as in dressi_silhouette_desc (the example's
+     * defaults for this technique are 0.5 / 0.5); 0 / 0 = none */
+    float laplacian, normal;
 } dressi_aa_silhouette_desc;
 
 int dressi_aa_silhouette_plan_create(const dressi_aa_silhouette_desc* desc,

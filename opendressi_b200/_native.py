@@ -39,6 +39,7 @@ class SilhouetteDesc(C.Structure):
         ("faces", _fp), ("mvps", _fp),
         ("loss_history", C.c_uint32),
         ("device", C.c_int),
+        ("laplacian", C.c_float), ("normal", C.c_float),
     ]
 
 
@@ -53,6 +54,7 @@ class AaSilhouetteDesc(C.Structure):
         ("faces", _fp), ("mvps", _fp),
         ("loss_history", C.c_uint32),
         ("device", C.c_int),
+        ("laplacian", C.c_float), ("normal", C.c_float),
     ]
 
 
@@ -111,6 +113,22 @@ SIGNATURES = {
                                  _vp]),
     "dressi_texture_grad": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _u32, _u32,
                                       _vp, _u32, _vp, _vp]),
+    "dressi_vertex_faces_tex": (C.c_int, [_vp, _u32, _u32, _u32, _vp,
+                                          C.POINTER(_u32)]),
+    "dressi_vertex_neighbors_tex": (C.c_int, [_vp, _u32, _u32, _u32, _vp,
+                                              C.POINTER(_u32)]),
+    "dressi_face_neighbors_tex": (C.c_int, [_vp, _u32, _vp]),
+    "dressi_vertex_neighbor_mean": (C.c_int, [_vp, _u32, _vp, _u32, _vp, _vp,
+                                              _vp]),
+    "dressi_normal_consistency_face_term": (C.c_int, [_vp, _u32, _vp, _u32,
+                                                      _vp, _vp, _vp, _vp]),
+    "dressi_normal_consistency_vertex_grad": (C.c_int, [_vp, _vp, _u32, _vp,
+                                                        _u32, _vp, _u32, _vp,
+                                                        _vp, _vp]),
+    "dressi_sum_all": (C.c_int, [_vp, _u32, _u32, _vp, _vp]),
+    "dressi_regularized_grad": (C.c_int, [_vp, _u32, _vp, _u32, _vp, _u32,
+                                          _vp, _vp, _u32, _vp, C.c_float,
+                                          C.c_float, _vp, _vp, _vp]),
     "dressi_texture_plan_create": (C.c_int, [C.POINTER(TextureDesc),
                                              C.POINTER(_vp)]),
     "dressi_image_fit_plan_create": (C.c_int, [_u32, _u32, C.c_float, C.c_int,

@@ -702,7 +702,13 @@ void aa_sil_forward_backward(const SilParams& p, const AaSilBuffers& b,
 void aa_sil_iteration(const SilParams& p, const AaSilBuffers& b,
                       cudaStream_t s) {
     aa_sil_forward_backward(p, b, s);
-    sil_grad_reduce(p, b.sil, true, s);
+    if (!p.reg) {
+        sil_grad_reduce(p, b.sil, true, s);
+        return;
+    }
+    sil_grad_reduce(p, b.sil, false, s);
+    sil_reg_terms(p, b.sil, s);
+    sil_update(p, b.sil, s);
 }
 
 void aa_sil_predict(const SilParams& p, const AaSilBuffers& b, float* out,

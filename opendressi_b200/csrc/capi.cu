@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -92,6 +93,58 @@ struct AsyncScratch {
 }  // namespace dressi
 
 using namespace dressi;
+
+namespace {
+
+// Host-built mesh tables of a silhouette plan's regulariser.
+struct RegTables {
+    std::vector<float> nbrs, fadj, vf;
+    int nbr_deg = 0, vf_deg = 0;
+};
+
+void reg_params(SilParams* p, float laplacian, float normal) {
+    DRESSI_REQUIRE(std::isfinite(laplacian) && std::isfinite(normal),
+                   "silhouette plan: regulariser weights must be finite");
+    p->laplacian = laplacian;
+    p->normal = normal;
+    p->reg = (laplacian != 0.f || normal != 0.f) ? 1 : 0;
+}
+
+void reg_tables(const SilParams& p, const float* faces, RegTables* t) {
+    if (!p.reg) return;
+    vertex_neighbors_table(faces, p.n_faces, p.n_verts, &t->nbrs,
+                           &t->nbr_deg);
+    face_neighbors_table(faces, p.n_faces, &t->fadj);
+    vertex_faces_table(faces, p.n_faces, p.n_verts, &t->vf, &t->vf_deg);
+}
+
+void carve_reg(Arena& a, const SilParams& p, const RegTables& t,
+               RegBuffers* r) {
+    *r = RegBuffers{};
+    if (!p.reg) return;
+    const size_t V = size_t(p.n_verts), F = size_t(p.n_faces);
+    r->nbrs = a.take<float>(t.nbrs.size());
+    r->nbr_deg = t.nbr_deg;
+    r->fadj = a.take<float>(t.fadj.size());
+    r->vf = a.take<float>(t.vf.size());
+    r->vf_deg = t.vf_deg;
+    r->term = a.take<float>(F * 3);
+    r->glap = a.take<float>(V * 3);
+    r->gnrm = a.take<float>(V * 3);
+    r->scale = a.take<float>(2);
+}
+
+void upload_reg(const RegTables& t, const RegBuffers& r) {
+    if (!r.nbrs) return;
+    DRESSI_CUDA(cudaMemcpy(r.nbrs, t.nbrs.data(), t.nbrs.size() * 4,
+                           cudaMemcpyHostToDevice));
+    DRESSI_CUDA(cudaMemcpy(r.fadj, t.fadj.data(), t.fadj.size() * 4,
+                           cudaMemcpyHostToDevice));
+    DRESSI_CUDA(cudaMemcpy(r.vf, t.vf.data(), t.vf.size() * 4,
+                           cudaMemcpyHostToDevice));
+}
+
+}  // namespace
 
 struct dressi_plan_s {
     enum Kind { kSil, kFit, kAa, kTex } kind = kSil;
@@ -496,6 +549,9 @@ int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
         p.eps = desc->eps;
         p.k = (2.f / float(desc->res)) * (2.f / float(desc->res)) / desc->sigma;
         p.c = 1.f / float(desc->res * desc->res);
+        reg_params(&p, desc->laplacian, desc->normal);
+        RegTables rt;
+        reg_tables(p, desc->faces, &rt);
         const int hist = desc->loss_history ? int(desc->loss_history) : 4096;
         const size_t V = desc->n_verts, F = desc->n_faces, NV = desc->n_views;
         const size_t R2 = size_t(desc->res) * desc->res;
@@ -516,6 +572,7 @@ int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
             b.hist_cap = hist;
             b.done = a.take<unsigned>(1);
             carve_soft_main(a, d, &b.soft);
+            carve_reg(a, p, rt, &b.reg);
         };
         Arena dry;
         carve(dry);
@@ -529,6 +586,7 @@ int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
                                cudaMemcpyHostToDevice));
         DRESSI_CUDA(cudaMemcpy(pl->b.mvps, desc->mvps, NV * 16 * sizeof(float),
                                cudaMemcpyHostToDevice));
+        upload_reg(rt, pl->b.reg);
         pl->alloc_bins();
         DRESSI_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&pl->ovf_host), 4,
                                   cudaHostAllocDefault));
@@ -576,6 +634,9 @@ int dressi_aa_silhouette_plan_create(const dressi_aa_silhouette_desc* desc,
         p.eps = desc->eps;
         p.c = 1.f / float(desc->res * desc->res);
         p.n_samples = int(desc->n_samples);
+        reg_params(&p, desc->laplacian, desc->normal);
+        RegTables rt;
+        reg_tables(p, desc->faces, &rt);
         const int hist = desc->loss_history ? int(desc->loss_history) : 4096;
         const size_t V = desc->n_verts, F = desc->n_faces, NV = desc->n_views;
         const size_t R2 = size_t(desc->res) * desc->res;
@@ -604,6 +665,7 @@ int dressi_aa_silhouette_plan_create(const dressi_aa_silhouette_desc* desc,
             ab.view_flags = a.take<int>(NV);
             ab.status = a.take<uint32_t>(4);
             ab.hard_ws = a.take<char>(ws);
+            carve_reg(a, p, rt, &b.reg);
         };
         Arena dry;
         carve(dry);
@@ -618,6 +680,7 @@ int dressi_aa_silhouette_plan_create(const dressi_aa_silhouette_desc* desc,
                                cudaMemcpyHostToDevice));
         DRESSI_CUDA(cudaMemcpy(pl->b.mvps, desc->mvps, NV * 16 * sizeof(float),
                                cudaMemcpyHostToDevice));
+        upload_reg(rt, pl->b.reg);
         pl->set_slot(DRESSI_SLOT_PARAM, pl->b.pos, V * 3 * 4);
         pl->set_slot(DRESSI_SLOT_ADAM_M, pl->b.adam_m, V * 3 * 4);
         pl->set_slot(DRESSI_SLOT_ADAM_V, pl->b.adam_v, V * 3 * 4);
@@ -728,6 +791,129 @@ int dressi_texture_grad(const float* gy, uint32_t sw, uint32_t sh,
         texture_gather_op(gy, int(sw), int(sh), int(n_comp), int(filter),
                           inv_uv, int(tw), int(th), uv_screen, grad_tex,
                           as_stream(stream));
+    });
+}
+
+namespace {
+
+int copy_table(const std::vector<float>& t, int deg, uint32_t cap, float* out,
+               uint32_t* deg_out, const char* what) {
+    DRESSI_REQUIRE(uint32_t(deg) <= cap,
+                   std::string(what) + ": table height " + std::to_string(deg) +
+                           " above cap " + std::to_string(cap));
+    std::copy(t.begin(), t.end(), out);
+    *deg_out = uint32_t(deg);
+    return 0;
+}
+
+}  // namespace
+
+int dressi_vertex_faces_tex(const float* faces, uint32_t n_faces,
+                            uint32_t n_verts, uint32_t cap, float* out,
+                            uint32_t* deg) {
+    return guarded([&] {
+        DRESSI_REQUIRE(faces && out && deg, "null pointer");
+        std::vector<float> t;
+        int d = 0;
+        vertex_faces_table(faces, int(n_faces), int(n_verts), &t, &d);
+        copy_table(t, d, cap, out, deg, "VertexFacesTex");
+    });
+}
+
+int dressi_vertex_neighbors_tex(const float* faces, uint32_t n_faces,
+                                uint32_t n_verts, uint32_t cap, float* out,
+                                uint32_t* deg) {
+    return guarded([&] {
+        DRESSI_REQUIRE(faces && out && deg, "null pointer");
+        std::vector<float> t;
+        int d = 0;
+        vertex_neighbors_table(faces, int(n_faces), int(n_verts), &t, &d);
+        copy_table(t, d, cap, out, deg, "VertexNeighborsTex");
+    });
+}
+
+int dressi_face_neighbors_tex(const float* faces, uint32_t n_faces,
+                              float* out) {
+    return guarded([&] {
+        DRESSI_REQUIRE(faces && out, "null pointer");
+        std::vector<float> t;
+        face_neighbors_table(faces, int(n_faces), &t);
+        std::copy(t.begin(), t.end(), out);
+    });
+}
+
+int dressi_vertex_neighbor_mean(const float* pos, uint32_t n_verts,
+                                const float* nbrs, uint32_t nbr_deg,
+                                float* out, uint32_t* status, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(pos && nbrs && out, "null pointer");
+        vertex_terms_op(pos, int(n_verts), nbrs, int(nbr_deg), false, out,
+                        nullptr, nullptr, 0, nullptr, 0, nullptr, status,
+                        as_stream(stream));
+    });
+}
+
+int dressi_normal_consistency_face_term(const float* pos, uint32_t n_verts,
+                                        const float* faces, uint32_t n_faces,
+                                        const float* face_adj, float* out,
+                                        uint32_t* status, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(pos && faces && face_adj && out, "null pointer");
+        nc_face_term_op(pos, int(n_verts), faces, face_adj, int(n_faces), out,
+                        status, as_stream(stream));
+    });
+}
+
+int dressi_normal_consistency_vertex_grad(const float* term, const float* pos,
+                                          uint32_t n_verts, const float* faces,
+                                          uint32_t n_faces,
+                                          const float* vtx_faces,
+                                          uint32_t vf_deg, float* out,
+                                          uint32_t* status, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(term && pos && faces && vtx_faces && out,
+                       "null pointer");
+        vertex_terms_op(pos, int(n_verts), nullptr, 0, false, nullptr, term,
+                        faces, int(n_faces), vtx_faces, int(vf_deg), out,
+                        status, as_stream(stream));
+    });
+}
+
+int dressi_sum_all(const float* x, uint32_t n_px, uint32_t n_comp, float* out,
+                   void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(x && out, "null pointer");
+        DRESSI_REQUIRE(n_comp >= 1 && n_comp <= 4, "SumAll: 1..4 components");
+        sum_all_op(x, int(n_px), int(n_comp), out, as_stream(stream));
+    });
+}
+
+int dressi_regularized_grad(const float* pos, uint32_t n_verts,
+                            const float* faces, uint32_t n_faces,
+                            const float* nbrs, uint32_t nbr_deg,
+                            const float* face_adj, const float* vtx_faces,
+                            uint32_t vf_deg, const float* g, float laplacian,
+                            float normal, float* out, uint32_t* status,
+                            void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(pos && faces && nbrs && face_adj && vtx_faces && g &&
+                               out,
+                       "null pointer");
+        DRESSI_REQUIRE(n_verts > 0, "regularized_grad: no vertices");
+        cudaStream_t s = as_stream(stream);
+        const size_t V3 = size_t(n_verts) * 3, F3 = size_t(n_faces) * 3;
+        AsyncScratch sc((F3 + 2 * V3 + 2) * sizeof(float), s);
+        float* term = static_cast<float*>(sc.p);
+        float* glap = term + F3;
+        float* gnrm = glap + V3;
+        float* scale = gnrm + V3;
+        nc_face_term_op(pos, int(n_verts), faces, face_adj, int(n_faces), term,
+                        status, s);
+        vertex_terms_op(pos, int(n_verts), nbrs, int(nbr_deg), true, glap,
+                        term, faces, int(n_faces), vtx_faces, int(vf_deg),
+                        gnrm, status, s);
+        reg_scale_op(g, glap, gnrm, int(n_verts), laplacian, normal, scale, s);
+        reg_combine_op(g, glap, gnrm, scale, int(V3), out, s);
     });
 }
 
@@ -998,6 +1184,7 @@ int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream) {
             if (phase == 0) {
                 aa_sil_forward_backward(p->p, p->ab, s);
                 sil_grad_reduce(p->p, p->b, false, s);
+                sil_reg_terms(p->p, p->b, s);
             } else {
                 sil_update(p->p, p->b, s);
             }
@@ -1007,6 +1194,7 @@ int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream) {
             p->grow_bins_if_needed(s);
             sil_forward_backward(p->d, p->p, p->b, nullptr, s);
             sil_grad_reduce(p->p, p->b, false, s);
+            sil_reg_terms(p->p, p->b, s);
             DRESSI_CUDA(cudaMemcpyAsync(p->ovf_host, p->b.soft.status + 1, 4,
                                         cudaMemcpyDeviceToHost, s));
         } else {

@@ -7,6 +7,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <vector>
 
 #include "common.h"
 #include "raster_soft.cuh"
@@ -142,6 +143,22 @@ struct SilParams {
     float k;  // (2/R)^2 / sigma
     float c;  // 1 / R^2
     int n_samples;  // AA plans: stochastic edge samples (0: exact)
+    // optimizer-side regulariser weights (run.cpp:407-420); reg = either
+    // weight non-zero
+    float laplacian, normal;
+    int reg;
+};
+// Mesh tables and scratch of the regulariser (ids as float, -1 padding).
+struct RegBuffers {
+    float* nbrs;     // [nbr_deg][V] VertexNeighborsTex
+    int nbr_deg;
+    float* fadj;     // [F][3] FaceNeighborsTex
+    float* vf;       // [vf_deg][V] VertexFacesTex
+    int vf_deg;
+    float* term;     // [F][3] NormalConsistencyFaceTerm
+    float* glap;     // [V][3] pos - VertexNeighborMean
+    float* gnrm;     // [V][3] NormalConsistencyVertexGrad
+    float* scale;    // [2] s_lap, s_nrm
 };
 struct SilBuffers {
     float* pos;       // [V*3]
@@ -159,6 +176,7 @@ struct SilBuffers {
     int hist_cap;
     unsigned* done;      // block-completion counter of the Adam step
     SoftBuffers soft;
+    RegBuffers reg;      // p.reg only
 };
 constexpr int kLossSlots = 4096;
 // Transform, raster, loss and per-view clip gradients (advances the Adam
@@ -180,6 +198,38 @@ void sil_transform(const SilParams& p, const SilBuffers& b, int advance,
 // clip = MVP (target_pos, 1) into b.clip (target rendering).
 void sil_transform_plain(const SilParams& p, const SilBuffers& b,
                          const float* target_pos, cudaStream_t s);
+// Regulariser terms of the current pos (g_lap, NC face term, g_nrm);
+// depend on pos only, so they run before the gradient all-reduce.
+void sil_reg_terms(const SilParams& p, const SilBuffers& b, cudaStream_t s);
+// The regulariser's scales from the reduced g_pos (before the Adam step).
+void sil_reg_scale(const SilParams& p, const SilBuffers& b, cudaStream_t s);
+// The reference's mesh tables (mesh_utils.cpp:53-101), host side.
+void vertex_faces_table(const float* faces, int n_faces, int n_verts,
+                        std::vector<float>* out, int* max_deg);
+void vertex_neighbors_table(const float* faces, int n_faces, int n_verts,
+                            std::vector<float>* out, int* max_deg);
+void face_neighbors_table(const float* faces, int n_faces,
+                          std::vector<float>* out);
+// Op level: NormalConsistencyFaceTerm, VertexNeighborMean (lap_diff: pos -
+// mean) + NormalConsistencyVertexGrad (either output nullable), SumAll.
+// Table ids out of range set kStatusIndexRange in status (nullable)
+// and are skipped.
+void nc_face_term_op(const float* pos, int n_verts, const float* faces,
+                     const float* fadj, int n_faces, float* term,
+                     uint32_t* status, cudaStream_t s);
+void vertex_terms_op(const float* pos, int n_verts, const float* nbrs,
+                     int nbr_deg, bool lap_diff, float* lap_out,
+                     const float* term, const float* faces, int n_faces,
+                     const float* vf, int vf_deg, float* nrm_out,
+                     uint32_t* status, cudaStream_t s);
+void sum_all_op(const float* x, int n_px, int nc, float* out, cudaStream_t s);
+// scale = {rms(g)/rms(glap)*laplacian, rms(g)/rms(gnrm)*normal}; out =
+// (g + glap*scale[0]) + gnrm*scale[1] over n floats.
+void reg_scale_op(const float* g, const float* glap, const float* gnrm,
+                  int n_verts, float laplacian, float normal, float* scale,
+                  cudaStream_t s);
+void reg_combine_op(const float* g, const float* glap, const float* gnrm,
+                    const float* scale, int n, float* out, cudaStream_t s);
 // One full single-device iteration.
 void sil_iteration(const SoftDims& d, const SilParams& p,
                    const SilBuffers& b, cudaStream_t s);

@@ -5,6 +5,7 @@
 //              RasterizeSoft sweeps 1/2 (exact survivor)    raster_soft.cuh
 //              loss image + dL/d dist + GatherDistGrad      k_sweep2_sil
 //   all views: g_pos = sum_v MVP_v^T g_clip_v               k_gpos_adam
+//              regulariser (laplacian / normal != 0)        regularize.cu
 //              in-graph Adam                                k_gpos_adam
 //
 // It computes what the reference's DressiAD::execStep computes for the graph
@@ -267,6 +268,15 @@ __global__ void k_gpos_adam(SilParams p, SilBuffers b, float omb1, float omb2,
     }
     if (!update) return;
     const float bc1 = b.scalars[1], bc2 = b.scalars[2];
+    if (p.reg) {
+        // g + g_lap * s_lap + g_nrm * s_nrm (run.cpp:419-420)
+        const float sl = b.reg.scale[0], sn = b.reg.scale[1];
+        const float* gl = b.reg.glap + size_t(u) * 3;
+        const float* gn = b.reg.gnrm + size_t(u) * 3;
+        g0 = (g0 + gl[0] * sl) + gn[0] * sn;
+        g1 = (g1 + gl[1] * sl) + gn[1] * sn;
+        g2 = (g2 + gl[2] * sl) + gn[2] * sn;
+    }
     const float g[3] = {g0, g1, g2};
 #pragma unroll
     for (int j = 0; j < 3; j++) {
@@ -319,6 +329,7 @@ void sil_grad_reduce(const SilParams& p, const SilBuffers& b, bool update,
 }
 
 void sil_update(const SilParams& p, const SilBuffers& b, cudaStream_t s) {
+    sil_reg_scale(p, b, s);
     ProfScope ps("adam", s);
     k_gpos_adam<<<(p.n_verts + 255) / 256, 256, 0, s>>>(
             p, b, 1.f - p.b1, 1.f - p.b2, 0, 1);
@@ -328,7 +339,14 @@ void sil_update(const SilParams& p, const SilBuffers& b, cudaStream_t s) {
 void sil_iteration(const SoftDims& d, const SilParams& p, const SilBuffers& b,
                    cudaStream_t s) {
     sil_forward_backward(d, p, b, nullptr, s);
-    sil_grad_reduce(p, b, true, s);
+    if (!p.reg) {
+        sil_grad_reduce(p, b, true, s);
+        return;
+    }
+    // the regulariser needs the whole g before the Adam step
+    sil_grad_reduce(p, b, false, s);
+    sil_reg_terms(p, b, s);
+    sil_update(p, b, s);
 }
 
 }  // namespace dressi

@@ -24,6 +24,14 @@ __all__ = [
     "antialias_grad",
     "texture",
     "texture_grad",
+    "vertex_faces_tex",
+    "vertex_neighbors_tex",
+    "face_neighbors_tex",
+    "vertex_neighbor_mean",
+    "normal_consistency_face_term",
+    "normal_consistency_vertex_grad",
+    "sum_all",
+    "regularized_grad",
     "check_status",
 ]
 
@@ -312,4 +320,143 @@ def texture_grad(gy, inv_uv, uv_screen, filter_mode: str = "nearest"):
            inv_uv.data_ptr(), inv_uv.shape[1], inv_uv.shape[0],
            uv_screen.data_ptr(), _FILTERS[filter_mode], out.data_ptr(),
            _stream())
+    return out
+
+
+# ---- optimizer-side regulariser (examples/silhouette_optimization/
+# run.cpp:407-420) and its mesh tables (mesh_utils.cpp:53-101)
+
+def _host_faces(faces):
+    import numpy as np
+
+    if isinstance(faces, torch.Tensor):
+        faces = faces.detach().cpu().numpy()
+    return np.ascontiguousarray(faces, np.float32).reshape(-1, 3)
+
+
+def _deg_table(fn, faces, n_verts: int, cap: int):
+    import ctypes as C
+
+    import numpy as np
+
+    f = _host_faces(faces)
+    out = np.zeros(cap * n_verts, np.float32)
+    deg = C.c_uint32(0)
+    N.call(fn, f.ctypes.data, f.shape[0], n_verts, cap, out.ctypes.data,
+           C.byref(deg))
+    return out[: deg.value * n_verts].reshape(deg.value, n_verts)
+
+
+def vertex_faces_tex(faces, n_verts: int, cap: int = 64):
+    """VertexFacesTex: host float table {V, max_deg} as [max_deg, V]
+    (incident faces in face order, -1 padding)."""
+    return _deg_table("dressi_vertex_faces_tex", faces, n_verts, cap)
+
+
+def vertex_neighbors_tex(faces, n_verts: int, cap: int = 64):
+    """VertexNeighborsTex: host float table [max_deg, V] (sorted
+    neighbours, -1 padding)."""
+    return _deg_table("dressi_vertex_neighbors_tex", faces, n_verts, cap)
+
+
+def face_neighbors_tex(faces):
+    """FaceNeighborsTex: host float table [F, 3] (-1 padding)."""
+    import numpy as np
+
+    f = _host_faces(faces)
+    out = np.zeros((f.shape[0], 3), np.float32)
+    N.call("dressi_face_neighbors_tex", f.ctypes.data, f.shape[0],
+           out.ctypes.data)
+    return out
+
+
+def vertex_neighbor_mean(pos, nbrs, check: bool = True):
+    """F::VertexNeighborMean: pos [V, 3], nbrs [deg, V] -> [V, 3]."""
+    pos = _dev(pos, "pos", 2)
+    nbrs = _dev(nbrs, "nbrs", 2)
+    out = torch.empty_like(pos)
+    st = _new_status(pos.device)
+    N.call("dressi_vertex_neighbor_mean", pos.data_ptr(), pos.shape[0],
+           nbrs.data_ptr(), nbrs.shape[0], out.data_ptr(), st.data_ptr(),
+           _stream())
+    if check:
+        check_status(st)
+    return out
+
+
+def normal_consistency_face_term(pos, faces, face_adj, check: bool = True):
+    """F::NormalConsistencyFaceTerm: pos [V, 3], faces [F, 3], face_adj
+    [F, 3] -> [F, 3]."""
+    pos = _dev(pos, "pos", 2)
+    faces = _dev(faces, "faces", 2)
+    face_adj = _dev(face_adj, "face_adj", 2)
+    out = torch.empty_like(faces)
+    st = _new_status(pos.device)
+    N.call("dressi_normal_consistency_face_term", pos.data_ptr(),
+           pos.shape[0], faces.data_ptr(), faces.shape[0],
+           face_adj.data_ptr(), out.data_ptr(), st.data_ptr(), _stream())
+    if check:
+        check_status(st)
+    return out
+
+
+def normal_consistency_vertex_grad(term, pos, faces, vtx_faces,
+                                   check: bool = True):
+    """F::NormalConsistencyVertexGrad: term [F, 3], pos [V, 3], faces
+    [F, 3], vtx_faces [deg, V] -> [V, 3]."""
+    term = _dev(term, "term", 2)
+    pos = _dev(pos, "pos", 2)
+    faces = _dev(faces, "faces", 2)
+    vtx_faces = _dev(vtx_faces, "vtx_faces", 2)
+    out = torch.empty_like(pos)
+    st = _new_status(pos.device)
+    N.call("dressi_normal_consistency_vertex_grad", term.data_ptr(),
+           pos.data_ptr(), pos.shape[0], faces.data_ptr(), faces.shape[0],
+           vtx_faces.data_ptr(), vtx_faces.shape[0], out.data_ptr(),
+           st.data_ptr(), _stream())
+    if check:
+        check_status(st)
+    return out
+
+
+def sum_all(x):
+    """F::SumAll of x [N, C] (C 1..4) or [N] -> a 1-element tensor, with
+    the reference's summation order."""
+    x = _dev(x, "x")
+    nc = 1 if x.dim() == 1 else x.shape[-1]
+    out = torch.empty(1, dtype=torch.float32, device=x.device)
+    N.call("dressi_sum_all", x.data_ptr(), x.numel() // nc, nc,
+           out.data_ptr(), _stream())
+    return out
+
+
+def regularized_grad(pos, faces, g, laplacian: float, normal: float,
+                     nbrs=None, face_adj=None, vtx_faces=None,
+                     check: bool = True):
+    """The silhouette optimizer's regularised gradient: g + g_lap (rms(g) /
+    rms(g_lap) laplacian) + g_nrm (rms(g) / rms(g_nrm) normal). The mesh
+    tables are built from faces when not given."""
+    pos = _dev(pos, "pos", 2)
+    faces = _dev(faces, "faces", 2)
+    g = _dev(g, "g", 2)
+    dev = pos.device
+    nv = pos.shape[0]
+    if nbrs is None:
+        nbrs = torch.as_tensor(vertex_neighbors_tex(faces, nv), device=dev)
+    if face_adj is None:
+        face_adj = torch.as_tensor(face_neighbors_tex(faces), device=dev)
+    if vtx_faces is None:
+        vtx_faces = torch.as_tensor(vertex_faces_tex(faces, nv), device=dev)
+    nbrs = _dev(nbrs, "nbrs", 2)
+    face_adj = _dev(face_adj, "face_adj", 2)
+    vtx_faces = _dev(vtx_faces, "vtx_faces", 2)
+    out = torch.empty_like(g)
+    st = _new_status(dev)
+    N.call("dressi_regularized_grad", pos.data_ptr(), nv, faces.data_ptr(),
+           faces.shape[0], nbrs.data_ptr(), nbrs.shape[0],
+           face_adj.data_ptr(), vtx_faces.data_ptr(), vtx_faces.shape[0],
+           g.data_ptr(), float(laplacian), float(normal), out.data_ptr(),
+           st.data_ptr(), _stream())
+    if check:
+        check_status(st)
     return out

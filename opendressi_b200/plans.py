@@ -143,12 +143,16 @@ class Plan:
 
 
 class SilhouettePlan(Plan):
-    """C3/C4 silhouette optimisation of vertex positions (HardSoftRas)."""
+    """C3/C4 silhouette optimisation of vertex positions (HardSoftRas).
+    laplacian / normal: the optimizer-side regulariser weights of the
+    reference example (run.cpp:407-420; its defaults 0.15 / 0.4 here,
+    0.5 / 0.5 for the AA plan); 0 / 0 = none."""
 
     def __init__(self, faces, mvps, n_verts: int, res: int, radius_px: float,
                  sigma: float = 1e-4, lr: float = 1e-3, beta1: float = 0.9,
                  beta2: float = 0.999, eps: float = 1e-8, device: int = 0,
-                 loss_history: int = 4096):
+                 loss_history: int = 4096, laplacian: float = 0.0,
+                 normal: float = 0.0):
         faces = np.ascontiguousarray(faces, np.float32).reshape(-1, 3)
         mvps = np.ascontiguousarray(mvps, np.float32).reshape(-1, 16)
         self.n_verts, self.n_faces = int(n_verts), faces.shape[0]
@@ -163,6 +167,7 @@ class SilhouettePlan(Plan):
         d.mvps = mvps.ctypes.data_as(C.POINTER(C.c_float))
         d.loss_history = loss_history
         d.device = device
+        d.laplacian, d.normal = laplacian, normal
         h = C.c_void_p(0)
         N.call("dressi_silhouette_plan_create", C.byref(d), C.byref(h))
         super().__init__(h, device)
@@ -209,7 +214,8 @@ class AaSilhouettePlan(SilhouettePlan):
     def __init__(self, faces, mvps, n_verts: int, res: int,
                  n_samples: int = 8, lr: float = 1e-3, beta1: float = 0.9,
                  beta2: float = 0.999, eps: float = 1e-8, device: int = 0,
-                 loss_history: int = 4096):
+                 loss_history: int = 4096, laplacian: float = 0.0,
+                 normal: float = 0.0):
         faces = np.ascontiguousarray(faces, np.float32).reshape(-1, 3)
         mvps = np.ascontiguousarray(mvps, np.float32).reshape(-1, 16)
         self.n_verts, self.n_faces = int(n_verts), faces.shape[0]
@@ -225,6 +231,7 @@ class AaSilhouettePlan(SilhouettePlan):
         d.mvps = mvps.ctypes.data_as(C.POINTER(C.c_float))
         d.loss_history = loss_history
         d.device = device
+        d.laplacian, d.normal = laplacian, normal
         h = C.c_void_p(0)
         N.call("dressi_aa_silhouette_plan_create", C.byref(d), C.byref(h))
         Plan.__init__(self, h, device)

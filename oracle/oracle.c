@@ -688,27 +688,82 @@ void orc_adam(float* p, float* m, float* v, float* t, const float* g,
     *t = t_new;
 }
 
+/* Mesh tables + scratch of the optimizer-side regulariser of the silhouette
+ * runs (laplacian = normal = 0: none, the gradient passes unchanged). */
+typedef struct {
+    float *vn, *fa, *vf, *g2;
+    uint32_t vn_deg, vf_deg;
+} reg_state_t;
+
+static void reg_free(reg_state_t* r) {
+    free(r->vn);
+    free(r->fa);
+    free(r->vf);
+    free(r->g2);
+    memset(r, 0, sizeof(*r));
+}
+
+static int reg_init(reg_state_t* r, const float* faces, uint32_t n_faces,
+                    uint32_t n_verts, float laplacian, float normal) {
+    memset(r, 0, sizeof(*r));
+    if (laplacian == 0.f && normal == 0.f) return 0;
+    r->vn = (float*)malloc(sizeof(float) * (size_t)n_verts * 64);
+    r->vf = (float*)malloc(sizeof(float) * (size_t)n_verts * 64);
+    r->fa = (float*)malloc(sizeof(float) * (size_t)n_faces * 3);
+    r->g2 = (float*)malloc(sizeof(float) * (size_t)n_verts * 3);
+    if (!r->vn || !r->vf || !r->fa || !r->g2) {
+        reg_free(r);
+        return fail("oom");
+    }
+    int rc = orc_vertex_neighbors_tex(faces, n_faces, n_verts, 64, r->vn,
+                                      &r->vn_deg);
+    if (!rc) rc = orc_face_neighbors_tex(faces, n_faces, r->fa);
+    if (!rc)
+        rc = orc_vertex_faces_tex(faces, n_faces, n_verts, 64, r->vf,
+                                  &r->vf_deg);
+    if (rc) reg_free(r);
+    return rc;
+}
+
+/* g <- the regularised gradient (run.cpp:407-420), when enabled. */
+static int reg_apply(reg_state_t* r, const float* pos, uint32_t n_verts,
+                     const float* faces, uint32_t n_faces, float laplacian,
+                     float normal, float* g) {
+    if (!r->vn) return 0;
+    const int rc = orc_regularized_grad(pos, n_verts, faces, n_faces, r->vn,
+                                        r->vn_deg, r->fa, r->vf, r->vf_deg, g,
+                                        laplacian, normal, r->g2);
+    if (!rc) memcpy(g, r->g2, sizeof(float) * (size_t)n_verts * 3);
+    return rc;
+}
+
 int orc_silhouette_run(float* pos, uint32_t n_verts, const float* faces,
                        uint32_t n_faces, uint32_t n_views, uint32_t res,
                        float radius, float sigma, float lr, const float* mvps,
                        const float* targets, uint32_t n_iters,
-                       uint32_t threads, float* loss_trace) {
+                       uint32_t threads, float laplacian, float normal,
+                       float* loss_trace) {
     const size_t n = (size_t)n_verts * 3;
     float* m = (float*)calloc(n, sizeof(float));
     float* v = (float*)calloc(n, sizeof(float));
     float* g = (float*)calloc(n, sizeof(float));
     float t = 0.f;
-    int rc = 0;
-    if (!m || !v || !g) rc = fail("oom");
+    reg_state_t reg;
+    int rc = reg_init(&reg, faces, n_faces, n_verts, laplacian, normal);
+    if (!rc && (!m || !v || !g)) rc = fail("oom");
     for (uint32_t it = 0; it < n_iters && !rc; it++) {
         double l = 0.0;
         rc = sil_loss_grad_mt(pos, n_verts, faces, n_faces, n_views, res,
                               radius, sigma, mvps, targets, &l, g, NULL,
                               threads);
+        if (!rc)
+            rc = reg_apply(&reg, pos, n_verts, faces, n_faces, laplacian,
+                           normal, g);
         if (rc) break;
         loss_trace[it] = (float)l;
         orc_adam(pos, m, v, &t, g, (uint32_t)n, lr, 0.9f, 0.999f, 1e-8f);
     }
+    reg_free(&reg);
     free(m);
     free(v);
     free(g);
@@ -1200,24 +1255,30 @@ int orc_aa_silhouette_run(float* pos, uint32_t n_verts, const float* faces,
                           uint32_t max_deg, uint32_t n_views, uint32_t res,
                           uint32_t n_samples, float lr, const float* mvps,
                           const float* targets, uint32_t n_iters,
-                          uint32_t threads, float* loss_trace) {
+                          uint32_t threads, float laplacian, float normal,
+                          float* loss_trace) {
     const size_t n = (size_t)n_verts * 3;
     float* m = (float*)calloc(n, sizeof(float));
     float* v = (float*)calloc(n, sizeof(float));
     float* g = (float*)calloc(n, sizeof(float));
     float t = 0.f;
-    int rc = 0;
-    if (!m || !v || !g) rc = fail("oom");
+    reg_state_t reg;
+    int rc = reg_init(&reg, faces, n_faces, n_verts, laplacian, normal);
+    if (!rc && (!m || !v || !g)) rc = fail("oom");
     for (uint32_t it = 0; it < n_iters && !rc; it++) {
         double l = 0.0;
         /* the in-graph counter (before its update) seeds the sampling */
         rc = orc_aa_silhouette_loss_grad(pos, n_verts, faces, n_faces, vft,
                                          max_deg, n_views, res, n_samples, t,
                                          mvps, targets, threads, &l, g, NULL);
+        if (!rc)
+            rc = reg_apply(&reg, pos, n_verts, faces, n_faces, laplacian,
+                           normal, g);
         if (rc) break;
         loss_trace[it] = (float)l;
         orc_adam(pos, m, v, &t, g, (uint32_t)n, lr, 0.9f, 0.999f, 1e-8f);
     }
+    reg_free(&reg);
     free(m);
     free(v);
     free(g);
@@ -1679,6 +1740,285 @@ int orc_c2_run(float* tex, uint32_t w_tex, uint32_t levels, const float* pos,
     free(v);
     free(g);
     return rc;
+}
+
+/* ------------------------------------------------------- regularisers */
+
+static int cmp_u32(const void* a, const void* b) {
+    const uint32_t x = *(const uint32_t*)a, y = *(const uint32_t*)b;
+    return x < y ? -1 : (x > y ? 1 : 0);
+}
+
+/* VertexNeighborsTex (mesh_utils.cpp:10-28, 73-86): sorted neighbour sets,
+ * {V, max_deg} row d at out[d*V], -1 padding. */
+int orc_vertex_neighbors_tex(const float* faces, uint32_t n_faces,
+                             uint32_t n_verts, uint32_t cap, float* out,
+                             uint32_t* max_deg) {
+    uint32_t* lst = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)n_verts * 64);
+    uint32_t* cnt = (uint32_t*)calloc(n_verts, sizeof(uint32_t));
+    if (!lst || !cnt) {
+        free(lst);
+        free(cnt);
+        return fail("oom");
+    }
+    int rc = 0;
+    for (uint32_t f = 0; f < n_faces && !rc; f++) {
+        uint32_t idx[3];
+        for (int k = 0; k < 3; k++) idx[k] = (uint32_t)faces[(size_t)f * 3 + k];
+        for (int k = 0; k < 3 && !rc; k++) {
+            const uint32_t v = idx[k];
+            if (v >= n_verts) { rc = fail("neighbors: vertex index"); break; }
+            const uint32_t nb[2] = {idx[(k + 1) % 3], idx[(k + 2) % 3]};
+            for (int j = 0; j < 2; j++) {
+                int seen = 0;
+                for (uint32_t i = 0; i < cnt[v]; i++)
+                    if (lst[(size_t)v * 64 + i] == nb[j]) seen = 1;
+                if (!seen) {
+                    if (cnt[v] >= 64) { rc = fail("neighbors: degree > 64"); break; }
+                    lst[(size_t)v * 64 + cnt[v]++] = nb[j];
+                }
+            }
+        }
+    }
+    uint32_t md = 1;
+    for (uint32_t v = 0; v < n_verts && !rc; v++) {
+        qsort(&lst[(size_t)v * 64], cnt[v], sizeof(uint32_t), cmp_u32);
+        if (cnt[v] > md) md = cnt[v];
+    }
+    if (!rc && md > cap) rc = fail("neighbors: capacity %u < %u", cap, md);
+    if (!rc) {
+        for (size_t i = 0; i < (size_t)n_verts * md; i++) out[i] = -1.f;
+        for (uint32_t v = 0; v < n_verts; v++)
+            for (uint32_t d = 0; d < cnt[v]; d++)
+                out[(size_t)d * n_verts + v] = (float)lst[(size_t)v * 64 + d];
+        *max_deg = md;
+    }
+    free(lst);
+    free(cnt);
+    return rc;
+}
+
+typedef struct {
+    uint32_t a, b, f;
+} edge_face_t;
+
+static int cmp_edge_face(const void* x, const void* y) {
+    const edge_face_t* p = (const edge_face_t*)x;
+    const edge_face_t* q = (const edge_face_t*)y;
+    if (p->a != q->a) return p->a < q->a ? -1 : 1;
+    if (p->b != q->b) return p->b < q->b ? -1 : 1;
+    return p->f < q->f ? -1 : (p->f > q->f ? 1 : 0);  /* insertion order */
+}
+
+/* FaceNeighborsTex (mesh_utils.cpp:30-52, 88-101): for each edge (ordered
+ * by (min, max) vertex) every pair of its faces, in face order; each face
+ * keeps its first 3 neighbours. out [F][3], -1 padding. */
+int orc_face_neighbors_tex(const float* faces, uint32_t n_faces, float* out) {
+    edge_face_t* e = (edge_face_t*)malloc(sizeof(edge_face_t) * (size_t)n_faces * 3);
+    uint32_t* n_adj = (uint32_t*)calloc(n_faces, sizeof(uint32_t));
+    if (!e || !n_adj) {
+        free(e);
+        free(n_adj);
+        return fail("oom");
+    }
+    for (uint32_t f = 0; f < n_faces; f++)
+        for (int k = 0; k < 3; k++) {
+            const uint32_t a = (uint32_t)faces[(size_t)f * 3 + k];
+            const uint32_t b = (uint32_t)faces[(size_t)f * 3 + (k + 1) % 3];
+            edge_face_t* t = &e[(size_t)f * 3 + k];
+            t->a = a < b ? a : b;
+            t->b = a < b ? b : a;
+            t->f = f;
+        }
+    qsort(e, (size_t)n_faces * 3, sizeof(edge_face_t), cmp_edge_face);
+    for (size_t i = 0; i < (size_t)n_faces * 3; i++) out[i] = -1.f;
+    size_t i = 0;
+    while (i < (size_t)n_faces * 3) {
+        size_t j = i;
+        while (j < (size_t)n_faces * 3 && e[j].a == e[i].a && e[j].b == e[i].b) j++;
+        for (size_t x = i; x < j; x++)
+            for (size_t y = x + 1; y < j; y++) {
+                const uint32_t pr[2] = {e[x].f, e[y].f};
+                for (int s = 0; s < 2; s++) {
+                    const uint32_t f = pr[s], g = pr[1 - s];
+                    if (n_adj[f] < 3) out[(size_t)f * 3 + n_adj[f]++] = (float)g;
+                }
+            }
+        i = j;
+    }
+    free(e);
+    free(n_adj);
+    return 0;
+}
+
+static void cross_of_face(const float* pos, const float* faces, uint32_t f,
+                          uint32_t idx[3], float c[3]) {
+    for (int k = 0; k < 3; k++)
+        idx[k] = to_u32_via_i64(faces[(size_t)f * 3 + k] + 0.5f);
+    const float* p0 = &pos[(size_t)idx[0] * 3];
+    const float* p1 = &pos[(size_t)idx[1] * 3];
+    const float* p2 = &pos[(size_t)idx[2] * 3];
+    const float e1[3] = {p1[0] - p0[0], p1[1] - p0[1], p1[2] - p0[2]};
+    const float e2[3] = {p2[0] - p0[0], p2[1] - p0[1], p2[2] - p0[2]};
+    c[0] = e1[1] * e2[2] - e1[2] * e2[1];
+    c[1] = e1[2] * e2[0] - e1[0] * e2[2];
+    c[2] = e1[0] * e2[1] - e1[1] * e2[0];
+}
+
+/* SumAll over n floats (f_ops.cpp:1119-1149 with SumPartial 1087-1115):
+ * above 256 elements, 64 strided partial sums in double (each rounded to
+ * float), then their double sum rounded to float. `elems` is the pixel
+ * count, `n` the components per pixel. */
+static float sum_all(const float* x, size_t elems, uint32_t n) {
+    if (elems <= 256) {
+        double s = 0.0;
+        for (size_t i = 0; i < elems * n; i++) s += x[i];
+        return (float)s;
+    }
+    double s = 0.0;
+    for (uint32_t p = 0; p < 64; p++) {
+        double q = 0.0;
+        for (size_t i = p; i < elems; i += 64)
+            for (uint32_t c = 0; c < n; c++) q += x[i * n + c];
+        s += (double)(float)q;
+    }
+    return (float)s;
+}
+
+/* rms(x) = sqrt(SumAll(x * x) * inv_cnt + 1e-24) (run.cpp:410-413) */
+static float reg_rms(const float* x, uint32_t n_verts, float* tmp) {
+    const float inv_cnt = 1.f / (float)(n_verts * 3);
+    for (size_t i = 0; i < (size_t)n_verts * 3; i++) tmp[i] = x[i] * x[i];
+    return sqrtf(sum_all(tmp, n_verts, 3) * inv_cnt + 1e-24f);
+}
+
+/* VertexNeighborMean (f_ops.cpp:1983-2029): the mean of the listed
+ * neighbours in table order; pos itself without neighbours. */
+void orc_vertex_neighbor_mean(const float* pos, uint32_t n_verts,
+                              const float* vnbrs, uint32_t nbr_deg,
+                              float* out) {
+    for (uint32_t v = 0; v < n_verts; v++) {
+        float mean[3] = {0.f, 0.f, 0.f};
+        uint32_t count = 0;
+        for (uint32_t d = 0; d < nbr_deg; d++) {
+            const float nv = vnbrs[(size_t)d * n_verts + v];
+            if (nv < -0.5f) continue;
+            const size_t nb = (size_t)to_u32_via_i64(nv + 0.5f);
+            for (int c = 0; c < 3; c++) mean[c] += pos[nb * 3 + c];
+            count++;
+        }
+        for (int c = 0; c < 3; c++)
+            out[(size_t)v * 3 + c] =
+                    count > 0 ? mean[c] / (float)count : pos[(size_t)v * 3 + c];
+    }
+}
+
+/* NormalConsistencyFaceTerm (f_ops.cpp:2031-2098): per face a (skipped
+ * when |c_a| < 1e-12), the sum over its edge neighbours b (|c_b| >= 1e-12)
+ * of -(n_b - (n_a . n_b) n_a) / |c_a|. */
+void orc_nc_face_term(const float* pos, const float* faces, uint32_t n_faces,
+                      const float* fadj, float* term) {
+    for (uint32_t f = 0; f < n_faces; f++) {
+        uint32_t ia[3];
+        float ca[3];
+        float gg[3] = {0.f, 0.f, 0.f};
+        cross_of_face(pos, faces, f, ia, ca);
+        const float la = sqrtf(ca[0] * ca[0] + ca[1] * ca[1] + ca[2] * ca[2]);
+        if (la >= 1e-12f) {
+            const float na[3] = {ca[0] / la, ca[1] / la, ca[2] / la};
+            for (int j = 0; j < 3; j++) {
+                const float gv = fadj[(size_t)f * 3 + j];
+                if (gv < -0.5f) continue;
+                uint32_t ib[3];
+                float cb[3];
+                cross_of_face(pos, faces, to_u32_via_i64(gv + 0.5f), ib, cb);
+                const float lb =
+                        sqrtf(cb[0] * cb[0] + cb[1] * cb[1] + cb[2] * cb[2]);
+                if (lb < 1e-12f) continue;
+                const float nb[3] = {cb[0] / lb, cb[1] / lb, cb[2] / lb};
+                const float d = na[0] * nb[0] + na[1] * nb[1] + na[2] * nb[2];
+                for (int c = 0; c < 3; c++) gg[c] += -(nb[c] - d * na[c]) / la;
+            }
+        }
+        for (int c = 0; c < 3; c++) term[(size_t)f * 3 + c] = gg[c];
+    }
+}
+
+/* NormalConsistencyVertexGrad (f_ops.cpp:2100-2181): per vertex over its
+ * incident faces in table order, the transpose of the cross product
+ * c = e1 x e2 applied to the face term. */
+void orc_nc_vertex_grad(const float* term, const float* pos, uint32_t n_verts,
+                        const float* faces, const float* vft,
+                        uint32_t vft_deg, float* out) {
+    for (uint32_t v = 0; v < n_verts; v++) {
+        float acc[3] = {0.f, 0.f, 0.f};
+        for (uint32_t d = 0; d < vft_deg; d++) {
+            const float fv = vft[(size_t)d * n_verts + v];
+            if (fv < -0.5f) continue;
+            const uint32_t f = to_u32_via_i64(fv + 0.5f);
+            uint32_t idx[3];
+            for (int k = 0; k < 3; k++)
+                idx[k] = to_u32_via_i64(faces[(size_t)f * 3 + k] + 0.5f);
+            const float* p0 = &pos[(size_t)idx[0] * 3];
+            const float* p1 = &pos[(size_t)idx[1] * 3];
+            const float* p2 = &pos[(size_t)idx[2] * 3];
+            const float e1[3] = {p1[0] - p0[0], p1[1] - p0[1], p1[2] - p0[2]};
+            const float e2[3] = {p2[0] - p0[0], p2[1] - p0[1], p2[2] - p0[2]};
+            const float* t = &term[(size_t)f * 3];
+            const float g1[3] = {e2[1] * t[2] - e2[2] * t[1],
+                                 e2[2] * t[0] - e2[0] * t[2],
+                                 e2[0] * t[1] - e2[1] * t[0]};
+            const float g2[3] = {t[1] * e1[2] - t[2] * e1[1],
+                                 t[2] * e1[0] - t[0] * e1[2],
+                                 t[0] * e1[1] - t[1] * e1[0]};
+            for (int c = 0; c < 3; c++) {
+                if (idx[1] == v) acc[c] += g1[c];
+                if (idx[2] == v) acc[c] += g2[c];
+                if (idx[0] == v) acc[c] -= g1[c] + g2[c];
+            }
+        }
+        for (int c = 0; c < 3; c++) out[(size_t)v * 3 + c] = acc[c];
+    }
+}
+
+float orc_sum_all(const float* x, size_t n_px, uint32_t n_comp) {
+    return sum_all(x, n_px, n_comp);
+}
+
+/* The regularised gradient of the reference's silhouette optimizer
+ * (examples/silhouette_optimization/run.cpp:407-420): g + g_lap *
+ * (rms(g) / rms(g_lap) * laplacian) + g_nrm * (rms(g) / rms(g_nrm) *
+ * normal), g_lap = pos - VertexNeighborMean(pos), g_nrm =
+ * NormalConsistencyVertexGrad(NormalConsistencyFaceTerm(pos)).
+ * vnbrs {V,nbr_deg}, fadj [F][3], vft {V,vft_deg}. */
+int orc_regularized_grad(const float* pos, uint32_t n_verts, const float* faces,
+                         uint32_t n_faces, const float* vnbrs, uint32_t nbr_deg,
+                         const float* fadj, const float* vft, uint32_t vft_deg,
+                         const float* g, float laplacian, float normal,
+                         float* out) {
+    const size_t n3 = (size_t)n_verts * 3;
+    float* glap = (float*)malloc(sizeof(float) * n3);
+    float* gnrm = (float*)malloc(sizeof(float) * n3);
+    float* term = (float*)malloc(sizeof(float) * (size_t)n_faces * 3);
+    float* tmp = (float*)malloc(sizeof(float) * n3);
+    if (!glap || !gnrm || !term || !tmp) {
+        free(glap); free(gnrm); free(term); free(tmp);
+        return fail("oom");
+    }
+    orc_vertex_neighbor_mean(pos, n_verts, vnbrs, nbr_deg, glap);
+    for (size_t i = 0; i < n3; i++) glap[i] = pos[i] - glap[i];
+    orc_nc_face_term(pos, faces, n_faces, fadj, term);
+    orc_nc_vertex_grad(term, pos, n_verts, faces, vft, vft_deg, gnrm);
+    const float data_rms = reg_rms(g, n_verts, tmp);
+    const float s_lap = data_rms / reg_rms(glap, n_verts, tmp) * laplacian;
+    const float s_nrm = data_rms / reg_rms(gnrm, n_verts, tmp) * normal;
+    for (size_t i = 0; i < n3; i++)
+        out[i] = (g[i] + glap[i] * s_lap) + gnrm[i] * s_nrm;
+    free(glap);
+    free(gnrm);
+    free(term);
+    free(tmp);
+    return 0;
 }
 
 /* --------------------------------------------------------- image fitting */

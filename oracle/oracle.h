@@ -92,7 +92,8 @@ int orc_silhouette_run(float* pos, uint32_t n_verts, const float* faces,
                        uint32_t n_faces, uint32_t n_views, uint32_t res,
                        float radius, float sigma, float lr, const float* mvps,
                        const float* targets, uint32_t n_iters,
-                       uint32_t threads, float* loss_trace);
+                       uint32_t threads, float laplacian, float normal,
+                       float* loss_trace);
 
 /* F::AntiAlias forward (f_ops.cpp:2543-2575 over EvalAaPair,
  * cpu_raster.cpp:371-454): img/out W*H*n_comp, tri W*H (face id + 1). */
@@ -145,7 +146,8 @@ int orc_aa_silhouette_run(float* pos, uint32_t n_verts, const float* faces,
                           uint32_t max_deg, uint32_t n_views, uint32_t res,
                           uint32_t n_samples, float lr, const float* mvps,
                           const float* targets, uint32_t n_iters,
-                          uint32_t threads, float* loss_trace);
+                          uint32_t threads, float laplacian, float normal,
+                          float* loss_trace);
 
 /* F::TextureBilinear forward (f_ops.cpp:2767-2778 over BilerpClamp,
  * ibl_math.h:91-115): tex [th][tw][n], uv [npx][2] -> out [npx][n]. */
@@ -198,6 +200,34 @@ int orc_c2_run(float* tex, uint32_t w_tex, uint32_t levels, const float* pos,
                uint32_t n_faces, const float* mvps, uint32_t n_views,
                uint32_t res, const float* targets, float lr, uint32_t n_iters,
                float* loss_trace);
+
+/* Mesh tables of the regularisers: VertexNeighborsTex (mesh_utils.cpp:
+ * 73-86; {V,max_deg} row d at out[d*V]) and FaceNeighborsTex (88-101;
+ * [F][3]); -1 padding. */
+int orc_vertex_neighbors_tex(const float* faces, uint32_t n_faces,
+                             uint32_t n_verts, uint32_t cap, float* out,
+                             uint32_t* max_deg);
+int orc_face_neighbors_tex(const float* faces, uint32_t n_faces, float* out);
+/* The regulariser's ops: VertexNeighborMean (f_ops.cpp:1983-2029),
+ * NormalConsistencyFaceTerm (2031-2098), NormalConsistencyVertexGrad
+ * (2100-2181), SumAll (1119-1149, with SumPartial 1087-1115). */
+void orc_vertex_neighbor_mean(const float* pos, uint32_t n_verts,
+                              const float* vnbrs, uint32_t nbr_deg,
+                              float* out);
+void orc_nc_face_term(const float* pos, const float* faces, uint32_t n_faces,
+                      const float* fadj, float* term);
+void orc_nc_vertex_grad(const float* term, const float* pos, uint32_t n_verts,
+                        const float* faces, const float* vft,
+                        uint32_t vft_deg, float* out);
+float orc_sum_all(const float* x, size_t n_px, uint32_t n_comp);
+/* The silhouette optimizer's regularised gradient (run.cpp:407-420):
+ * out = g + g_lap (rms(g)/rms(g_lap) laplacian) + g_nrm (rms(g)/rms(g_nrm)
+ * normal); pos, g, out [V][3]. */
+int orc_regularized_grad(const float* pos, uint32_t n_verts, const float* faces,
+                         uint32_t n_faces, const float* vnbrs, uint32_t nbr_deg,
+                         const float* fadj, const float* vft, uint32_t vft_deg,
+                         const float* g, float laplacian, float normal,
+                         float* out);
 
 /* 2-D image fitting (C1): loss = Mean((p - t)^2) over W*H*4, Adam on p.
  * loss_trace[n_iters] = loss at the start of each iteration. */

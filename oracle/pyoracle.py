@@ -151,7 +151,7 @@ class Port(_Lib):
         return loss.value, grad, rs
 
     def silhouette_run(self, pos, faces, mvps, targets, res, radius, sigma,
-                       lr, n_iters, threads=1):
+                       lr, n_iters, threads=1, laplacian=0.0, normal=0.0):
         pos = _f32(pos).copy()
         faces, mvps, targets = map(_f32, (faces, mvps, targets))
         trace = np.zeros(n_iters, np.float32)
@@ -159,7 +159,8 @@ class Port(_Lib):
             _fp(pos), _u32(pos.shape[0]), _fp(faces), _u32(faces.shape[0]),
             _u32(mvps.shape[0]), _u32(res), C.c_float(radius),
             C.c_float(sigma), C.c_float(lr), _fp(mvps), _fp(targets),
-            _u32(n_iters), _u32(threads), _fp(trace)), "silhouette_run")
+            _u32(n_iters), _u32(threads), C.c_float(laplacian),
+            C.c_float(normal), _fp(trace)), "silhouette_run")
         return trace, pos
 
     def adam(self, param, m, v, t, grad, lr, b1=0.9, b2=0.999, eps=1e-8):
@@ -249,7 +250,8 @@ class Port(_Lib):
         return loss.value, grad, pred
 
     def aa_silhouette_run(self, pos, faces, vft, mvps, targets, res,
-                          n_samples, lr, n_iters, threads=1):
+                          n_samples, lr, n_iters, threads=1, laplacian=0.0,
+                          normal=0.0):
         pos = _f32(pos).copy()
         faces, vft, mvps, targets = map(_f32, (faces, vft, mvps, targets))
         trace = np.zeros(n_iters, np.float32)
@@ -257,7 +259,8 @@ class Port(_Lib):
             _fp(pos), _u32(pos.shape[0]), _fp(faces), _u32(faces.shape[0]),
             _fp(vft), _u32(vft.shape[0]), _u32(mvps.shape[0]), _u32(res),
             _u32(n_samples), C.c_float(lr), _fp(mvps), _fp(targets),
-            _u32(n_iters), _u32(threads), _fp(trace)), "aa_silhouette_run")
+            _u32(n_iters), _u32(threads), C.c_float(laplacian),
+            C.c_float(normal), _fp(trace)), "aa_silhouette_run")
         return trace, pos
 
     # ---- texturing
@@ -393,6 +396,67 @@ class Port(_Lib):
             _fp(out), C.byref(md)), "vertex_faces_tex")
         return out[: n_verts * md.value].reshape(md.value, n_verts)
 
+    def vertex_neighbors_tex(self, faces, n_verts, cap=64):
+        faces = _f32(faces)
+        out = np.zeros(n_verts * cap, np.float32)
+        md = _u32(0)
+        self._err(self.lib.orc_vertex_neighbors_tex(
+            _fp(faces), _u32(faces.shape[0]), _u32(n_verts), _u32(cap),
+            _fp(out), C.byref(md)), "vertex_neighbors_tex")
+        return out[: n_verts * md.value].reshape(md.value, n_verts)
+
+    def face_neighbors_tex(self, faces):
+        faces = _f32(faces)
+        out = np.zeros((faces.shape[0], 3), np.float32)
+        self._err(self.lib.orc_face_neighbors_tex(
+            _fp(faces), _u32(faces.shape[0]), _fp(out)), "face_neighbors_tex")
+        return out
+
+    def vertex_neighbor_mean(self, pos, vnbrs):
+        pos, vnbrs = _f32(pos), _f32(vnbrs)
+        out = np.zeros_like(pos)
+        self.lib.orc_vertex_neighbor_mean(_fp(pos), _u32(pos.shape[0]),
+                                          _fp(vnbrs), _u32(vnbrs.shape[0]),
+                                          _fp(out))
+        return out
+
+    def nc_face_term(self, pos, faces, fadj):
+        pos, faces, fadj = map(_f32, (pos, faces, fadj))
+        out = np.zeros((faces.shape[0], 3), np.float32)
+        self.lib.orc_nc_face_term(_fp(pos), _fp(faces), _u32(faces.shape[0]),
+                                  _fp(fadj), _fp(out))
+        return out
+
+    def nc_vertex_grad(self, term, pos, faces, vft):
+        term, pos, faces, vft = map(_f32, (term, pos, faces, vft))
+        out = np.zeros_like(pos)
+        self.lib.orc_nc_vertex_grad(_fp(term), _fp(pos), _u32(pos.shape[0]),
+                                    _fp(faces), _fp(vft), _u32(vft.shape[0]),
+                                    _fp(out))
+        return out
+
+    def sum_all(self, x):
+        x = _f32(x)
+        nc = 1 if x.ndim == 1 else x.shape[-1]
+        self.lib.orc_sum_all.restype = C.c_float
+        return np.float32(self.lib.orc_sum_all(_fp(x), C.c_size_t(x.size // nc),
+                                               _u32(nc)))
+
+    def regularized_grad(self, pos, faces, g, laplacian, normal, vnbrs=None,
+                         fadj=None, vft=None):
+        pos, faces, g = _f32(pos), _f32(faces), _f32(g)
+        nv = pos.shape[0]
+        vnbrs = self.vertex_neighbors_tex(faces, nv) if vnbrs is None else vnbrs
+        fadj = self.face_neighbors_tex(faces) if fadj is None else fadj
+        vft = self.vertex_faces_tex(faces, nv) if vft is None else vft
+        out = np.zeros_like(pos)
+        self._err(self.lib.orc_regularized_grad(
+            _fp(pos), _u32(nv), _fp(faces), _u32(faces.shape[0]),
+            _fp(_f32(vnbrs)), _u32(vnbrs.shape[0]), _fp(_f32(fadj)),
+            _fp(_f32(vft)), _u32(vft.shape[0]), _fp(g), C.c_float(laplacian),
+            C.c_float(normal), _fp(out)), "regularized_grad")
+        return out
+
 
 class Ref(_Lib):
     """_ref/libdressi_ref.so -- the reference CPU implementation."""
@@ -458,7 +522,8 @@ class Ref(_Lib):
         return grad, rs
 
     def silhouette_run(self, pos, faces, vft, mvps, targets, res, radius,
-                       sigma, lr, n_iters, threads=1, want_grad0=False):
+                       sigma, lr, n_iters, threads=1, want_grad0=False,
+                       laplacian=0.0, normal=0.0):
         pos, faces, vft, mvps, targets = map(_f32, (pos, faces, vft, mvps,
                                                     targets))
         trace = np.zeros(n_iters, np.float32)
@@ -469,8 +534,9 @@ class Ref(_Lib):
             _u32(pos.shape[0]), _u32(faces.shape[0]), _u32(mvps.shape[0]),
             _u32(res), C.c_float(radius), C.c_float(sigma), C.c_float(lr),
             _fp(pos), _fp(faces), _fp(vft), _u32(vft.shape[0]), _fp(mvps),
-            _fp(targets), _u32(n_iters), _u32(threads), _fp(trace),
-            _fp(pos_out), _fp(grad0), C.byref(secs)), "silhouette_run")
+            _fp(targets), _u32(n_iters), _u32(threads), C.c_float(laplacian),
+            C.c_float(normal), _fp(trace), _fp(pos_out), _fp(grad0),
+            C.byref(secs)), "silhouette_run")
         return trace, pos_out, grad0, secs.value
 
     def antialias(self, img, tri, clip, faces, vft, seed=0.0, n_samples=0,
@@ -511,7 +577,7 @@ class Ref(_Lib):
 
     def aa_silhouette_run(self, pos, faces, vft, mvps, targets, res,
                           n_samples, lr, n_iters, threads=1,
-                          want_grad0=False):
+                          want_grad0=False, laplacian=0.0, normal=0.0):
         pos, faces, vft, mvps, targets = map(_f32, (pos, faces, vft, mvps,
                                                     targets))
         trace = np.zeros(n_iters, np.float32)
@@ -522,8 +588,9 @@ class Ref(_Lib):
             _u32(pos.shape[0]), _u32(faces.shape[0]), _u32(mvps.shape[0]),
             _u32(res), _u32(n_samples), C.c_float(lr), _fp(pos), _fp(faces),
             _fp(vft), _u32(vft.shape[0]), _fp(mvps), _fp(targets),
-            _u32(n_iters), _u32(threads), _fp(trace), _fp(pos_out),
-            _fp(grad0), C.byref(secs)), "aa_silhouette_run")
+            _u32(n_iters), _u32(threads), C.c_float(laplacian),
+            C.c_float(normal), _fp(trace), _fp(pos_out), _fp(grad0),
+            C.byref(secs)), "aa_silhouette_run")
         return trace, pos_out, grad0, secs.value
 
     def image_fit_run(self, param, target, lr, n_iters):
@@ -546,6 +613,35 @@ class Ref(_Lib):
             _fp(faces), _u32(faces.shape[0]), _u32(n_verts), _u32(cap),
             _fp(out), C.byref(md)), "vertex_faces_tex")
         return out[: n_verts * md.value].reshape(md.value, n_verts)
+
+    def mesh_tables(self, faces, n_verts, cap=64):
+        """(vertex neighbours {max_deg, V}, face neighbours [F, 3]) from the
+        reference's own builders."""
+        faces = _f32(faces)
+        vn = np.zeros(n_verts * cap, np.float32)
+        fa = np.zeros((faces.shape[0], 3), np.float32)
+        md = _u32(0)
+        self._err(self.lib.ref_mesh_tables(
+            _fp(faces), _u32(faces.shape[0]), _u32(n_verts), _u32(cap),
+            _fp(vn), C.byref(md), _fp(fa)), "mesh_tables")
+        return vn[: n_verts * md.value].reshape(md.value, n_verts), fa
+
+    def sum_all(self, x):
+        x = _f32(x)
+        nc = 1 if x.ndim == 1 else x.shape[-1]
+        out = C.c_float(0.0)
+        self._err(self.lib.ref_sum_all(_fp(x), _u32(x.size // nc), _u32(nc),
+                                       C.byref(out)), "sum_all")
+        return np.float32(out.value)
+
+    def regularized_grad(self, pos, faces, g, laplacian, normal):
+        pos, faces, g = _f32(pos), _f32(faces), _f32(g)
+        out = np.zeros_like(pos)
+        self._err(self.lib.ref_regularized_grad(
+            _fp(pos), _u32(pos.shape[0]), _fp(faces), _u32(faces.shape[0]),
+            _fp(g), C.c_float(laplacian), C.c_float(normal), _fp(out)),
+            "regularized_grad")
+        return out
 
 
 def soft_inputs(n_faces: int):

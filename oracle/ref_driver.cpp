@@ -18,6 +18,7 @@
 #include <cstdint>
 #include <cstring>
 #include <exception>
+#include <memory>
 #include <string>
 #include <thread>
 #include <vector>
@@ -67,6 +68,75 @@ Variable ClipOf(const Variable& pos, const float* m) {
     };
     return F::Vec4(row(0), row(1), row(2), row(3));
 }
+
+// The optimizer-side regulariser of examples/silhouette_optimization/
+// run.cpp:407-420 on graph leaves, with its mesh tables built by the
+// reference's own helpers (mesh_utils.cpp:53-101):
+//   out = g + g_lap * (rms(g) / rms(g_lap) * laplacian)
+//           + g_nrm * (rms(g) / rms(g_nrm) * normal)
+struct RegGraph {
+    uint32_t n_verts = 0;
+    float laplacian = 0.f, normal = 0.f;
+    Variable faces, vnb, vfa, vvf;
+    CpuTensor t_faces, t_vnb, t_vfa, t_vvf;
+
+    RegGraph(const float* faces_f, uint32_t n_faces, uint32_t nv, float lap,
+             float nrm)
+        : n_verts(nv), laplacian(lap), normal(nrm) {
+        CpuImage fimg(n_faces, 1, 3);
+        std::copy(faces_f, faces_f + size_t(n_faces) * 3, fimg.data.begin());
+        const CpuImage vn = VertexNeighborsTex(fimg, nv);
+        const CpuImage fa = FaceNeighborsTex(fimg);
+        const CpuImage vf = VertexFacesTex(fimg, nv);
+        faces = Variable(VEC3, {n_faces, 1});
+        vnb = Variable(FLOAT, {nv, vn.height});
+        vfa = Variable(VEC3, {n_faces, 1});
+        vvf = Variable(FLOAT, {nv, vf.height});
+        t_faces = Tensor(VEC3, {n_faces, 1}, faces_f);
+        t_vnb = Tensor(FLOAT, {nv, vn.height}, vn.data.data());
+        t_vfa = Tensor(VEC3, {n_faces, 1}, fa.data.data());
+        t_vvf = Tensor(FLOAT, {nv, vf.height}, vf.data.data());
+    }
+    Variable Apply(const Variable& pos, const Variable& g) const {
+        const float inv_cnt = 1.f / float(n_verts * 3);
+        const auto rms = [&](const Variable& x) {
+            return F::Sqrt(F::SumAll(x * x) * inv_cnt + 1e-24f);
+        };
+        Variable data_rms = rms(g);
+        Variable g_lap = pos - F::VertexNeighborMean(pos, vnb);
+        Variable g_nrm = F::NormalConsistencyVertexGrad(
+                F::NormalConsistencyFaceTerm(pos, faces, vfa), pos, faces,
+                vvf);
+        return g + g_lap * (data_rms / rms(g_lap) * laplacian) +
+               g_nrm * (data_rms / rms(g_nrm) * normal);
+    }
+    void Bind(CpuEvaluator& ev) const {
+        ev.bind(faces, t_faces);
+        ev.bind(vnb, t_vnb);
+        ev.bind(vfa, t_vfa);
+        ev.bind(vvf, t_vvf);
+    }
+};
+
+// Host-side form for the view-parallel drivers: g <- Apply(pos, g).
+struct RegStep {
+    RegGraph rg;
+    Variable pos, g, out;
+    RegStep(const float* faces_f, uint32_t n_faces, uint32_t nv, float lap,
+            float nrm)
+        : rg(faces_f, n_faces, nv, lap, nrm),
+          pos(VEC3, {nv, 1}),
+          g(VEC3, {nv, 1}) {
+        out = rg.Apply(pos, g);
+    }
+    void Run(const std::vector<float>& p, std::vector<float>& grad) const {
+        CpuEvaluator ev;
+        rg.Bind(ev);
+        ev.bind(pos, Tensor(VEC3, {rg.n_verts, 1}, p.data()));
+        ev.bind(g, Tensor(VEC3, {rg.n_verts, 1}, grad.data()));
+        grad = ev.eval(out).data;
+    }
+};
 
 struct SilInputs {
     uint32_t n_verts, n_faces, res, max_deg;
@@ -251,10 +321,12 @@ int ref_silhouette_run(uint32_t n_verts, uint32_t n_faces, uint32_t n_views,
                        const float* pos0, const float* faces,
                        const float* vft, uint32_t max_deg,
                        const float* mvps, const float* targets,
-                       uint32_t n_iters, uint32_t threads, float* loss_trace,
-                       float* pos_out, float* grad0, double* seconds) {
+                       uint32_t n_iters, uint32_t threads, float laplacian,
+                       float normal, float* loss_trace, float* pos_out,
+                       float* grad0, double* seconds) {
     return Guard([&] {
         SilInputs in{n_verts, n_faces, res, max_deg, radius_px, sigma};
+        const bool reg = laplacian != 0.f || normal != 0.f;
         const float b1 = 0.9f, b2 = 0.999f, eps = 1e-8f;
         std::vector<float> face_id(size_t(n_faces) * 3),
                 faces_soft(size_t(n_faces) * 3);
@@ -302,7 +374,12 @@ int ref_silhouette_run(uint32_t n_verts, uint32_t n_faces, uint32_t n_views,
             auto [xs, gxs] = BuildBackward(loss);
             DRESSI_CHECK(xs.size() == 1 && xs[0] == vpos,
                          "expected pos as the only gradient leaf");
-            Variable gp = gxs[0];
+            Variable gdata = gxs[0];
+            std::unique_ptr<RegGraph> rg;
+            if (reg)
+                rg = std::make_unique<RegGraph>(faces, n_faces, n_verts,
+                                                laplacian, normal);
+            Variable gp = rg ? rg->Apply(vpos, gdata) : gdata;
             Variable t_new = at + 1.f;
             Variable m_new = am * b1 + gp * (1.f - b1);
             Variable v_new = av * b2 + gp * gp * (1.f - b2);
@@ -317,6 +394,7 @@ int ref_silhouette_run(uint32_t n_verts, uint32_t n_faces, uint32_t n_views,
             for (uint32_t it = 0; it < n_iters; it++) {
                 CpuEvaluator ev;
                 bind_static(ev, g);
+                if (rg) rg->Bind(ev);
                 for (uint32_t v = 0; v < n_views; v++) {
                     ev.bind(g.targets[v],
                             Tensor(FLOAT, {res, res}, targets + v * px));
@@ -326,7 +404,7 @@ int ref_silhouette_run(uint32_t n_verts, uint32_t n_faces, uint32_t n_views,
                 ev.bind(av, tv);
                 ev.bind(at, Tensor(FLOAT, {1, 1}, &tt));
                 loss_trace[it] = float(SumAll(ev.eval(loss)));
-                if (it == 0 && grad0) CopyOut(ev.eval(gp), grad0);
+                if (it == 0 && grad0) CopyOut(ev.eval(gdata), grad0);
                 CpuTensor np = ev.eval(pos_new);
                 tm = ev.eval(m_new);
                 tv = ev.eval(v_new);
@@ -355,6 +433,10 @@ int ref_silhouette_run(uint32_t n_verts, uint32_t n_faces, uint32_t n_views,
             float t = 0.f;
             std::vector<std::vector<float>> grads(n_views);
             std::vector<double> vloss(n_views);
+            std::unique_ptr<RegStep> rstep;
+            if (reg)
+                rstep = std::make_unique<RegStep>(faces, n_faces, n_verts,
+                                                  laplacian, normal);
             for (uint32_t it = 0; it < n_iters; it++) {
                 std::atomic<uint32_t> next{0};
                 std::vector<std::string> errs(threads);
@@ -387,6 +469,7 @@ int ref_silhouette_run(uint32_t n_verts, uint32_t n_faces, uint32_t n_views,
                     for (size_t i = 0; i < g.size(); i++) g[i] += grads[v][i];
                 }
                 if (it == 0 && grad0) std::copy(g.begin(), g.end(), grad0);
+                if (rstep) rstep->Run(pos, g);
                 t = t + 1.f;
                 const float bc1 = 1.f - std::pow(b1, t);
                 const float bc2 = 1.f - std::pow(b2, t);
@@ -477,10 +560,14 @@ int ref_aa_silhouette_run(uint32_t n_verts, uint32_t n_faces, uint32_t n_views,
                           const float* vft, uint32_t max_deg,
                           const float* mvps, const float* targets,
                           uint32_t n_iters, uint32_t threads,
-                          float* loss_trace, float* pos_out, float* grad0,
-                          double* seconds) {
+                          float laplacian, float normal, float* loss_trace,
+                          float* pos_out, float* grad0, double* seconds) {
     return Guard([&] {
         const float b1 = 0.9f, b2 = 0.999f, eps = 1e-8f;
+        std::unique_ptr<RegStep> rstep;
+        if (laplacian != 0.f || normal != 0.f)
+            rstep = std::make_unique<RegStep>(faces, n_faces, n_verts,
+                                              laplacian, normal);
         const size_t px = size_t(res) * res;
         CpuTensor t_faces = Tensor(VEC3, {n_faces, 1}, faces);
         CpuTensor t_faces_i = t_faces;
@@ -581,6 +668,7 @@ int ref_aa_silhouette_run(uint32_t n_verts, uint32_t n_faces, uint32_t n_views,
             for (uint32_t v = 0; v < n_graphs; v++)
                 for (size_t i = 0; i < g.size(); i++) g[i] += grads[v][i];
             if (it == 0 && grad0) std::copy(g.begin(), g.end(), grad0);
+            if (rstep) rstep->Run(pos, g);
             t = t + 1.f;
             const float bc1 = 1.f - std::pow(b1, t);
             const float bc2 = 1.f - std::pow(b2, t);
@@ -623,6 +711,54 @@ int ref_texture_bilinear(const float* tex, uint32_t tw, uint32_t th,
         for (size_t i = 0; i < xs.size(); i++) {
             if (xs[i] == vtex) CopyOut(ev.eval(gxs[i]), out_grad);
         }
+    });
+}
+
+// Mesh tables of the regularisers built by the reference's own helpers
+// (mesh_utils.cpp:73-101): vnbrs {V,max_deg} (row-major, -1 padding; cap
+// floats per row limit) and fadj [F][3].
+int ref_mesh_tables(const float* faces, uint32_t n_faces, uint32_t n_verts,
+                    uint32_t cap, float* vnbrs, uint32_t* nbr_deg,
+                    float* fadj) {
+    return Guard([&] {
+        CpuImage fimg(n_faces, 1, 3);
+        std::copy(faces, faces + size_t(n_faces) * 3, fimg.data.begin());
+        const CpuImage vn = VertexNeighborsTex(fimg, n_verts);
+        DRESSI_CHECK(vn.height <= cap, "capacity too small");
+        *nbr_deg = vn.height;
+        std::copy(vn.data.begin(), vn.data.end(), vnbrs);
+        const CpuImage fa = FaceNeighborsTex(fimg);
+        std::copy(fa.data.begin(), fa.data.end(), fadj);
+    });
+}
+
+// The regularised gradient of examples/silhouette_optimization/
+// run.cpp:407-420 built with the reference's ops and evaluated by its CPU
+// evaluator: out = g + g_lap * (rms(g) / rms(g_lap) * laplacian) + g_nrm *
+// (rms(g) / rms(g_nrm) * normal).
+int ref_regularized_grad(const float* pos, uint32_t n_verts, const float* faces,
+                         uint32_t n_faces, const float* g, float laplacian,
+                         float normal, float* out) {
+    return Guard([&] {
+        RegStep rs(faces, n_faces, n_verts, laplacian, normal);
+        std::vector<float> p(pos, pos + size_t(n_verts) * 3);
+        std::vector<float> gr(g, g + size_t(n_verts) * 3);
+        rs.Run(p, gr);
+        std::copy(gr.begin(), gr.end(), out);
+    });
+}
+
+// F::SumAll of x {n_px, 1} with n_comp components (f_ops.cpp:1119-1149).
+int ref_sum_all(const float* x, uint32_t n_px, uint32_t n_comp, float* out) {
+    return Guard([&] {
+        const VType vt = n_comp == 1   ? FLOAT
+                         : n_comp == 2 ? VEC2
+                         : n_comp == 3 ? VEC3
+                                       : VEC4;
+        Variable vx(vt, {n_px, 1});
+        CpuEvaluator ev;
+        ev.bind(vx, Tensor(vt, {n_px, 1}, x));
+        *out = ev.eval(F::SumAll(vx)).data[0];
     });
 }
 

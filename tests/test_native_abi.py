@@ -60,3 +60,35 @@ def test_last_error_truncates():
     buf = C.create_string_buffer(5)
     full = lib.dressi_last_error(buf, 5)
     assert full > 4 and len(buf.value) == 4
+
+
+def test_mesh_tables_host_builders_match_oracle(port):
+    """The library's VertexFacesTex / VertexNeighborsTex / FaceNeighborsTex
+    (host code, no GPU) equal the C restatement, itself pinned to the
+    reference's builders."""
+    import numpy as np
+
+    from opendressi_b200 import ops, scene
+
+    cases = []
+    for lvl in (1, 3):
+        sc = scene.silhouette_scene(level=lvl, n_views=1, res=16, seed=1)
+        cases.append((sc.faces_f, sc.n_verts))
+    for seed in (0, 1):
+        rng = np.random.default_rng(seed)
+        nv = int(rng.integers(8, 300))
+        f = rng.integers(0, nv, (int(rng.integers(4, 600)), 3))
+        f = f[(f[:, 0] != f[:, 1]) & (f[:, 1] != f[:, 2]) &
+              (f[:, 0] != f[:, 2])]
+        cases.append((f.astype(np.float32), nv))
+    for f, nv in cases:
+        assert np.array_equal(ops.vertex_faces_tex(f, nv),
+                              port.vertex_faces_tex(f, nv))
+        assert np.array_equal(ops.vertex_neighbors_tex(f, nv),
+                              port.vertex_neighbors_tex(f, nv))
+        assert np.array_equal(ops.face_neighbors_tex(f),
+                              port.face_neighbors_tex(f))
+    with pytest.raises(N.DressiError, match="out of range"):
+        ops.vertex_faces_tex(np.array([[0, 1, 5]], np.float32), 3)
+    with pytest.raises(N.DressiError, match="above cap"):
+        ops.vertex_neighbors_tex(cases[1][0], cases[1][1], cap=3)
