@@ -131,7 +131,7 @@ void carve_reg(Arena& a, const SilParams& p, const RegTables& t,
     r->term = a.take<float>(F * 3);
     r->glap = a.take<float>(V * 3);
     r->gnrm = a.take<float>(V * 3);
-    r->scale = a.take<float>(2);
+    r->rms = a.take<float>(3);
 }
 
 void upload_reg(const RegTables& t, const RegBuffers& r) {
@@ -902,18 +902,19 @@ int dressi_regularized_grad(const float* pos, uint32_t n_verts,
         DRESSI_REQUIRE(n_verts > 0, "regularized_grad: no vertices");
         cudaStream_t s = as_stream(stream);
         const size_t V3 = size_t(n_verts) * 3, F3 = size_t(n_faces) * 3;
-        AsyncScratch sc((F3 + 2 * V3 + 2) * sizeof(float), s);
+        AsyncScratch sc((F3 + 2 * V3 + 3) * sizeof(float), s);
         float* term = static_cast<float*>(sc.p);
         float* glap = term + F3;
         float* gnrm = glap + V3;
-        float* scale = gnrm + V3;
+        float* rms = gnrm + V3;
         nc_face_term_op(pos, int(n_verts), faces, face_adj, int(n_faces), term,
                         status, s);
         vertex_terms_op(pos, int(n_verts), nbrs, int(nbr_deg), true, glap,
                         term, faces, int(n_faces), vtx_faces, int(vf_deg),
                         gnrm, status, s);
-        reg_scale_op(g, glap, gnrm, int(n_verts), laplacian, normal, scale, s);
-        reg_combine_op(g, glap, gnrm, scale, int(V3), out, s);
+        reg_rms_op(g, glap, gnrm, int(n_verts), rms, s);
+        reg_combine_op(g, glap, gnrm, rms, laplacian, normal, int(n_verts),
+                       out, s);
     });
 }
 

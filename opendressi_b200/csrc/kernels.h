@@ -57,7 +57,7 @@ struct SoftBuffers {
     FixedBins1 bin1{};         // sweep-1 bins per 16x16 tile
     FixedBins bin2{};          // rim-phase bins per 8x4 block
     int2* state = nullptr;     // packed survivors [views * W * H]
-    int* active = nullptr;     // open-block mask per tile [views * n_tiles]
+    uint8_t* active = nullptr; // open flag per 8x4 block [views*n_tiles*8]
     int* rim = nullptr;        // rim-possible flags [views * rim_cells]
     uint32_t* status = nullptr;
 };
@@ -158,7 +158,7 @@ struct RegBuffers {
     float* term;     // [F][3] NormalConsistencyFaceTerm
     float* glap;     // [V][3] pos - VertexNeighborMean
     float* gnrm;     // [V][3] NormalConsistencyVertexGrad
-    float* scale;    // [2] s_lap, s_nrm
+    float* rms;      // [3] rms(g), rms(g_lap), rms(g_nrm)
 };
 struct SilBuffers {
     float* pos;       // [V*3]
@@ -223,13 +223,13 @@ void vertex_terms_op(const float* pos, int n_verts, const float* nbrs,
                      const float* vf, int vf_deg, float* nrm_out,
                      uint32_t* status, cudaStream_t s);
 void sum_all_op(const float* x, int n_px, int nc, float* out, cudaStream_t s);
-// scale = {rms(g)/rms(glap)*laplacian, rms(g)/rms(gnrm)*normal}; out =
-// (g + glap*scale[0]) + gnrm*scale[1] over n floats.
-void reg_scale_op(const float* g, const float* glap, const float* gnrm,
-                  int n_verts, float laplacian, float normal, float* scale,
-                  cudaStream_t s);
+// rms = {rms(g), rms(glap), rms(gnrm)} over [n_verts][3] each; out =
+// (g + glap s_lap) + gnrm s_nrm, s = rms[0] / rms[1 | 2] * weight.
+void reg_rms_op(const float* g, const float* glap, const float* gnrm,
+                int n_verts, float* rms, cudaStream_t s);
 void reg_combine_op(const float* g, const float* glap, const float* gnrm,
-                    const float* scale, int n, float* out, cudaStream_t s);
+                    const float* rms, float laplacian, float normal,
+                    int n_verts, float* out, cudaStream_t s);
 // One full single-device iteration.
 void sil_iteration(const SoftDims& d, const SilParams& p,
                    const SilBuffers& b, cudaStream_t s);

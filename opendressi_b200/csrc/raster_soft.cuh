@@ -563,7 +563,9 @@ struct FixedBins1 {
     int* parked_n;                    // [1] overflowed tiles left to finish
     int* parked;                      // [views * tiles] their global bins
 };
-constexpr int kSortMax = 256;    // longest sweep-1 list sorted per tile
+constexpr int kSortMax = 256;    // keys gathered per round by k_sweep1_spill
+constexpr int kWarpSort = 128;   // longest per-warp sweep-1 list sorted
+constexpr int kWarpRecs = 16;    // records staged per warp and round
 constexpr int kSpillBlocks = 296;  // grid of k_sweep1_spill (2 per SM)
 static_assert(kSortMax >= kTileThreads, "spill gathers need blockDim keys");
 
@@ -777,19 +779,14 @@ template <class Epi>
 __device__ __forceinline__ void sweep1_finish(const SweepArgs& a, size_t bin,
                                               int x, int y, bool in,
                                               const Survivor& s, int2* state,
-                                              int* mask_out, int* warp_open,
+                                              uint8_t* active,
                                               const FixedBins& b2, Epi& epi) {
     const int w = threadIdx.x >> 5;
     const int cell = (y / kRimCell) * a.rim_cells_x + (x / kRimCell);
-    const unsigned ob = __ballot_sync(0xffffffffu, in && s.depth > 0.5f &&
-                                                           a.rim[cell] != 0);
-    if ((threadIdx.x & 31) == 0) warp_open[w] = ob != 0u;
-    __syncthreads();
-    int m = 0;
-#pragma unroll
-    for (int k = 0; k < 8; k++) m |= warp_open[k] << k;
-    if (threadIdx.x == 0) mask_out[bin] = m;
-    if ((m >> w) & 1) {
+    const bool open = __ballot_sync(0xffffffffu, in && s.depth > 0.5f &&
+                                                         a.rim[cell] != 0) != 0u;
+    if ((threadIdx.x & 31) == 0) active[bin * 8 + w] = open ? 1 : 0;
+    if (open) {
         // open block: survivors stored, the block queued for the rim phase
         if (in) state[size_t(a.v) * a.W * a.H + size_t(y) * a.W + x] = pack(s);
         if ((threadIdx.x & 31) == 0)
@@ -799,25 +796,69 @@ __device__ __forceinline__ void sweep1_finish(const SweepArgs& a, size_t bin,
     }
 }
 
-// Sweep 1 over the tile's bin: inside and boundary fragments are folded;
-// far (rim) fragments are left to the rim phase. At the end each warp (an
-// 8x4-pixel block) reports whether it still holds an open pixel
-// (depth > 0.5) inside some face's soft reach. Tiles without such blocks
-// finish here through the epilogue; the others store their survivors and
-// the open-block mask for the rim phase. A tile whose bin overflowed folds
-// the entries it holds and is parked for k_sweep1_spill (this kernel keeps
-// no spill code: compiled in, it slowed the common path).
+// Ascending bitonic sort of n <= kWarpSort keys in a warp's shared buffer
+// (padded with ~0 to a power of two), by the warp alone.
+__device__ __forceinline__ void warp_sort_smem(unsigned long long* k, int n) {
+    const int lane = threadIdx.x & 31;
+    int p = 64;
+    while (p < n) p <<= 1;
+    for (int i = n + lane; i < p; i += 32) k[i] = ~0ull;
+    __syncwarp();
+    for (int size = 2; size <= p; size <<= 1) {
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            for (int i = lane; i < p; i += 32) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long a = k[i], b = k[ixj];
+                    const bool up = (i & size) == 0;
+                    if (up ? a > b : a < b) {
+                        k[i] = b;
+                        k[ixj] = a;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
+// Stages the records of keys[0, n) (n <= kWarpRecs) into the warp's shared
+// slots: lane l copies 16-byte word l % 12 of record l / 12, ... .
+__device__ __forceinline__ void stage_records(const FaceRec* recs,
+                                              const unsigned long long* keys,
+                                              int n, FaceRec* dst_recs) {
+    const int lane = threadIdx.x & 31;
+    const float4* src = reinterpret_cast<const float4*>(recs);
+    float4* dst = reinterpret_cast<float4*>(dst_recs);
+    for (int i = lane; i < n * kRecVec4; i += 32) {
+        const int j = i / kRecVec4, q = i - j * kRecVec4;
+        const int f = int(uint32_t(keys[j])) >> 8;
+        dst[i] = src[size_t(f) * kRecVec4 + q];
+    }
+    __syncwarp();
+}
+
+// Sweep 1 over the tile's bin, one 8x4-pixel block per warp and every warp
+// on its own (no block barrier): the warp keeps the list entries whose
+// block mask has its bit, sorts them front to back (up to kWarpSort) and
+// folds inside and boundary fragments; far (rim) fragments are left to the
+// rim phase. A block still holding an open pixel (depth > 0.5) inside some
+// face's soft reach stores its survivors and is queued for the rim phase;
+// the others finish here through the epilogue. A tile whose bin overflowed
+// folds the entries it holds, stores its survivors and is parked for
+// k_sweep1_spill (this kernel keeps no spill code: compiled in, it slowed
+// the common path). The bin's cursor is reset by k_rim_bin.
 template <class Epi>
 static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
                                    const FixedBins& b2, int tile, int2* state,
-                                   int* mask_out, Epi& epi) {
-    __shared__ FaceRec sh[kRecChunk];
-    __shared__ unsigned long long keys[kSortMax];
-    __shared__ int warp_open[8];
-    __shared__ int n_entries;
+                                   uint8_t* active, Epi& epi) {
+    __shared__ FaceRec sh_all[8][kWarpRecs];
+    __shared__ unsigned long long keys_all[8][kWarpSort];
     int x, y;
     tile_xy(tile, a.tiles_x, &x, &y);
-    const int w = threadIdx.x >> 5;
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    FaceRec* sh = sh_all[w];
+    unsigned long long* keys = keys_all[w];
     const bool in = x < a.W && y < a.H;
     const float px = float(x) + 0.5f, py = float(y) + 0.5f;
     const size_t pix = size_t(y) * a.W + x;
@@ -825,12 +866,7 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
     const float prev = (in && peel) ? a.prev[pix] : 0.f;
     const bool fast_ok = a.radius < kMaxFastRadius;
     const size_t bin = size_t(a.v) * a.n_tiles + tile;
-    if (threadIdx.x == 0) {
-        n_entries = b1.cursor[bin];
-        b1.cursor[bin] = 0;  // ready for the next use
-    }
-    __syncthreads();
-    const int nent = n_entries;
+    const int nent = b1.cursor[bin];
     // overflow: the own list's entries are folded here, the tile is then
     // parked for k_sweep1_spill (spilled entries, or all faces)
     const bool over = nent > b1.cap;
@@ -841,58 +877,73 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
     }
     const int end = over ? b1.cap : nent;
     const unsigned long long* list = b1.list + bin * b1.cap;
-    // front-to-back order when the list fits the sort buffer
-    const bool sorted = !over && end <= kSortMax;
-    if (sorted && end <= 32) {
-        // one warp, register bitonic network (no block barriers)
-        if (w == 0) {
-            const int lane = threadIdx.x & 31;
-            unsigned long long k = lane < end ? list[lane] : ~0ull;
-#pragma unroll
-            for (int size = 2; size <= 32; size <<= 1) {
-#pragma unroll
-                for (int j = size >> 1; j > 0; j >>= 1) {
-                    const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, j);
-                    const bool up = (lane & size) == 0;
-                    const bool lower = (lane & j) == 0;
-                    const unsigned long long lo = k < o ? k : o;
-                    const unsigned long long hi = k < o ? o : k;
-                    k = (lower == up) ? lo : hi;
-                }
-            }
-            keys[lane] = k;
-        }
+    const unsigned lt = (1u << lane) - 1u;
+
+    // this warp's entries, in list order (first kWarpSort of them)
+    int cnt = 0;
+    for (int base = 0; base < end; base += 32) {
+        const unsigned long long k = base + lane < end ? list[base + lane] : 0ull;
+        const bool mine = (uint32_t(k) >> w) & 1u;
+        const unsigned bal = __ballot_sync(0xffffffffu, mine);
+        const int slot = cnt + __popc(bal & lt);
+        if (mine && slot < kWarpSort) keys[slot] = k;
+        cnt += __popc(bal);
+    }
+    __syncwarp();
+    // front-to-back order when the warp's list fits the sort buffer
+    const bool sorted = !over && cnt <= kWarpSort;
+    if (sorted && cnt <= 32) {
+        unsigned long long k = lane < cnt ? keys[lane] : ~0ull;
+        k = warp_sort_asc(k);
+        __syncwarp();
+        keys[lane] = k;
+        __syncwarp();
     } else if (sorted) {
-        for (int i = threadIdx.x; i < end; i += blockDim.x) keys[i] = list[i];
-        block_sort_asc(keys, end);
+        warp_sort_smem(keys, cnt);
     }
 
     Survivor s{1.f, -1, false};
     bool done = !in;  // sorted lists: every later face is behind the survivor
-    for (int base = 0; base < end; base += kRecChunk) {
-        const int n = imin_(kRecChunk, end - base);
-        __syncthreads();
-        if (!sorted && threadIdx.x < n) {
-            keys[threadIdx.x] = list[base + threadIdx.x];
-        }
-        __syncthreads();
-        const int kofs = sorted ? base : 0;
-        {
-            const float4* src = reinterpret_cast<const float4*>(a.recs);
-            float4* dst = reinterpret_cast<float4*>(sh);
-            for (int i = threadIdx.x; i < n * kRecVec4; i += blockDim.x) {
-                const int j = i / kRecVec4, q = i % kRecVec4;
-                const int f = int(uint32_t(keys[kofs + j])) >> 8;
-                dst[i] = src[size_t(f) * kRecVec4 + q];
+    // unsorted lists (over kWarpSort entries, or an overflowed tile) are
+    // walked in list order, re-gathered kWarpRecs at a time
+    int lpos = 0;
+    for (int base = 0; base < cnt; base += kWarpRecs) {
+        if (__all_sync(0xffffffffu, done)) break;
+        int n;
+        const unsigned long long* kb;
+        if (sorted) {
+            n = imin_(kWarpRecs, cnt - base);
+            kb = keys + base;
+        } else {
+            // next kWarpRecs of this warp's entries from the list
+            n = 0;
+            while (n < kWarpRecs && lpos < end) {
+                const int i = lpos + lane;
+                const unsigned long long k = i < end ? list[i] : 0ull;
+                const bool mine = (uint32_t(k) >> w) & 1u;
+                const unsigned bal = __ballot_sync(0xffffffffu, mine);
+                const int slot = n + __popc(bal & lt);
+                const int take = imin_(__popc(bal), kWarpRecs - n);
+                // entries past the room are revisited from their position
+                if (mine && slot < kWarpRecs) keys[slot] = k;
+                if (take < __popc(bal)) {
+                    // lane of the first entry left over
+                    unsigned rest = bal;
+                    for (int t = 0; t < take; t++) rest &= rest - 1u;
+                    lpos += __ffs(rest) - 1;
+                } else {
+                    lpos += 32;
+                }
+                n += take;
             }
+            __syncwarp();
+            kb = keys;
         }
-        __syncthreads();
-        if (__all_sync(0xffffffffu, done)) continue;
+        stage_records(a.recs, kb, n, sh);
         for (int i = 0; i < n; i++) {
-            const unsigned long long key = keys[kofs + i];
-            const int ent = int(uint32_t(key));
-            if (!((ent >> w) & 1)) continue;  // region misses this warp
             if (done) continue;
+            const unsigned long long key = kb[i];
+            const int ent = int(uint32_t(key));
             if (sorted && s.depth < __uint_as_float(uint32_t(key >> 32))) {
                 done = true;  // this face and all later ones lose
                 continue;
@@ -915,31 +966,23 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
                 eval_full(s, px, py, r, f, a.radius, peel, prev);
             }
         }
+        __syncwarp();  // sh / keys reuse by the next round
+        if (!sorted && lpos >= end) break;
     }
     const int cell = (y / kRimCell) * a.rim_cells_x + (x / kRimCell);
     // a parked tile reports every block open, so its survivors are stored
-    const unsigned ob = __ballot_sync(0xffffffffu, (in && s.depth > 0.5f &&
-                                                            a.rim[cell] != 0) ||
-                                                           over);
-    if ((threadIdx.x & 31) == 0) warp_open[w] = ob != 0u;
-    __syncthreads();
-    int m = 0;
-#pragma unroll
-    for (int k = 0; k < 8; k++) m |= warp_open[k] << k;
-    if (m == 0) {
-        if (threadIdx.x == 0) mask_out[bin] = 0;
-        epi(a, x, y, in, s);
+    const bool open = __ballot_sync(0xffffffffu, (in && s.depth > 0.5f &&
+                                                  a.rim[cell] != 0) ||
+                                                         over) != 0u;
+    if (lane == 0) active[bin * 8 + w] = open ? 1 : 0;
+    if (open) {
+        // open block (or a parked tile): survivors stored; an open block of
+        // an unparked tile is queued for the rim phase
+        if (in) state[size_t(a.v) * a.W * a.H + pix] = pack(s);
+        if (!over && lane == 0)
+            b2.open[atomicAdd(b2.open_n, 1)] = int(bin) * 8 + w;
     } else {
-        if (threadIdx.x == 0) mask_out[bin] = m;
-        if ((m >> w) & 1) {
-            // open block (or a parked tile): survivors stored; an open block
-            // of an unparked tile is queued for the rim phase
-            if (in) state[size_t(a.v) * a.W * a.H + pix] = pack(s);
-            if (!over && (threadIdx.x & 31) == 0)
-                b2.open[atomicAdd(b2.open_n, 1)] = int(bin) * 8 + w;
-        } else {
-            epi(a, x, y, in, s);
-        }
+        epi(a, x, y, in, s);
     }
 }
 
@@ -976,13 +1019,17 @@ __device__ __forceinline__ bool tri_touches_block(const FaceRec& r, int bx,
 // soft triangle may touch. One warp per face, lanes striding over the
 // blocks of its soft bbox.
 static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
-                          const FaceRec* recs_all, const int* mask,
+                          const FaceRec* recs_all, const uint8_t* active,
                           FixedBins b2, FixedBins1 b1) {
-    // sweep 1 has consumed the sweep-1 spill list and the parked tiles
+    // sweep 1 has consumed the sweep-1 bins, the spill list and the parked
+    // tiles: reset them for the next use
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
         *b1.spill_n = 0;
         *b1.parked_n = 0;
     }
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n_tiles;
+         t += gridDim.x * blockDim.x)
+        b1.cursor[size_t(blockIdx.y) * n_tiles + t] = 0;
     const int f = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     const int v = blockIdx.y;
@@ -991,14 +1038,15 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
     const uint32_t need = kFaceValid | kFaceSafe;
     if ((r.flags & need) != need) return;
     const int blocks_x = tiles_x * 2;
-    const int* mk = mask + size_t(v) * n_tiles;
+    const uint8_t* act = active + size_t(v) * n_tiles * 8;
     const size_t bin0 = size_t(v) * n_tiles * 8;
     // lanes tile the block range 8 wide x 4 tall (no integer division)
     const int lx = lane & 7, ly = lane >> 3;
     for (int by = (r.by0 >> 2) + ly; by <= (r.by1 >> 2); by += 4) {
         for (int bx = (r.bx0 >> 3) + lx; bx <= (r.bx1 >> 3); bx += 8) {
-            const int m = mk[(by >> 2) * tiles_x + (bx >> 1)];
-            if (!((m >> ((by & 3) * 2 + (bx & 1))) & 1)) continue;
+            if (!act[((by >> 2) * tiles_x + (bx >> 1)) * 8 + (by & 3) * 2 +
+                     (bx & 1)])
+                continue;
             if (!tri_touches_block(r, bx, by)) continue;
             const size_t bin = bin0 + size_t(by) * blocks_x + bx;
             const int slot = atomicAdd(&b2.cursor[bin], 1);
@@ -1113,14 +1161,14 @@ static __device__ void rim_block(const SweepArgs& a, FixedBins b2, int tile,
 template <class Epi>
 __global__ void __launch_bounds__(kTileThreads)
         k_sweep1(SweepArgs a0, FixedBins1 b1, FixedBins b2, int2* state,
-                 int* mask, size_t view_stride_recs, size_t view_stride_px,
-                 size_t view_stride_rim, Epi epi) {
+                 uint8_t* active, size_t view_stride_recs,
+                 size_t view_stride_px, size_t view_stride_rim, Epi epi) {
     SweepArgs a = a0;
     a.v = blockIdx.y;
     a.recs = a0.recs + a.v * view_stride_recs;
     a.rim = a0.rim + a.v * view_stride_rim;
     if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
-    sweep1_tile(a, b1, b2, blockIdx.x, state, mask, epi);
+    sweep1_tile(a, b1, b2, blockIdx.x, state, active, epi);
 }
 
 // Finishes the sweep-1 tiles whose bins overflowed into the spill list:
@@ -1130,12 +1178,11 @@ __global__ void __launch_bounds__(kTileThreads)
 template <class Epi>
 __global__ void __launch_bounds__(kTileThreads)
         k_sweep1_spill(SweepArgs a0, FixedBins1 b1, FixedBins b2, int2* state,
-                       int* mask, size_t view_stride_recs,
+                       uint8_t* active, size_t view_stride_recs,
                        size_t view_stride_px, size_t view_stride_rim,
                        Epi epi) {
     __shared__ FaceRec sh[kRecChunk];
     __shared__ unsigned long long keys[kSortMax];
-    __shared__ int warp_open[8];
     __shared__ int n_match;
     const int n_parked = *b1.parked_n;
     const int ns_all = *b1.spill_n;
@@ -1159,9 +1206,8 @@ __global__ void __launch_bounds__(kTileThreads)
         if (in) s = unpack(state[size_t(a.v) * a.W * a.H + pix]);
         sweep1_spilled(a, b1, bin, ns, all_faces, x, y, in, peel, prev,
                        a.radius < kMaxFastRadius, sh, keys, &n_match, s);
-        sweep1_finish(a, size_t(bin), x, y, in, s, state, mask, warp_open, b2,
-                      epi);
-        __syncthreads();  // warp_open / sh reuse by the next parked tile
+        sweep1_finish(a, size_t(bin), x, y, in, s, state, active, b2, epi);
+        __syncthreads();  // sh reuse by the next parked tile
     }
 }
 

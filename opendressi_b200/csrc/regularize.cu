@@ -5,8 +5,9 @@
 //   g_lap = pos - VertexNeighborMean(pos, nbrs)        k_vertex_terms
 //   term  = NormalConsistencyFaceTerm(pos, faces, adj)  k_nc_face_term
 //   g_nrm = NormalConsistencyVertexGrad(term, ...)      k_vertex_terms
-//   s_lap = rms(g) / rms(g_lap) * laplacian             k_reg_scale
-//   s_nrm = rms(g) / rms(g_nrm) * normal                k_reg_scale
+//   rms(g), rms(g_lap), rms(g_nrm)                     k_reg_rms
+//   s_lap = rms(g) / rms(g_lap) * laplacian             k_gpos_adam
+//   s_nrm = rms(g) / rms(g_nrm) * normal                k_gpos_adam
 //   g'    = (g + g_lap * s_lap) + g_nrm * s_nrm         k_gpos_adam
 //
 // rms(x) = sqrt(SumAll(x * x) * (1 / 3V) + 1e-24). SumAll is restated
@@ -77,101 +78,183 @@ __device__ __forceinline__ void face_cross(const float* pos,
 // NormalConsistencyFaceTerm (f_ops.cpp:2031-2098): per face a, with
 // n = c / |c| and faces closer to degenerate than |c| < 1e-12 skipped,
 // term_a = sum over edge neighbours b of -(n_b - (n_a . n_b) n_a) / |c_a|.
-__global__ void k_nc_face_term(const float* pos, int n_verts,
-                               const float* faces, const float* fadj,
-                               int n_faces, float* term, uint32_t* status) {
+// The three neighbours' crosses are loaded up front (independent loads);
+// the sum keeps the table order.
+__global__ void __launch_bounds__(128)
+k_nc_face_term(const float* pos, int n_verts, const float* faces,
+               const float* fadj, int n_faces, float* term,
+               uint32_t* status) {
     const int f = blockIdx.x * blockDim.x + threadIdx.x;
     if (f >= n_faces) return;
+    float gv[3];
+#pragma unroll
+    for (int j = 0; j < 3; j++) gv[j] = fadj[size_t(f) * 3 + j];
     int ia[3];
     float ca[3];
     face_cross(pos, faces, f, n_verts, status, ia, ca);
+    bool okb[3];
+    float cb[3][3];
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+        int ib[3];
+        okb[j] = !(gv[j] < -0.5f) && id_ok(gv[j], n_faces, status);
+        if (okb[j]) {
+            face_cross(pos, faces, tab_id(gv[j]), n_verts, status, ib, cb[j]);
+        } else {
+            cb[j][0] = cb[j][1] = cb[j][2] = 0.f;
+        }
+    }
     const float la = sqrtf(ca[0] * ca[0] + ca[1] * ca[1] + ca[2] * ca[2]);
     float gg[3] = {0.f, 0.f, 0.f};
     if (la >= 1e-12f) {
         const float na[3] = {ca[0] / la, ca[1] / la, ca[2] / la};
-#pragma unroll 1
+#pragma unroll
         for (int j = 0; j < 3; j++) {
-            const float gv = fadj[size_t(f) * 3 + j];
-            if (gv < -0.5f || !id_ok(gv, n_faces, status)) continue;
-            int ib[3];
-            float cb[3];
-            face_cross(pos, faces, tab_id(gv), n_verts, status, ib, cb);
-            const float lb =
-                    sqrtf(cb[0] * cb[0] + cb[1] * cb[1] + cb[2] * cb[2]);
+            if (!okb[j]) continue;
+            const float* c = cb[j];
+            const float lb = sqrtf(c[0] * c[0] + c[1] * c[1] + c[2] * c[2]);
             if (lb < 1e-12f) continue;
-            const float nb[3] = {cb[0] / lb, cb[1] / lb, cb[2] / lb};
+            const float nb[3] = {c[0] / lb, c[1] / lb, c[2] / lb};
             const float d = na[0] * nb[0] + na[1] * nb[1] + na[2] * nb[2];
 #pragma unroll
-            for (int c = 0; c < 3; c++) gg[c] += -(nb[c] - d * na[c]) / la;
+            for (int k = 0; k < 3; k++) gg[k] += -(nb[k] - d * na[k]) / la;
         }
     }
 #pragma unroll
-    for (int c = 0; c < 3; c++) term[size_t(f) * 3 + c] = gg[c];
+    for (int k = 0; k < 3; k++) term[size_t(f) * 3 + k] = gg[k];
 }
 
-// Per vertex: VertexNeighborMean (f_ops.cpp:1983-2029; the mean of the
-// listed neighbours in table order, pos itself without neighbours) as
-// `mean` or, with `lap_diff`, pos - mean; and NormalConsistencyVertexGrad
-// (f_ops.cpp:2100-2181) over the vertex's incident faces in table order.
-// Either output may be null.
-__global__ void k_vertex_terms(const float* pos, int n_verts,
-                               const float* nbrs, int nbr_deg, int lap_diff,
-                               float* lap_out, const float* term,
-                               const float* faces, int n_faces,
-                               const float* vf, int vf_deg, float* nrm_out,
-                               uint32_t* status) {
-    const int v = blockIdx.x * blockDim.x + threadIdx.x;
-    if (v >= n_verts) return;
-    const float* pv = pos + size_t(v) * 3;
-    if (lap_out) {
-        float mean[3] = {0.f, 0.f, 0.f};
-        int count = 0;
-#pragma unroll 1
-        for (int d = 0; d < nbr_deg; d++) {
-            const float nv = nbrs[size_t(d) * n_verts + v];
-            if (nv < -0.5f || !id_ok(nv, n_verts, status)) continue;
-            const float* pn = pos + size_t(tab_id(nv)) * 3;
-            mean[0] += pn[0];
-            mean[1] += pn[1];
-            mean[2] += pn[2];
+namespace {
+
+constexpr int kVtxThreads = 64;  // ~10k vertices: a block on every SM
+constexpr int kNbrBatch = 8;     // neighbour slots loaded per round
+constexpr int kFaceBatch = 4;    // incident faces loaded per round
+
+// VertexNeighborMean of vertex v (f_ops.cpp:1983-2029): the mean of the
+// listed neighbours in table order, pos itself without neighbours.
+__device__ __forceinline__ void neighbor_mean(const float* pos, int n_verts,
+                                              const float* nbrs, int nbr_deg,
+                                              int v, uint32_t* status,
+                                              float m[3]) {
+    float mean[3] = {0.f, 0.f, 0.f};
+    int count = 0;
+    for (int d0 = 0; d0 < nbr_deg; d0 += kNbrBatch) {
+        float nv[kNbrBatch];
+#pragma unroll
+        for (int k = 0; k < kNbrBatch; k++)
+            nv[k] = d0 + k < nbr_deg ? nbrs[size_t(d0 + k) * n_verts + v]
+                                     : -1.f;
+        bool ok[kNbrBatch];
+        float pn[kNbrBatch][3];
+#pragma unroll
+        for (int k = 0; k < kNbrBatch; k++) {
+            ok[k] = !(nv[k] < -0.5f) && id_ok(nv[k], n_verts, status);
+            const float* q = pos + size_t(ok[k] ? tab_id(nv[k]) : v) * 3;
+            pn[k][0] = q[0];
+            pn[k][1] = q[1];
+            pn[k][2] = q[2];
+        }
+#pragma unroll
+        for (int k = 0; k < kNbrBatch; k++) {
+            if (!ok[k]) continue;
+            mean[0] += pn[k][0];
+            mean[1] += pn[k][1];
+            mean[2] += pn[k][2];
             count++;
         }
-#pragma unroll
-        for (int c = 0; c < 3; c++) {
-            const float m = count > 0 ? mean[c] / float(count) : pv[c];
-            lap_out[size_t(v) * 3 + c] = lap_diff ? pv[c] - m : m;
-        }
     }
-    if (nrm_out) {
-        float acc[3] = {0.f, 0.f, 0.f};
-#pragma unroll 1
-        for (int d = 0; d < vf_deg; d++) {
-            const float fv = vf[size_t(d) * n_verts + v];
-            if (fv < -0.5f || !id_ok(fv, n_faces, status)) continue;
-            const int f = tab_id(fv);
-            int idx[3];
-            if (!face_ids(faces, f, n_verts, status, idx)) continue;
-            const float* p0 = pos + size_t(idx[0]) * 3;
-            const float* p1 = pos + size_t(idx[1]) * 3;
-            const float* p2 = pos + size_t(idx[2]) * 3;
-            const float e1[3] = {p1[0] - p0[0], p1[1] - p0[1], p1[2] - p0[2]};
-            const float e2[3] = {p2[0] - p0[0], p2[1] - p0[1], p2[2] - p0[2]};
-            const float* t = term + size_t(f) * 3;
-            const float g1[3] = {e2[1] * t[2] - e2[2] * t[1],
-                                 e2[2] * t[0] - e2[0] * t[2],
-                                 e2[0] * t[1] - e2[1] * t[0]};
-            const float g2[3] = {t[1] * e1[2] - t[2] * e1[1],
-                                 t[2] * e1[0] - t[0] * e1[2],
-                                 t[0] * e1[1] - t[1] * e1[0]};
+    const float* pv = pos + size_t(v) * 3;
+#pragma unroll
+    for (int c = 0; c < 3; c++)
+        m[c] = count > 0 ? mean[c] / float(count) : pv[c];
+}
+
+// NormalConsistencyVertexGrad of vertex v (f_ops.cpp:2100-2181): over its
+// incident faces in table order, the transpose of c = e1 x e2 applied to
+// the face term.
+__device__ __forceinline__ void nc_vertex_grad(const float* term,
+                                               const float* pos, int n_verts,
+                                               const float* faces, int n_faces,
+                                               const float* vf, int vf_deg,
+                                               int v, uint32_t* status,
+                                               float acc[3]) {
+    acc[0] = acc[1] = acc[2] = 0.f;
+    for (int d0 = 0; d0 < vf_deg; d0 += kFaceBatch) {
+        float fv[kFaceBatch];
+#pragma unroll
+        for (int k = 0; k < kFaceBatch; k++)
+            fv[k] = d0 + k < vf_deg ? vf[size_t(d0 + k) * n_verts + v] : -1.f;
+        bool ok[kFaceBatch];
+        int idx[kFaceBatch][3];
+#pragma unroll
+        for (int k = 0; k < kFaceBatch; k++) {
+            ok[k] = !(fv[k] < -0.5f) && id_ok(fv[k], n_faces, status);
+            ok[k] = ok[k] &&
+                    face_ids(faces, tab_id(fv[k]), n_verts, status, idx[k]);
+        }
+        float e1[kFaceBatch][3], e2[kFaceBatch][3], t[kFaceBatch][3];
+#pragma unroll
+        for (int k = 0; k < kFaceBatch; k++) {
+            const int f = ok[k] ? tab_id(fv[k]) : 0;
+            const int i0 = ok[k] ? idx[k][0] : 0;
+            const int i1 = ok[k] ? idx[k][1] : 0;
+            const int i2 = ok[k] ? idx[k][2] : 0;
+            const float* p0 = pos + size_t(i0) * 3;
+            const float* p1 = pos + size_t(i1) * 3;
+            const float* p2 = pos + size_t(i2) * 3;
 #pragma unroll
             for (int c = 0; c < 3; c++) {
-                if (idx[1] == v) acc[c] += g1[c];
-                if (idx[2] == v) acc[c] += g2[c];
-                if (idx[0] == v) acc[c] -= g1[c] + g2[c];
+                e1[k][c] = p1[c] - p0[c];
+                e2[k][c] = p2[c] - p0[c];
+                t[k][c] = term[size_t(f) * 3 + c];
             }
         }
 #pragma unroll
-        for (int c = 0; c < 3; c++) nrm_out[size_t(v) * 3 + c] = acc[c];
+        for (int k = 0; k < kFaceBatch; k++) {
+            if (!ok[k]) continue;
+            const float* a = e1[k];
+            const float* b = e2[k];
+            const float* tt = t[k];
+            const float g1[3] = {b[1] * tt[2] - b[2] * tt[1],
+                                 b[2] * tt[0] - b[0] * tt[2],
+                                 b[0] * tt[1] - b[1] * tt[0]};
+            const float g2[3] = {tt[1] * a[2] - tt[2] * a[1],
+                                 tt[2] * a[0] - tt[0] * a[2],
+                                 tt[0] * a[1] - tt[1] * a[0]};
+#pragma unroll
+            for (int c = 0; c < 3; c++) {
+                if (idx[k][1] == v) acc[c] += g1[c];
+                if (idx[k][2] == v) acc[c] += g2[c];
+                if (idx[k][0] == v) acc[c] -= g1[c] + g2[c];
+            }
+        }
+    }
+}
+
+}  // namespace
+
+// Per vertex, part 0: VertexNeighborMean as `mean` or, with lap_diff, pos -
+// mean; part 1: NormalConsistencyVertexGrad. part = part0 + blockIdx.y, so
+// both parts of a vertex run in separate threads.
+__global__ void __launch_bounds__(kVtxThreads)
+k_vertex_terms(const float* pos, int n_verts, const float* nbrs, int nbr_deg,
+               int lap_diff, float* lap_out, const float* term,
+               const float* faces, int n_faces, const float* vf, int vf_deg,
+               float* nrm_out, uint32_t* status, int part0) {
+    const int v = blockIdx.x * blockDim.x + threadIdx.x;
+    if (v >= n_verts) return;
+    float r[3];
+    if (part0 + int(blockIdx.y) == 0) {
+        neighbor_mean(pos, n_verts, nbrs, nbr_deg, v, status, r);
+        const float* pv = pos + size_t(v) * 3;
+#pragma unroll
+        for (int c = 0; c < 3; c++)
+            lap_out[size_t(v) * 3 + c] = lap_diff ? pv[c] - r[c] : r[c];
+    } else {
+        nc_vertex_grad(term, pos, n_verts, faces, n_faces, vf, vf_deg, v,
+                       status, r);
+#pragma unroll
+        for (int c = 0; c < 3; c++) nrm_out[size_t(v) * 3 + c] = r[c];
     }
 }
 
@@ -186,80 +269,108 @@ __device__ __forceinline__ double sum_elem(float x) {
     return kSq ? double(x * x) : double(x);
 }
 
-// SumPartial's part p (f_ops.cpp:1087-1115): the elements of pixels p,
-// p + 64, ... in pixel-then-component order, summed in double and rounded
-// to float. Pixel loads are issued eight at a time so the dependent double
-// additions wait on one load latency per batch.
-template <bool kSq>
-__device__ float sum_partial(const float* x, int n_px, int nc, int p) {
-    double s = 0.0;
-    int i = p;
-    for (; i + 7 * kSumParts < n_px; i += 8 * kSumParts) {
-        float v[8][4];
-#pragma unroll
-        for (int k = 0; k < 8; k++)
-#pragma unroll
-            for (int c = 0; c < 4; c++)
-                if (c < nc) v[k][c] = x[size_t(i + k * kSumParts) * nc + c];
-#pragma unroll
-        for (int k = 0; k < 8; k++)
-#pragma unroll
-            for (int c = 0; c < 4; c++)
-                if (c < nc) s += sum_elem<kSq>(v[k][c]);
-    }
-    for (; i < n_px; i += kSumParts)
-        for (int c = 0; c < nc; c++) s += sum_elem<kSq>(x[size_t(i) * nc + c]);
-    return float(s);
-}
+constexpr int kRmsThreads = 512;
+// shared staging buffer (floats); each round stages a multiple of
+// kSumParts pixels, so a part's pixels keep their residue in every round
+constexpr int kStageFloats = kSumParts * 180;
 
-// SumAll (f_ops.cpp:1119-1149) by a group of `kSumParts` threads (lane =
-// index in the group); the result is valid in lane 0. `parts` is the
-// group's shared scratch. Every thread of the block calls it with the same
-// n_px (it holds a block barrier).
-template <bool kSq>
-__device__ float sum_all_block(const float* x, int n_px, int nc, int lane,
+// SumAll (f_ops.cpp:1119-1149, SumPartial 1087-1115) of x [n_px][nc] by
+// one block of kRmsThreads threads; the result is valid in thread 0.
+// Above 256 pixels, part p (thread p < 64) sums the elements of pixels p,
+// p + 64, ... in pixel-then-component order in double, rounded to float;
+// the 64 parts are summed in double. Rounds of pixels are staged
+// in shared memory by the whole block (coalesced) so each part's serial
+// chain reads shared memory only.
+template <bool kSq, int kNc>
+__device__ float sum_all_block(const float* x, int n_px, float* stage,
                                float* parts) {
+    constexpr int nc = kNc;
+    constexpr int round_px = kStageFloats / nc / kSumParts * kSumParts;
+    const int tid = threadIdx.x;
     if (n_px <= 256) {
         // one serial pass over every element
-        if (lane != 0) return 0.f;
         double s = 0.0;
-        for (size_t i = 0; i < size_t(n_px) * nc; i++)
-            s += sum_elem<kSq>(x[i]);
+        if (tid == 0)
+            for (size_t i = 0; i < size_t(n_px) * nc; i++)
+                s += sum_elem<kSq>(x[i]);
         return float(s);
     }
-    parts[lane] = sum_partial<kSq>(x, n_px, nc, lane);
-    __syncthreads();
-    if (lane != 0) return 0.f;
     double s = 0.0;
-    for (int q = 0; q < kSumParts; q++) s += double(parts[q]);
-    return float(s);
+    for (int base = 0; base < n_px; base += round_px) {
+        const int np = min(round_px, n_px - base);
+        const float* src = x + size_t(base) * nc;
+        for (int i = tid; i < np * nc; i += blockDim.x) stage[i] = src[i];
+        __syncthreads();
+        if (tid < kSumParts) {
+            // shared loads four pixels ahead of the dependent double adds
+            int j = tid;
+            for (; j + 3 * kSumParts < np; j += 4 * kSumParts) {
+                float v[4][nc];
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+#pragma unroll
+                    for (int c = 0; c < nc; c++)
+                        v[k][c] = stage[(j + k * kSumParts) * nc + c];
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+#pragma unroll
+                    for (int c = 0; c < nc; c++) s += sum_elem<kSq>(v[k][c]);
+            }
+            for (; j < np; j += kSumParts)
+#pragma unroll
+                for (int c = 0; c < nc; c++)
+                    s += sum_elem<kSq>(stage[j * nc + c]);
+        }
+        __syncthreads();
+    }
+    if (tid < kSumParts) parts[tid] = float(s);
+    __syncthreads();
+    double t = 0.0;
+    if (tid == 0)
+        for (int q = 0; q < kSumParts; q++) t += double(parts[q]);
+    return float(t);
 }
 
 }  // namespace
 
 // out[0] = SumAll(x) for x [n_px][nc] (op level).
-__global__ void k_sum_all(const float* x, int n_px, int nc, float* out) {
+__global__ void __launch_bounds__(kRmsThreads)
+k_sum_all(const float* x, int n_px, int nc, float* out) {
+    __shared__ float stage[kStageFloats];
     __shared__ float parts[kSumParts];
-    const float s = sum_all_block<false>(x, n_px, nc, threadIdx.x, parts);
+    float s = 0.f;
+    switch (nc) {
+        case 1: s = sum_all_block<false, 1>(x, n_px, stage, parts); break;
+        case 2: s = sum_all_block<false, 2>(x, n_px, stage, parts); break;
+        case 3: s = sum_all_block<false, 3>(x, n_px, stage, parts); break;
+        default: s = sum_all_block<false, 4>(x, n_px, stage, parts); break;
+    }
     if (threadIdx.x == 0) out[0] = s;
 }
 
-// The three RMS values of the regulariser, one group of 64 threads each
-// (g, g_lap, g_nrm), then scale = {s_lap, s_nrm}.
-__global__ void k_reg_scale(const float* g, const float* glap,
-                            const float* gnrm, int n_verts, float inv_cnt,
-                            float laplacian, float normal, float* scale) {
-    __shared__ float parts[3][kSumParts];
-    __shared__ float rms[3];
-    const int grp = threadIdx.x / kSumParts, lane = threadIdx.x % kSumParts;
-    const float* x = grp == 0 ? g : (grp == 1 ? glap : gnrm);
-    const float s = sum_all_block<true>(x, n_verts, 3, lane, parts[grp]);
-    if (lane == 0) rms[grp] = sqrtf(s * inv_cnt + 1e-24f);
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        scale[0] = rms[0] / rms[1] * laplacian;
-        scale[1] = rms[0] / rms[2] * normal;
-    }
+// rms[b] = sqrt(SumAll(x_b * x_b) * inv_cnt + 1e-24) for x = (g, g_lap,
+// g_nrm), one block each.
+__global__ void __launch_bounds__(kRmsThreads)
+k_reg_rms(const float* g, const float* glap, const float* gnrm, int n_verts,
+          float inv_cnt, float* rms) {
+    __shared__ float stage[kStageFloats];
+    __shared__ float parts[kSumParts];
+    const float* x = blockIdx.x == 0 ? g : (blockIdx.x == 1 ? glap : gnrm);
+    const float s = sum_all_block<true, 3>(x, n_verts, stage, parts);
+    if (threadIdx.x == 0) rms[blockIdx.x] = sqrtf(s * inv_cnt + 1e-24f);
+}
+
+// out = (g + glap * s_lap) + gnrm * s_nrm with s = rms(g) / rms(term) *
+// weight (op level; out may alias g).
+__global__ void k_reg_combine(const float* g, const float* glap,
+                              const float* gnrm, const float* rms,
+                              float laplacian, float normal, int n,
+                              float* out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float sl = rms[0] / rms[1] * laplacian;
+    const float sn = rms[0] / rms[2] * normal;
+    out[i] = (g[i] + glap[i] * sl) + gnrm[i] * sn;
 }
 
 static void check_launch() { DRESSI_CUDA(cudaGetLastError()); }
@@ -279,46 +390,40 @@ void vertex_terms_op(const float* pos, int n_verts, const float* nbrs,
                      const float* term, const float* faces, int n_faces,
                      const float* vf, int vf_deg, float* nrm_out,
                      uint32_t* status, cudaStream_t s) {
-    if (n_verts <= 0) return;
+    if (n_verts <= 0 || (!lap_out && !nrm_out)) return;
     ProfScope ps("vertex_terms", s);
-    k_vertex_terms<<<(n_verts + 127) / 128, 128, 0, s>>>(
+    const int part0 = lap_out ? 0 : 1;
+    const int parts = (lap_out && nrm_out) ? 2 : 1;
+    const dim3 grid((n_verts + kVtxThreads - 1) / kVtxThreads, parts);
+    k_vertex_terms<<<grid, kVtxThreads, 0, s>>>(
             pos, n_verts, nbrs, nbr_deg, lap_diff ? 1 : 0, lap_out, term,
-            faces, n_faces, vf, vf_deg, nrm_out, status);
-    check_launch();
-}
-
-void reg_scale_op(const float* g, const float* glap, const float* gnrm,
-                  int n_verts, float laplacian, float normal, float* scale,
-                  cudaStream_t s) {
-    ProfScope ps("reg_scale", s);
-    k_reg_scale<<<1, 3 * kSumParts, 0, s>>>(g, glap, gnrm, n_verts,
-                                            1.f / float(n_verts * 3),
-                                            laplacian, normal, scale);
-    check_launch();
-}
-
-// out = (g + glap * scale[0]) + gnrm * scale[1] (op level; out may alias g)
-__global__ void k_reg_combine(const float* g, const float* glap,
-                              const float* gnrm, const float* scale, int n,
-                              float* out) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    out[i] = (g[i] + glap[i] * scale[0]) + gnrm[i] * scale[1];
-}
-
-void reg_combine_op(const float* g, const float* glap, const float* gnrm,
-                    const float* scale, int n, float* out, cudaStream_t s) {
-    if (n <= 0) return;
-    ProfScope ps("reg_combine", s);
-    k_reg_combine<<<(n + 255) / 256, 256, 0, s>>>(g, glap, gnrm, scale, n,
-                                                  out);
+            faces, n_faces, vf, vf_deg, nrm_out, status, part0);
     check_launch();
 }
 
 void sum_all_op(const float* x, int n_px, int nc, float* out,
                 cudaStream_t s) {
     ProfScope ps("sum_all", s);
-    k_sum_all<<<1, kSumParts, 0, s>>>(x, n_px, nc, out);
+    k_sum_all<<<1, kRmsThreads, 0, s>>>(x, n_px, nc, out);
+    check_launch();
+}
+
+void reg_rms_op(const float* g, const float* glap, const float* gnrm,
+                int n_verts, float* rms, cudaStream_t s) {
+    ProfScope ps("reg_rms", s);
+    k_reg_rms<<<3, kRmsThreads, 0, s>>>(g, glap, gnrm, n_verts,
+                                        1.f / float(n_verts * 3), rms);
+    check_launch();
+}
+
+void reg_combine_op(const float* g, const float* glap, const float* gnrm,
+                    const float* rms, float laplacian, float normal,
+                    int n_verts, float* out, cudaStream_t s) {
+    const int n = n_verts * 3;
+    if (n <= 0) return;
+    ProfScope ps("reg_combine", s);
+    k_reg_combine<<<(n + 255) / 256, 256, 0, s>>>(g, glap, gnrm, rms,
+                                                  laplacian, normal, n, out);
     check_launch();
 }
 
@@ -337,8 +442,7 @@ void sil_reg_terms(const SilParams& p, const SilBuffers& b, cudaStream_t s) {
 void sil_reg_scale(const SilParams& p, const SilBuffers& b, cudaStream_t s) {
     if (!p.reg) return;
     const RegBuffers& r = b.reg;
-    reg_scale_op(b.gpos, r.glap, r.gnrm, p.n_verts, p.laplacian, p.normal,
-                 r.scale, s);
+    reg_rms_op(b.gpos, r.glap, r.gnrm, p.n_verts, r.rms, s);
 }
 
 // ---- host: the reference's mesh tables (mesh_utils.cpp:53-101) ----

@@ -218,19 +218,31 @@ struct EpiSil {
     }
 };
 
+// Small blocks: one thread per vertex and ~10k vertices, so 64 threads put
+// a block on every SM.
+constexpr int kGposThreads = 64;
+
 // g_pos = sum_v MVP_v^T g_clip_v (TransformToClipVar's backward); zeroes
 // g_clip for the next iteration. With `update`, also applies the in-graph
 // Adam and (block 0) publishes the loss of this iteration.
 __global__ void k_gpos_adam(SilParams p, SilBuffers b, float omb1, float omb2,
                             int do_grad, int update) {
     const int u = blockIdx.x * blockDim.x + threadIdx.x;
-    if (blockIdx.x == 0) {
-        // reduce + clear the loss slots (written by k_sweep2_sil)
-        __shared__ double red[256];
+    if (blockIdx.x == 0 && do_grad) {
+        // reduce + clear the loss slots (written by the sweep epilogues);
+        // the loads are issued 16 at a time ahead of the dependent adds
+        __shared__ double red[kGposThreads];
         double acc = 0.0;
-        for (int i = threadIdx.x; i < kLossSlots; i += blockDim.x) {
-            acc += b.loss_slots[i];
-            b.loss_slots[i] = 0.0;
+        static_assert(kLossSlots % (kGposThreads * 16) == 0, "slot batches");
+        for (int i0 = threadIdx.x; i0 < kLossSlots; i0 += 16 * kGposThreads) {
+            double v[16];
+#pragma unroll
+            for (int k = 0; k < 16; k++) v[k] = b.loss_slots[i0 + k * kGposThreads];
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                acc += v[k];
+                b.loss_slots[i0 + k * kGposThreads] = 0.0;
+            }
         }
         red[threadIdx.x] = acc;
         __syncthreads();
@@ -238,7 +250,7 @@ __global__ void k_gpos_adam(SilParams p, SilBuffers b, float omb1, float omb2,
             if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
             __syncthreads();
         }
-        if (threadIdx.x == 0 && do_grad) {
+        if (threadIdx.x == 0) {
             const float loss = float(red[0]);
             b.scalars[3] = loss;
             const int it = int(b.scalars[0]) - 1;
@@ -249,15 +261,20 @@ __global__ void k_gpos_adam(SilParams p, SilBuffers b, float omb1, float omb2,
     float g0, g1, g2;
     if (do_grad) {
         g0 = g1 = g2 = 0.f;
+        float4* gc4 = reinterpret_cast<float4*>(b.gclip) + u;
+        // all loads first (no store in this loop, so the view loads and the
+        // uniform matrix loads pipeline), then the clearing stores
+#pragma unroll 8
         for (int v = 0; v < p.views; v++) {
-            float4* gcp = reinterpret_cast<float4*>(b.gclip) + size_t(v) * p.n_verts + u;
-            const float4 gc = *gcp;
-            *gcp = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 gc = __ldcs(gc4 + size_t(v) * p.n_verts);
             const float* m = b.mvps + v * 16;
             g0 += gc.x * m[0] + gc.y * m[1] + gc.z * m[2] + gc.w * m[3];
             g1 += gc.x * m[4] + gc.y * m[5] + gc.z * m[6] + gc.w * m[7];
             g2 += gc.x * m[8] + gc.y * m[9] + gc.z * m[10] + gc.w * m[11];
         }
+#pragma unroll 8
+        for (int v = 0; v < p.views; v++)
+            gc4[size_t(v) * p.n_verts] = make_float4(0.f, 0.f, 0.f, 0.f);
         b.gpos[u * 3 + 0] = g0;
         b.gpos[u * 3 + 1] = g1;
         b.gpos[u * 3 + 2] = g2;
@@ -269,8 +286,10 @@ __global__ void k_gpos_adam(SilParams p, SilBuffers b, float omb1, float omb2,
     if (!update) return;
     const float bc1 = b.scalars[1], bc2 = b.scalars[2];
     if (p.reg) {
-        // g + g_lap * s_lap + g_nrm * s_nrm (run.cpp:419-420)
-        const float sl = b.reg.scale[0], sn = b.reg.scale[1];
+        // g + g_lap * s_lap + g_nrm * s_nrm (run.cpp:419-420), s = rms(g) /
+        // rms(term) * weight
+        const float sl = b.reg.rms[0] / b.reg.rms[1] * p.laplacian;
+        const float sn = b.reg.rms[0] / b.reg.rms[2] * p.normal;
         const float* gl = b.reg.glap + size_t(u) * 3;
         const float* gn = b.reg.gnrm + size_t(u) * 3;
         g0 = (g0 + gl[0] * sl) + gn[0] * sn;
@@ -323,7 +342,8 @@ void sil_forward_backward(const SoftDims& d, const SilParams& p,
 void sil_grad_reduce(const SilParams& p, const SilBuffers& b, bool update,
                      cudaStream_t s) {
     ProfScope ps("gpos_adam", s);
-    k_gpos_adam<<<(p.n_verts + 255) / 256, 256, 0, s>>>(
+    k_gpos_adam<<<(p.n_verts + kGposThreads - 1) / kGposThreads, kGposThreads,
+                  0, s>>>(
             p, b, 1.f - p.b1, 1.f - p.b2, 1, update ? 1 : 0);
     check_launch();
 }
@@ -331,7 +351,8 @@ void sil_grad_reduce(const SilParams& p, const SilBuffers& b, bool update,
 void sil_update(const SilParams& p, const SilBuffers& b, cudaStream_t s) {
     sil_reg_scale(p, b, s);
     ProfScope ps("adam", s);
-    k_gpos_adam<<<(p.n_verts + 255) / 256, 256, 0, s>>>(
+    k_gpos_adam<<<(p.n_verts + kGposThreads - 1) / kGposThreads, kGposThreads,
+                  0, s>>>(
             p, b, 1.f - p.b1, 1.f - p.b2, 0, 1);
     check_launch();
 }

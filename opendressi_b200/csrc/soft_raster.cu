@@ -41,7 +41,7 @@ void carve_soft_main(Arena& a, const SoftDims& d, SoftBuffers* b) {
     const size_t vt = size_t(d.views) * d.n_tiles;
     b->recs = a.take<FaceRec>(size_t(d.views) * std::max(d.n_faces, 1));
     b->state = a.take<int2>(size_t(d.views) * d.W * d.H);
-    b->active = a.take<int>(vt);
+    b->active = a.take<uint8_t>(vt * 8);
     b->rim = a.take<int>(size_t(d.views) * std::max(d.rim_cells, 1));
     b->status = a.take<uint32_t>(4);
 }
