@@ -112,6 +112,7 @@ void reg_params(SilParams* p, float laplacian, float normal) {
 
 void reg_tables(const SilParams& p, const float* faces, RegTables* t) {
     if (!p.reg) return;
+    sum_all_setup();
     vertex_neighbors_table(faces, p.n_faces, p.n_verts, &t->nbrs,
                            &t->nbr_deg);
     face_neighbors_table(faces, p.n_faces, &t->fadj);
@@ -884,6 +885,7 @@ int dressi_sum_all(const float* x, uint32_t n_px, uint32_t n_comp, float* out,
     return guarded([&] {
         DRESSI_REQUIRE(x && out, "null pointer");
         DRESSI_REQUIRE(n_comp >= 1 && n_comp <= 4, "SumAll: 1..4 components");
+        sum_all_setup();
         sum_all_op(x, int(n_px), int(n_comp), out, as_stream(stream));
     });
 }
@@ -901,6 +903,7 @@ int dressi_regularized_grad(const float* pos, uint32_t n_verts,
                        "null pointer");
         DRESSI_REQUIRE(n_verts > 0, "regularized_grad: no vertices");
         cudaStream_t s = as_stream(stream);
+        sum_all_setup();
         const size_t V3 = size_t(n_verts) * 3, F3 = size_t(n_faces) * 3;
         AsyncScratch sc((F3 + 2 * V3 + 3) * sizeof(float), s);
         float* term = static_cast<float*>(sc.p);

@@ -223,6 +223,9 @@ void vertex_terms_op(const float* pos, int n_verts, const float* nbrs,
                      const float* vf, int vf_deg, float* nrm_out,
                      uint32_t* status, cudaStream_t s);
 void sum_all_op(const float* x, int n_px, int nc, float* out, cudaStream_t s);
+// Dynamic shared memory opt-in of the SumAll kernels on the current device;
+// call before launching them (and before any stream capture).
+void sum_all_setup();
 // rms = {rms(g), rms(glap), rms(gnrm)} over [n_verts][3] each; out =
 // (g + glap s_lap) + gnrm s_nrm, s = rms[0] / rms[1 | 2] * weight.
 void reg_rms_op(const float* g, const float* glap, const float* gnrm,

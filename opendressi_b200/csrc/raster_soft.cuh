@@ -33,6 +33,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cstddef>
 #include <cstdint>
 
 #include "exact.cuh"
@@ -78,6 +79,11 @@ struct __align__(16) FaceRec {
 };
 static_assert(sizeof(FaceRec) == 192, "FaceRec layout");
 constexpr int kRecVec4 = sizeof(FaceRec) / 16;
+// the 16-byte word holding (lbx0, lbx1, lby0, lby1)
+constexpr int kRecLbVec4 = 8;
+static_assert(offsetof(FaceRec, lbx0) == kRecLbVec4 * 16 &&
+                      offsetof(FaceRec, lby1) == kRecLbVec4 * 16 + 12,
+              "FaceRec bbox word");
 
 // Survivor of a pixel: Eq.3 depth, soft face index (-1 = none) and whether
 // its signed distance is >= 0 (a "hard" fragment). The distance and hard
@@ -525,7 +531,7 @@ static __global__ void k_bin_scan(BinSet b, int n_tiles, uint32_t* status) {
 
 constexpr int kRecChunk = 64;
 constexpr int kRimCell = 64;     // pixels per side of a rim-flag cell
-constexpr int kRimChunk = 16;    // records staged per warp in the rim phase
+constexpr int kRimChunk = 8;     // records per rim staging buffer (2/warp)
 
 // Fixed-capacity bins filled in one pass: entry i of bin k lives at
 // list[k * cap + i]; the bin's cursor counts every append. Appends past the
@@ -987,32 +993,37 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
 }
 
 // Conservative test whether the soft triangle can cover a pixel centre of
-// 8x4 block (bx, by): false only if, for one barycentric coordinate, all
-// four corner centres are below -margin. The coordinates are affine in the
-// pixel centre; the margin (~170 float ulps of the terms' magnitude) bounds
-// the rounding of this float evaluation and of soft_covers' own.
+// 8x4 block (bx, by): false only if, for one barycentric coordinate, its
+// maximum over the rectangle of the block's pixel centres is below
+// -margin. The coordinates are affine in the pixel centre, so that maximum
+// is the value at the rectangle's centre plus |gradient| times the half
+// extents (3.5, 1.5); the margin (~80 float ulps of the largest magnitude
+// the products reach over the block) bounds the rounding of this float
+// evaluation and of soft_covers' own.
 __device__ __forceinline__ bool tri_touches_block(const FaceRec& r, int bx,
                                                   int by) {
-    const float xs[2] = {float(bx * 8) + 0.5f, float(bx * 8) + 7.5f};
-    const float ys[2] = {float(by * 4) + 0.5f, float(by * 4) + 3.5f};
+    const float cx = float(bx * 8) + 4.f, cy = float(by * 4) + 2.f;
     const float ia = fabsf(r.s_inv_area);
-    float mx0 = -3e38f, mx1 = -3e38f, mx2 = -3e38f, mag = 0.f;
-#pragma unroll
-    for (int i = 0; i < 2; i++)
-#pragma unroll
-        for (int j = 0; j < 2; j++) {
-            const float px = xs[i], py = ys[j];
-            const float a0 = (r.s1x - px) * (r.s2y - py), b0 = (r.s1y - py) * (r.s2x - px);
-            const float a1 = (r.s2x - px) * (r.s0y - py), b1 = (r.s2y - py) * (r.s0x - px);
-            const float l0 = (a0 - b0) * r.s_inv_area;
-            const float l1 = (a1 - b1) * r.s_inv_area;
-            mx0 = fmaxf(mx0, l0);
-            mx1 = fmaxf(mx1, l1);
-            mx2 = fmaxf(mx2, 1.f - l0 - l1);
-            mag = fmaxf(mag, (fabsf(a0) + fabsf(b0) + fabsf(a1) + fabsf(b1)) * ia);
-        }
+    const float a0 = (r.s1x - cx) * (r.s2y - cy), b0 = (r.s1y - cy) * (r.s2x - cx);
+    const float a1 = (r.s2x - cx) * (r.s0y - cy), b1 = (r.s2y - cy) * (r.s0x - cx);
+    const float l0 = (a0 - b0) * r.s_inv_area;
+    const float l1 = (a1 - b1) * r.s_inv_area;
+    const float g0x = (r.s1y - r.s2y) * r.s_inv_area;
+    const float g0y = (r.s2x - r.s1x) * r.s_inv_area;
+    const float g1x = (r.s2y - r.s0y) * r.s_inv_area;
+    const float g1y = (r.s0x - r.s2x) * r.s_inv_area;
+    const float e0 = fabsf(g0x) * 3.5f + fabsf(g0y) * 1.5f;
+    const float e1 = fabsf(g1x) * 3.5f + fabsf(g1y) * 1.5f;
+    const float e2 = fabsf(g0x + g1x) * 3.5f + fabsf(g0y + g1y) * 1.5f;
+    // an upper bound of the products' magnitudes at every pixel centre of
+    // the block (each factor widened by the half extent)
+    const float u0x = fabsf(r.s0x - cx) + 3.5f, u0y = fabsf(r.s0y - cy) + 1.5f;
+    const float u1x = fabsf(r.s1x - cx) + 3.5f, u1y = fabsf(r.s1y - cy) + 1.5f;
+    const float u2x = fabsf(r.s2x - cx) + 3.5f, u2y = fabsf(r.s2y - cy) + 1.5f;
+    const float mag = (u1x * u2y + u1y * u2x + u2x * u0y + u2y * u0x) * ia;
     const float margin = 1e-5f * (1.f + mag);
-    return !(mx0 < -margin || mx1 < -margin || mx2 < -margin);
+    return !(l0 + e0 < -margin || l1 + e1 < -margin ||
+             (1.f - l0 - l1) + e2 < -margin);
 }
 
 // Rim-phase binning: a safe face enters the bin of every open 8x4 block its
@@ -1060,17 +1071,116 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
     }
 }
 
+// Asynchronous 16-byte global -> shared copies (cp.async), committed and
+// waited for per thread in groups.
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
+    const unsigned d =
+            static_cast<unsigned>(__cvta_generic_to_shared(dst_smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 16;\n" ::"r"(d),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int kPending>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(kPending) : "memory");
+}
+
+// Starts the copy of the records ids[0, cn) into a warp's buffer (one
+// commit group per lane).
+__device__ __forceinline__ void rim_issue(const FaceRec* recs, const int* ids,
+                                          int cn, FaceRec* buf) {
+    const int lane = threadIdx.x & 31;
+    const float4* src = reinterpret_cast<const float4*>(recs);
+    float4* dst = reinterpret_cast<float4*>(buf);
+    for (int i = lane; i < cn * kRecVec4; i += 32) {
+        const int j = i / kRecVec4, q = i - j * kRecVec4;
+        cp_async16(dst + i, src + size_t(ids[j]) * kRecVec4 + q);
+    }
+    cp_async_commit();
+}
+
+// Folds the staged records buf[0, cn) of faces ids[0, cn) into the pixel's
+// survivor (kb: their sort keys, or null). The bounds are explained at
+// rim_block.
+__device__ __forceinline__ void rim_fold_chunk(
+        const SweepArgs& a, int x, int y, float px, float py, bool peel,
+        float prev, int cn, const FaceRec* buf, const int* ids,
+        const unsigned long long* kb, Survivor& s, bool& done) {
+    const float r2 = a.radius * a.radius;
+    for (int j = 0; j < cn; j++) {
+        if (done) break;
+        if (kb && s.depth < __uint_as_float(uint32_t(kb[j] >> 32))) {
+            done = true;  // this entry and all later ones lose
+            break;
+        }
+        const int f = ids[j];
+        const FaceRec& r = buf[j];
+        const uint32_t need = kFaceValid | kFaceSafe;
+        if ((r.flags & need) != need) continue;
+        if (x < r.bx0 || x > r.bx1 || y < r.by0 || y > r.by1) continue;
+        const float dx = fmaxf(fmaxf(r.lbx0 - px, px - r.lbx1), 0.f);
+        const float dy = fmaxf(fmaxf(r.lby0 - py, py - r.lby1), 0.f);
+        const float d2 = (dx * dx + dy * dy) * 0.998f;
+        if (s.depth < 1.f) {
+            const float t = 2.f * s.depth - 1.f;
+            if (d2 > t * t * r2) continue;  // bound above the survivor
+        }
+        const bool far = d2 >= r2;  // depth exactly 1
+        if (far && f < s.face) continue;  // 1.0 tie, older face
+        if (!soft_covers(px, py, r)) continue;
+        if (far) {
+            if (peel && 1.f <= prev + 1e-4f) continue;
+            fold(s, 1.f, f, false);
+        } else {
+            eval_full(s, px, py, r, f, a.radius, peel, prev);
+        }
+    }
+}
+
+// Face ids of the list entries [base, base + cn) of a rim block into ids
+// (lane < cn): from the sorted keys, the bin's list, or (identity) all
+// faces from the last.
+__device__ __forceinline__ void rim_load_ids(const SweepArgs& a,
+                                             const unsigned long long* keys,
+                                             const int* lst, bool sorted,
+                                             bool identity, int base, int cn,
+                                             int* ids) {
+    const int lane = threadIdx.x & 31;
+    if (lane < cn) {
+        if (sorted) {
+            const unsigned long long k = keys[base + lane];
+            const uint32_t lo = uint32_t(k);
+            ids[lane] = int(uint32_t(k >> 32) == __float_as_uint(1.f)
+                                    ? 0xffffffffu - lo
+                                    : lo);
+        } else {
+            ids[lane] = identity ? a.n_faces - 1 - (base + lane)
+                                 : lst[base + lane];
+        }
+    }
+    __syncwarp();
+}
+
 // Rim phase for the open pixels of an open 8x4 block: folds every fragment
 // of the faces in the block's bin (records staged per warp in shared
-// memory), pruned by the bbox depth bound. Fragments at |dist| >= radius
-// all have depth exactly 1, where the latest covering face wins: once a
-// pixel holds such a survivor, older faces at depth 1 are skipped without a
-// coverage test (in list order this costs ~ln(n) tests, as for a running
-// maximum).
+// memory, the next chunk's copy in flight while one is folded), pruned by
+// the bbox depth bound. Fragments at |dist| >= radius all have depth
+// exactly 1, where the latest covering face wins: once a pixel holds such
+// a survivor, older faces at depth 1 are skipped without a coverage test.
+//
+// The per-fragment bound is rim_depth_lb's, tested on squared distances:
+// with q = 0.999 d / R, lb = 0.5 + 0.5 min(q, 1) > depth  <=>  q > t =
+// 2 depth - 1 (t < 1), i.e. d^2 0.999^2 > t^2 R^2, and lb = 1 <=> d^2
+// 0.999^2 >= R^2. Using 0.998 < 0.999^2 keeps both bounds below the true
+// depth with the same ~1e-3 slack against rounding (~1e-7).
 template <class Epi>
-static __device__ void rim_block(const SweepArgs& a, FixedBins b2, int tile,
+static __device__ __forceinline__ void rim_block(const SweepArgs& a, FixedBins b2, int tile,
                                  int w, const int2* state, FaceRec* recs_w,
-                                 int* ids_w, Epi& epi) {
+                                 int* ids_w, unsigned long long* keys_w,
+                                 Epi& epi) {
     const int lane = threadIdx.x & 31;
     const int x = (tile % a.tiles_x) * kTile + (w & 1) * 8 + (lane & 7);
     const int y = (tile / a.tiles_x) * kTile + (w >> 1) * 4 + (lane >> 3);
@@ -1103,42 +1213,68 @@ static __device__ void rim_block(const SweepArgs& a, FixedBins b2, int tile,
     const int end = identity ? a.n_faces : (over ? b2.cap : n);
     const int* lst = b2.list + bin * b2.cap;
     const float4* src = reinterpret_cast<const float4*>(a.recs);
-    // Stages the records of ids_w[0..cn) and folds their fragments.
-    auto run = [&](int cn) {
-        __syncwarp();
-        float4* dst = reinterpret_cast<float4*>(recs_w);
-        for (int i = lane; i < cn * kRecVec4; i += 32) {
-            const int j = i / kRecVec4, q = i % kRecVec4;
-            dst[i] = src[size_t(ids_w[j]) * kRecVec4 + q];
+    // Front-to-back order when the list fits the key buffer: per entry the
+    // depth bound of the whole block (rim_depth_lb at the distance from the
+    // block's pixel-centre rectangle to the face's bbox; rounding is
+    // monotonic, so it is <= every pixel's own bound), ascending; entries
+    // whose bound is 1 (|dist| >= radius: depth exactly 1, latest face
+    // wins) by descending face. A pixel is done at the first entry whose
+    // bound is above its survivor's depth.
+    const bool sorted = !over && end > 0 && end <= kWarpSort;
+    if (sorted) {
+        const float xlo = float(bx * 8) + 0.5f, xhi = float(bx * 8) + 7.5f;
+        const float ylo = float(by * 4) + 0.5f, yhi = float(by * 4) + 3.5f;
+        for (int i = lane; i < end; i += 32) {
+            const int f = lst[i];
+            const float4 lbq = src[size_t(f) * kRecVec4 + kRecLbVec4];
+            const float dx = fmaxf(fmaxf(lbq.x - xhi, xlo - lbq.y), 0.f);
+            const float dy = fmaxf(fmaxf(lbq.z - yhi, ylo - lbq.w), 0.f);
+            const float d = sqrtf(dx * dx + dy * dy) * 0.999f;
+            const float lbb = 0.5f + 0.5f * std_min(d / a.radius, 1.f);
+            const uint32_t lo = lbb == 1.f ? 0xffffffffu - uint32_t(f)
+                                           : uint32_t(f);
+            keys_w[i] = (uint64_t(__float_as_uint(lbb)) << 32) | lo;
         }
         __syncwarp();
-        if (!open) return;
-        for (int j = 0; j < cn; j++) {
-            const int f = ids_w[j];
-            const FaceRec& r = recs_w[j];
-            const uint32_t need = kFaceValid | kFaceSafe;
-            if ((r.flags & need) != need) continue;
-            if (x < r.bx0 || x > r.bx1 || y < r.by0 || y > r.by1) continue;
-            const float lb = rim_depth_lb(px, py, r, a.radius);
-            if (lb > s.depth) continue;
-            if (lb == 1.f && f < s.face) continue;  // 1.0 tie, older face
-            if (!soft_covers(px, py, r)) continue;
-            if (lb == 1.f) {
-                // |dist| >= radius: the Eq.3 depth is exactly 1
-                if (peel && 1.f <= prev + 1e-4f) continue;
-                fold(s, 1.f, f, false);
+        if (end <= 32) {
+            unsigned long long k = lane < end ? keys_w[lane] : ~0ull;
+            k = warp_sort_asc(k);
+            __syncwarp();
+            keys_w[lane] = k;
+            __syncwarp();
+        } else {
+            warp_sort_smem(keys_w, end);
+        }
+    }
+    bool done = !open;
+    // double-buffered pass over the list: chunk c folds from buffer c & 1
+    // while chunk c + 1 is copied into the other
+    if (end > 0 && !__all_sync(0xffffffffu, done)) {
+        int cn = imin_(kRimChunk, end);
+        rim_load_ids(a, keys_w, lst, sorted, identity, 0, cn, ids_w);
+        rim_issue(a.recs, ids_w, cn, recs_w);
+        for (int base = 0, c = 0; base < end; base += kRimChunk, c ^= 1) {
+            const int nbase = base + kRimChunk;
+            const bool more = nbase < end && !__all_sync(0xffffffffu, done);
+            const int ncn = more ? imin_(kRimChunk, end - nbase) : 0;
+            if (more) {
+                int* nids = ids_w + (c ^ 1) * kRimChunk;
+                rim_load_ids(a, keys_w, lst, sorted, identity, nbase, ncn,
+                             nids);
+                rim_issue(a.recs, nids, ncn, recs_w + (c ^ 1) * kRimChunk);
+                cp_async_wait<1>();
             } else {
-                eval_full(s, px, py, r, f, a.radius, peel, prev);
+                cp_async_wait<0>();
             }
+            __syncwarp();
+            if (open)
+                rim_fold_chunk(a, x, y, px, py, peel, prev, cn,
+                               recs_w + c * kRimChunk, ids_w + c * kRimChunk,
+                               sorted ? keys_w + base : nullptr, s, done);
+            __syncwarp();  // buffer c is refilled two chunks on
+            if (!more) break;
+            cn = ncn;
         }
-    };
-    for (int base = 0; base < end; base += kRimChunk) {
-        const int cn = imin_(kRimChunk, end - base);
-        __syncwarp();
-        if (lane < cn)
-            ids_w[lane] = identity ? a.n_faces - 1 - (base + lane)
-                                   : lst[base + lane];
-        run(cn);
     }
     if (over && !identity) {
         // this block's spilled entries, kRimChunk scanned per step
@@ -1151,11 +1287,18 @@ static __device__ void rim_block(const SweepArgs& a, FixedBins b2, int tile,
             if (mm == 0u) continue;
             __syncwarp();
             if (match) ids_w[__popc(mm & ((1u << lane) - 1u))] = e.y;
-            run(__popc(mm));
+            __syncwarp();
+            rim_issue(a.recs, ids_w, __popc(mm), recs_w);
+            cp_async_wait<0>();
+            __syncwarp();
+            if (open)
+                rim_fold_chunk(a, x, y, px, py, peel, prev, __popc(mm),
+                               recs_w, ids_w, nullptr, s, done);
+            __syncwarp();
         }
     }
     epi(a, x, y, in, s);
-    __syncwarp();  // recs_w / ids_w reuse by the warp's next block
+    __syncwarp();  // buffers reused by the warp's next block
 }
 
 template <class Epi>
@@ -1219,8 +1362,9 @@ __global__ void __launch_bounds__(kTileThreads)
         k_rim(SweepArgs a0, FixedBins b2, const int2* state,
               size_t view_stride_recs, size_t view_stride_px,
               size_t view_stride_rim, Epi epi) {
-    __shared__ FaceRec recs_sh[8][kRimChunk];
-    __shared__ int ids_sh[8][kRimChunk];
+    __shared__ FaceRec recs_sh[8][2 * kRimChunk];
+    __shared__ int ids_sh[8][2 * kRimChunk];
+    __shared__ unsigned long long keys_sh[8][kWarpSort];
     const int wc = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_open = *b2.open_n;
     for (;;) {
@@ -1236,7 +1380,8 @@ __global__ void __launch_bounds__(kTileThreads)
         a.recs = a0.recs + a.v * view_stride_recs;
         a.rim = a0.rim + a.v * view_stride_rim;
         if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
-        rim_block(a, b2, tile, w, state, recs_sh[wc], ids_sh[wc], epi);
+        rim_block(a, b2, tile, w, state, recs_sh[wc], ids_sh[wc], keys_sh[wc],
+                  epi);
     }
 }
 constexpr int kRimCtas = 148 * 4;  // persistent grid of k_rim

@@ -269,18 +269,21 @@ __device__ __forceinline__ double sum_elem(float x) {
     return kSq ? double(x * x) : double(x);
 }
 
-constexpr int kRmsThreads = 512;
-// shared staging buffer (floats); each round stages a multiple of
-// kSumParts pixels, so a part's pixels keep their residue in every round
-constexpr int kStageFloats = kSumParts * 180;
+constexpr int kRmsThreads = 1024;
+// dynamic shared staging buffer of the SumAll kernels (floats): 19200
+// pixels x 3 components per round, within the 227 KB a block may opt into
+constexpr int kStageFloats = kSumParts * 900;
+constexpr int kStageBytes = kStageFloats * 4 + kSumParts * 4;
+static_assert(kStageBytes <= 227 * 1024, "SumAll staging above 227 KB");
+constexpr int kLoadBatch = 8;  // global loads in flight per thread
 
-// SumAll (f_ops.cpp:1119-1149, SumPartial 1087-1115) of x [n_px][nc] by
+// SumAll (f_ops.cpp:1119-1149, SumPartial 1087-1115) of x [n_px][kNc] by
 // one block of kRmsThreads threads; the result is valid in thread 0.
 // Above 256 pixels, part p (thread p < 64) sums the elements of pixels p,
 // p + 64, ... in pixel-then-component order in double, rounded to float;
-// the 64 parts are summed in double. Rounds of pixels are staged
-// in shared memory by the whole block (coalesced) so each part's serial
-// chain reads shared memory only.
+// the 64 parts are summed in double. The pixels are staged in shared
+// memory by the whole block (all of a batch's loads issued before its
+// stores), so each part's serial chain reads shared memory only.
 template <bool kSq, int kNc>
 __device__ float sum_all_block(const float* x, int n_px, float* stage,
                                float* parts) {
@@ -299,7 +302,20 @@ __device__ float sum_all_block(const float* x, int n_px, float* stage,
     for (int base = 0; base < n_px; base += round_px) {
         const int np = min(round_px, n_px - base);
         const float* src = x + size_t(base) * nc;
-        for (int i = tid; i < np * nc; i += blockDim.x) stage[i] = src[i];
+        const int total = np * nc;
+        for (int i0 = tid; i0 < total; i0 += kLoadBatch * kRmsThreads) {
+            float v[kLoadBatch];
+#pragma unroll
+            for (int k = 0; k < kLoadBatch; k++) {
+                const int i = i0 + k * kRmsThreads;
+                v[k] = i < total ? src[i] : 0.f;
+            }
+#pragma unroll
+            for (int k = 0; k < kLoadBatch; k++) {
+                const int i = i0 + k * kRmsThreads;
+                if (i < total) stage[i] = v[k];
+            }
+        }
         __syncthreads();
         if (tid < kSumParts) {
             // shared loads four pixels ahead of the dependent double adds
@@ -336,8 +352,9 @@ __device__ float sum_all_block(const float* x, int n_px, float* stage,
 // out[0] = SumAll(x) for x [n_px][nc] (op level).
 __global__ void __launch_bounds__(kRmsThreads)
 k_sum_all(const float* x, int n_px, int nc, float* out) {
-    __shared__ float stage[kStageFloats];
-    __shared__ float parts[kSumParts];
+    extern __shared__ float dyn[];
+    float* stage = dyn;
+    float* parts = dyn + kStageFloats;
     float s = 0.f;
     switch (nc) {
         case 1: s = sum_all_block<false, 1>(x, n_px, stage, parts); break;
@@ -353,11 +370,23 @@ k_sum_all(const float* x, int n_px, int nc, float* out) {
 __global__ void __launch_bounds__(kRmsThreads)
 k_reg_rms(const float* g, const float* glap, const float* gnrm, int n_verts,
           float inv_cnt, float* rms) {
-    __shared__ float stage[kStageFloats];
-    __shared__ float parts[kSumParts];
+    extern __shared__ float dyn[];
+    float* stage = dyn;
+    float* parts = dyn + kStageFloats;
     const float* x = blockIdx.x == 0 ? g : (blockIdx.x == 1 ? glap : gnrm);
     const float s = sum_all_block<true, 3>(x, n_verts, stage, parts);
     if (threadIdx.x == 0) rms[blockIdx.x] = sqrtf(s * inv_cnt + 1e-24f);
+}
+
+// Opts the SumAll kernels into kStageBytes of dynamic shared memory on the
+// current device (host side, outside any stream capture).
+void sum_all_setup() {
+    DRESSI_CUDA(cudaFuncSetAttribute(
+            k_sum_all, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            kStageBytes));
+    DRESSI_CUDA(cudaFuncSetAttribute(
+            k_reg_rms, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            kStageBytes));
 }
 
 // out = (g + glap * s_lap) + gnrm * s_nrm with s = rms(g) / rms(term) *
@@ -404,15 +433,15 @@ void vertex_terms_op(const float* pos, int n_verts, const float* nbrs,
 void sum_all_op(const float* x, int n_px, int nc, float* out,
                 cudaStream_t s) {
     ProfScope ps("sum_all", s);
-    k_sum_all<<<1, kRmsThreads, 0, s>>>(x, n_px, nc, out);
+    k_sum_all<<<1, kRmsThreads, kStageBytes, s>>>(x, n_px, nc, out);
     check_launch();
 }
 
 void reg_rms_op(const float* g, const float* glap, const float* gnrm,
                 int n_verts, float* rms, cudaStream_t s) {
     ProfScope ps("reg_rms", s);
-    k_reg_rms<<<3, kRmsThreads, 0, s>>>(g, glap, gnrm, n_verts,
-                                        1.f / float(n_verts * 3), rms);
+    k_reg_rms<<<3, kRmsThreads, kStageBytes, s>>>(
+            g, glap, gnrm, n_verts, 1.f / float(n_verts * 3), rms);
     check_launch();
 }
 
