@@ -243,16 +243,22 @@ class ClockSampler:
 
 # ---------------------------------------------------- byte model (roofline)
 
-def iteration_bytes(views: int, res: int, n_verts: int, n_faces: int) -> float:
+def iteration_bytes(views: int, res: int, n_verts: int, n_faces: int,
+                    reg: bool = False) -> float:
     """Algorithmic HBM bytes of one fwd+bwd+Adam silhouette iteration (the
     per-iteration figure of the survey's byte model): 16 B per view-pixel
     (target read 4, triangle-ID write 4, depth write 4, triangle-ID read in
     the backward 4), per view the clip positions written and read (32 B per
     vertex) and the face indices (12 B per face), and the replicated Adam
     (read p, g, m, v = 48 B, write p, m, v = 36 B per vertex) plus the
-    gradient buffer (12 B written + read per vertex)."""
+    gradient buffer (12 B written + read per vertex). With the regulariser:
+    per vertex pos read 12, neighbour and incident-face tables 48, g_lap and
+    g_nrm written 24, the three RMS reads 36 and Adam's extra reads of
+    g_lap / g_nrm 24 (144 B); per face the indices, the adjacency and the
+    NC term written 36 B."""
+    reg_bytes = (144.0 * n_verts + 36.0 * n_faces) if reg else 0.0
     return (16.0 * views * res * res + views * (32.0 * n_verts + 12.0 * n_faces)
-            + (48.0 + 36.0 + 24.0) * n_verts)
+            + (48.0 + 36.0 + 24.0) * n_verts + reg_bytes)
 
 
 def texture_iteration_bytes(views: int, res: int, tex: int) -> float:
@@ -401,7 +407,8 @@ def run_ours(args):
     if args.config == "c2":
         alg = texture_iteration_bytes(nvw, args.res, sc.tex_size)
     else:
-        alg = iteration_bytes(nvw, args.res, sc.n_verts, sc.n_faces)
+        alg = iteration_bytes(nvw, args.res, sc.n_verts, sc.n_faces,
+                              reg=args.laplacian != 0.0 or args.normal != 0.0)
     peak, peak_kind = peaks()
     ms_step = ms_max / args.steps
     achieved = alg / (ms_step * 1e-3) / 1e9
