@@ -27,6 +27,8 @@
  *  - RasterizeSoft backward (ColSum(GatherDistGrad))
  *                                              src/core/f_ops.cpp:1218-1358
  *  - dressi.torch.rasterize_soft / rasterize   python/dressi/torch/ops.py:682, 118
+ *  - F::EquirectSample / IrradianceConv / PrefilterConv /
+ *    BrdfIntegrationLut / AvgPool2x2      include/dressi/f.h (IBL ops)
  *  - F::VertexNeighborMean / NormalConsistency* / SumAll and the mesh
  *    tables of the silhouette optimizer         include/dressi/f.h:97, 240-255;
  *                                              include/dressi/mesh_utils.h:26-34
@@ -275,6 +277,46 @@ int dressi_regularized_grad(const float* pos, uint32_t n_verts,
                             uint32_t vf_deg, const float* g, float laplacian,
                             float normal, float* out, uint32_t* status,
                             void* stream);
+
+/* Split-sum IBL ops (config C5; f_ops.cpp:2785-3415, ibl_math.h). Maps
+ * are equirect images [h][w][n_comp] (n_comp 1..4), directions [n_px][3].
+ * Within float tolerance of the reference (its transcendentals are the
+ * host libm's, here CUDA's); AvgPool2x2 bit-exact.
+ *
+ * F::EquirectSample: 4-tap bilinear (u wraps, v clamps) along the
+ * normalised direction, 0 for |dir| < 1e-8; its map transpose (g_map
+ * written). */
+int dressi_equirect_sample(const float* map, uint32_t mw, uint32_t mh,
+                           uint32_t n_comp, const float* dir, uint64_t n_px,
+                           float* out, void* stream);
+int dressi_equirect_sample_grad(const float* gy, const float* dir,
+                                uint64_t n_px, uint32_t mw, uint32_t mh,
+                                uint32_t n_comp, float* g_map, void* stream);
+/* F::IrradianceConv (E(N)/pi of env [sh][sw] into [oh][ow]) and its exact
+ * transpose (g_env written). */
+int dressi_irradiance_conv(const float* env, uint32_t sw, uint32_t sh,
+                           uint32_t n_comp, uint32_t ow, uint32_t oh,
+                           float* out, void* stream);
+int dressi_irradiance_conv_grad(const float* gy, uint32_t ow, uint32_t oh,
+                                uint32_t n_comp, uint32_t sw, uint32_t sh,
+                                float* g_env, void* stream);
+/* F::PrefilterConv (GGX-NDF-weighted, normalised by PrefilterConvNorm,
+ * alpha = max(roughness, 0.045)^2) and its exact transpose. */
+int dressi_prefilter_conv(const float* env, uint32_t sw, uint32_t sh,
+                          uint32_t n_comp, uint32_t ow, uint32_t oh,
+                          float roughness, float* out, void* stream);
+int dressi_prefilter_conv_grad(const float* gy, uint32_t ow, uint32_t oh,
+                               uint32_t n_comp, uint32_t sw, uint32_t sh,
+                               float roughness, float* g_env, void* stream);
+/* F::BrdfIntegrationLut: out [h][w][2] = (A, B) over (NdotV, roughness). */
+int dressi_brdf_lut(uint32_t w, uint32_t h, uint32_t n_samples, float* out,
+                    void* stream);
+/* F::AvgPool2x2 (even sizes; out [h/2][w/2][n]) and its transpose (g_x
+ * [h][w][n] written). */
+int dressi_avg_pool2x2(const float* x, uint32_t w, uint32_t h,
+                       uint32_t n_comp, float* out, void* stream);
+int dressi_avg_pool2x2_grad(const float* gy, uint32_t w, uint32_t h,
+                            uint32_t n_comp, float* g_x, void* stream);
 
 /* ------------------------------------------------------------------------
  * Plans: one fused fwd + bwd + Adam iteration, resident on one device,

@@ -129,6 +129,21 @@ SIGNATURES = {
     "dressi_regularized_grad": (C.c_int, [_vp, _u32, _vp, _u32, _vp, _u32,
                                           _vp, _vp, _u32, _vp, C.c_float,
                                           C.c_float, _vp, _vp, _vp]),
+    "dressi_equirect_sample": (C.c_int, [_vp, _u32, _u32, _u32, _vp,
+                                         C.c_uint64, _vp, _vp]),
+    "dressi_equirect_sample_grad": (C.c_int, [_vp, _vp, C.c_uint64, _u32,
+                                              _u32, _u32, _vp, _vp]),
+    "dressi_irradiance_conv": (C.c_int, [_vp, _u32, _u32, _u32, _u32, _u32,
+                                         _vp, _vp]),
+    "dressi_irradiance_conv_grad": (C.c_int, [_vp, _u32, _u32, _u32, _u32,
+                                              _u32, _vp, _vp]),
+    "dressi_prefilter_conv": (C.c_int, [_vp, _u32, _u32, _u32, _u32, _u32,
+                                        C.c_float, _vp, _vp]),
+    "dressi_prefilter_conv_grad": (C.c_int, [_vp, _u32, _u32, _u32, _u32,
+                                             _u32, C.c_float, _vp, _vp]),
+    "dressi_brdf_lut": (C.c_int, [_u32, _u32, _u32, _vp, _vp]),
+    "dressi_avg_pool2x2": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp]),
+    "dressi_avg_pool2x2_grad": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp]),
     "dressi_texture_plan_create": (C.c_int, [C.POINTER(TextureDesc),
                                              C.POINTER(_vp)]),
     "dressi_image_fit_plan_create": (C.c_int, [_u32, _u32, C.c_float, C.c_int,

@@ -921,6 +921,130 @@ int dressi_regularized_grad(const float* pos, uint32_t n_verts,
     });
 }
 
+// ---------------------------------------------------- split-sum IBL ops
+
+namespace {
+
+void ibl_checks(const void* a, const void* b, uint32_t n_comp) {
+    DRESSI_REQUIRE(a && b, "null pointer");
+    DRESSI_REQUIRE(n_comp >= 1 && n_comp <= 4, "IBL op: 1..4 components");
+}
+
+}  // namespace
+
+int dressi_equirect_sample(const float* map, uint32_t mw, uint32_t mh,
+                           uint32_t n_comp, const float* dir, uint64_t n_px,
+                           float* out, void* stream) {
+    return guarded([&] {
+        ibl_checks(map, dir, n_comp);
+        DRESSI_REQUIRE(out, "null pointer");
+        DRESSI_REQUIRE(mw >= 1 && mh >= 1, "EquirectSample: empty map");
+        equirect_sample_op(map, int(mw), int(mh), int(n_comp), dir,
+                           (long long)n_px, out, as_stream(stream));
+    });
+}
+
+int dressi_equirect_sample_grad(const float* gy, const float* dir,
+                                uint64_t n_px, uint32_t mw, uint32_t mh,
+                                uint32_t n_comp, float* g_map, void* stream) {
+    return guarded([&] {
+        ibl_checks(gy, dir, n_comp);
+        DRESSI_REQUIRE(g_map, "null pointer");
+        DRESSI_REQUIRE(mw >= 1 && mh >= 1, "EquirectSample grad: empty map");
+        equirect_sample_bwd_op(gy, dir, (long long)n_px, int(mw), int(mh),
+                               int(n_comp), g_map, as_stream(stream));
+    });
+}
+
+int dressi_irradiance_conv(const float* env, uint32_t sw, uint32_t sh,
+                           uint32_t n_comp, uint32_t ow, uint32_t oh,
+                           float* out, void* stream) {
+    return guarded([&] {
+        ibl_checks(env, out, n_comp);
+        DRESSI_REQUIRE(sw && sh && ow && oh, "IrradianceConv: empty image");
+        cudaStream_t s = as_stream(stream);
+        AsyncScratch sc(env_conv_scratch_floats(int(sw), int(sh), int(ow),
+                                                int(oh)) * 4, s);
+        irradiance_conv_op(env, int(sw), int(sh), int(n_comp), int(ow),
+                           int(oh), out, static_cast<float*>(sc.p), s);
+    });
+}
+
+int dressi_irradiance_conv_grad(const float* gy, uint32_t ow, uint32_t oh,
+                                uint32_t n_comp, uint32_t sw, uint32_t sh,
+                                float* g_env, void* stream) {
+    return guarded([&] {
+        ibl_checks(gy, g_env, n_comp);
+        DRESSI_REQUIRE(sw && sh && ow && oh, "IrradianceConv grad: empty image");
+        cudaStream_t s = as_stream(stream);
+        AsyncScratch sc(env_conv_scratch_floats(int(sw), int(sh), int(ow),
+                                                int(oh)) * 4, s);
+        irradiance_conv_bwd_op(gy, int(ow), int(oh), int(n_comp), int(sw),
+                               int(sh), g_env, static_cast<float*>(sc.p), s);
+    });
+}
+
+int dressi_prefilter_conv(const float* env, uint32_t sw, uint32_t sh,
+                          uint32_t n_comp, uint32_t ow, uint32_t oh,
+                          float roughness, float* out, void* stream) {
+    return guarded([&] {
+        ibl_checks(env, out, n_comp);
+        DRESSI_REQUIRE(sw && sh && ow && oh, "PrefilterConv: empty image");
+        cudaStream_t s = as_stream(stream);
+        AsyncScratch sc(env_conv_scratch_floats(int(sw), int(sh), int(ow),
+                                                int(oh)) * 4, s);
+        prefilter_conv_op(env, int(sw), int(sh), int(n_comp), int(ow),
+                          int(oh), roughness, out,
+                          static_cast<float*>(sc.p), s);
+    });
+}
+
+int dressi_prefilter_conv_grad(const float* gy, uint32_t ow, uint32_t oh,
+                               uint32_t n_comp, uint32_t sw, uint32_t sh,
+                               float roughness, float* g_env, void* stream) {
+    return guarded([&] {
+        ibl_checks(gy, g_env, n_comp);
+        DRESSI_REQUIRE(sw && sh && ow && oh, "PrefilterConv grad: empty image");
+        cudaStream_t s = as_stream(stream);
+        AsyncScratch sc(env_conv_scratch_floats(int(sw), int(sh), int(ow),
+                                                int(oh)) * 4, s);
+        prefilter_conv_bwd_op(gy, int(ow), int(oh), int(n_comp), int(sw),
+                              int(sh), roughness, g_env,
+                              static_cast<float*>(sc.p), s);
+    });
+}
+
+int dressi_brdf_lut(uint32_t w, uint32_t h, uint32_t n_samples, float* out,
+                    void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(out, "null pointer");
+        DRESSI_REQUIRE(w && h && n_samples,
+                       "BrdfIntegrationLut: empty size or no samples");
+        brdf_lut_op(int(w), int(h), int(n_samples), out, as_stream(stream));
+    });
+}
+
+int dressi_avg_pool2x2(const float* x, uint32_t w, uint32_t h,
+                       uint32_t n_comp, float* out, void* stream) {
+    return guarded([&] {
+        ibl_checks(x, out, n_comp);
+        DRESSI_REQUIRE(w >= 2 && h >= 2 && w % 2 == 0 && h % 2 == 0,
+                       "AvgPool2x2: even sizes only");
+        avg_pool2x2_op(x, int(w), int(h), int(n_comp), out, as_stream(stream));
+    });
+}
+
+int dressi_avg_pool2x2_grad(const float* gy, uint32_t w, uint32_t h,
+                            uint32_t n_comp, float* g_x, void* stream) {
+    return guarded([&] {
+        ibl_checks(gy, g_x, n_comp);
+        DRESSI_REQUIRE(w >= 2 && h >= 2 && w % 2 == 0 && h % 2 == 0,
+                       "AvgPool2x2 grad: even sizes only");
+        avg_pool2x2_bwd_op(gy, int(w), int(h), int(n_comp), g_x,
+                           as_stream(stream));
+    });
+}
+
 int dressi_texture_plan_create(const dressi_texture_desc* desc,
                                dressi_plan* out) {
     return guarded([&] {

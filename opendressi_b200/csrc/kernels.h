@@ -233,6 +233,35 @@ void reg_rms_op(const float* g, const float* glap, const float* gnrm,
 void reg_combine_op(const float* g, const float* glap, const float* gnrm,
                     const float* rms, float laplacian, float normal,
                     int n_verts, float* out, cudaStream_t s);
+// --- split-sum IBL ops (ibl.cu) ---
+void equirect_sample_op(const float* map, int mw, int mh, int n,
+                        const float* dir, long long n_px, float* out,
+                        cudaStream_t s);
+// g_map [mh][mw][n] is overwritten (zeroed, then scattered into).
+void equirect_sample_bwd_op(const float* gy, const float* dir, long long n_px,
+                            int mw, int mh, int n, float* g_map,
+                            cudaStream_t s);
+// Scratch floats of the convolutions: direction tables of both sides and
+// the prefilter normaliser.
+size_t env_conv_scratch_floats(int sw, int sh, int ow, int oh);
+void irradiance_conv_op(const float* env, int sw, int sh, int n, int ow,
+                        int oh, float* out, float* scratch, cudaStream_t s);
+void irradiance_conv_bwd_op(const float* gy, int ow, int oh, int n, int sw,
+                            int sh, float* g_env, float* scratch,
+                            cudaStream_t s);
+float prefilter_alpha(float roughness);
+void prefilter_conv_op(const float* env, int sw, int sh, int n, int ow,
+                       int oh, float roughness, float* out, float* scratch,
+                       cudaStream_t s);
+void prefilter_conv_bwd_op(const float* gy, int ow, int oh, int n, int sw,
+                           int sh, float roughness, float* g_env,
+                           float* scratch, cudaStream_t s);
+void brdf_lut_op(int w, int h, int n_samples, float* out, cudaStream_t s);
+void avg_pool2x2_op(const float* x, int w, int h, int n, float* out,
+                    cudaStream_t s);
+void avg_pool2x2_bwd_op(const float* gy, int w, int h, int n, float* g,
+                        cudaStream_t s);
+
 // One full single-device iteration.
 void sil_iteration(const SoftDims& d, const SilParams& p,
                    const SilBuffers& b, cudaStream_t s);

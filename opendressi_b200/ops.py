@@ -32,6 +32,15 @@ __all__ = [
     "normal_consistency_vertex_grad",
     "sum_all",
     "regularized_grad",
+    "equirect_sample",
+    "equirect_sample_grad",
+    "irradiance_conv",
+    "irradiance_conv_grad",
+    "prefilter_conv",
+    "prefilter_conv_grad",
+    "brdf_lut",
+    "avg_pool2x2",
+    "avg_pool2x2_grad",
     "check_status",
 ]
 
@@ -459,4 +468,120 @@ def regularized_grad(pos, faces, g, laplacian: float, normal: float,
            st.data_ptr(), _stream())
     if check:
         check_status(st)
+    return out
+
+
+# ---- split-sum IBL (config C5; f_ops.cpp:2785-3415)
+
+def _img3(t, name):
+    t = _dev(t, name)
+    if t.dim() == 2:
+        t = t.unsqueeze(-1)
+    if t.dim() != 3 or not 1 <= t.shape[2] <= 4:
+        raise N.DressiError(N.ERR_INVALID, f"{name} must be [H, W, C<=4]")
+    return t.contiguous()
+
+
+def equirect_sample(env, dirs):
+    """F::EquirectSample: env [H, W, C] sampled along dirs [..., 3]."""
+    env = _img3(env, "env")
+    dirs = _dev(dirs, "dirs")
+    n = env.shape[2]
+    out = torch.empty(dirs.shape[:-1] + (n,), dtype=torch.float32,
+                      device=env.device)
+    N.call("dressi_equirect_sample", env.data_ptr(), env.shape[1],
+           env.shape[0], n, dirs.data_ptr(), dirs.numel() // 3,
+           out.data_ptr(), _stream())
+    return out
+
+
+def equirect_sample_grad(gy, dirs, width: int, height: int):
+    """The map gradient of equirect_sample: gy [..., C] -> [H, W, C]."""
+    gy = _dev(gy, "gy")
+    dirs = _dev(dirs, "dirs")
+    n = gy.shape[-1]
+    out = torch.empty((height, width, n), dtype=torch.float32,
+                      device=gy.device)
+    N.call("dressi_equirect_sample_grad", gy.data_ptr(), dirs.data_ptr(),
+           dirs.numel() // 3, width, height, n, out.data_ptr(), _stream())
+    return out
+
+
+def irradiance_conv(env, width: int, height: int):
+    """F::IrradianceConv: env [H, W, C] -> [height, width, C]."""
+    env = _img3(env, "env")
+    n = env.shape[2]
+    out = torch.empty((height, width, n), dtype=torch.float32,
+                      device=env.device)
+    N.call("dressi_irradiance_conv", env.data_ptr(), env.shape[1],
+           env.shape[0], n, width, height, out.data_ptr(), _stream())
+    return out
+
+
+def irradiance_conv_grad(gy, width: int, height: int):
+    """The env gradient of irradiance_conv: gy [h, w, C] -> [height,
+    width, C]."""
+    gy = _img3(gy, "gy")
+    n = gy.shape[2]
+    out = torch.empty((height, width, n), dtype=torch.float32,
+                      device=gy.device)
+    N.call("dressi_irradiance_conv_grad", gy.data_ptr(), gy.shape[1],
+           gy.shape[0], n, width, height, out.data_ptr(), _stream())
+    return out
+
+
+def prefilter_conv(env, width: int, height: int, roughness: float):
+    """F::PrefilterConv: env [H, W, C] -> [height, width, C]."""
+    env = _img3(env, "env")
+    n = env.shape[2]
+    out = torch.empty((height, width, n), dtype=torch.float32,
+                      device=env.device)
+    N.call("dressi_prefilter_conv", env.data_ptr(), env.shape[1],
+           env.shape[0], n, width, height, float(roughness), out.data_ptr(),
+           _stream())
+    return out
+
+
+def prefilter_conv_grad(gy, width: int, height: int, roughness: float):
+    """The env gradient of prefilter_conv: gy [h, w, C] -> [height, width,
+    C]."""
+    gy = _img3(gy, "gy")
+    n = gy.shape[2]
+    out = torch.empty((height, width, n), dtype=torch.float32,
+                      device=gy.device)
+    N.call("dressi_prefilter_conv_grad", gy.data_ptr(), gy.shape[1],
+           gy.shape[0], n, width, height, float(roughness), out.data_ptr(),
+           _stream())
+    return out
+
+
+def brdf_lut(width: int = 256, height: int = 256, n_samples: int = 512,
+             device=None):
+    """F::BrdfIntegrationLut: [height, width, 2] (A, B)."""
+    dev = device if device is not None else torch.device("cuda")
+    out = torch.empty((height, width, 2), dtype=torch.float32, device=dev)
+    N.call("dressi_brdf_lut", width, height, n_samples, out.data_ptr(),
+           _stream())
+    return out
+
+
+def avg_pool2x2(x):
+    """F::AvgPool2x2: [H, W, C] -> [H/2, W/2, C] (even sizes)."""
+    x = _img3(x, "x")
+    h, w, n = x.shape
+    out = torch.empty((h // 2, w // 2, n), dtype=torch.float32,
+                      device=x.device)
+    N.call("dressi_avg_pool2x2", x.data_ptr(), w, h, n, out.data_ptr(),
+           _stream())
+    return out
+
+
+def avg_pool2x2_grad(gy):
+    """The transpose of avg_pool2x2: [h, w, C] -> [2h, 2w, C]."""
+    gy = _img3(gy, "gy")
+    h, w, n = gy.shape
+    out = torch.empty((2 * h, 2 * w, n), dtype=torch.float32,
+                      device=gy.device)
+    N.call("dressi_avg_pool2x2_grad", gy.data_ptr(), 2 * w, 2 * h, n,
+           out.data_ptr(), _stream())
     return out

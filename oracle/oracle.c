@@ -2021,6 +2021,385 @@ int orc_regularized_grad(const float* pos, uint32_t n_verts, const float* faces,
     return 0;
 }
 
+/* ------------------------------------------------ split-sum IBL (C5) */
+
+/* Constants of src/core/ibl_math.h:16-19 (float literals). */
+#define IBL_PI 3.14159265358979323846f
+#define IBL_TWO_PI 6.28318530717958647692f
+#define IBL_INV_PI 0.31830988618379067154f
+#define IBL_INV_TWO_PI 0.15915494309189533577f
+
+static inline float dot3(const float a[3], const float b[3]) {
+    return a[0] * b[0] + a[1] * b[1] + a[2] * b[2];
+}
+
+/* EquirectUvFromDir (ibl_math.h:39-44): u wraps at the atan2 seam, v = 0
+ * at +Y. */
+static void equirect_uv(const float d[3], float* u, float* v) {
+    *u = atan2f(d[2], d[0]) * IBL_INV_TWO_PI + 0.5f;
+    const float y = d[1] < -1.f ? -1.f : (d[1] > 1.f ? 1.f : d[1]);
+    *v = acosf(y) * IBL_INV_PI;
+}
+
+/* DirFromEquirectUv (ibl_math.h:47-52) */
+static void equirect_dir(float u, float v, float d[3]) {
+    const float phi = (u - 0.5f) * IBL_TWO_PI;
+    const float theta = v * IBL_PI;
+    const float st = sinf(theta);
+    d[0] = st * cosf(phi);
+    d[1] = cosf(theta);
+    d[2] = st * sinf(phi);
+}
+
+/* BilerpWrap (ibl_math.h:56-86): 4 taps, u wraps, v clamps; taps in (dy,
+ * dx) order. Calls tap(x, y, weight) through the caller's loop instead of
+ * summing when out is NULL (used by the transposes). */
+static void bilerp_wrap_taps(uint32_t w, uint32_t h, float u, float v,
+                             int tx[4], int ty[4], float tw[4]) {
+    const float sx = u * (float)w - 0.5f;
+    const float sy = v * (float)h - 0.5f;
+    const int ix = to_i32(floorf(sx));
+    const int iy = to_i32(floorf(sy));
+    const float fx = sx - (float)ix;
+    const float fy = sy - (float)iy;
+    int k = 0;
+    for (int dy = 0; dy <= 1; dy++)
+        for (int dx = 0; dx <= 1; dx++, k++) {
+            int x = ix + dx;
+            if (x < 0) x += (int)w;
+            if (x >= (int)w) x -= (int)w;
+            int y = iy + dy;
+            y = y < 0 ? 0 : (y > (int)h - 1 ? (int)h - 1 : y);
+            tx[k] = x;
+            ty[k] = y;
+            tw[k] = (dx == 0 ? 1.f - fx : fx) * (dy == 0 ? 1.f - fy : fy);
+        }
+}
+
+/* The direction of a dir-image pixel, normalised; 0 for |d| < 1e-8 (the
+ * rasterizer's background; f_ops.cpp:2944-2950). */
+static int unit_dir(const float* p, float d[3]) {
+    d[0] = p[0];
+    d[1] = p[1];
+    d[2] = p[2];
+    const float len = sqrtf(dot3(d, d));
+    if (len < 1e-8f) return 0;
+    d[0] = d[0] / len;
+    d[1] = d[1] / len;
+    d[2] = d[2] / len;
+    return 1;
+}
+
+/* EquirectSample (f_ops.cpp:2913-2964): map [mh][mw][n] sampled along dir
+ * [n_px][3] -> out [n_px][n]. */
+void orc_equirect_sample(const float* map, uint32_t mw, uint32_t mh,
+                         uint32_t n, const float* dir, size_t n_px,
+                         float* out) {
+    for (size_t p = 0; p < n_px; p++) {
+        float* o = &out[p * n];
+        for (uint32_t c = 0; c < n; c++) o[c] = 0.f;
+        float d[3], u, v;
+        if (!unit_dir(&dir[p * 3], d)) continue;
+        equirect_uv(d, &u, &v);
+        int tx[4], ty[4];
+        float tw[4];
+        bilerp_wrap_taps(mw, mh, u, v, tx, ty, tw);
+        for (int k = 0; k < 4; k++) {
+            const float* e = &map[((size_t)ty[k] * mw + tx[k]) * n];
+            for (uint32_t c = 0; c < n; c++) o[c] += tw[k] * e[c];
+        }
+    }
+}
+
+/* EquirectSampleBwd + TileSum (f_ops.cpp:2831-2909, 2785-2821): the exact
+ * transpose w.r.t. the map, accumulated in k band partials of the dir
+ * image (k = the smallest power of two with map texels * k >= 65536, at
+ * most the dir height), each summed in pixel order, then added in band
+ * order. gy [dh][dw][n], dir [dh][dw][3] -> g_map [mh][mw][n]. */
+int orc_equirect_sample_bwd(const float* gy, const float* dir, uint32_t dw,
+                            uint32_t dh, uint32_t mw, uint32_t mh, uint32_t n,
+                            float* g_map) {
+    uint32_t k = 1;
+    while ((size_t)mw * mh * k < 65536 && k < dh) k *= 2;
+    const uint32_t rows_per = (dh + k - 1) / k;
+    const size_t plane = (size_t)mw * mh * n;
+    float* part = (float*)calloc(plane * k, sizeof(float));
+    if (!part) return fail("oom");
+    for (uint32_t py = 0; py < dh; py++) {
+        float* dst = part + plane * (py / rows_per);
+        for (uint32_t px = 0; px < dw; px++) {
+            const size_t p = (size_t)py * dw + px;
+            float d[3], u, v;
+            if (!unit_dir(&dir[p * 3], d)) continue;
+            equirect_uv(d, &u, &v);
+            int tx[4], ty[4];
+            float tw[4];
+            bilerp_wrap_taps(mw, mh, u, v, tx, ty, tw);
+            for (int q = 0; q < 4; q++) {
+                float* o = &dst[((size_t)ty[q] * mw + tx[q]) * n];
+                for (uint32_t c = 0; c < n; c++) o[c] += gy[p * n + c] * tw[q];
+            }
+        }
+    }
+    for (size_t i = 0; i < plane; i++) g_map[i] = 0.f;
+    for (uint32_t b = 0; b < k; b++)
+        for (size_t i = 0; i < plane; i++) g_map[i] += part[plane * b + i];
+    free(part);
+    return 0;
+}
+
+/* IrradianceConv (f_ops.cpp:3023-3105): out(N) = 2 pi / (sw sh) * sum_s
+ * max(N . d_s, 0) sin(theta_s) env(s), summed in source row-major order
+ * per output texel. env [sh][sw][n] -> out [oh][ow][n]. */
+void orc_irradiance_conv(const float* env, uint32_t sw, uint32_t sh,
+                         uint32_t n, uint32_t ow, uint32_t oh, float* out) {
+    const float scale = IBL_TWO_PI / ((float)sw * (float)sh);
+    for (uint32_t oy = 0; oy < oh; oy++)
+        for (uint32_t ox = 0; ox < ow; ox++) {
+            float N[3];
+            equirect_dir(((float)ox + 0.5f) / (float)ow,
+                         ((float)oy + 0.5f) / (float)oh, N);
+            float* o = &out[((size_t)oy * ow + ox) * n];
+            for (uint32_t c = 0; c < n; c++) o[c] = 0.f;
+            for (uint32_t sy = 0; sy < sh; sy++) {
+                const float sv = ((float)sy + 0.5f) / (float)sh;
+                const float sin_th = sinf(sv * IBL_PI);
+                for (uint32_t sx = 0; sx < sw; sx++) {
+                    float d[3];
+                    equirect_dir(((float)sx + 0.5f) / (float)sw, sv, d);
+                    const float nd = dot3(N, d);
+                    const float w = (nd < 0.f ? 0.f : nd) * sin_th;
+                    const float* e = &env[((size_t)sy * sw + sx) * n];
+                    for (uint32_t c = 0; c < n; c++) o[c] += e[c] * w;
+                }
+            }
+            for (uint32_t c = 0; c < n; c++) o[c] *= scale;
+        }
+}
+
+/* IrradianceConvBwd (f_ops.cpp:2970-3019): the exact transpose, per source
+ * texel the sum over output texels in row-major order, times sin and the
+ * scale. gy [oh][ow][n] -> g_env [sh][sw][n]. */
+void orc_irradiance_conv_bwd(const float* gy, uint32_t ow, uint32_t oh,
+                             uint32_t n, uint32_t sw, uint32_t sh,
+                             float* g_env) {
+    const float scale = IBL_TWO_PI / ((float)sw * (float)sh);
+    for (uint32_t sy = 0; sy < sh; sy++) {
+        const float sv = ((float)sy + 0.5f) / (float)sh;
+        const float sin_th = sinf(sv * IBL_PI);
+        for (uint32_t sx = 0; sx < sw; sx++) {
+            float d[3];
+            equirect_dir(((float)sx + 0.5f) / (float)sw, sv, d);
+            float* o = &g_env[((size_t)sy * sw + sx) * n];
+            for (uint32_t c = 0; c < n; c++) o[c] = 0.f;
+            for (uint32_t ty = 0; ty < oh; ty++)
+                for (uint32_t tx = 0; tx < ow; tx++) {
+                    float N[3];
+                    equirect_dir(((float)tx + 0.5f) / (float)ow,
+                                 ((float)ty + 0.5f) / (float)oh, N);
+                    const float nd = dot3(N, d);
+                    const float w = (nd < 0.f ? 0.f : nd) * sin_th;
+                    const float* g = &gy[((size_t)ty * ow + tx) * n];
+                    for (uint32_t c = 0; c < n; c++) o[c] += g[c] * w;
+                }
+            for (uint32_t c = 0; c < n; c++) o[c] *= scale;
+        }
+    }
+}
+
+/* GgxConvWeight (ibl_math.h:160-168) */
+static inline float ggx_conv_weight(float c, float alpha) {
+    if (c <= 0.f) return 0.f;
+    const float ch2 = (1.f + c) * 0.5f;
+    const float a2 = alpha * alpha;
+    const float d = ch2 * (a2 - 1.f) + 1.f;
+    return a2 / (IBL_PI * d * d) * c;
+}
+
+/* alpha of PrefilterConv (f_ops.cpp:3280-3283): max(r, 0.045)^2 */
+float orc_prefilter_alpha(float roughness) {
+    const float r = roughness < 0.045f ? 0.045f : roughness;
+    return r * r;
+}
+
+/* PrefilterConvNorm (f_ops.cpp:3166-3205): W(t) = sum_s w(R_t . d_s)
+ * sin(theta_s), a float sum in source row-major order. */
+void orc_prefilter_conv_norm(uint32_t ow, uint32_t oh, uint32_t sw,
+                             uint32_t sh, float alpha, float* out) {
+    for (uint32_t oy = 0; oy < oh; oy++)
+        for (uint32_t ox = 0; ox < ow; ox++) {
+            float r[3];
+            equirect_dir(((float)ox + 0.5f) / (float)ow,
+                         ((float)oy + 0.5f) / (float)oh, r);
+            float acc = 0.f;
+            for (uint32_t sy = 0; sy < sh; sy++) {
+                const float sv = ((float)sy + 0.5f) / (float)sh;
+                const float sin_th = sinf(sv * IBL_PI);
+                for (uint32_t sx = 0; sx < sw; sx++) {
+                    float d[3];
+                    equirect_dir(((float)sx + 0.5f) / (float)sw, sv, d);
+                    acc += ggx_conv_weight(dot3(r, d), alpha) * sin_th;
+                }
+            }
+            out[(size_t)oy * ow + ox] = acc;
+        }
+}
+
+/* PrefilterConv (f_ops.cpp:3272-3345): pref(t) = sum_s w sin env(s) /
+ * max(W(t), 1e-12). */
+void orc_prefilter_conv(const float* env, uint32_t sw, uint32_t sh,
+                        uint32_t n, const float* norm, uint32_t ow,
+                        uint32_t oh, float alpha, float* out) {
+    for (uint32_t oy = 0; oy < oh; oy++)
+        for (uint32_t ox = 0; ox < ow; ox++) {
+            float r[3];
+            equirect_dir(((float)ox + 0.5f) / (float)ow,
+                         ((float)oy + 0.5f) / (float)oh, r);
+            float* o = &out[((size_t)oy * ow + ox) * n];
+            for (uint32_t c = 0; c < n; c++) o[c] = 0.f;
+            for (uint32_t sy = 0; sy < sh; sy++) {
+                const float sv = ((float)sy + 0.5f) / (float)sh;
+                const float sin_th = sinf(sv * IBL_PI);
+                for (uint32_t sx = 0; sx < sw; sx++) {
+                    float d[3];
+                    equirect_dir(((float)sx + 0.5f) / (float)sw, sv, d);
+                    const float w = ggx_conv_weight(dot3(r, d), alpha) * sin_th;
+                    const float* e = &env[((size_t)sy * sw + sx) * n];
+                    for (uint32_t c = 0; c < n; c++) o[c] += e[c] * w;
+                }
+            }
+            const float nv = norm[(size_t)oy * ow + ox];
+            const float wn = nv < 1e-12f ? 1e-12f : nv;
+            for (uint32_t c = 0; c < n; c++) o[c] /= wn;
+        }
+}
+
+/* PrefilterConvBwd (f_ops.cpp:3210-3268): g_env(s) = sin(theta_s) sum_t
+ * gy(t) w(t, s) / max(W(t), 1e-12), skipping w <= 0. */
+void orc_prefilter_conv_bwd(const float* gy, const float* norm, uint32_t ow,
+                            uint32_t oh, uint32_t n, uint32_t sw, uint32_t sh,
+                            float alpha, float* g_env) {
+    for (uint32_t sy = 0; sy < sh; sy++) {
+        const float sv = ((float)sy + 0.5f) / (float)sh;
+        const float sin_th = sinf(sv * IBL_PI);
+        for (uint32_t sx = 0; sx < sw; sx++) {
+            float d[3];
+            equirect_dir(((float)sx + 0.5f) / (float)sw, sv, d);
+            float* o = &g_env[((size_t)sy * sw + sx) * n];
+            for (uint32_t c = 0; c < n; c++) o[c] = 0.f;
+            for (uint32_t ty = 0; ty < oh; ty++)
+                for (uint32_t tx = 0; tx < ow; tx++) {
+                    float r[3];
+                    equirect_dir(((float)tx + 0.5f) / (float)ow,
+                                 ((float)ty + 0.5f) / (float)oh, r);
+                    const float w = ggx_conv_weight(dot3(r, d), alpha);
+                    if (w <= 0.f) continue;
+                    const float nv = norm[(size_t)ty * ow + tx];
+                    const float wn = w / (nv < 1e-12f ? 1e-12f : nv);
+                    const float* g = &gy[((size_t)ty * ow + tx) * n];
+                    for (uint32_t c = 0; c < n; c++) o[c] += g[c] * wn;
+                }
+            for (uint32_t c = 0; c < n; c++) o[c] *= sin_th;
+        }
+    }
+}
+
+/* RadicalInverse / Hammersley (ibl_math.h:119-131) */
+static float radical_inverse(uint32_t b) {
+    b = (b << 16u) | (b >> 16u);
+    b = ((b & 0x55555555u) << 1u) | ((b & 0xAAAAAAAAu) >> 1u);
+    b = ((b & 0x33333333u) << 2u) | ((b & 0xCCCCCCCCu) >> 2u);
+    b = ((b & 0x0F0F0F0Fu) << 4u) | ((b & 0xF0F0F0F0u) >> 4u);
+    b = ((b & 0x00FF00FFu) << 8u) | ((b & 0xFF00FF00u) >> 8u);
+    return (float)b * 2.3283064365386963e-10f;
+}
+
+static void normalize3(float v[3]) {
+    const float len = sqrtf(dot3(v, v));
+    v[0] = v[0] / len;
+    v[1] = v[1] / len;
+    v[2] = v[2] / len;
+}
+
+/* ImportanceSampleGGX about N = +Z (ibl_math.h:135-150; the tangent frame
+ * of +Z is built from up = (1, 0, 0)). */
+static void ggx_sample_z(float xi0, float xi1, float rough, float h[3]) {
+    const float a = rough * rough;
+    const float phi = IBL_TWO_PI * xi0;
+    const float ct = sqrtf((1.f - xi1) / (1.f + (a * a - 1.f) * xi1));
+    const float st2 = 1.f - ct * ct;
+    const float st = sqrtf(st2 < 0.f ? 0.f : st2);
+    const float ht[3] = {cosf(phi) * st, sinf(phi) * st, ct};
+    /* up = (1,0,0) since |n.z| = 1 >= 0.999; tx = normalize(up x n),
+     * ty = n x tx with n = (0,0,1) */
+    float tx[3] = {0.f * 1.f - 0.f * 0.f, 0.f * 0.f - 1.f * 1.f,
+                   1.f * 0.f - 0.f * 0.f};
+    normalize3(tx);
+    const float ty[3] = {0.f * tx[2] - 1.f * tx[1], 1.f * tx[0] - 0.f * tx[2],
+                         0.f * tx[1] - 0.f * tx[0]};
+    h[0] = tx[0] * ht[0] + ty[0] * ht[1] + 0.f * ht[2];
+    h[1] = tx[1] * ht[0] + ty[1] * ht[1] + 0.f * ht[2];
+    h[2] = tx[2] * ht[0] + ty[2] * ht[1] + 1.f * ht[2];
+    normalize3(h);
+}
+
+/* BrdfIntegrationLut (f_ops.cpp:3350-3408): (A, B) over (NdotV, rough)
+ * texel centres, n_samples Hammersley GGX samples, Smith G with k =
+ * rough^2 / 2. out [h][w][2]. */
+void orc_brdf_lut(uint32_t w, uint32_t h, uint32_t n_samples, float* out) {
+    for (uint32_t oy = 0; oy < h; oy++) {
+        const float rough = ((float)oy + 0.5f) / (float)h;
+        const float k = rough * rough / 2.f;
+        for (uint32_t ox = 0; ox < w; ox++) {
+            const float ndv = ((float)ox + 0.5f) / (float)w;
+            const float s2 = 1.f - ndv * ndv;
+            const float V[3] = {sqrtf(s2 < 0.f ? 0.f : s2), 0.f, ndv};
+            float a = 0.f, b = 0.f;
+            for (uint32_t i = 0; i < n_samples; i++) {
+                const float xi0 = (float)i / (float)n_samples;
+                const float xi1 = radical_inverse(i);
+                float hv[3];
+                ggx_sample_z(xi0, xi1, rough, hv);
+                const float vdh2 = 2.f * dot3(V, hv);
+                float l[3] = {vdh2 * hv[0] - V[0], vdh2 * hv[1] - V[1],
+                              vdh2 * hv[2] - V[2]};
+                normalize3(l);
+                const float nol = l[2] < 0.f ? 0.f : l[2];
+                const float noh = hv[2] < 0.f ? 0.f : hv[2];
+                const float vh = dot3(V, hv);
+                const float voh = vh < 0.f ? 0.f : vh;
+                if (nol > 0.f) {
+                    const float g = (ndv / (ndv * (1.f - k) + k)) *
+                                    (nol / (nol * (1.f - k) + k));
+                    const float den = noh * ndv;
+                    const float gv = g * voh / (den < 1e-8f ? 1e-8f : den);
+                    const float fc = powf(1.f - voh, 5.f);
+                    a += (1.f - fc) * gv;
+                    b += fc * gv;
+                }
+            }
+            out[((size_t)oy * w + ox) * 2 + 0] = a / (float)n_samples;
+            out[((size_t)oy * w + ox) * 2 + 1] = b / (float)n_samples;
+        }
+    }
+}
+
+/* AvgPool2x2 = Reduce2x2Sum * 0.25 (f_ops.cpp:3411-3415, 995-1033): each
+ * output sums its 2x2 sources in row-major order. w, h even. */
+void orc_avg_pool2x2(const float* x, uint32_t w, uint32_t h, uint32_t n,
+                     float* out) {
+    const uint32_t ow = w / 2, oh = h / 2;
+    for (uint32_t oy = 0; oy < oh; oy++)
+        for (uint32_t ox = 0; ox < ow; ox++)
+            for (uint32_t c = 0; c < n; c++) {
+                const float a = x[((size_t)(2 * oy) * w + 2 * ox) * n + c];
+                const float b = x[((size_t)(2 * oy) * w + 2 * ox + 1) * n + c];
+                const float cc = x[((size_t)(2 * oy + 1) * w + 2 * ox) * n + c];
+                const float d = x[((size_t)(2 * oy + 1) * w + 2 * ox + 1) * n + c];
+                out[((size_t)oy * ow + ox) * n + c] = (((a + b) + cc) + d) * 0.25f;
+            }
+}
+
 /* --------------------------------------------------------- image fitting */
 
 /* Sum (f_ops.cpp:1037-1043, the Reduce2x2Sum chain 998-1033) followed by

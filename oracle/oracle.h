@@ -229,6 +229,32 @@ int orc_regularized_grad(const float* pos, uint32_t n_verts, const float* faces,
                          const float* g, float laplacian, float normal,
                          float* out);
 
+/* Split-sum IBL ops (C5; f_ops.cpp:2785-3415, ibl_math.h). Images are
+ * [h][w][n] row-major, directions [n_px][3]. */
+void orc_equirect_sample(const float* map, uint32_t mw, uint32_t mh,
+                         uint32_t n, const float* dir, size_t n_px,
+                         float* out);
+int orc_equirect_sample_bwd(const float* gy, const float* dir, uint32_t dw,
+                            uint32_t dh, uint32_t mw, uint32_t mh, uint32_t n,
+                            float* g_map);
+void orc_irradiance_conv(const float* env, uint32_t sw, uint32_t sh,
+                         uint32_t n, uint32_t ow, uint32_t oh, float* out);
+void orc_irradiance_conv_bwd(const float* gy, uint32_t ow, uint32_t oh,
+                             uint32_t n, uint32_t sw, uint32_t sh,
+                             float* g_env);
+float orc_prefilter_alpha(float roughness);
+void orc_prefilter_conv_norm(uint32_t ow, uint32_t oh, uint32_t sw,
+                             uint32_t sh, float alpha, float* out);
+void orc_prefilter_conv(const float* env, uint32_t sw, uint32_t sh,
+                        uint32_t n, const float* norm, uint32_t ow,
+                        uint32_t oh, float alpha, float* out);
+void orc_prefilter_conv_bwd(const float* gy, const float* norm, uint32_t ow,
+                            uint32_t oh, uint32_t n, uint32_t sw, uint32_t sh,
+                            float alpha, float* g_env);
+void orc_brdf_lut(uint32_t w, uint32_t h, uint32_t n_samples, float* out);
+void orc_avg_pool2x2(const float* x, uint32_t w, uint32_t h, uint32_t n,
+                     float* out);
+
 /* 2-D image fitting (C1): loss = Mean((p - t)^2) over W*H*4, Adam on p.
  * loss_trace[n_iters] = loss at the start of each iteration. */
 int orc_image_fit_run(float* param, const float* target, uint32_t w,

@@ -396,6 +396,91 @@ class Port(_Lib):
             _fp(out), C.byref(md)), "vertex_faces_tex")
         return out[: n_verts * md.value].reshape(md.value, n_verts)
 
+    # ---- split-sum IBL (C5)
+    def equirect_sample(self, env, dirs):
+        env, dirs = _f32(env), _f32(dirs)
+        mh, mw = env.shape[:2]
+        n = 1 if env.ndim == 2 else env.shape[2]
+        out = np.zeros(dirs.shape[:-1] + ((n,) if env.ndim == 3 else ()),
+                       np.float32)
+        self.lib.orc_equirect_sample(_fp(env), _u32(mw), _u32(mh), _u32(n),
+                                     _fp(dirs), C.c_size_t(dirs.size // 3),
+                                     _fp(out))
+        return out
+
+    def equirect_sample_bwd(self, gy, dirs, mw, mh):
+        gy, dirs = _f32(gy), _f32(dirs)
+        dh, dw = dirs.shape[:2]
+        n = 1 if gy.ndim == 2 else gy.shape[2]
+        out = np.zeros((mh, mw) + ((n,) if gy.ndim == 3 else ()), np.float32)
+        self._err(self.lib.orc_equirect_sample_bwd(
+            _fp(gy), _fp(dirs), _u32(dw), _u32(dh), _u32(mw), _u32(mh),
+            _u32(n), _fp(out)), "equirect_sample_bwd")
+        return out
+
+    def irradiance_conv(self, env, ow, oh):
+        env = _f32(env)
+        sh, sw, n = env.shape
+        out = np.zeros((oh, ow, n), np.float32)
+        self.lib.orc_irradiance_conv(_fp(env), _u32(sw), _u32(sh), _u32(n),
+                                     _u32(ow), _u32(oh), _fp(out))
+        return out
+
+    def irradiance_conv_bwd(self, gy, sw, sh):
+        gy = _f32(gy)
+        oh, ow, n = gy.shape
+        out = np.zeros((sh, sw, n), np.float32)
+        self.lib.orc_irradiance_conv_bwd(_fp(gy), _u32(ow), _u32(oh), _u32(n),
+                                         _u32(sw), _u32(sh), _fp(out))
+        return out
+
+    def prefilter_alpha(self, rough):
+        self.lib.orc_prefilter_alpha.restype = C.c_float
+        return np.float32(self.lib.orc_prefilter_alpha(C.c_float(rough)))
+
+    def prefilter_conv_norm(self, ow, oh, sw, sh, alpha):
+        out = np.zeros((oh, ow), np.float32)
+        self.lib.orc_prefilter_conv_norm(_u32(ow), _u32(oh), _u32(sw),
+                                         _u32(sh), C.c_float(alpha), _fp(out))
+        return out
+
+    def prefilter_conv(self, env, ow, oh, rough, norm=None):
+        env = _f32(env)
+        sh, sw, n = env.shape
+        alpha = self.prefilter_alpha(rough)
+        if norm is None:
+            norm = self.prefilter_conv_norm(ow, oh, sw, sh, alpha)
+        out = np.zeros((oh, ow, n), np.float32)
+        self.lib.orc_prefilter_conv(_fp(env), _u32(sw), _u32(sh), _u32(n),
+                                    _fp(_f32(norm)), _u32(ow), _u32(oh),
+                                    C.c_float(alpha), _fp(out))
+        return out
+
+    def prefilter_conv_bwd(self, gy, sw, sh, rough, norm=None):
+        gy = _f32(gy)
+        oh, ow, n = gy.shape
+        alpha = self.prefilter_alpha(rough)
+        if norm is None:
+            norm = self.prefilter_conv_norm(ow, oh, sw, sh, alpha)
+        out = np.zeros((sh, sw, n), np.float32)
+        self.lib.orc_prefilter_conv_bwd(_fp(gy), _fp(_f32(norm)), _u32(ow),
+                                        _u32(oh), _u32(n), _u32(sw), _u32(sh),
+                                        C.c_float(alpha), _fp(out))
+        return out
+
+    def brdf_lut(self, w, h, n_samples):
+        out = np.zeros((h, w, 2), np.float32)
+        self.lib.orc_brdf_lut(_u32(w), _u32(h), _u32(n_samples), _fp(out))
+        return out
+
+    def avg_pool2x2(self, x):
+        x = _f32(x)
+        h, w = x.shape[:2]
+        n = 1 if x.ndim == 2 else x.shape[2]
+        out = np.zeros((h // 2, w // 2) + x.shape[2:], np.float32)
+        self.lib.orc_avg_pool2x2(_fp(x), _u32(w), _u32(h), _u32(n), _fp(out))
+        return out
+
     def vertex_neighbors_tex(self, faces, n_verts, cap=64):
         faces = _f32(faces)
         out = np.zeros(n_verts * cap, np.float32)
@@ -613,6 +698,60 @@ class Ref(_Lib):
             _fp(faces), _u32(faces.shape[0]), _u32(n_verts), _u32(cap),
             _fp(out), C.byref(md)), "vertex_faces_tex")
         return out[: n_verts * md.value].reshape(md.value, n_verts)
+
+    # ---- split-sum IBL (C5): (out, grad of the input image for gy)
+    def _img(self, x):
+        x = _f32(x)
+        h, w = x.shape[:2]
+        return x, w, h, 1 if x.ndim == 2 else x.shape[2]
+
+    def equirect_sample(self, env, dirs, gy=None):
+        env, mw, mh, n = self._img(env)
+        dirs = _f32(dirs)
+        dh, dw = dirs.shape[:2]
+        out = np.zeros((dh, dw) + env.shape[2:], np.float32)
+        g = np.zeros_like(env) if gy is not None else None
+        self._err(self.lib.ref_equirect_sample(
+            _fp(env), _u32(mw), _u32(mh), _u32(n), _fp(dirs), _u32(dw),
+            _u32(dh), _fp(None if gy is None else _f32(gy)), _fp(out),
+            _fp(g)), "equirect_sample")
+        return out if gy is None else (out, g)
+
+    def irradiance_conv(self, env, ow, oh, gy=None):
+        env, sw, sh, n = self._img(env)
+        out = np.zeros((oh, ow) + env.shape[2:], np.float32)
+        g = np.zeros_like(env) if gy is not None else None
+        self._err(self.lib.ref_irradiance_conv(
+            _fp(env), _u32(sw), _u32(sh), _u32(n), _u32(ow), _u32(oh),
+            _fp(None if gy is None else _f32(gy)), _fp(out), _fp(g)),
+            "irradiance_conv")
+        return out if gy is None else (out, g)
+
+    def prefilter_conv(self, env, ow, oh, rough, gy=None):
+        env, sw, sh, n = self._img(env)
+        out = np.zeros((oh, ow) + env.shape[2:], np.float32)
+        g = np.zeros_like(env) if gy is not None else None
+        self._err(self.lib.ref_prefilter_conv(
+            _fp(env), _u32(sw), _u32(sh), _u32(n), _u32(ow), _u32(oh),
+            C.c_float(rough), _fp(None if gy is None else _f32(gy)),
+            _fp(out), _fp(g)), "prefilter_conv")
+        return out if gy is None else (out, g)
+
+    def avg_pool2x2(self, x, gy=None):
+        x, w, h, n = self._img(x)
+        out = np.zeros((h // 2, w // 2) + x.shape[2:], np.float32)
+        g = np.zeros_like(x) if gy is not None else None
+        self._err(self.lib.ref_avg_pool2x2(
+            _fp(x), _u32(w), _u32(h), _u32(n),
+            _fp(None if gy is None else _f32(gy)), _fp(out), _fp(g)),
+            "avg_pool2x2")
+        return out if gy is None else (out, g)
+
+    def brdf_lut(self, w, h, n_samples):
+        out = np.zeros((h, w, 2), np.float32)
+        self._err(self.lib.ref_brdf_lut(_u32(w), _u32(h), _u32(n_samples),
+                                        _fp(out)), "brdf_lut")
+        return out
 
     def mesh_tables(self, faces, n_verts, cap=64):
         """(vertex neighbours {max_deg, V}, face neighbours [F, 3]) from the

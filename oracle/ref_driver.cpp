@@ -27,6 +27,7 @@
 #include "core/cpu_eval.h"
 #include "core/cpu_raster.h"
 #include "dressi/dressi.h"
+#include "dressi/ibl.h"
 #include "dressi/mesh_utils.h"
 
 using namespace dressi;
@@ -178,6 +179,34 @@ double SumAll(const CpuTensor& t) {
     double s = 0.0;
     for (float v : t.data) s += v;
     return s;
+}
+
+VType CompType(uint32_t n) {
+    DRESSI_CHECK(n >= 1 && n <= 4, "n_comp 1..4");
+    return n == 1 ? FLOAT : n == 2 ? VEC2 : n == 3 ? VEC3 : VEC4;
+}
+
+// y = op(x) for one image leaf x {xw, xh, n}; out receives y, and with gy
+// (y's shape) g_x receives d(sum gy * y)/dx from BuildBackward.
+template <typename Op>
+void RunLeafOp(const float* x, uint32_t xw, uint32_t xh, uint32_t n, Op op,
+               const float* gy, float* out, float* g_x) {
+    const VType vt = CompType(n);
+    Variable vx(vt, {xw, xh});
+    Variable y = op(vx);
+    CpuEvaluator ev;
+    ev.bind(vx, Tensor(vt, {xw, xh}, x));
+    CpuTensor ty = ev.eval(y);
+    CopyOut(ty, out);
+    if (!gy || !g_x) return;
+    Variable vgy(y.getVType(), y.getImgSize());
+    ev.bind(vgy, Tensor(y.getVType(), y.getImgSize(), gy));
+    Variable loss = F::StopGradient(vgy) * y;
+    Variable vx_mut = vx;
+    vx_mut.setRequiresGradRecursively();
+    auto [xs, gxs] = BuildBackward(loss);
+    for (size_t i = 0; i < xs.size(); i++)
+        if (xs[i] == vx) CopyOut(ev.eval(gxs[i]), g_x);
 }
 
 }  // namespace
@@ -759,6 +788,84 @@ int ref_sum_all(const float* x, uint32_t n_px, uint32_t n_comp, float* out) {
         CpuEvaluator ev;
         ev.bind(vx, Tensor(vt, {n_px, 1}, x));
         *out = ev.eval(F::SumAll(vx)).data[0];
+    });
+}
+
+// ---------------------------------------------------------------- IBL (C5)
+
+// F::EquirectSample(map, dir) (f_ops.cpp:2913-2964) and its map gradient.
+int ref_equirect_sample(const float* map, uint32_t mw, uint32_t mh,
+                                   uint32_t n, const float* dir, uint32_t dw,
+                                   uint32_t dh, const float* gy, float* out,
+                                   float* g_map) {
+    return Guard([&] {
+        Variable vdir(VEC3, {dw, dh});
+        CpuTensor tdir = Tensor(VEC3, {dw, dh}, dir);
+        const VType vt = CompType(n);
+        Variable vmap(vt, {mw, mh});
+        Variable y = F::EquirectSample(vmap, vdir);
+        CpuEvaluator ev;
+        ev.bind(vmap, Tensor(vt, {mw, mh}, map));
+        ev.bind(vdir, tdir);
+        CopyOut(ev.eval(y), out);
+        if (!gy || !g_map) return;
+        Variable vgy(vt, {dw, dh});
+        ev.bind(vgy, Tensor(vt, {dw, dh}, gy));
+        Variable loss = F::StopGradient(vgy) * y;
+        Variable vm = vmap;
+        vm.setRequiresGradRecursively();
+        auto [xs, gxs] = BuildBackward(loss);
+        for (size_t i = 0; i < xs.size(); i++)
+            if (xs[i] == vmap) CopyOut(ev.eval(gxs[i]), g_map);
+    });
+}
+
+// F::IrradianceConv(env, {ow, oh}) (f_ops.cpp:3023-3105) and its env
+// gradient.
+int ref_irradiance_conv(const float* env, uint32_t sw, uint32_t sh,
+                                   uint32_t n, uint32_t ow, uint32_t oh,
+                                   const float* gy, float* out, float* g_env) {
+    return Guard([&] {
+        RunLeafOp(env, sw, sh, n,
+                  [&](const Variable& x) {
+                      return F::IrradianceConv(x, ImgSize{ow, oh});
+                  },
+                  gy, out, g_env);
+    });
+}
+
+// F::PrefilterConv(env, {ow, oh}, roughness) (f_ops.cpp:3272-3345) and its
+// env gradient.
+int ref_prefilter_conv(const float* env, uint32_t sw, uint32_t sh,
+                                  uint32_t n, uint32_t ow, uint32_t oh,
+                                  float roughness, const float* gy,
+                                  float* out, float* g_env) {
+    return Guard([&] {
+        RunLeafOp(env, sw, sh, n,
+                  [&](const Variable& x) {
+                      return F::PrefilterConv(x, ImgSize{ow, oh}, roughness);
+                  },
+                  gy, out, g_env);
+    });
+}
+
+// F::AvgPool2x2(x) (f_ops.cpp:3411-3415) and its gradient.
+int ref_avg_pool2x2(const float* x, uint32_t w, uint32_t h,
+                               uint32_t n, const float* gy, float* out,
+                               float* g_x) {
+    return Guard([&] {
+        RunLeafOp(x, w, h, n, [](const Variable& v) { return F::AvgPool2x2(v); },
+                  gy, out, g_x);
+    });
+}
+
+// F::BrdfIntegrationLut({w, h}, n_samples) (f_ops.cpp:3350-3408).
+int ref_brdf_lut(uint32_t w, uint32_t h, uint32_t n_samples,
+                            float* out) {
+    return Guard([&] {
+        Variable y = F::BrdfIntegrationLut(ImgSize{w, h}, n_samples);
+        CpuEvaluator ev;
+        CopyOut(ev.eval(y), out);
     });
 }
 
