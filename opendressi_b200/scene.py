@@ -324,3 +324,168 @@ def texture_scene(level: int = 4, n_views: int = 8, res: int = 512,
     return TextureScene(pos.astype(np.float32), faces, sphere_uv(pos),
                         orbit_cameras(n_views, seed), res, tex_size, levels,
                         checker_texture(seed + 1, tex_size), lr)
+
+
+# ------------------------------------------------------------------ C5 (PBR)
+
+def camera_frame(eye, fovy_deg: float = 45.0, aspect: float = 1.0):
+    """The per-view frame of the PBR shader (pbr_material_optimization
+    run.cpp:309-318): cam_pos, cam_fwd, cam_right * tan(fov/2) * aspect,
+    cam_up * tan(fov/2) (look_at the origin, +y up), float32 [12]."""
+    vm = look_at(eye, (0, 0, 0), (0, 1, 0))
+    t = math.tan(math.radians(fovy_deg) * 0.5)
+    fwd = np.array([-vm[2], -vm[6], -vm[10]])
+    right = np.array([vm[0], vm[4], vm[8]]) * t * aspect
+    up = np.array([vm[1], vm[5], vm[9]]) * t
+    return np.concatenate([np.asarray(eye, np.float64), fwd, right,
+                           up]).astype(np.float32)
+
+
+LIGHT_POS = (2.0, 2.0, 2.0)   # the material example's point light
+LIGHT_COL = (20.0, 20.0, 20.0)
+
+
+def sphere_gbuffer(w: int, h: int, seed: int = 0, radius: float = 3.0):
+    """An analytic G-buffer of the unit sphere from a seeded camera on a
+    radius-3 orbit (fov 45): (g_n [h][w][3], g_p [h][w][3], mask [h][w],
+    frame [18] = camera frame + light position + light colour); background
+    pixels hold 0 normals and positions, as the rasterizer writes."""
+    rng = np.random.default_rng(seed)
+    az = rng.uniform(0, 2 * math.pi)
+    el = rng.uniform(-0.6, 0.6)
+    eye = radius * np.array([math.cos(el) * math.sin(az), math.sin(el),
+                             math.cos(el) * math.cos(az)])
+    fr = camera_frame(eye)
+    cam, fwd, right, up = fr[0:3], fr[3:6], fr[6:9], fr[9:12]
+    ys, xs = np.mgrid[0:h, 0:w]
+    ndx = (xs + 0.5) * (2.0 / w) - 1.0
+    ndy = (ys + 0.5) * (2.0 / h) - 1.0
+    d = (fwd[None, None] + right[None, None] * ndx[..., None] -
+         up[None, None] * ndy[..., None]).astype(np.float64)
+    d /= np.linalg.norm(d, axis=-1, keepdims=True)
+    b = (d * cam).sum(-1)
+    disc = b * b - ((cam.astype(np.float64) ** 2).sum() - 1.0)
+    hit = disc > 0
+    t = -b - np.sqrt(np.maximum(disc, 0.0))
+    p = np.where(hit[..., None], cam + d * t[..., None], 0.0)
+    frame = np.concatenate([fr, LIGHT_POS, LIGHT_COL]).astype(np.float32)
+    return (p.astype(np.float32), p.astype(np.float32),
+            hit.astype(np.float32), frame)
+
+
+def ibl_environment(w: int = 512, h: int = 256, seed: int = 0) -> np.ndarray:
+    """The C5 environment: a sky gradient plus 4 seeded Gaussian-lobe
+    lights, radiance in [0, 50], stored as fp16 values (float32 [h][w][3])."""
+    rng = np.random.default_rng(seed)
+    v = (np.arange(h) + 0.5) / h
+    u = (np.arange(w) + 0.5) / w
+    uu, vv = np.meshgrid(u, v)
+    theta, phi = vv * math.pi, (uu - 0.5) * 2 * math.pi
+    d = np.stack([np.sin(theta) * np.cos(phi), np.cos(theta),
+                  np.sin(theta) * np.sin(phi)], -1)
+    sky = np.clip(d[..., 1:2], 0, 1) * np.array([0.4, 0.6, 1.0]) + 0.15
+    env = np.broadcast_to(sky, (h, w, 3)).copy()
+    for _ in range(4):
+        c = rng.standard_normal(3)
+        c /= np.linalg.norm(c)
+        sharp = rng.uniform(20.0, 200.0)
+        col = rng.uniform(0.3, 1.0, 3) * rng.uniform(10.0, 49.0)
+        lobe = np.exp(sharp * ((d @ c) - 1.0))
+        env += lobe[..., None] * col
+    env = np.clip(env, 0.0, 50.0)
+    return env.astype(np.float16).astype(np.float32)
+
+
+def value_noise(size: int, seed: int, cells: int = 8,
+                octaves: int = 3) -> np.ndarray:
+    """Seeded smooth value noise in [0, 1], float32 [size, size] (bilinear
+    interpolation of random lattices, octaves halving the cell size)."""
+    rng = np.random.default_rng(seed)
+    out = np.zeros((size, size))
+    amp, tot = 1.0, 0.0
+    for o in range(octaves):
+        n = cells * (2 ** o)
+        lat = rng.random((n + 1, n + 1))
+        x = np.arange(size) * n / size
+        i = np.floor(x).astype(int)
+        f = x - i
+        f = f * f * (3 - 2 * f)
+        row = lat[i][:, i] * (1 - f)[None, :] + lat[i][:, i + 1] * f[None, :]
+        row2 = (lat[i + 1][:, i] * (1 - f)[None, :] +
+                lat[i + 1][:, i + 1] * f[None, :])
+        out += amp * (row * (1 - f)[:, None] + row2 * f[:, None])
+        tot += amp
+        amp *= 0.5
+    out /= tot
+    return ((out - out.min()) / (out.max() - out.min())).astype(np.float32)
+
+
+class PbrScene:
+    """C5: a UV icosphere (unit radius, spherical uv, normals = positions)
+    seen from seeded orbit cameras, GGX Cook-Torrance with split-sum IBL;
+    the optimised parameters are the albedo and metallic-roughness maps
+    (G = roughness, B = metallic) and the environment."""
+
+    def __init__(self, pos, faces, uv, mvps, frames, res, tex_size, env_gt,
+                 levels, albedo_gt, mr_gt, lr):
+        self.pos = pos
+        self.faces = faces
+        self.faces_f = faces.astype(np.float32)
+        self.uv = uv
+        self.mvps = mvps
+        self.frames = frames
+        self.res = res
+        self.tex_size = tex_size
+        self.env_gt = env_gt
+        self.levels = levels
+        self.albedo_gt = albedo_gt
+        self.mr_gt = mr_gt
+        self.albedo0 = np.full_like(albedo_gt, 0.5)
+        self.mr0 = np.full_like(mr_gt, 0.5)
+        self.env0 = np.full_like(env_gt, 0.3)
+        self.lr = lr
+        self.light = np.concatenate([LIGHT_POS, LIGHT_COL]).astype(np.float32)
+
+    @property
+    def n_verts(self):
+        return self.pos.shape[0]
+
+    @property
+    def n_faces(self):
+        return self.faces.shape[0]
+
+    @property
+    def n_views(self):
+        return self.mvps.shape[0]
+
+
+def pbr_scene(level: int = 6, n_views: int = 32, res: int = 1024,
+              tex_size: int = 1024, env_w: int = 512, env_h: int = 256,
+              levels: int = 6, seed: int = 0, lr: float = 1e-2) -> PbrScene:
+    """Config C5: icosphere-6 (40962 v / 81920 f) with spherical uv, 32
+    seeded cameras on a radius-3 orbit (fov 45) at 1024^2, 1024^2 albedo
+    and metallic-roughness maps (seeded value noise, roughness in [0.05,
+    1]), a 512x256 fp16-valued environment (4 lobes + sky), 6 prefilter
+    levels, Adam lr 1e-2."""
+    pos, faces = icosphere(level)
+    pos = pos.astype(np.float32)
+    rng = np.random.default_rng(seed)
+    proj = perspective_vk(math.radians(45.0), 1.0, 0.1, 10.0)
+    mvps = np.empty((n_views, 16), np.float32)
+    frames = np.empty((n_views, 12), np.float32)
+    for v in range(n_views):
+        az = rng.uniform(0.0, 2.0 * math.pi)
+        el = math.asin(rng.uniform(-math.sin(math.pi / 3),
+                                   math.sin(math.pi / 3)))
+        eye = 3.0 * np.array([math.cos(el) * math.sin(az), math.sin(el),
+                              math.cos(el) * math.cos(az)])
+        mvps[v] = _mat_mul(proj, look_at(eye, (0, 0, 0), (0, 1, 0)))
+        frames[v] = camera_frame(eye)
+    alb = np.stack([value_noise(tex_size, seed + 10 + c) for c in range(3)],
+                   -1)
+    rough = 0.05 + 0.95 * value_noise(tex_size, seed + 20)
+    metal = value_noise(tex_size, seed + 30, cells=4)
+    mr = np.stack([np.zeros_like(rough), rough, metal], -1).astype(np.float32)
+    return PbrScene(pos, faces, sphere_uv(pos), mvps, frames, res, tex_size,
+                    ibl_environment(env_w, env_h, seed + 40), levels,
+                    alb.astype(np.float32), mr, lr)

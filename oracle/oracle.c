@@ -2400,6 +2400,554 @@ void orc_avg_pool2x2(const float* x, uint32_t w, uint32_t h, uint32_t n,
             }
 }
 
+/* ---------------------------------------------- PBR shading graph (C5) */
+
+/* BilerpClamp of a [h][w][n] image at (u, v) (ibl_math.h:91-115); the taps
+ * and weights, (dy, dx) order, both axes clamped. */
+static void clamp_taps(uint32_t w, uint32_t h, float u, float v, int idx[4],
+                       float wt[4]) {
+    const float sx = u * (float)w - 0.5f;
+    const float sy = v * (float)h - 0.5f;
+    const int ix = to_i32(floorf(sx));
+    const int iy = to_i32(floorf(sy));
+    const float fx = sx - (float)ix;
+    const float fy = sy - (float)iy;
+    int k = 0;
+    for (int dy = 0; dy <= 1; dy++)
+        for (int dx = 0; dx <= 1; dx++, k++) {
+            int x = ix + dx, y = iy + dy;
+            x = x < 0 ? 0 : (x > (int)w - 1 ? (int)w - 1 : x);
+            y = y < 0 ? 0 : (y > (int)h - 1 ? (int)h - 1 : y);
+            idx[k] = y * (int)w + x;
+            wt[k] = (dx == 0 ? 1.f - fx : fx) * (dy == 0 ? 1.f - fy : fy);
+        }
+}
+
+static void sample_clamp(const float* img, uint32_t w, uint32_t h, uint32_t n,
+                         float u, float v, float* out) {
+    int idx[4];
+    float wt[4];
+    clamp_taps(w, h, u, v, idx, wt);
+    for (uint32_t c = 0; c < n; c++) out[c] = 0.f;
+    for (int k = 0; k < 4; k++)
+        for (uint32_t c = 0; c < n; c++) out[c] += wt[k] * img[(size_t)idx[k] * n + c];
+}
+
+static void scatter_clamp(float* g, uint32_t w, uint32_t h, uint32_t n,
+                          float u, float v, const float* gy) {
+    int idx[4];
+    float wt[4];
+    clamp_taps(w, h, u, v, idx, wt);
+    for (int k = 0; k < 4; k++)
+        for (uint32_t c = 0; c < n; c++) g[(size_t)idx[k] * n + c] += gy[c] * wt[k];
+}
+
+/* EquirectSample of a VEC3 map along d (0 for |d| < 1e-8) and its
+ * transpose (scatter, any order). */
+static void sample_equirect3(const float* map, uint32_t w, uint32_t h,
+                             const float dir[3], float out[3]) {
+    orc_equirect_sample(map, w, h, 3, dir, 1, out);
+}
+
+static void scatter_equirect3(float* g, uint32_t w, uint32_t h,
+                              const float dir[3], const float gy[3]) {
+    float d[3], u, v;
+    if (!unit_dir(dir, d)) return;
+    equirect_uv(d, &u, &v);
+    int tx[4], ty[4];
+    float tw[4];
+    bilerp_wrap_taps(w, h, u, v, tx, ty, tw);
+    for (int q = 0; q < 4; q++)
+        for (int c = 0; c < 3; c++)
+            g[((size_t)ty[q] * w + tx[q]) * 3 + c] += gy[c] * tw[q];
+}
+
+/* SafeNormalize (pbr_graph.cpp:17-19): v * InverseSqrt(dot(v, v) + 1e-12),
+ * InverseSqrt = 1 / sqrt. */
+static void safe_normalize(const float v[3], float out[3]) {
+    const float is = 1.f / sqrtf(dot3(v, v) + 1e-12f);
+    out[0] = v[0] * is;
+    out[1] = v[1] * is;
+    out[2] = v[2] * is;
+}
+
+static inline float fmax_ref(float a, float b) { return (a < b) ? b : a; }
+
+/* The pixel-static terms of BuildPbrShade (pbr_graph.cpp:47-138) without
+ * normal mapping: everything that depends on the G-buffer and the frame
+ * only. */
+void orc_pbr_static(const float g_n[3], const float g_p[3],
+                    const float cam_pos[3], const float light_pos[3],
+                    const float light_col[3], float out[ORC_PBR_STATIC]) {
+    float n[3], v[3], l[3], h[3], vl[3], cp[3], tl[3];
+    safe_normalize(g_n, n);
+    for (int c = 0; c < 3; c++) cp[c] = cam_pos[c] - g_p[c];
+    safe_normalize(cp, v);
+    const float ndv = fmax_ref(dot3(n, v), 1e-4f);
+    for (int c = 0; c < 3; c++) tl[c] = light_pos[c] - g_p[c];
+    const float dist2 = fmax_ref(dot3(tl, tl), 1e-4f);
+    safe_normalize(tl, l);
+    for (int c = 0; c < 3; c++) vl[c] = v[c] + l[c];
+    safe_normalize(vl, h);
+    const float ndl = fmax_ref(dot3(n, l), 0.f);
+    const float ndh = fmax_ref(dot3(n, h), 0.f);
+    const float vdh = fmax_ref(dot3(v, h), 0.f);
+    /* Reflect(-v, n) = I - (2 dot(n, I)) n (f_ops.cpp:737-741) */
+    const float I[3] = {-v[0], -v[1], -v[2]};
+    const float k2 = 2.f * dot3(n, I);
+    out[0] = ndv;
+    out[1] = ndl;
+    out[2] = ndh;
+    out[3] = vdh;
+    out[4] = powf(1.f - ndv, 5.f);
+    out[5] = powf(1.f - vdh, 5.f);
+    for (int c = 0; c < 3; c++) out[6 + c] = light_col[c] / dist2;
+    for (int c = 0; c < 3; c++) out[9 + c] = n[c];
+    for (int c = 0; c < 3; c++) out[12 + c] = I[c] - k2 * n[c];
+}
+
+/* One pixel of BuildPbrShade (no normal mapping) and the gradient of its
+ * loss term, in the reference autodiff's rules (f_ops.cpp: Max/Min give a
+ * tie to the first operand, Clamp passes inside [lo, hi] inclusive, Abs ->
+ * Sign, Pow -> p x^(p-1); broadcast FLOAT operands receive the component
+ * sum). st: orc_pbr_static; A, mr, E: the material samples, ao the ao
+ * sample; irr, P[L], bg: the environment samples; ab the LUT sample.
+ * Writes hdr / mapped and the gradients of loss = wgt * |T - mapped| summed
+ * (loss_kind 1) or wgt * (T - mapped)^2 (loss_kind 2). */
+typedef struct {
+    float gA[3], g_rough, g_metal, g_irr[3], g_bg[3];
+    float g_P[ORC_PBR_MAX_LEVELS][3];
+    float mapped[3];
+    double loss;
+} pbr_px_out_t;
+
+static void pbr_pixel(const float* st, float mask, const float A[3],
+                      float rough_raw, float metal, float ao, const float E[3],
+                      const float irr[3], const float (*P)[3], int L,
+                      const float ab[2], const float bg[3], const float T[3],
+                      int loss_kind, float wgt, pbr_px_out_t* o) {
+    const float ndv = st[0], ndl = st[1], ndh = st[2];
+    const float p5v = st[4], p5h = st[5];
+    const float* rad = &st[6];
+    const float pi = IBL_PI;
+    /* ---- forward */
+    const float rough = rough_raw < 0.045f ? 0.045f
+                        : (1.f < rough_raw ? 1.f : rough_raw);
+    float f0[3], fres[3], kdd[3], fibl[3], kdi[3], mx[3];
+    for (int c = 0; c < 3; c++) f0[c] = 0.04f + (A[c] - 0.04f) * metal;
+    const float alpha = rough * rough;
+    const float alpha2 = alpha * alpha;
+    const float dd = ndh * ndh * (alpha2 - 1.f) + 1.f;
+    const float D = pi * dd * dd;
+    const float dist_d = alpha2 / D;
+    const float r1a = rough + 1.f, r1b = rough + 1.f;
+    const float k = r1a * r1b / 8.f;
+    const float omk = 1.f - k;
+    const float den_v = ndv * omk + k;
+    const float gv = ndv / den_v;
+    const float ndlc = fmax_ref(ndl, 1e-4f);
+    const float den_l = ndlc * omk + k;
+    const float gl = ndlc / den_l;
+    for (int c = 0; c < 3; c++) fres[c] = f0[c] + (1.f - f0[c]) * p5h;
+    const float num = dist_d * gv * gl;
+    const float den_s = 4.f * ndv * ndl + 1e-4f;
+    const float sd = num / den_s;
+    const float om_metal = 1.f - metal;
+    for (int c = 0; c < 3; c++) kdd[c] = (1.f - fres[c]) * om_metal;
+    float lo[3], w1[3];
+    for (int c = 0; c < 3; c++) {
+        w1[c] = kdd[c] * A[c] / pi + fres[c] * sd;
+        lo[c] = w1[c] * rad[c] * ndl;
+    }
+    const float omr = 1.f - rough;
+    for (int c = 0; c < 3; c++) {
+        mx[c] = fmax_ref(omr, f0[c]);
+        fibl[c] = f0[c] + (mx[c] - f0[c]) * p5v;
+        kdi[c] = (1.f - fibl[c]) * om_metal;
+    }
+    const float lod = rough * (float)(L - 1);
+    float wl[ORC_PBR_MAX_LEVELS], xl[ORC_PBR_MAX_LEVELS];
+    float pref[3] = {0.f, 0.f, 0.f};
+    for (int i = 0; i < L; i++) {
+        xl[i] = 1.f - fabsf(lod - (float)i);
+        wl[i] = xl[i] < 0.f ? 0.f : (1.f < xl[i] ? 1.f : xl[i]);
+    }
+    /* at most two non-zero terms: their sum does not depend on the order */
+    for (int i = 0; i < L; i++)
+        for (int c = 0; c < 3; c++)
+            if (wl[i] != 0.f) pref[c] += P[i][c] * wl[i];
+    float q[3], spec_ibl[3], amb[3], shaded[3], hdr[3];
+    for (int c = 0; c < 3; c++) {
+        q[c] = f0[c] * ab[0] + ab[1];
+        spec_ibl[c] = pref[c] * q[c];
+        amb[c] = (kdi[c] * irr[c] * A[c] + spec_ibl[c]) * ao;
+        shaded[c] = lo[c] + amb[c] + E[c];
+        hdr[c] = mask * shaded[c] + (1.f - mask) * bg[c];
+        o->mapped[c] = hdr[c] / (hdr[c] + 1.f);
+    }
+    /* ---- loss and backward */
+    float g_hdr[3];
+    o->loss = 0.0;
+    for (int c = 0; c < 3; c++) {
+        const float diff = T[c] - o->mapped[c];
+        float g_diff;
+        if (loss_kind == 1) {
+            o->loss += (double)(fabsf(diff) * wgt);
+            g_diff = wgt * (float)((diff > 0.f) - (diff < 0.f));
+        } else {
+            o->loss += (double)(diff * diff * wgt);
+            g_diff = wgt * diff + wgt * diff;
+        }
+        const float g_m = -g_diff;
+        const float h1 = hdr[c] + 1.f;
+        g_hdr[c] = g_m / h1 + -(g_m * hdr[c] / (h1 * h1));
+    }
+    float g_sh[3], g_A[3] = {0.f, 0.f, 0.f}, g_f0[3] = {0.f, 0.f, 0.f};
+    float g_rough = 0.f, g_metal = 0.f;
+    for (int c = 0; c < 3; c++) {
+        g_sh[c] = g_hdr[c] * mask;
+        o->g_bg[c] = g_hdr[c] * (1.f - mask);
+    }
+    /* ambient = ((kdi * irr) * A + spec_ibl) * ao */
+    float g_kdi[3], g_q[3], g_pref[3];
+    for (int c = 0; c < 3; c++) {
+        const float g_t1 = g_sh[c] * ao;
+        const float g_ki = g_t1 * A[c];
+        g_A[c] += g_t1 * (kdi[c] * irr[c]);
+        g_kdi[c] = g_ki * irr[c];
+        o->g_irr[c] = g_ki * kdi[c];
+        g_pref[c] = g_t1 * q[c];
+        g_q[c] = g_t1 * pref[c];
+        g_f0[c] += g_q[c] * ab[0];
+    }
+    /* pref = sum_i P_i w_i, w_i = Clamp(1 - |lod - i|, 0, 1) */
+    float g_lod = 0.f;
+    for (int i = 0; i < L; i++) {
+        float gw = 0.f;
+        for (int c = 0; c < 3; c++) {
+            o->g_P[i][c] = g_pref[c] * wl[i];
+            gw += g_pref[c] * P[i][c];
+        }
+        const float inside = (xl[i] >= 0.f && 1.f >= xl[i]) ? 1.f : 0.f;
+        const float g_x = gw * inside;
+        const float dl = lod - (float)i;
+        const float sgn = (float)((dl > 0.f) - (dl < 0.f));
+        g_lod += -g_x * sgn;
+    }
+    g_rough += g_lod * (float)(L - 1);
+    /* kdi = (1 - fibl) * (1 - metal) */
+    float g_fibl[3], g_omm = 0.f;
+    for (int c = 0; c < 3; c++) {
+        g_fibl[c] = -(g_kdi[c] * om_metal);
+        g_omm += g_kdi[c] * (1.f - fibl[c]);
+    }
+    /* fibl = f0 + (Max(1 - rough, f0) - f0) * p5v */
+    float g_omr = 0.f;
+    for (int c = 0; c < 3; c++) {
+        g_f0[c] += g_fibl[c];
+        const float g_mx = g_fibl[c] * p5v;
+        g_f0[c] += -g_mx;
+        const float m = (omr >= f0[c]) ? 1.f : 0.f;
+        g_omr += g_mx * m;
+        g_f0[c] += g_mx * (1.f - m);
+    }
+    g_rough += -g_omr;
+    /* lo = ((kdd * A / pi + fres * sd) * rad) * ndl */
+    float g_kdd[3], g_fres[3] = {0.f, 0.f, 0.f}, g_sd = 0.f;
+    for (int c = 0; c < 3; c++) {
+        const float g_w1 = g_sh[c] * ndl * rad[c];
+        const float g_kA = g_w1 / pi;
+        g_kdd[c] = g_kA * A[c];
+        g_A[c] += g_kA * kdd[c];
+        g_fres[c] += g_w1 * sd;
+        g_sd += g_w1 * fres[c];
+    }
+    /* kdd = (1 - fres) * (1 - metal) */
+    for (int c = 0; c < 3; c++) {
+        g_fres[c] += -(g_kdd[c] * om_metal);
+        g_omm += g_kdd[c] * (1.f - fres[c]);
+    }
+    g_metal += -g_omm;
+    /* fres = f0 + (1 - f0) * p5h */
+    for (int c = 0; c < 3; c++) {
+        g_f0[c] += g_fres[c];
+        g_f0[c] += -(g_fres[c] * p5h);
+    }
+    /* sd = ((dist_d * gv) * gl) / den_s */
+    const float g_num = g_sd / den_s;
+    const float g_dg = g_num * gl;
+    const float g_gl = g_num * (dist_d * gv);
+    const float g_dist = g_dg * gv;
+    const float g_gv = g_dg * dist_d;
+    /* gv = ndv / (ndv * (1 - k) + k), gl likewise */
+    float g_k = 0.f;
+    {
+        const float g_den = -(g_gv * ndv / (den_v * den_v));
+        g_k += g_den;
+        g_k += -(g_den * ndv);
+        const float g_den2 = -(g_gl * ndlc / (den_l * den_l));
+        g_k += g_den2;
+        g_k += -(g_den2 * ndlc);
+    }
+    /* k = ((rough + 1) * (rough + 1)) / 8 */
+    const float g_sq = g_k / 8.f;
+    g_rough += g_sq * r1b + g_sq * r1a;
+    /* dist_d = alpha2 / ((pi * dd) * dd), dd = (ndh ndh)(alpha2 - 1) + 1 */
+    float g_a2 = g_dist / D;
+    const float g_D = -(g_dist * alpha2 / (D * D));
+    const float g_pdd = g_D * dd;
+    const float g_dd = g_D * (pi * dd) + g_pdd * pi;
+    g_a2 += g_dd * (ndh * ndh);
+    const float g_alpha = g_a2 * alpha + g_a2 * alpha;
+    g_rough += g_alpha * rough + g_alpha * rough;
+    /* f0 = 0.04 + (A - 0.04) * metal */
+    for (int c = 0; c < 3; c++) {
+        g_A[c] += g_f0[c] * metal;
+        g_metal += g_f0[c] * (A[c] - 0.04f);
+    }
+    for (int c = 0; c < 3; c++) o->gA[c] = g_A[c];
+    /* rough = Clamp(mr.y, 0.045, 1) */
+    const int rin = rough_raw >= 0.045f && 1.f >= rough_raw;
+    o->g_rough = rin ? g_rough : 0.f;
+    o->g_metal = g_metal;
+}
+
+/* PoolTo (ibl.cpp:14-20) by halving until it fits; returns the level. */
+static float* pool_to(const float* env, uint32_t w, uint32_t h, uint32_t mw,
+                      uint32_t mh, uint32_t* ow, uint32_t* oh) {
+    float* cur = (float*)malloc(sizeof(float) * (size_t)w * h * 3);
+    memcpy(cur, env, sizeof(float) * (size_t)w * h * 3);
+    while (w > mw || h > mh) {
+        float* nx = (float*)malloc(sizeof(float) * (size_t)(w / 2) * (h / 2) * 3);
+        orc_avg_pool2x2(cur, w, h, 3, nx);
+        free(cur);
+        cur = nx;
+        w /= 2;
+        h /= 2;
+    }
+    *ow = w;
+    *oh = h;
+    return cur;
+}
+
+/* g of the level at (w, h) -> g of the source env, through the pooling
+ * chain's transposes (each 2x2 source texel receives 0.25 g). */
+static void unpool_add(const float* g, uint32_t w, uint32_t h, uint32_t ew,
+                       uint32_t eh, float* g_env) {
+    float* cur = (float*)malloc(sizeof(float) * (size_t)w * h * 3);
+    memcpy(cur, g, sizeof(float) * (size_t)w * h * 3);
+    while (w < ew) {
+        float* nx = (float*)malloc(sizeof(float) * (size_t)w * h * 12);
+        for (uint32_t y = 0; y < 2 * h; y++)
+            for (uint32_t x = 0; x < 2 * w; x++)
+                for (int c = 0; c < 3; c++)
+                    nx[((size_t)y * 2 * w + x) * 3 + c] =
+                            cur[((size_t)(y / 2) * w + x / 2) * 3 + c] * 0.25f;
+        free(cur);
+        cur = nx;
+        w *= 2;
+        h *= 2;
+    }
+    for (size_t i = 0; i < (size_t)ew * eh * 3; i++) g_env[i] += cur[i];
+    free(cur);
+}
+
+/* The split-sum IBL maps of an env (pbr_graph.cpp:23-34 with the
+ * differentiable prefilter; ibl.cpp:22-60): irradiance 32x16 of the env
+ * pooled to <= 64x32, L PrefilterConv levels from the env pooled to <=
+ * 128x64 (level i at roughness i / (L-1), sizes halving from min(128x64,
+ * src)). */
+typedef struct {
+    uint32_t ew, eh, iw, ih, irr_sw, irr_sh, pw, ph, L;
+    float* irr_src;
+    float* irr;
+    float* pref_src;
+    float* pref[ORC_PBR_MAX_LEVELS];
+    uint32_t lw[ORC_PBR_MAX_LEVELS], lh[ORC_PBR_MAX_LEVELS];
+    float* norm[ORC_PBR_MAX_LEVELS];
+} ibl_maps_t;
+
+static void ibl_free(ibl_maps_t* m) {
+    free(m->irr_src);
+    free(m->irr);
+    free(m->pref_src);
+    for (uint32_t i = 0; i < m->L; i++) {
+        free(m->pref[i]);
+        free(m->norm[i]);
+    }
+}
+
+static void ibl_build(const float* env, uint32_t ew, uint32_t eh, uint32_t L,
+                      ibl_maps_t* m) {
+    memset(m, 0, sizeof(*m));
+    m->ew = ew;
+    m->eh = eh;
+    m->L = L;
+    m->iw = 32;
+    m->ih = 16;
+    m->irr_src = pool_to(env, ew, eh, 64, 32, &m->irr_sw, &m->irr_sh);
+    m->irr = (float*)malloc(sizeof(float) * 32 * 16 * 3);
+    orc_irradiance_conv(m->irr_src, m->irr_sw, m->irr_sh, 3, 32, 16, m->irr);
+    m->pref_src = pool_to(env, ew, eh, 128, 64, &m->pw, &m->ph);
+    uint32_t w = m->pw < 128 ? m->pw : 128, h = m->ph < 64 ? m->ph : 64;
+    for (uint32_t i = 0; i < L; i++) {
+        const float rough = (float)i / (float)(L - 1);
+        const float alpha = orc_prefilter_alpha(rough);
+        m->lw[i] = w;
+        m->lh[i] = h;
+        m->norm[i] = (float*)malloc(sizeof(float) * w * h);
+        orc_prefilter_conv_norm(w, h, m->pw, m->ph, alpha, m->norm[i]);
+        m->pref[i] = (float*)malloc(sizeof(float) * w * h * 3);
+        orc_prefilter_conv(m->pref_src, m->pw, m->ph, 3, m->norm[i], w, h,
+                           alpha, m->pref[i]);
+        w = w > 1 ? w / 2 : 1;
+        h = h > 1 ? h / 2 : 1;
+    }
+}
+
+/* BuildPbrShade with per-pixel G-buffer and material images sampled at
+ * pixel centres (identity uv: the w x h material "textures" are the
+ * per-pixel values), the L1 / L2 loss against T (Mean per image), and its
+ * gradients w.r.t. albedo, mr and the env through the whole IBL chain
+ * (EquirectSample / IrradianceConv / PrefilterConv / pooling transposes).
+ * Images [h][w][c]; env [eh][ew][3]; frame: cam_pos, cam_fwd, cam_right,
+ * cam_up, light_pos, light_col (3 each); lut [lh][lw][2]. */
+int orc_pbr_shade_grad(uint32_t w, uint32_t h, const float* g_n,
+                       const float* g_p, const float* mask,
+                       const float* albedo, const float* mr, const float* ao,
+                       const float* emissive, const float* frame,
+                       const float* env, uint32_t ew, uint32_t eh, uint32_t L,
+                       const float* lut, uint32_t lw, uint32_t lh,
+                       const float* target, int loss_kind, float* mapped,
+                       double* loss, float* g_albedo, float* g_mr,
+                       float* g_env) {
+    memset(g_albedo, 0, sizeof(float) * (size_t)w * h * 3);
+    memset(g_mr, 0, sizeof(float) * (size_t)w * h * 3);
+    memset(g_env, 0, sizeof(float) * (size_t)ew * eh * 3);
+    return orc_pbr_shade_grad_uv(w, h, g_n, g_p, mask, NULL, w, h, albedo,
+                                 mr, ao, emissive, frame, env, ew, eh, L, lut,
+                                 lw, lh, target, loss_kind, mapped, loss,
+                                 g_albedo, g_mr, g_env);
+}
+
+/* The same with material textures of tw x th sampled at the G-buffer's uv
+ * [h][w][2] (NULL: pixel centres with tw x th = w x h). With a uv image ao
+ * and emissive are constant 1 x 1 textures (ao = 1 and emissive = 0 in
+ * the C5 plan), otherwise [th][tw][3] images. The material gradients are
+ * the exact transpose of the bilinear samples (scatter); every gradient is
+ * accumulated (+=), so views sum by repeated calls. */
+int orc_pbr_shade_grad_uv(uint32_t w, uint32_t h, const float* g_n,
+                          const float* g_p, const float* mask,
+                          const float* uv_img, uint32_t tw, uint32_t th,
+                          const float* albedo, const float* mr,
+                          const float* ao, const float* emissive,
+                          const float* frame, const float* env, uint32_t ew,
+                          uint32_t eh, uint32_t L, const float* lut,
+                          uint32_t lw, uint32_t lh, const float* target,
+                          int loss_kind, float* mapped, double* loss,
+                          float* g_albedo, float* g_mr, float* g_env) {
+    if (L < 2 || L > ORC_PBR_MAX_LEVELS) return fail("pbr: levels 2..%d", ORC_PBR_MAX_LEVELS);
+    {
+        /* the reference's prefilter levels must stay non-uniform (> 1x1) */
+        uint32_t w0 = ew, h0 = eh;
+        while (w0 > 128 || h0 > 64) {
+            w0 /= 2;
+            h0 /= 2;
+        }
+        for (uint32_t i = 1; i < L; i++) {
+            w0 = w0 > 1 ? w0 / 2 : 1;
+            h0 = h0 > 1 ? h0 / 2 : 1;
+        }
+        if (w0 * h0 <= 1) return fail("pbr: prefilter level %u would be 1x1", L - 1);
+    }
+    ibl_maps_t m;
+    ibl_build(env, ew, eh, L, &m);
+    const float wgt = 1.f / ((float)w * (float)h * 3.f);
+    float* g_irr = (float*)calloc(32 * 16 * 3, sizeof(float));
+    float* g_pref[ORC_PBR_MAX_LEVELS];
+    for (uint32_t i = 0; i < L; i++)
+        g_pref[i] = (float*)calloc((size_t)m.lw[i] * m.lh[i] * 3, sizeof(float));
+    double tot = 0.0;
+    const int const_ao = tw != w || th != h || uv_img != NULL;
+    const float* cam_pos = frame;
+    const float* fwd = frame + 3;
+    const float* right = frame + 6;
+    const float* up = frame + 9;
+    const float* light_pos = frame + 12;
+    const float* light_col = frame + 15;
+    for (uint32_t py = 0; py < h; py++)
+        for (uint32_t px = 0; px < w; px++) {
+            const size_t p = (size_t)py * w + px;
+            float st[ORC_PBR_STATIC];
+            orc_pbr_static(&g_n[p * 3], &g_p[p * 3], cam_pos, light_pos,
+                           light_col, st);
+            const float u = uv_img ? uv_img[p * 2 + 0]
+                                   : ((float)px + 0.5f) / (float)w;
+            const float v = uv_img ? uv_img[p * 2 + 1]
+                                   : ((float)py + 0.5f) / (float)h;
+            float A[3], MR[3], AO[3], E[3], irr[3], bg[3], ab[2];
+            float P[ORC_PBR_MAX_LEVELS][3];
+            sample_clamp(albedo, tw, th, 3, u, v, A);
+            sample_clamp(mr, tw, th, 3, u, v, MR);
+            if (const_ao) {
+                /* 1x1 textures: every tap reads the one texel */
+                sample_clamp(ao, 1, 1, 3, u, v, AO);
+                sample_clamp(emissive, 1, 1, 3, u, v, E);
+            } else {
+                sample_clamp(ao, tw, th, 3, u, v, AO);
+                sample_clamp(emissive, tw, th, 3, u, v, E);
+            }
+            sample_equirect3(m.irr, 32, 16, &st[9], irr);
+            for (uint32_t i = 0; i < L; i++)
+                sample_equirect3(m.pref[i], m.lw[i], m.lh[i], &st[12], P[i]);
+            const float rough = MR[1] < 0.045f ? 0.045f
+                                : (1.f < MR[1] ? 1.f : MR[1]);
+            sample_clamp(lut, lw, lh, 2, st[0], rough, ab);
+            /* background ray (pbr_graph.cpp:115-121) */
+            const float ndc_x = ((float)px + 0.5f) * (2.f / (float)w) - 1.f;
+            const float ndc_y = ((float)py + 0.5f) * (2.f / (float)h) - 1.f;
+            float ray[3];
+            for (int c = 0; c < 3; c++)
+                ray[c] = fwd[c] + right[c] * ndc_x - up[c] * ndc_y;
+            sample_equirect3(env, ew, eh, ray, bg);
+            pbr_px_out_t o;
+            pbr_pixel(st, mask[p], A, MR[1], MR[2], AO[0], E, irr,
+                      (const float(*)[3])P, (int)L, ab, bg, &target[p * 3],
+                      loss_kind, wgt, &o);
+            tot += o.loss;
+            for (int c = 0; c < 3; c++) mapped[p * 3 + c] = o.mapped[c];
+            scatter_clamp(g_albedo, tw, th, 3, u, v, o.gA);
+            const float gmr[3] = {0.f, o.g_rough, o.g_metal};
+            scatter_clamp(g_mr, tw, th, 3, u, v, gmr);
+            scatter_equirect3(g_irr, 32, 16, &st[9], o.g_irr);
+            for (uint32_t i = 0; i < L; i++)
+                scatter_equirect3(g_pref[i], m.lw[i], m.lh[i], &st[12], o.g_P[i]);
+            scatter_equirect3(g_env, ew, eh, ray, o.g_bg);
+        }
+    *loss = tot;
+    /* the IBL chain's transposes */
+    float* g_isrc = (float*)malloc(sizeof(float) * (size_t)m.irr_sw * m.irr_sh * 3);
+    orc_irradiance_conv_bwd(g_irr, 32, 16, 3, m.irr_sw, m.irr_sh, g_isrc);
+    unpool_add(g_isrc, m.irr_sw, m.irr_sh, ew, eh, g_env);
+    float* g_psrc = (float*)calloc((size_t)m.pw * m.ph * 3, sizeof(float));
+    float* tmp = (float*)malloc(sizeof(float) * (size_t)m.pw * m.ph * 3);
+    for (uint32_t i = 0; i < L; i++) {
+        orc_prefilter_conv_bwd(g_pref[i], m.norm[i], m.lw[i], m.lh[i], 3,
+                               m.pw, m.ph,
+                               orc_prefilter_alpha((float)i / (float)(L - 1)),
+                               tmp);
+        for (size_t j = 0; j < (size_t)m.pw * m.ph * 3; j++) g_psrc[j] += tmp[j];
+    }
+    unpool_add(g_psrc, m.pw, m.ph, ew, eh, g_env);
+    free(tmp);
+    free(g_psrc);
+    free(g_isrc);
+    free(g_irr);
+    for (uint32_t i = 0; i < L; i++) free(g_pref[i]);
+    ibl_free(&m);
+    return 0;
+}
+
 /* --------------------------------------------------------- image fitting */
 
 /* Sum (f_ops.cpp:1037-1043, the Reduce2x2Sum chain 998-1033) followed by

@@ -255,6 +255,40 @@ void orc_brdf_lut(uint32_t w, uint32_t h, uint32_t n_samples, float* out);
 void orc_avg_pool2x2(const float* x, uint32_t w, uint32_t h, uint32_t n,
                      float* out);
 
+/* PBR shading graph (C5; examples/common/pbr_graph.cpp:47-138, no normal
+ * mapping). orc_pbr_static: the pixel-static terms (ndv, ndl, ndh, vdh,
+ * (1-ndv)^5, (1-vdh)^5, radiance[3], n[3], refl[3]). orc_pbr_shade_grad:
+ * per-pixel G-buffer and material images (identity uv), L1 (loss_kind 1)
+ * or L2 (2) Mean loss against target, gradients w.r.t. albedo, mr and the
+ * env through the IBL chain. frame = cam_pos, cam_fwd, cam_right, cam_up,
+ * light_pos, light_col. */
+#define ORC_PBR_STATIC 15
+#define ORC_PBR_MAX_LEVELS 8
+void orc_pbr_static(const float g_n[3], const float g_p[3],
+                    const float cam_pos[3], const float light_pos[3],
+                    const float light_col[3], float out[ORC_PBR_STATIC]);
+int orc_pbr_shade_grad(uint32_t w, uint32_t h, const float* g_n,
+                       const float* g_p, const float* mask,
+                       const float* albedo, const float* mr, const float* ao,
+                       const float* emissive, const float* frame,
+                       const float* env, uint32_t ew, uint32_t eh, uint32_t L,
+                       const float* lut, uint32_t lw, uint32_t lh,
+                       const float* target, int loss_kind, float* mapped,
+                       double* loss, float* g_albedo, float* g_mr,
+                       float* g_env);
+/* uv_img [h][w][2] (NULL: pixel centres); textures [th][tw][3]; with a uv
+ * image ao / emissive are 1x1; gradients accumulate (+=). */
+int orc_pbr_shade_grad_uv(uint32_t w, uint32_t h, const float* g_n,
+                          const float* g_p, const float* mask,
+                          const float* uv_img, uint32_t tw, uint32_t th,
+                          const float* albedo, const float* mr,
+                          const float* ao, const float* emissive,
+                          const float* frame, const float* env, uint32_t ew,
+                          uint32_t eh, uint32_t L, const float* lut,
+                          uint32_t lw, uint32_t lh, const float* target,
+                          int loss_kind, float* mapped, double* loss,
+                          float* g_albedo, float* g_mr, float* g_env);
+
 /* 2-D image fitting (C1): loss = Mean((p - t)^2) over W*H*4, Adam on p.
  * loss_trace[n_iters] = loss at the start of each iteration. */
 int orc_image_fit_run(float* param, const float* target, uint32_t w,

@@ -481,6 +481,27 @@ class Port(_Lib):
         self.lib.orc_avg_pool2x2(_fp(x), _u32(w), _u32(h), _u32(n), _fp(out))
         return out
 
+    def pbr_shade_grad(self, g_n, g_p, mask, albedo, mr, ao, emissive, frame,
+                       env, levels, lut, target, loss_kind=1):
+        h, w = mask.shape
+        eh, ew = env.shape[:2]
+        lh, lw = lut.shape[:2]
+        args = [_f32(a) for a in (g_n, g_p, mask, albedo, mr, ao, emissive,
+                                   frame, env, lut, target)]
+        mapped = np.zeros((h, w, 3), np.float32)
+        ga = np.zeros((h, w, 3), np.float32)
+        gm = np.zeros((h, w, 3), np.float32)
+        ge = np.zeros((eh, ew, 3), np.float32)
+        loss = C.c_double(0.0)
+        self._err(self.lib.orc_pbr_shade_grad(
+            _u32(w), _u32(h), _fp(args[0]), _fp(args[1]), _fp(args[2]),
+            _fp(args[3]), _fp(args[4]), _fp(args[5]), _fp(args[6]),
+            _fp(args[7]), _fp(args[8]), _u32(ew), _u32(eh), _u32(levels),
+            _fp(args[9]), _u32(lw), _u32(lh), _fp(args[10]),
+            C.c_int(loss_kind), _fp(mapped), C.byref(loss), _fp(ga),
+            _fp(gm), _fp(ge)), "pbr_shade_grad")
+        return mapped, loss.value, ga, gm, ge
+
     def vertex_neighbors_tex(self, faces, n_verts, cap=64):
         faces = _f32(faces)
         out = np.zeros(n_verts * cap, np.float32)
@@ -752,6 +773,27 @@ class Ref(_Lib):
         self._err(self.lib.ref_brdf_lut(_u32(w), _u32(h), _u32(n_samples),
                                         _fp(out)), "brdf_lut")
         return out
+
+    def pbr_shade_grad(self, g_n, g_p, mask, albedo, mr, ao, emissive, frame,
+                       env, levels, lut_w, lut_h, lut_samples, target,
+                       loss_kind=1):
+        h, w = mask.shape
+        eh, ew = env.shape[:2]
+        args = [_f32(a) for a in (g_n, g_p, mask, albedo, mr, ao, emissive,
+                                   frame, env, target)]
+        mapped = np.zeros((h, w, 3), np.float32)
+        ga = np.zeros((h, w, 3), np.float32)
+        gm = np.zeros((h, w, 3), np.float32)
+        ge = np.zeros((eh, ew, 3), np.float32)
+        loss = C.c_float(0.0)
+        self._err(self.lib.ref_pbr_shade_grad(
+            _u32(w), _u32(h), _fp(args[0]), _fp(args[1]), _fp(args[2]),
+            _fp(args[3]), _fp(args[4]), _fp(args[5]), _fp(args[6]),
+            _fp(args[7]), _fp(args[8]), _u32(ew), _u32(eh), _u32(levels),
+            _u32(lut_w), _u32(lut_h), _u32(lut_samples), _fp(args[9]),
+            C.c_int(loss_kind), _fp(mapped), C.byref(loss), _fp(ga),
+            _fp(gm), _fp(ge)), "pbr_shade_grad")
+        return mapped, loss.value, ga, gm, ge
 
     def mesh_tables(self, faces, n_verts, cap=64):
         """(vertex neighbours {max_deg, V}, face neighbours [F, 3]) from the

@@ -29,6 +29,7 @@
 #include "dressi/dressi.h"
 #include "dressi/ibl.h"
 #include "dressi/mesh_utils.h"
+#include "pbr_graph.h"
 
 using namespace dressi;
 
@@ -866,6 +867,105 @@ int ref_brdf_lut(uint32_t w, uint32_t h, uint32_t n_samples,
         Variable y = F::BrdfIntegrationLut(ImgSize{w, h}, n_samples);
         CpuEvaluator ev;
         CopyOut(ev.eval(y), out);
+    });
+}
+
+// BuildPbrShade (examples/common/pbr_graph.cpp:47-138, no normal mapping)
+// over per-pixel G-buffer leaves and w x h material textures sampled at the
+// pixel centres (identity uv and inverse-uv table), with the IBL maps of
+// the env built as the envmap example does (differentiable prefilter; L
+// levels), the Mean L1 (loss_kind 1) or L2 (2) loss against target, and
+// the gradients w.r.t. the albedo and mr textures and the env from
+// BuildBackward. frame = cam_pos, cam_fwd, cam_right, cam_up, light_pos,
+// light_col.
+int ref_pbr_shade_grad(uint32_t w, uint32_t h, const float* g_n,
+                       const float* g_p, const float* mask,
+                       const float* albedo, const float* mr, const float* ao,
+                       const float* emissive, const float* frame,
+                       const float* env, uint32_t ew, uint32_t eh, uint32_t L,
+                       uint32_t lut_w, uint32_t lut_h, uint32_t lut_samples,
+                       const float* target, int loss_kind, float* mapped,
+                       float* loss, float* g_albedo, float* g_mr,
+                       float* g_env) {
+    return Guard([&] {
+        using namespace dressi_examples;
+        const ImgSize scr{w, h};
+        std::vector<float> uvi(size_t(w) * h * 2), inv(size_t(w) * h * 4);
+        for (uint32_t y = 0; y < h; y++)
+            for (uint32_t x = 0; x < w; x++) {
+                const size_t p = size_t(y) * w + x;
+                uvi[p * 2 + 0] = (float(x) + 0.5f) / float(w);
+                uvi[p * 2 + 1] = (float(y) + 0.5f) / float(h);
+                inv[p * 4 + 0] = float(x) + 0.5f;
+                inv[p * 4 + 1] = float(y) + 0.5f;
+                inv[p * 4 + 2] = 1.f;
+                inv[p * 4 + 3] = 1.f;
+            }
+        Variable venv(VEC3, {ew, eh});
+        PbrIblMaps ibl;
+        ibl.env = venv;
+        ibl.irr = BuildIrradianceSample(venv);
+        ibl.pref = BuildPrefEnvironmentSampleConv(venv, L);
+        ibl.lut = BuildBrdfIntegrationMap({lut_w, lut_h}, lut_samples);
+        PbrGBuffer gb;
+        gb.uv = Variable(VEC2, scr);
+        gb.mask = Variable(FLOAT, scr);
+        gb.handed = Variable(FLOAT, scr);
+        gb.g_n = Variable(VEC3, scr);
+        gb.g_t = Variable(VEC3, scr);
+        gb.g_p = Variable(VEC3, scr);
+        PbrMaterialLeaves mat;
+        mat.albedo = Variable(VEC3, scr);
+        mat.mr = Variable(VEC3, scr);
+        mat.normal_map = Variable(VEC3, scr);
+        mat.ao = Variable(VEC3, scr);
+        mat.emissive = Variable(VEC3, scr);
+        PbrFrameLeaves fr;
+        fr.cam_pos = Variable(VEC3, {1, 1});
+        fr.cam_fwd = Variable(VEC3, {1, 1});
+        fr.cam_right = Variable(VEC3, {1, 1});
+        fr.cam_up = Variable(VEC3, {1, 1});
+        fr.light_pos = Variable(VEC3, {1, 1});
+        fr.light_col = Variable(VEC3, {1, 1});
+        Variable vinv(VEC4, scr), vtgt(VEC3, scr);
+        const PbrOutputs out = BuildPbrShade(gb, mat, fr, ibl, vinv, scr,
+                                             false);
+        Variable diff = F::StopGradient(vtgt) - out.mapped;
+        Variable vloss = loss_kind == 1 ? F::Mean(F::Abs(diff))
+                                        : F::Mean(diff * diff);
+        CpuEvaluator ev;
+        const size_t np = size_t(w) * h;
+        std::vector<float> zeros(np * 3, 0.f), ones(np, 1.f);
+        ev.bind(gb.uv, Tensor(VEC2, scr, uvi.data()));
+        ev.bind(gb.mask, Tensor(FLOAT, scr, mask));
+        ev.bind(gb.handed, Tensor(FLOAT, scr, ones.data()));
+        ev.bind(gb.g_n, Tensor(VEC3, scr, g_n));
+        ev.bind(gb.g_t, Tensor(VEC3, scr, zeros.data()));
+        ev.bind(gb.g_p, Tensor(VEC3, scr, g_p));
+        ev.bind(mat.albedo, Tensor(VEC3, scr, albedo));
+        ev.bind(mat.mr, Tensor(VEC3, scr, mr));
+        ev.bind(mat.normal_map, Tensor(VEC3, scr, zeros.data()));
+        ev.bind(mat.ao, Tensor(VEC3, scr, ao));
+        ev.bind(mat.emissive, Tensor(VEC3, scr, emissive));
+        const Variable* fv[6] = {&fr.cam_pos, &fr.cam_fwd, &fr.cam_right,
+                                 &fr.cam_up, &fr.light_pos, &fr.light_col};
+        for (int i = 0; i < 6; i++)
+            ev.bind(*fv[i], Tensor(VEC3, {1, 1}, frame + 3 * i));
+        ev.bind(venv, Tensor(VEC3, {ew, eh}, env));
+        ev.bind(vinv, Tensor(VEC4, scr, inv.data()));
+        ev.bind(vtgt, Tensor(VEC3, scr, target));
+        CopyOut(ev.eval(out.mapped), mapped);
+        *loss = ev.eval(vloss).data[0];
+        Variable a_mut = mat.albedo, m_mut = mat.mr, e_mut = venv;
+        a_mut.setRequiresGradRecursively();
+        m_mut.setRequiresGradRecursively();
+        e_mut.setRequiresGradRecursively();
+        auto [xs, gxs] = BuildBackward(vloss);
+        for (size_t i = 0; i < xs.size(); i++) {
+            if (xs[i] == mat.albedo) CopyOut(ev.eval(gxs[i]), g_albedo);
+            if (xs[i] == mat.mr) CopyOut(ev.eval(gxs[i]), g_mr);
+            if (xs[i] == venv) CopyOut(ev.eval(gxs[i]), g_env);
+        }
     });
 }
 
