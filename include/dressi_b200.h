@@ -417,6 +417,41 @@ int dressi_texture_plan_create(const dressi_texture_desc* desc,
 
 /* 2-D image fitting (config C1): loss = Mean((param - target)^2) over a
  * [h][w][4] image, Adam(lr, 0.9, 0.999, 1e-8) on param. */
+/* PBR material + environment optimisation (config C5): a fixed UV mesh
+ * seen from n_views cameras, GGX Cook-Torrance with split-sum IBL
+ * (examples/common/pbr_graph.cpp:47-138, no normal mapping, ao = 1,
+ * emissive = 0; irradiance 32x16 from the env pooled to <= 64x32,
+ * `levels` PrefilterConv levels from the env pooled to <= 128x64, a
+ * lut_size^2 BRDF LUT), a per-view Mean L1 (loss_kind 1) or L2 (2) of the
+ * Reinhard-mapped render against the targets, Adam on the PARAM slot
+ * [albedo tex^2 x 3 | metallic-roughness tex^2 x 3 (G = roughness, B =
+ * metallic) | env env_h x env_w x 3] with the maps clamped to [0, 1] and
+ * the env to >= 0. Targets: dressi_plan_render_targets with the
+ * ground-truth parameters in that layout (host). */
+typedef struct {
+    uint32_t struct_size;  /* sizeof(dressi_pbr_desc) */
+    uint32_t n_verts, n_faces, n_views, res;
+    uint32_t tex_size;     /* square material maps */
+    uint32_t env_w, env_h; /* powers of two */
+    uint32_t levels;       /* prefilter levels, 2..8 */
+    uint32_t lut_size, lut_samples;  /* 256, 512 in the reference */
+    uint32_t loss_kind;    /* 1 = L1, 2 = L2 */
+    float lr, beta1, beta2, eps;
+    const float* pos;      /* host [n_verts][3] world positions */
+    const float* normal;   /* host [n_verts][3] */
+    const float* uv;       /* host [n_verts][2] */
+    const float* faces;    /* host [n_faces][3] */
+    const float* mvps;     /* host [n_views][16], column-major */
+    const float* frames;   /* host [n_views][12]: cam_pos, cam_fwd,
+                              cam_right * tan(fov/2) * aspect,
+                              cam_up * tan(fov/2) */
+    const float* light;    /* host [6]: light position, light colour */
+    uint32_t loss_history; /* ring capacity (0 -> 4096) */
+    int device;
+} dressi_pbr_desc;
+
+int dressi_pbr_plan_create(const dressi_pbr_desc* desc, dressi_plan* out);
+
 int dressi_image_fit_plan_create(uint32_t width, uint32_t height, float lr,
                                  int device, dressi_plan* out);
 

@@ -58,6 +58,24 @@ class AaSilhouetteDesc(C.Structure):
     ]
 
 
+class PbrDesc(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("n_verts", C.c_uint32), ("n_faces", C.c_uint32),
+        ("n_views", C.c_uint32), ("res", C.c_uint32),
+        ("tex_size", C.c_uint32), ("env_w", C.c_uint32),
+        ("env_h", C.c_uint32), ("levels", C.c_uint32),
+        ("lut_size", C.c_uint32), ("lut_samples", C.c_uint32),
+        ("loss_kind", C.c_uint32),
+        ("lr", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float),
+        ("eps", C.c_float),
+        ("pos", _fp), ("normal", _fp), ("uv", _fp), ("faces", _fp),
+        ("mvps", _fp), ("frames", _fp), ("light", _fp),
+        ("loss_history", C.c_uint32),
+        ("device", C.c_int),
+    ]
+
+
 class TextureDesc(C.Structure):
     _fields_ = [
         ("struct_size", C.c_uint32),
@@ -144,6 +162,7 @@ SIGNATURES = {
     "dressi_brdf_lut": (C.c_int, [_u32, _u32, _u32, _vp, _vp]),
     "dressi_avg_pool2x2": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp]),
     "dressi_avg_pool2x2_grad": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp]),
+    "dressi_pbr_plan_create": (C.c_int, [C.POINTER(PbrDesc), C.POINTER(_vp)]),
     "dressi_texture_plan_create": (C.c_int, [C.POINTER(TextureDesc),
                                              C.POINTER(_vp)]),
     "dressi_image_fit_plan_create": (C.c_int, [_u32, _u32, C.c_float, C.c_int,

@@ -148,7 +148,7 @@ void upload_reg(const RegTables& t, const RegBuffers& r) {
 }  // namespace
 
 struct dressi_plan_s {
-    enum Kind { kSil, kFit, kAa, kTex } kind = kSil;
+    enum Kind { kSil, kFit, kAa, kTex, kPbr } kind = kSil;
     int device = 0;
     void* mem = nullptr;
     size_t mem_bytes = 0;
@@ -164,6 +164,9 @@ struct dressi_plan_s {
     // texture plans
     TexParams tp{};
     TexBuffers tb{};
+    // PBR plans
+    PbrDims pd{};
+    PbrBuffers pb{};
     // image fit
     size_t n = 0;
     float lr = 0.f;
@@ -239,6 +242,8 @@ struct dressi_plan_s {
             aa_sil_iteration(p, ab, s);
         } else if (kind == kTex) {
             tex_iteration(tp, tb, s);
+        } else if (kind == kPbr) {
+            pbr_iteration(pd, pb, s);
         } else {
             fit_iteration(n, lr, fb, s);
         }
@@ -1045,6 +1050,219 @@ int dressi_avg_pool2x2_grad(const float* gy, uint32_t w, uint32_t h,
     });
 }
 
+int dressi_pbr_plan_create(const dressi_pbr_desc* desc, dressi_plan* out) {
+    return guarded([&] {
+        DRESSI_REQUIRE(desc && out, "null pointer");
+        DRESSI_REQUIRE(desc->struct_size == sizeof(dressi_pbr_desc),
+                       "dressi_pbr_desc: struct_size mismatch");
+        DRESSI_REQUIRE(desc->n_verts > 0 && desc->n_faces > 0 &&
+                               desc->n_views > 0 && desc->res > 0,
+                       "PBR plan: empty mesh, views or screen");
+        DRESSI_REQUIRE(desc->pos && desc->normal && desc->uv && desc->faces &&
+                               desc->mvps && desc->frames && desc->light,
+                       "null pointer");
+        auto pow2 = [](uint32_t x) { return x && !(x & (x - 1)); };
+        DRESSI_REQUIRE(desc->tex_size >= 1 && desc->tex_size <= 8192,
+                       "PBR plan: tex_size 1..8192");
+        DRESSI_REQUIRE(pow2(desc->env_w) && pow2(desc->env_h) &&
+                               desc->env_w >= 2 && desc->env_h >= 2,
+                       "PBR plan: env sizes must be powers of two");
+        DRESSI_REQUIRE(desc->levels >= 2 && desc->levels <= kPbrMaxLevels,
+                       "PBR plan: 2..8 prefilter levels");
+        DRESSI_REQUIRE(desc->loss_kind == 1 || desc->loss_kind == 2,
+                       "PBR plan: loss_kind 1 (L1) or 2 (L2)");
+        DRESSI_REQUIRE(desc->lut_size >= 2 && desc->lut_samples >= 1,
+                       "PBR plan: lut_size >= 2, lut_samples >= 1");
+        DRESSI_REQUIRE(desc->res <= 16384, "PBR plan: res > 16384");
+        *out = nullptr;
+        DeviceGuard dg(desc->device);
+        auto pl = std::make_unique<dressi_plan_s>();
+        pl->kind = dressi_plan_s::kPbr;
+        pl->device = desc->device;
+        PbrDims& d = pl->pd;
+        d.views = int(desc->n_views);
+        d.res = int(desc->res);
+        d.tex = int(desc->tex_size);
+        d.ew = int(desc->env_w);
+        d.eh = int(desc->env_h);
+        d.levels = int(desc->levels);
+        d.n_verts = int(desc->n_verts);
+        d.n_faces = int(desc->n_faces);
+        d.lut_w = d.lut_h = int(desc->lut_size);
+        d.lut_samples = int(desc->lut_samples);
+        d.loss_kind = int(desc->loss_kind);
+        d.inv_n = 1.f / (float(desc->res) * float(desc->res) * 3.f);
+        d.lr = desc->lr;
+        d.b1 = desc->beta1;
+        d.b2 = desc->beta2;
+        d.eps = desc->eps;
+        // PoolTo (ibl.cpp:14-20): halve until the size fits
+        auto pools_to = [&](int mw, int mh) {
+            int k = 0, w = d.ew, h = d.eh;
+            while (w > mw || h > mh) {
+                w /= 2;
+                h /= 2;
+                k++;
+            }
+            return k;
+        };
+        const int ki = pools_to(64, 32), kp = pools_to(128, 64);
+        d.n_pool = std::max(ki, kp);
+        d.irr_pool = ki - 1;
+        d.pref_pool = kp - 1;
+        d.irr_sw = d.ew >> ki;
+        d.irr_sh = d.eh >> ki;
+        d.pref_sw = d.ew >> kp;
+        d.pref_sh = d.eh >> kp;
+        d.irr_w = 32;
+        d.irr_h = 16;
+        int off = 0;
+        for (int k = 0; k < d.n_pool; k++) {
+            d.pool_off[k] = off;
+            off += (d.ew >> (k + 1)) * (d.eh >> (k + 1)) * 3;
+        }
+        d.pool_floats = off;
+        // prefilter levels (ibl.cpp:41-60): min(128x64, src), halving
+        int lw = std::min(128, d.pref_sw), lh = std::min(64, d.pref_sh);
+        int texels = 0;
+        d.smem_level0 = d.levels;
+        for (int i = 0; i < d.levels; i++) {
+            DRESSI_REQUIRE(lw * lh > 1,
+                           "PBR plan: a prefilter level would be 1x1");
+            d.lw[i] = lw;
+            d.lh[i] = lh;
+            d.loff[i] = texels;
+            texels += lw * lh;
+            const float rough = float(i) / float(d.levels - 1);
+            d.alpha[i] = prefilter_alpha(rough);
+            if (d.smem_level0 == d.levels && lw * lh <= 2048) d.smem_level0 = i;
+            lw = lw > 1 ? lw / 2 : 1;
+            lh = lh > 1 ? lh / 2 : 1;
+        }
+        d.pref_texels = texels;
+        int dc = 0;
+        d.dir_irr_src = dc;
+        dc += d.irr_sw * d.irr_sh;
+        d.dir_irr_out = dc;
+        dc += d.irr_w * d.irr_h;
+        d.dir_pref_src = dc;
+        dc += d.pref_sw * d.pref_sh;
+        for (int i = 0; i < d.levels; i++) {
+            d.dir_lvl[i] = dc;
+            dc += d.lw[i] * d.lh[i];
+        }
+        d.dir_count = dc;
+        int sms = 0;
+        DRESSI_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount,
+                                           desc->device));
+        d.pixel_ctas = std::max(1, sms) * 2;
+        const int hist = desc->loss_history ? int(desc->loss_history) : 4096;
+        const size_t V = desc->n_verts, F = desc->n_faces, NV = desc->n_views;
+        const size_t R2 = size_t(desc->res) * desc->res;
+        const size_t T2 = size_t(desc->tex_size) * desc->tex_size;
+        const size_t E = size_t(desc->env_w) * desc->env_h;
+        const size_t NP = T2 * 6 + E * 3;
+        auto carve = [&](Arena& a) {
+            PbrBuffers& b = pl->pb;
+            b.params = a.take<float>(NP);
+            b.grad = a.take<float>(NP);
+            b.adam_m = a.take<float>(NP);
+            b.adam_v = a.take<float>(NP);
+            b.scalars = a.take<float>(4);
+            b.pools = a.take<float>(std::max(d.pool_floats, 1));
+            b.g_pools = a.take<float>(std::max(d.pool_floats, 1));
+            b.irr = a.take<float>(size_t(d.irr_w) * d.irr_h * 3);
+            b.g_irr = a.take<float>(size_t(d.irr_w) * d.irr_h * 3);
+            b.pref = a.take<float>(size_t(texels) * 3);
+            b.g_pref = a.take<float>(size_t(texels) * 3);
+            b.pref_norm = a.take<float>(size_t(texels));
+            b.dirs = a.take<float4>(size_t(dc));
+            b.lut = a.take<float>(size_t(d.lut_w) * d.lut_h * 2);
+            b.loss_slots = a.take<double>(kLossSlots);
+            b.loss_hist = a.take<float>(size_t(hist));
+            b.hist_cap = hist;
+            b.px = a.take<float>(NV * R2 * 20);
+            b.target = a.take<float>(NV * R2 * 3);
+            b.pos = a.take<float>(V * 3);
+            b.nrm = a.take<float>(V * 3);
+            b.uvh_attr = a.take<float>(V * 4);
+            b.faces = a.take<float>(F * 3);
+            b.mvps = a.take<float>(NV * 16);
+            b.frames = a.take<float>(NV * 12);
+            b.light = a.take<float>(6);
+            b.status = a.take<uint32_t>(4);
+        };
+        Arena dry;
+        carve(dry);
+        pl->mem_bytes = dry.used + 256;
+        DRESSI_CUDA(cudaMalloc(&pl->mem, pl->mem_bytes));
+        Arena a{static_cast<char*>(pl->mem), pl->mem_bytes, 0};
+        carve(a);
+        PbrBuffers& b = pl->pb;
+        DRESSI_CUDA(cudaMemset(pl->mem, 0, pl->mem_bytes));
+        DRESSI_CUDA(cudaMemcpy(b.pos, desc->pos, V * 12, cudaMemcpyHostToDevice));
+        DRESSI_CUDA(cudaMemcpy(b.nrm, desc->normal, V * 12,
+                               cudaMemcpyHostToDevice));
+        {
+            std::vector<float> uvh(V * 4);
+            for (size_t i = 0; i < V; i++) {
+                uvh[i * 4 + 0] = desc->uv[i * 2 + 0];
+                uvh[i * 4 + 1] = desc->uv[i * 2 + 1];
+                uvh[i * 4 + 2] = 1.f;
+                uvh[i * 4 + 3] = 0.f;
+            }
+            DRESSI_CUDA(cudaMemcpy(b.uvh_attr, uvh.data(), V * 16,
+                                   cudaMemcpyHostToDevice));
+        }
+        DRESSI_CUDA(cudaMemcpy(b.faces, desc->faces, F * 12,
+                               cudaMemcpyHostToDevice));
+        DRESSI_CUDA(cudaMemcpy(b.mvps, desc->mvps, NV * 64,
+                               cudaMemcpyHostToDevice));
+        DRESSI_CUDA(cudaMemcpy(b.frames, desc->frames, NV * 48,
+                               cudaMemcpyHostToDevice));
+        DRESSI_CUDA(cudaMemcpy(b.light, desc->light, 24, cudaMemcpyHostToDevice));
+        // set-up scratch: clip positions, raster workspace, G-buffer
+        HardDims hd;
+        hd.W = hd.H = d.res;
+        hd.views = d.views;
+        hd.n_faces = d.n_faces;
+        hd.n_verts = d.n_verts;
+        hd.n_comp = 4;
+        hd.attr_shared = 1;
+        const size_t ws = hard_workspace_bytes(hd);
+        Arena st_dry;
+        auto carve_setup = [&](Arena& q) {
+            b.clip = q.take<float>(NV * V * 4);
+            b.hard_ws = q.take<char>(ws);
+            b.gbuf_uvh = q.take<float>(NV * R2 * 4);
+            b.gbuf_n = q.take<float>(NV * R2 * 3);
+            b.gbuf_p = q.take<float>(NV * R2 * 3);
+        };
+        carve_setup(st_dry);
+        void* setup_mem = nullptr;
+        DRESSI_CUDA(cudaMalloc(&setup_mem, st_dry.used + 256));
+        Arena st{static_cast<char*>(setup_mem), st_dry.used + 256, 0};
+        carve_setup(st);
+        pbr_static_setup(d, b, nullptr);
+        DRESSI_CUDA(cudaDeviceSynchronize());
+        cudaFree(setup_mem);
+        b.clip = nullptr;
+        b.hard_ws = nullptr;
+        b.gbuf_uvh = b.gbuf_n = b.gbuf_p = nullptr;
+        pl->set_slot(DRESSI_SLOT_PARAM, b.params, NP * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_M, b.adam_m, NP * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_V, b.adam_v, NP * 4);
+        pl->set_slot(DRESSI_SLOT_ADAM_T, b.scalars, 4);
+        pl->set_slot(DRESSI_SLOT_TARGET, b.target, NV * R2 * 12);
+        pl->set_slot(DRESSI_SLOT_GRAD, b.grad, NP * 4);
+        pl->set_slot(DRESSI_SLOT_LOSS, b.scalars + 3, 4);
+        pl->set_slot(DRESSI_SLOT_LOSS_HISTORY, b.loss_hist, size_t(hist) * 4);
+        pl->set_slot(DRESSI_SLOT_RASTER, nullptr, NV * R2 * 12);
+        pl->set_slot(DRESSI_SLOT_MVP, b.mvps, NV * 64);
+        *out = pl.release();
+    });
+}
+
 int dressi_texture_plan_create(const dressi_texture_desc* desc,
                                dressi_plan* out) {
     return guarded([&] {
@@ -1260,6 +1478,17 @@ int dressi_plan_render_targets(dressi_plan p, const float* target_pos_host,
                        "render_targets: not a silhouette or texture plan");
         DeviceGuard dg(p->device);
         cudaStream_t s = as_stream(stream);
+        if (p->kind == dressi_plan_s::kPbr) {
+            // the ground-truth parameters [albedo | mr | env]
+            const size_t n = p->slots[DRESSI_SLOT_PARAM].bytes;
+            AsyncScratch gt(n, s);
+            DRESSI_CUDA(cudaMemcpyAsync(gt.p, target_pos_host, n,
+                                        cudaMemcpyHostToDevice, s));
+            pbr_render(p->pd, p->pb, static_cast<const float*>(gt.p),
+                       p->pb.target, s);
+            DRESSI_CUDA(cudaStreamSynchronize(s));
+            return;
+        }
         if (p->kind == dressi_plan_s::kTex) {
             const size_t tb = size_t(p->tp.w_tex) * p->tp.w_tex * 3 * sizeof(float);
             AsyncScratch gt(tb, s);
@@ -1308,6 +1537,13 @@ int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream) {
                 tex_update(p->tp, p->tb, s);
             return;
         }
+        if (p->kind == dressi_plan_s::kPbr) {
+            if (phase == 0)
+                pbr_forward_backward(p->pd, p->pb, s);
+            else
+                pbr_update(p->pd, p->pb, s);
+            return;
+        }
         if (p->kind == dressi_plan_s::kAa) {
             if (phase == 0) {
                 aa_sil_forward_backward(p->p, p->ab, s);
@@ -1345,6 +1581,12 @@ int dressi_plan_render(dressi_plan p, void* stream) {
             DRESSI_CUDA(cudaStreamSynchronize(s));
             return;
         }
+        if (p->kind == dressi_plan_s::kPbr) {
+            pbr_render(p->pd, p->pb, p->pb.params,
+                       static_cast<float*>(slot.ptr), s);
+            DRESSI_CUDA(cudaStreamSynchronize(s));
+            return;
+        }
         if (p->kind == dressi_plan_s::kAa) {
             aa_sil_predict(p->p, p->ab, static_cast<float*>(slot.ptr), s);
             DRESSI_CUDA(cudaStreamSynchronize(s));
@@ -1379,6 +1621,9 @@ int dressi_plan_status(dressi_plan p, uint32_t* word, void* stream) {
                                         cudaMemcpyDeviceToHost, s));
         } else if (p->kind == dressi_plan_s::kTex) {
             DRESSI_CUDA(cudaMemcpyAsync(word, p->tb.status, 4,
+                                        cudaMemcpyDeviceToHost, s));
+        } else if (p->kind == dressi_plan_s::kPbr) {
+            DRESSI_CUDA(cudaMemcpyAsync(word, p->pb.status, 4,
                                         cudaMemcpyDeviceToHost, s));
         }
         DRESSI_CUDA(cudaStreamSynchronize(s));

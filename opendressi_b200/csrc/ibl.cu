@@ -230,14 +230,14 @@ template <int NC, int kKind>
 __global__ void __launch_bounds__(kConvThreads)
 k_env_conv_bwd(const float* gy, const float4* out_dirs, int n_out,
                const float4* src_dirs, float scale_or_alpha,
-               const float* norm, float* g_env) {
+               const float* norm, float* g_env, int acc) {
     __shared__ float red[kConvThreads / 32][NC];
     const int s = blockIdx.x;
     const float4 d4 = src_dirs[s];
     const float d[3] = {d4.x, d4.y, d4.z};
-    float acc[NC];
+    float sum[NC];
 #pragma unroll
-    for (int c = 0; c < NC; c++) acc[c] = 0.f;
+    for (int c = 0; c < NC; c++) sum[c] = 0.f;
     for (int t = threadIdx.x; t < n_out; t += blockDim.x) {
         const float4 r4 = out_dirs[t];
         const float r[3] = {r4.x, r4.y, r4.z};
@@ -251,14 +251,16 @@ k_env_conv_bwd(const float* gy, const float4* out_dirs, int n_out,
             w = g / fmaxf(norm[t], 1e-12f);
         }
 #pragma unroll
-        for (int c = 0; c < NC; c++) acc[c] += gy[size_t(t) * NC + c] * w;
+        for (int c = 0; c < NC; c++) sum[c] += gy[size_t(t) * NC + c] * w;
     }
-    block_sum<NC>(acc, red);
+    block_sum<NC>(sum, red);
     if (threadIdx.x == 0) {
 #pragma unroll
-        for (int c = 0; c < NC; c++)
-            g_env[size_t(s) * NC + c] =
-                    kKind == 0 ? acc[c] * scale_or_alpha : acc[c] * d4.w;
+        for (int c = 0; c < NC; c++) {
+            const float v = kKind == 0 ? sum[c] * scale_or_alpha
+                                       : sum[c] * d4.w;
+            g_env[size_t(s) * NC + c] = acc ? g_env[size_t(s) * NC + c] + v : v;
+        }
     }
 }
 
@@ -461,15 +463,48 @@ void env_conv_bwd_launch(const float* gy, int n, const ConvTables& t,
                          int n_src, int n_out, float scale_or_alpha,
                          float* g_env, cudaStream_t s) {
     switch (n) {
-        case 1: k_env_conv_bwd<1, kKind><<<n_src, kConvThreads, 0, s>>>(gy, t.out, n_out, t.src, scale_or_alpha, t.norm, g_env); break;
-        case 2: k_env_conv_bwd<2, kKind><<<n_src, kConvThreads, 0, s>>>(gy, t.out, n_out, t.src, scale_or_alpha, t.norm, g_env); break;
-        case 3: k_env_conv_bwd<3, kKind><<<n_src, kConvThreads, 0, s>>>(gy, t.out, n_out, t.src, scale_or_alpha, t.norm, g_env); break;
-        default: k_env_conv_bwd<4, kKind><<<n_src, kConvThreads, 0, s>>>(gy, t.out, n_out, t.src, scale_or_alpha, t.norm, g_env); break;
+        case 1: k_env_conv_bwd<1, kKind><<<n_src, kConvThreads, 0, s>>>(gy, t.out, n_out, t.src, scale_or_alpha, t.norm, g_env, 0); break;
+        case 2: k_env_conv_bwd<2, kKind><<<n_src, kConvThreads, 0, s>>>(gy, t.out, n_out, t.src, scale_or_alpha, t.norm, g_env, 0); break;
+        case 3: k_env_conv_bwd<3, kKind><<<n_src, kConvThreads, 0, s>>>(gy, t.out, n_out, t.src, scale_or_alpha, t.norm, g_env, 0); break;
+        default: k_env_conv_bwd<4, kKind><<<n_src, kConvThreads, 0, s>>>(gy, t.out, n_out, t.src, scale_or_alpha, t.norm, g_env, 0); break;
     }
     check_launch();
 }
 
 }  // namespace
+
+void env_conv_run(int kind, const float* env, int n, const float4* src_dirs,
+                  int n_src, const float4* out_dirs, int n_out,
+                  float scale_or_alpha, const float* norm, float* out,
+                  cudaStream_t s) {
+    const ConvTables t{const_cast<float4*>(src_dirs),
+                       const_cast<float4*>(out_dirs),
+                       const_cast<float*>(norm)};
+    if (kind == 0)
+        env_conv_launch<0>(env, n, t, n_src, n_out, scale_or_alpha, out, s);
+    else
+        env_conv_launch<1>(env, n, t, n_src, n_out, scale_or_alpha, out, s);
+}
+
+void env_conv_bwd_run(int kind, const float* gy, int n,
+                      const float4* src_dirs, int n_src,
+                      const float4* out_dirs, int n_out, float scale_or_alpha,
+                      const float* norm, float* g_env, bool accumulate,
+                      cudaStream_t s) {
+    const int acc = accumulate ? 1 : 0;
+#define DRESSI_BWD(NC, K)                                                    \
+    k_env_conv_bwd<NC, K><<<n_src, kConvThreads, 0, s>>>(                    \
+            gy, out_dirs, n_out, src_dirs, scale_or_alpha, norm, g_env, acc)
+    if (kind == 0) {
+        if (n == 3) DRESSI_BWD(3, 0); else if (n == 1) DRESSI_BWD(1, 0);
+        else if (n == 2) DRESSI_BWD(2, 0); else DRESSI_BWD(4, 0);
+    } else {
+        if (n == 3) DRESSI_BWD(3, 1); else if (n == 1) DRESSI_BWD(1, 1);
+        else if (n == 2) DRESSI_BWD(2, 1); else DRESSI_BWD(4, 1);
+    }
+#undef DRESSI_BWD
+    check_launch();
+}
 
 void prefilter_norm_op(const float4* src_dirs, int n_src,
                        const float4* out_dirs, int n_out, float alpha,

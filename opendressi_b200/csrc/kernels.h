@@ -261,6 +261,23 @@ void avg_pool2x2_op(const float* x, int w, int h, int n, float* out,
                     cudaStream_t s);
 void avg_pool2x2_bwd_op(const float* gy, int w, int h, int n, float* g,
                         cudaStream_t s);
+// Direction + sin(theta) table of a w x h equirect map.
+void texel_dirs_op(int w, int h, float4* out, cudaStream_t s);
+void prefilter_norm_op(const float4* src_dirs, int n_src,
+                       const float4* out_dirs, int n_out, float alpha,
+                       float* norm, cudaStream_t s);
+// The convolutions over precomputed direction tables (kind 0 irradiance
+// with scale 2 pi / n_src, kind 1 prefilter with alpha and norm);
+// the transpose optionally accumulates into g_env.
+void env_conv_run(int kind, const float* env, int n, const float4* src_dirs,
+                  int n_src, const float4* out_dirs, int n_out,
+                  float scale_or_alpha, const float* norm, float* out,
+                  cudaStream_t s);
+void env_conv_bwd_run(int kind, const float* gy, int n,
+                      const float4* src_dirs, int n_src,
+                      const float4* out_dirs, int n_out, float scale_or_alpha,
+                      const float* norm, float* g_env, bool accumulate,
+                      cudaStream_t s);
 
 // One full single-device iteration.
 void sil_iteration(const SoftDims& d, const SilParams& p,
@@ -409,7 +426,80 @@ void tex_predict(const TexParams& p, const TexBuffers& b, float* out,
 void tex_render_targets(const TexParams& p, const TexBuffers& b,
                         const float* gt_tex, cudaStream_t s);
 
-// --- dressi.torch-style interpolation (interp.cu) ---
+// --- C5 PBR material + environment optimisation (pbr.cu) ---
+constexpr int kPbrThreads = 512;
+constexpr int kPbrMaxLevels = 8;
+struct PbrDims {
+    int views, res, tex, ew, eh, levels, n_verts, n_faces;
+    int lut_w, lut_h, lut_samples, loss_kind;
+    float inv_n;  // 1 / (R * R * 3): the per-view Mean
+    float lr, b1, b2, eps;
+    // IBL: irradiance out 32x16 from the env pooled to <= 64x32; the
+    // prefilter levels from the env pooled to <= 128x64
+    int irr_w, irr_h, irr_sw, irr_sh, pref_sw, pref_sh;
+    int n_pool, pool_floats, pool_off[8];  // pooled levels ew/2, ew/4, ...
+    int irr_pool, pref_pool;               // their source level (-1: env)
+    int lw[kPbrMaxLevels], lh[kPbrMaxLevels], loff[kPbrMaxLevels];
+    int pref_texels;
+    float alpha[kPbrMaxLevels];
+    int dir_irr_src, dir_irr_out, dir_pref_src, dir_lvl[kPbrMaxLevels];
+    int dir_count;
+    int smem_level0;  // first prefilter level accumulated in shared memory
+    int pixel_ctas;
+};
+struct PbrBuffers {
+    float* px;        // [views][R*R][5 float4] pixel-static records
+    float* target;    // [views][R*R][3] tone-mapped targets
+    float* params;    // albedo [T*T*3] | mr [T*T*3] | env [eh*ew*3]
+    float* grad;      // same layout
+    float* adam_m;
+    float* adam_v;
+    float* scalars;   // t, bc1, bc2, loss
+    float* pools;     // pooled env levels
+    float* g_pools;
+    float* irr;       // [16][32][3]
+    float* g_irr;
+    float* pref;      // levels concatenated [texels][3]
+    float* g_pref;
+    float* pref_norm; // [texels]
+    float4* dirs;     // direction tables
+    float* lut;       // [lut_h][lut_w][2]
+    double* loss_slots;
+    float* loss_hist;
+    int hist_cap;
+    // set-up only
+    float* pos;       // [V][3] (also the world-position attribute)
+    float* nrm;       // [V][3]
+    float* uvh_attr;  // [V][4] = (u, v, 1, 0)
+    float* faces;     // [F][3]
+    float* mvps;      // [views][16]
+    float* frames;    // [views][12]
+    float* light;     // [6]
+    float* clip;      // [views][V][4]
+    void* hard_ws;
+    float* gbuf_uvh;  // [views][R*R][4]
+    float* gbuf_n;    // [views][R*R][3]
+    float* gbuf_p;    // [views][R*R][3]
+    uint32_t* status;
+};
+__global__ void k_pbr_static(PbrDims d, const float* uvh, const float* nrm,
+                             const float* wpos, const float* frames,
+                             const float* light, float4* rec);
+size_t pbr_smem_bytes(const PbrDims& d);
+// Direction tables, normalisers, the LUT, the G-buffer and the
+// pixel-static records (plan creation).
+void pbr_static_setup(const PbrDims& d, const PbrBuffers& b, cudaStream_t s);
+// Forward + loss + gradient of [albedo | mr | env] into grad (advances the
+// Adam counter; publishes the loss).
+void pbr_forward_backward(const PbrDims& d, const PbrBuffers& b,
+                          cudaStream_t s);
+void pbr_update(const PbrDims& d, const PbrBuffers& b, cudaStream_t s);
+void pbr_iteration(const PbrDims& d, const PbrBuffers& b, cudaStream_t s);
+// out [views][R][R][3] = the tone-mapped render of params.
+void pbr_render(const PbrDims& d, const PbrBuffers& b, const float* params,
+                float* out, cudaStream_t s);
+
+// --- dressi.torch-style interpolation (interp.cu) ---// --- dressi.torch-style interpolation (interp.cu) ---
 // attr [attr_views][V][n_comp] (attr_views 1: shared), rast
 // [views][H][W][4] -> out [views][H][W][n_comp]; the grad ADDS into
 // grad [attr_views][V][n_comp].

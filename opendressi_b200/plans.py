@@ -326,3 +326,87 @@ class ImageFitPlan(Plan):
                device, C.byref(h))
         self.width, self.height = width, height
         super().__init__(h, device)
+
+
+class PbrPlan(Plan):
+    """C5: split-sum PBR material + environment optimisation on a fixed UV
+    mesh. PARAM = [albedo | metallic-roughness | env] (flat), optimised by
+    Adam with the maps clamped to [0, 1] and the env to >= 0."""
+
+    def __init__(self, pos, normal, uv, faces, mvps, frames, light, res: int,
+                 tex_size: int, env_w: int, env_h: int, levels: int = 6,
+                 lut_size: int = 256, lut_samples: int = 512,
+                 loss_kind: int = 1, lr: float = 1e-2, beta1: float = 0.9,
+                 beta2: float = 0.999, eps: float = 1e-8, device: int = 0,
+                 loss_history: int = 4096):
+        arrs = [np.ascontiguousarray(a, np.float32) for a in
+                (pos, normal, uv, faces, mvps, frames, light)]
+        self._keep = arrs
+        pos, normal, uv, faces, mvps, frames, light = arrs
+        self.n_views, self.res = mvps.reshape(-1, 16).shape[0], int(res)
+        self.tex_size, self.env_w, self.env_h = tex_size, env_w, env_h
+        d = N.PbrDesc()
+        d.struct_size = C.sizeof(N.PbrDesc)
+        d.n_verts = pos.reshape(-1, 3).shape[0]
+        d.n_faces = faces.reshape(-1, 3).shape[0]
+        d.n_views, d.res = self.n_views, self.res
+        d.tex_size, d.env_w, d.env_h = tex_size, env_w, env_h
+        d.levels, d.lut_size, d.lut_samples = levels, lut_size, lut_samples
+        d.loss_kind = loss_kind
+        d.lr, d.beta1, d.beta2, d.eps = lr, beta1, beta2, eps
+        fp = C.POINTER(C.c_float)
+        d.pos, d.normal = pos.ctypes.data_as(fp), normal.ctypes.data_as(fp)
+        d.uv, d.faces = uv.ctypes.data_as(fp), faces.ctypes.data_as(fp)
+        d.mvps, d.frames = mvps.ctypes.data_as(fp), frames.ctypes.data_as(fp)
+        d.light = light.ctypes.data_as(fp)
+        d.loss_history = loss_history
+        d.device = device
+        h = C.c_void_p(0)
+        N.call("dressi_pbr_plan_create", C.byref(d), C.byref(h))
+        super().__init__(h, device)
+
+    @classmethod
+    def from_scene(cls, scene, device: int = 0, views=None, **kw):
+        sel = slice(None) if views is None else views
+        kw.setdefault("lr", scene.lr)
+        kw.setdefault("levels", scene.levels)
+        return cls(scene.pos, scene.pos, scene.uv, scene.faces_f,
+                   scene.mvps[sel], scene.frames[sel], scene.light,
+                   scene.res, scene.tex_size, scene.env_gt.shape[1],
+                   scene.env_gt.shape[0], device=device, **kw)
+
+    @staticmethod
+    def pack(albedo, mr, env) -> np.ndarray:
+        return np.concatenate([np.ascontiguousarray(a, np.float32).ravel()
+                               for a in (albedo, mr, env)])
+
+    def unpack(self, flat):
+        t2 = self.tex_size * self.tex_size * 3
+        a = flat[:t2].reshape(self.tex_size, self.tex_size, 3)
+        m = flat[t2:2 * t2].reshape(self.tex_size, self.tex_size, 3)
+        e = flat[2 * t2:].reshape(self.env_h, self.env_w, 3)
+        return a, m, e
+
+    def render_targets(self, albedo, mr, env, stream=None):
+        flat = self.pack(albedo, mr, env)
+        N.call("dressi_plan_render_targets", self._h,
+               flat.ctypes.data_as(C.POINTER(C.c_float)), _stream_ptr(stream))
+
+    def render(self, stream=None) -> torch.Tensor:
+        """Tone-mapped renders of the current parameters [views, R, R, 3]."""
+        N.call("dressi_plan_render", self._h, _stream_ptr(stream))
+        return self.slot_tensor(N.SLOT_RASTER,
+                                (self.n_views, self.res, self.res, 3)).clone()
+
+    def forward_backward(self, stream=None):
+        N.call("dressi_plan_exec_phase", self._h, 0, _stream_ptr(stream))
+
+    def apply_update(self, stream=None):
+        N.call("dressi_plan_exec_phase", self._h, 1, _stream_ptr(stream))
+
+    def grad_tensor(self) -> torch.Tensor:
+        n = self.slot_bytes(N.SLOT_GRAD) // 4
+        return self.slot_tensor(N.SLOT_GRAD, (n,))
+
+    def loss_tensor(self) -> torch.Tensor:
+        return self.slot_tensor(N.SLOT_LOSS, (1,))

@@ -502,6 +502,31 @@ class Port(_Lib):
             _fp(gm), _fp(ge)), "pbr_shade_grad")
         return mapped, loss.value, ga, gm, ge
 
+    def pbr_view_grad(self, g_n, g_p, mask, uv, albedo, mr, frame, env,
+                      levels, lut, target, loss_kind, g_albedo, g_mr, g_env):
+        """One textured view of the C5 shading (ao = 1, emissive = 0):
+        returns (mapped, loss) and ADDS the gradients into g_*."""
+        h, w = mask.shape
+        th, tw = albedo.shape[:2]
+        eh, ew = env.shape[:2]
+        lh, lw = lut.shape[:2]
+        ao = np.ones((1, 1, 3), np.float32)
+        em = np.zeros((1, 1, 3), np.float32)
+        args = [_f32(a) for a in (g_n, g_p, mask, uv, albedo, mr, frame, env,
+                                   lut, target)]
+        mapped = np.zeros((h, w, 3), np.float32)
+        loss = C.c_double(0.0)
+        for a in (g_albedo, g_mr, g_env):
+            assert a.dtype == np.float32 and a.flags.c_contiguous
+        self._err(self.lib.orc_pbr_shade_grad_uv(
+            _u32(w), _u32(h), _fp(args[0]), _fp(args[1]), _fp(args[2]),
+            _fp(args[3]), _u32(tw), _u32(th), _fp(args[4]), _fp(args[5]),
+            _fp(ao), _fp(em), _fp(args[6]), _fp(args[7]), _u32(ew), _u32(eh),
+            _u32(levels), _fp(args[8]), _u32(lw), _u32(lh), _fp(args[9]),
+            C.c_int(loss_kind), _fp(mapped), C.byref(loss), _fp(g_albedo),
+            _fp(g_mr), _fp(g_env)), "pbr_view_grad")
+        return mapped, loss.value
+
     def vertex_neighbors_tex(self, faces, n_verts, cap=64):
         faces = _f32(faces)
         out = np.zeros(n_verts * cap, np.float32)
