@@ -1140,6 +1140,7 @@ int dressi_pbr_plan_create(const dressi_pbr_desc* desc, dressi_plan* out) {
             lh = lh > 1 ? lh / 2 : 1;
         }
         d.pref_texels = texels;
+        d.loff[d.levels] = texels;
         int dc = 0;
         d.dir_irr_src = dc;
         dc += d.irr_sw * d.irr_sh;

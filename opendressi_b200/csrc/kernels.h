@@ -439,7 +439,8 @@ struct PbrDims {
     int irr_w, irr_h, irr_sw, irr_sh, pref_sw, pref_sh;
     int n_pool, pool_floats, pool_off[8];  // pooled levels ew/2, ew/4, ...
     int irr_pool, pref_pool;               // their source level (-1: env)
-    int lw[kPbrMaxLevels], lh[kPbrMaxLevels], loff[kPbrMaxLevels];
+    int lw[kPbrMaxLevels], lh[kPbrMaxLevels];
+    int loff[kPbrMaxLevels + 1];  // texel offsets; loff[levels] = the total
     int pref_texels;
     float alpha[kPbrMaxLevels];
     int dir_irr_src, dir_irr_out, dir_pref_src, dir_lvl[kPbrMaxLevels];
