@@ -37,6 +37,21 @@ sys.path.insert(0, ROOT)
 
 METRIC = "fwd+bwd+Adam iterations/sec"
 
+DATA = {
+    "c2": "synthetic (seeded icosphere with spherical uv, seeded value-noise "
+          "target texture, seeded cameras; no dataset)",
+    "c3": "synthetic (seeded icosphere + SH-displaced target, seeded "
+          "cameras; no dataset)",
+    "c4": "synthetic (seeded icosphere + SH-displaced target, seeded "
+          "cameras; no dataset)",
+    "c5": "synthetic (seeded value-noise albedo / metallic-roughness maps, "
+          "seeded lobe-and-sky environment, seeded cameras; no dataset)",
+}
+GRAD_NAME = {"c2": "texture", "c3": "position", "c4": "position",
+             "c5": "[albedo | metallic-roughness | environment]"}
+# bytes per view-pixel kept resident between the passes of an iteration
+PX_STATE = {"c2": 24, "c3": 16, "c4": 16, "c5": 92}
+
 
 def parse():
     ap = argparse.ArgumentParser()
@@ -44,11 +59,12 @@ def parse():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c2", "c3", "c4"], default="c3")
+    ap.add_argument("--config", choices=["c2", "c3", "c4", "c5"],
+                    default="c3")
     ap.add_argument("--res", type=int, default=None,
-                    help="default: 512 (c2), 1024 (c3, c4)")
+                    help="default: 512 (c2), 1024 (c3, c4, c5)")
     ap.add_argument("--views", type=int, default=None,
-                    help="default: 8 (c2), 16 (c3), 64 (c4)")
+                    help="default: 8 (c2), 16 (c3), 64 (c4), 32 (c5)")
     ap.add_argument("--samples", type=int, default=8,
                     help="c4: stochastic edge samples per face (0: exact)")
     ap.add_argument("--laplacian", type=float, default=None,
@@ -63,11 +79,13 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     if args.views is None:
-        args.views = {"c2": 8, "c3": 16, "c4": 64}[args.config]
+        args.views = {"c2": 8, "c3": 16, "c4": 64, "c5": 32}[args.config]
     if args.res is None:
         args.res = 512 if args.config == "c2" else 1024
     if args.config == "c2" and args.level == 5:
         args.level = 4  # C2's mesh is icosphere-4
+    if args.config == "c5" and args.level == 5:
+        args.level = 6  # C5's mesh is icosphere-6
     # the silhouette example's per-technique defaults (run.cpp:127-132)
     lap0, nrm0 = {"c3": (0.15, 0.4), "c4": (0.5, 0.5)}.get(args.config,
                                                           (0.0, 0.0))
@@ -94,6 +112,20 @@ def workload(args):
             "views": args.views,
             "res": args.res,
             "texture": "1024x1024x3, 10 mip levels",
+            "lr": 1e-2,
+        }
+    if args.config == "c5":
+        return {
+            "workload": "C5 split-sum PBR material + environment "
+                        "optimisation fwd+bwd+Adam",
+            "mesh": f"icosphere-{args.level} (uv sphere, fixed geometry)",
+            "views": args.views,
+            "res": args.res,
+            "textures": "albedo + metallic-roughness 1024x1024x3, "
+                        "environment 512x256x3",
+            "ibl": "irradiance 32x16, 6 prefilter levels, BRDF LUT "
+                   "256^2 x 512 samples",
+            "loss": "L1",
             "lr": 1e-2,
         }
     if args.config == "c4":
@@ -272,6 +304,21 @@ def texture_iteration_bytes(views: int, res: int, tex: int) -> float:
             + 84.0 * tex * tex)
 
 
+def pbr_iteration_bytes(views: int, res: int, tex: int, env_w: int,
+                        env_h: int) -> float:
+    """Algorithmic HBM bytes of one C5 iteration: per view-pixel the
+    G-buffer (normal 12, position 12, coverage 4, uv 8) and the target (12)
+    read once (48 B); the two material maps read once by the sampling
+    (12 B per RGB texel each) and their gradients scattered
+    (read-modify-write, 24 B per texel) and cleared (12 B); the
+    environment the same way (its IBL maps are < 1 MB); Adam over every
+    parameter float (read p, g, m, v = 16 B, write p, m, v = 12 B)."""
+    n_tex = 2.0 * tex * tex
+    n_env = float(env_w * env_h)
+    per_texel = 12.0 + 24.0 + 12.0 + 3.0 * 28.0
+    return 48.0 * views * res * res + (n_tex + n_env) * per_texel
+
+
 # ------------------------------------------------------------- GPU arm
 
 def run_ours(args):
@@ -281,8 +328,8 @@ def run_ours(args):
     from opendressi_b200 import _native as N
     from opendressi_b200 import scene
     from opendressi_b200.distributed import ShardedStep, shard_views
-    from opendressi_b200.plans import (AaSilhouettePlan, SilhouettePlan,
-                                       TexturePlan)
+    from opendressi_b200.plans import (AaSilhouettePlan, PbrPlan,
+                                       SilhouettePlan, TexturePlan)
 
     world, rank, local = dist_env()
     if world != args.gpus:
@@ -296,12 +343,18 @@ def run_ours(args):
     if args.config == "c2":
         sc = scene.texture_scene(level=args.level, n_views=args.views,
                                  res=args.res, seed=args.seed)
+    elif args.config == "c5":
+        sc = scene.pbr_scene(level=args.level, n_views=args.views,
+                             res=args.res, seed=args.seed)
     else:
         sc = scene.silhouette_scene(level=args.level, n_views=args.views,
                                     res=args.res, seed=args.seed)
     shard = shard_views(args.views, world, rank)
     if args.config == "c2":
         plan = TexturePlan.from_scene(sc, views=shard, device=local)
+    elif args.config == "c5":
+        plan = PbrPlan.from_scene(sc, views=shard, device=local,
+                                  lut_size=256, lut_samples=512)
     elif args.config == "c4":
         plan = AaSilhouettePlan.from_scene(sc, views=shard, device=local,
                                            n_samples=args.samples,
@@ -315,6 +368,11 @@ def run_ours(args):
         plan.upload(N.SLOT_PARAM, sc.tex0)
         plan.render_targets(sc.gt_tex)
         param0, n_param = sc.tex0, sc.tex0.size
+    elif args.config == "c5":
+        plan.render_targets(sc.albedo_gt, sc.mr_gt, sc.env_gt)
+        param0 = plan.pack(sc.albedo0, sc.mr0, sc.env0)
+        plan.upload(N.SLOT_PARAM, param0)
+        n_param = param0.size
     else:
         plan.upload(N.SLOT_PARAM, sc.pos0)
         plan.render_targets(sc.target_pos)
@@ -401,11 +459,18 @@ def run_ours(args):
     # times come from an un-graphed run with CUDA events around each launch.
     prof = plan.profile(n_iters=10)
     per_iter = {p["name"]: round(p["total_ms"] / 10.0, 4) for p in prof}
-    launches_per_iter = sum(p["launches"] for p in prof) / 10.0
+    # kernel nodes of the fused iteration's CUDA graph (world 1), else the
+    # profiled launch sites of an un-graphed iteration
+    launches_per_iter = plan.launches_per_iter() if world == 1 else 0
+    if launches_per_iter == 0:
+        launches_per_iter = sum(p["launches"] for p in prof) / 10.0
     dom = max(prof, key=lambda p: p["total_ms"])
     nvw = len(shard)
     if args.config == "c2":
         alg = texture_iteration_bytes(nvw, args.res, sc.tex_size)
+    elif args.config == "c5":
+        alg = pbr_iteration_bytes(nvw, args.res, sc.tex_size,
+                                  sc.env_gt.shape[1], sc.env_gt.shape[0])
     else:
         alg = iteration_bytes(nvw, args.res, sc.n_verts, sc.n_faces,
                               reg=args.laplacian != 0.0 or args.normal != 0.0)
@@ -439,15 +504,15 @@ def run_ours(args):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded icosphere + SH-displaced target, "
-                    "seeded cameras; no dataset)",
+            "data": DATA[args.config],
             "config": dict(workload(args), parallelism=f"views/{world} "
-                           "(view-sharded, NCCL all-reduce of the position "
-                           "gradient, replicated Adam)",
+                           "(view-sharded, NCCL all-reduce of the "
+                           f"{GRAD_NAME[args.config]} gradient, replicated "
+                           "Adam)",
                            l2="per-iteration working set > L2 (per-pixel "
-                              "state 16 B/px = "
-                              f"{nvw * args.res * args.res * 16 / 1e6:.0f} MB "
-                              "per rank)"),
+                              f"state {PX_STATE[args.config]} B/px = "
+                              f"{nvw * args.res * args.res * PX_STATE[args.config] / 1e6:.0f}"
+                              " MB per rank)"),
             "gpu_launches": int(round(launches_per_iter * args.steps)),
             "loss_last": loss, "device_status": status,
             "clocks": clk, "e2e": e2e, "roofline": roofline,
@@ -460,6 +525,122 @@ def run_ours(args):
 
 
 # -------------------------------------------------------- CPU baselines
+
+class PbrCpuSample:
+    """C5 on the host cores through the C restatement (kind "port"): the
+    reference's graph evaluator transposes EquirectSample by scanning every
+    pixel direction per environment texel (f_ops.cpp:2831-2909), which at
+    512x256 x 1024^2 per view does not finish in a bench run. The geometry is
+    fixed, so the G-buffers are built once outside the timed region (as the
+    GPU plan's static per-pixel records are). One sample times (1) the IBL
+    build + its transposes alone (an 8x8 screen), (2) T views in parallel on
+    T threads (each call also rebuilds the IBL), (3) the reduction of the
+    per-thread gradients, Adam and the clamps; the iteration is
+    t_ibl + ceil(views / T) x (W - t_ibl) + t_update."""
+
+    def __init__(self, args):
+        from concurrent.futures import ThreadPoolExecutor
+
+        from oracle import pyoracle
+        from opendressi_b200 import scene
+
+        self.port = pyoracle.Port()
+        self.sc = sc = scene.pbr_scene(level=args.level, n_views=args.views,
+                                       res=args.res, seed=args.seed)
+        self.args = args
+        self.threads = max(1, min(os.cpu_count() or 1, args.views))
+        self.pool = ThreadPoolExecutor(self.threads)
+        self.lut = self.port.brdf_lut(256, 256, 512)
+        self.gb = list(self.pool.map(self._gbuffer, range(self.threads)))
+        # targets: renders of the ground-truth maps (also the warm-up pass)
+        self.targets = [None] * self.threads
+        self.targets = list(self.pool.map(
+            lambda i: self._view(i, (sc.albedo_gt, sc.mr_gt, sc.env_gt),
+                                 self._zero_grads())[0],
+            range(self.threads)))
+        self.p = np.concatenate([a.ravel() for a in
+                                 (sc.albedo0, sc.mr0, sc.env0)])
+        self.m = np.zeros_like(self.p)
+        self.v = np.zeros_like(self.p)
+        self.t = 0.0
+
+    def _gbuffer(self, v):
+        sc, port = self.sc, self.port
+        ones = np.ones((sc.n_verts, 1), np.float32)
+        uvh = np.concatenate([sc.uv, ones, 0 * ones], 1)
+        clip = port.transform_clip(sc.pos, sc.mvps[v])
+        g_uvh = port.rasterize_hard(clip, uvh, sc.faces_f, sc.res, sc.res)
+        g = port.rasterize_hard(clip, sc.pos, sc.faces_f, sc.res, sc.res)
+        frame = np.concatenate([sc.frames[v], sc.light]).astype(np.float32)
+        return (g, np.ascontiguousarray(g_uvh[..., 2]),
+                np.ascontiguousarray(g_uvh[..., :2]), frame)
+
+    def _zero_grads(self):
+        sc = self.sc
+        return (np.zeros_like(sc.albedo0), np.zeros_like(sc.mr0),
+                np.zeros_like(sc.env0))
+
+    def _view(self, i, params, grads):
+        g, mask, uv, frame = self.gb[i]
+        t = self.targets[i]
+        if t is None:
+            t = np.zeros((self.sc.res, self.sc.res, 3), np.float32)
+        alb, mr, env = params
+        return self.port.pbr_view_grad(g, g, mask, uv, alb, mr, frame, env,
+                                       self.sc.levels, self.lut, t, 1,
+                                       *grads)
+
+    def _params(self):
+        sc = self.sc
+        t2 = sc.tex_size * sc.tex_size * 3
+        return (self.p[:t2].reshape(sc.albedo0.shape),
+                self.p[t2:2 * t2].reshape(sc.mr0.shape),
+                self.p[2 * t2:].reshape(sc.env0.shape))
+
+    def iteration_seconds(self):
+        sc, port, T = self.sc, self.port, self.threads
+        params = self._params()
+        w = 8
+        gn = np.zeros((w, w, 3), np.float32)
+        gn[..., 2] = 1.0
+        t0 = time.perf_counter()
+        port.pbr_view_grad(gn, gn, np.ones((w, w), np.float32),
+                           np.full((w, w, 2), 0.5, np.float32), params[0],
+                           params[1], self.gb[0][3], params[2], sc.levels,
+                           self.lut,
+                           np.zeros((w, w, 3), np.float32), 1,
+                           *self._zero_grads())
+        t_ibl = time.perf_counter() - t0
+        grads = [self._zero_grads() for _ in range(T)]
+        t0 = time.perf_counter()
+        list(self.pool.map(lambda i: self._view(i, params, grads[i]),
+                           range(T)))
+        wall = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        g = [sum(gr[k] for gr in grads) for k in range(3)]
+        flat = np.concatenate([a.ravel() for a in g])
+        self.t = port.adam(self.p, self.m, self.v, self.t, flat, sc.lr)
+        t2 = 2 * sc.tex_size * sc.tex_size * 3
+        np.clip(self.p[:t2], 0.0, 1.0, out=self.p[:t2])
+        np.maximum(self.p[t2:], 0.0, out=self.p[t2:])
+        t_upd = time.perf_counter() - t0
+        rounds = math.ceil(self.args.views / T)
+        est = t_ibl + rounds * max(wall - t_ibl, 0.0) + t_upd
+        self.last = (t_ibl, wall, t_upd, est)
+        return est
+
+    def describe(self, n):
+        t_ibl, wall, t_upd, est = self.last
+        a = self.args
+        return (f"{n} sample(s) of the c5 iteration ({a.views} views at "
+                f"{a.res}^2, icosphere-{a.level}, textures 1024^2, env "
+                f"512x256): IBL build + transposes alone {t_ibl:.2f} s, "
+                f"{self.threads} views in parallel on {self.threads} threads "
+                f"{wall:.2f} s, gradient reduction + Adam {t_upd:.2f} s -> "
+                f"{est:.2f} s per iteration (t_ibl + "
+                f"{math.ceil(a.views / self.threads)} x (wall - t_ibl) + "
+                "update); G-buffers built once outside (fixed geometry)")
+
 
 def _cpu_setup(args):
     from oracle import pyoracle
@@ -484,6 +665,12 @@ def _cpu_setup(args):
 def cpu_reference_rate(args, max_seconds=40.0, min_iters=1, max_iters=2):
     """The reference CPU implementation (oracle/_ref, else the C port) on the
     same workload, view-parallel on the host cores."""
+    if args.config == "c5":
+        cs = PbrCpuSample(args)
+        secs = cs.iteration_seconds()
+        return {"value": 1.0 / secs, "unit": "iterations/s",
+                "cores": cs.threads, "kind": "port",
+                "sample": cs.describe(1)}
     sc, ref, port, vft, targets, threads = _cpu_setup(args)
     kind = "reference" if ref is not None else "port"
     if args.config == "c2":
@@ -512,6 +699,8 @@ def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return None
+    if args.config == "c5":
+        return _run_reference_c5(args, world)
     sc, ref, port, vft, targets, threads = _cpu_setup(args)
     # Each step is one full view-parallel iteration; the run is capped at
     # ~170 s of timed work (steps beyond it are not run; `sample` says so).
@@ -548,6 +737,40 @@ def run_reference(args):
         "data": "synthetic", "config": workload(args), "impl": "reference",
         "cpu_baseline": {"value": value, "unit": "iterations/s",
                          "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "iterations/s",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def _run_reference_c5(args, world):
+    cs = PbrCpuSample(args)
+    budget = 170.0
+    t_start = time.perf_counter()
+    times, done_w = [], 0
+    for i in range(args.warmup + args.steps):
+        est = cs.iteration_seconds()
+        if i < args.warmup:
+            done_w += 1
+            if time.perf_counter() - t_start > budget / 4:
+                break
+            continue
+        times.append(est)
+        if time.perf_counter() - t_start > budget:
+            break
+    if not times:
+        times.append(est)
+    value = len(times) / sum(times)
+    sample = (f"{len(times)} of {args.steps} requested steps timed, "
+              f"{done_w} warm-up; last: " + cs.describe(len(times)))
+    return {
+        "metric": METRIC, "value": value, "unit": "iterations/s",
+        "n_gpus": world, "steps": len(times), "warmup": done_w,
+        "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload(args), "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "iterations/s",
+                         "cores": cs.threads, "kind": "port",
+                         "sample": sample},
         "e2e": {"value": value, "unit": "iterations/s",
                 "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

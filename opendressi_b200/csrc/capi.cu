@@ -1135,12 +1135,20 @@ int dressi_pbr_plan_create(const dressi_pbr_desc* desc, dressi_plan* out) {
             texels += lw * lh;
             const float rough = float(i) / float(d.levels - 1);
             d.alpha[i] = prefilter_alpha(rough);
-            if (d.smem_level0 == d.levels && lw * lh <= 2048) d.smem_level0 = i;
             lw = lw > 1 ? lw / 2 : 1;
             lh = lh > 1 ? lh / 2 : 1;
         }
         d.pref_texels = texels;
         d.loff[d.levels] = texels;
+        // the pixel kernel accumulates the irradiance gradient and the
+        // prefilter levels from smem_level0 on in shared memory (the levels
+        // are at most 128x64, so all of them fit in practice)
+        constexpr int kPbrSmemBudget = 200 * 1024;
+        d.smem_level0 = 0;
+        while (d.smem_level0 < d.levels &&
+               size_t(d.irr_w * d.irr_h + texels - d.loff[d.smem_level0]) * 12 >
+                       size_t(kPbrSmemBudget))
+            d.smem_level0++;
         int dc = 0;
         d.dir_irr_src = dc;
         dc += d.irr_sw * d.irr_sh;
@@ -1156,7 +1164,7 @@ int dressi_pbr_plan_create(const dressi_pbr_desc* desc, dressi_plan* out) {
         int sms = 0;
         DRESSI_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount,
                                            desc->device));
-        d.pixel_ctas = std::max(1, sms) * 2;
+        d.pixel_ctas = std::max(1, sms) * pbr_pixel_blocks_per_sm(d);
         const int hist = desc->loss_history ? int(desc->loss_history) : 4096;
         const size_t V = desc->n_verts, F = desc->n_faces, NV = desc->n_views;
         const size_t R2 = size_t(desc->res) * desc->res;
@@ -1179,6 +1187,12 @@ int dressi_pbr_plan_create(const dressi_pbr_desc* desc, dressi_plan* out) {
             b.pref_norm = a.take<float>(size_t(texels));
             b.dirs = a.take<float4>(size_t(dc));
             b.lut = a.take<float>(size_t(d.lut_w) * d.lut_h * 2);
+            b.mat4 = a.take<float4>(T2);
+            b.metal = a.take<float>(T2);
+            b.env4 = a.take<float4>(E);
+            b.ibl4 = a.take<float4>(size_t(d.irr_w) * d.irr_h + texels);
+            b.gmat4 = a.take<float4>(T2);
+            b.gmetal = a.take<float>(T2);
             b.loss_slots = a.take<double>(kLossSlots);
             b.loss_hist = a.take<float>(size_t(hist));
             b.hist_cap = hist;

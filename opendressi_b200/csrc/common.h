@@ -74,13 +74,15 @@ inline size_t align_up(size_t n, size_t a) { return (n + a - 1) / a * a; }
 
 // Debug timing of individual kernels outside the CUDA graph: while a
 // profiler is installed on the calling thread, every launch site wrapped in
-// a ProfScope is bracketed by a pair of CUDA events on its stream.
+// a ProfScope (the outermost of nested ones) is bracketed by a pair of CUDA
+// events on its stream.
 struct KernelProfiler {
     struct Rec {
         const char* name;
         cudaEvent_t a, b;
     };
     std::vector<Rec> recs;
+    int depth = 0;  // open scopes; a scope nested in another is not timed
     void begin(const char* name, cudaStream_t s);
     void end(cudaStream_t s);
     // Synchronises and accumulates per-name totals (ms) and launch counts.
@@ -94,10 +96,10 @@ struct ProfScope {
     cudaStream_t s;
     KernelProfiler* p;
     ProfScope(const char* name, cudaStream_t st) : s(st), p(current_profiler()) {
-        if (p) p->begin(name, s);
+        if (p && p->depth++ == 0) p->begin(name, s);
     }
     ~ProfScope() {
-        if (p) p->end(s);
+        if (p && --p->depth == 0) p->end(s);
     }
 };
 

@@ -465,6 +465,14 @@ struct PbrBuffers {
     float* pref_norm; // [texels]
     float4* dirs;     // direction tables
     float* lut;       // [lut_h][lut_w][2]
+    // per-iteration float4 copies gathered by the pixel kernel
+    float4* mat4;     // [T*T] (albedo rgb, roughness)
+    float* metal;     // [T*T]
+    float4* env4;     // [eh*ew] (rgb, 0)
+    float4* ibl4;     // irradiance texels, then the prefilter texels
+    // material gradient accumulators (folded into grad, then cleared)
+    float4* gmat4;    // [T*T] (d albedo rgb, d roughness)
+    float* gmetal;    // [T*T]
     double* loss_slots;
     float* loss_hist;
     int hist_cap;
@@ -487,6 +495,8 @@ __global__ void k_pbr_static(PbrDims d, const float* uvh, const float* nrm,
                              const float* wpos, const float* frames,
                              const float* light, float4* rec);
 size_t pbr_smem_bytes(const PbrDims& d);
+// Sets the pixel kernel's shared-memory limit; its resident CTAs per SM.
+int pbr_pixel_blocks_per_sm(const PbrDims& d);
 // Direction tables, normalisers, the LUT, the G-buffer and the
 // pixel-static records (plan creation).
 void pbr_static_setup(const PbrDims& d, const PbrBuffers& b, cudaStream_t s);

@@ -20,7 +20,9 @@
 // static branches. Each per-pixel expression keeps the reference's
 // operation order; the backward follows its autodiff rules (ties of Max /
 // Min to the first operand, Clamp's inclusive interior, broadcast operands
-// receive the component sum).
+// receive the component sum). This file is compiled with FMA contraction
+// and the fast (<= 2 ulp) division: its contract with the reference is a
+// tolerance (1e-4 abs + 1e-3 rel), as for a shader compiler's output.
 #include <algorithm>
 
 #include "kernels.h"
@@ -104,17 +106,6 @@ __device__ __forceinline__ void taps_clamp(int w, int h, float u, float v,
     }
 }
 
-template <int N>
-__device__ __forceinline__ void gather(const float* img, const int idx[4],
-                                       const float wt[4], float out[N]) {
-#pragma unroll
-    for (int c = 0; c < N; c++) out[c] = 0.f;
-#pragma unroll
-    for (int k = 0; k < 4; k++)
-#pragma unroll
-        for (int c = 0; c < N; c++) out[c] += wt[k] * img[size_t(idx[k]) * N + c];
-}
-
 constexpr uint32_t kIrrValid = 1u, kReflValid = 2u, kBgValid = 4u;
 
 }  // namespace
@@ -175,48 +166,150 @@ __global__ void k_pbr_static(PbrDims d, const float* uvh, const float* nrm,
 
 namespace {
 
-// Adds gy[c] * w at texel `key` (stride N) of g from every lane of the
-// warp; lanes holding the same key sum first, so each distinct key costs
-// one atomic per component. key < 0: nothing to add.
-template <int N>
-__device__ __forceinline__ void warp_agg_add(float* g, int key, float w,
-                                             const float gy[N]) {
+constexpr unsigned kFull = 0xffffffffu;
+
+// Bilinear taps over a float4 image: out[c] = sum_k wt[k] * img[idx[k]].c,
+// summed in tap order as gather() does.
+__device__ __forceinline__ void gather4(const float4* img, const int idx[4],
+                                        const float wt[4], float out[4]) {
+    out[0] = out[1] = out[2] = out[3] = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float4 t = img[idx[k]];
+        out[0] += wt[k] * t.x;
+        out[1] += wt[k] * t.y;
+        out[2] += wt[k] * t.z;
+        out[3] += wt[k] * t.w;
+    }
+}
+
+// Runs of consecutive lanes whose four tap texels are all equal (the taps
+// of neighbouring pixels of a row usually share texels). Lanes that add
+// nothing carry keys of -1 and form runs of their own.
+struct Runs {
+    unsigned heads;  // lanes that start a run
+    int start;       // first lane of this lane's run
+    int steps;       // scan steps that cover the longest run
+};
+
+__device__ __forceinline__ Runs tap_runs(const int key[4]) {
     const int lane = threadIdx.x & 31;
-    const unsigned peers = __match_any_sync(0xffffffffu, key);
-    const int leader = __ffs(peers) - 1;
-    float s[N];
+    bool head = lane == 0;
 #pragma unroll
-    for (int c = 0; c < N; c++) s[c] = gy[c] * w;
-    // every lane walks its group in lane order; the group's leader keeps
-    // the total
-    const int cnt = __popc(peers);
-    const int rounds = __reduce_max_sync(0xffffffffu, cnt);
-    unsigned rest = peers & ~(1u << leader);
-    float tot[N];
+    for (int k = 0; k < 4; k++)
+        head |= __shfl_up_sync(kFull, key[k], 1) != key[k];
+    Runs r;
+    r.heads = __ballot_sync(kFull, head);
+    r.start = 31 - __clz(r.heads & (kFull >> (31 - lane)));
+    const unsigned longest =
+            __reduce_max_sync(kFull, unsigned(lane - r.start + 1));
+    r.steps = longest <= 1u ? 0 : 32 - __clz(longest - 1u);
+    return r;
+}
+
+// Segmented inclusive scan of v over the runs: the last lane of each run
+// ends with the run's total. Every lane of the warp must call it.
+template <int M>
+__device__ __forceinline__ void run_scan(const Runs& r, float v[M]) {
+    const int lane = threadIdx.x & 31;
+    for (int st = 0; st < r.steps; st++) {
+        const int off = 1 << st;
+        const bool take = lane - off >= r.start;
 #pragma unroll
-    for (int c = 0; c < N; c++) tot[c] = s[c];
-    for (int j = 1; j < rounds; j++) {
-        const int src = rest ? __ffs(rest) - 1 : lane;
-        if (rest) rest &= rest - 1u;
-        const bool take = src != lane;
-#pragma unroll
-        for (int c = 0; c < N; c++) {
-            const float o = __shfl_sync(0xffffffffu, s[c], src);
-            if (take) tot[c] += o;
+        for (int c = 0; c < M; c++) {
+            const float o = __shfl_up_sync(kFull, v[c], off);
+            if (take) v[c] += o;
         }
     }
-    if (lane == leader && key >= 0) {
+}
+
+__device__ __forceinline__ bool run_tail(const Runs& r) {
+    const int lane = threadIdx.x & 31;
+    return lane == 31 || ((r.heads >> (lane + 1)) & 1u);
+}
+
+// dst[idx[k] * 3 + c] += gy[c] * wt[k] over the four taps of each lane with
+// `on`, the lanes of a run summed first (one atomic per run, tap and
+// component). Every lane of the warp must call it.
+__device__ __forceinline__ void scatter_taps3(float* dst, bool on,
+                                              const int idx[4],
+                                              const float wt[4],
+                                              const float gy[3]) {
+    if (!__any_sync(kFull, on)) return;
+    int key[4];
+    float v[12];
 #pragma unroll
-        for (int c = 0; c < N; c++) atomicAdd(&g[size_t(key) * N + c], tot[c]);
+    for (int k = 0; k < 4; k++) {
+        key[k] = on ? idx[k] : -1;
+#pragma unroll
+        for (int c = 0; c < 3; c++) v[k * 3 + c] = on ? gy[c] * wt[k] : 0.f;
+    }
+    const Runs r = tap_runs(key);
+    run_scan<12>(r, v);
+    if (on && run_tail(r)) {
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+#pragma unroll
+            for (int c = 0; c < 3; c++)
+                atomicAdd(&dst[size_t(idx[k]) * 3 + c], v[k * 3 + c]);
     }
 }
 
 }  // namespace
 
+// The per-iteration float4 copies the pixel kernel gathers from: the
+// material maps as (albedo rgb, roughness) + metallic, the environment as
+// rgb0, and the irradiance and prefilter texels (their concatenation).
+__global__ void k_pbr_prep(PbrDims d, PbrBuffers b, const float* params) {
+    const size_t T2 = size_t(d.tex) * d.tex;
+    const size_t E = size_t(d.ew) * d.eh;
+    const size_t irr_n = size_t(d.irr_w) * d.irr_h;
+    const size_t n = T2 + E + irr_n + size_t(d.pref_texels);
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n;
+         i += size_t(gridDim.x) * blockDim.x) {
+        if (i < T2) {
+            const float* a = params + i * 3;
+            const float* m = params + (T2 + i) * 3;
+            b.mat4[i] = make_float4(a[0], a[1], a[2], m[1]);
+            b.metal[i] = m[2];
+        } else if (i < T2 + E) {
+            const float* e = params + T2 * 6 + (i - T2) * 3;
+            b.env4[i - T2] = make_float4(e[0], e[1], e[2], 0.f);
+        } else {
+            const size_t j = i - T2 - E;
+            const float* s = j < irr_n ? b.irr + j * 3 : b.pref + (j - irr_n) * 3;
+            b.ibl4[j] = make_float4(s[0], s[1], s[2], 0.f);
+        }
+    }
+}
+
+// The material gradients into the flat [albedo | mr] layout of grad (mr's
+// R channel is unused: 0), clearing the accumulators for the next
+// iteration.
+__global__ void k_pbr_fold(PbrDims d, PbrBuffers b) {
+    const size_t T2 = size_t(d.tex) * d.tex;
+    const size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+    if (i >= T2) return;
+    const float4 g = b.gmat4[i];
+    const float gm = b.gmetal[i];
+    float* ga = b.grad + i * 3;
+    float* gr = b.grad + (T2 + i) * 3;
+    ga[0] = g.x;
+    ga[1] = g.y;
+    ga[2] = g.z;
+    gr[0] = 0.f;
+    gr[1] = g.w;
+    gr[2] = gm;
+    b.gmat4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    b.gmetal[i] = 0.f;
+}
+
 // One pixel per thread (persistent grid). mode 0: forward + loss +
 // backward; mode 1: the tone-mapped render only (out [px][3]).
 // Shared memory: the gradients of the irradiance map and of the prefilter
 // levels >= d.smem_level0 (level offsets in d.loff), flushed once per CTA.
+// Every scatter is run-merged across the warp (scatter_taps3); the material
+// gradients go to float4 / float accumulators (k_pbr_fold).
 __global__ void __launch_bounds__(kPbrThreads)
 k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
     extern __shared__ float sacc[];
@@ -230,12 +323,10 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
     float* s_irr = sacc;
     float* s_pref = sacc + irr_n - d.loff[d.smem_level0] * 3;  // by texel
     const int T = d.tex;
-    const float* albedo = b.params;
-    const float* mr = b.params + size_t(T) * T * 3;
-    const float* env = mr + size_t(T) * T * 3;
-    float* g_alb = b.grad;
-    float* g_mr = b.grad + size_t(T) * T * 3;
-    float* g_env = g_mr + size_t(T) * T * 3;
+    const float4* irr4 = b.ibl4;
+    const float4* pref4 = b.ibl4 + d.irr_w * d.irr_h;
+    const float2* lut2 = reinterpret_cast<const float2*>(b.lut);
+    float* g_env = b.grad + size_t(T) * T * 6;
     const long long npx = (long long)d.res * d.res;
     const long long total = npx * d.views;
     const float wgt = d.inv_n;
@@ -254,7 +345,7 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
         float hdr[3] = {0.f, 0.f, 0.f};
         // ---- foreground (mask != 0): BuildPbrShade
         float A[3] = {0.f, 0.f, 0.f}, rough_raw = 0.f, metal = 0.f, ao = 0.f;
-        int tidx[4] = {-1, -1, -1, -1};
+        int tidx[4] = {0, 0, 0, 0};
         float twt[4] = {0.f, 0.f, 0.f, 0.f};
         float shaded[3] = {0.f, 0.f, 0.f};
         // values the backward needs; the prefilter levels with
@@ -266,7 +357,7 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
         float sd = 0.f, dist_d = 0.f, D = 0.f, dd = 0.f, alpha = 0.f;
         float alpha2 = 0.f, gv = 0.f, gl = 0.f, den_v = 0.f, den_l = 0.f;
         float r1a = 0.f, r1b = 0.f, rough = 0.f, lod = 0.f, ab0 = 0.f;
-        int iidx[4] = {-1, -1, -1, -1}, pidx[3][4];
+        int iidx[4] = {0, 0, 0, 0}, pidx[3][4];
         float iwt[4] = {0.f, 0.f, 0.f, 0.f}, pwt[3][4];
 #pragma unroll
         for (int j = 0; j < 3; j++) {
@@ -274,7 +365,7 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
             P[j][0] = P[j][1] = P[j][2] = 0.f;
 #pragma unroll
             for (int k = 0; k < 4; k++) {
-                pidx[j][k] = -1;
+                pidx[j][k] = 0;
                 pwt[j][k] = 0.f;
             }
         }
@@ -284,11 +375,15 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
         const float ndlc = fmax_ref(ndl, 1e-4f);
         if (mask != 0.f) {
             taps_clamp(T, T, r0.y, r0.z, tidx, twt);
-            float mrs[3];
-            gather<3>(albedo, tidx, twt, A);
-            gather<3>(mr, tidx, twt, mrs);
-            rough_raw = mrs[1];
-            metal = mrs[2];
+            float m4[4];
+            gather4(b.mat4, tidx, twt, m4);
+            A[0] = m4[0];
+            A[1] = m4[1];
+            A[2] = m4[2];
+            rough_raw = m4[3];
+            metal = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; k++) metal += twt[k] * b.metal[tidx[k]];
             // ao: the constant 1x1 texture (ao = 1): the sum of the taps
             ao = 0.f;
 #pragma unroll
@@ -326,7 +421,11 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
             // irradiance (EquirectSample of the 32x16 map along n)
             if (flags & kIrrValid) {
                 taps_wrap(d.irr_w, d.irr_h, r3.x, r3.y, iidx, iwt);
-                gather<3>(b.irr, iidx, iwt, irr);
+                float t4[4];
+                gather4(irr4, iidx, iwt, t4);
+                irr[0] = t4[0];
+                irr[1] = t4[1];
+                irr[2] = t4[2];
             } else {
                 irr[0] = irr[1] = irr[2] = 0.f;
             }
@@ -345,8 +444,11 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
                 wl[j] = xl[j] < 0.f ? 0.f : (1.f < xl[j] ? 1.f : xl[j]);
                 if (flags & kReflValid) {
                     taps_wrap(d.lw[li], d.lh[li], r3.z, r3.w, pidx[j], pwt[j]);
-                    gather<3>(b.pref + size_t(d.loff[li]) * 3, pidx[j],
-                              pwt[j], P[j]);
+                    float t4[4];
+                    gather4(pref4 + d.loff[li], pidx[j], pwt[j], t4);
+                    P[j][0] = t4[0];
+                    P[j][1] = t4[1];
+                    P[j][2] = t4[2];
                 }
             }
             // at most two non-zero terms: their sum is order-free
@@ -356,9 +458,14 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
                     for (int c = 0; c < 3; c++) pref[c] += P[j][c] * wl[j];
             // BRDF LUT at (ndv, rough), clamp-to-edge bilinear
             int lidx[4];
-            float lwt[4], ab[2];
+            float lwt[4], ab[2] = {0.f, 0.f};
             taps_clamp(d.lut_w, d.lut_h, ndv, rough, lidx, lwt);
-            gather<2>(b.lut, lidx, lwt, ab);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float2 t = lut2[lidx[k]];
+                ab[0] += lwt[k] * t.x;
+                ab[1] += lwt[k] * t.y;
+            }
             ab0 = ab[0];
             for (int c = 0; c < 3; c++) {
                 q[c] = f0[c] * ab[0] + ab[1];
@@ -368,13 +475,13 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
             }
         }
         // ---- background (mask != 1)
-        int bidx[4] = {-1, -1, -1, -1};
+        int bidx[4] = {0, 0, 0, 0};
         float bwt[4] = {0.f, 0.f, 0.f, 0.f};
         if (live && mask != 1.f) {
-            float bg[3] = {0.f, 0.f, 0.f};
+            float bg[4] = {0.f, 0.f, 0.f, 0.f};
             if (flags & kBgValid) {
                 taps_wrap(d.ew, d.eh, r4.x, r4.y, bidx, bwt);
-                gather<3>(env, bidx, bwt, bg);
+                gather4(b.env4, bidx, bwt, bg);
             }
             for (int c = 0; c < 3; c++)
                 hdr[c] = mask * shaded[c] + (1.f - mask) * bg[c];
@@ -407,10 +514,8 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
         {
             float gb[3];
             for (int c = 0; c < 3; c++) gb[c] = g_hdr[c] * (1.f - mask);
-            const bool any = live && mask != 1.f && (flags & kBgValid);
-#pragma unroll
-            for (int k = 0; k < 4; k++)
-                warp_agg_add<3>(g_env, any ? bidx[k] : -1, bwt[k], gb);
+            scatter_taps3(g_env, live && mask != 1.f && (flags & kBgValid),
+                          bidx, bwt, gb);
         }
         float gA[3] = {0.f, 0.f, 0.f}, g_rough = 0.f, g_metal = 0.f;
         float g_irr[3] = {0.f, 0.f, 0.f}, g_pref[3] = {0.f, 0.f, 0.f};
@@ -498,67 +603,82 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
             const bool rin = rough_raw >= 0.045f && 1.f >= rough_raw;
             g_rough = rin ? g_rough : 0.f;
         }
+        const bool fg = live && mask != 0.f;
         // material transposes: the bilinear taps of albedo and mr (G, B)
-        {
-            const bool fg = live && mask != 0.f;
-            const float gm[2] = {g_rough, g_metal};
+        // into the float4 (albedo rgb, roughness) and metallic accumulators
+        if (__any_sync(kFull, fg)) {
+            int key[4];
+            float v[20];
 #pragma unroll
             for (int k = 0; k < 4; k++) {
-                if (fg) {
+                key[k] = fg ? tidx[k] : -1;
+                v[k * 5 + 0] = gA[0] * twt[k];
+                v[k * 5 + 1] = gA[1] * twt[k];
+                v[k * 5 + 2] = gA[2] * twt[k];
+                v[k * 5 + 3] = g_rough * twt[k];
+                v[k * 5 + 4] = g_metal * twt[k];
+            }
+            const Runs rr = tap_runs(key);
+            run_scan<20>(rr, v);
+            if (fg && run_tail(rr)) {
 #pragma unroll
-                    for (int c = 0; c < 3; c++)
-                        atomicAdd(&g_alb[size_t(tidx[k]) * 3 + c], gA[c] * twt[k]);
-                    atomicAdd(&g_mr[size_t(tidx[k]) * 3 + 1], gm[0] * twt[k]);
-                    atomicAdd(&g_mr[size_t(tidx[k]) * 3 + 2], gm[1] * twt[k]);
+                for (int k = 0; k < 4; k++) {
+                    atomicAdd(&b.gmat4[tidx[k]],
+                              make_float4(v[k * 5 + 0], v[k * 5 + 1],
+                                          v[k * 5 + 2], v[k * 5 + 3]));
+                    atomicAdd(&b.gmetal[tidx[k]], v[k * 5 + 4]);
                 }
             }
         }
-        // irradiance and prefilter taps: shared-memory accumulators (the
-        // largest prefilter levels: warp-aggregated global atomics)
-        if (live && mask != 0.f) {
-            if (flags & kIrrValid)
-#pragma unroll
-                for (int k = 0; k < 4; k++)
-#pragma unroll
-                    for (int c = 0; c < 3; c++)
-                        atomicAdd(&s_irr[iidx[k] * 3 + c], g_irr[c] * iwt[k]);
-#pragma unroll
-            for (int j = 0; j < 3; j++) {
-                const int li = lv0 + j;
-                if (j >= nlv || li < d.smem_level0 || pidx[j][0] < 0 ||
-                    wl[j] == 0.f)
-                    continue;
-                float* sp = s_pref + size_t(d.loff[li]) * 3;
-#pragma unroll
-                for (int k = 0; k < 4; k++)
-#pragma unroll
-                    for (int c = 0; c < 3; c++)
-                        atomicAdd(&sp[pidx[j][k] * 3 + c],
-                                  g_pref[c] * wl[j] * pwt[j][k]);
-            }
-        }
-        // the large prefilter levels (below smem_level0): warp-aggregated
-        // global atomics, keyed by the texel's index in the concatenated
-        // levels
+        // irradiance taps: shared-memory accumulator
+        scatter_taps3(s_irr, fg && (flags & kIrrValid), iidx, iwt, g_irr);
+        // prefilter taps, keyed by the texel's index in the concatenated
+        // levels: levels >= smem_level0 into the shared-memory accumulator,
+        // the larger ones into global memory
 #pragma unroll
         for (int j = 0; j < 3; j++) {
             const int li = lv0 + j;
-            const bool on = live && mask != 0.f && j < nlv &&
-                            li < d.smem_level0 && pidx[j][0] >= 0 &&
+            const bool on = fg && j < nlv && (flags & kReflValid) &&
                             wl[j] != 0.f;
+            const bool in_smem = li >= d.smem_level0;
             float gp[3];
             for (int c = 0; c < 3; c++) gp[c] = g_pref[c] * wl[j];
             const int base = on ? d.loff[li] : 0;
+            int key[4];
 #pragma unroll
-            for (int k = 0; k < 4; k++)
-                warp_agg_add<3>(b.g_pref, on ? base + pidx[j][k] : -1,
-                                pwt[j][k], gp);
+            for (int k = 0; k < 4; k++) key[k] = base + pidx[j][k];
+            if (!__any_sync(kFull, on)) continue;
+            int rk[4];
+            float v[12];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                rk[k] = on ? key[k] : -1;
+#pragma unroll
+                for (int c = 0; c < 3; c++) v[k * 3 + c] = on ? gp[c] * pwt[j][k] : 0.f;
+            }
+            const Runs rp = tap_runs(rk);
+            run_scan<12>(rp, v);
+            if (on && run_tail(rp)) {
+                if (in_smem) {
+#pragma unroll
+                    for (int k = 0; k < 4; k++)
+#pragma unroll
+                        for (int c = 0; c < 3; c++)
+                            atomicAdd(&s_pref[size_t(key[k]) * 3 + c], v[k * 3 + c]);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 4; k++)
+#pragma unroll
+                        for (int c = 0; c < 3; c++)
+                            atomicAdd(&b.g_pref[size_t(key[k]) * 3 + c], v[k * 3 + c]);
+                }
+            }
         }
     }
     if (mode != 0) return;
     // loss: warp sum into the double slots
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_down_sync(0xffffffffu, lsum, o);
+    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_down_sync(kFull, lsum, o);
     if ((threadIdx.x & 31) == 0)
         atomicAdd(&b.loss_slots[(blockIdx.x * (blockDim.x >> 5) +
                                  (threadIdx.x >> 5)) % kLossSlots],
@@ -678,6 +798,17 @@ static void pbr_ibl_forward(const PbrDims& d, const PbrBuffers& b,
                      s);
 }
 
+int pbr_pixel_blocks_per_sm(const PbrDims& d) {
+    const size_t smem = pbr_smem_bytes(d);
+    DRESSI_CUDA(cudaFuncSetAttribute(k_pbr_pixel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     int(smem)));
+    int n = 0;
+    DRESSI_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &n, k_pbr_pixel, kPbrThreads, smem));
+    return std::max(1, n);
+}
+
 void pbr_static_setup(const PbrDims& d, const PbrBuffers& b, cudaStream_t s) {
     // direction tables and the prefilter normalisers (static)
     texel_dirs_op(d.irr_sw, d.irr_sh, b.dirs + d.dir_irr_src, s);
@@ -715,24 +846,42 @@ void pbr_static_setup(const PbrDims& d, const PbrBuffers& b, cudaStream_t s) {
     check_launch();
 }
 
+static void pbr_prep(const PbrDims& d, const PbrBuffers& b,
+                     const float* params, cudaStream_t s) {
+    ProfScope ps("pbr_prep", s);
+    const size_t n = size_t(d.tex) * d.tex + size_t(d.ew) * d.eh +
+                     size_t(d.irr_w) * d.irr_h + size_t(d.pref_texels);
+    const unsigned blocks = unsigned(std::min<size_t>((n + 255) / 256, 148 * 16));
+    k_pbr_prep<<<blocks, 256, 0, s>>>(d, b, params);
+    check_launch();
+}
+
 static void pbr_pixels(const PbrDims& d, const PbrBuffers& b, int mode,
                        float* out, cudaStream_t s) {
     ProfScope ps(mode == 0 ? "pbr_pixel" : "pbr_render", s);
     k_pbr_pixel<<<d.pixel_ctas, kPbrThreads, pbr_smem_bytes(d), s>>>(
             d, b, mode, out);
     check_launch();
+    if (mode == 0) {
+        const size_t T2 = size_t(d.tex) * d.tex;
+        k_pbr_fold<<<unsigned((T2 + 255) / 256), 256, 0, s>>>(d, b);
+        check_launch();
+    }
 }
 
 void pbr_forward_backward(const PbrDims& d, const PbrBuffers& b,
                           cudaStream_t s) {
     k_pbr_begin<<<1, 1, 0, s>>>(d, b);
     check_launch();
-    const size_t n_grad = size_t(d.tex) * d.tex * 6 + size_t(d.ew) * d.eh * 3;
-    DRESSI_CUDA(cudaMemsetAsync(b.grad, 0, n_grad * 4, s));
+    // the env part of grad takes the background scatter; the map parts are
+    // written by k_pbr_fold
+    DRESSI_CUDA(cudaMemsetAsync(b.grad + size_t(d.tex) * d.tex * 6, 0,
+                                size_t(d.ew) * d.eh * 12, s));
     DRESSI_CUDA(cudaMemsetAsync(b.g_irr, 0, size_t(d.irr_w) * d.irr_h * 12, s));
     DRESSI_CUDA(cudaMemsetAsync(b.g_pref, 0, size_t(d.pref_texels) * 12, s));
     const float* env = b.params + size_t(d.tex) * d.tex * 6;
     pbr_ibl_forward(d, b, env, s);
+    pbr_prep(d, b, b.params, s);
     pbr_pixels(d, b, 0, nullptr, s);
     {
         ProfScope ps("pbr_ibl_bwd", s);
@@ -787,6 +936,7 @@ void pbr_render(const PbrDims& d, const PbrBuffers& b, const float* params,
     PbrBuffers bb = b;
     bb.params = const_cast<float*>(params);
     pbr_ibl_forward(d, bb, params + size_t(d.tex) * d.tex * 6, s);
+    pbr_prep(d, bb, params, s);
     pbr_pixels(d, bb, 1, out, s);
 }
 

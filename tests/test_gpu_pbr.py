@@ -3,7 +3,9 @@ optimisation, csrc/pbr.cu) against the C restatement (pinned to the
 reference's BuildPbrShade + BuildBackward in test_oracle_pbr.py), on the
 same G-buffers (the hard raster is bit-exact with the reference): targets
 and renders within 1e-4 abs + 1e-3 rel (CUDA's transcendentals differ from
-the host libm by a few ulps), the first gradient of [albedo | mr | env]
+the host libm by a few ulps, and the shading is compiled with FMA contraction
+and the <= 2 ulp division, as shader compilers do), the first gradient of
+[albedo | mr | env]
 within 1e-4 abs + 1e-3 rel, loss traces within 1e-3 rel; the sharded
 phases reproduce the fused iteration."""
 
