@@ -319,6 +319,46 @@ int dressi_avg_pool2x2_grad(const float* gy, uint32_t w, uint32_t h,
                             uint32_t n_comp, float* g_x, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Indexed access of the paper's HardSoftRas (f_ops.cpp:1490-1799). Device
+ * pointers, float ids (the reference's leaves), n_comp 1..4; each output is
+ * written. A table id out of range sets DRESSI_STATUS_INDEX_RANGE in
+ * `status` (nullable) and reads nothing.
+ * ---------------------------------------------------------------------- */
+
+/* F::ScreenCoord({w, h}): out [h][w][2] = (x + 0.5, y + 0.5); a uniform
+ * size ({1, 1}) is rejected, as by the reference. */
+int dressi_screen_coord(uint32_t w, uint32_t h, float* out, void* stream);
+
+/* F::LookupFaces(vtx_attr, faces, vtx_faces, corner): out [F][n] =
+ * attr[faces[f][corner]]. */
+int dressi_lookup_faces(const float* attr, uint32_t n_verts, uint32_t n_comp,
+                        const float* faces, uint32_t n_faces, uint32_t corner,
+                        float* out, uint32_t* status, void* stream);
+/* Its exact transpose (LookupFacesBwd): g_attr [V][n] = sum of gy[f] over
+ * the faces of v's VertexFacesTex list (vf {V, max_deg}: [max_deg][V], -1
+ * padding) whose corner `corner` is v, in list order. */
+int dressi_lookup_faces_grad(const float* gy, uint32_t n_comp,
+                             const float* faces, uint32_t n_faces,
+                             const float* vf, uint32_t n_verts,
+                             uint32_t max_deg, uint32_t corner, float* g_attr,
+                             uint32_t* status, void* stream);
+
+/* F::FaceFetch forward: out [h][w][n] = attr[idx(p) - 1] (0 where idx is
+ * 0 or past the table). */
+int dressi_face_fetch(const float* attr, uint32_t n_faces, uint32_t n_comp,
+                      const float* idx, uint32_t w, uint32_t h, float* out,
+                      void* stream);
+/* FaceFetchBwd: g_attr [F][n]. n_samples == 0: the exact VJP (each face's
+ * screen bbox +-1 px scanned); > 0: the paper's hashed edge samples
+ * (band +-radius_px, jitter `seed`). prj0..2 [F][4]: the corners' clip
+ * positions (LookupFaces of the clip positions). */
+int dressi_face_fetch_grad(const float* gy, uint32_t n_comp, const float* idx,
+                           uint32_t w, uint32_t h, const float* prj0,
+                           const float* prj1, const float* prj2,
+                           uint32_t n_faces, float seed, float radius_px,
+                           uint32_t n_samples, float* g_attr, void* stream);
+
+/* ------------------------------------------------------------------------
  * Plans: one fused fwd + bwd + Adam iteration, resident on one device,
  * replayed as a CUDA graph with no per-iteration host traffic
  * (the reference's one pre-recorded command buffer per execStep,

@@ -162,6 +162,16 @@ SIGNATURES = {
     "dressi_brdf_lut": (C.c_int, [_u32, _u32, _u32, _vp, _vp]),
     "dressi_avg_pool2x2": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp]),
     "dressi_avg_pool2x2_grad": (C.c_int, [_vp, _u32, _u32, _u32, _vp, _vp]),
+    "dressi_screen_coord": (C.c_int, [_u32, _u32, _vp, _vp]),
+    "dressi_lookup_faces": (C.c_int, [_vp, _u32, _u32, _vp, _u32, _u32, _vp,
+                                      _vp, _vp]),
+    "dressi_lookup_faces_grad": (C.c_int, [_vp, _u32, _vp, _u32, _vp, _u32,
+                                           _u32, _u32, _vp, _vp, _vp]),
+    "dressi_face_fetch": (C.c_int, [_vp, _u32, _u32, _vp, _u32, _u32, _vp,
+                                    _vp]),
+    "dressi_face_fetch_grad": (C.c_int, [_vp, _u32, _vp, _u32, _u32, _vp, _vp,
+                                         _vp, _u32, C.c_float, C.c_float,
+                                         _u32, _vp, _vp]),
     "dressi_pbr_plan_create": (C.c_int, [C.POINTER(PbrDesc), C.POINTER(_vp)]),
     "dressi_texture_plan_create": (C.c_int, [C.POINTER(TextureDesc),
                                              C.POINTER(_vp)]),

@@ -22,7 +22,7 @@ LIB = os.path.join(HERE, "libdressi_b200.so")
 SOURCES = ["capi.cu", "soft_raster.cu", "silhouette.cu", "hard_raster.cu",
            "fit.cu", "noalloc.cu",
            "antialias.cu", "texture.cu", "interp.cu", "regularize.cu",
-           "ibl.cu", "pbr.cu"]
+           "ibl.cu", "pbr.cu", "faces.cu"]
 HEADERS = ["common.h", "exact.cuh", "kernels.h", "raster_soft.cuh"]
 
 NVCC_FLAGS = [

@@ -1050,6 +1050,74 @@ int dressi_avg_pool2x2_grad(const float* gy, uint32_t w, uint32_t h,
     });
 }
 
+int dressi_screen_coord(uint32_t w, uint32_t h, float* out, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(!(w == 1 && h == 1),
+                       "ScreenCoord: size must be non-uniform");
+        DRESSI_REQUIRE(out || size_t(w) * h == 0, "null pointer");
+        screen_coord_op(int(w), int(h), out, as_stream(stream));
+    });
+}
+
+int dressi_lookup_faces(const float* attr, uint32_t n_verts, uint32_t n_comp,
+                        const float* faces, uint32_t n_faces, uint32_t corner,
+                        float* out, uint32_t* status, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(n_comp >= 1 && n_comp <= 4, "n_comp must be 1..4");
+        DRESSI_REQUIRE(corner < 3, "LookupFaces: corner must be 0, 1 or 2");
+        DRESSI_REQUIRE((attr && faces && out) || n_faces == 0,
+                       "null pointer");
+        lookup_faces_op(attr, int(n_verts), int(n_comp), faces, int(n_faces),
+                        int(corner), out, status, as_stream(stream));
+    });
+}
+
+int dressi_lookup_faces_grad(const float* gy, uint32_t n_comp,
+                             const float* faces, uint32_t n_faces,
+                             const float* vf, uint32_t n_verts,
+                             uint32_t max_deg, uint32_t corner, float* g_attr,
+                             uint32_t* status, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(n_comp >= 1 && n_comp <= 4, "n_comp must be 1..4");
+        DRESSI_REQUIRE(corner < 3, "LookupFaces: corner must be 0, 1 or 2");
+        DRESSI_REQUIRE((gy && faces && vf && g_attr) || n_verts == 0,
+                       "null pointer");
+        lookup_faces_bwd_op(gy, int(n_comp), faces, int(n_faces), vf,
+                            int(n_verts), int(max_deg), int(corner), g_attr,
+                            status, as_stream(stream));
+    });
+}
+
+int dressi_face_fetch(const float* attr, uint32_t n_faces, uint32_t n_comp,
+                      const float* idx, uint32_t w, uint32_t h, float* out,
+                      void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(n_comp >= 1 && n_comp <= 4, "n_comp must be 1..4");
+        DRESSI_REQUIRE((attr || n_faces == 0) && idx && out, "null pointer");
+        face_fetch_op(attr, int(n_faces), int(n_comp), idx,
+                      (long long)w * h, out, as_stream(stream));
+    });
+}
+
+int dressi_face_fetch_grad(const float* gy, uint32_t n_comp, const float* idx,
+                           uint32_t w, uint32_t h, const float* prj0,
+                           const float* prj1, const float* prj2,
+                           uint32_t n_faces, float seed, float radius_px,
+                           uint32_t n_samples, float* g_attr, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(n_comp >= 1 && n_comp <= 4, "n_comp must be 1..4");
+        DRESSI_REQUIRE(radius_px > 0.f || n_samples == 0,
+                       "FaceFetch: radius must be positive (or n_samples == 0 "
+                       "for the exact backward)");
+        DRESSI_REQUIRE((gy && idx && prj0 && prj1 && prj2 && g_attr) ||
+                               n_faces == 0,
+                       "null pointer");
+        face_fetch_bwd_op(gy, int(n_comp), idx, int(w), int(h), prj0, prj1,
+                          prj2, int(n_faces), seed, radius_px, int(n_samples),
+                          g_attr, as_stream(stream));
+    });
+}
+
 int dressi_pbr_plan_create(const dressi_pbr_desc* desc, dressi_plan* out) {
     return guarded([&] {
         DRESSI_REQUIRE(desc && out, "null pointer");

@@ -39,6 +39,23 @@ __host__ __device__ __forceinline__ uint32_t x86_u32_via_i64(float x) {
                    : 0u;
 }
 
+// Wang's integer hash and its [0,1) mapping (f_ops.cpp:1473-1487).
+__host__ __device__ __forceinline__ uint32_t wang_hash(uint32_t x) {
+    x = (x ^ 61u) ^ (x >> 16);
+    x *= 9u;
+    x ^= x >> 4;
+    x *= 0x27d4eb2du;
+    x ^= x >> 15;
+    return x;
+}
+__host__ __device__ __forceinline__ float hash_to_unit(uint32_t f, uint32_t s,
+                                                       uint32_t seed,
+                                                       uint32_t salt) {
+    const uint32_t h = wang_hash(f * 9781u ^ s * 6151u ^ seed * 26699u ^
+                                 salt * 42589u);
+    return float(h & 0xFFFFFFu) / 16777216.f;
+}
+
 __host__ __device__ __forceinline__ int imin_(int a, int b) {
     return a < b ? a : b;
 }

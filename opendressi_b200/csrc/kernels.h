@@ -426,6 +426,22 @@ void tex_predict(const TexParams& p, const TexBuffers& b, float* out,
 void tex_render_targets(const TexParams& p, const TexBuffers& b,
                         const float* gt_tex, cudaStream_t s);
 
+// --- indexed access of the paper's HardSoftRas (faces.cu) ---
+void screen_coord_op(int w, int h, float* out, cudaStream_t s);
+void lookup_faces_op(const float* attr, int n_verts, int n, const float* faces,
+                     int n_faces, int corner, float* out, uint32_t* status,
+                     cudaStream_t s);
+void lookup_faces_bwd_op(const float* gy, int n, const float* faces,
+                         int n_faces, const float* vf, int n_verts,
+                         int max_deg, int corner, float* out,
+                         uint32_t* status, cudaStream_t s);
+void face_fetch_op(const float* attr, int n_faces, int n, const float* idx,
+                   long long n_px, float* out, cudaStream_t s);
+void face_fetch_bwd_op(const float* gy, int n, const float* idx, int w, int h,
+                       const float* prj0, const float* prj1, const float* prj2,
+                       int n_faces, float seed, float radius_px,
+                       int n_samples, float* out, cudaStream_t s);
+
 // --- C5 PBR material + environment optimisation (pbr.cu) ---
 constexpr int kPbrThreads = 512;
 constexpr int kPbrMaxLevels = 8;

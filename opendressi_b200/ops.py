@@ -585,3 +585,90 @@ def avg_pool2x2_grad(gy):
     N.call("dressi_avg_pool2x2_grad", gy.data_ptr(), 2 * w, 2 * h, n,
            out.data_ptr(), _stream())
     return out
+
+
+# ------------------------------------------------- indexed access (HSR)
+
+def _comp2(t: torch.Tensor, name: str) -> torch.Tensor:
+    """[N] or [N, n] (n 1..4) as a contiguous [N, n] float32 CUDA tensor."""
+    t = _dev(t, name)
+    if t.dim() == 1:
+        t = t.unsqueeze(1)
+    if t.dim() != 2 or not 1 <= t.shape[1] <= 4:
+        raise N.DressiError(N.ERR_INVALID, f"{name} must be [N, 1..4]")
+    return t.contiguous()
+
+
+def screen_coord(w: int, h: int, device=None) -> torch.Tensor:
+    """F::ScreenCoord: [h, w, 2] pixel centres (x + 0.5, y + 0.5)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) \
+        if device is None else torch.device(device)
+    out = torch.empty((h, w, 2), dtype=torch.float32, device=dev)
+    N.call("dressi_screen_coord", w, h, out.data_ptr(), _stream())
+    return out
+
+
+def lookup_faces(attr, faces, corner: int, check: bool = True):
+    """F::LookupFaces: attr [V, n], faces [F, 3] (float ids) -> [F, n] =
+    attr[faces[:, corner]]."""
+    attr = _comp2(attr, "attr")
+    faces = _dev(faces, "faces", 2)
+    nf = faces.shape[0]
+    out = torch.empty((nf, attr.shape[1]), dtype=torch.float32,
+                      device=attr.device)
+    st = _new_status(attr.device)
+    N.call("dressi_lookup_faces", attr.data_ptr(), attr.shape[0],
+           attr.shape[1], faces.data_ptr(), nf, corner, out.data_ptr(),
+           st.data_ptr(), _stream())
+    if check:
+        check_status(st)
+    return out
+
+
+def lookup_faces_grad(gy, faces, vertex_faces, corner: int,
+                      check: bool = True):
+    """LookupFacesBwd: gy [F, n], vertex_faces [max_deg, V] (VertexFacesTex)
+    -> [V, n]."""
+    gy = _comp2(gy, "gy")
+    faces = _dev(faces, "faces", 2)
+    vf = _dev(vertex_faces, "vertex_faces", 2)
+    md, nv = vf.shape
+    out = torch.empty((nv, gy.shape[1]), dtype=torch.float32,
+                      device=gy.device)
+    st = _new_status(gy.device)
+    N.call("dressi_lookup_faces_grad", gy.data_ptr(), gy.shape[1],
+           faces.data_ptr(), faces.shape[0], vf.data_ptr(), nv, md, corner,
+           out.data_ptr(), st.data_ptr(), _stream())
+    if check:
+        check_status(st)
+    return out
+
+
+def face_fetch(attr, idx):
+    """F::FaceFetch forward: attr [F, n], idx [H, W] float face ids (0 =
+    background) -> [H, W, n]."""
+    attr = _comp2(attr, "attr")
+    idx = _dev(idx, "idx", 2)
+    h, w = idx.shape
+    out = torch.empty((h, w, attr.shape[1]), dtype=torch.float32,
+                      device=attr.device)
+    N.call("dressi_face_fetch", attr.data_ptr(), attr.shape[0],
+           attr.shape[1], idx.data_ptr(), w, h, out.data_ptr(), _stream())
+    return out
+
+
+def face_fetch_grad(gy, idx, prj0, prj1, prj2, seed: float = 0.0,
+                    radius_px: float = 1.0, n_samples: int = 4):
+    """FaceFetchBwd: gy [H, W, n], idx [H, W], prj* [F, 4] corner clip
+    positions -> [F, n]. n_samples 0: the exact VJP."""
+    gy = _dev(gy, "gy", 3)
+    idx = _dev(idx, "idx", 2)
+    prj = [_dev(p, f"prj{k}", 2) for k, p in enumerate((prj0, prj1, prj2))]
+    h, w, n = gy.shape
+    nf = prj[0].shape[0]
+    out = torch.empty((nf, n), dtype=torch.float32, device=gy.device)
+    N.call("dressi_face_fetch_grad", gy.data_ptr(), n, idx.data_ptr(), w, h,
+           prj[0].data_ptr(), prj[1].data_ptr(), prj[2].data_ptr(), nf,
+           float(seed), float(radius_px), n_samples, out.data_ptr(),
+           _stream())
+    return out

@@ -2948,6 +2948,139 @@ int orc_pbr_shade_grad_uv(uint32_t w, uint32_t h, const float* g_n,
     return 0;
 }
 
+/* ---------------------------------------------- indexed access (HSR) */
+
+/* ScreenCoord (f_ops.cpp:1490-1513): out [h][w][2] = (x + 0.5, y + 0.5). */
+void orc_screen_coord(uint32_t w, uint32_t h, float* out) {
+    for (uint32_t py = 0; py < h; py++)
+        for (uint32_t px = 0; px < w; px++) {
+            const size_t o = ((size_t)py * w + px) * 2;
+            out[o + 0] = (float)px + 0.5f;
+            out[o + 1] = (float)py + 0.5f;
+        }
+}
+
+/* LookupFaces (f_ops.cpp:1568-1619): out[f] = attr[faces[f][corner]]
+ * (n components). A vertex id out of range is an error here (the reference
+ * reads out of bounds). */
+int orc_lookup_faces(const float* attr, uint32_t n_verts, uint32_t n,
+                     const float* faces, uint32_t n_faces, uint32_t corner,
+                     float* out) {
+    if (corner > 2) return fail("lookup_faces: corner must be 0..2");
+    for (uint32_t f = 0; f < n_faces; f++) {
+        const uint32_t vi = to_u32_via_i64(faces[(size_t)f * 3 + corner] + 0.5f);
+        if (vi >= n_verts) return fail("lookup_faces: vertex index range");
+        for (uint32_t c = 0; c < n; c++)
+            out[(size_t)f * n + c] = attr[(size_t)vi * n + c];
+    }
+    return 0;
+}
+
+/* LookupFacesBwd (f_ops.cpp:1521-1564): out[v] = sum, in the order of the
+ * vertex's incident-face list vf {V, max_deg} (-1 padding), of gy[f] over
+ * the faces whose corner `corner` is v. */
+int orc_lookup_faces_bwd(const float* gy, uint32_t n, const float* faces,
+                         uint32_t n_faces, const float* vf, uint32_t n_verts,
+                         uint32_t max_deg, uint32_t corner, float* out) {
+    if (corner > 2) return fail("lookup_faces_bwd: corner must be 0..2");
+    for (size_t i = 0; i < (size_t)n_verts * n; i++) out[i] = 0.f;
+    for (uint32_t v = 0; v < n_verts; v++)
+        for (uint32_t d = 0; d < max_deg; d++) {
+            const float fv = vf[(size_t)d * n_verts + v];
+            if (fv < -0.5f) continue;
+            const uint32_t f = to_u32_via_i64(fv + 0.5f);
+            if (f >= n_faces) return fail("lookup_faces_bwd: face index range");
+            const uint32_t vi =
+                    to_u32_via_i64(faces[(size_t)f * 3 + corner] + 0.5f);
+            if (vi != v) continue;
+            for (uint32_t c = 0; c < n; c++)
+                out[(size_t)v * n + c] += gy[(size_t)f * n + c];
+        }
+    return 0;
+}
+
+/* FaceFetch (f_ops.cpp:1736-1799): out(p) = attr[idx(p) - 1], 0 for the
+ * background and for ids past the attribute table. */
+void orc_face_fetch(const float* attr, uint32_t n_faces, uint32_t n,
+                    const float* idx, size_t n_px, float* out) {
+    for (size_t p = 0; p < n_px; p++) {
+        /* int(x) - 1 wraps INT_MIN to INT_MAX on x86: skipped either way */
+        const int64_t f = (int64_t)to_i32(idx[p] + 0.5f) - 1;
+        for (uint32_t c = 0; c < n; c++)
+            out[p * n + c] = (f < 0 || f >= (int64_t)n_faces)
+                                     ? 0.f
+                                     : attr[(size_t)f * n + c];
+    }
+}
+
+/* FaceFetchBwd (f_ops.cpp:1631-1732). n_samples == 0: the exact VJP, the
+ * face's screen bbox (+-1 px) scanned row by row, summing gy where the id
+ * image names the face. n_samples > 0: the paper's edge samples -- sample
+ * s on edge s % 3 at HashToUnit(f, s, seed, 0) along it and an offset of
+ * (2 HashToUnit(f, s, seed, 1) - 1) radius_px across it, gathered where the
+ * id image confirms the face. prj[k] [F][4]: corner k's clip position. */
+void orc_face_fetch_bwd(const float* gy, uint32_t n, const float* idx,
+                        uint32_t w, uint32_t h, const float* prj0,
+                        const float* prj1, const float* prj2,
+                        uint32_t n_faces, float seed, float radius_px,
+                        uint32_t n_samples, float* out) {
+    const float* prj[3] = {prj0, prj1, prj2};
+    const uint32_t seed_u = to_u32_via_i64(seed + 0.5f);
+    for (size_t i = 0; i < (size_t)n_faces * n; i++) out[i] = 0.f;
+    for (uint32_t f = 0; f < n_faces; f++) {
+        float s[3][2];
+        int ok = 1;
+        for (int k = 0; k < 3; k++) {
+            const float* c = &prj[k][(size_t)f * 4];
+            if (c[3] <= 1e-6f) {
+                ok = 0;
+                break;
+            }
+            s[k][0] = (c[0] / c[3] * 0.5f + 0.5f) * (float)w;
+            s[k][1] = (c[1] / c[3] * 0.5f + 0.5f) * (float)h;
+        }
+        if (!ok) continue;
+        float* dst = &out[(size_t)f * n];
+        if (n_samples == 0) {
+            const float lo_x = smin(smin(s[0][0], s[1][0]), s[2][0]);
+            const float hi_x = smax(smax(s[0][0], s[1][0]), s[2][0]);
+            const float lo_y = smin(smin(s[0][1], s[1][1]), s[2][1]);
+            const float hi_y = smax(smax(s[0][1], s[1][1]), s[2][1]);
+            const int x0 = imax(to_i32(floorf(lo_x - 1.f)), 0);
+            const int x1 = imin(to_i32(ceilf(hi_x + 1.f)), (int)w - 1);
+            const int y0 = imax(to_i32(floorf(lo_y - 1.f)), 0);
+            const int y1 = imin(to_i32(ceilf(hi_y + 1.f)), (int)h - 1);
+            for (int iy = y0; iy <= y1; iy++)
+                for (int ix = x0; ix <= x1; ix++) {
+                    const size_t p = (size_t)iy * w + (size_t)ix;
+                    if (to_u32_via_i64(idx[p] + 0.5f) != f + 1) continue;
+                    for (uint32_t c = 0; c < n; c++) dst[c] += gy[p * n + c];
+                }
+            continue;
+        }
+        for (uint32_t smp = 0; smp < n_samples; smp++) {
+            const int e = (int)(smp % 3);
+            const float* a = s[e];
+            const float* b = s[(e + 1) % 3];
+            const float ex = b[0] - a[0];
+            const float ey = b[1] - a[1];
+            const float len = sqrtf(ex * ex + ey * ey);
+            if (len < 1e-6f) continue;
+            const float u = hash_to_unit(f, smp, seed_u, 0);
+            const float o = (hash_to_unit(f, smp, seed_u, 1) * 2.f - 1.f) *
+                            radius_px;
+            const float px = a[0] + u * ex - o * (ey / len);
+            const float py = a[1] + u * ey + o * (ex / len);
+            const int ix = to_i32(floorf(px));
+            const int iy = to_i32(floorf(py));
+            if (ix < 0 || iy < 0 || ix >= (int)w || iy >= (int)h) continue;
+            const size_t p = (size_t)iy * w + (size_t)ix;
+            if (to_u32_via_i64(idx[p] + 0.5f) != f + 1) continue;
+            for (uint32_t c = 0; c < n; c++) dst[c] += gy[p * n + c];
+        }
+    }
+}
+
 /* --------------------------------------------------------- image fitting */
 
 /* Sum (f_ops.cpp:1037-1043, the Reduce2x2Sum chain 998-1033) followed by

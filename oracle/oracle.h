@@ -289,6 +289,26 @@ int orc_pbr_shade_grad_uv(uint32_t w, uint32_t h, const float* g_n,
                           int loss_kind, float* mapped, double* loss,
                           float* g_albedo, float* g_mr, float* g_env);
 
+/* Indexed access of the paper's HardSoftRas (f_ops.cpp:1490-1799):
+ * ScreenCoord; LookupFaces and its exact transpose over the vertex-face
+ * table vf {V, max_deg} (row-major [max_deg][V], -1 padding); FaceFetch
+ * and its backward (n_samples == 0: exact bbox scan; > 0: the hashed edge
+ * samples). Gradients are written (not accumulated). */
+void orc_screen_coord(uint32_t w, uint32_t h, float* out);
+int orc_lookup_faces(const float* attr, uint32_t n_verts, uint32_t n,
+                     const float* faces, uint32_t n_faces, uint32_t corner,
+                     float* out);
+int orc_lookup_faces_bwd(const float* gy, uint32_t n, const float* faces,
+                         uint32_t n_faces, const float* vf, uint32_t n_verts,
+                         uint32_t max_deg, uint32_t corner, float* out);
+void orc_face_fetch(const float* attr, uint32_t n_faces, uint32_t n,
+                    const float* idx, size_t n_px, float* out);
+void orc_face_fetch_bwd(const float* gy, uint32_t n, const float* idx,
+                        uint32_t w, uint32_t h, const float* prj0,
+                        const float* prj1, const float* prj2,
+                        uint32_t n_faces, float seed, float radius_px,
+                        uint32_t n_samples, float* out);
+
 /* 2-D image fitting (C1): loss = Mean((p - t)^2) over W*H*4, Adam on p.
  * loss_trace[n_iters] = loss at the start of each iteration. */
 int orc_image_fit_run(float* param, const float* target, uint32_t w,

@@ -566,6 +566,55 @@ class Port(_Lib):
                                     _fp(out))
         return out
 
+    # indexed access of the paper's HardSoftRas (f_ops.cpp:1490-1799)
+    def screen_coord(self, w, h):
+        out = np.zeros((h, w, 2), np.float32)
+        self.lib.orc_screen_coord(_u32(w), _u32(h), _fp(out))
+        return out
+
+    def lookup_faces(self, attr, faces, corner):
+        attr, faces = _f32(attr), _f32(faces)
+        nv = attr.shape[0]
+        n = 1 if attr.ndim == 1 else attr.shape[1]
+        out = np.zeros((faces.shape[0], n), np.float32)
+        self._err(self.lib.orc_lookup_faces(
+            _fp(attr), _u32(nv), _u32(n), _fp(faces), _u32(faces.shape[0]),
+            _u32(corner), _fp(out)), "lookup_faces")
+        return out
+
+    def lookup_faces_bwd(self, gy, faces, vf, corner):
+        """vf: [max_deg, V] (VertexFacesTex)."""
+        gy, faces, vf = _f32(gy), _f32(faces), _f32(vf)
+        n = 1 if gy.ndim == 1 else gy.shape[1]
+        md, nv = vf.shape
+        out = np.zeros((nv, n), np.float32)
+        self._err(self.lib.orc_lookup_faces_bwd(
+            _fp(gy), _u32(n), _fp(faces), _u32(faces.shape[0]), _fp(vf),
+            _u32(nv), _u32(md), _u32(corner), _fp(out)), "lookup_faces_bwd")
+        return out
+
+    def face_fetch(self, attr, idx):
+        attr, idx = _f32(attr), _f32(idx)
+        n = 1 if attr.ndim == 1 else attr.shape[1]
+        out = np.zeros(idx.shape + (n,), np.float32)
+        self.lib.orc_face_fetch(_fp(attr), _u32(attr.shape[0]), _u32(n),
+                                _fp(idx), C.c_size_t(idx.size), _fp(out))
+        return out
+
+    def face_fetch_bwd(self, gy, idx, prj0, prj1, prj2, seed, radius_px,
+                       n_samples):
+        gy, idx = _f32(gy), _f32(idx)
+        prj = [_f32(p) for p in (prj0, prj1, prj2)]
+        h, w = idx.shape
+        n = gy.shape[-1]
+        nf = prj[0].shape[0]
+        out = np.zeros((nf, n), np.float32)
+        self.lib.orc_face_fetch_bwd(
+            _fp(gy), _u32(n), _fp(idx), _u32(w), _u32(h), _fp(prj[0]),
+            _fp(prj[1]), _fp(prj[2]), _u32(nf), C.c_float(seed),
+            C.c_float(radius_px), _u32(n_samples), _fp(out))
+        return out
+
     def sum_all(self, x):
         x = _f32(x)
         nc = 1 if x.ndim == 1 else x.shape[-1]
@@ -831,6 +880,46 @@ class Ref(_Lib):
             _fp(faces), _u32(faces.shape[0]), _u32(n_verts), _u32(cap),
             _fp(vn), C.byref(md), _fp(fa)), "mesh_tables")
         return vn[: n_verts * md.value].reshape(md.value, n_verts), fa
+
+    def screen_coord(self, w, h):
+        out = np.zeros((h, w, 2), np.float32)
+        self._err(self.lib.ref_screen_coord(_u32(w), _u32(h), _fp(out)),
+                  "screen_coord")
+        return out
+
+    def lookup_faces(self, attr, faces, vf, corner, gy=None):
+        """(out [F, n], g_attr [V, n] or None) through BuildBackward."""
+        attr, faces, vf = _f32(attr), _f32(faces), _f32(vf)
+        nv = attr.shape[0]
+        n = 1 if attr.ndim == 1 else attr.shape[1]
+        nf = faces.shape[0]
+        out = np.zeros((nf, n), np.float32)
+        g = np.zeros((nv, n), np.float32) if gy is not None else None
+        keep = _f32(gy) if gy is not None else None
+        gyp = _fp(keep) if keep is not None else None
+        self._err(self.lib.ref_lookup_faces(
+            _fp(attr), _u32(nv), _u32(n), _fp(faces), _u32(nf), _fp(vf),
+            _u32(vf.shape[0]), _u32(corner), gyp, _fp(out),
+            _fp(g) if g is not None else None), "lookup_faces")
+        return out, g
+
+    def face_fetch(self, attr, idx, prj0, prj1, prj2, seed, radius_px,
+                   n_samples, gy=None):
+        attr, idx = _f32(attr), _f32(idx)
+        prj = [_f32(p) for p in (prj0, prj1, prj2)]
+        n = 1 if attr.ndim == 1 else attr.shape[1]
+        nf = attr.shape[0]
+        h, w = idx.shape
+        out = np.zeros((h, w, n), np.float32)
+        g = np.zeros((nf, n), np.float32) if gy is not None else None
+        keep = _f32(gy) if gy is not None else None
+        self._err(self.lib.ref_face_fetch(
+            _fp(attr), _u32(nf), _u32(n), _fp(idx), _u32(w), _u32(h),
+            _fp(prj[0]), _fp(prj[1]), _fp(prj[2]), C.c_float(seed),
+            C.c_float(radius_px), _u32(n_samples),
+            _fp(keep) if keep is not None else None, _fp(out),
+            _fp(g) if g is not None else None), "face_fetch")
+        return out, g
 
     def sum_all(self, x):
         x = _f32(x)

@@ -1020,6 +1020,84 @@ int ref_image_fit_run(uint32_t w, uint32_t h, const float* param0,
     });
 }
 
+// ------------------------------------------------ indexed access (HSR)
+
+// F::ScreenCoord({w, h}) (f_ops.cpp:1490-1513).
+int ref_screen_coord(uint32_t w, uint32_t h, float* out) {
+    return Guard([&] {
+        CpuEvaluator ev;
+        CopyOut(ev.eval(F::ScreenCoord({w, h})), out);
+    });
+}
+
+// F::LookupFaces(attr, faces, vf, corner) (f_ops.cpp:1568-1619) and, with
+// gy [F][n], the attribute gradient BuildBackward gives (LookupFacesBwd).
+// vf: {V, max_deg} row-major [max_deg][V].
+int ref_lookup_faces(const float* attr, uint32_t n_verts, uint32_t n,
+                     const float* faces, uint32_t n_faces, const float* vf,
+                     uint32_t max_deg, uint32_t corner, const float* gy,
+                     float* out, float* g_attr) {
+    return Guard([&] {
+        const VType vt = CompType(n);
+        Variable va(vt, {n_verts, 1});
+        Variable vfaces(VEC3, {n_faces, 1});
+        Variable vvf(FLOAT, {n_verts, max_deg});
+        Variable y = F::LookupFaces(va, vfaces, vvf, corner);
+        CpuEvaluator ev;
+        ev.bind(va, Tensor(vt, {n_verts, 1}, attr));
+        ev.bind(vfaces, Tensor(VEC3, {n_faces, 1}, faces));
+        ev.bind(vvf, Tensor(FLOAT, {n_verts, max_deg}, vf));
+        CopyOut(ev.eval(y), out);
+        if (!gy || !g_attr) return;
+        Variable vgy(vt, {n_faces, 1});
+        ev.bind(vgy, Tensor(vt, {n_faces, 1}, gy));
+        Variable loss = F::StopGradient(vgy) * y;
+        Variable vm = va;
+        vm.setRequiresGradRecursively();
+        auto [xs, gxs] = BuildBackward(loss);
+        for (size_t i = 0; i < xs.size(); i++)
+            if (xs[i] == va) CopyOut(ev.eval(gxs[i]), g_attr);
+    });
+}
+
+// F::FaceFetch(attr, idx, prj0, prj1, prj2, seed, radius_px, n_samples)
+// (f_ops.cpp:1736-1799) and, with gy [h][w][n], the attribute gradient of
+// BuildBackward (FaceFetchBwd, f_ops.cpp:1631-1732). prj*: [F][4].
+int ref_face_fetch(const float* attr, uint32_t n_faces, uint32_t n,
+                   const float* idx, uint32_t w, uint32_t h,
+                   const float* prj0, const float* prj1, const float* prj2,
+                   float seed, float radius_px, uint32_t n_samples,
+                   const float* gy, float* out, float* g_attr) {
+    return Guard([&] {
+        const VType vt = CompType(n);
+        Variable va(vt, {n_faces, 1});
+        Variable vidx(FLOAT, {w, h});
+        Variable vp[3] = {Variable(VEC4, {n_faces, 1}),
+                          Variable(VEC4, {n_faces, 1}),
+                          Variable(VEC4, {n_faces, 1})};
+        Variable vseed(FLOAT, {1, 1});
+        Variable y = F::FaceFetch(va, vidx, vp[0], vp[1], vp[2], vseed,
+                                  radius_px, n_samples);
+        CpuEvaluator ev;
+        ev.bind(va, Tensor(vt, {n_faces, 1}, attr));
+        ev.bind(vidx, Tensor(FLOAT, {w, h}, idx));
+        const float* prj[3] = {prj0, prj1, prj2};
+        for (int k = 0; k < 3; k++)
+            ev.bind(vp[k], Tensor(VEC4, {n_faces, 1}, prj[k]));
+        ev.bind(vseed, Tensor(FLOAT, {1, 1}, &seed));
+        CopyOut(ev.eval(y), out);
+        if (!gy || !g_attr) return;
+        Variable vgy(vt, {w, h});
+        ev.bind(vgy, Tensor(vt, {w, h}, gy));
+        Variable loss = F::StopGradient(vgy) * y;
+        Variable vm = va;
+        vm.setRequiresGradRecursively();
+        auto [xs, gxs] = BuildBackward(loss);
+        for (size_t i = 0; i < xs.size(); i++)
+            if (xs[i] == va) CopyOut(ev.eval(gxs[i]), g_attr);
+    });
+}
+
 // Vertex -> incident-face adjacency (src/core/mesh_utils.cpp:53-69).
 // Returns max_deg via *max_deg; out must hold n_verts*cap floats and is
 // written row-major {V, max_deg} (-1 padding). Returns nonzero if cap is
