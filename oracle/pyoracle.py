@@ -881,6 +881,25 @@ class Ref(_Lib):
             _fp(vn), C.byref(md), _fp(fa)), "mesh_tables")
         return vn[: n_verts * md.value].reshape(md.value, n_verts), fa
 
+    def paper_sil_grad(self, pos, faces, vft, mvps, targets, res, radius_px,
+                       samples, peels, seed):
+        """The paper-path silhouette loss of all views (examples/
+        silhouette_optimization/run.cpp:229-396) and d loss / d pos:
+        (loss, grad [V, 3], pred [views, R, R])."""
+        pos, faces, vft = _f32(pos), _f32(faces), _f32(vft)
+        mvps, targets = _f32(mvps), _f32(targets)
+        nv, nf = pos.shape[0], faces.shape[0]
+        nviews = mvps.reshape(-1, 16).shape[0]
+        loss = C.c_float(0.0)
+        grad = np.zeros((nv, 3), np.float32)
+        pred = np.zeros((nviews, res, res), np.float32)
+        self._err(self.lib.ref_paper_sil_grad(
+            _u32(nv), _u32(nf), _u32(nviews), _u32(res), C.c_float(radius_px),
+            _u32(samples), _u32(peels), _fp(pos), _fp(faces), _fp(vft),
+            _u32(vft.shape[0]), _fp(mvps), _fp(targets), C.c_float(seed),
+            C.byref(loss), _fp(grad), _fp(pred)), "paper_sil_grad")
+        return loss.value, grad, pred
+
     def screen_coord(self, w, h):
         out = np.zeros((h, w, 2), np.float32)
         self._err(self.lib.ref_screen_coord(_u32(w), _u32(h), _fp(out)),

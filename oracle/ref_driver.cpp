@@ -176,6 +176,95 @@ Variable SilViewLoss(const Variable& clip, const SilGraph& g,
     return diff * diff * (1.f / float(in.res * in.res));
 }
 
+// The paper's HardSoftRas prediction of one view, composed as the
+// silhouette example composes it (examples/silhouette_optimization/
+// run.cpp:229-345): K soft layers (stop-gradient; layer k > 0 discards
+// fragments at or in front of layer k-1's Eq.3 shifted depth), per layer
+// D_k = mask * sigmoid(dist * 7 / r) with the pixel's signed distance to
+// its face's edges, the corners fetched per pixel (FaceFetch of the
+// LookupFaces corner positions; backward: the face's edge samples, jitter
+// `seed`); Eq.6 I_s = 1 - prod_k (1 - D_k); pred = max(hard, I_s).
+Variable PaperViewPred(const Variable& clip, const SilGraph& g,
+                       const SilInputs& in, uint32_t peels, uint32_t samples,
+                       const Variable& seed) {
+    const ImgSize screen = {in.res, in.res};
+    const float sigma_scale = 7.f / in.radius_px;
+    Variable soft_clip = F::SoftClip(clip, g.faces_f, screen, in.radius_px);
+    Variable tri0 = F::LookupFaces(clip, g.faces_f, g.vft, 0);
+    Variable tri1 = F::LookupFaces(clip, g.faces_f, g.vft, 1);
+    Variable tri2 = F::LookupFaces(clip, g.faces_f, g.vft, 2);
+    Variable pc = F::ScreenCoord(screen);
+    Variable zero = F::Float(0.f);
+    Variable one = F::Float(1.f);
+    const auto soft_prob = [&](const Variable& idx) {
+        Variable mask = F::Greater(idx, F::Float(0.5f));
+        const auto fetch = [&](const Variable& tri) {
+            return F::FaceFetch(tri, idx, tri0, tri1, tri2, seed,
+                                in.radius_px, samples);
+        };
+        const auto screen_of = [&](const Variable& c) {
+            Variable w = F::GetW(c) + (1.f - mask);
+            Variable sx = (F::GetX(c) / w * 0.5f + 0.5f) * float(screen.w);
+            Variable sy = (F::GetY(c) / w * 0.5f + 0.5f) * float(screen.h);
+            return F::Vec2(sx, sy);
+        };
+        Variable s0 = screen_of(fetch(tri0));
+        Variable s1 = screen_of(fetch(tri1));
+        Variable s2 = screen_of(fetch(tri2));
+        const auto edge_dist = [&](const Variable& a, const Variable& b) {
+            Variable e = b - a;
+            Variable t = F::Clamp(F::Dot(pc - a, e) / (F::Dot(e, e) + 1e-12f),
+                                  zero, one);
+            Variable dd = pc - (a + t * e);
+            return F::Sqrt(F::Dot(dd, dd) + 1e-12f);
+        };
+        const auto edge_cross = [&](const Variable& a, const Variable& b) {
+            Variable e = b - a;
+            return F::GetX(e) * (F::GetY(pc) - F::GetY(a)) -
+                   F::GetY(e) * (F::GetX(pc) - F::GetX(a));
+        };
+        Variable dmin = F::Min(F::Min(edge_dist(s0, s1), edge_dist(s1, s2)),
+                               edge_dist(s2, s0));
+        Variable cr0 = edge_cross(s0, s1);
+        Variable cr1 = edge_cross(s1, s2);
+        Variable cr2 = edge_cross(s2, s0);
+        Variable inside = F::Min(
+                F::Step(zero, cr0) * F::Step(zero, cr1) * F::Step(zero, cr2) +
+                        F::Step(zero, -cr0) * F::Step(zero, -cr1) *
+                                F::Step(zero, -cr2),
+                one);
+        Variable dist = (inside * 2.f - 1.f) * dmin;
+        return mask * F::Sigmoid(dist * sigma_scale);
+    };
+    Variable one_minus = one;
+    Variable prev_shift(nullptr);
+    Variable hard(nullptr);
+    for (uint32_t peel = 0; peel < peels; peel++) {
+        Variable rs = F::StopGradient(
+                peel == 0 ? F::RasterizeSoft(soft_clip, g.face_id,
+                                             g.faces_soft, clip, g.faces_f,
+                                             g.vft, screen, in.radius_px)
+                          : F::RasterizeSoft(soft_clip, g.face_id,
+                                             g.faces_soft, clip, g.faces_f,
+                                             g.vft, prev_shift, screen,
+                                             in.radius_px));
+        Variable dist_c = F::GetX(rs);
+        Variable cov = F::GetW(rs);
+        Variable ge = F::Step(zero, dist_c);
+        prev_shift = cov * (ge * (F::Clamp(F::GetZ(rs), zero, one) * 0.5f) +
+                            (1.f - ge) *
+                                    (F::Clamp(-dist_c * (1.f / in.radius_px),
+                                              zero, one) *
+                                             0.5f +
+                                     0.5f));
+        Variable idx = (F::GetY(rs) + 1.f) * cov;
+        one_minus = one_minus * (1.f - soft_prob(idx));
+        if (peel == 0) hard = cov * ge;
+    }
+    Variable soft_sil = 1.f - one_minus;
+    return F::Max(hard, soft_sil);
+}
+
 double SumAll(const CpuTensor& t) {
     double s = 0.0;
     for (float v : t.data) s += v;
@@ -1017,6 +1106,64 @@ int ref_image_fit_run(uint32_t w, uint32_t h, const float* param0,
         const auto t1 = std::chrono::steady_clock::now();
         if (seconds) *seconds = std::chrono::duration<double>(t1 - t0).count();
         CopyOut(tp, param_out);
+    });
+}
+
+// One evaluation of the paper-path silhouette loss over all views
+// (SumPixelWise of (target - pred)^2 / R^2, BuildBackward): loss_out = the
+// summed loss image, grad_out [V][3] = d loss / d pos, pred_out (nullable)
+// [views][R][R]. `seed` is FaceFetch's jitter (the example passes its Adam
+// counter).
+int ref_paper_sil_grad(uint32_t n_verts, uint32_t n_faces, uint32_t n_views,
+                       uint32_t res, float radius_px, uint32_t samples,
+                       uint32_t peels, const float* pos, const float* faces,
+                       const float* vft, uint32_t max_deg, const float* mvps,
+                       const float* targets, float seed, float* loss_out,
+                       float* grad_out, float* pred_out) {
+    return Guard([&] {
+        SilInputs in{n_verts, n_faces, res, max_deg, radius_px, 0.f};
+        std::vector<float> face_id(size_t(n_faces) * 3),
+                faces_soft(size_t(n_faces) * 3);
+        for (uint32_t f = 0; f < n_faces; f++)
+            for (uint32_t k = 0; k < 3; k++) {
+                face_id[f * 3 + k] = float(f);
+                faces_soft[f * 3 + k] = float(f * 3 + k);
+            }
+        SilGraph g;
+        g.faces_f = Variable(VEC3, {n_faces, 1});
+        g.vft = Variable(FLOAT, {n_verts, max_deg});
+        g.face_id = Variable(FLOAT, {n_faces * 3, 1});
+        g.faces_soft = Variable(IVEC3, {n_faces, 1});
+        Variable vpos(VEC3, {n_verts, 1});
+        Variable vseed(FLOAT, {1, 1});
+        Variables losses, preds;
+        for (uint32_t v = 0; v < n_views; v++) {
+            g.targets.emplace_back(FLOAT, ImgSize{res, res});
+            preds.push_back(PaperViewPred(ClipOf(vpos, mvps + v * 16), g, in,
+                                          peels, samples, vseed));
+            Variable diff = g.targets.back() - preds.back();
+            losses.push_back(diff * diff * (1.f / float(res * res)));
+        }
+        Variable loss = F::SumPixelWise(losses);
+        vpos.setRequiresGradRecursively();
+        auto [xs, gxs] = BuildBackward(loss);
+        DRESSI_CHECK(xs.size() == 1 && xs[0] == vpos,
+                     "expected pos as the only gradient leaf");
+        CpuEvaluator ev;
+        ev.bind(g.faces_f, Tensor(VEC3, {n_faces, 1}, faces));
+        ev.bind(g.vft, Tensor(FLOAT, {n_verts, max_deg}, vft));
+        ev.bind(g.face_id, Tensor(FLOAT, {n_faces * 3, 1}, face_id.data()));
+        ev.bind(g.faces_soft, Tensor(IVEC3, {n_faces, 1}, faces_soft.data()));
+        const size_t px = size_t(res) * res;
+        for (uint32_t v = 0; v < n_views; v++)
+            ev.bind(g.targets[v], Tensor(FLOAT, {res, res}, targets + v * px));
+        ev.bind(vpos, Tensor(VEC3, {n_verts, 1}, pos));
+        ev.bind(vseed, Tensor(FLOAT, {1, 1}, &seed));
+        *loss_out = float(SumAll(ev.eval(loss)));
+        CopyOut(ev.eval(gxs[0]), grad_out);
+        if (pred_out)
+            for (uint32_t v = 0; v < n_views; v++)
+                CopyOut(ev.eval(preds[v]), pred_out + v * px);
     });
 }
 
