@@ -90,7 +90,7 @@ void launch_sweeps(const SoftDims& d, const SoftBuffers& b,
                  sm = size_t(d.rim_cells);
     {
         ProfScope ps("sweep1", s);
-        k_sweep1<Epi><<<grid, kTileThreads, 0, s>>>(a, b.bin1, b.bin2, b.state,
+        k_sweep1<Epi><<<grid, kSweep1Threads, 0, s>>>(a, b.bin1, b.bin2, b.state,
                                                     b.active, sr, sp, sm, epi);
     }
     DRESSI_CUDA(cudaGetLastError());

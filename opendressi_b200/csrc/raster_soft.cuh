@@ -570,7 +570,10 @@ struct FixedBins1 {
     int* parked;                      // [views * tiles] their global bins
 };
 constexpr int kSortMax = 256;    // keys gathered per round by k_sweep1_spill
-constexpr int kWarpSort = 128;   // longest per-warp sweep-1 list sorted
+#ifndef DRESSI_WARP_SORT
+#define DRESSI_WARP_SORT 128
+#endif
+constexpr int kWarpSort = DRESSI_WARP_SORT;  // longest per-warp list sorted
 constexpr int kWarpRecs = 16;    // records staged per warp and round
 constexpr int kSpillBlocks = 296;  // grid of k_sweep1_spill (2 per SM)
 static_assert(kSortMax >= kTileThreads, "spill gathers need blockDim keys");
@@ -844,33 +847,54 @@ __device__ __forceinline__ void stage_records(const FaceRec* recs,
     __syncwarp();
 }
 
-// Sweep 1 over the tile's bin, one 8x4-pixel block per warp and every warp
-// on its own (no block barrier): the warp keeps the list entries whose
-// block mask has its bit, sorts them front to back (up to kWarpSort) and
-// folds inside and boundary fragments; far (rim) fragments are left to the
-// rim phase. A block still holding an open pixel (depth > 0.5) inside some
-// face's soft reach stores its survivors and is queued for the rim phase;
-// the others finish here through the epilogue. A tile whose bin overflowed
-// folds the entries it holds, stores its survivors and is parked for
-// k_sweep1_spill (this kernel keeps no spill code: compiled in, it slowed
-// the common path). The bin's cursor is reset by k_rim_bin.
+// Sweep 1 runs kSweepWarps warps per 16x16 tile, each over kSweepPx of the
+// tile's 8x4 blocks, one pixel of each per lane, so the warp's list
+// filtering, sorting and record staging serve 32 kSweepPx pixels.
+#ifndef DRESSI_SWEEP_WARPS
+#define DRESSI_SWEEP_WARPS 4
+#endif
+constexpr int kSweepWarps = DRESSI_SWEEP_WARPS;
+constexpr int kSweepPx = 8 / kSweepWarps;
+constexpr int kSweep1Threads = 32 * kSweepWarps;
+
+// Pixel j of this lane in sweep-1 warp W: block w = kSweepPx W + j of the
+// tile, numbered as tile_xy's warps (w & 1: x half, w >> 1: row of blocks).
+__device__ __forceinline__ void sweep1_xy(int tile, int tiles_x, int wb,
+                                          int lane, int* x, int* y) {
+    *x = (tile % tiles_x) * kTile + (wb & 1) * 8 + (lane & 7);
+    *y = (tile / tiles_x) * kTile + (wb >> 1) * 4 + (lane >> 3);
+}
+
+// Sweep 1 over the tile's bin, every warp on its own (no block barrier):
+// the warp keeps the list entries whose block mask meets its four blocks,
+// sorts them front to back (up to kWarpSort) and folds inside and boundary
+// fragments into each lane's four survivors; far (rim) fragments are left
+// to the rim phase. A block still holding an open pixel (depth > 0.5)
+// inside some face's soft reach stores its survivors and is queued for the
+// rim phase; the others finish here through the epilogue. A tile whose bin
+// overflowed folds the entries it holds, stores its survivors and is parked
+// for k_sweep1_spill (this kernel keeps no spill code: compiled in, it
+// slowed the common path). The bin's cursor is reset by k_rim_bin.
 template <class Epi>
 static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
                                    const FixedBins& b2, int tile, int2* state,
                                    uint8_t* active, Epi& epi) {
-    __shared__ FaceRec sh_all[8][kWarpRecs];
-    __shared__ unsigned long long keys_all[8][kWarpSort];
-    int x, y;
-    tile_xy(tile, a.tiles_x, &x, &y);
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    FaceRec* sh = sh_all[w];
-    unsigned long long* keys = keys_all[w];
-    const bool in = x < a.W && y < a.H;
-    const float px = float(x) + 0.5f, py = float(y) + 0.5f;
-    const size_t pix = size_t(y) * a.W + x;
+    __shared__ FaceRec sh_all[kSweepWarps][kWarpRecs];
+    __shared__ unsigned long long keys_all[kSweepWarps][kWarpSort];
+    const int wq = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    FaceRec* sh = sh_all[wq];
+    unsigned long long* keys = keys_all[wq];
     const bool peel = a.prev != nullptr;
-    const float prev = (in && peel) ? a.prev[pix] : 0.f;
     const bool fast_ok = a.radius < kMaxFastRadius;
+    int xs[kSweepPx], ys[kSweepPx];
+    bool ins[kSweepPx];
+    float prevs[kSweepPx];
+#pragma unroll
+    for (int j = 0; j < kSweepPx; j++) {
+        sweep1_xy(tile, a.tiles_x, kSweepPx * wq + j, lane, &xs[j], &ys[j]);
+        ins[j] = xs[j] < a.W && ys[j] < a.H;
+        prevs[j] = (ins[j] && peel) ? a.prev[size_t(ys[j]) * a.W + xs[j]] : 0.f;
+    }
     const size_t bin = size_t(a.v) * a.n_tiles + tile;
     const int nent = b1.cursor[bin];
     // overflow: the own list's entries are folded here, the tile is then
@@ -884,12 +908,13 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
     const int end = over ? b1.cap : nent;
     const unsigned long long* list = b1.list + bin * b1.cap;
     const unsigned lt = (1u << lane) - 1u;
+    const uint32_t wmask = ((1u << kSweepPx) - 1u) << (kSweepPx * wq);
 
     // this warp's entries, in list order (first kWarpSort of them)
     int cnt = 0;
     for (int base = 0; base < end; base += 32) {
         const unsigned long long k = base + lane < end ? list[base + lane] : 0ull;
-        const bool mine = (uint32_t(k) >> w) & 1u;
+        const bool mine = (uint32_t(k) & wmask) != 0u;
         const unsigned bal = __ballot_sync(0xffffffffu, mine);
         const int slot = cnt + __popc(bal & lt);
         if (mine && slot < kWarpSort) keys[slot] = k;
@@ -908,13 +933,24 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
         warp_sort_smem(keys, cnt);
     }
 
-    Survivor s{1.f, -1, false};
-    bool done = !in;  // sorted lists: every later face is behind the survivor
+    Survivor s[kSweepPx];
+    bool done[kSweepPx];
+    auto all_done = [&]() {
+        bool d = true;
+#pragma unroll
+        for (int j = 0; j < kSweepPx; j++) d = d && done[j];
+        return d;
+    };
+#pragma unroll
+    for (int j = 0; j < kSweepPx; j++) {
+        s[j] = Survivor{1.f, -1, false};
+        done[j] = !ins[j];  // sorted lists: every later face is behind
+    }
     // unsorted lists (over kWarpSort entries, or an overflowed tile) are
     // walked in list order, re-gathered kWarpRecs at a time
     int lpos = 0;
     for (int base = 0; base < cnt; base += kWarpRecs) {
-        if (__all_sync(0xffffffffu, done)) break;
+        if (__all_sync(0xffffffffu, all_done())) break;
         int n;
         const unsigned long long* kb;
         if (sorted) {
@@ -926,7 +962,7 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
             while (n < kWarpRecs && lpos < end) {
                 const int i = lpos + lane;
                 const unsigned long long k = i < end ? list[i] : 0ull;
-                const bool mine = (uint32_t(k) >> w) & 1u;
+                const bool mine = (uint32_t(k) & wmask) != 0u;
                 const unsigned bal = __ballot_sync(0xffffffffu, mine);
                 const int slot = n + __popc(bal & lt);
                 const int take = imin_(__popc(bal), kWarpRecs - n);
@@ -947,48 +983,63 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
         }
         stage_records(a.recs, kb, n, sh);
         for (int i = 0; i < n; i++) {
-            if (done) continue;
+            if (all_done()) continue;
             const unsigned long long key = kb[i];
             const int ent = int(uint32_t(key));
-            if (sorted && s.depth < __uint_as_float(uint32_t(key >> 32))) {
-                done = true;  // this face and all later ones lose
-                continue;
-            }
+            const float bound = __uint_as_float(uint32_t(key >> 32));
             const FaceRec& r = sh[i];
-            if (x < r.rx0 || x > r.rx1 || y < r.ry0 || y > r.ry1) continue;
-            if (!(r.flags & kFaceValid)) continue;
             const int f = ent >> 8;
-            int c = classify(px, py, r);
-            if (c == kFar && !fast_ok) c = kBoundary;
-            if (c == kInside) {
-                if (!(r.flags & kFaceSoftInside) && !soft_covers(px, py, r))
+#pragma unroll
+            for (int j = 0; j < kSweepPx; j++) {
+                if (done[j]) continue;
+                if (sorted && s[j].depth < bound) {
+                    done[j] = true;  // this face and all later ones lose
                     continue;
-                const float depth =
-                        0.5f * std_min(std_max(hard_depth(px, py, r), 0.f), 1.f);
-                if (peel && depth <= prev + 1e-4f) continue;
-                fold(s, depth, f, true);
-            } else if (c == kBoundary) {
-                if (!soft_covers(px, py, r)) continue;
-                eval_full(s, px, py, r, f, a.radius, peel, prev);
+                }
+                if (!((ent >> (kSweepPx * wq + j)) & 1)) continue;
+                const int x = xs[j], y = ys[j];
+                if (x < r.rx0 || x > r.rx1 || y < r.ry0 || y > r.ry1) continue;
+                if (!(r.flags & kFaceValid)) continue;
+                const float px = float(x) + 0.5f, py = float(y) + 0.5f;
+                int c = classify(px, py, r);
+                if (c == kFar && !fast_ok) c = kBoundary;
+                if (c == kInside) {
+                    if (!(r.flags & kFaceSoftInside) && !soft_covers(px, py, r))
+                        continue;
+                    const float depth = 0.5f * std_min(
+                            std_max(hard_depth(px, py, r), 0.f), 1.f);
+                    if (peel && depth <= prevs[j] + 1e-4f) continue;
+                    fold(s[j], depth, f, true);
+                } else if (c == kBoundary) {
+                    if (!soft_covers(px, py, r)) continue;
+                    eval_full(s[j], px, py, r, f, a.radius, peel, prevs[j]);
+                }
             }
         }
         __syncwarp();  // sh / keys reuse by the next round
         if (!sorted && lpos >= end) break;
     }
-    const int cell = (y / kRimCell) * a.rim_cells_x + (x / kRimCell);
-    // a parked tile reports every block open, so its survivors are stored
-    const bool open = __ballot_sync(0xffffffffu, (in && s.depth > 0.5f &&
-                                                  a.rim[cell] != 0) ||
-                                                         over) != 0u;
-    if (lane == 0) active[bin * 8 + w] = open ? 1 : 0;
-    if (open) {
-        // open block (or a parked tile): survivors stored; an open block of
-        // an unparked tile is queued for the rim phase
-        if (in) state[size_t(a.v) * a.W * a.H + pix] = pack(s);
-        if (!over && lane == 0)
-            b2.open[atomicAdd(b2.open_n, 1)] = int(bin) * 8 + w;
-    } else {
-        epi(a, x, y, in, s);
+#pragma unroll
+    for (int j = 0; j < kSweepPx; j++) {
+        const int wb = kSweepPx * wq + j;
+        const int x = xs[j], y = ys[j];
+        const int cell = (y / kRimCell) * a.rim_cells_x + (x / kRimCell);
+        // a parked tile reports every block open, so its survivors are stored
+        const bool open =
+                __ballot_sync(0xffffffffu, (ins[j] && s[j].depth > 0.5f &&
+                                            a.rim[cell] != 0) ||
+                                                   over) != 0u;
+        if (lane == 0) active[bin * 8 + wb] = open ? 1 : 0;
+        if (open) {
+            // open block (or a parked tile): survivors stored; an open block
+            // of an unparked tile is queued for the rim phase
+            if (ins[j])
+                state[size_t(a.v) * a.W * a.H + size_t(y) * a.W + x] = pack(s[j]);
+            if (!over && lane == 0)
+                b2.open[atomicAdd(b2.open_n, 1)] = int(bin) * 8 + wb;
+        } else {
+            epi(a, x, y, ins[j], s[j]);
+        }
     }
 }
 
@@ -1302,7 +1353,7 @@ static __device__ __forceinline__ void rim_block(const SweepArgs& a, FixedBins b
 }
 
 template <class Epi>
-__global__ void __launch_bounds__(kTileThreads)
+__global__ void __launch_bounds__(kSweep1Threads)
         k_sweep1(SweepArgs a0, FixedBins1 b1, FixedBins b2, int2* state,
                  uint8_t* active, size_t view_stride_recs,
                  size_t view_stride_px, size_t view_stride_rim, Epi epi) {
