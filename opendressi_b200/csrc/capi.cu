@@ -1389,7 +1389,7 @@ int dressi_texture_plan_create(const dressi_texture_desc* desc,
         auto carve = [&](Arena& a) {
             TexBuffers& b = pl->tb;
             b.pyr = a.take<float>(nmip);
-            b.gpyr = a.take<float>(nmip);
+            b.gpyr = a.take<float4>(nmip / 3);
             b.grad = a.take<float>(T0);
             b.adam_m = a.take<float>(T0);
             b.adam_v = a.take<float>(T0);
@@ -1439,6 +1439,8 @@ int dressi_texture_plan_create(const dressi_texture_desc* desc,
         DRESSI_CUDA(cudaMemcpy(pl->tb.clip, clip.data(),
                                clip.size() * sizeof(float),
                                cudaMemcpyHostToDevice));
+        tex_static_setup(pl->tp, pl->tb, nullptr);
+        DRESSI_CUDA(cudaDeviceSynchronize());
         pl->set_slot(DRESSI_SLOT_PARAM, pl->tb.pyr, T0 * 4);
         pl->set_slot(DRESSI_SLOT_ADAM_M, pl->tb.adam_m, T0 * 4);
         pl->set_slot(DRESSI_SLOT_ADAM_V, pl->tb.adam_v, T0 * 4);

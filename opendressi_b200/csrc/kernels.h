@@ -394,7 +394,8 @@ struct TexParams {
 };
 struct TexBuffers {
     float* pyr;       // mip pyramid, level 0 = the optimised texture
-    float* gpyr;      // its gradient (levels > 0 zeroed by the mip build)
+    float4* gpyr;     // its gradient, one (r, g, b, unused) per texel
+                      // (levels > 0 zeroed by the mip build)
     float* grad;      // d loss / d level 0 [w][w][3]
     float* adam_m;    // [w][w][3]
     float* adam_v;
@@ -413,6 +414,10 @@ struct TexBuffers {
 size_t tex_mip_floats(int w, int levels);
 size_t tex_workspace_bytes(const TexParams& p);
 // Forward + loss + d loss / d level 0 into grad (advances the Adam counter).
+// The G-buffer (uv, mask) of every view: the geometry and cameras are fixed,
+// so it is rasterised once at plan creation.
+void tex_static_setup(const TexParams& p, const TexBuffers& b,
+                      cudaStream_t s);
 void tex_forward_backward(const TexParams& p, const TexBuffers& b,
                           float* pred_out, cudaStream_t s);
 // Adam on level 0 from grad (and the loss of the iteration).

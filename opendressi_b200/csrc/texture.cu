@@ -186,7 +186,7 @@ __host__ __device__ __forceinline__ size_t mip_off(int w, int level) {
 
 // Level l+1 from level l (2x2 box, row-major order); zeroes the matching
 // gradient entries for this iteration.
-__global__ void k_mip_level(float* pyr, float* gpyr, int w, int level) {
+__global__ void k_mip_level(float* pyr, float4* gpyr, int w, int level) {
     const int s = w >> level, t = s >> 1;
     const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= size_t(t) * t * 3) return;
@@ -199,7 +199,75 @@ __global__ void k_mip_level(float* pyr, float* gpyr, int w, int level) {
     const float d = src[(size_t(2 * y + 1) * s + 2 * x + 1) * 3 + c];
     const size_t o = mip_off(w, level + 1) + i;
     pyr[o] = 0.25f * (((a + b) + cc) + d);
-    if (gpyr) gpyr[o] = 0.f;
+    if (gpyr && c == 0) gpyr[o / 3] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// Levels 1..nlev (nlev <= 5) of one 32x32 level-0 tile per block, the
+// intermediate levels kept in shared memory; every value is k_mip_level's
+// 0.25 (((a + b) + c) + d) of the same four inputs.
+constexpr int kMipTile = 32;
+__global__ void __launch_bounds__(256)
+        k_mip_tiles(float* pyr, float4* gpyr, int w, int nlev) {
+    __shared__ float buf[2][(kMipTile / 2) * (kMipTile / 2) * 3];
+    const int tiles = w / kMipTile;
+    const int tx = blockIdx.x % tiles, ty = blockIdx.x / tiles;
+    for (int k = 1; k <= nlev; k++) {
+        const int n = kMipTile >> k;          // this level's tile side
+        const int sl = w >> k;                // this level's image side
+        float* dst = buf[k & 1];
+        const float* src = buf[(k - 1) & 1];
+        const int ps = 2 * n;                 // the source tile side
+        const size_t off = mip_off(w, k);
+        float* out = pyr + off;
+        const float* lvl0 = pyr;
+        for (int i = threadIdx.x; i < n * n * 3; i += blockDim.x) {
+            const int c = i % 3, q = i / 3, x = q % n, y = q / n;
+            float a, b, cc, d;
+            if (k == 1) {
+                const size_t r0 = size_t(ty * kMipTile + 2 * y) * w +
+                                  tx * kMipTile + 2 * x;
+                a = lvl0[r0 * 3 + c];
+                b = lvl0[(r0 + 1) * 3 + c];
+                cc = lvl0[(r0 + w) * 3 + c];
+                d = lvl0[(r0 + w + 1) * 3 + c];
+            } else {
+                const int r0 = (2 * y) * ps + 2 * x;
+                a = src[r0 * 3 + c];
+                b = src[(r0 + 1) * 3 + c];
+                cc = src[(r0 + ps) * 3 + c];
+                d = src[(r0 + ps + 1) * 3 + c];
+            }
+            const float v = 0.25f * (((a + b) + cc) + d);
+            dst[i] = v;
+            const size_t texel = size_t(ty * n + y) * sl + tx * n + x;
+            out[texel * 3 + c] = v;
+            if (gpyr && c == 0)
+                gpyr[off / 3 + texel] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        __syncthreads();
+    }
+}
+
+// Levels from + 1 .. levels - 1 by one block (level `from` at most 64x64),
+// level by level; the block's barrier orders its own global writes.
+__global__ void __launch_bounds__(1024)
+        k_mip_top(float* pyr, float4* gpyr, int w, int from, int levels) {
+    for (int l = from; l + 1 < levels; l++) {
+        const int sp = w >> l, t = sp >> 1;
+        const float* src = pyr + mip_off(w, l);
+        const size_t o0 = mip_off(w, l + 1);
+        for (int i = threadIdx.x; i < t * t * 3; i += blockDim.x) {
+            const int c = i % 3, q = i / 3, x = q % t, y = q / t;
+            const float a = src[(size_t(2 * y) * sp + 2 * x) * 3 + c];
+            const float b = src[(size_t(2 * y) * sp + 2 * x + 1) * 3 + c];
+            const float cc = src[(size_t(2 * y + 1) * sp + 2 * x) * 3 + c];
+            const float d = src[(size_t(2 * y + 1) * sp + 2 * x + 1) * 3 + c];
+            pyr[o0 + i] = 0.25f * (((a + b) + cc) + d);
+            if (gpyr && c == 0)
+                gpyr[(o0 + i) / 3] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        __syncthreads();
+    }
 }
 
 // lod from the level-0 footprint rho: e + (m - 1) for rho = m * 2^e,
@@ -243,7 +311,7 @@ __device__ __forceinline__ float pixel_rho(const float* gb, int W, int H,
 // sampling scattered into gpyr; out (nullable) gets mask * sample.
 __global__ void __launch_bounds__(256)
         k_c2_pixel(TexParams p, const float* pyr, const float* gbuf,
-                   const float* targets, float* gpyr, double* loss_slots,
+                   const float* targets, float4* gpyr, double* loss_slots,
                    float* out, int train) {
     const int v = blockIdx.y;
     const int tiles_x = (p.res + 15) / 16;
@@ -298,7 +366,7 @@ __global__ void __launch_bounds__(256)
                     const int iy = x86_i32(floorf(sy));
                     const float fx = sx - float(ix);
                     const float fy = sy - float(iy);
-                    float* gl = gpyr + mip_off(p.w_tex, level);
+                    float4* gl = gpyr + mip_off(p.w_tex, level) / 3;
 #pragma unroll
                     for (int dy = 0; dy <= 1; dy++)
 #pragma unroll
@@ -307,9 +375,10 @@ __global__ void __launch_bounds__(256)
                             const int ty = iclamp(iy + dy, 0, s - 1);
                             const float wt = (dx == 0 ? 1.f - fx : fx) *
                                              (dy == 0 ? 1.f - fy : fy);
-                            float* q = gl + (size_t(ty) * s + tx) * 3;
-#pragma unroll
-                            for (int c = 0; c < 3; c++) atomicAdd(q + c, g[c] * lw * wt);
+                            // one vector atomic per tap (rgb + unused)
+                            atomicAdd(gl + size_t(ty) * s + tx,
+                                      make_float4(g[0] * lw * wt, g[1] * lw * wt,
+                                                  g[2] * lw * wt, 0.f));
                         }
                 }
             }
@@ -326,12 +395,16 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+__device__ __forceinline__ float comp3(const float4& q, int c) {
+    return c == 0 ? q.x : (c == 1 ? q.y : q.z);
+}
+
 // Folds the pyramid gradient down to level 0 (the transpose of the box
 // mips: each level adds 0.25 of its parent, from the top level down, which
-// per level-0 texel is the chain acc_l = g_l + 0.25 acc_{l+1}) into grad;
-// zeroes level 0 of gpyr. Block 0 also publishes the iteration's loss and
-// advances the Adam counter.
-__global__ void k_mip_fold(TexParams p, float* gpyr, float* grad,
+// per level-0 texel and channel is the chain acc_l = g_l + 0.25 acc_{l+1})
+// into grad; zeroes level 0 of gpyr. One thread per level-0 texel. Block 0
+// also publishes the iteration's loss and advances the Adam counter.
+__global__ void k_mip_fold(TexParams p, float4* gpyr, float* grad,
                            float* scalars, double* loss_slots,
                            float* loss_hist, int hist_cap) {
     if (blockIdx.x == 0) {
@@ -358,26 +431,32 @@ __global__ void k_mip_fold(TexParams p, float* gpyr, float* grad,
             if (hist_cap > 0) loss_hist[it % hist_cap] = loss;
         }
     }
-    const size_t n0 = size_t(p.w_tex) * p.w_tex * 3;
+    const size_t n0 = size_t(p.w_tex) * p.w_tex;
     const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n0) return;
-    const int c = int(i % 3), px = int(i / 3);
-    const int x = px % p.w_tex, y = px / p.w_tex;
-    float g0 = gpyr[i];
+    const int x = int(i % p.w_tex), y = int(i / p.w_tex);
+    const float4 q0 = gpyr[i];
+    float g0[3] = {q0.x, q0.y, q0.z};
     if (p.levels > 1) {
         const int top = p.levels - 1;
+        // texel offsets of the levels walked down from the top
+        size_t off = mip_off(p.w_tex, top) / 3;
         const int st = p.w_tex >> top;
-        float acc = gpyr[mip_off(p.w_tex, top) +
-                         (size_t(y >> top) * st + (x >> top)) * 3 + c];
+        const float4 qt = gpyr[off + size_t(y >> top) * st + (x >> top)];
+        float acc[3] = {qt.x, qt.y, qt.z};
         for (int l = top - 1; l >= 1; l--) {
             const int sl = p.w_tex >> l;
-            acc = gpyr[mip_off(p.w_tex, l) + (size_t(y >> l) * sl + (x >> l)) * 3 + c] +
-                  0.25f * acc;
+            off -= size_t(sl) * size_t(sl);
+            const float4 q = gpyr[off + size_t(y >> l) * sl + (x >> l)];
+#pragma unroll
+            for (int c = 0; c < 3; c++) acc[c] = comp3(q, c) + 0.25f * acc[c];
         }
-        g0 = g0 + 0.25f * acc;
+#pragma unroll
+        for (int c = 0; c < 3; c++) g0[c] = g0[c] + 0.25f * acc[c];
     }
-    grad[i] = g0;
-    gpyr[i] = 0.f;
+#pragma unroll
+    for (int c = 0; c < 3; c++) grad[i * 3 + c] = g0[c];
+    gpyr[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 __global__ void k_tex_adam(TexParams p, float* param, const float* grad,
@@ -395,13 +474,27 @@ __global__ void k_tex_adam(TexParams p, float* param, const float* grad,
     v[i] = v_new;
 }
 
-void mip_build(const TexParams& p, float* pyr, float* gpyr, cudaStream_t s) {
+void mip_build(const TexParams& p, float* pyr, float4* gpyr, cudaStream_t s) {
     ProfScope ps("mip_build", s);
-    for (int l = 0; l + 1 < p.levels; l++) {
-        const int t = (p.w_tex >> l) >> 1;
-        const size_t n = size_t(t) * t * 3;
-        k_mip_level<<<unsigned((n + 255) / 256), 256, 0, s>>>(pyr, gpyr,
-                                                              p.w_tex, l);
+    const int w = p.w_tex;
+    int l = 0;
+    if (p.levels > 1 && w % kMipTile == 0) {
+        // levels 1..5 tile by tile
+        const int nlev = std::min(5, p.levels - 1);
+        const int tiles = w / kMipTile;
+        k_mip_tiles<<<unsigned(tiles * tiles), 256, 0, s>>>(pyr, gpyr, w, nlev);
+        l = nlev;
+    }
+    if (l + 1 < p.levels && (w >> l) <= 64) {
+        // the small top levels in one block
+        k_mip_top<<<1, 1024, 0, s>>>(pyr, gpyr, w, l, p.levels);
+    } else {
+        for (; l + 1 < p.levels; l++) {
+            const int t = (w >> l) >> 1;
+            const size_t n = size_t(t) * t * 3;
+            k_mip_level<<<unsigned((n + 255) / 256), 256, 0, s>>>(pyr, gpyr,
+                                                                  w, l);
+        }
     }
     check_launch();
 }
@@ -435,10 +528,14 @@ size_t tex_workspace_bytes(const TexParams& p) {
     return hard_workspace_bytes(hd);
 }
 
+void tex_static_setup(const TexParams& p, const TexBuffers& b,
+                      cudaStream_t s) {
+    gbuffer(p, b, s);
+}
+
 void tex_forward_backward(const TexParams& p, const TexBuffers& b,
                           float* pred_out, cudaStream_t s) {
     mip_build(p, b.pyr, b.gpyr, s);
-    gbuffer(p, b, s);
     {
         ProfScope ps("c2_pixel", s);
         k_c2_pixel<<<pixel_grid(p), 256, 0, s>>>(p, b.pyr, b.gbuf, b.targets,
@@ -448,7 +545,7 @@ void tex_forward_backward(const TexParams& p, const TexBuffers& b,
     check_launch();
     {
         ProfScope ps("mip_fold", s);
-        const size_t n0 = size_t(p.w_tex) * p.w_tex * 3;
+        const size_t n0 = size_t(p.w_tex) * p.w_tex;
         k_mip_fold<<<unsigned((n0 + 255) / 256), 256, 0, s>>>(
                 p, b.gpyr, b.grad, b.scalars, b.loss_slots, b.loss_hist,
                 b.hist_cap);
@@ -473,7 +570,6 @@ void tex_iteration(const TexParams& p, const TexBuffers& b, cudaStream_t s) {
 void tex_predict(const TexParams& p, const TexBuffers& b, float* out,
                  cudaStream_t s) {
     mip_build(p, b.pyr, nullptr, s);
-    gbuffer(p, b, s);
     k_c2_pixel<<<pixel_grid(p), 256, 0, s>>>(p, b.pyr, b.gbuf, nullptr, nullptr,
                                              nullptr, out, 0);
     check_launch();
@@ -484,13 +580,12 @@ void tex_render_targets(const TexParams& p, const TexBuffers& b,
     const size_t nmip = tex_mip_floats(p.w_tex, p.levels);
     void* tmp = nullptr;
     DRESSI_CUDA(cudaMallocAsync(&tmp, nmip * sizeof(float), s));
-    float* gpyr = static_cast<float*>(tmp);
-    DRESSI_CUDA(cudaMemcpyAsync(gpyr, gt_tex,
+    float* gt_pyr = static_cast<float*>(tmp);
+    DRESSI_CUDA(cudaMemcpyAsync(gt_pyr, gt_tex,
                                 size_t(p.w_tex) * p.w_tex * 3 * sizeof(float),
                                 cudaMemcpyDeviceToDevice, s));
-    mip_build(p, gpyr, nullptr, s);
-    gbuffer(p, b, s);
-    k_c2_pixel<<<pixel_grid(p), 256, 0, s>>>(p, gpyr, b.gbuf, nullptr, nullptr,
+    mip_build(p, gt_pyr, nullptr, s);
+    k_c2_pixel<<<pixel_grid(p), 256, 0, s>>>(p, gt_pyr, b.gbuf, nullptr, nullptr,
                                              nullptr, b.targets, 0);
     check_launch();
     DRESSI_CUDA(cudaFreeAsync(tmp, s));
