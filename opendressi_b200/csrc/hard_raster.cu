@@ -2,9 +2,9 @@
 // bit-exact with the reference's RasterizeCore (cpu_raster.cpp:31-110).
 //
 // The reference keeps, per pixel, the fragment with the smallest NDC z and
-// the latest face on ties (`if (z > zb) continue;`). Each thread owns one
-// pixel and folds every fragment of its tile's face list into that key, so
-// list order does not matter. The survivor's barycentrics are recomputed
+// the latest face on ties (`if (z > zb) continue;`). Each thread owns two
+// pixels and folds every fragment of its tile's face list into their keys,
+// so list order does not matter. The survivor's barycentrics are recomputed
 // once at the end for the attribute interpolation, with the reference's
 // expressions (shade lambda, cpu_raster.cpp:205-223).
 #include <algorithm>
@@ -158,110 +158,25 @@ __device__ __forceinline__ void hard_bary(const HardRec& r, float px, float py,
     *l2 = 1.f - *l0 - *l1;
 }
 
-constexpr int kHardChunk = 128;
-static_assert(kHardChunk <= kSortMax, "a chunk must fit the sort buffer");
-
 // Order-preserving key of a float (ascending floats -> ascending keys).
 __device__ __forceinline__ unsigned long long zlb_key(float z) {
     const uint32_t u = __float_as_uint(z);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// attr == nullptr: writes float(face)+1 / 0 into out[v][H][W].
-// Otherwise writes the perspective-correct attribute (n_comp channels).
-__global__ void __launch_bounds__(kTileThreads)
-        k_hard_sweep(HardDims d, HardBuffers b, const float* attr, float* out,
-                     float* depth_out, float* id_out) {
-    __shared__ HardRec sh[kHardChunk];
-    __shared__ int fid_sh[kHardChunk];
-    __shared__ unsigned long long order[kSortMax];  // (zlb key, record index)
-    __shared__ unsigned char wlist[8][kHardChunk];  // per-warp sorted faces
-    const int v = blockIdx.y, tile = blockIdx.x;
-    const int tx = tile % d.tiles_x, ty = tile / d.tiles_x;
-    int x, y;
-    tile_xy(tile, d.tiles_x, &x, &y);  // 8 warps of 8x4 pixels
-    const int w = threadIdx.x >> 5;
-    const int wx0 = tx * kTile + (w & 1) * 8, wy0 = ty * kTile + (w >> 1) * 4;
-    const bool in = x < d.W && y < d.H;
+// The float of a zlb_key.
+__device__ __forceinline__ float zlb_of_key(unsigned long long k) {
+    const uint32_t u = uint32_t(k >> 32);
+    return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
+}
+
+// The outputs of one pixel from its survivor (best_f < 0: background).
+__device__ __forceinline__ void hard_out(const HardDims& d, const float* attr,
+                                         float* out, float* depth_out,
+                                         float* id_out, const HardRec* recs,
+                                         int v, int x, int y, bool in,
+                                         float best_z, int best_f) {
     const float px = float(x) + 0.5f, py = float(y) + 0.5f;
-    const HardRec* recs = b.recs + size_t(v) * d.n_faces;
-    const bool identity = b.bin.overflow[v] != 0;
-    const int tl = v * d.n_tiles + tile;
-    const int beg = identity ? 0 : b.bin.offset[tl];
-    const int end = identity ? d.n_faces : b.bin.cursor[tl];
-    const int* list = b.bin.list + size_t(v) * b.bin.cap;
-    float best_z = 1.f;
-    int best_f = -1;
-    for (int base = beg; base < end; base += kHardChunk) {
-        const int n = imin_(kHardChunk, end - base);
-        __syncthreads();
-        const float4* src = reinterpret_cast<const float4*>(recs);
-        float4* dst = reinterpret_cast<float4*>(sh);
-        for (int i = threadIdx.x; i < n * kHardVec4; i += blockDim.x) {
-            const int j = i / kHardVec4, q = i % kHardVec4;
-            const int f = identity ? base + j : list[base + j];
-            dst[i] = src[size_t(f) * kHardVec4 + q];
-            if (q == 0) fid_sh[j] = f;
-        }
-        __syncthreads();
-        // front to back by the depth lower bound
-        if (n <= 32) {
-            if (threadIdx.x < 32) {
-                const int lane = threadIdx.x;
-                unsigned long long k =
-                        lane < n ? (zlb_key(sh[lane].zlb) << 32) | unsigned(lane)
-                                 : ~0ull;
-                k = warp_sort_asc(k);
-                order[lane] = k;
-            }
-        } else {
-            for (int j = threadIdx.x; j < n; j += blockDim.x)
-                order[j] = (zlb_key(sh[j].zlb) << 32) | unsigned(j);
-            block_sort_asc(order, n);
-        }
-        __syncthreads();
-        // this warp's list: the valid faces whose pixel range meets its 8x4
-        // block, kept in front-to-back order
-        const int lane = threadIdx.x & 31;
-        int cnt = 0;
-        for (int o0 = 0; o0 < n; o0 += 32) {
-            const int o = o0 + lane;
-            int j = 0;
-            bool hit = false;
-            if (o < n) {
-                j = int(uint32_t(order[o]));
-                const HardRec& r = sh[j];
-                hit = (r.flags & kFaceValid) && !(r.bx1 < wx0 || r.bx0 > wx0 + 7 ||
-                                                  r.by1 < wy0 || r.by0 > wy0 + 3);
-            }
-            const unsigned m = __ballot_sync(0xffffffffu, hit);
-            if (hit) wlist[w][cnt + __popc(m & ((1u << lane) - 1u))] = (unsigned char)j;
-            cnt += __popc(m);
-        }
-        __syncwarp();
-        for (int t = 0; t < cnt; t++) {
-            const int i = wlist[w][t];
-            const HardRec& r = sh[i];
-            // the warp leaves the chunk once every pixel holds a survivor in
-            // front of this face (and so of all later ones)
-            if (__all_sync(0xffffffffu, !in || (best_f >= 0 && best_z < r.zlb)))
-                break;
-            if (!in) continue;
-            if (x < r.bx0 || x > r.bx1 || y < r.by0 || y > r.by1) continue;
-            // every fragment of this face lies behind the survivor (no tie)
-            if (best_f >= 0 && r.zlb > best_z) continue;
-            float l0, l1, l2;
-            hard_bary(r, px, py, &l0, &l1, &l2);
-            if (l0 < 0.f || l1 < 0.f || l2 < 0.f) continue;
-            const float z = l0 * r.z0 + l1 * r.z1 + l2 * r.z2;
-            if (z < 0.f || z > 1.f) continue;
-            const int f = fid_sh[i];
-            if (beats(z, f, best_z, best_f)) {
-                best_z = z;
-                best_f = f;
-            }
-        }
-    }
     if (!in) return;
     const size_t pix = size_t(v) * d.W * d.H + size_t(y) * d.W + x;
     if (depth_out) depth_out[pix] = best_f >= 0 ? best_z : 1.f;
@@ -318,6 +233,147 @@ __global__ void __launch_bounds__(kTileThreads)
     }
 }
 
+// The sweep runs kHardWarps warps per 16x16 tile, each over a 16x4 region
+// (two of the tile's 8x4 blocks, one pixel of each per lane) and on its
+// own: it gathers the tile-list faces whose pixel range meets its region
+// (up to kHardWin at a time), sorts them front to back by their depth lower
+// bound, stages their records kHardRecs at a time in its shared slots and
+// folds each lane's two pixels. With a single sorted window a pixel stops
+// at the first face whose bound lies behind its survivor.
+constexpr int kHardWarps = 4;
+constexpr int kHardThreads = 32 * kHardWarps;
+constexpr int kHardWin = 128;
+constexpr int kHardRecs = 16;
+
+__global__ void __launch_bounds__(kHardThreads)
+        k_hard_sweep(HardDims d, HardBuffers b, const float* attr, float* out,
+                     float* depth_out, float* id_out) {
+    __shared__ HardRec sh_all[kHardWarps][kHardRecs];
+    __shared__ unsigned long long keys_all[kHardWarps][kHardWin];
+    const int v = blockIdx.y, tile = blockIdx.x;
+    const int tx = tile % d.tiles_x, ty = tile / d.tiles_x;
+    const int wq = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    HardRec* sh = sh_all[wq];
+    unsigned long long* keys = keys_all[wq];
+    // the warp's region: columns tx*16 .. +15, rows ty*16 + 4 wq .. +3;
+    // pixel j of the lane: x = tx*16 + 8 j + (lane & 7), y = row + (lane >> 3)
+    const int rx0 = tx * kTile, ry0 = ty * kTile + 4 * wq;
+    int xs[2], ys[2];
+    bool ins[2];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        xs[j] = rx0 + 8 * j + (lane & 7);
+        ys[j] = ry0 + (lane >> 3);
+        ins[j] = xs[j] < d.W && ys[j] < d.H;
+    }
+    const HardRec* recs = b.recs + size_t(v) * d.n_faces;
+    const bool identity = b.bin.overflow[v] != 0;
+    const int tl = v * d.n_tiles + tile;
+    const int beg = identity ? 0 : b.bin.offset[tl];
+    const int end = identity ? d.n_faces : b.bin.cursor[tl];
+    const int* list = b.bin.list + size_t(v) * b.bin.cap;
+    const unsigned lt = (1u << lane) - 1u;
+    float best_z[2] = {1.f, 1.f};
+    int best_f[2] = {-1, -1};
+    int pos = beg;
+    bool first = true;
+    while (pos < end) {
+        // next window: up to kHardWin entries meeting the region, in list
+        // order from pos
+        int n = 0;
+        while (n < kHardWin && pos < end) {
+            const int i = pos + lane;
+            bool hit = false;
+            unsigned long long k = 0ull;
+            if (i < end) {
+                const int f = identity ? i : list[i];
+                const int4 bb = reinterpret_cast<const int4*>(recs + f)[4];
+                hit = !(bb.y < rx0 || bb.x > rx0 + 15 || bb.w < ry0 ||
+                        bb.z > ry0 + 3);
+                if (hit)
+                    k = (zlb_key(recs[f].zlb) << 32) | uint32_t(f);
+            }
+            const unsigned bal = __ballot_sync(0xffffffffu, hit);
+            const int take = imin_(__popc(bal), kHardWin - n);
+            const int slot = n + __popc(bal & lt);
+            if (hit && slot < kHardWin) keys[slot] = k;
+            if (take < __popc(bal)) {
+                // resume at the first entry left over
+                unsigned rest = bal;
+                for (int t = 0; t < take; t++) rest &= rest - 1u;
+                pos += __ffs(rest) - 1;
+            } else {
+                pos = imin_(pos + 32, end);
+            }
+            n += take;
+        }
+        __syncwarp();
+        // a single window covering the whole list allows the early stop
+        const bool sorted = first && pos >= end;
+        first = false;
+        if (n <= 32) {
+            unsigned long long k = lane < n ? keys[lane] : ~0ull;
+            k = warp_sort_asc(k);
+            __syncwarp();
+            if (lane < n) keys[lane] = k;
+            __syncwarp();
+        } else {
+            warp_sort_smem(keys, n);
+        }
+        for (int base = 0; base < n; base += kHardRecs) {
+            const int cn = imin_(kHardRecs, n - base);
+            // the warp leaves once every pixel holds a survivor in front of
+            // the next face (and so of all later ones)
+            if (sorted) {
+                const float zn = zlb_of_key(keys[base]);
+                bool stop = true;
+#pragma unroll
+                for (int j = 0; j < 2; j++)
+                    stop = stop && (!ins[j] || (best_f[j] >= 0 && best_z[j] < zn));
+                if (__all_sync(0xffffffffu, stop)) break;
+            }
+            {
+                const float4* src = reinterpret_cast<const float4*>(recs);
+                float4* dst = reinterpret_cast<float4*>(sh);
+                for (int i = lane; i < cn * kHardVec4; i += 32) {
+                    const int jj = i / kHardVec4, q = i - jj * kHardVec4;
+                    const int f = int(uint32_t(keys[base + jj]));
+                    dst[i] = src[size_t(f) * kHardVec4 + q];
+                }
+                __syncwarp();
+            }
+            for (int t = 0; t < cn; t++) {
+                const HardRec& r = sh[t];
+                const int f = int(uint32_t(keys[base + t]));
+                if (!(r.flags & kFaceValid)) continue;
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    if (!ins[j]) continue;
+                    const int x = xs[j], y = ys[j];
+                    if (x < r.bx0 || x > r.bx1 || y < r.by0 || y > r.by1) continue;
+                    // every fragment of this face lies behind the survivor
+                    if (best_f[j] >= 0 && r.zlb > best_z[j]) continue;
+                    float l0, l1, l2;
+                    hard_bary(r, float(x) + 0.5f, float(y) + 0.5f, &l0, &l1, &l2);
+                    if (l0 < 0.f || l1 < 0.f || l2 < 0.f) continue;
+                    const float z = l0 * r.z0 + l1 * r.z1 + l2 * r.z2;
+                    if (z < 0.f || z > 1.f) continue;
+                    if (beats(z, f, best_z[j], best_f[j])) {
+                        best_z[j] = z;
+                        best_f[j] = f;
+                    }
+                }
+            }
+            __syncwarp();  // sh reuse by the next chunk
+        }
+        __syncwarp();  // keys reuse by the next window
+    }
+#pragma unroll
+    for (int j = 0; j < 2; j++)
+        hard_out(d, attr, out, depth_out, id_out, recs, v, xs[j], ys[j],
+                 ins[j], best_z[j], best_f[j]);
+}
+
 static void check_launch() { DRESSI_CUDA(cudaGetLastError()); }
 
 void hard_raster_op(const HardDims& d0, void* workspace, const float* clip,
@@ -347,7 +403,7 @@ void hard_raster_op(const HardDims& d0, void* workspace, const float* clip,
     }
     {
         ProfScope ps("hard_sweep", s);
-        k_hard_sweep<<<dim3(d.n_tiles, d.views), kTileThreads, 0, s>>>(
+        k_hard_sweep<<<dim3(d.n_tiles, d.views), kHardThreads, 0, s>>>(
                 d, b, attr, out, depth_out, id_out);
     }
     check_launch();
