@@ -38,6 +38,8 @@ sys.path.insert(0, ROOT)
 METRIC = "fwd+bwd+Adam iterations/sec"
 
 DATA = {
+    "c3p": "synthetic (seeded icosphere + SH-displaced target, seeded "
+           "cameras; no dataset)",
     "c2": "synthetic (seeded icosphere with spherical uv, seeded value-noise "
           "target texture, seeded cameras; no dataset)",
     "c3": "synthetic (seeded icosphere + SH-displaced target, seeded "
@@ -47,10 +49,11 @@ DATA = {
     "c5": "synthetic (seeded value-noise albedo / metallic-roughness maps, "
           "seeded lobe-and-sky environment, seeded cameras; no dataset)",
 }
-GRAD_NAME = {"c2": "texture", "c3": "position", "c4": "position",
+GRAD_NAME = {"c2": "texture", "c3": "position", "c3p": "position",
+             "c4": "position",
              "c5": "[albedo | metallic-roughness | environment]"}
 # bytes per view-pixel kept resident between the passes of an iteration
-PX_STATE = {"c2": 24, "c3": 16, "c4": 16, "c5": 92}
+PX_STATE = {"c2": 24, "c3": 16, "c3p": 16 + 64, "c4": 16, "c5": 92}
 
 
 def parse():
@@ -59,8 +62,12 @@ def parse():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c2", "c3", "c4", "c5"],
-                    default="c3")
+    ap.add_argument("--config", choices=["c2", "c3", "c3p", "c4", "c5"],
+                    default="c3",
+                    help="c3p: C3 on the paper's HardSoftRas path (FaceFetch "
+                         "backward, --peels layers)")
+    ap.add_argument("--peels", type=int, default=1,
+                    help="c3p: depth-peeling layers (1..4)")
     ap.add_argument("--res", type=int, default=None,
                     help="default: 512 (c2), 1024 (c3, c4, c5)")
     ap.add_argument("--views", type=int, default=None,
@@ -79,7 +86,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     if args.views is None:
-        args.views = {"c2": 8, "c3": 16, "c4": 64, "c5": 32}[args.config]
+        args.views = {"c2": 8, "c3": 16, "c3p": 16, "c4": 64,
+                      "c5": 32}[args.config]
     if args.res is None:
         args.res = 512 if args.config == "c2" else 1024
     if args.config == "c2" and args.level == 5:
@@ -87,7 +95,8 @@ def parse():
     if args.config == "c5" and args.level == 5:
         args.level = 6  # C5's mesh is icosphere-6
     # the silhouette example's per-technique defaults (run.cpp:127-132)
-    lap0, nrm0 = {"c3": (0.15, 0.4), "c4": (0.5, 0.5)}.get(args.config,
+    lap0, nrm0 = {"c3": (0.15, 0.4), "c3p": (0.15, 0.4),
+                  "c4": (0.5, 0.5)}.get(args.config,
                                                           (0.0, 0.0))
     if args.laplacian is None:
         args.laplacian = lap0
@@ -101,6 +110,12 @@ def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return world, rank, local
+
+
+def _scene_radius(res: int) -> float:
+    from opendressi_b200 import scene
+
+    return scene.silhouette_radius_px(res, 1e-4)
 
 
 def workload(args):
@@ -139,6 +154,20 @@ def workload(args):
             "regularizer": {"laplacian": args.laplacian,
                             "normal": args.normal},
         }
+    if args.config == "c3p":
+        return {
+            "workload": "C3 silhouette, the paper's HardSoftRas path "
+                        "(FaceFetch / LookupFaces backward) fwd+bwd+Adam",
+            "mesh": f"icosphere-{args.level}",
+            "views": args.views,
+            "res": args.res,
+            "radius_px": _scene_radius(args.res),
+            "peels": args.peels,
+            "edge_samples": args.samples,
+            "lr": 1e-3,
+            "regularizer": {"laplacian": args.laplacian,
+                            "normal": args.normal},
+        }
     return {
         "workload": "C3 silhouette HardSoftRas fwd+bwd+Adam",
         "mesh": f"icosphere-{args.level}",
@@ -161,7 +190,7 @@ def cpu_targets(args, sc, ref, port, threads):
     """Targets of the CPU arms, computed by the CPU code itself (hard
     silhouettes for c3; the reference's anti-aliased masks for c4, views on
     a thread pool)."""
-    if args.config == "c3":
+    if args.config in ("c3", "c3p"):
         return np.stack([(port.rasterize_face_id(
             port.transform_clip(sc.target_pos, m), sc.faces_f, sc.res, sc.res)
             > 0).astype(np.float32) for m in sc.mvps])
@@ -192,6 +221,19 @@ def cpu_run(args, sc, ref, port, vft, targets, pos, n, threads):
         return port.c2_run(pos, sc.levels, sc.pos, sc.uv, sc.faces_f, sc.mvps,
                            targets, sc.res, sc.lr, n)[1]
     reg = dict(laplacian=args.laplacian, normal=args.normal)
+    if args.config == "c3p":
+        # the reference's own graph of the paper path, one view per thread,
+        # gradients summed (loss + backward; its Adam step is ~1e-4 of it)
+        from concurrent.futures import ThreadPoolExecutor
+
+        def one(v):
+            return ref.paper_sil_grad(pos, sc.faces_f, vft, sc.mvps[v:v + 1],
+                                      targets[v:v + 1], sc.res, sc.radius_px,
+                                      args.samples, args.peels, 0.0)[1]
+        for _ in range(n):
+            with ThreadPoolExecutor(threads) as ex:
+                sum(ex.map(one, range(sc.n_views)))
+        return pos
     if args.config == "c4":
         if ref is not None:
             return ref.aa_silhouette_run(pos, sc.faces_f, vft, sc.mvps,
@@ -328,8 +370,8 @@ def run_ours(args):
     from opendressi_b200 import _native as N
     from opendressi_b200 import scene
     from opendressi_b200.distributed import ShardedStep, shard_views
-    from opendressi_b200.plans import (AaSilhouettePlan, PbrPlan,
-                                       SilhouettePlan, TexturePlan)
+    from opendressi_b200.plans import (AaSilhouettePlan, PaperSilhouettePlan,
+                                       PbrPlan, SilhouettePlan, TexturePlan)
 
     world, rank, local = dist_env()
     if world != args.gpus:
@@ -355,6 +397,12 @@ def run_ours(args):
     elif args.config == "c5":
         plan = PbrPlan.from_scene(sc, views=shard, device=local,
                                   lut_size=256, lut_samples=512)
+    elif args.config == "c3p":
+        plan = PaperSilhouettePlan.from_scene(sc, views=shard, device=local,
+                                              laplacian=args.laplacian,
+                                              normal=args.normal,
+                                              peels=args.peels,
+                                              n_samples=args.samples)
     elif args.config == "c4":
         plan = AaSilhouettePlan.from_scene(sc, views=shard, device=local,
                                            n_samples=args.samples,
@@ -474,6 +522,10 @@ def run_ours(args):
     else:
         alg = iteration_bytes(nvw, args.res, sc.n_verts, sc.n_faces,
                               reg=args.laplacian != 0.0 or args.normal != 0.0)
+        if args.config == "c3p":
+            # per layer and view-pixel: the soft layer written and read
+            # (32 B) and the fetched corners' gradients written (48 B)
+            alg += 80.0 * args.peels * nvw * args.res * args.res
     peak, peak_kind = peaks()
     ms_step = ms_max / args.steps
     achieved = alg / (ms_step * 1e-3) / 1e9

@@ -405,6 +405,18 @@ typedef struct {
 int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
                                   dressi_plan* out);
 
+/* The silhouette example's own HardSoftRas technique, the paper path
+ * (examples/silhouette_optimization/run.cpp:229-396): `peels` (1..4) soft
+ * layers, each pixel's D_k = mask * sigmoid(signed distance to its face's
+ * edges * 7 / radius_px) from the corners fetched with FaceFetch of
+ * LookupFaces, pred = max(hard, 1 - prod_k (1 - D_k)); FaceFetch's backward
+ * takes n_samples hashed edge samples per face (0: the exact bbox scan),
+ * jittered by the Adam counter. Same descriptor as above (sigma unused),
+ * same slots, targets, regulariser and phases. */
+int dressi_paper_silhouette_plan_create(const dressi_silhouette_desc* desc,
+                                        uint32_t peels, uint32_t n_samples,
+                                        dressi_plan* out);
+
 /* AA silhouette optimisation (config C4; examples/silhouette_optimization/
  * run.cpp:230-238): per view v, clip = MVP_v (pos, 1); mask =
  * Rasterize(clip, ones); tri = RasterizeFaceId(clip); pred =

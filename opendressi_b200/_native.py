@@ -118,6 +118,9 @@ SIGNATURES = {
                                         _vp]),
     "dressi_silhouette_plan_create": (C.c_int, [C.POINTER(SilhouetteDesc),
                                                 C.POINTER(_vp)]),
+    "dressi_paper_silhouette_plan_create": (C.c_int, [C.POINTER(SilhouetteDesc),
+                                                      _u32, _u32,
+                                                      C.POINTER(_vp)]),
     "dressi_aa_silhouette_plan_create": (C.c_int, [C.POINTER(AaSilhouetteDesc),
                                                    C.POINTER(_vp)]),
     "dressi_rasterize_uvzw": (C.c_int, [_vp, _vp, _u32, _vp, _u32, _u32, _u32,

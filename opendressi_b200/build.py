@@ -22,7 +22,7 @@ LIB = os.path.join(HERE, "libdressi_b200.so")
 SOURCES = ["capi.cu", "soft_raster.cu", "silhouette.cu", "hard_raster.cu",
            "fit.cu", "noalloc.cu",
            "antialias.cu", "texture.cu", "interp.cu", "regularize.cu",
-           "ibl.cu", "pbr.cu", "faces.cu"]
+           "ibl.cu", "pbr.cu", "faces.cu", "paper.cu", "paper_pixel.cu"]
 HEADERS = ["common.h", "exact.cuh", "kernels.h", "raster_soft.cuh"]
 
 NVCC_FLAGS = [
@@ -34,12 +34,15 @@ NVCC_FLAGS = [
 ]
 
 
-# The C5 shading (pbr.cu) has a tolerance contract, not a bit-exact one:
-# it contracts a * b + c into FMAs and uses the fast (<= 2 ulp) division, as
+# The C5 shading (pbr.cu) and the paper path's per-pixel chain
+# (paper_pixel.cu) have a tolerance contract, not a bit-exact one:
+# they contract a * b + c into FMAs and use the fast (<= 2 ulp) division, as
 # GPU shader compilers do. Every other translation unit keeps the strict
 # flags above (the raster and IBL ops are bit-exact with the reference).
 FILE_FLAGS = {"pbr.cu": {"-fmad=false": "-fmad=true",
-                         "-prec-div=true": "-prec-div=false"}}
+                         "-prec-div=true": "-prec-div=false"},
+              "paper_pixel.cu": {"-fmad=false": "-fmad=true",
+                                 "-prec-div=true": "-prec-div=false"}}
 
 
 def flags_for(src: str) -> list[str]:

@@ -516,8 +516,11 @@ int dressi_antialias_grad(const float* gy, const float* img, uint32_t n_comp,
     });
 }
 
-int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
-                                  dressi_plan* out) {
+// The silhouette plans: RasterizeSoft's own backward (paper = 0) or the
+// paper path (paper = 1: peels layers, n_samples FaceFetch edge samples).
+static int create_silhouette(const dressi_silhouette_desc* desc, int paper,
+                             uint32_t peels, uint32_t n_samples,
+                             dressi_plan* out) {
     return guarded([&] {
         DRESSI_REQUIRE(desc && out, "null pointer");
         DRESSI_REQUIRE(desc->struct_size == sizeof(dressi_silhouette_desc),
@@ -527,8 +530,11 @@ int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
                        "silhouette plan: empty mesh, views or screen");
         DRESSI_REQUIRE(desc->res <= 32768, "silhouette plan: res > 32768");
         DRESSI_REQUIRE(desc->faces && desc->mvps, "null pointer");
-        DRESSI_REQUIRE(desc->radius_px > 0.f && desc->sigma > 0.f,
+        DRESSI_REQUIRE(desc->radius_px > 0.f && (paper || desc->sigma > 0.f),
                        "silhouette plan: radius_px and sigma must be > 0");
+        DRESSI_REQUIRE(!paper || (peels >= 1 && peels <= uint32_t(kPaperMaxPeels)),
+                       "paper silhouette plan: peels must be 1..4");
+        DRESSI_REQUIRE(n_samples <= 4096, "silhouette plan: n_samples > 4096");
         *out = nullptr;
         DeviceGuard dg(desc->device);
         auto pl = std::make_unique<dressi_plan_s>();
@@ -553,8 +559,14 @@ int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
         p.b1 = desc->beta1;
         p.b2 = desc->beta2;
         p.eps = desc->eps;
-        p.k = (2.f / float(desc->res)) * (2.f / float(desc->res)) / desc->sigma;
+        p.k = paper ? 0.f
+                    : (2.f / float(desc->res)) * (2.f / float(desc->res)) /
+                              desc->sigma;
         p.c = 1.f / float(desc->res * desc->res);
+        p.paper = paper;
+        p.peels = paper ? int(peels) : 1;
+        p.n_samples = int(n_samples);
+        p.sigma_scale = 7.f / desc->radius_px;
         reg_params(&p, desc->laplacian, desc->normal);
         RegTables rt;
         reg_tables(p, desc->faces, &rt);
@@ -563,6 +575,11 @@ int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
         const size_t R2 = size_t(desc->res) * desc->res;
         auto carve = [&](Arena& a) {
             SilBuffers& b = pl->b;
+            if (paper) {
+                b.paper_layers = a.take<float4>(size_t(peels) * NV * R2);
+                b.paper_prev = a.take<float>(NV * R2);
+                b.paper_gfetch = a.take<float4>(size_t(peels) * 3 * NV * R2);
+            }
             b.pos = a.take<float>(V * 3);
             b.adam_m = a.take<float>(V * 3);
             b.adam_v = a.take<float>(V * 3);
@@ -609,6 +626,17 @@ int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
         pl->set_slot(DRESSI_SLOT_MVP, pl->b.mvps, NV * 16 * 4);
         *out = pl.release();
     });
+}
+
+int dressi_silhouette_plan_create(const dressi_silhouette_desc* desc,
+                                  dressi_plan* out) {
+    return create_silhouette(desc, 0, 1, 0, out);
+}
+
+int dressi_paper_silhouette_plan_create(const dressi_silhouette_desc* desc,
+                                        uint32_t peels, uint32_t n_samples,
+                                        dressi_plan* out) {
+    return create_silhouette(desc, 1, peels, n_samples, out);
 }
 
 int dressi_aa_silhouette_plan_create(const dressi_aa_silhouette_desc* desc,

@@ -147,7 +147,13 @@ struct SilParams {
     // weight non-zero
     float laplacian, normal;
     int reg;
+    // the paper's HardSoftRas path (paper.cu): peels layers, D = mask *
+    // sigmoid(dist * sigma_scale) with sigma_scale = 7 / radius; n_samples
+    // edge samples per face in FaceFetch's backward (0: exact)
+    int paper, peels;
+    float sigma_scale;
 };
+constexpr int kPaperMaxPeels = 4;
 // Mesh tables and scratch of the regulariser (ids as float, -1 padding).
 struct RegBuffers {
     float* nbrs;     // [nbr_deg][V] VertexNeighborsTex
@@ -177,12 +183,31 @@ struct SilBuffers {
     unsigned* done;      // block-completion counter of the Adam step
     SoftBuffers soft;
     RegBuffers reg;      // p.reg only
+    // p.paper only: the soft layers [peels][views*R*R], the peeling
+    // threshold [views*R*R], the per-pixel gradients of the fetched corners
+    // [peels][3][views*R*R]
+    float4* paper_layers;
+    float* paper_prev;
+    float4* paper_gfetch;
 };
 constexpr int kLossSlots = 4096;
 // Transform, raster, loss and per-view clip gradients (advances the Adam
 // counter). rs_out (nullable) receives the RasterizeSoft images.
 void sil_forward_backward(const SoftDims& d, const SilParams& p,
                           const SilBuffers& b, float* rs_out, cudaStream_t s);
+// The soft-raster face records and bins of this iteration's clip positions.
+void sil_face_setup(const SoftDims& d, const SilBuffers& b, cudaStream_t s);
+// The paper path's per-pixel loss and fetched-corner gradients
+// (paper_pixel.cu): one thread per pixel of every view.
+void paper_pixel_launch(const SilParams& p, const float4* layers,
+                        const float* targets, const float4* clip,
+                        const float* faces, float4* gfetch,
+                        double* loss_slots, unsigned blocks, cudaStream_t s);
+// The paper path's forward/backward into g_clip (p.paper; called by
+// sil_forward_backward). rs_out (nullable) receives layer 0.
+void paper_forward_backward(const SoftDims& d, const SilParams& p,
+                            const SilBuffers& b, float* rs_out,
+                            cudaStream_t s);
 // g_pos = sum_v MVP_v^T g_clip_v, the loss of the iteration, and (update)
 // the Adam step.
 void sil_grad_reduce(const SilParams& p, const SilBuffers& b, bool update,

@@ -1352,6 +1352,26 @@ static __device__ __forceinline__ void rim_block(const SweepArgs& a, FixedBins b
     __syncwarp();  // buffers reused by the warp's next block
 }
 
+// Epilogue of the op-level RasterizeSoft: the reference's output channels
+// (dist, face_id, hard_z, coverage) recomputed for the survivor.
+struct EpiRS {
+    float4* out;  // [views][H][W]
+    __device__ void operator()(const SweepArgs& a, int x, int y, bool in,
+                               const Survivor& s) const {
+        if (!in) return;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (s.face >= 0) {
+            const FaceRec& r = a.recs[s.face];
+            const float px = float(x) + 0.5f, py = float(y) + 0.5f;
+            o.x = signed_dist(px, py, r).dist;
+            o.y = r.fid;
+            o.z = hard_depth(px, py, r);
+            o.w = 1.f;
+        }
+        out[size_t(a.v) * a.W * a.H + size_t(y) * a.W + x] = o;
+    }
+};
+
 template <class Epi>
 __global__ void __launch_bounds__(kSweep1Threads)
         k_sweep1(SweepArgs a0, FixedBins1 b1, FixedBins b2, int2* state,

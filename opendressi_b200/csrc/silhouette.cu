@@ -322,17 +322,23 @@ void sil_transform(const SilParams& p, const SilBuffers& b, int advance,
     check_launch();
 }
 
+void sil_face_setup(const SoftDims& d, const SilBuffers& b, cudaStream_t s) {
+    const dim3 fg((d.n_faces + 127) / 128, d.views);
+    ProfScope ps("face_setup", s);
+    k_face_setup_sil<<<fg, 128, 0, s>>>(
+            d, reinterpret_cast<const float4*>(b.clip), b.faces, b.soft);
+    check_launch();
+}
+
 void sil_forward_backward(const SoftDims& d, const SilParams& p,
                           const SilBuffers& b, float* rs_out,
                           cudaStream_t s) {
-    sil_transform(p, b, 1, b.soft.rim, d.rim_cells, b.soft.status, s);
-    const dim3 fg((d.n_faces + 127) / 128, d.views);
-    {
-        ProfScope ps("face_setup", s);
-        k_face_setup_sil<<<fg, 128, 0, s>>>(
-                d, reinterpret_cast<const float4*>(b.clip), b.faces, b.soft);
+    if (p.paper) {
+        paper_forward_backward(d, p, b, rs_out, s);
+        return;
     }
-    check_launch();
+    sil_transform(p, b, 1, b.soft.rim, d.rim_cells, b.soft.status, s);
+    sil_face_setup(d, b, s);
     EpiSil epi{b.targets, reinterpret_cast<const float4*>(b.clip), b.gclip,
                b.loss_slots, reinterpret_cast<float4*>(rs_out), p.k, p.c,
                p.n_verts};

@@ -171,25 +171,6 @@ void soft_rim_bins(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
     check_launch();
 }
 
-// Epilogue of the op-level RasterizeSoft: the reference's output channels
-// (dist, face_id, hard_z, coverage) recomputed for the survivor.
-struct EpiRS {
-    float4* out;  // [views][H][W]
-    __device__ void operator()(const SweepArgs& a, int x, int y, bool in,
-                               const Survivor& s) const {
-        if (!in) return;
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (s.face >= 0) {
-            const FaceRec& r = a.recs[s.face];
-            const float px = float(x) + 0.5f, py = float(y) + 0.5f;
-            o.x = signed_dist(px, py, r).dist;
-            o.y = r.fid;
-            o.z = hard_depth(px, py, r);
-            o.w = 1.f;
-        }
-        out[size_t(a.v) * a.W * a.H + size_t(y) * a.W + x] = o;
-    }
-};
 
 void soft_raster_op(const SoftDims& d, const SoftBuffers& b,
                     const SoftOpInputs& in, float* out, cudaStream_t s) {

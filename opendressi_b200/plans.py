@@ -152,7 +152,7 @@ class SilhouettePlan(Plan):
                  sigma: float = 1e-4, lr: float = 1e-3, beta1: float = 0.9,
                  beta2: float = 0.999, eps: float = 1e-8, device: int = 0,
                  loss_history: int = 4096, laplacian: float = 0.0,
-                 normal: float = 0.0):
+                 normal: float = 0.0, _paper=None):
         faces = np.ascontiguousarray(faces, np.float32).reshape(-1, 3)
         mvps = np.ascontiguousarray(mvps, np.float32).reshape(-1, 16)
         self.n_verts, self.n_faces = int(n_verts), faces.shape[0]
@@ -169,7 +169,11 @@ class SilhouettePlan(Plan):
         d.device = device
         d.laplacian, d.normal = laplacian, normal
         h = C.c_void_p(0)
-        N.call("dressi_silhouette_plan_create", C.byref(d), C.byref(h))
+        if _paper is None:
+            N.call("dressi_silhouette_plan_create", C.byref(d), C.byref(h))
+        else:
+            N.call("dressi_paper_silhouette_plan_create", C.byref(d),
+                   int(_paper[0]), int(_paper[1]), C.byref(h))
         super().__init__(h, device)
 
     @classmethod
@@ -177,8 +181,9 @@ class SilhouettePlan(Plan):
         mvps = scene.mvps if views is None else scene.mvps[views]
         kw.setdefault("lr", scene.lr)
         kw.setdefault("sigma", scene.sigma)
-        return cls(scene.faces_f, mvps, scene.n_verts, scene.res,
-                   scene.radius_px, device=device, **kw)
+        radius = kw.pop("radius_px", scene.radius_px)
+        return cls(scene.faces_f, mvps, scene.n_verts, scene.res, radius,
+                   device=device, **kw)
 
     def render_targets(self, target_pos, stream=None):
         tp = np.ascontiguousarray(target_pos, np.float32)
@@ -204,6 +209,21 @@ class SilhouettePlan(Plan):
 
     def loss_tensor(self) -> torch.Tensor:
         return self.slot_tensor(N.SLOT_LOSS, (1,))
+
+
+class PaperSilhouettePlan(SilhouettePlan):
+    """The silhouette example's own HardSoftRas technique (the paper path,
+    run.cpp:229-396) as one fused plan: `peels` (1..4) soft layers, the
+    per-pixel edge distance from FaceFetch of the LookupFaces corners, Eq. 6
+    union, FaceFetch's backward with n_samples hashed edge samples per face
+    (0: exact) jittered by the Adam counter. radius_px sets the sigmoid
+    scale (7 / radius_px); sigma is unused."""
+
+    def __init__(self, faces, mvps, n_verts: int, res: int, radius_px: float,
+                 peels: int = 1, n_samples: int = 8, **kw):
+        kw.setdefault("sigma", 1.0)
+        super().__init__(faces, mvps, n_verts, res, radius_px,
+                         _paper=(peels, n_samples), **kw)
 
 
 class AaSilhouettePlan(SilhouettePlan):
