@@ -174,6 +174,7 @@ struct dressi_plan_s {
     // replay
     cudaStream_t cap_stream = nullptr;
     cudaGraphExec_t exec = nullptr;
+    cudaGraphExec_t phase_exec[2] = {nullptr, nullptr};  // exec_phase graphs
     uint32_t kernels_per_iter = 0;
     // silhouette bins live in their own allocation so they can grow
     void* bins_mem = nullptr;
@@ -220,6 +221,10 @@ struct dressi_plan_s {
         if (exec) {
             cudaGraphExecDestroy(exec);
             exec = nullptr;
+        }
+        for (auto& g : phase_exec) {
+            if (g) cudaGraphExecDestroy(g);
+            g = nullptr;
         }
         DRESSI_CUDA(cudaFree(bins_mem));
         bins_mem = nullptr;
@@ -281,11 +286,66 @@ struct dressi_plan_s {
         DRESSI_CUDA(e);
     }
 
+    // One phase of a sharded iteration (0: forward/backward into GRAD, 1:
+    // the update from GRAD), as exec_phase replays it.
+    void record_phase(int phase, cudaStream_t s) {
+        if (kind == kTex) {
+            if (phase == 0)
+                tex_forward_backward(tp, tb, nullptr, s);
+            else
+                tex_update(tp, tb, s);
+        } else if (kind == kPbr) {
+            if (phase == 0)
+                pbr_forward_backward(pd, pb, s);
+            else
+                pbr_update(pd, pb, s);
+        } else if (kind == kAa) {
+            if (phase == 0) {
+                aa_sil_forward_backward(p, ab, s);
+                sil_grad_reduce(p, b, false, s);
+                sil_reg_terms(p, b, s);
+            } else {
+                sil_update(p, b, s);
+            }
+        } else if (phase == 0) {
+            sil_forward_backward(d, p, b, nullptr, s);
+            sil_grad_reduce(p, b, false, s);
+            sil_reg_terms(p, b, s);
+            DRESSI_CUDA(cudaMemcpyAsync(ovf_host, b.soft.status + 1, 4,
+                                        cudaMemcpyDeviceToHost, s));
+        } else {
+            sil_update(p, b, s);
+        }
+    }
+
+    void ensure_phase_graph(int phase) {
+        if (phase_exec[phase]) return;
+        if (!cap_stream)
+            DRESSI_CUDA(cudaStreamCreateWithFlags(&cap_stream,
+                                                  cudaStreamNonBlocking));
+        cudaGraph_t g = nullptr;
+        DRESSI_CUDA(cudaStreamBeginCapture(cap_stream,
+                                           cudaStreamCaptureModeThreadLocal));
+        try {
+            record_phase(phase, cap_stream);
+        } catch (...) {
+            cudaStreamEndCapture(cap_stream, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        DRESSI_CUDA(cudaStreamEndCapture(cap_stream, &g));
+        const cudaError_t e = cudaGraphInstantiate(&phase_exec[phase], g, 0);
+        cudaGraphDestroy(g);
+        DRESSI_CUDA(e);
+    }
+
     ~dressi_plan_s() {
         int prev = -1;
         cudaGetDevice(&prev);
         cudaSetDevice(device);
         if (exec) cudaGraphExecDestroy(exec);
+        for (auto g : phase_exec)
+            if (g) cudaGraphExecDestroy(g);
         if (cap_stream) cudaStreamDestroy(cap_stream);
         if (mem) cudaFree(mem);
         if (bins_mem) cudaFree(bins_mem);
@@ -1643,40 +1703,11 @@ int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream) {
         DRESSI_REQUIRE(phase == 0 || phase == 1, "exec_phase: phase is 0 or 1");
         DeviceGuard dg(p->device);
         cudaStream_t s = as_stream(stream);
-        if (p->kind == dressi_plan_s::kTex) {
-            if (phase == 0)
-                tex_forward_backward(p->tp, p->tb, nullptr, s);
-            else
-                tex_update(p->tp, p->tb, s);
-            return;
-        }
-        if (p->kind == dressi_plan_s::kPbr) {
-            if (phase == 0)
-                pbr_forward_backward(p->pd, p->pb, s);
-            else
-                pbr_update(p->pd, p->pb, s);
-            return;
-        }
-        if (p->kind == dressi_plan_s::kAa) {
-            if (phase == 0) {
-                aa_sil_forward_backward(p->p, p->ab, s);
-                sil_grad_reduce(p->p, p->b, false, s);
-                sil_reg_terms(p->p, p->b, s);
-            } else {
-                sil_update(p->p, p->b, s);
-            }
-            return;
-        }
-        if (phase == 0) {
+        // each phase is one CUDA-graph replay (captured on first use)
+        if (phase == 0 && p->kind == dressi_plan_s::kSil)
             p->grow_bins_if_needed(s);
-            sil_forward_backward(p->d, p->p, p->b, nullptr, s);
-            sil_grad_reduce(p->p, p->b, false, s);
-            sil_reg_terms(p->p, p->b, s);
-            DRESSI_CUDA(cudaMemcpyAsync(p->ovf_host, p->b.soft.status + 1, 4,
-                                        cudaMemcpyDeviceToHost, s));
-        } else {
-            sil_update(p->p, p->b, s);
-        }
+        p->ensure_phase_graph(phase);
+        DRESSI_CUDA(cudaGraphLaunch(p->phase_exec[phase], s));
     });
 }
 

@@ -103,6 +103,11 @@ void launch_sweeps(const SoftDims& d, const SoftBuffers& b,
     DRESSI_CUDA(cudaGetLastError());
     soft_rim_bins(d, b, s);
     {
+        ProfScope ps("rim_order", s);
+        k_rim_order<<<148 * 2, 256, 0, s>>>(b.bin2, d.n_tiles, d.tiles_x);
+    }
+    DRESSI_CUDA(cudaGetLastError());
+    {
         ProfScope ps("rim", s);
         k_rim<Epi><<<kRimCtas, kTileThreads, 0, s>>>(a, b.bin2, b.state, sr,
                                                      sp, sm, epi);

@@ -552,6 +552,10 @@ struct FixedBins {
     int* open_n;      // [1]
     int* open;        // [views * tiles * 8]
     int* take;        // [1]
+    // the work list reordered heavy blocks first (k_rim_order): the rim
+    // warps take the long lists first, so no long block starts last
+    int* order;       // [views * tiles * 8]
+    int* order_n;     // [2] heavy / light items placed (reset by k_rim_bin)
 };
 
 // Sweep-1 bins: 64-bit entries, high word = a lower bound of the depth of
@@ -574,6 +578,10 @@ constexpr int kSortMax = 256;    // keys gathered per round by k_sweep1_spill
 #define DRESSI_WARP_SORT 128
 #endif
 constexpr int kWarpSort = DRESSI_WARP_SORT;  // longest per-warp list sorted
+#ifndef DRESSI_RIM_SORT
+#define DRESSI_RIM_SORT 128
+#endif
+constexpr int kRimSort = DRESSI_RIM_SORT;  // longest rim-block list sorted
 constexpr int kWarpRecs = 16;    // records staged per warp and round
 constexpr int kSpillBlocks = 296;  // grid of k_sweep1_spill (2 per SM)
 static_assert(kSortMax >= kTileThreads, "spill gathers need blockDim keys");
@@ -1088,6 +1096,8 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
         *b1.spill_n = 0;
         *b1.parked_n = 0;
+        b2.order_n[0] = 0;
+        b2.order_n[1] = 0;
     }
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n_tiles;
          t += gridDim.x * blockDim.x)
@@ -1119,6 +1129,28 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
                 if (sp < b2.spill_cap) b2.spill[sp] = make_int2(int(bin), f);
             }
         }
+    }
+}
+
+// The rim work list with the blocks whose bins hold more than kRimHeavy
+// entries first (their lists are longest: unsorted past kRimSort, no early
+// stop), the others after them; within each class the order is arbitrary.
+constexpr int kRimHeavy = 96;
+static __global__ void k_rim_order(FixedBins b2, int n_tiles, int tiles_x) {
+    const int n = *b2.open_n;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += gridDim.x * blockDim.x) {
+        const int e = b2.open[i];
+        const int tbin = e >> 3, w = e & 7;
+        const int v = tbin / n_tiles, tile = tbin - v * n_tiles;
+        // the block's rim bin, indexed as in rim_block
+        const int bx = (tile % tiles_x) * 2 + (w & 1);
+        const int by = (tile / tiles_x) * 4 + (w >> 1);
+        const size_t bin = size_t(v) * n_tiles * 8 + size_t(by) * (tiles_x * 2) + bx;
+        const int slot = b2.cursor[bin] > kRimHeavy
+                                 ? atomicAdd(&b2.order_n[0], 1)
+                                 : n - 1 - atomicAdd(&b2.order_n[1], 1);
+        b2.order[slot] = e;
     }
 }
 
@@ -1271,7 +1303,7 @@ static __device__ __forceinline__ void rim_block(const SweepArgs& a, FixedBins b
     // whose bound is 1 (|dist| >= radius: depth exactly 1, latest face
     // wins) by descending face. A pixel is done at the first entry whose
     // bound is above its survivor's depth.
-    const bool sorted = !over && end > 0 && end <= kWarpSort;
+    const bool sorted = !over && end > 0 && end <= kRimSort;
     if (sorted) {
         const float xlo = float(bx * 8) + 0.5f, xhi = float(bx * 8) + 7.5f;
         const float ylo = float(by * 4) + 0.5f, yhi = float(by * 4) + 3.5f;
@@ -1435,7 +1467,7 @@ __global__ void __launch_bounds__(kTileThreads)
               size_t view_stride_rim, Epi epi) {
     __shared__ FaceRec recs_sh[8][2 * kRimChunk];
     __shared__ int ids_sh[8][2 * kRimChunk];
-    __shared__ unsigned long long keys_sh[8][kWarpSort];
+    __shared__ unsigned long long keys_sh[8][kRimSort];
     const int wc = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_open = *b2.open_n;
     for (;;) {
@@ -1443,7 +1475,7 @@ __global__ void __launch_bounds__(kTileThreads)
         if (lane == 0) item = atomicAdd(b2.take, 1);
         item = __shfl_sync(0xffffffffu, item, 0);
         if (item >= n_open) break;
-        const int e = b2.open[item];
+        const int e = b2.order[item];
         const int tbin = e >> 3, w = e & 7;
         SweepArgs a = a0;
         a.v = tbin / a0.n_tiles;

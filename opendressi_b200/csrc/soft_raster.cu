@@ -67,6 +67,8 @@ void carve_soft_bins(Arena& a, const SoftDims& d, SoftBuffers* b) {
     b->bin2.open_n = a.take<int>(1);
     b->bin2.take = a.take<int>(1);
     b->bin2.open = a.take<int>(std::max<size_t>(vb, 1));
+    b->bin2.order = a.take<int>(std::max<size_t>(vb, 1));
+    b->bin2.order_n = a.take<int>(2);
 }
 
 void carve_soft(Arena& a, const SoftDims& d, SoftBuffers* b) {
