@@ -530,7 +530,7 @@ static __global__ void k_bin_scan(BinSet b, int n_tiles, uint32_t* status) {
 // ------------------------------------------------------------ tile sweeps
 
 constexpr int kRecChunk = 64;
-constexpr int kRimCell = 64;     // pixels per side of a rim-flag cell
+constexpr int kRimCell = 32;     // pixels per side of a rim-flag cell
 constexpr int kRimChunk = 8;     // records per rim staging buffer (2/warp)
 
 // Fixed-capacity bins filled in one pass: entry i of bin k lives at
