@@ -196,6 +196,8 @@ struct dressi_plan_s {
         DRESSI_CUDA(cudaMemset(b.soft.bin2.spill_n, 0, sizeof(int)));
         DRESSI_CUDA(cudaMemset(b.soft.bin2.open_n, 0, sizeof(int)));
         DRESSI_CUDA(cudaMemset(b.soft.bin2.take, 0, sizeof(int)));
+        DRESSI_CUDA(cudaMemset(b.soft.bin2.best, 0xff,
+                               size_t(d.views) * d.W * d.H * 8));
     }
 
     // Reactive growth: a bin set that overflowed in the last replayed

@@ -108,8 +108,21 @@ void launch_sweeps(const SoftDims& d, const SoftBuffers& b,
     }
     DRESSI_CUDA(cudaGetLastError());
     {
+        // split long lists (only when the open blocks are few)
+        ProfScope ps("rim_seg", s);
+        k_rim_seg<<<kRimCtas, kTileThreads, 0, s>>>(a, b.bin2, b.state, sr, sp,
+                                                    sm);
+    }
+    DRESSI_CUDA(cudaGetLastError());
+    {
         ProfScope ps("rim", s);
         k_rim<Epi><<<kRimCtas, kTileThreads, 0, s>>>(a, b.bin2, b.state, sr,
+                                                     sp, sm, epi);
+    }
+    DRESSI_CUDA(cudaGetLastError());
+    {
+        ProfScope ps("rim_split_epi", s);
+        k_rim_split_epi<Epi><<<148 * 2, 256, 0, s>>>(a, b.bin2, b.state, sr,
                                                      sp, sm, epi);
     }
     DRESSI_CUDA(cudaGetLastError());

@@ -552,10 +552,21 @@ struct FixedBins {
     int* open_n;      // [1]
     int* open;        // [views * tiles * 8]
     int* take;        // [1]
-    // the work list reordered heavy blocks first (k_rim_order): the rim
-    // warps take the long lists first, so no long block starts last
+    // the work list reordered by k_rim_order, whole blocks with the long
+    // lists at the front and the others from the back, so the rim warps
+    // take the long lists first and no long block starts last
     int* order;       // [views * tiles * 8]
-    int* order_n;     // [2] heavy / light items placed (reset by k_rim_bin)
+    // split blocks: their segments (block, segment) for k_rim_seg and the
+    // blocks themselves for k_rim_split_epi
+    int* seg_block;   // [kRimSplit * views * tiles * 8]
+    int* seg_index;   // [kRimSplit * views * tiles * 8]
+    int* split;       // [views * tiles * 8]
+    // [0] front and [1] back whole blocks placed, [2] segments, [3] split
+    // blocks, [4] k_rim_seg's work cursor (all reset by k_rim_bin)
+    int* order_n;
+    // per pixel, the best fragment the segments of a heavy block found
+    // (rim_key_of; ~0 = none), consumed and reset by rim_split_finish
+    unsigned long long* best;  // [views * H * W]
 };
 
 // Sweep-1 bins: 64-bit entries, high word = a lower bound of the depth of
@@ -1096,8 +1107,7 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
         *b1.spill_n = 0;
         *b1.parked_n = 0;
-        b2.order_n[0] = 0;
-        b2.order_n[1] = 0;
+        for (int i = 0; i < 5; i++) b2.order_n[i] = 0;
     }
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n_tiles;
          t += gridDim.x * blockDim.x)
@@ -1132,10 +1142,19 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
     }
 }
 
-// The rim work list with the blocks whose bins hold more than kRimHeavy
-// entries first (their lists are longest: unsorted past kRimSort, no early
-// stop), the others after them; within each class the order is arbitrary.
+// The rim work list with the longest lists first: blocks whose bins hold
+// more than kRimSort entries (too long to sort: no early stop) as kRimSplit
+// segments when the open blocks are few, then those above kRimHeavy whole,
+// then the others; within each class the order is arbitrary.
 constexpr int kRimHeavy = 96;
+constexpr int kRimSplit = 4;  // segments of a heavy block (strided entries)
+// Splitting costs work (each segment prunes against its own survivor only)
+// and pays only when the open blocks are too few to fill the machine and
+// the longest list sets the phase's time (few views per GPU).
+#ifndef DRESSI_RIM_SPLIT_MAX_OPEN
+#define DRESSI_RIM_SPLIT_MAX_OPEN 16384
+#endif
+constexpr int kRimSplitMaxOpen = DRESSI_RIM_SPLIT_MAX_OPEN;
 static __global__ void k_rim_order(FixedBins b2, int n_tiles, int tiles_x) {
     const int n = *b2.open_n;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -1147,11 +1166,41 @@ static __global__ void k_rim_order(FixedBins b2, int n_tiles, int tiles_x) {
         const int bx = (tile % tiles_x) * 2 + (w & 1);
         const int by = (tile / tiles_x) * 4 + (w >> 1);
         const size_t bin = size_t(v) * n_tiles * 8 + size_t(by) * (tiles_x * 2) + bx;
-        const int slot = b2.cursor[bin] > kRimHeavy
-                                 ? atomicAdd(&b2.order_n[0], 1)
-                                 : n - 1 - atomicAdd(&b2.order_n[1], 1);
-        b2.order[slot] = e;
+        const int cnt = b2.cursor[bin];
+        if (n < kRimSplitMaxOpen && cnt > kRimSort && cnt <= b2.cap) {
+            // a list too long to sort (and not spilled): kRimSplit warps
+            // fold a strided share each, k_rim_split_epi finishes the block
+            const int slot = atomicAdd(&b2.order_n[2], kRimSplit);
+            for (int sg = 0; sg < kRimSplit; sg++) {
+                b2.seg_block[slot + sg] = e;
+                b2.seg_index[slot + sg] = sg;
+            }
+            b2.split[atomicAdd(&b2.order_n[3], 1)] = e;
+        } else if (cnt > kRimHeavy) {
+            // long but sorted: one warp, early in the list
+            b2.order[atomicAdd(&b2.order_n[0], 1)] = e;
+        } else {
+            b2.order[n - 1 - atomicAdd(&b2.order_n[1], 1)] = e;
+        }
     }
+}
+
+// The 64-bit key of a survivor: ascending keys order as `beats` does
+// (lower depth first; at equal depth the later face; no face last), with
+// the hard bit alongside.
+__device__ __forceinline__ unsigned long long rim_key_of(const Survivor& s) {
+    const uint32_t lo = s.face < 0 ? 0xffffffffu
+                                   : ((uint32_t(0x7fffffff - s.face) << 1) |
+                                      (s.hard ? 1u : 0u));
+    return (uint64_t(__float_as_uint(s.depth)) << 32) | lo;
+}
+__device__ __forceinline__ Survivor rim_survivor_of(unsigned long long k) {
+    Survivor s;
+    s.depth = __uint_as_float(uint32_t(k >> 32));
+    const uint32_t lo = uint32_t(k);
+    s.face = lo == 0xffffffffu ? -1 : 0x7fffffff - int(lo >> 1);
+    s.hard = lo != 0xffffffffu && (lo & 1u);
+    return s;
 }
 
 // Asynchronous 16-byte global -> shared copies (cp.async), committed and
@@ -1384,6 +1433,82 @@ static __device__ __forceinline__ void rim_block(const SweepArgs& a, FixedBins b
     __syncwarp();  // buffers reused by the warp's next block
 }
 
+// One segment of a heavy rim block: the list entries seg, seg + kRimSplit,
+// ... folded into the sweep-1 survivors of the block's open pixels and
+// merged into b2.best (atomic minimum of rim_key_of). The argmin is
+// order-free, so the segments' merge equals one warp's whole pass.
+static __device__ __forceinline__ void rim_segment(const SweepArgs& a,
+                                                   FixedBins b2, int tile,
+                                                   int w, int seg,
+                                                   const int2* state,
+                                                   FaceRec* recs_w,
+                                                   int* ids_w) {
+    const int lane = threadIdx.x & 31;
+    const int x = (tile % a.tiles_x) * kTile + (w & 1) * 8 + (lane & 7);
+    const int y = (tile / a.tiles_x) * kTile + (w >> 1) * 4 + (lane >> 3);
+    const bool in = x < a.W && y < a.H;
+    const float px = float(x) + 0.5f, py = float(y) + 0.5f;
+    const size_t pix = size_t(y) * a.W + x;
+    const bool peel = a.prev != nullptr;
+    const float prev = (in && peel) ? a.prev[pix] : 0.f;
+    Survivor s{1.f, -1, false};
+    if (in) s = unpack(state[size_t(a.v) * a.W * a.H + pix]);
+    const bool open = in && s.depth > 0.5f;
+    const int bx = (tile % a.tiles_x) * 2 + (w & 1);
+    const int by = (tile / a.tiles_x) * 4 + (w >> 1);
+    const size_t bin = size_t(a.v) * a.n_tiles * 8 +
+                       size_t(by) * (a.tiles_x * 2) + bx;
+    const int n = b2.cursor[bin];  // <= cap (heavy blocks are not spilled)
+    const int* lst = b2.list + bin * b2.cap;
+    const int ns = n > seg ? (n - seg + kRimSplit - 1) / kRimSplit : 0;
+    bool done = !open;
+    for (int base = 0; base < ns; base += kRimChunk) {
+        if (__all_sync(0xffffffffu, done)) break;
+        const int cn = imin_(kRimChunk, ns - base);
+        if (lane < cn) ids_w[lane] = lst[seg + (base + lane) * kRimSplit];
+        __syncwarp();
+        rim_issue(a.recs, ids_w, cn, recs_w);
+        cp_async_wait<0>();
+        __syncwarp();
+        if (open)
+            rim_fold_chunk(a, x, y, px, py, peel, prev, cn, recs_w, ids_w,
+                           nullptr, s, done);
+        __syncwarp();
+    }
+    if (open) atomicMin(&b2.best[size_t(a.v) * a.W * a.H + pix], rim_key_of(s));
+}
+
+// Finishes a split rim block (its segments ran in k_rim_seg): per pixel the
+// best of the sweep-1 survivor and the segments' fragments, then the
+// epilogue; resets b2.best and the block's bin cursor for the next use.
+template <class Epi>
+__device__ __forceinline__ void rim_split_finish(const SweepArgs& a, FixedBins b2,
+                                                 int tile, int w,
+                                                 const int2* state,
+                                                 const Epi& epi) {
+    const int lane = threadIdx.x & 31;
+    const int x = (tile % a.tiles_x) * kTile + (w & 1) * 8 + (lane & 7);
+    const int y = (tile / a.tiles_x) * kTile + (w >> 1) * 4 + (lane >> 3);
+    const bool in = x < a.W && y < a.H;
+    Survivor s{1.f, -1, false};
+    if (in) {
+        const size_t pi = size_t(a.v) * a.W * a.H + size_t(y) * a.W + x;
+        s = unpack(state[pi]);
+        const unsigned long long k = b2.best[pi];
+        if (k != ~0ull) {
+            if (k < rim_key_of(s)) s = rim_survivor_of(k);
+            b2.best[pi] = ~0ull;
+        }
+    }
+    if (lane == 0) {
+        const int bx = (tile % a.tiles_x) * 2 + (w & 1);
+        const int by = (tile / a.tiles_x) * 4 + (w >> 1);
+        b2.cursor[size_t(a.v) * a.n_tiles * 8 + size_t(by) * (a.tiles_x * 2) +
+                  bx] = 0;
+    }
+    epi(a, x, y, in, s);
+}
+
 // Epilogue of the op-level RasterizeSoft: the reference's output channels
 // (dist, face_id, hard_z, coverage) recomputed for the survivor.
 struct EpiRS {
@@ -1457,6 +1582,34 @@ __global__ void __launch_bounds__(kTileThreads)
     }
 }
 
+// The segments of the split rim blocks (few open blocks, lists too long to
+// sort), by persistent warps; k_rim_split_epi finishes those blocks.
+static __global__ void __launch_bounds__(kTileThreads)
+        k_rim_seg(SweepArgs a0, FixedBins b2, const int2* state,
+                  size_t view_stride_recs, size_t view_stride_px,
+                  size_t view_stride_rim) {
+    __shared__ FaceRec recs_sh[8][kRimChunk];
+    __shared__ int ids_sh[8][kRimChunk];
+    const int wc = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_seg = b2.order_n[2];
+    for (;;) {
+        int item = 0;
+        if (lane == 0) item = atomicAdd(&b2.order_n[4], 1);
+        item = __shfl_sync(0xffffffffu, item, 0);
+        if (item >= n_seg) break;
+        const int e = b2.seg_block[item];
+        const int tbin = e >> 3, w = e & 7;
+        SweepArgs a = a0;
+        a.v = tbin / a0.n_tiles;
+        const int tile = tbin - a.v * a0.n_tiles;
+        a.recs = a0.recs + a.v * view_stride_recs;
+        a.rim = a0.rim + a.v * view_stride_rim;
+        if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
+        rim_segment(a, b2, tile, w, b2.seg_index[item], state, recs_sh[wc],
+                    ids_sh[wc]);
+    }
+}
+
 // The rim phase: persistent warps take the open 8x4 blocks queued by sweep
 // 1 from the work list (an atomic cursor balances blocks of very different
 // cost), so every resident warp has work.
@@ -1470,12 +1623,15 @@ __global__ void __launch_bounds__(kTileThreads)
     __shared__ unsigned long long keys_sh[8][kRimSort];
     const int wc = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_open = *b2.open_n;
+    const int n_front = b2.order_n[0], n_back = b2.order_n[1];
     for (;;) {
         int item = 0;
         if (lane == 0) item = atomicAdd(b2.take, 1);
         item = __shfl_sync(0xffffffffu, item, 0);
-        if (item >= n_open) break;
-        const int e = b2.order[item];
+        if (item >= n_front + n_back) break;
+        // the long lists first (the split blocks are not in this list)
+        const int e = b2.order[item < n_front ? item
+                                              : n_open - 1 - (item - n_front)];
         const int tbin = e >> 3, w = e & 7;
         SweepArgs a = a0;
         a.v = tbin / a0.n_tiles;
@@ -1485,6 +1641,28 @@ __global__ void __launch_bounds__(kTileThreads)
         if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
         rim_block(a, b2, tile, w, state, recs_sh[wc], ids_sh[wc], keys_sh[wc],
                   epi);
+    }
+}
+
+// The split blocks' epilogues (rim_split_finish), one warp per block, after
+// k_rim_seg.
+template <class Epi>
+__global__ void __launch_bounds__(256)
+        k_rim_split_epi(SweepArgs a0, FixedBins b2, const int2* state,
+                        size_t view_stride_recs, size_t view_stride_px,
+                        size_t view_stride_rim, Epi epi) {
+    const int n_split = b2.order_n[3];
+    for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < n_split;
+         t += (gridDim.x * blockDim.x) >> 5) {
+        const int e = b2.split[t];
+        const int tbin = e >> 3, w = e & 7;
+        SweepArgs a = a0;
+        a.v = tbin / a0.n_tiles;
+        const int tile = tbin - a.v * a0.n_tiles;
+        a.recs = a0.recs + a.v * view_stride_recs;
+        a.rim = a0.rim + a.v * view_stride_rim;
+        if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
+        rim_split_finish(a, b2, tile, w, state, epi);
     }
 }
 constexpr int kRimCtas = 148 * 4;  // persistent grid of k_rim

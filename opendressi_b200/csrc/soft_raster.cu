@@ -68,7 +68,12 @@ void carve_soft_bins(Arena& a, const SoftDims& d, SoftBuffers* b) {
     b->bin2.take = a.take<int>(1);
     b->bin2.open = a.take<int>(std::max<size_t>(vb, 1));
     b->bin2.order = a.take<int>(std::max<size_t>(vb, 1));
-    b->bin2.order_n = a.take<int>(2);
+    b->bin2.seg_block = a.take<int>(std::max<size_t>(kRimSplit * vb, 1));
+    b->bin2.seg_index = a.take<int>(std::max<size_t>(kRimSplit * vb, 1));
+    b->bin2.split = a.take<int>(std::max<size_t>(vb, 1));
+    b->bin2.order_n = a.take<int>(5);
+    b->bin2.best = a.take<unsigned long long>(
+            std::max<size_t>(size_t(d.views) * d.W * d.H, 1));
 }
 
 void carve_soft(Arena& a, const SoftDims& d, SoftBuffers* b) {
@@ -85,6 +90,8 @@ void init_soft(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
     DRESSI_CUDA(cudaMemsetAsync(b.bin2.spill_n, 0, sizeof(int), s));
     DRESSI_CUDA(cudaMemsetAsync(b.bin2.open_n, 0, sizeof(int), s));
     DRESSI_CUDA(cudaMemsetAsync(b.bin2.take, 0, sizeof(int), s));
+    DRESSI_CUDA(cudaMemsetAsync(b.bin2.best, 0xff,
+                                size_t(d.views) * d.W * d.H * 8, s));
     DRESSI_CUDA(cudaMemsetAsync(b.status, 0, 4 * sizeof(uint32_t), s));
     DRESSI_CUDA(cudaMemsetAsync(b.rim, 0,
                                 size_t(d.views) * d.rim_cells * sizeof(int), s));
