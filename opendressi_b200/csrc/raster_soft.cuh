@@ -1529,8 +1529,11 @@ struct EpiRS {
     }
 };
 
+// Nine CTAs per SM (56 registers): issue-bound, so residency pays over the
+// few spilled bytes (7 CTAs at the unbounded 72 registers; 8, 10 and 12 per
+// SM timed slower).
 template <class Epi>
-__global__ void __launch_bounds__(kSweep1Threads)
+__global__ void __launch_bounds__(kSweep1Threads, 9)
         k_sweep1(SweepArgs a0, FixedBins1 b1, FixedBins b2, int2* state,
                  uint8_t* active, size_t view_stride_recs,
                  size_t view_stride_px, size_t view_stride_rim, Epi epi) {
