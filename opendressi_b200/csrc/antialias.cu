@@ -183,8 +183,11 @@ static __device__ __noinline__ float aa_pair_r(const AaFace* fr, int n_faces,
     return pr.r;
 }
 
+// Eight CTAs per SM (32 registers, a few spilled bytes): the kernel is
+// latency-bound on its neighbour and face-record loads, so full residency
+// beats the unbounded 48 registers (5 CTAs; 1.12 -> 0.87 ms at C4).
 template <class Epi, int NC>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 8)
         k_aa_forward(AaDims d, const AaFace* frs, const float* img,
                      const float* tri, const int* view_flags, Epi epi) {
     __shared__ float vals[18][18];  // n_comp == 1: the image tile + halo
@@ -488,7 +491,9 @@ __global__ void k_aa_bwd_vtx_vft(AaDims d, const AaFace* frs, const float* gy,
 // evaluated once and credited to the face's vertices with their
 // multiplicity -- the same sum as the per-incidence form when the adjacency
 // is VertexFacesTex of the faces (the plans build it that way).
-__global__ void k_aa_bwd_vtx_faces(AaDims d, const AaFace* frs,
+// Six CTAs per SM (40 registers): 0.58 -> 0.56 ms at C4 against the
+// unbounded 59 registers; eight spill and time slower.
+__global__ void __launch_bounds__(256, 6) k_aa_bwd_vtx_faces(AaDims d, const AaFace* frs,
                                    const float* gy, const float* img,
                                    const float* tri, const float4* clip,
                                    const float* t_ptr, float t_add,
