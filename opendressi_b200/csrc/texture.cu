@@ -309,7 +309,9 @@ __device__ __forceinline__ float pixel_rho(const float* gb, int W, int H,
 // Per view pixel: lod, trilinear sample of the pyramid. train: the loss of
 // the pixel (warp-summed into loss_slots) and the exact transpose of its
 // sampling scattered into gpyr; out (nullable) gets mask * sample.
-__global__ void __launch_bounds__(256)
+// Eight CTAs per SM (32 registers instead of 40): 0.121 -> 0.120 ms per
+// C2 iteration.
+__global__ void __launch_bounds__(256, 8)
         k_c2_pixel(TexParams p, const float* pyr, const float* gbuf,
                    const float* targets, float4* gpyr, double* loss_slots,
                    float* out, int train) {
