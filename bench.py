@@ -13,8 +13,11 @@ the replicated Adam step.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3|c4]
                     [--impl reference]
 
-Prints one JSON line (rank 0). See DESIGN.md for the byte model of the
-roofline and the definition of the end-to-end (e2e) step.
+Prints one JSON line (rank 0). The roofline's algorithmic bytes are the
+survey's byte model (iteration_bytes() and its siblings below: 16 B per
+view-pixel plus the per-view clip / face terms and Adam for the silhouette
+configs); the end-to-end (e2e) step uploads the parameters from pinned host
+memory, replays one iteration and downloads the parameters and the loss.
 """
 
 from __future__ import annotations

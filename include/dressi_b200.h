@@ -122,8 +122,11 @@ int dressi_rasterize_face_id(const float* clip, uint32_t n_verts,
  * about views * (96 F + 12 T + 4 max(16 F, 4 T) + 16 K) bytes for F faces
  * and T 16x16-pixel tiles (one 1024x1024 view of 20480 faces: 3.4 MB).
  * The first call on a device looks up the scratch address (and may load the
- * module): make it outside any stream capture. Calls that overlap in time
- * on one device share the scratch and race. */
+ * module): make it outside any stream capture. A device reset
+ * (cudaDeviceReset, or the primary context destroyed and re-created) can
+ * move the array; the next call notices the new context and looks the
+ * address up again, so it counts as a first call too. Calls that overlap in
+ * time on one device share the scratch and race. */
 int dressi_rasterize_face_id_noalloc(const float* clip, uint32_t n_verts,
                                      const float* faces, uint32_t n_faces,
                                      uint32_t views, uint32_t width,
@@ -446,10 +449,24 @@ int dressi_aa_silhouette_plan_create(const dressi_aa_silhouette_desc* desc,
  * (u, v, 1)), pred = mask * trilinear(mips(tex), uv) with `levels` box-
  * filtered mip levels and a per-pixel lod from the uv differences, loss =
  * sum_v Mean((target - pred)^2); Adam on the [tex_size][tex_size][3]
- * texture (PARAM slot). The mip path has no counterpart in the reference
- * (which samples one level); its definition is in oracle.c. Targets:
- * dressi_plan_render_targets with the target TEXTURE (host
- * [tex_size][tex_size][3]). */
+ * texture (PARAM slot). Targets: dressi_plan_render_targets with the
+ * target TEXTURE (host [tex_size][tex_size][3]).
+ * The mip path has no counterpart in the reference (which samples one
+ * level); it is defined here:
+ *  - level l + 1 texel (x, y) = 0.25 * (((a + b) + c) + d) of the level-l
+ *    texels a = (2x, 2y), b = (2x+1, 2y), c = (2x, 2y+1), d = (2x+1, 2y+1);
+ *  - per covered pixel, du_x = uv(x+1, y) - uv(x, y) if the right
+ *    neighbour is covered and inside the screen, else uv(x, y) - uv(x-1, y)
+ *    if the left one is, else 0 (du_y likewise with the rows);
+ *    rho = max(|du_x|, |du_y|) * tex_size (Euclidean lengths);
+ *  - lod = 0 for rho <= 1, else e + (m - 1) with rho = m 2^e, m in [1, 2)
+ *    (a piecewise-linear log2, exact in float), clamped to levels - 1;
+ *  - sample = (1 - f) B(l0) + f B(l0 + 1), l0 = floor(lod), f = lod - l0,
+ *    B(l) the clamp-to-edge bilinear tap set of level l at uv (the
+ *    reference's BilerpClamp); f = 0 or l0 = levels - 1 uses B(l0) alone;
+ *  - the backward is the exact transpose: every tap weight times the
+ *    pixel's gradient added to the level's texel, then the chain
+ *    acc_l = g_l + 0.25 acc_(l+1) folded down to level 0. */
 typedef struct {
     uint32_t struct_size;  /* sizeof(dressi_texture_desc) */
     uint32_t n_verts, n_faces, n_views, res;

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstring>
 #include <memory>
@@ -463,6 +464,9 @@ static int hard_common(const float* clip, uint32_t n_verts, const float* attr,
                        "Rasterize: screen larger than 32768");
         DRESSI_REQUIRE(n_comp >= 1 && n_comp <= 4,
                        "Rasterize: attribute must have 1..4 components");
+        DRESSI_REQUIRE(n_faces <= uint32_t(INT_MAX) &&
+                               n_verts <= uint32_t(INT_MAX),
+                       "Rasterize: face or vertex count above INT_MAX");
         cudaStream_t s = as_stream(stream);
         HardDims d;
         d.W = int(width);

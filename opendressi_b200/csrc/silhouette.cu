@@ -8,9 +8,11 @@
 //              regulariser (laplacian / normal != 0)        regularize.cu
 //              in-graph Adam                                k_gpos_adam
 //
-// It computes what the reference's DressiAD::execStep computes for the graph
-// built in oracle/ref_driver.cpp (SilViewLoss + in-graph Adam of
-// examples/silhouette_optimization/run.cpp:421-436), with the RasterizeSoft
+// It computes what the reference's DressiAD::execStep computes for the
+// silhouette graph of examples/silhouette_optimization/run.cpp:228-437 (per
+// view: RasterizeSoft of SoftClip(clip), pred = max(hard, soft), loss =
+// (target - pred)^2 / R^2, summed over views; the in-graph Adam of
+// run.cpp:421-436), with the RasterizeSoft
 // output, the loss image and the per-view clip gradients kept on chip
 // instead of round-tripping through HBM between passes.
 #include <algorithm>
@@ -20,9 +22,14 @@
 namespace dressi {
 
 // Per-pixel loss and dL/d dist of the silhouette graph, in the operation
-// order of the reference autodiff (see oracle.c sil_pixel for the
-// derivation): pred = max(cov*step(0,d), cov*sigmoid(d*|d|*k)),
-// loss = (target - pred)^2 * c.
+// order of the reference autodiff: pred = max(cov*step(0,d),
+// cov*sigmoid(d*|d|*k)), loss = (target - pred)^2 * c. Backward, op by op
+// as BuildBackward emits it (src/core/build_backward.cpp:62-149 with the
+// rules of src/core/f_ops.cpp): the seed 1 through Mul(., c) gives c; the
+// square (Mul(diff, diff)) adds gy*diff twice; Sub gives -g to pred; Max
+// passes g to its first operand where hard >= soft (Step(soft, hard)) and
+// to the second elsewhere; Sigmoid multiplies by s*(1-s); the product
+// d*|d|*k gives g*k*|d| + g*k*d*sign(d) to d (Step has no gradient).
 __device__ __forceinline__ float sil_pixel(float dist, float cov, float target,
                                            float k, float c, float* g_dist) {
     const float step = dist < 0.f ? 0.f : 1.f;

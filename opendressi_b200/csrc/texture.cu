@@ -8,7 +8,9 @@
 // (src/codegen/glsl_codegen.cpp:658-709, src/vk/executor.cpp:193-202).
 //
 // Config C2 (no reference implementation of mips; defined from first
-// principles, restated in oracle.c): a box-filtered mip pyramid of the
+// principles, the definition is spelled out beside
+// dressi_texture_plan_create in the public header): a box-filtered mip
+// pyramid of the
 // optimised texture, per-pixel trilinear sampling at a lod taken from the
 // G-buffer's uv differences, the loss of the reference's texture graph
 // (examples/texture_optimization/run.cpp:115-126: per view

@@ -671,6 +671,20 @@ int orc_silhouette_loss_grad(const float* pos, uint32_t n_verts,
                             1);
 }
 
+/* orc_silhouette_loss_grad with the views spread over `threads` host
+ * threads (the per-view results are summed in view order, as above). */
+int orc_silhouette_loss_grad_mt(const float* pos, uint32_t n_verts,
+                                const float* faces, uint32_t n_faces,
+                                uint32_t n_views, uint32_t res, float radius,
+                                float sigma, const float* mvps,
+                                const float* targets, double* loss,
+                                float* grad, float* rs_out,
+                                uint32_t threads) {
+    return sil_loss_grad_mt(pos, n_verts, faces, n_faces, n_views, res,
+                            radius, sigma, mvps, targets, loss, grad, rs_out,
+                            threads);
+}
+
 /* In-graph Adam (examples/silhouette_optimization/run.cpp:421-436) */
 void orc_adam(float* p, float* m, float* v, float* t, const float* g,
               uint32_t n, float lr, float b1, float b2, float eps) {

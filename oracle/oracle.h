@@ -79,6 +79,13 @@ int orc_silhouette_loss_grad(const float* pos, uint32_t n_verts,
                              float sigma, const float* mvps,
                              const float* targets, double* loss, float* grad,
                              float* rs_out);
+int orc_silhouette_loss_grad_mt(const float* pos, uint32_t n_verts,
+                                const float* faces, uint32_t n_faces,
+                                uint32_t n_views, uint32_t res, float radius,
+                                float sigma, const float* mvps,
+                                const float* targets, double* loss,
+                                float* grad, float* rs_out,
+                                uint32_t threads);
 
 /* In-graph Adam of examples/silhouette_optimization/run.cpp:421-436, one
  * step over n params; t is the counter BEFORE the step (updated in place). */

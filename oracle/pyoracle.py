@@ -39,9 +39,15 @@ def build_port() -> str:
     return PORT_SO
 
 
-def build_ref(ref_dir: str = "/root/reference") -> str | None:
-    """Builds _ref/libdressi_ref.so when the reference checkout exists."""
-    if not os.path.isdir(os.path.join(ref_dir, "src", "core")):
+def build_ref(ref_dir: str | None = None) -> str | None:
+    """Builds _ref/libdressi_ref.so from the reference checkout named by
+    `ref_dir` or, when that is None, by the DRESSI_REF_DIR environment
+    variable. Without a checkout (the GPU box has none) it returns the
+    prebuilt library if there is one, else None."""
+    if ref_dir is None:
+        ref_dir = os.environ.get("DRESSI_REF_DIR")
+    if not ref_dir or not os.path.isdir(os.path.join(ref_dir, "src",
+                                                     "core")):
         return REF_SO if os.path.exists(REF_SO) else None
     subprocess.run(["make", "-s", "-j8", "-C", HERE, "ref",
                     f"REF_DIR={ref_dir}"], check=True)
@@ -137,17 +143,17 @@ class Port(_Lib):
         return out
 
     def silhouette_loss_grad(self, pos, faces, mvps, targets, res, radius,
-                             sigma, want_rs=False):
+                             sigma, want_rs=False, threads=1):
         pos, faces, mvps, targets = map(_f32, (pos, faces, mvps, targets))
         nv = mvps.shape[0]
         grad = np.zeros_like(pos)
         loss = C.c_double(0.0)
         rs = np.zeros((nv, res, res, 4), np.float32) if want_rs else None
-        self._err(self.lib.orc_silhouette_loss_grad(
+        self._err(self.lib.orc_silhouette_loss_grad_mt(
             _fp(pos), _u32(pos.shape[0]), _fp(faces), _u32(faces.shape[0]),
             _u32(nv), _u32(res), C.c_float(radius), C.c_float(sigma),
-            _fp(mvps), _fp(targets), C.byref(loss), _fp(grad), _fp(rs)),
-            "silhouette_loss_grad")
+            _fp(mvps), _fp(targets), C.byref(loss), _fp(grad), _fp(rs),
+            _u32(max(1, int(threads)))), "silhouette_loss_grad")
         return loss.value, grad, rs
 
     def silhouette_run(self, pos, faces, mvps, targets, res, radius, sigma,

@@ -1,0 +1,240 @@
+"""Parity at the benchmark's own configurations (the sizes bench.py times),
+not only on reduced scenes:
+
+- C3 (icosphere-5, 16 views at 1024^2, the example's regulariser 0.15 /
+  0.4): the first iteration's position gradient against the C restatement
+  on all 16 views, and the regularised Adam step bit-exact from it;
+- C3 per-step ("teacher-forced") checks over several iterations: at every
+  iterate the plan's gradient matches the restatement's gradient at the
+  plan's own positions, and the plan's update is exactly the regularised
+  Adam step of that gradient;
+- C3 over the configured 300 iterations (16 views, 256^2): every loss of the
+  trace and the final loss within 1e-3 rel of the restatement's own run;
+- C3 at the metric's other resolutions, 512^2 (16 views) and 2048^2 (2
+  views): RasterizeSoft images bit-exact, first gradient 1e-4 / 1e-3;
+- C4 (64 views at 1024^2, 8 edge samples, regulariser 0.5 / 0.5) and C5
+  (icosphere-6, 32 views at 1024^2, full-size maps and environment): one
+  step's gradient against the restatement.
+
+Tolerances: images bit-exact; gradients 1e-4 abs + 1e-3 rel; losses after N
+optimizer steps 1e-3 rel (the north star's bars)."""
+
+import os
+from concurrent.futures import ThreadPoolExecutor
+
+import numpy as np
+import pytest
+
+from opendressi_b200 import scene
+
+pytestmark = pytest.mark.gpu
+
+TOL = dict(atol=1e-4, rtol=1e-3)
+THREADS = max(1, os.cpu_count() or 1)
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def _pmap(fn, items):
+    with ThreadPoolExecutor(THREADS) as ex:
+        return list(ex.map(fn, items))
+
+
+def _sil_targets(port, sc):
+    return np.stack(_pmap(
+        lambda m: (port.rasterize_face_id(
+            port.transform_clip(sc.target_pos, m), sc.faces_f, sc.res,
+            sc.res) > 0).astype(np.float32), list(sc.mvps)))
+
+
+def _sil_plan(sc, **kw):
+    from opendressi_b200 import _native as N
+    from opendressi_b200.plans import SilhouettePlan
+
+    plan = SilhouettePlan.from_scene(sc, **kw)
+    plan.upload(N.SLOT_PARAM, sc.pos0)
+    plan.render_targets(sc.target_pos)
+    targets = plan.download(N.SLOT_TARGET).reshape(-1, sc.res, sc.res)
+    return plan, targets
+
+
+def _adam_regularised(port, pos, m, v, t, g, faces, lap, nrm, lr):
+    p = np.ascontiguousarray(pos, np.float32).copy()
+    gr = port.regularized_grad(pos, faces, g, lap, nrm) if (lap or nrm) \
+        else g
+    t = port.adam(p, m, v, t, np.ascontiguousarray(gr, np.float32), lr)
+    return p, t
+
+
+def test_c3_full_size_first_step(cuda, port):
+    """C3 exactly as bench.py runs it: all 16 views at 1024^2."""
+    from opendressi_b200 import _native as N
+
+    sc = scene.silhouette_scene(level=5, n_views=16, res=1024, seed=0)
+    plan, targets = _sil_plan(sc, laplacian=0.15, normal=0.4)
+    assert np.array_equal(targets, _sil_targets(port, sc))
+    plan.step(1)
+    loss, g_cpu, _ = port.silhouette_loss_grad(
+        sc.pos0, sc.faces_f, sc.mvps, targets, 1024, sc.radius_px, sc.sigma,
+        threads=THREADS)
+    g = plan.download(N.SLOT_GRAD).reshape(-1, 3)
+    np.testing.assert_allclose(g, g_cpu, **TOL)
+    assert np.abs(g_cpu).max() > 1e-5
+    assert plan.loss() == pytest.approx(loss, rel=1e-5)
+    p, _ = _adam_regularised(port, sc.pos0, np.zeros_like(g), np.zeros_like(g),
+                             0.0, g, sc.faces_f, 0.15, 0.4, sc.lr)
+    pos = plan.download(N.SLOT_PARAM).reshape(-1, 3)
+    assert np.array_equal(bits(pos), bits(p)), \
+        "regularised Adam step from the plan's gradient not bit-exact"
+    assert plan.status() == 0
+
+
+@pytest.mark.parametrize("res", [256, 1024])
+def test_c3_teacher_forced_steps(cuda, port, res):
+    """Several iterations of C3 (16 views, regulariser on), each checked on
+    its own: the gradient at the plan's current positions against the
+    restatement (1e-4 / 1e-3) and the plan's update bit-exact against the
+    regularised Adam step of the plan's own gradient. This bounds every
+    iterate, where a comparison of two free-running trajectories cannot
+    (Adam turns a sign difference of a near-zero gradient into a full step)."""
+    from opendressi_b200 import _native as N
+
+    sc = scene.silhouette_scene(level=5, n_views=16, res=res, seed=0)
+    plan, targets = _sil_plan(sc, laplacian=0.15, normal=0.4)
+    n_verts = sc.n_verts
+    m = np.zeros((n_verts, 3), np.float32)
+    v = np.zeros((n_verts, 3), np.float32)
+    t = 0.0
+    pos = np.ascontiguousarray(sc.pos0, np.float32).copy()
+    steps = 6 if res == 256 else 3
+    for k in range(steps):
+        plan.step(1)
+        g = plan.download(N.SLOT_GRAD).reshape(-1, 3)
+        loss, g_cpu, _ = port.silhouette_loss_grad(
+            pos, sc.faces_f, sc.mvps, targets, res, sc.radius_px, sc.sigma,
+            threads=THREADS)
+        np.testing.assert_allclose(g, g_cpu, **TOL,
+                                   err_msg=f"gradient of iteration {k}")
+        assert plan.loss() == pytest.approx(loss, rel=1e-5)
+        pos, t = _adam_regularised(port, pos, m, v, t, g, sc.faces_f, 0.15,
+                                   0.4, sc.lr)
+        got = plan.download(N.SLOT_PARAM).reshape(-1, 3)
+        assert np.array_equal(bits(got), bits(pos)), \
+            f"Adam update of iteration {k} not bit-exact"
+    assert plan.status() == 0
+
+
+def test_c3_300_iterations(cuda, port):
+    """The configured iteration count (300) at 256^2 on the C3 mesh and
+    view count, regulariser on: every loss of the trace, and the final loss,
+    within 1e-3 rel of the restatement's own 300-iteration run."""
+    from opendressi_b200 import _native as N
+
+    sc = scene.silhouette_scene(level=5, n_views=16, res=256, seed=0)
+    plan, targets = _sil_plan(sc, laplacian=0.15, normal=0.4)
+    n = 300
+    plan.step(n)
+    trace = plan.loss_history(n)
+    trace_cpu, pos_cpu = port.silhouette_run(
+        sc.pos0, sc.faces_f, sc.mvps, targets, 256, sc.radius_px, sc.sigma,
+        sc.lr, n, threads=THREADS, laplacian=0.15, normal=0.4)
+    assert trace[-1] == pytest.approx(trace_cpu[-1], rel=1e-3)
+    np.testing.assert_allclose(trace, trace_cpu, rtol=1e-3)
+    assert trace[-1] < 0.5 * trace[0]          # it optimises
+    pos = plan.download(N.SLOT_PARAM).reshape(-1, 3)
+    # the shapes agree: every vertex within 1e-3 of the restatement's
+    assert np.abs(pos - pos_cpu).max() < 1e-3
+    assert plan.status() == 0
+
+
+@pytest.mark.parametrize("res,views", [(512, 16), (2048, 2)])
+def test_c3_other_resolutions(cuda, port, res, views):
+    from opendressi_b200 import _native as N
+
+    sc = scene.silhouette_scene(level=5, n_views=views, res=res, seed=0)
+    plan, targets = _sil_plan(sc, laplacian=0.15, normal=0.4)
+    assert np.array_equal(targets, _sil_targets(port, sc))
+    rs = plan.render().cpu().numpy()
+    loss, g_cpu, rs_cpu = port.silhouette_loss_grad(
+        sc.pos0, sc.faces_f, sc.mvps, targets, res, sc.radius_px, sc.sigma,
+        want_rs=True, threads=THREADS)
+    assert np.array_equal(bits(rs), bits(rs_cpu)), "RasterizeSoft images"
+    plan.step(1)
+    np.testing.assert_allclose(plan.download(N.SLOT_GRAD).reshape(-1, 3),
+                               g_cpu, **TOL)
+    assert plan.loss() == pytest.approx(loss, rel=1e-5)
+    assert plan.status() == 0
+
+
+def test_c4_full_size_first_step(cuda, port):
+    """C4 at its configured size: 64 views at 1024^2, 8 stochastic edge
+    samples per face, the example's AA regulariser 0.5 / 0.5."""
+    from opendressi_b200 import _native as N
+    from opendressi_b200.plans import AaSilhouettePlan
+
+    sc = scene.silhouette_scene(level=5, n_views=64, res=1024, seed=0)
+    plan = AaSilhouettePlan.from_scene(sc, n_samples=8, laplacian=0.5,
+                                       normal=0.5)
+    plan.upload(N.SLOT_PARAM, sc.pos0)
+    plan.render_targets(sc.target_pos)
+    targets = plan.download(N.SLOT_TARGET).reshape(64, 1024, 1024)
+    t_cpu = port.aa_targets(sc.target_pos, sc.faces_f, sc.mvps, 1024)
+    assert np.array_equal(bits(targets), bits(t_cpu))
+    vft = port.vertex_faces_tex(sc.faces_f, sc.n_verts)
+    loss, g_cpu, _ = port.aa_silhouette_loss_grad(
+        sc.pos0, sc.faces_f, vft, sc.mvps, targets, 1024, 8, 0.0,
+        threads=THREADS)
+    plan.step(1)
+    g = plan.download(N.SLOT_GRAD).reshape(-1, 3)
+    np.testing.assert_allclose(g, g_cpu, **TOL)
+    assert np.abs(g_cpu).max() > 1e-5
+    assert plan.loss() == pytest.approx(loss, rel=1e-5)
+    p, _ = _adam_regularised(port, sc.pos0, np.zeros_like(g), np.zeros_like(g),
+                             0.0, g, sc.faces_f, 0.5, 0.5, sc.lr)
+    assert np.array_equal(bits(plan.download(N.SLOT_PARAM).reshape(-1, 3)),
+                          bits(p))
+    assert plan.status() == 0
+
+
+def test_c5_full_size_first_step(cuda, port):
+    """C5 at its configured size: icosphere-6, 32 views at 1024^2, 1024^2
+    maps, the 512x256 environment with 6 prefilter levels and the 256^2 x
+    512-sample BRDF LUT; the loss and the first gradient of [albedo | mr |
+    env] against the restatement on the same G-buffers."""
+    from opendressi_b200 import _native as N
+    from opendressi_b200.plans import PbrPlan
+
+    sc = scene.pbr_scene()
+    plan = PbrPlan.from_scene(sc)
+    plan.render_targets(sc.albedo_gt, sc.mr_gt, sc.env_gt)
+    targets = plan.download(N.SLOT_TARGET).reshape(sc.n_views, sc.res,
+                                                   sc.res, 3)
+    plan.upload(N.SLOT_PARAM, plan.pack(sc.albedo0, sc.mr0, sc.env0))
+    plan.step(1)
+    lut = port.brdf_lut(256, 256, 512)
+    ones = np.ones((sc.n_verts, 1), np.float32)
+    uvh = np.concatenate([sc.uv, ones, 0 * ones], 1)
+
+    def view(v):
+        clip = port.transform_clip(sc.pos, sc.mvps[v])
+        g_uvh = port.rasterize_hard(clip, uvh, sc.faces_f, sc.res, sc.res)
+        gp = port.rasterize_hard(clip, sc.pos, sc.faces_f, sc.res, sc.res)
+        frame = np.concatenate([sc.frames[v], sc.light]).astype(np.float32)
+        ga = np.zeros_like(sc.albedo0)
+        gm = np.zeros_like(sc.mr0)
+        ge = np.zeros_like(sc.env0)
+        _, lv = port.pbr_view_grad(gp, gp, np.ascontiguousarray(g_uvh[..., 2]),
+                                   np.ascontiguousarray(g_uvh[..., :2]),
+                                   sc.albedo0, sc.mr0, frame, sc.env0,
+                                   sc.levels, lut, targets[v], 1, ga, gm, ge)
+        return lv, ga, gm, ge
+
+    parts = _pmap(view, range(sc.n_views))
+    loss = sum(p[0] for p in parts)
+    grads = [sum(p[k] for p in parts) for k in (1, 2, 3)]
+    assert plan.loss() == pytest.approx(loss, rel=1e-3)
+    for got, exp in zip(plan.unpack(plan.download(N.SLOT_GRAD)), grads):
+        np.testing.assert_allclose(got, exp, **TOL)
+    assert plan.status() == 0

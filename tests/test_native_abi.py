@@ -92,3 +92,18 @@ def test_mesh_tables_host_builders_match_oracle(port):
         ops.vertex_faces_tex(np.array([[0, 1, 5]], np.float32), 3)
     with pytest.raises(N.DressiError, match="above cap"):
         ops.vertex_neighbors_tex(cases[1][0], cases[1][1], cap=3)
+
+
+@pytest.mark.parametrize("name", ["dressi_rasterize_face_id",
+                                  "dressi_rasterize_face_id_noalloc"])
+def test_face_id_rejects_counts_above_int_max(name):
+    """Face or vertex counts above INT_MAX are argument errors, reported
+    before any CUDA call (the pointers are never dereferenced)."""
+    lib = N.load()
+    fake = C.c_void_p(256)
+    big = 2**31
+    for nv, nf in ((3, big), (big, 1)):
+        rc = getattr(lib, name)(fake, nv, fake, nf, 1, 8, 8, fake, None,
+                                fake, None)
+        assert rc == N.ERR_INVALID
+        assert "INT_MAX" in N.last_error()

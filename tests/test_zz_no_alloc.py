@@ -50,7 +50,7 @@ def _bits(a):
 
 
 @pytest.mark.parametrize("case", ["random", "sphere"])
-def test_noalloc_matches_allocating_entry(cuda, case):
+def test_noalloc_matches_allocating_entry(cuda, port, case):
     if case == "random":
         clip, faces = S.random_triangles(71, 300, 96, spread=1.1,
                                          w_range=(0.2, 3.0))
@@ -69,6 +69,10 @@ def test_noalloc_matches_allocating_entry(cuda, case):
                     w, h)
     ref = res["dressi_rasterize_face_id"][0]
     assert (ref[0] > 0).any()
+    # and both against the C restatement of RasterizeFaceId
+    for v in range(views):
+        exp = port.rasterize_face_id(clip[v], faces, w, h)
+        assert np.array_equal(_bits(ref[0][v]), _bits(exp)), f"view {v}"
     for k, (out, depth, st) in enumerate(res["dressi_rasterize_face_id_noalloc"]):
         assert np.array_equal(_bits(out), _bits(ref[0])), f"face id, call {k}"
         assert np.array_equal(_bits(depth), _bits(ref[1])), f"depth, call {k}"
