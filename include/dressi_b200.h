@@ -571,6 +571,131 @@ int dressi_plan_profile(dressi_plan p, uint32_t n_iters, void* stream,
 
 int dressi_plan_destroy(dressi_plan p);
 
+/* ------------------------------------------------------------------------
+ * Graph path: Variables, F:: ops, BuildBackward and DressiAD
+ *
+ * Replaces (unclearness/opendressi):
+ *  - Variable handles, VType, ImgSize     include/dressi/variable.h:18-49,
+ *                                         include/dressi/types.h:12-33
+ *  - the F:: op library                    include/dressi/f.h:12-317
+ *  - DressiAD (setLossVar, setOptimizer, addUpdate, markOutput,
+ *    setGradOutputsEnabled, inputGrads, setRebuildCounts, execStep,
+ *    sendImg, recvImg)                     include/dressi/dressi_ad.h:44-131
+ *  - BuildBackward, the packer and the Vulkan executor behind execStep
+ *                                         src/core/build_backward.cpp:62-149,
+ *                                         src/pack/greedy_packer.cpp:388-586,
+ *                                         src/vk/executor.h:43-66
+ * A graph is built on the host from Variable handles; execStep lowers it
+ * (reverse graph, optimizer graph, fusion of the pixel-wise ops into pixel
+ * programs, reductions and rendering kernels) into one CUDA graph on the
+ * DressiAD's device and replays it. Values are float images [h][w][ncomp]
+ * (integer VTypes hold their values as floats, as the reference's CPU
+ * tensors do). Host-only calls (graph building) need no GPU.
+ * --------------------------------------------------------------------- */
+
+/* VType values: the reference's enumeration order. */
+#define DRESSI_VT_FLOAT 0
+#define DRESSI_VT_VEC2 1
+#define DRESSI_VT_VEC3 2
+#define DRESSI_VT_VEC4 3
+#define DRESSI_VT_MAT2 4
+#define DRESSI_VT_MAT3 5
+#define DRESSI_VT_MAT4 6
+#define DRESSI_VT_INT 7
+#define DRESSI_VT_IVEC2 8
+#define DRESSI_VT_IVEC3 9
+#define DRESSI_VT_IVEC4 10
+#define DRESSI_VT_UINT 11
+
+/* A reference to a graph Variable. Every handle returned by the library is
+ * owned by the caller and released with dressi_var_release; the Variable
+ * lives while a handle, a graph node consuming it or a DressiAD holds it. */
+typedef struct dressi_var_s* dressi_var;
+typedef struct dressi_ad_s* dressi_ad;
+
+/* Variable(VType, ImgSize) (variable.h:20): a leaf image of w x h. */
+int dressi_var_create(int vtype, uint32_t w, uint32_t h, dressi_var* out);
+/* A second handle to the same Variable. */
+int dressi_var_clone(dressi_var v, dressi_var* out);
+int dressi_var_release(dressi_var v);
+/* Type, size, creation id, and whether an op computes it (1) or it is a
+ * leaf (0); any output pointer may be NULL. */
+int dressi_var_info(dressi_var v, int* vtype, uint32_t* w, uint32_t* h,
+                    uint64_t* id, int* computed);
+/* setRequiresGrad / setRequiresGradRecursively (recursive = 1: the
+ * Variable and everything computed from it so far). */
+int dressi_var_set_requires_grad(dressi_var v, int req, int recursive);
+int dressi_var_requires_grad(dressi_var v, int* req);
+/* setDirty / setDirtyRecursively (the reactive cache's change marks). */
+int dressi_var_set_dirty(dressi_var v, int dirty, int recursive);
+
+/* Any F:: op by its reference name ("Add", "Sigmoid", "RasterizeSoft",
+ * "Mean", "Vec3", "GetX", ...) over inputs xs, with its float parameters
+ * (constants, radius_px, roughness) and integer parameters (image sizes as
+ * (w, h), n_samples, corner, offsets). Argument errors (types, sizes,
+ * counts) are DRESSI_ERR_INVALID with the reference's message. */
+int dressi_op(const char* name, const dressi_var* xs, uint32_t n_xs,
+              const float* fparams, uint32_t n_f, const int64_t* iparams,
+              uint32_t n_i, dressi_var* out);
+
+/* DressiAD::Optimizer: given the requires-grad leaves xs and their
+ * gradients gxs (handles borrowed for the call), write one new handle per
+ * input into out (the library takes them over); return 0 on success. The
+ * callback may call dressi_ad_add_update for optimizer state. */
+typedef int (*dressi_optimizer_fn)(void* user, const dressi_var* xs,
+                                   const dressi_var* gxs, uint32_t n,
+                                   dressi_var* out);
+
+int dressi_ad_create(int device, dressi_ad* out);
+int dressi_ad_destroy(dressi_ad ad);
+int dressi_ad_set_loss(dressi_ad ad, dressi_var loss);
+int dressi_ad_set_optimizer(dressi_ad ad, dressi_optimizer_fn fn, void* user);
+int dressi_ad_add_update(dressi_ad ad, dressi_var input_leaf,
+                         dressi_var updated);
+int dressi_ad_mark_output(dressi_ad ad, dressi_var v);
+int dressi_ad_set_grad_outputs(dressi_ad ad, int enable);
+/* setRebuildCounts: stable iterations before the reactive re-plan that
+ * prunes cached static branches (0 disables that trigger). */
+int dressi_ad_set_rebuild_counts(dressi_ad ad, uint32_t fast, uint32_t full);
+/* Upper bound on the ops fused into one pixel program (default 512; 1 =
+ * one kernel per op, the reference's Naive packing mode). */
+int dressi_ad_set_max_fusion(dressi_ad ad, uint32_t max_ops);
+/* inputGrads(): up to cap (leaf, gradient) pairs as new handles; *n gets
+ * the total. Valid after the first exec_step. */
+int dressi_ad_input_grads(dressi_ad ad, dressi_var* xs, dressi_var* gxs,
+                          uint32_t cap, uint32_t* n);
+/* execStep(): (re)builds when needed, then replays the iteration's CUDA
+ * graph on `stream` (asynchronous). */
+int dressi_ad_exec_step(dressi_ad ad, void* stream);
+/* sendImg / recvImg: n_floats = w * h * ncomp; host (on_device = 0,
+ * synchronous) or device pointers (asynchronous on `stream`). A send marks
+ * the Variable dirty. recv needs a Variable with a device image: a root
+ * (loss, optimizer outputs, markOutput, gradients when enabled) or an
+ * input of any step. */
+int dressi_ad_send(dressi_ad ad, dressi_var v, const float* data,
+                   size_t n_floats, int on_device, void* stream);
+int dressi_ad_recv(dressi_ad ad, dressi_var v, float* data, size_t n_floats,
+                   int on_device, void* stream);
+
+typedef struct {
+    uint32_t n_funcs;          /* ops of the full graph (getFuncCount) */
+    uint32_t n_exec_funcs;     /* ops executed per iteration after pruning */
+    uint32_t n_steps;          /* lowered steps (programs + kernels) */
+    uint32_t n_programs;       /* fused pixel programs */
+    uint32_t n_fused_ops;      /* ops inside the programs */
+    uint32_t n_program_instructions;
+    uint32_t max_program_regs;
+    uint32_t n_materialized;   /* values with a device image */
+    uint32_t kernels_per_iter; /* kernel nodes of the CUDA graph */
+    uint32_t rebuilds;
+    uint32_t pruning_active;
+} dressi_ad_stats_t;
+
+int dressi_ad_stats(dressi_ad ad, dressi_ad_stats_t* out);
+/* Device status word (DRESSI_STATUS_* bits) accumulated by the graph's
+ * kernels; synchronises the device; clear = 1 resets it. */
+int dressi_ad_status(dressi_ad ad, uint32_t* word, int clear);
+
 #ifdef __cplusplus
 }
 #endif

@@ -197,7 +197,47 @@ SIGNATURES = {
                                       C.POINTER(C.c_char_p), _fp,
                                       C.POINTER(_u32), C.POINTER(_u32)]),
     "dressi_plan_destroy": (C.c_int, [_vp]),
+    # graph path
+    "dressi_var_create": (C.c_int, [C.c_int, _u32, _u32, C.POINTER(_vp)]),
+    "dressi_var_clone": (C.c_int, [_vp, C.POINTER(_vp)]),
+    "dressi_var_release": (C.c_int, [_vp]),
+    "dressi_var_info": (C.c_int, [_vp, C.POINTER(C.c_int), C.POINTER(_u32),
+                                  C.POINTER(_u32), C.POINTER(C.c_uint64),
+                                  C.POINTER(C.c_int)]),
+    "dressi_var_set_requires_grad": (C.c_int, [_vp, C.c_int, C.c_int]),
+    "dressi_var_requires_grad": (C.c_int, [_vp, C.POINTER(C.c_int)]),
+    "dressi_var_set_dirty": (C.c_int, [_vp, C.c_int, C.c_int]),
+    "dressi_op": (C.c_int, [C.c_char_p, C.POINTER(_vp), _u32,
+                            C.POINTER(C.c_float), _u32,
+                            C.POINTER(C.c_int64), _u32, C.POINTER(_vp)]),
+    "dressi_ad_create": (C.c_int, [C.c_int, C.POINTER(_vp)]),
+    "dressi_ad_destroy": (C.c_int, [_vp]),
+    "dressi_ad_set_loss": (C.c_int, [_vp, _vp]),
+    "dressi_ad_set_optimizer": (C.c_int, [_vp, _vp, _vp]),
+    "dressi_ad_add_update": (C.c_int, [_vp, _vp, _vp]),
+    "dressi_ad_mark_output": (C.c_int, [_vp, _vp]),
+    "dressi_ad_set_grad_outputs": (C.c_int, [_vp, C.c_int]),
+    "dressi_ad_set_rebuild_counts": (C.c_int, [_vp, _u32, _u32]),
+    "dressi_ad_set_max_fusion": (C.c_int, [_vp, _u32]),
+    "dressi_ad_input_grads": (C.c_int, [_vp, C.POINTER(_vp), C.POINTER(_vp),
+                                        _u32, C.POINTER(_u32)]),
+    "dressi_ad_exec_step": (C.c_int, [_vp, _vp]),
+    "dressi_ad_send": (C.c_int, [_vp, _vp, _vp, C.c_size_t, C.c_int, _vp]),
+    "dressi_ad_recv": (C.c_int, [_vp, _vp, _vp, C.c_size_t, C.c_int, _vp]),
+    "dressi_ad_stats": (C.c_int, [_vp, _vp]),
+    "dressi_ad_status": (C.c_int, [_vp, C.POINTER(_u32), C.c_int]),
 }
+
+# DressiAD::Optimizer through the C ABI (dressi_optimizer_fn)
+OPTIMIZER_FN = C.CFUNCTYPE(C.c_int, _vp, C.POINTER(_vp), C.POINTER(_vp), _u32,
+                           C.POINTER(_vp))
+
+
+class AdStats(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in (
+        "n_funcs", "n_exec_funcs", "n_steps", "n_programs", "n_fused_ops",
+        "n_program_instructions", "max_program_regs", "n_materialized",
+        "kernels_per_iter", "rebuilds", "pruning_active")]
 
 
 class DressiError(RuntimeError):

@@ -22,8 +22,10 @@ LIB = os.path.join(HERE, "libdressi_b200.so")
 SOURCES = ["capi.cu", "soft_raster.cu", "silhouette.cu", "hard_raster.cu",
            "fit.cu", "noalloc.cu",
            "antialias.cu", "texture.cu", "interp.cu", "regularize.cu",
-           "ibl.cu", "pbr.cu", "faces.cu", "paper.cu", "paper_pixel.cu"]
-HEADERS = ["common.h", "exact.cuh", "kernels.h", "raster_soft.cuh"]
+           "ibl.cu", "pbr.cu", "faces.cu", "paper.cu", "paper_pixel.cu",
+           "graph_ops.cpp", "graph_exec.cu", "graph_ad.cu"]
+HEADERS = ["common.h", "exact.cuh", "kernels.h", "raster_soft.cuh",
+           "graph.h", "graph_exec.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -74,7 +76,7 @@ def build(force: bool = False, verbose: bool = False, jobs: int = 8) -> str:
     os.makedirs(obj_dir, exist_ok=True)
     objs, procs = [], []
     for src in SOURCES:
-        obj = os.path.join(obj_dir, src.replace(".cu", ".o"))
+        obj = os.path.join(obj_dir, os.path.splitext(src)[0] + ".o")
         objs.append(obj)
         cmd = [nvcc(), *flags_for(src), "-c", os.path.join(CSRC, src), "-o",
                obj]

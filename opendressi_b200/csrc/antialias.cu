@@ -466,12 +466,15 @@ __device__ __forceinline__ void aa_sample(const AaDims& d, int v,
 __global__ void k_aa_bwd_vtx_vft(AaDims d, const AaFace* frs, const float* gy,
                                  const float* img, const float* tri,
                                  const float4* clip, const float* vft,
-                                 int max_deg, uint32_t seed_u, int n_samples,
+                                 int max_deg, uint32_t seed_u,
+                                 const float* seed_dev, int n_samples,
                                  float* grad) {
     const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     const int v = blockIdx.y;
     const long long total = (long long)d.n_verts * max_deg * n_samples;
     if (i >= total) return;
+    // seed from device memory (an in-graph {1,1} value) when given
+    if (seed_dev) seed_u = x86_u32_via_i64(seed_dev[0] + 0.5f);
     const int smp = int(i % n_samples);
     const long long vd = i / n_samples;
     const int u = int(vd % d.n_verts);
@@ -566,7 +569,7 @@ void aa_bwd_img_op(const AaDims& d, const AaFace* fr, const float* gy,
 void aa_bwd_vtx_op(const AaDims& d, const AaFace* fr, const float* gy,
                    const float* img, const float* tri, const float* clip,
                    const float* vft, int max_deg, float seed, int n_samples,
-                   float* grad, cudaStream_t s) {
+                   float* grad, cudaStream_t s, const float* seed_dev) {
     ProfScope ps("aa_bwd_vtx", s);
     const float4* c4 = reinterpret_cast<const float4*>(clip);
     if (n_samples == 0) {
@@ -578,7 +581,7 @@ void aa_bwd_vtx_op(const AaDims& d, const AaFace* fr, const float* gy,
         const uint32_t seed_u = x86_u32_via_i64(seed + 0.5f);
         k_aa_bwd_vtx_vft<<<dim3(unsigned((total + 255) / 256), d.views), 256,
                            0, s>>>(d, fr, gy, img, tri, c4, vft, max_deg,
-                                   seed_u, n_samples, grad);
+                                   seed_u, seed_dev, n_samples, grad);
     }
     check_launch();
 }

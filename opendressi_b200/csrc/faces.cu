@@ -77,10 +77,12 @@ __global__ void k_face_fetch_bwd(const float* gy, int n, const float* idx,
                                  int w, int h, const float4* prj0,
                                  const float4* prj1, const float4* prj2,
                                  int n_faces, uint32_t seed_u,
-                                 float radius_px, int n_samples,
-                                 float* out) {
+                                 const float* seed_dev, float radius_px,
+                                 int n_samples, float* out) {
     const int f = blockIdx.x * blockDim.x + threadIdx.x;
     if (f >= n_faces) return;
+    // seed from device memory (an in-graph {1,1} value) when given
+    if (seed_dev) seed_u = x86_u32_via_i64(seed_dev[0] + 0.5f);
     const float4 c4[3] = {prj0[f], prj1[f], prj2[f]};
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     float s[3][2];
@@ -186,14 +188,16 @@ void face_fetch_op(const float* attr, int n_faces, int n, const float* idx,
 void face_fetch_bwd_op(const float* gy, int n, const float* idx, int w, int h,
                        const float* prj0, const float* prj1, const float* prj2,
                        int n_faces, float seed, float radius_px,
-                       int n_samples, float* out, cudaStream_t s) {
+                       int n_samples, float* out, cudaStream_t s,
+                       const float* seed_dev) {
     ProfScope ps("face_fetch_bwd", s);
     if (n_faces == 0) return;
     k_face_fetch_bwd<<<blocks_for(n_faces), kThreads, 0, s>>>(
             gy, n, idx, w, h, reinterpret_cast<const float4*>(prj0),
             reinterpret_cast<const float4*>(prj1),
             reinterpret_cast<const float4*>(prj2), n_faces,
-            x86_u32_via_i64(seed + 0.5f), radius_px, n_samples, out);
+            x86_u32_via_i64(seed + 0.5f), seed_dev, radius_px, n_samples,
+            out);
     check_launch();
 }
 

@@ -385,10 +385,12 @@ void aa_bwd_img_op(const AaDims& d, const AaFace* fr, const float* gy,
                    const float* tri, float* out, cudaStream_t s);
 // grad [views][V][4] += d(sum gy * aa)/d clip; n_samples 0 = exact scan,
 // else stochastic over vft [max_deg][V] seeded by `seed`.
+// seed_dev (nullable): read the seed from device memory instead of `seed`.
 void aa_bwd_vtx_op(const AaDims& d, const AaFace* fr, const float* gy,
                    const float* img, const float* tri, const float* clip,
                    const float* vft, int max_deg, float seed, int n_samples,
-                   float* grad, cudaStream_t s);
+                   float* grad, cudaStream_t s,
+                   const float* seed_dev = nullptr);
 
 // --- AA silhouette (C4): hard raster + AntiAlias + stochastic vertex
 // gradient, sharing the HardSoftRas plan's transform, gradient reduction
@@ -488,7 +490,8 @@ void face_fetch_op(const float* attr, int n_faces, int n, const float* idx,
 void face_fetch_bwd_op(const float* gy, int n, const float* idx, int w, int h,
                        const float* prj0, const float* prj1, const float* prj2,
                        int n_faces, float seed, float radius_px,
-                       int n_samples, float* out, cudaStream_t s);
+                       int n_samples, float* out, cudaStream_t s,
+                       const float* seed_dev = nullptr);
 
 // --- C5 PBR material + environment optimisation (pbr.cu) ---
 constexpr int kPbrThreads = 512;

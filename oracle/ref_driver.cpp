@@ -18,7 +18,10 @@
 #include <cstdint>
 #include <cstring>
 #include <exception>
+#include <map>
 #include <memory>
+#include <cctype>
+#include <cstdlib>
 #include <string>
 #include <thread>
 #include <vector>
@@ -1263,3 +1266,243 @@ int ref_vertex_faces_tex(const float* faces, uint32_t n_faces,
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------
+// Generic graph programs: the same op list the library's graph path builds
+// (tests/graph_programs.py writes it), built here with the reference's own
+// F:: API, differentiated by its BuildBackward and evaluated by its
+// CpuEvaluator. One item per line:
+//   leaf <id> <vtype> <w> <h> <requires_grad 0|1>
+//   op <id> <Name> <n_in> <in ids> <n_f> <floats> <n_i> <ints>
+//   loss <id>                 the Variable BuildBackward differentiates
+//   grad <id> <leaf id>       that leaf's gradient Variable (after `loss`)
+//   eval <id>                 a value to return, in order
+// leaf_data: the leaves' images concatenated in declaration order; out:
+// the evaluated images concatenated in `eval` order.
+namespace {
+
+Variable RefNamedOp(const std::string& name, const Variables& xs,
+                    const std::vector<float>& fp,
+                    const std::vector<long long>& ip) {
+    auto S = [&](size_t i) {
+        return ImgSize{uint32_t(ip.at(i)), uint32_t(ip.at(i + 1))};
+    };
+    if (name == "Float") return F::Float(fp.at(0));
+    if (name == "Vec2")
+        return xs.empty() ? F::Vec2(fp.at(0), fp.at(1))
+                          : F::Vec2(xs.at(0), xs.at(1));
+    if (name == "Vec3") {
+        if (xs.empty()) return F::Vec3(fp.at(0), fp.at(1), fp.at(2));
+        if (xs.size() == 2) return F::Vec3(xs[0], xs[1]);
+        return F::Vec3(xs.at(0), xs.at(1), xs.at(2));
+    }
+    if (name == "Vec4") {
+        if (xs.empty()) return F::Vec4(fp.at(0), fp.at(1), fp.at(2), fp.at(3));
+        if (xs.size() == 2) return F::Vec4(xs[0], xs[1]);
+        return F::Vec4(xs.at(0), xs.at(1), xs.at(2), xs.at(3));
+    }
+    if (name == "Add") return F::Add(xs.at(0), xs.at(1));
+    if (name == "Sub") return F::Sub(xs.at(0), xs.at(1));
+    if (name == "Mul") return F::Mul(xs.at(0), xs.at(1));
+    if (name == "Div") return F::Div(xs.at(0), xs.at(1));
+    if (name == "Neg") return F::Neg(xs.at(0));
+    if (name == "Sin") return F::Sin(xs.at(0));
+    if (name == "Cos") return F::Cos(xs.at(0));
+    if (name == "Tan") return F::Tan(xs.at(0));
+    if (name == "Asin") return F::Asin(xs.at(0));
+    if (name == "Acos") return F::Acos(xs.at(0));
+    if (name == "Atan") return F::Atan(xs.at(0));
+    if (name == "Atan2") return F::Atan2(xs.at(0), xs.at(1));
+    if (name == "Exp") return F::Exp(xs.at(0));
+    if (name == "Exp2") return F::Exp2(xs.at(0));
+    if (name == "Log") return F::Log(xs.at(0));
+    if (name == "Log2") return F::Log2(xs.at(0));
+    if (name == "Sqrt") return F::Sqrt(xs.at(0));
+    if (name == "InverseSqrt") return F::InverseSqrt(xs.at(0));
+    if (name == "Abs") return F::Abs(xs.at(0));
+    if (name == "Sign") return F::Sign(xs.at(0));
+    if (name == "Floor") return F::Floor(xs.at(0));
+    if (name == "Fract") return F::Fract(xs.at(0));
+    if (name == "Mod") return F::Mod(xs.at(0), xs.at(1));
+    if (name == "Pow") return F::Pow(xs.at(0), xs.at(1));
+    if (name == "Max") return F::Max(xs.at(0), xs.at(1));
+    if (name == "Min") return F::Min(xs.at(0), xs.at(1));
+    if (name == "Clamp") return F::Clamp(xs.at(0), xs.at(1), xs.at(2));
+    if (name == "Mix") return F::Mix(xs.at(0), xs.at(1), xs.at(2));
+    if (name == "Step") return F::Step(xs.at(0), xs.at(1));
+    if (name == "SmoothStep")
+        return F::SmoothStep(xs.at(0), xs.at(1), xs.at(2));
+    if (name == "Sigmoid") return F::Sigmoid(xs.at(0));
+    if (name == "Less") return F::Less(xs.at(0), xs.at(1));
+    if (name == "LessEqual") return F::LessEqual(xs.at(0), xs.at(1));
+    if (name == "Greater") return F::Greater(xs.at(0), xs.at(1));
+    if (name == "GreaterEqual") return F::GreaterEqual(xs.at(0), xs.at(1));
+    if (name == "GetX") return F::GetX(xs.at(0));
+    if (name == "GetY") return F::GetY(xs.at(0));
+    if (name == "GetZ") return F::GetZ(xs.at(0));
+    if (name == "GetW") return F::GetW(xs.at(0));
+    if (name == "Dot") return F::Dot(xs.at(0), xs.at(1));
+    if (name == "Cross") return F::Cross(xs.at(0), xs.at(1));
+    if (name == "Length") return F::Length(xs.at(0));
+    if (name == "Distance") return F::Distance(xs.at(0), xs.at(1));
+    if (name == "Normalize") return F::Normalize(xs.at(0));
+    if (name == "Reflect") return F::Reflect(xs.at(0), xs.at(1));
+    if (name == "CompSum") return F::CompSum(xs.at(0));
+    if (name == "MatMul") return F::MatMul(xs.at(0), xs.at(1));
+    if (name == "Transpose") return F::Transpose(xs.at(0));
+    if (name == "OuterProduct") return F::OuterProduct(xs.at(0), xs.at(1));
+    if (name == "SumPixelWise") return F::SumPixelWise(xs);
+    if (name == "Sum") return F::Sum(xs.at(0));
+    if (name == "Mean") return F::Mean(xs.at(0));
+    if (name == "SumAll") return F::SumAll(xs.at(0));
+    if (name == "Broadcast") return F::Broadcast(xs.at(0), S(0));
+    if (name == "StopGradient") return F::StopGradient(xs.at(0));
+    if (name == "SetFragDepth") return F::SetFragDepth(xs.at(0));
+    if (name == "ScreenCoord") return F::ScreenCoord(S(0));
+    if (name == "Rasterize")
+        return F::Rasterize(xs.at(0), xs.at(1), xs.at(2), S(0));
+    if (name == "RasterizeFaceId")
+        return F::RasterizeFaceId(xs.at(0), xs.at(1), xs.at(2), S(0));
+    if (name == "RasterizeSoft") {
+        if (xs.size() == 7)
+            return F::RasterizeSoft(xs[0], xs[1], xs[2], xs[3], xs[4], xs[5],
+                                    xs[6], S(0), fp.at(0));
+        return F::RasterizeSoft(xs.at(0), xs.at(1), xs.at(2), xs.at(3),
+                                xs.at(4), xs.at(5), S(0), fp.at(0));
+    }
+    if (name == "SoftClip")
+        return F::SoftClip(xs.at(0), xs.at(1), S(0), fp.at(0));
+    if (name == "AntiAlias")
+        return F::AntiAlias(xs.at(0), xs.at(1), xs.at(2), xs.at(3), xs.at(4),
+                            xs.at(5), ip.empty() ? 8u : uint32_t(ip[0]));
+    if (name == "VertexNeighborMean")
+        return F::VertexNeighborMean(xs.at(0), xs.at(1));
+    if (name == "NormalConsistencyFaceTerm")
+        return F::NormalConsistencyFaceTerm(xs.at(0), xs.at(1), xs.at(2));
+    if (name == "NormalConsistencyVertexGrad")
+        return F::NormalConsistencyVertexGrad(xs.at(0), xs.at(1), xs.at(2),
+                                              xs.at(3));
+    if (name == "LookupFaces")
+        return F::LookupFaces(xs.at(0), xs.at(1), xs.at(2),
+                              uint32_t(ip.at(0)));
+    if (name == "FaceFetch")
+        return F::FaceFetch(xs.at(0), xs.at(1), xs.at(2), xs.at(3), xs.at(4),
+                            xs.at(5), fp.at(0),
+                            ip.empty() ? 4u : uint32_t(ip[0]));
+    if (name == "Texture") return F::Texture(xs.at(0), xs.at(1), xs.at(2));
+    if (name == "TextureBilinear")
+        return F::TextureBilinear(xs.at(0), xs.at(1), xs.at(2));
+    if (name == "EquirectSample") return F::EquirectSample(xs.at(0), xs.at(1));
+    if (name == "IrradianceConv") return F::IrradianceConv(xs.at(0), S(0));
+    if (name == "PrefilterConv")
+        return F::PrefilterConv(xs.at(0), S(0), fp.at(0));
+    if (name == "BrdfIntegrationLut")
+        return F::BrdfIntegrationLut(S(0),
+                                     ip.size() > 2 ? uint32_t(ip[2]) : 512u);
+    if (name == "AvgPool2x2") return F::AvgPool2x2(xs.at(0));
+    if (name == "PixelFetch")
+        return F::PixelFetch(xs.at(0), uint32_t(ip.at(0)), xs.at(1));
+    if (name == "TileFetch")
+        return F::TileFetch(xs.at(0), xs.at(1), uint32_t(ip.at(0)));
+    DRESSI_CHECK(false, "ref_graph_eval: unknown op " + name);
+    return nullptr;
+}
+
+}  // namespace
+
+// Whitespace tokenizer of the program text (no iostreams: their locale
+// facets are not safe to use from every host process that loads this
+// library).
+struct Tokens {
+    const char* p;
+    bool next(std::string* out) {
+        while (*p && std::isspace(static_cast<unsigned char>(*p))) p++;
+        if (!*p) return false;
+        const char* b = p;
+        while (*p && !std::isspace(static_cast<unsigned char>(*p))) p++;
+        out->assign(b, p);
+        return true;
+    }
+    std::string str() {
+        std::string t;
+        DRESSI_CHECK(next(&t), "ref_graph_eval: truncated program");
+        return t;
+    }
+    long long i64() { return std::strtoll(str().c_str(), nullptr, 10); }
+    float f32() { return std::strtof(str().c_str(), nullptr); }
+};
+
+extern "C" int ref_graph_eval(const char* program, const float* leaf_data,
+                              float* out) {
+    return Guard([&] {
+        std::map<long long, Variable> vars;
+        std::vector<Variable> leaves, evals;
+        Variable loss(nullptr);
+        std::map<Variable, Variable> grads;
+        bool have_grads = false;
+        Tokens in{program};
+        std::string kind;
+        while (in.next(&kind)) {
+            if (kind == "leaf") {
+                const long long id = in.i64();
+                const int vt = int(in.i64());
+                const uint32_t w = uint32_t(in.i64());
+                const uint32_t h = uint32_t(in.i64());
+                const int rg = int(in.i64());
+                Variable v(VType(vt), {w, h});
+                if (rg) v.setRequiresGrad(true);
+                vars[id] = v;
+                leaves.push_back(v);
+            } else if (kind == "op") {
+                const long long id = in.i64();
+                const std::string name = in.str();
+                size_t n = size_t(in.i64());
+                Variables xs(n);
+                for (auto& x : xs) x = vars.at(in.i64());
+                std::vector<float> fp(size_t(in.i64()));
+                for (auto& f : fp) f = in.f32();
+                std::vector<long long> ip(size_t(in.i64()));
+                for (auto& i : ip) i = in.i64();
+                vars[id] = RefNamedOp(name, xs, fp, ip);
+            } else if (kind == "loss") {
+                loss = vars.at(in.i64());
+            } else if (kind == "grad") {
+                const long long id = in.i64();
+                const long long leaf = in.i64();
+                DRESSI_CHECK(loss, "ref_graph_eval: grad before loss");
+                if (!have_grads) {
+                    // requires-grad marks reach everything computed so far
+                    for (auto& l : leaves)
+                        if (l.getRequiresGrad())
+                            l.setRequiresGradRecursively(true);
+                    auto [xs, gxs] = BuildBackward(loss);
+                    for (size_t i = 0; i < xs.size(); i++)
+                        grads[xs[i]] = gxs[i];
+                    have_grads = true;
+                }
+                auto it = grads.find(vars.at(leaf));
+                DRESSI_CHECK(it != grads.end(),
+                             "ref_graph_eval: leaf without gradient");
+                vars[id] = it->second;
+            } else if (kind == "eval") {
+                evals.push_back(vars.at(in.i64()));
+            } else {
+                DRESSI_CHECK(false, "ref_graph_eval: bad line " + kind);
+            }
+        }
+        CpuEvaluator ev;
+        size_t off = 0;
+        for (auto& l : leaves) {
+            const size_t n = size_t(l.getImgSize().w) * l.getImgSize().h *
+                             NumComponents(l.getVType());
+            ev.bind(l, Tensor(l.getVType(), l.getImgSize(), leaf_data + off));
+            off += n;
+        }
+        size_t o = 0;
+        for (auto& e : evals) {
+            CpuTensor t = ev.eval(e);
+            CopyOut(t, out + o);
+            o += t.data.size();
+        }
+    });
+}
