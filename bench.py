@@ -65,7 +65,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c2", "c3", "c3p", "c4", "c5"],
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c3p", "c4",
+                                         "c5"],
                     default="c3",
                     help="c3p: C3 on the paper's HardSoftRas path (FaceFetch "
                          "backward, --peels layers)")
@@ -85,14 +86,19 @@ def parse():
     ap.add_argument("--normal", type=float, default=None)
     ap.add_argument("--level", type=int, default=5)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--path", choices=["plan", "graph"], default="plan",
+                    help="plan: the hand-fused plan (default); graph: the "
+                         "same workload built with the F:: graph API and run "
+                         "by DressiAD (fusion planner + CUDA-graph executor); "
+                         "c1 and c3, one GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     if args.views is None:
-        args.views = {"c2": 8, "c3": 16, "c3p": 16, "c4": 64,
+        args.views = {"c1": 1, "c2": 8, "c3": 16, "c3p": 16, "c4": 64,
                       "c5": 32}[args.config]
     if args.res is None:
-        args.res = 512 if args.config == "c2" else 1024
+        args.res = {"c1": 256, "c2": 512}.get(args.config, 1024)
     if args.config == "c2" and args.level == 5:
         args.level = 4  # C2's mesh is icosphere-4
     if args.config == "c5" and args.level == 5:
@@ -579,6 +585,83 @@ def run_ours(args):
     return out
 
 
+def run_graph(args):
+    """The workload built with the graph API (opendressi_b200.examples) and
+    run by DressiAD: the generic path's fusion plan and its CUDA graph,
+    timed like the plan (CUDA events around `steps` exec_step calls)."""
+    import torch
+
+    from opendressi_b200 import _native as N
+    from opendressi_b200 import examples, scene
+    from opendressi_b200 import graph as G
+    from opendressi_b200.plans import SilhouettePlan
+
+    if args.config not in ("c1", "c3") or args.gpus != 1:
+        raise SystemExit("--path graph: configs c1 and c3 on one GPU")
+    torch.cuda.set_device(0)
+    N.load()
+    ad = G.DressiAD(0)
+    if args.config == "c1":
+        p0, t0 = scene.image_fit_scene(args.seed, args.res, args.res)
+        p, tg, loss = examples.image_fit(ad, args.res, args.res, lr=1e-2)
+        ad.mark_output(loss)
+        ad.send_img(p, p0)
+        ad.send_img(tg, t0)
+        alg = 112.0 * args.res * args.res
+        workload_ = {"workload": "C1 image fit (256^2 x 4, Mean L2, Adam) "
+                                 "fwd+bwd+Adam", "res": args.res, "lr": 1e-2}
+    else:
+        sc = scene.silhouette_scene(level=args.level, n_views=args.views,
+                                    res=args.res, seed=args.seed)
+        tp = SilhouettePlan.from_scene(sc)
+        tp.upload(N.SLOT_PARAM, sc.pos0)
+        tp.render_targets(sc.target_pos)
+        targets = tp.download(N.SLOT_TARGET).reshape(args.views, args.res,
+                                                     args.res)
+        tp.close()
+        sg = examples.SilhouetteGraph(ad, sc.faces_f, sc.n_verts, sc.mvps,
+                                      args.res, sc.radius_px, sc.sigma, sc.lr,
+                                      args.laplacian, args.normal)
+        sg.send_static(targets)
+        ad.send_img(sg.pos, sc.pos0)
+        alg = iteration_bytes(args.views, args.res, sc.n_verts, sc.n_faces,
+                              reg=args.laplacian != 0.0 or args.normal != 0.0)
+        workload_ = workload(args)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        ad.exec_step(stream)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(0)
+    clocks.start()
+    t0_ = torch.cuda.Event(enable_timing=True)
+    t1_ = torch.cuda.Event(enable_timing=True)
+    t0_.record(stream)
+    for _ in range(args.steps):
+        ad.exec_step(stream)
+    t1_.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0_.elapsed_time(t1_) / args.steps
+    st = ad.stats()
+    peak, peak_kind = peaks()
+    achieved = alg / (ms * 1e-3) / 1e9
+    return {
+        "metric": METRIC, "value": 1e3 / ms, "unit": "iterations/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": DATA.get(args.config,
+                                                                "synthetic"),
+        "config": dict(workload_, path="graph (F:: graph, DressiAD fusion "
+                                       "planner, one CUDA graph)"),
+        "gpu_launches": int(st["kernels_per_iter"]) * args.steps,
+        "graph": st, "clocks": clk, "device_status": ad.status(),
+        "roofline": {"bound": "hbm", "kernel": "iteration (one CUDA graph)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_kind,
+                     "alg_bytes_per_launch": alg, "avg_ms": ms},
+    }
+
+
 # -------------------------------------------------------- CPU baselines
 
 class PbrCpuSample:
@@ -838,6 +921,10 @@ def main():
         out = run_reference(args)
         if out is not None:
             print(json.dumps(out), flush=True)
+        return
+    if args.path == "graph":
+        out = run_graph(args)
+        print(json.dumps(out), flush=True)
         return
     out = run_ours(args)
     if rank == 0 and out is not None:

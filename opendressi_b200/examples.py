@@ -1,15 +1,17 @@
-"""Test helper: the benchmark workloads written as graphs with the library's
-graph API (opendressi_b200.graph), composed as the reference's examples
-compose them (examples/silhouette_optimization/run.cpp:228-437,
-examples/image_fitting) -- the F:: forward, BuildBackward inside
+"""The benchmark workloads written as graphs with the graph API
+(opendressi_b200.graph), composed as the reference's examples compose them
+(examples/silhouette_optimization/run.cpp:228-437, examples/image_fitting of
+unclearness/opendressi): the F:: forward, BuildBackward inside
 DressiAD.exec_step, and the in-graph Adam of the optimizer callback with
-its state kept on the device through add_update."""
+its state kept on the device through add_update. The fused plans
+(opendressi_b200.plans) compute the same iterations with hand-fused
+kernels."""
 
 from __future__ import annotations
 
 import numpy as np
 
-from opendressi_b200 import graph as G
+from . import graph as G
 
 f = G.f
 VT = G.VType

@@ -12,8 +12,8 @@ steps 1e-3 rel."""
 import numpy as np
 import pytest
 
-import graph_models as gm
 import graph_programs as gp
+from opendressi_b200 import examples as gm
 from opendressi_b200 import graph as G
 from opendressi_b200 import scene
 
