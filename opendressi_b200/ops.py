@@ -64,17 +64,56 @@ def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
+# Index errors the reference throws from inside its CPU kernels are bits of
+# a device status word here. Every op ORs into one persistent word per
+# device instead of reading its own back, so an op never waits for the GPU;
+# check_status() synchronises once and raises for every op since the last
+# check. set_eager_checks(True) restores a check after every op.
+_words: dict = {}
+_eager = False
+
+
+def set_eager_checks(on: bool) -> None:
+    """Check the status word (synchronising) after every op when on."""
+    global _eager
+    _eager = bool(on)
+
+
+def status_word(device=None) -> torch.Tensor:
+    """The device's accumulated status word (an int32 CUDA tensor)."""
+    dev = torch.device(device) if device is not None else torch.device(
+        "cuda", torch.cuda.current_device())
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    w = _words.get(key)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=f"cuda:{key}")
+        _words[key] = w
+    return w
+
+
 def _new_status(device):
-    return torch.zeros(1, dtype=torch.int32, device=device)
+    return status_word(device)
 
 
-def check_status(status: torch.Tensor) -> int:
-    """Synchronises and raises if a kernel reported an index error."""
-    word = int(status.item()) & 0xFFFFFFFF
+def check_status(device=None, reset: bool = True) -> int:
+    """Synchronises with `device` (a device, a tensor on it, or None for
+    the current device) and raises DressiError if a kernel reported an
+    index error since the last check; reset clears the word."""
+    if isinstance(device, torch.Tensor):
+        device = device.device
+    w = status_word(device)
+    word = int(w.item()) & 0xFFFFFFFF
+    if reset and word:
+        w.zero_()
     if word & N.STATUS_INDEX_RANGE:
         raise N.DressiError(N.ERR_DEVICE,
                             "index out of range (face or vertex id)")
     return word
+
+
+def _after(status: torch.Tensor) -> None:
+    if _eager:
+        check_status(status.device)
 
 
 def _views(t: torch.Tensor, base_dims: int) -> tuple[torch.Tensor, int]:
@@ -109,7 +148,7 @@ def soft_clip(clip, faces, width: int, height: int, radius_px: float,
            faces.data_ptr(), n_faces, views, width, height, float(radius_px),
            out.data_ptr(), st.data_ptr(), _stream())
     if check:
-        check_status(st)
+        _after(st)
     return out[0] if squeeze else out
 
 
@@ -147,7 +186,7 @@ def rasterize_soft(soft_clip, face_id, faces_soft, hard_clip, faces_tex,
            views, width, height, float(radius_px), _ptr(prev_depth),
            out.data_ptr(), st.data_ptr(), _stream())
     if check:
-        check_status(st)
+        _after(st)
     return out[0] if squeeze else out
 
 
@@ -171,7 +210,7 @@ def rasterize_soft_grad(gy, rs, clip, faces, check: bool = True):
            clip.data_ptr(), clip.shape[1], faces.data_ptr(), faces.shape[0],
            views, w, h, grad.data_ptr(), st.data_ptr(), _stream())
     if check:
-        check_status(st)
+        _after(st)
     return grad[0] if squeeze else grad
 
 
@@ -190,7 +229,7 @@ def rasterize_face_id(clip, faces, width: int, height: int,
            faces.data_ptr(), faces.shape[0], views, width, height,
            out.data_ptr(), _ptr(depth), st.data_ptr(), _stream())
     if check:
-        check_status(st)
+        _after(st)
     if squeeze:
         out = out[0]
         depth = depth[0] if depth is not None else None
@@ -216,7 +255,7 @@ def rasterize(clip, attr, faces, width: int, height: int, check: bool = True):
            attr.data_ptr(), n_comp, faces.data_ptr(), faces.shape[0], views,
            width, height, out.data_ptr(), st.data_ptr(), _stream())
     if check:
-        check_status(st)
+        _after(st)
     return out[0] if squeeze else out
 
 
@@ -254,7 +293,7 @@ def antialias(img, tri, clip, faces, check: bool = True):
            clip.data_ptr(), clip.shape[1], faces.data_ptr(), faces.shape[0],
            views, w, h, out.data_ptr(), st.data_ptr(), _stream())
     if check:
-        check_status(st)
+        _after(st)
     return out.reshape(shape)
 
 
@@ -288,7 +327,7 @@ def antialias_grad(gy, img, tri, clip, faces, vft=None, seed: float = 0.0,
            faces.shape[0], _ptr(vft_t), max_deg, float(seed), int(n_samples),
            views, w, h, _ptr(gi), _ptr(gc), st.data_ptr(), _stream())
     if check:
-        check_status(st)
+        _after(st)
     if gi is not None:
         gi = gi.reshape(shape)
     if gc is not None and squeeze:
@@ -389,7 +428,7 @@ def vertex_neighbor_mean(pos, nbrs, check: bool = True):
            nbrs.data_ptr(), nbrs.shape[0], out.data_ptr(), st.data_ptr(),
            _stream())
     if check:
-        check_status(st)
+        _after(st)
     return out
 
 
@@ -405,7 +444,7 @@ def normal_consistency_face_term(pos, faces, face_adj, check: bool = True):
            pos.shape[0], faces.data_ptr(), faces.shape[0],
            face_adj.data_ptr(), out.data_ptr(), st.data_ptr(), _stream())
     if check:
-        check_status(st)
+        _after(st)
     return out
 
 
@@ -424,7 +463,7 @@ def normal_consistency_vertex_grad(term, pos, faces, vtx_faces,
            vtx_faces.data_ptr(), vtx_faces.shape[0], out.data_ptr(),
            st.data_ptr(), _stream())
     if check:
-        check_status(st)
+        _after(st)
     return out
 
 
@@ -467,7 +506,7 @@ def regularized_grad(pos, faces, g, laplacian: float, normal: float,
            g.data_ptr(), float(laplacian), float(normal), out.data_ptr(),
            st.data_ptr(), _stream())
     if check:
-        check_status(st)
+        _after(st)
     return out
 
 
@@ -621,7 +660,7 @@ def lookup_faces(attr, faces, corner: int, check: bool = True):
            attr.shape[1], faces.data_ptr(), nf, corner, out.data_ptr(),
            st.data_ptr(), _stream())
     if check:
-        check_status(st)
+        _after(st)
     return out
 
 
@@ -640,7 +679,7 @@ def lookup_faces_grad(gy, faces, vertex_faces, corner: int,
            faces.data_ptr(), faces.shape[0], vf.data_ptr(), nv, md, corner,
            out.data_ptr(), st.data_ptr(), _stream())
     if check:
-        check_status(st)
+        _after(st)
     return out
 
 

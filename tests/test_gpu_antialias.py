@@ -137,6 +137,7 @@ def test_antialias_index_error(cuda):
     with pytest.raises(DressiError):
         ops.antialias(torch.zeros((16, 16), device=cuda), tri,
                       T(clip, cuda), T(bad, cuda))
+        ops.check_status()
 
 
 @pytest.mark.parametrize("wild", [False, True])

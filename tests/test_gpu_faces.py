@@ -93,8 +93,10 @@ def test_index_out_of_range_reports_status(cuda, port):
     attr = np.ones((sc.n_verts, 2), np.float32)
     with pytest.raises(N.DressiError, match="out of range"):
         ops.lookup_faces(T(attr, cuda), T(faces, cuda), 1)
+        ops.check_status()
     vf = port.vertex_faces_tex(sc.faces_f, sc.n_verts)
     vf[0, 0] = float(sc.n_faces + 2)
     with pytest.raises(N.DressiError, match="out of range"):
         ops.lookup_faces_grad(T(np.ones((sc.n_faces, 2), np.float32), cuda),
                               T(sc.faces_f, cuda), T(vf, cuda), 0)
+        ops.check_status()

@@ -162,8 +162,10 @@ def test_empty_mesh_and_index_errors(cuda, port):
     bad[2, 1] = 1e6  # vertex index out of range: the reference throws
     with pytest.raises(DressiError):
         ops.rasterize_face_id(T(clip, cuda), T(bad, cuda), 16, 16)
+        ops.check_status()
     with pytest.raises(DressiError):
         ops.soft_clip(T(clip, cuda), T(bad, cuda), 16, 16, 2.0)
+        ops.check_status()
 
 
 @pytest.mark.parametrize("spill_cap", [None, "0"])

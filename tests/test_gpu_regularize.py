@@ -95,11 +95,13 @@ def test_table_index_out_of_range_reports_status(cuda):
     vn[0, 5] = float(pos.shape[0] + 10)   # read would be out of range
     with pytest.raises(N.DressiError, match="out of range"):
         ops.vertex_neighbor_mean(T(pos, cuda), T(vn, cuda))
+        ops.check_status()
     fa = ops.face_neighbors_tex(f)
     fa[3, 0] = 1e7
     with pytest.raises(N.DressiError, match="out of range"):
         ops.normal_consistency_face_term(T(pos, cuda), T(f, cuda),
                                          T(fa, cuda))
+        ops.check_status()
 
 
 def _targets(port, sc):

@@ -225,3 +225,93 @@ def test_antialias_silhouette_optimisation_runs(cuda):
         opt.step()
         losses.append(float(loss.detach()))
     assert losses[-1] < 0.7 * losses[0]
+
+
+def test_ops_under_torch_compile_and_no_sync(cuda):
+    """The ops are torch.library custom ops with fake implementations: a
+    function using them compiles with torch.compile (graph breaks allowed
+    around the mesh-table lookups) and gives the eager results, forward and
+    backward. No op reads the device status back: check_status() is the one
+    synchronisation."""
+    import torch
+    from opendressi_b200 import torch_api as dr
+
+    pos, tri, _ = _mesh_pos(11, level=3, res=64)
+    ctx = dr.RasterizeContext()
+    tt = torch.tensor(tri, device=cuda)
+    target = torch.rand((1, 64, 64, 1), device=cuda)
+
+    def loss_fn(p):
+        rast, _ = dr.rasterize(ctx, p, tt, (64, 64))
+        ones = torch.ones((p.shape[-2], 1), device=cuda)
+        mask, _ = dr.interpolate(ones, rast, tt)
+        aa = dr.antialias(mask, rast, p, tt, n_samples=0)
+        soft = dr.rasterize_soft(ctx, p, tt, (64, 64), radius_px=2.0)
+        return ((aa - target) ** 2).mean() + 1e-3 * soft[..., 0].mean()
+
+    p1 = torch.tensor(pos, device=cuda, requires_grad=True)
+    l1 = loss_fn(p1)
+    l1.backward()
+    compiled = torch.compile(loss_fn, fullgraph=False)
+    p2 = torch.tensor(pos, device=cuda, requires_grad=True)
+    l2 = compiled(p2)
+    l2.backward()
+    assert torch.equal(l1.detach(), l2.detach())
+    torch.testing.assert_close(p2.grad, p1.grad, atol=1e-5, rtol=1e-4)
+    assert dr.check_status() == 0
+    # the ops are registered custom ops with fake kernels
+    assert hasattr(torch.ops.dressi_b200, "rasterize")
+    assert hasattr(torch.ops.dressi_b200, "antialias_grad")
+
+
+def test_mesh_cache_pins_tri(cuda, port):
+    """A tri tensor freed and replaced by another of the same shape must not
+    hit the cached tables of the first (the cache keeps the first alive)."""
+    import torch
+    from opendressi_b200 import torch_api as dr
+
+    pos, tri, _ = _mesh_pos(13)
+    ctx = dr.RasterizeContext()
+    pt = torch.tensor(pos, device=cuda)
+    t1 = torch.tensor(tri, device=cuda)
+    r1, _ = dr.rasterize(ctx, pt, t1, (48, 48))
+    ptr1 = t1.data_ptr()
+    del t1
+    tri2 = tri[:, [0, 2, 1]].copy()            # same shape, other faces
+    tri2[: tri.shape[0] // 2] = tri2[: tri.shape[0] // 2][::-1]
+    t2 = torch.tensor(tri2, device=cuda)
+    r2, _ = dr.rasterize(ctx, pt, t2, (48, 48))
+    assert t2.data_ptr() != ptr1
+    ref2 = _rast_ref(port, pos, tri2, 48, 48)
+    assert np.array_equal(bits(npy(r2[0])), bits(ref2))
+    ctx.clear_cache()
+
+
+def test_ops_run_on_the_inputs_device():
+    """Inputs on a device other than the current one: the ops run there (on
+    that device's current stream), with no peer access involved."""
+    import torch
+    from opendressi_b200 import torch_api as dr
+
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    from opendressi_b200 import _native
+
+    _native.load()
+    pos, tri, _ = _mesh_pos(15)
+    ctx = dr.RasterizeContext()
+    outs = []
+    for dev in ("cuda:0", "cuda:1"):
+        torch.cuda.set_device(0)
+        p = torch.tensor(pos, device=dev, requires_grad=True)
+        t = torch.tensor(tri, device=dev)
+        rast, _ = dr.rasterize(ctx, p, t, (40, 40))
+        mask, _ = dr.interpolate(torch.ones((pos.shape[0], 1), device=dev),
+                                 rast, t)
+        out = dr.antialias(mask, rast, p, t, n_samples=0)
+        out.sum().backward()
+        assert out.device == torch.device(dev) and p.grad.device == out.device
+        outs.append((npy(out), npy(p.grad)))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    np.testing.assert_allclose(outs[0][1], outs[1][1], atol=1e-5)
+    assert dr.check_status("cuda:1") == 0
