@@ -436,7 +436,9 @@ def run_ours(args):
         param0, n_param = sc.pos0, sc.n_verts * 3
     stream = torch.cuda.current_stream()
 
-    sharded = ShardedStep(plan) if world > 1 else None
+    # N > 1: phase 0, the NCCL all-reduce and phase 1 captured as one CUDA
+    # graph, replayed once per iteration
+    sharded = ShardedStep(plan, graph=True) if world > 1 else None
 
     def step():
         if world == 1:
@@ -556,6 +558,11 @@ def run_ours(args):
         "kernels_ms_per_iter": per_iter,
     }
 
+    # per-phase split (uncaptured, CUDA events): the parts a strong-scaling
+    # run divides (forward + backward of the local views) and those it does
+    # not (the all-reduce, the replicated regulariser scale and Adam)
+    phase_ms = (sharded if sharded is not None
+                else ShardedStep(plan)).phase_times(5)
     status = plan.status()
     out = None
     if rank == 0:
@@ -577,8 +584,10 @@ def run_ours(args):
             "gpu_launches": int(round(launches_per_iter * args.steps)),
             "loss_last": loss, "device_status": status,
             "clocks": clk, "e2e": e2e, "roofline": roofline,
+            "phase_ms": phase_ms,
         }
     if world > 1:
+        sharded.close()
         plan.close()
         dist.barrier()
         dist.destroy_process_group()

@@ -549,6 +549,14 @@ int dressi_plan_exec(dressi_plan p, uint32_t n_iters, void* stream);
  *  phase 1: Adam from the GRAD slot (after the caller all-reduced it). */
 int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream);
 
+/* The same phase with its kernels launched directly on `stream` instead of
+ * as the plan's own CUDA graph, so that a stream capture the caller runs
+ * records them: phase 0, the caller's collective on the GRAD slot and phase
+ * 1 then replay as ONE graph (no host round trip per iteration). Make the
+ * first call outside capture. Within the caller's graph the bins do not
+ * grow after an overflow; the overflow path stays exact. */
+int dressi_plan_record_phase(dressi_plan p, int phase, void* stream);
+
 /* Silhouette plans: forward pass writing the RASTER slot (no update). */
 int dressi_plan_render(dressi_plan p, void* stream);
 

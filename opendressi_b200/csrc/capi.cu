@@ -1717,6 +1717,20 @@ int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream) {
     });
 }
 
+int dressi_plan_record_phase(dressi_plan p, int phase, void* stream) {
+    return guarded([&] {
+        DRESSI_REQUIRE(p, "null plan");
+        DRESSI_REQUIRE(p->kind != dressi_plan_s::kFit,
+                       "record_phase: not a silhouette or texture plan");
+        DRESSI_REQUIRE(phase == 0 || phase == 1,
+                       "record_phase: phase is 0 or 1");
+        DeviceGuard dg(p->device);
+        // the phase's kernels go straight onto the stream, so a capture the
+        // caller runs on it (with its collective in between) records them
+        p->record_phase(phase, as_stream(stream));
+    });
+}
+
 int dressi_plan_render(dressi_plan p, void* stream) {
     return guarded([&] {
         DRESSI_REQUIRE(p, "null plan");

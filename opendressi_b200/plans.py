@@ -107,6 +107,13 @@ class Plan:
     def step(self, n_iters: int = 1, stream=None):
         N.call("dressi_plan_exec", self._h, int(n_iters), _stream_ptr(stream))
 
+    def record_phase(self, phase: int, stream=None):
+        """Launches phase 0 (forward + backward into GRAD) or 1 (the update)
+        directly on the stream, so that a CUDA-graph capture running there
+        records it (dressi_plan_record_phase)."""
+        N.call("dressi_plan_record_phase", self._h, int(phase),
+               _stream_ptr(stream))
+
     def status(self, stream=None) -> int:
         w = C.c_uint32(0)
         N.call("dressi_plan_status", self._h, C.byref(w), _stream_ptr(stream))

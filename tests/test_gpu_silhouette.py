@@ -200,3 +200,33 @@ def test_bins_grow_after_overflow(cuda, port, monkeypatch):
                                              sc.sigma, 1e-2, 8)
     np.testing.assert_allclose(plan.loss_history(8), trace_cpu, rtol=1e-3)
     assert plan.status() & N.STATUS_BIN_OVERFLOW
+
+
+def test_captured_sharded_step_matches_fused(cuda, port):
+    """ShardedStep(graph=True): phase 0, the (here world-1, absent)
+    collective and phase 1 captured into one CUDA graph by torch through
+    dressi_plan_record_phase, replayed per iteration: the same positions
+    as the plan's own fused iteration."""
+    import torch
+    from opendressi_b200 import _native as N
+    from opendressi_b200.distributed import ShardedStep
+    from opendressi_b200.plans import SilhouettePlan
+
+    sc = scene.silhouette_scene(level=3, n_views=3, res=96, seed=8)
+    targets = _targets(port, sc)
+    plans = []
+    for _ in range(2):
+        p = SilhouettePlan.from_scene(sc, lr=1e-2, laplacian=0.15,
+                                      normal=0.4)
+        p.upload(N.SLOT_PARAM, sc.pos0)
+        p.upload(N.SLOT_TARGET, targets)
+        plans.append(p)
+    step = ShardedStep(plans[1], graph=True)
+    for _ in range(5):
+        plans[0].step(1)
+        step()
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(plans[1].download(N.SLOT_PARAM),
+                               plans[0].download(N.SLOT_PARAM), atol=1e-5)
+    assert step._graph is not None
+    step.close()
