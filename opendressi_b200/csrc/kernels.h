@@ -58,6 +58,9 @@ struct SoftBuffers {
     FixedBins bin2{};          // rim-phase bins per 8x4 block
     int2* state = nullptr;     // packed survivors [views * W * H]
     uint8_t* active = nullptr; // open flag per 8x4 block [views*n_tiles*8]
+    // summed-area table of the open blocks per 16x16 tile, with a zero
+    // first row and column: [views][(tiles_y + 1) * (tiles_x + 1)]
+    int* sat = nullptr;
     int* rim = nullptr;        // rim-possible flags [views * rim_cells]
     uint32_t* status = nullptr;
 };

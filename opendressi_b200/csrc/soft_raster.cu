@@ -42,6 +42,7 @@ void carve_soft_main(Arena& a, const SoftDims& d, SoftBuffers* b) {
     b->recs = a.take<FaceRec>(size_t(d.views) * std::max(d.n_faces, 1));
     b->state = a.take<int2>(size_t(d.views) * d.W * d.H);
     b->active = a.take<uint8_t>(vt * 8);
+    b->sat = a.take<int>(size_t(d.views) * (d.tiles_x + 1) * (d.tiles_y + 1));
     b->rim = a.take<int>(size_t(d.views) * std::max(d.rim_cells, 1));
     b->status = a.take<uint32_t>(4);
 }
@@ -173,10 +174,15 @@ static void check_launch() { DRESSI_CUDA(cudaGetLastError()); }
 
 void soft_rim_bins(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
     if (d.n_faces == 0) return;
-    const dim3 fg((d.n_faces + 7) / 8, d.views);  // one warp per face
     ProfScope ps("rim_bin", s);
-    k_rim_bin<<<fg, 256, 0, s>>>(d.n_faces, d.n_tiles, d.tiles_x, b.recs,
-                                 b.active, b.bin2, b.bin1);
+    // per view: which tiles hold open blocks, as a summed-area table
+    k_open_sat<<<d.views, 512, 0, s>>>(d.n_tiles, d.tiles_x, d.tiles_y,
+                                       b.active, b.sat);
+    check_launch();
+    // one thread per face for the filter, then its warp per kept face
+    const dim3 fg((d.n_faces + 255) / 256, d.views);
+    k_rim_bin<<<fg, 256, 0, s>>>(d.n_faces, d.n_tiles, d.tiles_x, d.tiles_y,
+                                 b.recs, b.active, b.sat, b.bin2, b.bin1);
     check_launch();
 }
 
