@@ -61,6 +61,8 @@ struct SoftBuffers {
     // summed-area table of the open blocks per 16x16 tile, with a zero
     // first row and column: [views][(tiles_y + 1) * (tiles_x + 1)]
     int* sat = nullptr;
+    int* kept = nullptr;    // faces near an open block [views][n_faces]
+    int* kept_n = nullptr;  // their count per view [views]
     int* rim = nullptr;        // rim-possible flags [views * rim_cells]
     uint32_t* status = nullptr;
 };

@@ -1099,10 +1099,13 @@ __device__ __forceinline__ bool tri_touches_block(const FaceRec& r, int bx,
 // Summed-area table of the open blocks per 16x16 tile of one view (block
 // = view): sat[(ty + 1) (tiles_x + 1) + tx + 1] = the open blocks of the
 // tiles (0..tx, 0..ty); row 0 and column 0 are zero. Rows are prefix-summed
-// by one thread each, then columns.
+// by one thread each, then columns. Also zeroes the view's count of faces
+// kept for the rim binning.
 static __global__ void k_open_sat(int n_tiles, int tiles_x, int tiles_y,
-                                  const uint8_t* active, int* sat_all) {
+                                  const uint8_t* active, int* sat_all,
+                                  int* kept_n) {
     const int v = blockIdx.x;
+    if (threadIdx.x == 0) kept_n[v] = 0;
     const int w1 = tiles_x + 1;
     int* sat = sat_all + size_t(v) * w1 * (tiles_y + 1);
     const uint8_t* act = active + size_t(v) * n_tiles * 8;
@@ -1129,18 +1132,16 @@ static __global__ void k_open_sat(int n_tiles, int tiles_x, int tiles_y,
     }
 }
 
-// Rim-phase binning: a safe face enters the bin of every open 8x4 block its
-// soft triangle may touch. One thread per face first asks the view's
-// summed-area table whether any tile under the face's soft bbox holds an
-// open block (most faces lie away from every open block and stop there);
-// the warp then takes its kept faces one at a time, lanes striding over the
-// blocks of the face's soft bbox.
-static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
-                                 int tiles_y, const FaceRec* recs_all,
-                                 const uint8_t* active, const int* sat_all,
-                                 FixedBins b2, FixedBins1 b1) {
-    // sweep 1 has consumed the sweep-1 bins, the spill list and the parked
-    // tiles: reset them for the next use
+// Rim-phase face filter: one thread per face asks the view's summed-area
+// table whether any tile under the face's soft bbox holds an open block
+// (most faces lie away from every open block); the kept faces of a view are
+// appended to its list. Also resets what sweep 1 consumed (the sweep-1
+// bins, the spill list and the parked tiles) and the rim order counters.
+static __global__ void k_rim_filter(int n_faces, int n_tiles, int tiles_x,
+                                    int tiles_y, const FaceRec* recs_all,
+                                    const int* sat_all, int* kept_all,
+                                    int* kept_n, FixedBins b2,
+                                    FixedBins1 b1) {
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
         *b1.spill_n = 0;
         *b1.parked_n = 0;
@@ -1149,15 +1150,12 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n_tiles;
          t += gridDim.x * blockDim.x)
         b1.cursor[size_t(blockIdx.y) * n_tiles + t] = 0;
-    const int lane = threadIdx.x & 31;
     const int v = blockIdx.y;
-    const int f_me = blockIdx.x * blockDim.x + threadIdx.x;
-    const int f0 = f_me - lane;
-    const FaceRec* recs = recs_all + size_t(v) * n_faces;
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t need = kFaceValid | kFaceSafe;
     bool keep = false;
-    if (f_me < n_faces) {
-        const FaceRec& r = recs[f_me];
+    if (f < n_faces) {
+        const FaceRec& r = recs_all[size_t(v) * n_faces + f];
         if ((r.flags & need) == need && r.bx0 <= r.bx1 && r.by0 <= r.by1) {
             const int w1 = tiles_x + 1;
             const int* sat = sat_all + size_t(v) * w1 * (tiles_y + 1);
@@ -1168,31 +1166,48 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
             keep = open > 0;
         }
     }
-    unsigned todo = __ballot_sync(0xffffffffu, keep);
+    // warp-aggregated append
+    const unsigned m = __ballot_sync(0xffffffffu, keep);
+    const int lane = threadIdx.x & 31;
+    int base = 0;
+    if (lane == 0 && m) base = atomicAdd(&kept_n[v], __popc(m));
+    base = __shfl_sync(0xffffffffu, base, 0);
+    if (keep)
+        kept_all[size_t(v) * n_faces + base +
+                 __popc(m & ((1u << lane) - 1u))] = f;
+}
+
+// Rim-phase binning: a kept face enters the bin of every open 8x4 block its
+// soft triangle may touch. One warp per kept face, lanes striding over the
+// blocks of its soft bbox.
+static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
+                                 const FaceRec* recs_all,
+                                 const uint8_t* active, const int* kept_all,
+                                 const int* kept_n, FixedBins b2) {
+    const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int v = blockIdx.y;
+    if (i >= kept_n[v]) return;
+    const int f = kept_all[size_t(v) * n_faces + i];
+    const FaceRec& r = recs_all[size_t(v) * n_faces + f];
     const int blocks_x = tiles_x * 2;
     const uint8_t* act = active + size_t(v) * n_tiles * 8;
     const size_t bin0 = size_t(v) * n_tiles * 8;
     // lanes tile the block range 8 wide x 4 tall (no integer division)
     const int lx = lane & 7, ly = lane >> 3;
-    while (todo) {
-        const int f = f0 + __ffs(todo) - 1;
-        todo &= todo - 1;
-        const FaceRec& r = recs[f];
-        for (int by = (r.by0 >> 2) + ly; by <= (r.by1 >> 2); by += 4) {
-            for (int bx = (r.bx0 >> 3) + lx; bx <= (r.bx1 >> 3); bx += 8) {
-                if (!act[((by >> 2) * tiles_x + (bx >> 1)) * 8 +
-                         (by & 3) * 2 + (bx & 1)])
-                    continue;
-                if (!tri_touches_block(r, bx, by)) continue;
-                const size_t bin = bin0 + size_t(by) * blocks_x + bx;
-                const int slot = atomicAdd(&b2.cursor[bin], 1);
-                if (slot < b2.cap) {
-                    b2.list[bin * b2.cap + slot] = f;
-                } else {
-                    const int sp = atomicAdd(b2.spill_n, 1);
-                    if (sp < b2.spill_cap)
-                        b2.spill[sp] = make_int2(int(bin), f);
-                }
+    for (int by = (r.by0 >> 2) + ly; by <= (r.by1 >> 2); by += 4) {
+        for (int bx = (r.bx0 >> 3) + lx; bx <= (r.bx1 >> 3); bx += 8) {
+            if (!act[((by >> 2) * tiles_x + (bx >> 1)) * 8 + (by & 3) * 2 +
+                     (bx & 1)])
+                continue;
+            if (!tri_touches_block(r, bx, by)) continue;
+            const size_t bin = bin0 + size_t(by) * blocks_x + bx;
+            const int slot = atomicAdd(&b2.cursor[bin], 1);
+            if (slot < b2.cap) {
+                b2.list[bin * b2.cap + slot] = f;
+            } else {
+                const int sp = atomicAdd(b2.spill_n, 1);
+                if (sp < b2.spill_cap) b2.spill[sp] = make_int2(int(bin), f);
             }
         }
     }

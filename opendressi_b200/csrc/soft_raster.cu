@@ -43,6 +43,8 @@ void carve_soft_main(Arena& a, const SoftDims& d, SoftBuffers* b) {
     b->state = a.take<int2>(size_t(d.views) * d.W * d.H);
     b->active = a.take<uint8_t>(vt * 8);
     b->sat = a.take<int>(size_t(d.views) * (d.tiles_x + 1) * (d.tiles_y + 1));
+    b->kept = a.take<int>(size_t(d.views) * std::max(d.n_faces, 1));
+    b->kept_n = a.take<int>(size_t(d.views));
     b->rim = a.take<int>(size_t(d.views) * std::max(d.rim_cells, 1));
     b->status = a.take<uint32_t>(4);
 }
@@ -177,12 +179,18 @@ void soft_rim_bins(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
     ProfScope ps("rim_bin", s);
     // per view: which tiles hold open blocks, as a summed-area table
     k_open_sat<<<d.views, 512, 0, s>>>(d.n_tiles, d.tiles_x, d.tiles_y,
-                                       b.active, b.sat);
+                                       b.active, b.sat, b.kept_n);
     check_launch();
-    // one thread per face for the filter, then its warp per kept face
-    const dim3 fg((d.n_faces + 255) / 256, d.views);
-    k_rim_bin<<<fg, 256, 0, s>>>(d.n_faces, d.n_tiles, d.tiles_x, d.tiles_y,
-                                 b.recs, b.active, b.sat, b.bin2, b.bin1);
+    // one thread per face keeps the faces near an open block ...
+    const dim3 tg((d.n_faces + 255) / 256, d.views);
+    k_rim_filter<<<tg, 256, 0, s>>>(d.n_faces, d.n_tiles, d.tiles_x,
+                                    d.tiles_y, b.recs, b.sat, b.kept,
+                                    b.kept_n, b.bin2, b.bin1);
+    check_launch();
+    // ... and one warp per kept face bins it (warps past the count exit)
+    const dim3 fg((d.n_faces + 7) / 8, d.views);
+    k_rim_bin<<<fg, 256, 0, s>>>(d.n_faces, d.n_tiles, d.tiles_x, b.recs,
+                                 b.active, b.kept, b.kept_n, b.bin2);
     check_launch();
 }
 
