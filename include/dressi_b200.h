@@ -557,6 +557,17 @@ int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream);
  * grow after an overflow; the overflow path stays exact. */
 int dressi_plan_record_phase(dressi_plan p, int phase, void* stream);
 
+/* Deterministic gradient mode of a HardSoftRas silhouette plan (on = 1):
+ * instead of float atomics per pixel, the iteration stores each pixel's
+ * (survivor face, dL/d dist), sums each face's corner partials over its
+ * pixels in row-major order and each vertex's over its incident faces in
+ * the order of the vertex -> face table -- the order of the reference's
+ * GatherDistGrad + ColSum -- so that repeated runs give bit-identical
+ * gradients and positions. Costs extra passes (one thread per face scans
+ * its soft bbox) and [views][R][R] float2 + [views][F][3] float4 of device
+ * memory. Re-captures the plan's graphs. */
+int dressi_plan_set_deterministic(dressi_plan p, int on);
+
 /* Silhouette plans: forward pass writing the RASTER slot (no update). */
 int dressi_plan_render(dressi_plan p, void* stream);
 

@@ -191,6 +191,7 @@ SIGNATURES = {
     "dressi_plan_exec": (C.c_int, [_vp, _u32, _vp]),
     "dressi_plan_exec_phase": (C.c_int, [_vp, C.c_int, _vp]),
     "dressi_plan_record_phase": (C.c_int, [_vp, C.c_int, _vp]),
+    "dressi_plan_set_deterministic": (C.c_int, [_vp, C.c_int]),
     "dressi_plan_render": (C.c_int, [_vp, _vp]),
     "dressi_plan_status": (C.c_int, [_vp, C.POINTER(_u32), _vp]),
     "dressi_plan_launches_per_iter": (C.c_int, [_vp, C.POINTER(_u32)]),

@@ -179,6 +179,7 @@ struct dressi_plan_s {
     uint32_t kernels_per_iter = 0;
     // silhouette bins live in their own allocation so they can grow
     void* bins_mem = nullptr;
+    void* det_mem = nullptr;  // deterministic-mode buffers (b.det_*)
     uint32_t* ovf_host = nullptr;  // pinned: overflow bits of the last
                                    // replayed iteration (written by the graph)
 
@@ -355,6 +356,7 @@ struct dressi_plan_s {
         // the render slot is allocated on first use
         if (slots[DRESSI_SLOT_RASTER].ptr) cudaFree(slots[DRESSI_SLOT_RASTER].ptr);
         if (ovf_host) cudaFreeHost(ovf_host);
+        if (det_mem) cudaFree(det_mem);
         if (prev >= 0) cudaSetDevice(prev);
     }
 };
@@ -1714,6 +1716,56 @@ int dressi_plan_exec_phase(dressi_plan p, int phase, void* stream) {
             p->grow_bins_if_needed(s);
         p->ensure_phase_graph(phase);
         DRESSI_CUDA(cudaGraphLaunch(p->phase_exec[phase], s));
+    });
+}
+
+int dressi_plan_set_deterministic(dressi_plan p, int on) {
+    return guarded([&] {
+        DRESSI_REQUIRE(p, "null plan");
+        DRESSI_REQUIRE(p->kind == dressi_plan_s::kSil && !p->p.paper,
+                       "set_deterministic: HardSoftRas silhouette plans only");
+        DeviceGuard dg(p->device);
+        DRESSI_CUDA(cudaDeviceSynchronize());
+        if (p->exec) {
+            cudaGraphExecDestroy(p->exec);
+            p->exec = nullptr;
+        }
+        for (auto& g : p->phase_exec) {
+            if (g) cudaGraphExecDestroy(g);
+            g = nullptr;
+        }
+        SilBuffers& b = p->b;
+        if (!on) {
+            if (p->det_mem) cudaFree(p->det_mem);
+            p->det_mem = nullptr;
+            b.det_pix = nullptr;
+            b.det_part = nullptr;
+            b.det_vf = nullptr;
+            b.det_vf_deg = 0;
+            return;
+        }
+        if (p->det_mem) return;
+        const SilParams& sp = p->p;
+        std::vector<float> faces(size_t(sp.n_faces) * 3);
+        DRESSI_CUDA(cudaMemcpy(faces.data(), b.faces, faces.size() * 4,
+                               cudaMemcpyDeviceToHost));
+        std::vector<float> vf;
+        int vf_deg = 0;
+        vertex_faces_table(faces.data(), sp.n_faces, sp.n_verts, &vf, &vf_deg);
+        const size_t px = size_t(sp.views) * sp.res * sp.res;
+        auto carve = [&](Arena& a) {
+            b.det_pix = a.take<float2>(px);
+            b.det_part = a.take<float4>(size_t(sp.views) * sp.n_faces * 3);
+            b.det_vf = a.take<float>(vf.size());
+        };
+        Arena dry;
+        carve(dry);
+        DRESSI_CUDA(cudaMalloc(&p->det_mem, dry.used + 256));
+        Arena a{static_cast<char*>(p->det_mem), dry.used + 256, 0};
+        carve(a);
+        b.det_vf_deg = vf_deg;
+        DRESSI_CUDA(cudaMemcpy(const_cast<float*>(b.det_vf), vf.data(),
+                               vf.size() * 4, cudaMemcpyHostToDevice));
     });
 }
 

@@ -212,8 +212,20 @@ struct SilBuffers {
     float4* paper_layers;
     float* paper_prev;
     float4* paper_gfetch;
+    // Deterministic gradient mode (null = off): the epilogue writes each
+    // pixel's (survivor face, dL/d dist) instead of scattering with float
+    // atomics; det_face_op then gathers per face in pixel order and per
+    // vertex in vertex -> face table order (the reference's GatherDistGrad
+    // + ColSum order).
+    float2* det_pix;   // [views*R*R] (face as int bits or -1, g)
+    float4* det_part;  // [views*F*3] per-face corner partials (x, y, -, w)
+    const float* det_vf;  // VertexFacesTex [vf_deg][V] (ids as float)
+    int det_vf_deg;
 };
 constexpr int kLossSlots = 4096;
+// Deterministic mode: partials per face, then g_clip per vertex.
+void sil_det_gather(const SoftDims& d, const SilParams& p, const SilBuffers& b,
+                    cudaStream_t s);
 // Transform, raster, loss and per-view clip gradients (advances the Adam
 // counter). rs_out (nullable) receives the RasterizeSoft images.
 void sil_forward_backward(const SoftDims& d, const SilParams& p,

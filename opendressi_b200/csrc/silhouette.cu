@@ -182,6 +182,7 @@ struct EpiSil {
     float4* rs_out;         // optional RasterizeSoft images
     float k, c;
     int n_verts;
+    float2* det_pix;        // deterministic mode: (face, g) per pixel
     __device__ void operator()(const SweepArgs& a, int x, int y, bool in,
                                const Survivor& s) const {
         double lv = 0.0;
@@ -204,13 +205,16 @@ struct EpiSil {
                     if (rs_out)
                         rs_out[pix] = make_float4(td.dist, r.fid,
                                                   hard_depth(px, py, r), 1.f);
-                    if (g != 0.f)
+                    if (g != 0.f && !det_pix)
                         sil_scatter(px, py, g, td, r,
                                     clip + size_t(a.v) * n_verts, float(a.W),
                                     float(a.H),
                                     gclip + size_t(a.v) * n_verts * 4);
                 }
             }
+            if (det_pix)
+                det_pix[pix] = make_float2(
+                        __int_as_float(g != 0.f ? s.face : -1), g);
         }
         // warp sum of the loss image (no block barrier: the warps of a
         // tile finish independently)
@@ -348,8 +352,115 @@ void sil_forward_backward(const SoftDims& d, const SilParams& p,
     sil_face_setup(d, b, s);
     EpiSil epi{b.targets, reinterpret_cast<const float4*>(b.clip), b.gclip,
                b.loss_slots, reinterpret_cast<float4*>(rs_out), p.k, p.c,
-               p.n_verts};
+               p.n_verts, b.det_pix};
     launch_sweeps(d, b.soft, nullptr, epi, s);
+    if (b.det_pix) sil_det_gather(d, p, b, s);
+}
+
+// Deterministic gradient, part 1: per (view, face), the partials of its
+// three corners summed over the pixels whose survivor it is, in row-major
+// order over the face's soft bbox (the reference's GatherDistGrad scans a
+// face's pixels in the same order); the arithmetic per pixel is
+// sil_scatter's.
+__global__ void k_det_face(int n_faces, int n_verts, int W, int H,
+                           const FaceRec* recs_all, const float2* pix_all,
+                           const float4* clip_all, float4* part_all) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    const int v = blockIdx.y;
+    if (f >= n_faces) return;
+    const FaceRec& r = recs_all[size_t(v) * n_faces + f];
+    float4 acc[3];
+#pragma unroll
+    for (int k = 0; k < 3; k++) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if ((r.flags & kFaceValid) && r.bx0 <= r.bx1 && r.by0 <= r.by1) {
+        const float2* pix = pix_all + size_t(v) * W * H;
+        const float4* clip_v = clip_all + size_t(v) * n_verts;
+        const float fw = float(W), fh = float(H);
+        const float hx[3] = {r.h0x, r.h1x, r.h2x};
+        const float hy[3] = {r.h0y, r.h1y, r.h2y};
+        const uint32_t idx[3] = {r.i0, r.i1, r.i2};
+        for (int y = r.by0; y <= r.by1; y++) {
+            for (int x = r.bx0; x <= r.bx1; x++) {
+                const float2 e = pix[size_t(y) * W + x];
+                if (__float_as_int(e.x) != f) continue;
+                const float g = e.y;
+                const float px = float(x) + 0.5f, py = float(y) + 0.5f;
+                const TriDist td = signed_dist(px, py, r);
+                const float d = fabsf(td.dist);
+                if (d < 1e-6f) continue;
+                const int ia = td.edge, ib = (td.edge + 1) % 3;
+                const float qx = hx[ia] + td.t * (hx[ib] - hx[ia]);
+                const float qy = hy[ia] + td.t * (hy[ib] - hy[ia]);
+                const float sgn = td.dist >= 0.f ? 1.f : -1.f;
+                const float nx = (px - qx) / d;
+                const float ny = (py - qy) / d;
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const int k = j == 0 ? ia : ib;
+                    const float wgt = j == 0 ? (1.f - td.t) : td.t;
+                    const float gsx = g * (-sgn * wgt * nx);
+                    const float gsy = g * (-sgn * wgt * ny);
+                    if (gsx == 0.f && gsy == 0.f) continue;
+                    const float4 c = clip_v[idx[k]];
+                    acc[k].x += gsx * 0.5f * fw / c.w;
+                    acc[k].y += gsy * 0.5f * fh / c.w;
+                    acc[k].w += -(gsx * 0.5f * fw * c.x +
+                                  gsy * 0.5f * fh * c.y) / (c.w * c.w);
+                }
+            }
+        }
+    }
+    float4* out = part_all + (size_t(v) * n_faces + f) * 3;
+#pragma unroll
+    for (int k = 0; k < 3; k++) out[k] = acc[k];
+}
+
+// Part 2: per (view, vertex), the sum of its incident faces' corner
+// partials in the order of the vertex -> face table (the reference's
+// ColSum over GatherDistGrad's columns).
+__global__ void k_det_vertex(int n_faces, int n_verts, const float* faces,
+                             const float* vf, int vf_deg,
+                             const float4* part_all, float* gclip_all) {
+    const int u = blockIdx.x * blockDim.x + threadIdx.x;
+    const int v = blockIdx.y;
+    if (u >= n_verts) return;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < vf_deg; j++) {
+        const float fv = vf[size_t(j) * n_verts + u];
+        if (fv < -0.5f) continue;
+        const uint32_t f = x86_u32_via_i64(fv + 0.5f);
+        if (f >= uint32_t(n_faces)) continue;
+        const float4* p = part_all + (size_t(v) * n_faces + f) * 3;
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            if (x86_u32_via_i64(faces[size_t(f) * 3 + k] + 0.5f) !=
+                uint32_t(u))
+                continue;
+            acc.x += p[k].x;
+            acc.y += p[k].y;
+            acc.w += p[k].w;
+        }
+    }
+    float* g = gclip_all + (size_t(v) * n_verts + u) * 4;
+    g[0] = acc.x;
+    g[1] = acc.y;
+    g[2] = 0.f;
+    g[3] = acc.w;
+}
+
+void sil_det_gather(const SoftDims& d, const SilParams& p, const SilBuffers& b,
+                    cudaStream_t s) {
+    ProfScope ps("det_gather", s);
+    const dim3 fg((p.n_faces + 127) / 128, p.views);
+    k_det_face<<<fg, 128, 0, s>>>(p.n_faces, p.n_verts, d.W, d.H, b.soft.recs,
+                                  b.det_pix,
+                                  reinterpret_cast<const float4*>(b.clip),
+                                  b.det_part);
+    check_launch();
+    const dim3 vg((p.n_verts + 127) / 128, p.views);
+    k_det_vertex<<<vg, 128, 0, s>>>(p.n_faces, p.n_verts, b.faces, b.det_vf,
+                                    b.det_vf_deg, b.det_part, b.gclip);
+    check_launch();
 }
 
 void sil_grad_reduce(const SilParams& p, const SilBuffers& b, bool update,

@@ -214,6 +214,11 @@ class SilhouettePlan(Plan):
     def grad_tensor(self) -> torch.Tensor:
         return self.slot_tensor(N.SLOT_GRAD, (self.n_verts, 3))
 
+    def set_deterministic(self, on: bool = True):
+        """Deterministic gradient mode: per-face then per-vertex gathers in
+        a fixed order instead of float atomics (bit-identical reruns)."""
+        N.call("dressi_plan_set_deterministic", self._h, int(bool(on)))
+
     def loss_tensor(self) -> torch.Tensor:
         return self.slot_tensor(N.SLOT_LOSS, (1,))
 
