@@ -241,9 +241,25 @@ struct dressi_plan_s {
         slots[i].bytes = bytes;
     }
 
+    // the side stream of the regulariser's fork (silhouette plans with a
+    // regulariser), created on first use
+    StreamFork fork;
+    const StreamFork* reg_fork() {
+        if (kind != kSil || !p.reg) return nullptr;
+        if (!fork.side) {
+            DRESSI_CUDA(cudaStreamCreateWithFlags(&fork.side,
+                                                  cudaStreamNonBlocking));
+            DRESSI_CUDA(cudaEventCreateWithFlags(&fork.begin,
+                                                 cudaEventDisableTiming));
+            DRESSI_CUDA(cudaEventCreateWithFlags(&fork.end,
+                                                 cudaEventDisableTiming));
+        }
+        return &fork;
+    }
+
     void record_iteration(cudaStream_t s) {
         if (kind == kSil) {
-            sil_iteration(d, p, b, s);
+            sil_iteration(d, p, b, s, reg_fork());
             if (ovf_host)
                 DRESSI_CUDA(cudaMemcpyAsync(ovf_host, b.soft.status + 1, 4,
                                             cudaMemcpyDeviceToHost, s));
@@ -312,9 +328,20 @@ struct dressi_plan_s {
                 sil_update(p, b, s);
             }
         } else if (phase == 0) {
+            // the regulariser's terms (pos only) on a parallel branch
+            const StreamFork* fk = reg_fork();
+            if (fk) {
+                DRESSI_CUDA(cudaEventRecord(fk->begin, s));
+                DRESSI_CUDA(cudaStreamWaitEvent(fk->side, fk->begin, 0));
+                sil_reg_terms(p, b, fk->side);
+                DRESSI_CUDA(cudaEventRecord(fk->end, fk->side));
+            }
             sil_forward_backward(d, p, b, nullptr, s);
             sil_grad_reduce(p, b, false, s);
-            sil_reg_terms(p, b, s);
+            if (fk)
+                DRESSI_CUDA(cudaStreamWaitEvent(s, fk->end, 0));
+            else
+                sil_reg_terms(p, b, s);
             DRESSI_CUDA(cudaMemcpyAsync(ovf_host, b.soft.status + 1, 4,
                                         cudaMemcpyDeviceToHost, s));
         } else {
@@ -357,6 +384,9 @@ struct dressi_plan_s {
         if (slots[DRESSI_SLOT_RASTER].ptr) cudaFree(slots[DRESSI_SLOT_RASTER].ptr);
         if (ovf_host) cudaFreeHost(ovf_host);
         if (det_mem) cudaFree(det_mem);
+        if (fork.side) cudaStreamDestroy(fork.side);
+        if (fork.begin) cudaEventDestroy(fork.begin);
+        if (fork.end) cudaEventDestroy(fork.end);
         if (prev >= 0) cudaSetDevice(prev);
     }
 };

@@ -339,9 +339,18 @@ void env_conv_bwd_run(int kind, const float* gy, int n,
                       const float* norm, float* g_env, bool accumulate,
                       cudaStream_t s);
 
-// One full single-device iteration.
+// A side stream and the two events of a fork / join, so that independent
+// work of an iteration runs concurrently (a fork inside a stream capture
+// becomes parallel branches of the graph).
+struct StreamFork {
+    cudaStream_t side = nullptr;
+    cudaEvent_t begin = nullptr, end = nullptr;
+};
+// One full single-device iteration (fork: the regulariser's terms on the
+// side stream; null: all on s).
 void sil_iteration(const SoftDims& d, const SilParams& p,
-                   const SilBuffers& b, cudaStream_t s);
+                   const SilBuffers& b, cudaStream_t s,
+                   const StreamFork* fork = nullptr);
 // Renders hard silhouettes (face id > 0) of pos into targets (setup only).
 void sil_render_targets(const SoftDims& d, const SilParams& p,
                         const SilBuffers& b, const float* target_pos,

@@ -482,15 +482,27 @@ void sil_update(const SilParams& p, const SilBuffers& b, cudaStream_t s) {
 }
 
 void sil_iteration(const SoftDims& d, const SilParams& p, const SilBuffers& b,
-                   cudaStream_t s) {
-    sil_forward_backward(d, p, b, nullptr, s);
+                   cudaStream_t s, const StreamFork* fork) {
     if (!p.reg) {
+        sil_forward_backward(d, p, b, nullptr, s);
         sil_grad_reduce(p, b, true, s);
         return;
     }
+    // the regulariser's terms depend on pos only: with a fork they run on
+    // the side stream, concurrently with the raster passes
+    if (fork) {
+        DRESSI_CUDA(cudaEventRecord(fork->begin, s));
+        DRESSI_CUDA(cudaStreamWaitEvent(fork->side, fork->begin, 0));
+        sil_reg_terms(p, b, fork->side);
+        DRESSI_CUDA(cudaEventRecord(fork->end, fork->side));
+    }
+    sil_forward_backward(d, p, b, nullptr, s);
     // the regulariser needs the whole g before the Adam step
     sil_grad_reduce(p, b, false, s);
-    sil_reg_terms(p, b, s);
+    if (fork)
+        DRESSI_CUDA(cudaStreamWaitEvent(s, fork->end, 0));
+    else
+        sil_reg_terms(p, b, s);
     sil_update(p, b, s);
 }
 
