@@ -462,6 +462,7 @@ struct TexParams {
     int w_tex, levels, views, res, n_verts, n_faces;
     float lr, b1, b2, eps;
     float inv_n;  // 1 / (R * R * 3): the per-view Mean
+    int scatter_runs;  // 1: run-merged warp scatter, 0: one atomic per tap
 };
 struct TexBuffers {
     float* pyr;       // mip pyramid, level 0 = the optimised texture

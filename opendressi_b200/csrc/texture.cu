@@ -313,10 +313,22 @@ __device__ __forceinline__ float pixel_rho(const float* gb, int W, int H,
 // sampling scattered into gpyr; out (nullable) gets mask * sample.
 // Eight CTAs per SM (32 registers instead of 40): 0.121 -> 0.120 ms per
 // C2 iteration.
-__global__ void __launch_bounds__(256, 8)
+//
+// Scatter of the transpose (kRuns): each lane's bilinear tap quad of a level
+// is one (four texels, four weights) set. With kRuns = false every tap is a
+// float4 vector atomic (red.v4.f32); with kRuns = true the lanes of a warp
+// whose quads name the same four texels (neighbouring pixels of a row in a
+// magnified region) are first summed by a segmented warp scan and one lane
+// per run issues the atomics (warp-aggregated accumulation).
+template <bool kRuns>
+__global__ void __launch_bounds__(256, kRuns ? 4 : 8)
         k_c2_pixel(TexParams p, const float* pyr, const float* gbuf,
                    const float* targets, float4* gpyr, double* loss_slots,
                    float* out, int train) {
+    // the quads of the (up to) two levels this lane scatters into
+    int qkey[2][4] = {{-1, -1, -1, -1}, {-1, -1, -1, -1}};
+    float qw[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    float gq[3] = {0.f, 0.f, 0.f};
     const int v = blockIdx.y;
     const int tiles_x = (p.res + 15) / 16;
     const int x = (blockIdx.x % tiles_x) * 16 + (threadIdx.x & 15);
@@ -370,7 +382,8 @@ __global__ void __launch_bounds__(256, 8)
                     const int iy = x86_i32(floorf(sy));
                     const float fx = sx - float(ix);
                     const float fy = sy - float(iy);
-                    float4* gl = gpyr + mip_off(p.w_tex, level) / 3;
+                    const size_t lbase = mip_off(p.w_tex, level) / 3;
+                    float4* gl = gpyr + lbase;
 #pragma unroll
                     for (int dy = 0; dy <= 1; dy++)
 #pragma unroll
@@ -379,12 +392,66 @@ __global__ void __launch_bounds__(256, 8)
                             const int ty = iclamp(iy + dy, 0, s - 1);
                             const float wt = (dx == 0 ? 1.f - fx : fx) *
                                              (dy == 0 ? 1.f - fy : fy);
-                            // one vector atomic per tap (rgb + unused)
-                            atomicAdd(gl + size_t(ty) * s + tx,
-                                      make_float4(g[0] * lw * wt, g[1] * lw * wt,
-                                                  g[2] * lw * wt, 0.f));
+                            if (kRuns) {
+                                qkey[lvl][dy * 2 + dx] =
+                                        int(lbase + size_t(ty) * s + tx);
+                                qw[lvl][dy * 2 + dx] = lw * wt;
+                            } else {
+                                // one vector atomic per tap (rgb + unused)
+                                atomicAdd(gl + size_t(ty) * s + tx,
+                                          make_float4(g[0] * lw * wt,
+                                                      g[1] * lw * wt,
+                                                      g[2] * lw * wt, 0.f));
+                            }
                         }
                 }
+                if (kRuns) {
+#pragma unroll
+                    for (int c = 0; c < 3; c++) gq[c] = g[c];
+                }
+            }
+        }
+    }
+    if (kRuns && train) {
+        // every lane of the warp takes part (lanes without taps carry key
+        // -1 and form runs of their own)
+#pragma unroll
+        for (int lvl = 0; lvl < 2; lvl++) {
+            const bool on = qkey[lvl][0] >= 0;
+            if (!__any_sync(0xffffffffu, on)) continue;
+            const int lane = threadIdx.x & 31;
+            bool head = lane == 0;
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                head |= __shfl_up_sync(0xffffffffu, qkey[lvl][k], 1) !=
+                        qkey[lvl][k];
+            const unsigned heads = __ballot_sync(0xffffffffu, head);
+            const int start = 31 - __clz(heads & (0xffffffffu >> (31 - lane)));
+            const unsigned longest = __reduce_max_sync(
+                    0xffffffffu, unsigned(lane - start + 1));
+            const int steps = longest <= 1u ? 0 : 32 - __clz(longest - 1u);
+            float val[12];
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+#pragma unroll
+                for (int c = 0; c < 3; c++)
+                    val[k * 3 + c] = on ? gq[c] * qw[lvl][k] : 0.f;
+            for (int st = 0; st < steps; st++) {
+                const int off = 1 << st;
+                const bool take = lane - off >= start;
+#pragma unroll
+                for (int q = 0; q < 12; q++) {
+                    const float o = __shfl_up_sync(0xffffffffu, val[q], off);
+                    if (take) val[q] += o;
+                }
+            }
+            const bool tail = lane == 31 || ((heads >> (lane + 1)) & 1u);
+            if (on && tail) {
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    atomicAdd(gpyr + qkey[lvl][k],
+                              make_float4(val[k * 3], val[k * 3 + 1],
+                                          val[k * 3 + 2], 0.f));
             }
         }
     }
@@ -542,9 +609,14 @@ void tex_forward_backward(const TexParams& p, const TexBuffers& b,
     mip_build(p, b.pyr, b.gpyr, s);
     {
         ProfScope ps("c2_pixel", s);
-        k_c2_pixel<<<pixel_grid(p), 256, 0, s>>>(p, b.pyr, b.gbuf, b.targets,
-                                                 b.gpyr, b.loss_slots,
-                                                 pred_out, 1);
+        if (p.scatter_runs)
+            k_c2_pixel<true><<<pixel_grid(p), 256, 0, s>>>(
+                    p, b.pyr, b.gbuf, b.targets, b.gpyr, b.loss_slots,
+                    pred_out, 1);
+        else
+            k_c2_pixel<false><<<pixel_grid(p), 256, 0, s>>>(
+                    p, b.pyr, b.gbuf, b.targets, b.gpyr, b.loss_slots,
+                    pred_out, 1);
     }
     check_launch();
     {
@@ -574,8 +646,8 @@ void tex_iteration(const TexParams& p, const TexBuffers& b, cudaStream_t s) {
 void tex_predict(const TexParams& p, const TexBuffers& b, float* out,
                  cudaStream_t s) {
     mip_build(p, b.pyr, nullptr, s);
-    k_c2_pixel<<<pixel_grid(p), 256, 0, s>>>(p, b.pyr, b.gbuf, nullptr, nullptr,
-                                             nullptr, out, 0);
+    k_c2_pixel<false><<<pixel_grid(p), 256, 0, s>>>(
+            p, b.pyr, b.gbuf, nullptr, nullptr, nullptr, out, 0);
     check_launch();
 }
 
@@ -589,8 +661,8 @@ void tex_render_targets(const TexParams& p, const TexBuffers& b,
                                 size_t(p.w_tex) * p.w_tex * 3 * sizeof(float),
                                 cudaMemcpyDeviceToDevice, s));
     mip_build(p, gt_pyr, nullptr, s);
-    k_c2_pixel<<<pixel_grid(p), 256, 0, s>>>(p, gt_pyr, b.gbuf, nullptr, nullptr,
-                                             nullptr, b.targets, 0);
+    k_c2_pixel<false><<<pixel_grid(p), 256, 0, s>>>(
+            p, gt_pyr, b.gbuf, nullptr, nullptr, nullptr, b.targets, 0);
     check_launch();
     DRESSI_CUDA(cudaFreeAsync(tmp, s));
 }
