@@ -91,6 +91,9 @@ def parse():
                          "same workload built with the F:: graph API and run "
                          "by DressiAD (fusion planner + CUDA-graph executor); "
                          "c1 and c3, one GPU")
+    ap.add_argument("--deterministic", action="store_true",
+                    help="c3: the plan's deterministic gradient mode "
+                         "(ordered gathers instead of float atomics)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
@@ -178,7 +181,9 @@ def workload(args):
                             "normal": args.normal},
         }
     return {
-        "workload": "C3 silhouette HardSoftRas fwd+bwd+Adam",
+        "workload": "C3 silhouette HardSoftRas fwd+bwd+Adam" +
+                    (" (deterministic gradients)" if args.deterministic
+                     else ""),
         "mesh": f"icosphere-{args.level}",
         "views": args.views,
         "res": args.res,
@@ -421,6 +426,8 @@ def run_ours(args):
         plan = SilhouettePlan.from_scene(sc, views=shard, device=local,
                                          laplacian=args.laplacian,
                                          normal=args.normal)
+        if args.deterministic:
+            plan.set_deterministic(True)
     if args.config == "c2":
         plan.upload(N.SLOT_PARAM, sc.tex0)
         plan.render_targets(sc.gt_tex)
