@@ -1099,8 +1099,8 @@ __device__ __forceinline__ bool tri_touches_block(const FaceRec& r, int bx,
 // Summed-area table of the open blocks per 16x16 tile of one view (block
 // = view): sat[(ty + 1) (tiles_x + 1) + tx + 1] = the open blocks of the
 // tiles (0..tx, 0..ty); row 0 and column 0 are zero. Rows are prefix-summed
-// by one thread each, then columns. Also zeroes the view's count of faces
-// kept for the rim binning.
+// by one warp each (warp scans over 32 tiles at a time), then columns.
+// Also zeroes the view's count of faces kept for the rim binning.
 static __global__ void k_open_sat(int n_tiles, int tiles_x, int tiles_y,
                                   const uint8_t* active, int* sat_all,
                                   int* kept_n) {
@@ -1109,25 +1109,46 @@ static __global__ void k_open_sat(int n_tiles, int tiles_x, int tiles_y,
     const int w1 = tiles_x + 1;
     int* sat = sat_all + size_t(v) * w1 * (tiles_y + 1);
     const uint8_t* act = active + size_t(v) * n_tiles * 8;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int n_warps = blockDim.x >> 5;
     for (int x = threadIdx.x; x < w1; x += blockDim.x) sat[x] = 0;
-    for (int ty = threadIdx.x; ty < tiles_y; ty += blockDim.x) {
+    // rows: one warp per row, 32 tiles per step, a warp scan per step
+    for (int ty = warp; ty < tiles_y; ty += n_warps) {
         int* row = sat + size_t(ty + 1) * w1;
         const uint2* a = reinterpret_cast<const uint2*>(act) +
                          size_t(ty) * tiles_x;
-        int run = 0;
-        row[0] = 0;
-        for (int tx = 0; tx < tiles_x; tx++) {
-            const uint2 b = a[tx];  // the tile's 8 block flags (0 / 1 bytes)
-            run += __popc(b.x) + __popc(b.y);
-            row[tx + 1] = run;
+        if (lane == 0) row[0] = 0;
+        int carry = 0;
+        for (int t0 = 0; t0 < tiles_x; t0 += 32) {
+            const int tx = t0 + lane;
+            int c = 0;
+            if (tx < tiles_x) {
+                const uint2 b = a[tx];  // the tile's 8 block flags (0 / 1)
+                c = __popc(b.x) + __popc(b.y);
+            }
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, c, o);
+                if (lane >= o) c += n;
+            }
+            if (tx < tiles_x) row[tx + 1] = carry + c;
+            carry += __shfl_sync(0xffffffffu, c, 31);
         }
     }
     __syncthreads();
-    for (int x = threadIdx.x; x < w1; x += blockDim.x) {
-        int run = 0;
-        for (int ty = 1; ty <= tiles_y; ty++) {
-            run += sat[size_t(ty) * w1 + x];
-            sat[size_t(ty) * w1 + x] = run;
+    // columns: one warp per column, 32 rows per step
+    for (int x = warp; x < w1; x += n_warps) {
+        int carry = 0;
+        for (int r0 = 1; r0 <= tiles_y; r0 += 32) {
+            const int ty = r0 + lane;
+            int c = ty <= tiles_y ? sat[size_t(ty) * w1 + x] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, c, o);
+                if (lane >= o) c += n;
+            }
+            if (ty <= tiles_y) sat[size_t(ty) * w1 + x] = carry + c;
+            carry += __shfl_sync(0xffffffffu, c, 31);
         }
     }
 }
