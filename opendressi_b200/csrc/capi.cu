@@ -1778,6 +1778,7 @@ int dressi_plan_set_deterministic(dressi_plan p, int on) {
             b.det_part = nullptr;
             b.det_vf = nullptr;
             b.det_vf_deg = 0;
+            b.det_touch = nullptr;
             return;
         }
         if (p->det_mem) return;
@@ -1793,12 +1794,14 @@ int dressi_plan_set_deterministic(dressi_plan p, int on) {
             b.det_pix = a.take<float2>(px);
             b.det_part = a.take<float4>(size_t(sp.views) * sp.n_faces * 3);
             b.det_vf = a.take<float>(vf.size());
+            b.det_touch = a.take<uint8_t>(size_t(sp.views) * sp.n_faces);
         };
         Arena dry;
         carve(dry);
         DRESSI_CUDA(cudaMalloc(&p->det_mem, dry.used + 256));
         Arena a{static_cast<char*>(p->det_mem), dry.used + 256, 0};
         carve(a);
+        DRESSI_CUDA(cudaMemset(b.det_touch, 0, size_t(sp.views) * sp.n_faces));
         b.det_vf_deg = vf_deg;
         DRESSI_CUDA(cudaMemcpy(const_cast<float*>(b.det_vf), vf.data(),
                                vf.size() * 4, cudaMemcpyHostToDevice));

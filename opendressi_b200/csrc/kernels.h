@@ -221,6 +221,9 @@ struct SilBuffers {
     float4* det_part;  // [views*F*3] per-face corner partials (x, y, -, w)
     const float* det_vf;  // VertexFacesTex [vf_deg][V] (ids as float)
     int det_vf_deg;
+    // faces that received a gradient pixel this iteration [views*F]: set by
+    // the epilogue, read and cleared by the per-face gather
+    uint8_t* det_touch;
 };
 constexpr int kLossSlots = 4096;
 // Deterministic mode: partials per face, then g_clip per vertex.

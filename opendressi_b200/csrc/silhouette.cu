@@ -183,6 +183,7 @@ struct EpiSil {
     float k, c;
     int n_verts;
     float2* det_pix;        // deterministic mode: (face, g) per pixel
+    uint8_t* det_touch;     // ... and the faces that got a gradient pixel
     __device__ void operator()(const SweepArgs& a, int x, int y, bool in,
                                const Survivor& s) const {
         double lv = 0.0;
@@ -212,9 +213,12 @@ struct EpiSil {
                                     gclip + size_t(a.v) * n_verts * 4);
                 }
             }
-            if (det_pix)
+            if (det_pix) {
                 det_pix[pix] = make_float2(
                         __int_as_float(g != 0.f ? s.face : -1), g);
+                if (g != 0.f && s.face >= 0)
+                    det_touch[size_t(a.v) * a.n_faces + s.face] = 1;
+            }
         }
         // warp sum of the loss image (no block barrier: the warps of a
         // tile finish independently)
@@ -352,7 +356,7 @@ void sil_forward_backward(const SoftDims& d, const SilParams& p,
     sil_face_setup(d, b, s);
     EpiSil epi{b.targets, reinterpret_cast<const float4*>(b.clip), b.gclip,
                b.loss_slots, reinterpret_cast<float4*>(rs_out), p.k, p.c,
-               p.n_verts, b.det_pix};
+               p.n_verts, b.det_pix, b.det_touch};
     launch_sweeps(d, b.soft, nullptr, epi, s);
     if (b.det_pix) sil_det_gather(d, p, b, s);
 }
@@ -364,7 +368,8 @@ void sil_forward_backward(const SoftDims& d, const SilParams& p,
 // sil_scatter's.
 __global__ void k_det_face(int n_faces, int n_verts, int W, int H,
                            const FaceRec* recs_all, const float2* pix_all,
-                           const float4* clip_all, float4* part_all) {
+                           const float4* clip_all, uint8_t* touch_all,
+                           float4* part_all) {
     const int f = blockIdx.x * blockDim.x + threadIdx.x;
     const int v = blockIdx.y;
     if (f >= n_faces) return;
@@ -372,7 +377,11 @@ __global__ void k_det_face(int n_faces, int n_verts, int W, int H,
     float4 acc[3];
 #pragma unroll
     for (int k = 0; k < 3; k++) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if ((r.flags & kFaceValid) && r.bx0 <= r.bx1 && r.by0 <= r.by1) {
+    // only faces some pixel gave a gradient to have anything to sum
+    uint8_t& touched = touch_all[size_t(v) * n_faces + f];
+    const bool any = touched != 0;
+    if (any) touched = 0;
+    if (any && (r.flags & kFaceValid) && r.bx0 <= r.bx1 && r.by0 <= r.by1) {
         const float2* pix = pix_all + size_t(v) * W * H;
         const float4* clip_v = clip_all + size_t(v) * n_verts;
         const float fw = float(W), fh = float(H);
@@ -455,7 +464,7 @@ void sil_det_gather(const SoftDims& d, const SilParams& p, const SilBuffers& b,
     k_det_face<<<fg, 128, 0, s>>>(p.n_faces, p.n_verts, d.W, d.H, b.soft.recs,
                                   b.det_pix,
                                   reinterpret_cast<const float4*>(b.clip),
-                                  b.det_part);
+                                  b.det_touch, b.det_part);
     check_launch();
     const dim3 vg((p.n_verts + 127) / 128, p.views);
     k_det_vertex<<<vg, 128, 0, s>>>(p.n_faces, p.n_verts, b.faces, b.det_vf,

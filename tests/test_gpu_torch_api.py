@@ -256,7 +256,9 @@ def test_ops_under_torch_compile_and_no_sync(cuda):
     p2 = torch.tensor(pos, device=cuda, requires_grad=True)
     l2 = compiled(p2)
     l2.backward()
-    assert torch.equal(l1.detach(), l2.detach())
+    # the compiled graph fuses the loss arithmetic around the custom ops
+    # (its own reduction order), so the results agree to rounding
+    torch.testing.assert_close(l2.detach(), l1.detach(), atol=0, rtol=1e-5)
     torch.testing.assert_close(p2.grad, p1.grad, atol=1e-5, rtol=1e-4)
     assert dr.check_status() == 0
     # the ops are registered custom ops with fake kernels
