@@ -49,7 +49,10 @@ FILE_FLAGS = {"pbr.cu": {"-fmad=false": "-fmad=true",
 
 def flags_for(src: str) -> list[str]:
     sub = FILE_FLAGS.get(src, {})
-    return [sub.get(f, f) for f in NVCC_FLAGS]
+    # DRESSI_NVCC_DEFINES: extra -D tuning macros of the kernels (for
+    # instance "-DDRESSI_WARP_SORT=64"); empty in a normal build
+    extra = os.environ.get("DRESSI_NVCC_DEFINES", "").split()
+    return [sub.get(f, f) for f in NVCC_FLAGS] + extra
 
 
 def nvcc() -> str:

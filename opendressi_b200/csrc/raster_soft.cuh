@@ -593,7 +593,10 @@ constexpr int kWarpSort = DRESSI_WARP_SORT;  // longest per-warp list sorted
 #define DRESSI_RIM_SORT 128
 #endif
 constexpr int kRimSort = DRESSI_RIM_SORT;  // longest rim-block list sorted
-constexpr int kWarpRecs = 16;    // records staged per warp and round
+#ifndef DRESSI_WARP_RECS
+#define DRESSI_WARP_RECS 16
+#endif
+constexpr int kWarpRecs = DRESSI_WARP_RECS;  // records staged per warp and round
 constexpr int kSpillBlocks = 296;  // grid of k_sweep1_spill (2 per SM)
 static_assert(kSortMax >= kTileThreads, "spill gathers need blockDim keys");
 
@@ -1625,7 +1628,10 @@ struct EpiRS {
 // few spilled bytes (7 CTAs at the unbounded 72 registers; 8, 10 and 12 per
 // SM timed slower).
 template <class Epi>
-__global__ void __launch_bounds__(kSweep1Threads, 9)
+#ifndef DRESSI_SWEEP1_CTAS
+#define DRESSI_SWEEP1_CTAS 9
+#endif
+__global__ void __launch_bounds__(kSweep1Threads, DRESSI_SWEEP1_CTAS)
         k_sweep1(SweepArgs a0, FixedBins1 b1, FixedBins b2, int2* state,
                  uint8_t* active, size_t view_stride_recs,
                  size_t view_stride_px, size_t view_stride_rim, Epi epi) {
