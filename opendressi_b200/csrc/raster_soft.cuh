@@ -597,6 +597,14 @@ constexpr int kRimSort = DRESSI_RIM_SORT;  // longest rim-block list sorted
 #define DRESSI_WARP_RECS 16
 #endif
 constexpr int kWarpRecs = DRESSI_WARP_RECS;  // records staged per warp and round
+// warp_sort_smem pads a list to a power of two of at least 64 keys inside
+// the buffer these size
+static_assert(kWarpSort >= 64 && (kWarpSort & (kWarpSort - 1)) == 0,
+              "DRESSI_WARP_SORT must be a power of two >= 64");
+static_assert(kRimSort >= 64 && (kRimSort & (kRimSort - 1)) == 0,
+              "DRESSI_RIM_SORT must be a power of two >= 64");
+static_assert(kWarpRecs >= 1 && kWarpRecs <= 32,
+              "DRESSI_WARP_RECS must lie in [1, 32]");
 constexpr int kSpillBlocks = 296;  // grid of k_sweep1_spill (2 per SM)
 static_assert(kSortMax >= kTileThreads, "spill gathers need blockDim keys");
 
