@@ -183,21 +183,57 @@ static __device__ __noinline__ float aa_pair_r(const AaFace* fr, int n_faces,
     return pr.r;
 }
 
+// r of the pair (s, n) from the tile's shared triangle ids.
+static __device__ __noinline__ float aa_pair_r_ids(const AaFace* fr,
+                                                   int n_faces, int its,
+                                                   int itn, int x, int y,
+                                                   int nx, int ny) {
+    AaPairD pr;
+    if (!aa_pair(fr, n_faces, its, itn, float(x) + 0.5f, float(y) + 0.5f,
+                 float(nx) + 0.5f, float(ny) + 0.5f, &pr))
+        return -1.f;
+    return pr.r;
+}
+
+// Coverage of a pixel from its triangle id: the mask Rasterize(clip, ones)
+// of a covered pixel is (sum_k l_k / w_k) / (sum_k l_k / w_k), which is
+// exactly 1 (the two sums are the same products added in the same order)
+// whenever that sum is non-zero (it is finite: the raster keeps w > 1e-6),
+// and 0 on the background. A zero sum, where the reference's mask is NaN,
+// needs an exact cancellation against a rounding-negative barycentric.
+__device__ __forceinline__ float aa_mask_of_id(int id) {
+    return (id != 0 && id != INT_MIN) ? 1.f : 0.f;
+}
+
 // Eight CTAs per SM (32 registers, a few spilled bytes): the kernel is
 // latency-bound on its neighbour and face-record loads, so full residency
 // beats the unbounded 48 registers (5 CTAs; 1.12 -> 0.87 ms at C4).
-template <class Epi, int NC>
+// kIdMask (NC == 1): the image is the hard mask of the triangle ids, taken
+// from the id tile in shared memory (img unused), so the mask image is
+// neither written by the raster nor read here.
+template <class Epi, int NC, bool kIdMask = false>
 __global__ void __launch_bounds__(256, 8)
         k_aa_forward(AaDims d, const AaFace* frs, const float* img,
                      const float* tri, const int* view_flags, Epi epi) {
+    static_assert(!kIdMask || NC == 1, "id masks have one component");
     __shared__ float vals[18][18];  // n_comp == 1: the image tile + halo
+    __shared__ int ids_sh[kIdMask ? 18 : 1][kIdMask ? 18 : 1];
     const int v = blockIdx.y;
     const int tiles_x = (d.W + 15) / 16;
     const int x0 = (blockIdx.x % tiles_x) * 16, y0 = (blockIdx.x / tiles_x) * 16;
     const size_t px0 = size_t(v) * d.W * d.H;
     constexpr int nc = NC;
-    const float* im = img + px0 * nc;
-    if (nc == 1) {
+    const float* im = kIdMask ? nullptr : img + px0 * nc;
+    if (kIdMask) {
+        for (int i = threadIdx.x; i < 18 * 18; i += blockDim.x) {
+            const int hx = x0 - 1 + i % 18, hy = y0 - 1 + i / 18;
+            const int id = (hx >= 0 && hy >= 0 && hx < d.W && hy < d.H)
+                                   ? aa_tri_id(tri[px0 + size_t(hy) * d.W + hx])
+                                   : INT_MIN;
+            ids_sh[kIdMask ? i / 18 : 0][kIdMask ? i % 18 : 0] = id;
+            vals[i / 18][i % 18] = aa_mask_of_id(id);
+        }
+    } else if (nc == 1) {
         for (int i = threadIdx.x; i < 18 * 18; i += blockDim.x) {
             const int hx = x0 - 1 + i % 18, hy = y0 - 1 + i / 18;
             vals[i / 18][i % 18] = (hx >= 0 && hy >= 0 && hx < d.W && hy < d.H)
@@ -260,7 +296,13 @@ __global__ void __launch_bounds__(256, 8)
                     continue;
                 }
             }
-            const float r = aa_pair_r(fr, d.n_faces, tri + px0, d.W, x, y, nx, ny);
+            const float r =
+                    kIdMask ? aa_pair_r_ids(fr, d.n_faces,
+                                            ids_sh[kIdMask ? ly + 1 : 0][kIdMask ? lx + 1 : 0],
+                                            ids_sh[kIdMask ? ly + 1 + kAaOffY[k] : 0]
+                                                  [kIdMask ? lx + 1 + kAaOffX[k] : 0],
+                                            x, y, nx, ny)
+                            : aa_pair_r(fr, d.n_faces, tri + px0, d.W, x, y, nx, ny);
             if (r == -1.f) {
 #pragma unroll
                 for (int c = 0; c < nc; c++) dst[c] += cs[c];
@@ -378,6 +420,7 @@ __device__ __forceinline__ void aa_accumulate(const AaDims& d, int v,
 
 // Exact vertex gradient (n_samples = 0): every boundary pair of every
 // pixel (f_ops.cpp:2373-2396), scattered to both edge endpoints.
+template <bool kIdMask = false>
 __global__ void __launch_bounds__(256)
         k_aa_bwd_vtx_exact(AaDims d, const AaFace* frs, const float* gy,
                            const float* img, const float* tri,
@@ -398,10 +441,20 @@ __global__ void __launch_bounds__(256)
     for (int k = 0; k < 8; k++) {
         const int nx = x + kAaOffX[k], ny = y + kAaOffY[k];
         if (nx < 0 || ny < 0 || nx >= d.W || ny >= d.H) continue;
-        const float gr = aa_pair_weight(d, v, gy, img, x, y, nx, ny);
+        const int itn = ids[ly + 1 + kAaOffY[k]][lx + 1 + kAaOffX[k]];
+        float gr;
+        if (kIdMask) {
+            // aa_pair_weight's sum with c = the id mask
+            const size_t so = size_t(v) * d.W * d.H + size_t(y) * d.W + x;
+            float acc = 0.f;
+            acc += gy[so] * (aa_mask_of_id(its) - aa_mask_of_id(itn));
+            gr = acc / 9.f;
+        } else {
+            gr = aa_pair_weight(d, v, gy, img, x, y, nx, ny);
+        }
         if (gr == 0.f) continue;
         AaPairD pr;
-        if (!aa_pair(fr, d.n_faces, its, ids[ly + 1 + kAaOffY[k]][lx + 1 + kAaOffX[k]],
+        if (!aa_pair(fr, d.n_faces, its, itn,
                      psx, psy, float(nx) + 0.5f, float(ny) + 0.5f, &pr) ||
             pr.r >= 1.f)
             continue;
@@ -413,6 +466,8 @@ __global__ void __launch_bounds__(256)
 // (f_ops.cpp:2430-2468). `only` >= 0: accumulate to that vertex only
 // (multiplicity 1); else to the face's own vertices with their
 // multiplicity in the face (the sum over its VertexFacesTex incidences).
+// kIdMask: the image is the hard mask of the triangle ids (img unused).
+template <bool kIdMask = false>
 __device__ __forceinline__ void aa_sample(const AaDims& d, int v,
                                           const AaFace* fr, const AaFace& r,
                                           uint32_t f, uint32_t smp,
@@ -441,11 +496,23 @@ __device__ __forceinline__ void aa_sample(const AaDims& d, int v,
     for (int k = 0; k < 8; k++) {
         const int nx = x + kAaOffX[k], ny = y + kAaOffY[k];
         if (nx < 0 || ny < 0 || nx >= d.W || ny >= d.H) continue;
-        const float gr = aa_pair_weight(d, v, gy, img, x, y, nx, ny);
+        int itn = 0;
+        float gr;
+        if (kIdMask) {
+            // aa_pair_weight's sum with c = the id mask
+            itn = aa_tri_id(tv[size_t(ny) * d.W + nx]);
+            const size_t so = size_t(v) * d.W * d.H + size_t(y) * d.W + x;
+            float acc = 0.f;
+            acc += gy[so] * (aa_mask_of_id(its) - aa_mask_of_id(itn));
+            gr = acc / 9.f;
+        } else {
+            gr = aa_pair_weight(d, v, gy, img, x, y, nx, ny);
+        }
         if (gr == 0.f) continue;
+        if (!kIdMask) itn = aa_tri_id(tv[size_t(ny) * d.W + nx]);
         AaPairD pr;
-        if (!aa_pair(fr, d.n_faces, its, aa_tri_id(tv[size_t(ny) * d.W + nx]),
-                     psx, psy, float(nx) + 0.5f, float(ny) + 0.5f, &pr) ||
+        if (!aa_pair(fr, d.n_faces, its, itn, psx, psy, float(nx) + 0.5f,
+                     float(ny) + 0.5f, &pr) ||
             pr.r >= 1.f)
             continue;
         int ma, mb;
@@ -496,6 +563,7 @@ __global__ void k_aa_bwd_vtx_vft(AaDims d, const AaFace* frs, const float* gy,
 // is VertexFacesTex of the faces (the plans build it that way).
 // Six CTAs per SM (40 registers): 0.58 -> 0.56 ms at C4 against the
 // unbounded 59 registers; eight spill and time slower.
+template <bool kIdMask = false>
 __global__ void __launch_bounds__(256, 6) k_aa_bwd_vtx_faces(AaDims d, const AaFace* frs,
                                    const float* gy, const float* img,
                                    const float* tri, const float4* clip,
@@ -510,7 +578,8 @@ __global__ void __launch_bounds__(256, 6) k_aa_bwd_vtx_faces(AaDims d, const AaF
     const AaFace r = fr[f];
     if (!(r.flags & kAaSValid)) return;
     const uint32_t seed_u = x86_u32_via_i64((t_ptr[0] + t_add) + 0.5f);
-    aa_sample(d, v, fr, r, f, smp, seed_u, -1, gy, img, tri, clip, grad);
+    aa_sample<kIdMask>(d, v, fr, r, f, smp, seed_u, -1, gy, img, tri, clip,
+                       grad);
 }
 
 namespace {
@@ -632,9 +701,11 @@ static void aa_sil_render(const SilParams& p, const AaSilBuffers& b,
     hd.views = p.views;
     hd.n_faces = p.n_faces;
     hd.n_verts = p.n_verts;
-    hd.attr_ones = 1;
-    hard_raster_op(hd, b.hard_ws, b.sil.clip, nullptr, b.sil.faces, b.mask,
-                   nullptr, b.status, s, b.tri);
+    // no attribute: the raster writes the triangle-id image only; the mask
+    // Rasterize(clip, ones) is derived from it (aa_mask_of_id)
+    hd.attr_ones = 0;
+    hard_raster_op(hd, b.hard_ws, b.sil.clip, nullptr, b.sil.faces, b.tri,
+                   nullptr, b.status, s, nullptr);
     AaDims d;
     d.W = d.H = p.res;
     d.views = p.views;
@@ -645,9 +716,8 @@ static void aa_sil_render(const SilParams& p, const AaSilBuffers& b,
                   s);
     {
         ProfScope ps("aa_forward", s);
-        k_aa_forward<Epi, 1><<<tile_grid(d), 256, 0, s>>>(d, b.frs, b.mask,
-                                                          b.tri, b.view_flags,
-                                                          epi);
+        k_aa_forward<Epi, 1, true><<<tile_grid(d), 256, 0, s>>>(
+                d, b.frs, nullptr, b.tri, b.view_flags, epi);
     }
     check_launch();
 }
@@ -658,7 +728,6 @@ size_t aa_sil_workspace_bytes(const SilParams& p) {
     hd.views = p.views;
     hd.n_faces = p.n_faces;
     hd.n_verts = p.n_verts;
-    hd.attr_ones = 1;
     return hard_workspace_bytes(hd);
 }
 
@@ -676,15 +745,15 @@ void aa_sil_forward_backward(const SilParams& p, const AaSilBuffers& b,
     const float4* c4 = reinterpret_cast<const float4*>(b.sil.clip);
     ProfScope ps("aa_bwd_vtx", s);
     if (p.n_samples == 0) {
-        k_aa_bwd_vtx_exact<<<tile_grid(d), 256, 0, s>>>(d, b.frs, b.gy, b.mask,
-                                                        b.tri, c4, b.sil.gclip);
+        k_aa_bwd_vtx_exact<true><<<tile_grid(d), 256, 0, s>>>(
+                d, b.frs, b.gy, nullptr, b.tri, c4, b.sil.gclip);
     } else {
         // the sampling seed is the Adam counter before this iteration's
         // update: scalars[0] - 1 once the transform has advanced it (exact
         // for counters below 2^24)
         const long long n = (long long)p.n_faces * p.n_samples;
-        k_aa_bwd_vtx_faces<<<dim3(unsigned((n + 255) / 256), p.views), 256,
-                             0, s>>>(d, b.frs, b.gy, b.mask, b.tri, c4,
+        k_aa_bwd_vtx_faces<true><<<dim3(unsigned((n + 255) / 256), p.views),
+                                   256, 0, s>>>(d, b.frs, b.gy, nullptr, b.tri, c4,
                                      b.sil.scalars, -1.f, p.n_samples,
                                      b.sil.gclip);
     }

@@ -792,7 +792,6 @@ int dressi_aa_silhouette_plan_create(const dressi_aa_silhouette_desc* desc,
             b.done = a.take<unsigned>(1);
             AaSilBuffers& ab = pl->ab;
             ab.tri = a.take<float>(NV * R2);
-            ab.mask = a.take<float>(NV * R2);
             ab.gy = a.take<float>(NV * R2);
             ab.frs = a.take<AaFace>(NV * F);
             ab.view_flags = a.take<int>(NV);
@@ -1391,7 +1390,8 @@ int dressi_pbr_plan_create(const dressi_pbr_desc* desc, dressi_plan* out) {
             b.loss_slots = a.take<double>(kLossSlots);
             b.loss_hist = a.take<float>(size_t(hist));
             b.hist_cap = hist;
-            b.px = a.take<float>(NV * R2 * 20);
+            b.px = a.take<float>(NV * R2 * 12);
+            b.px_side = a.take<float4>(NV * R2);
             b.target = a.take<float>(NV * R2 * 3);
             b.pos = a.take<float>(V * 3);
             b.nrm = a.take<float>(V * 3);

@@ -426,8 +426,8 @@ void aa_bwd_vtx_op(const AaDims& d, const AaFace* fr, const float* gy,
 // and Adam.
 struct AaSilBuffers {
     SilBuffers sil;     // pos / Adam / targets / clip / gclip / loss ...
-    float* tri;         // [views][R][R] face id + 1
-    float* mask;        // [views][R][R] Rasterize(clip, ones)
+    float* tri;         // [views][R][R] face id + 1 (the mask Rasterize(
+                        // clip, ones) is 1 exactly where it is non-zero)
     float* gy;          // [views][R][R] dL / d pred
     AaFace* frs;        // [views][F]
     int* view_flags;    // [views]
@@ -546,7 +546,8 @@ struct PbrDims {
     int pixel_ctas;
 };
 struct PbrBuffers {
-    float* px;        // [views][R*R][5 float4] pixel-static records
+    float* px;        // [views][R*R][3 float4] pixel-static records
+    float4* px_side;  // [views][R*R] (mask, background u, v, 0)
     float* target;    // [views][R*R][3] tone-mapped targets
     float* params;    // albedo [T*T*3] | mr [T*T*3] | env [eh*ew*3]
     float* grad;      // same layout
@@ -590,7 +591,8 @@ struct PbrBuffers {
 };
 __global__ void k_pbr_static(PbrDims d, const float* uvh, const float* nrm,
                              const float* wpos, const float* frames,
-                             const float* light, float4* rec);
+                             const float* light, float4* rec,
+                             float4* side);
 size_t pbr_smem_bytes(const PbrDims& d);
 // Sets the pixel kernel's shared-memory limit; its resident CTAs per SM.
 int pbr_pixel_blocks_per_sm(const PbrDims& d);

@@ -107,16 +107,24 @@ __device__ __forceinline__ void taps_clamp(int w, int h, float u, float v,
 }
 
 constexpr uint32_t kIrrValid = 1u, kReflValid = 2u, kBgValid = 4u;
+constexpr uint32_t kMaskOne = 8u, kMaskZero = 16u;  // else 0 < mask < 1
 
 }  // namespace
 
-// The pixel-static record of every (view, pixel): BuildPbrGBuffer's uv /
-// mask from uvh, SafeNormalize(n), v, l, h and the products BuildPbrShade
-// takes of them, and the EquirectSample coordinates of n, the reflection
-// and the background ray.
+// The pixel-static record of every (view, pixel), 48 bytes: BuildPbrGBuffer's
+// uv from uvh, the products BuildPbrShade takes of SafeNormalize(n), v, l
+// and h, the squared light distance and the EquirectSample coordinates of n
+// and the reflection:
+//   q0 = (u, v, n.v, n.l)   q1 = (n.h, (1 - v.h)^5, dist^2, flags)
+//   q2 = (irradiance u, v, reflection u, v)
+// and, for a background pixel (mask 0), q0 = (background-ray u, v, 0, 0).
+// The pixel kernel recomputes (1 - n.v)^5 and the radiance light / dist^2
+// with the same expressions. The mask, 0 or 1 on the plan's G-buffer, is a
+// flag; a pixel whose mask is neither reads side = (mask, background u, v,
+// 0), which is written for every pixel.
 __global__ void k_pbr_static(PbrDims d, const float* uvh, const float* nrm,
                              const float* wpos, const float* frames,
-                             const float* light, float4* rec) {
+                             const float* light, float4* rec, float4* side) {
     const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     const long long npx = (long long)d.res * d.res;
     if (i >= npx * d.views) return;
@@ -154,14 +162,16 @@ __global__ void k_pbr_static(PbrDims d, const float* uvh, const float* nrm,
     if (equirect_coords(n, &iu, &iv)) flags |= kIrrValid;
     if (equirect_coords(refl, &ru, &rv)) flags |= kReflValid;
     if (equirect_coords(ray, &bu, &bv)) flags |= kBgValid;
-    float4* r = rec + i * 5;
+    float4* r = rec + i * 3;
     const float* q = uvh + i * 4;
-    r[0] = make_float4(q[2], q[0], q[1], ndv);
-    r[1] = make_float4(ndl, ndh, powf(1.f - ndv, 5.f), powf(1.f - vdh, 5.f));
-    r[2] = make_float4(light[3] / dist2, light[4] / dist2, light[5] / dist2,
-                       __uint_as_float(flags));
-    r[3] = make_float4(iu, iv, ru, rv);
-    r[4] = make_float4(bu, bv, 0.f, 0.f);
+    const float mask = q[2];
+    if (mask == 1.f) flags |= kMaskOne;
+    if (mask == 0.f) flags |= kMaskZero;
+    r[0] = mask == 0.f ? make_float4(bu, bv, 0.f, 0.f)
+                       : make_float4(q[0], q[1], ndv, ndl);
+    r[1] = make_float4(ndh, powf(1.f - vdh, 5.f), dist2, __uint_as_float(flags));
+    r[2] = make_float4(iu, iv, ru, rv);
+    side[i] = make_float4(mask, bu, bv, 0.f);
 }
 
 namespace {
@@ -338,10 +348,24 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
          base += stride) {
         const long long i = base + threadIdx.x;
         const bool live = i < total;
-        const float4* r = reinterpret_cast<const float4*>(b.px) + (live ? i : 0) * 5;
-        const float4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3], r4 = r[4];
-        const float mask = live ? r0.x : 0.f;
-        const uint32_t flags = __float_as_uint(r2.w);
+        const float4* r = reinterpret_cast<const float4*>(b.px) + (live ? i : 0) * 3;
+        const float4 r0 = r[0], r1 = r[1], r2 = r[2];
+        const uint32_t flags = __float_as_uint(r1.w);
+        float mask, bu, bv;
+        if (flags & kMaskOne) {
+            mask = 1.f;
+            bu = bv = 0.f;
+        } else if (flags & kMaskZero) {
+            mask = 0.f;
+            bu = r0.x;
+            bv = r0.y;
+        } else {
+            const float4 sd = b.px_side[live ? i : 0];
+            mask = sd.x;
+            bu = sd.y;
+            bv = sd.z;
+        }
+        if (!live) mask = 0.f;
         float hdr[3] = {0.f, 0.f, 0.f};
         // ---- foreground (mask != 0): BuildPbrShade
         float A[3] = {0.f, 0.f, 0.f}, rough_raw = 0.f, metal = 0.f, ao = 0.f;
@@ -369,12 +393,16 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
                 pwt[j][k] = 0.f;
             }
         }
-        const float ndv = r0.w, ndl = r1.x, ndh = r1.y, p5v = r1.z,
-                    p5h = r1.w;
-        const float rad[3] = {r2.x, r2.y, r2.z};
+        const float ndv = r0.z, ndl = r0.w, ndh = r1.x, p5h = r1.y;
+        float p5v = 0.f, rad[3] = {0.f, 0.f, 0.f};
         const float ndlc = fmax_ref(ndl, 1e-4f);
         if (mask != 0.f) {
-            taps_clamp(T, T, r0.y, r0.z, tidx, twt);
+            p5v = powf(1.f - ndv, 5.f);
+            const float dist2 = r1.z;
+            rad[0] = b.light[3] / dist2;
+            rad[1] = b.light[4] / dist2;
+            rad[2] = b.light[5] / dist2;
+            taps_clamp(T, T, r0.x, r0.y, tidx, twt);
             float m4[4];
             gather4(b.mat4, tidx, twt, m4);
             A[0] = m4[0];
@@ -420,7 +448,7 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
             }
             // irradiance (EquirectSample of the 32x16 map along n)
             if (flags & kIrrValid) {
-                taps_wrap(d.irr_w, d.irr_h, r3.x, r3.y, iidx, iwt);
+                taps_wrap(d.irr_w, d.irr_h, r2.x, r2.y, iidx, iwt);
                 float t4[4];
                 gather4(irr4, iidx, iwt, t4);
                 irr[0] = t4[0];
@@ -443,7 +471,7 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
                 xl[j] = 1.f - fabsf(lod - float(li));
                 wl[j] = xl[j] < 0.f ? 0.f : (1.f < xl[j] ? 1.f : xl[j]);
                 if (flags & kReflValid) {
-                    taps_wrap(d.lw[li], d.lh[li], r3.z, r3.w, pidx[j], pwt[j]);
+                    taps_wrap(d.lw[li], d.lh[li], r2.z, r2.w, pidx[j], pwt[j]);
                     float t4[4];
                     gather4(pref4 + d.loff[li], pidx[j], pwt[j], t4);
                     P[j][0] = t4[0];
@@ -480,7 +508,7 @@ k_pbr_pixel(PbrDims d, PbrBuffers b, int mode, float* out) {
         if (live && mask != 1.f) {
             float bg[4] = {0.f, 0.f, 0.f, 0.f};
             if (flags & kBgValid) {
-                taps_wrap(d.ew, d.eh, r4.x, r4.y, bidx, bwt);
+                taps_wrap(d.ew, d.eh, bu, bv, bidx, bwt);
                 gather4(b.env4, bidx, bwt, bg);
             }
             for (int c = 0; c < 3; c++)
@@ -842,7 +870,7 @@ void pbr_static_setup(const PbrDims& d, const PbrBuffers& b, cudaStream_t s) {
     const long long n = (long long)d.res * d.res * d.views;
     k_pbr_static<<<unsigned((n + 255) / 256), 256, 0, s>>>(
             d, b.gbuf_uvh, b.gbuf_n, b.gbuf_p, b.frames, b.light,
-            reinterpret_cast<float4*>(b.px));
+            reinterpret_cast<float4*>(b.px), b.px_side);
     check_launch();
 }
 
