@@ -532,6 +532,12 @@ static __global__ void k_bin_scan(BinSet b, int n_tiles, uint32_t* status) {
 constexpr int kRecChunk = 64;
 constexpr int kRimCell = 32;     // pixels per side of a rim-flag cell
 constexpr int kRimChunk = 8;     // records per rim staging buffer (2/warp)
+#ifndef DRESSI_RIM_LINE_LB
+#define DRESSI_RIM_LINE_LB 0  // 1: edge-line distance bounds in the rim fold
+#endif
+#ifndef DRESSI_RIM_PREFETCH
+#define DRESSI_RIM_PREFETCH 0  // 1: k_rim takes its next block ahead
+#endif
 
 // Fixed-capacity bins filled in one pass: entry i of bin k lives at
 // list[k * cap + i]; the bin's cursor counts every append. Appends past the
@@ -1360,10 +1366,43 @@ __device__ __forceinline__ void rim_fold_chunk(
         const float dy = fmaxf(fmaxf(r.lby0 - py, py - r.lby1), 0.f);
         const float d2 = (dx * dx + dy * dy) * 0.998f;
         if (s.depth < 1.f) {
-            const float t = 2.f * s.depth - 1.f;
+            const float t = 2.f * s.depth - 1.f + 2.3841858e-7f;
             if (d2 > t * t * r2) continue;  // bound above the survivor
         }
-        const bool far = d2 >= r2;  // depth exactly 1
+        bool far = d2 >= r2;  // depth exactly 1
+#if DRESSI_RIM_LINE_LB
+        if (!far && r.orient != 0.f) {
+            // The triangle lies in the inner half-plane of each edge, so the
+            // distance is >= the outward distance to any edge line, -o cr_k
+            // / |e_k|, whose rounding on a kFaceFast face is < 0.001 px
+            // (build_record). In squares: m_k = -o cr_k > 0 and m_k^2 >
+            // |e_k|^2 (0.001 + 1.001 D)^2 give a distance > D.
+            const float crs[3] = {
+                    r.ex0 * (py - r.h0y) - r.ey0 * (px - r.h0x),
+                    r.ex1 * (py - r.h1y) - r.ey1 * (px - r.h1x),
+                    r.ex2 * (py - r.h2y) - r.ey2 * (px - r.h2x)};
+            const float l2s[3] = {r.len2_0, r.len2_1, r.len2_2};
+            const float dr = 0.001f + 1.001f * a.radius;
+            const float kr = dr * dr;
+            float ks = kr;
+            if (s.depth < 1.f) {
+                const float ds = 0.001f + 1.001f * (2.f * s.depth - 1.f +
+                                                    2.3841858e-7f) * a.radius;
+                ks = ds * ds;
+            }
+            bool beyond = false;
+#pragma unroll
+            for (int k = 0; k < 3; k++) {
+                const float m = -r.orient * crs[k];
+                if (m > 0.f) {
+                    const float mm = m * m;
+                    beyond = beyond || mm > l2s[k] * ks;
+                    far = far || mm > l2s[k] * kr;
+                }
+            }
+            if (beyond && s.depth < 1.f) continue;  // above the survivor
+        }
+#endif
         if (far && f < s.face) continue;  // 1.0 tie, older face
         if (!soft_covers(px, py, r)) continue;
         if (far) {
@@ -1410,7 +1449,12 @@ __device__ __forceinline__ void rim_load_ids(const SweepArgs& a,
 // with q = 0.999 d / R, lb = 0.5 + 0.5 min(q, 1) > depth  <=>  q > t =
 // 2 depth - 1 (t < 1), i.e. d^2 0.999^2 > t^2 R^2, and lb = 1 <=> d^2
 // 0.999^2 >= R^2. Using 0.998 < 0.999^2 keeps both bounds below the true
-// depth with the same ~1e-3 slack against rounding (~1e-7).
+// depth with the same ~1e-3 slack against rounding (~1e-7). A skipped
+// fragment must also round to a depth strictly above the survivor's (an
+// equal depth is a tie that the later face wins): t is raised by 2^-22,
+// two units in the last place of depths in [0.5, 1), so the skip holds
+// for survivors at any distance, not only where the relative slack
+// exceeds an ulp.
 template <class Epi>
 static __device__ __forceinline__ void rim_block(const SweepArgs& a, FixedBins b2, int tile,
                                  int w, const int2* state, FaceRec* recs_w,
@@ -1733,11 +1777,22 @@ __global__ void __launch_bounds__(kTileThreads)
     const int wc = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_open = *b2.open_n;
     const int n_front = b2.order_n[0], n_back = b2.order_n[1];
+#if DRESSI_RIM_PREFETCH
+    // the next work item is taken while this one is folded, so the cursor's
+    // round trip leaves the chain of dependent loads of every block
+    int item = 0;
+    if (lane == 0) item = atomicAdd(b2.take, 1);
+    item = __shfl_sync(0xffffffffu, item, 0);
+    while (item < n_front + n_back) {
+        int next = 0;
+        if (lane == 0) next = atomicAdd(b2.take, 1);
+#else
     for (;;) {
         int item = 0;
         if (lane == 0) item = atomicAdd(b2.take, 1);
         item = __shfl_sync(0xffffffffu, item, 0);
         if (item >= n_front + n_back) break;
+#endif
         // the long lists first (the split blocks are not in this list)
         const int e = b2.order[item < n_front ? item
                                               : n_open - 1 - (item - n_front)];
@@ -1750,6 +1805,9 @@ __global__ void __launch_bounds__(kTileThreads)
         if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
         rim_block(a, b2, tile, w, state, recs_sh[wc], ids_sh[wc], keys_sh[wc],
                   epi);
+#if DRESSI_RIM_PREFETCH
+        item = __shfl_sync(0xffffffffu, next, 0);
+#endif
     }
 }
 
