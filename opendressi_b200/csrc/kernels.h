@@ -131,6 +131,12 @@ void launch_sweeps(const SoftDims& d, const SoftBuffers& b,
                                                      sp, sm, epi);
     }
     DRESSI_CUDA(cudaGetLastError());
+    {
+        ProfScope ps("rim_empty", s);
+        k_rim_empty<Epi><<<148 * 4, 256, 0, s>>>(a, b.bin2, b.state, sr, sp,
+                                                 sm, epi);
+    }
+    DRESSI_CUDA(cudaGetLastError());
 }
 
 // --- op-level soft raster (explicit soft geometry, one or more views) ---

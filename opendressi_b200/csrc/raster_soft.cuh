@@ -567,8 +567,12 @@ struct FixedBins {
     int* seg_block;   // [kRimSplit * views * tiles * 8]
     int* seg_index;   // [kRimSplit * views * tiles * 8]
     int* split;       // [views * tiles * 8]
+    // open blocks whose bins stayed empty: no fragment left to fold, only
+    // the epilogue of their sweep-1 survivors (k_rim_empty)
+    int* empty;       // [views * tiles * 8]
     // [0] front and [1] back whole blocks placed, [2] segments, [3] split
-    // blocks, [4] k_rim_seg's work cursor (all reset by k_rim_bin)
+    // blocks, [4] k_rim_seg's work cursor, [5] empty blocks (all reset by
+    // k_rim_filter)
     int* order_n;
     // per pixel, the best fragment the segments of a heavy block found
     // (rim_key_of; ~0 = none), consumed and reset by rim_split_finish
@@ -1183,7 +1187,7 @@ static __global__ void k_rim_filter(int n_faces, int n_tiles, int tiles_x,
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
         *b1.spill_n = 0;
         *b1.parked_n = 0;
-        for (int i = 0; i < 5; i++) b2.order_n[i] = 0;
+        for (int i = 0; i < 6; i++) b2.order_n[i] = 0;
     }
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n_tiles;
          t += gridDim.x * blockDim.x)
@@ -1216,13 +1220,17 @@ static __global__ void k_rim_filter(int n_faces, int n_tiles, int tiles_x,
 }
 
 // Rim-phase binning: a kept face enters the bin of every open 8x4 block its
-// soft triangle may touch. One warp per kept face, lanes striding over the
-// blocks of its soft bbox.
+// soft triangle may touch. One warp per kept face: the lanes read the open
+// flags of the 16x16 tiles under the face's soft bbox, eight at a time (one
+// 8-byte word per tile), compact the open blocks inside the bbox into the
+// warp's shared list and then test and append those, one per lane.
 static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
                                  const FaceRec* recs_all,
                                  const uint8_t* active, const int* kept_all,
                                  const int* kept_n, FixedBins b2) {
-    const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    __shared__ uint16_t sh_blk[8][256];  // per warp: (lane << 3) | block
+    const int wi = threadIdx.x >> 5;
+    const int i = blockIdx.x * (blockDim.x >> 5) + wi;
     const int lane = threadIdx.x & 31;
     const int v = blockIdx.y;
     if (i >= kept_n[v]) return;
@@ -1231,13 +1239,49 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
     const int blocks_x = tiles_x * 2;
     const uint8_t* act = active + size_t(v) * n_tiles * 8;
     const size_t bin0 = size_t(v) * n_tiles * 8;
-    // lanes tile the block range 8 wide x 4 tall (no integer division)
-    const int lx = lane & 7, ly = lane >> 3;
-    for (int by = (r.by0 >> 2) + ly; by <= (r.by1 >> 2); by += 4) {
-        for (int bx = (r.bx0 >> 3) + lx; bx <= (r.bx1 >> 3); bx += 8) {
-            if (!act[((by >> 2) * tiles_x + (bx >> 1)) * 8 + (by & 3) * 2 +
-                     (bx & 1)])
-                continue;
+    const int bx_lo = r.bx0 >> 3, bx_hi = r.bx1 >> 3;
+    const int by_lo = r.by0 >> 2, by_hi = r.by1 >> 2;
+    const int tx0 = bx_lo >> 1, ty0 = by_lo >> 2;
+    const int ntx = (bx_hi >> 1) - tx0 + 1;
+    const int nt = ntx * ((by_hi >> 2) - ty0 + 1);
+    for (int t0 = 0; t0 < nt; t0 += 32) {
+        // this lane's tile: its open blocks inside the bbox's block range
+        const int t = t0 + lane;
+        uint32_t m = 0;
+        if (t < nt) {
+            const int ty = ty0 + t / ntx, tx = tx0 + t % ntx;
+            const uint2 a8 = *reinterpret_cast<const uint2*>(
+                    act + (size_t(ty) * tiles_x + tx) * 8);
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const uint32_t word = k < 4 ? a8.x : a8.y;
+                const int bx = tx * 2 + (k & 1), by = ty * 4 + (k >> 1);
+                if (((word >> (8 * (k & 3))) & 0xffu) != 0u && bx >= bx_lo &&
+                    bx <= bx_hi && by >= by_lo && by <= by_hi)
+                    m |= 1u << k;
+            }
+        }
+        // warp-exclusive scan of the counts, then the compacted list
+        const int c = __popc(m);
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += n;
+        }
+        const int total = __shfl_sync(0xffffffffu, incl, 31);
+        int pos = incl - c;
+        while (m) {
+            const int k = __ffs(m) - 1;
+            m &= m - 1u;
+            sh_blk[wi][pos++] = uint16_t((lane << 3) | k);
+        }
+        __syncwarp();
+        for (int j = lane; j < total; j += 32) {
+            const int e = sh_blk[wi][j];
+            const int tt = t0 + (e >> 3), k = e & 7;
+            const int bx = (tx0 + tt % ntx) * 2 + (k & 1);
+            const int by = (ty0 + tt / ntx) * 4 + (k >> 1);
             if (!tri_touches_block(r, bx, by)) continue;
             const size_t bin = bin0 + size_t(by) * blocks_x + bx;
             const int slot = atomicAdd(&b2.cursor[bin], 1);
@@ -1248,6 +1292,7 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
                 if (sp < b2.spill_cap) b2.spill[sp] = make_int2(int(bin), f);
             }
         }
+        __syncwarp();  // sh_blk reuse by the next round
     }
 }
 
@@ -1276,7 +1321,10 @@ static __global__ void k_rim_order(FixedBins b2, int n_tiles, int tiles_x) {
         const int by = (tile / tiles_x) * 4 + (w >> 1);
         const size_t bin = size_t(v) * n_tiles * 8 + size_t(by) * (tiles_x * 2) + bx;
         const int cnt = b2.cursor[bin];
-        if (n < kRimSplitMaxOpen && cnt > kRimSort && cnt <= b2.cap) {
+        if (cnt == 0) {
+            // nothing to fold (an empty bin spilled nothing either)
+            b2.empty[atomicAdd(&b2.order_n[5], 1)] = e;
+        } else if (n < kRimSplitMaxOpen && cnt > kRimSort && cnt <= b2.cap) {
             // a list too long to sort (and not spilled): kRimSplit warps
             // fold a strided share each, k_rim_split_epi finishes the block
             const int slot = atomicAdd(&b2.order_n[2], kRimSplit);
@@ -1830,6 +1878,36 @@ __global__ void __launch_bounds__(256)
         a.rim = a0.rim + a.v * view_stride_rim;
         if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
         rim_split_finish(a, b2, tile, w, state, epi);
+    }
+}
+// The open blocks whose rim bins stayed empty (most of them: the rim-flag
+// cells are coarse): the rim phase would fold nothing into their sweep-1
+// survivors, so one warp per block only runs the epilogue, as rim_block
+// does for an empty list.
+template <class Epi>
+__global__ void __launch_bounds__(256)
+        k_rim_empty(SweepArgs a0, FixedBins b2, const int2* state,
+                    size_t view_stride_recs, size_t view_stride_px,
+                    size_t view_stride_rim, Epi epi) {
+    const int n_empty = b2.order_n[5];
+    const int lane = threadIdx.x & 31;
+    for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < n_empty;
+         t += (gridDim.x * blockDim.x) >> 5) {
+        const int e = b2.empty[t];
+        const int tbin = e >> 3, w = e & 7;
+        SweepArgs a = a0;
+        a.v = tbin / a0.n_tiles;
+        const int tile = tbin - a.v * a0.n_tiles;
+        a.recs = a0.recs + a.v * view_stride_recs;
+        a.rim = a0.rim + a.v * view_stride_rim;
+        if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
+        const int x = (tile % a.tiles_x) * kTile + (w & 1) * 8 + (lane & 7);
+        const int y = (tile / a.tiles_x) * kTile + (w >> 1) * 4 + (lane >> 3);
+        const bool in = x < a.W && y < a.H;
+        Survivor s{1.f, -1, false};
+        if (in)
+            s = unpack(state[size_t(a.v) * a.W * a.H + size_t(y) * a.W + x]);
+        epi(a, x, y, in, s);
     }
 }
 constexpr int kRimCtas = 148 * 4;  // persistent grid of k_rim

@@ -74,7 +74,8 @@ void carve_soft_bins(Arena& a, const SoftDims& d, SoftBuffers* b) {
     b->bin2.seg_block = a.take<int>(std::max<size_t>(kRimSplit * vb, 1));
     b->bin2.seg_index = a.take<int>(std::max<size_t>(kRimSplit * vb, 1));
     b->bin2.split = a.take<int>(std::max<size_t>(vb, 1));
-    b->bin2.order_n = a.take<int>(5);
+    b->bin2.empty = a.take<int>(std::max<size_t>(vb, 1));
+    b->bin2.order_n = a.take<int>(6);
     b->bin2.best = a.take<unsigned long long>(
             std::max<size_t>(size_t(d.views) * d.W * d.H, 1));
 }
