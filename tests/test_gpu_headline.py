@@ -136,7 +136,9 @@ def test_c3_300_iterations(cuda, port):
     pixel changes the gradient by a step. So the trace is held to 1e-3 rel
     over its first 25 iterations, and the final loss and positions to 1e-3
     or, beyond that, to twice the restatement's own spread measured in the
-    same test."""
+    same test: the largest deviation, from its unperturbed run, of four
+    restatement runs whose starts differ by such one-ulp moves (one sample
+    of a chaotic spread is too few to bound it)."""
     from opendressi_b200 import _native as N
 
     sc = scene.silhouette_scene(level=5, n_views=16, res=256, seed=0)
@@ -148,20 +150,23 @@ def test_c3_300_iterations(cuda, port):
     trace_cpu, pos_cpu = port.silhouette_run(
         sc.pos0, sc.faces_f, sc.mvps, targets, 256, sc.radius_px, sc.sigma,
         sc.lr, n, **run)
-    p1 = np.ascontiguousarray(sc.pos0, np.float32).copy()
-    flat = p1.reshape(-1)
-    idx = np.random.default_rng(1).integers(0, flat.size, 50)
-    flat[idx] = np.nextafter(flat[idx], np.float32(10))
-    trace_pert, pos_pert = port.silhouette_run(
-        p1, sc.faces_f, sc.mvps, targets, 256, sc.radius_px, sc.sigma, sc.lr,
-        n, **run)
+    spread, pos_spread = 0.0, 0.0
+    for seed in range(1, 5):
+        p1 = np.ascontiguousarray(sc.pos0, np.float32).copy()
+        flat = p1.reshape(-1)
+        idx = np.random.default_rng(seed).integers(0, flat.size, 50)
+        flat[idx] = np.nextafter(flat[idx], np.float32(10))
+        trace_pert, pos_pert = port.silhouette_run(
+            p1, sc.faces_f, sc.mvps, targets, 256, sc.radius_px, sc.sigma,
+            sc.lr, n, **run)
+        spread = max(spread,
+                     abs(trace_pert[-1] - trace_cpu[-1]) / trace_cpu[-1])
+        pos_spread = max(pos_spread, float(np.abs(pos_pert - pos_cpu).max()))
     np.testing.assert_allclose(trace[:25], trace_cpu[:25], rtol=1e-3)
-    spread = abs(trace_pert[-1] - trace_cpu[-1]) / trace_cpu[-1]
     rel = abs(trace[-1] - trace_cpu[-1]) / trace_cpu[-1]
     assert rel <= max(1e-3, 2.0 * spread), (rel, spread)
     assert trace[-1] < 0.5 * trace[0]          # it optimises
     pos = plan.download(N.SLOT_PARAM).reshape(-1, 3)
-    pos_spread = np.abs(pos_pert - pos_cpu).max()
     assert np.abs(pos - pos_cpu).max() <= max(1e-3, 2.0 * pos_spread)
     assert plan.status() == 0
 
