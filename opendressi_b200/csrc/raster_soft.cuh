@@ -20,13 +20,16 @@
 //           rim fragments of safe faces: the deferred ones and those outside
 //           the sweep-1 region.
 // A fragment outside the hard bbox + margin of a *safe* face is provably a
-// rim fragment with dist <= -kHardMargin, hence depth > 0.5, so it can never
-// beat a hard fragment: leaving it out for pixels whose depth is <= 0.5
-// cannot change any output. "Safe" bounds the sign-test rounding error:
-// every angle of the hard triangle must satisfy sin(theta/2) > kSafeSlope *
-// L, L the largest pixel distance the face's soft bbox reaches from a hard
-// vertex (the rounding error of the edge function is <= ~5u*|e|*L, its
-// exact value outside the margin is >= 2*sin(theta/2)*|e| * kHardMargin/2);
+// rim fragment with dist <= -(kHardMargin + 1) (the region's integer bounds
+// floor(min - 0.5) - margin .. ceil(max - 0.5) + margin leave every pixel
+// centre outside it at least margin + 1 px from the bbox), hence depth >
+// 0.5, so it can never beat a hard fragment: leaving it out for pixels whose
+// depth is <= 0.5 cannot change any output. "Safe" bounds the sign-test
+// rounding error: every angle of the hard triangle must satisfy
+// sin(theta/2) > kSafeSlope * L, L the largest pixel distance the face's
+// soft bbox reaches from a hard vertex (the rounding error of the edge
+// function is <= ~5u*|e|*L, its exact value outside the margin is >=
+// 2*sin(theta/2)*|e| * (kHardMargin + 1)/2 = 2*sin(theta/2)*|e|);
 // faces failing it, or with huge coordinates, are evaluated exhaustively in
 // sweep 1.
 #pragma once
@@ -42,7 +45,11 @@ namespace dressi {
 
 constexpr int kTile = 16;                // tile edge in pixels
 constexpr int kTileThreads = kTile * kTile;
-constexpr int kHardMargin = 2;           // sweep-1 bbox growth (pixels)
+#ifndef DRESSI_HARD_MARGIN
+#define DRESSI_HARD_MARGIN 1
+#endif
+constexpr int kHardMargin = DRESSI_HARD_MARGIN;  // sweep-1 bbox growth (px)
+static_assert(kHardMargin >= 1, "the safety bound needs centres >= 2 px out");
 constexpr float kSafeSlope = 1.5e-6f;    // see header comment
 constexpr float kCoordLimit = 1048576.f; // |screen coord| bound for "safe"
 
