@@ -1230,17 +1230,16 @@ static __global__ void k_rim_filter(int n_faces, int n_tiles, int tiles_x,
 // soft triangle may touch. One warp per kept face: the lanes read the open
 // flags of the 16x16 tiles under the face's soft bbox, eight at a time (one
 // 8-byte word per tile), compact the open blocks inside the bbox into the
-// warp's shared list and then test and append those, one per lane.
-static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
-                                 const FaceRec* recs_all,
-                                 const uint8_t* active, const int* kept_all,
-                                 const int* kept_n, FixedBins b2) {
-    __shared__ uint16_t sh_blk[8][256];  // per warp: (lane << 3) | block
-    const int wi = threadIdx.x >> 5;
-    const int i = blockIdx.x * (blockDim.x >> 5) + wi;
+// warp's shared list (blk, 256 entries) and then test and append those, one
+// per lane.
+__device__ __forceinline__ void rim_bin_face(int v, int i, int n_faces,
+                                             int n_tiles, int tiles_x,
+                                             const FaceRec* recs_all,
+                                             const uint8_t* active,
+                                             const int* kept_all,
+                                             const FixedBins& b2,
+                                             uint16_t* blk) {
     const int lane = threadIdx.x & 31;
-    const int v = blockIdx.y;
-    if (i >= kept_n[v]) return;
     const int f = kept_all[size_t(v) * n_faces + i];
     const FaceRec& r = recs_all[size_t(v) * n_faces + f];
     const int blocks_x = tiles_x * 2;
@@ -1281,11 +1280,11 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
         while (m) {
             const int k = __ffs(m) - 1;
             m &= m - 1u;
-            sh_blk[wi][pos++] = uint16_t((lane << 3) | k);
+            blk[pos++] = uint16_t((lane << 3) | k);
         }
         __syncwarp();
         for (int j = lane; j < total; j += 32) {
-            const int e = sh_blk[wi][j];
+            const int e = blk[j];
             const int tt = t0 + (e >> 3), k = e & 7;
             const int bx = (tx0 + tt % ntx) * 2 + (k & 1);
             const int by = (ty0 + tt / ntx) * 4 + (k >> 1);
@@ -1299,7 +1298,24 @@ static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
                 if (sp < b2.spill_cap) b2.spill[sp] = make_int2(int(bin), f);
             }
         }
-        __syncwarp();  // sh_blk reuse by the next round
+        __syncwarp();  // blk reuse by the next round
+    }
+}
+
+// A persistent grid (whole warps) strides over the kept faces of every view.
+static __global__ void __launch_bounds__(256)
+        k_rim_bin(int n_faces, int n_tiles, int tiles_x, int views,
+                  const FaceRec* recs_all, const uint8_t* active,
+                  const int* kept_all, const int* kept_n, FixedBins b2) {
+    __shared__ uint16_t sh_blk[8][256];
+    const int wi = threadIdx.x >> 5;
+    const int gw = blockIdx.x * (blockDim.x >> 5) + wi;
+    const int nw = gridDim.x * (blockDim.x >> 5);
+    for (int v = 0; v < views; v++) {
+        const int nk = kept_n[v];
+        for (int i = gw; i < nk; i += nw)
+            rim_bin_face(v, i, n_faces, n_tiles, tiles_x, recs_all, active,
+                         kept_all, b2, sh_blk[wi]);
     }
 }
 
