@@ -607,9 +607,18 @@ constexpr int kSortMax = 256;    // keys gathered per round by k_sweep1_spill
 #endif
 constexpr int kWarpSort = DRESSI_WARP_SORT;  // longest per-warp list sorted
 #ifndef DRESSI_RIM_SORT
-#define DRESSI_RIM_SORT 128
+#define DRESSI_RIM_SORT 256
 #endif
-constexpr int kRimSort = DRESSI_RIM_SORT;  // longest rim-block list sorted
+constexpr int kRimSort = DRESSI_RIM_SORT;  // longest rim-block list ordered
+constexpr int kRimBuckets = 65;  // rim depth-bound buckets (rim_bucket_order)
+// Bucket of a rim block bound lbb in [0.5, 1]: (lbb - 0.5) * 128 is exact
+// (lbb - 0.5 by Sterbenz, the product a power of two), so its floor puts lbb
+// at or above the bucket's edge 0.5 + b/128; lbb == 1 alone takes 64.
+// (Clamped so that a NaN bound, which converts to 0, or any other stray
+// value stays inside the count array.)
+__device__ __forceinline__ int rim_bucket_of(float lbb) {
+    return lbb >= 1.f ? 64 : imin_(imax_(int((lbb - 0.5f) * 128.f), 0), 63);
+}
 #ifndef DRESSI_WARP_RECS
 #define DRESSI_WARP_RECS 16
 #endif
@@ -620,6 +629,9 @@ static_assert(kWarpSort >= 64 && (kWarpSort & (kWarpSort - 1)) == 0,
               "DRESSI_WARP_SORT must be a power of two >= 64");
 static_assert(kRimSort >= 64 && (kRimSort & (kRimSort - 1)) == 0,
               "DRESSI_RIM_SORT must be a power of two >= 64");
+static_assert(2 * kRimChunk * sizeof(FaceRec) >=
+                      kRimSort * sizeof(unsigned long long),
+              "rim_bucket_order's scratch is a warp's record buffer");
 static_assert(kWarpRecs >= 1 && kWarpRecs <= 32,
               "DRESSI_WARP_RECS must lie in [1, 32]");
 constexpr int kSpillBlocks = 296;  // grid of k_sweep1_spill (2 per SM)
@@ -1227,11 +1239,11 @@ static __global__ void k_rim_filter(int n_faces, int n_tiles, int tiles_x,
 }
 
 // Rim-phase binning: a kept face enters the bin of every open 8x4 block its
-// soft triangle may touch. One warp per kept face: the lanes read the open
-// flags of the 16x16 tiles under the face's soft bbox, eight at a time (one
-// 8-byte word per tile), compact the open blocks inside the bbox into the
-// warp's shared list (blk, 256 entries) and then test and append those, one
-// per lane.
+// soft triangle may touch. One warp per kept face: in rounds of 8 x 4 tiles
+// of the face's soft bbox, the lanes read the open flags of their tile's
+// eight blocks (one 8-byte word), compact the open blocks inside the bbox
+// into the warp's shared list (blk, 256 entries) and then test and append
+// those, one per lane.
 __device__ __forceinline__ void rim_bin_face(int v, int i, int n_faces,
                                              int n_tiles, int tiles_x,
                                              const FaceRec* recs_all,
@@ -1248,57 +1260,60 @@ __device__ __forceinline__ void rim_bin_face(int v, int i, int n_faces,
     const int bx_lo = r.bx0 >> 3, bx_hi = r.bx1 >> 3;
     const int by_lo = r.by0 >> 2, by_hi = r.by1 >> 2;
     const int tx0 = bx_lo >> 1, ty0 = by_lo >> 2;
-    const int ntx = (bx_hi >> 1) - tx0 + 1;
-    const int nt = ntx * ((by_hi >> 2) - ty0 + 1);
-    for (int t0 = 0; t0 < nt; t0 += 32) {
-        // this lane's tile: its open blocks inside the bbox's block range
-        const int t = t0 + lane;
-        uint32_t m = 0;
-        if (t < nt) {
-            const int ty = ty0 + t / ntx, tx = tx0 + t % ntx;
-            const uint2 a8 = *reinterpret_cast<const uint2*>(
-                    act + (size_t(ty) * tiles_x + tx) * 8);
+    const int tx1 = bx_hi >> 1, ty1 = by_hi >> 2;
+    // rounds of 8 x 4 tiles (lane -> tile without integer division)
+    for (int oy = ty0; oy <= ty1; oy += 4) {
+        for (int ox = tx0; ox <= tx1; ox += 8) {
+            // this lane's tile: its open blocks inside the bbox's range
+            const int tx = ox + (lane & 7), ty = oy + (lane >> 3);
+            uint32_t m = 0;
+            if (tx <= tx1 && ty <= ty1) {
+                const uint2 a8 = *reinterpret_cast<const uint2*>(
+                        act + (size_t(ty) * tiles_x + tx) * 8);
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
-                const uint32_t word = k < 4 ? a8.x : a8.y;
-                const int bx = tx * 2 + (k & 1), by = ty * 4 + (k >> 1);
-                if (((word >> (8 * (k & 3))) & 0xffu) != 0u && bx >= bx_lo &&
-                    bx <= bx_hi && by >= by_lo && by <= by_hi)
-                    m |= 1u << k;
+                for (int k = 0; k < 8; k++) {
+                    const uint32_t word = k < 4 ? a8.x : a8.y;
+                    const int bx = tx * 2 + (k & 1), by = ty * 4 + (k >> 1);
+                    if (((word >> (8 * (k & 3))) & 0xffu) != 0u &&
+                        bx >= bx_lo && bx <= bx_hi && by >= by_lo &&
+                        by <= by_hi)
+                        m |= 1u << k;
+                }
             }
-        }
-        // warp-exclusive scan of the counts, then the compacted list
-        const int c = __popc(m);
-        int incl = c;
+            // warp-exclusive scan of the counts, then the compacted list
+            const int c = __popc(m);
+            int incl = c;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int n = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += n;
-        }
-        const int total = __shfl_sync(0xffffffffu, incl, 31);
-        int pos = incl - c;
-        while (m) {
-            const int k = __ffs(m) - 1;
-            m &= m - 1u;
-            blk[pos++] = uint16_t((lane << 3) | k);
-        }
-        __syncwarp();
-        for (int j = lane; j < total; j += 32) {
-            const int e = blk[j];
-            const int tt = t0 + (e >> 3), k = e & 7;
-            const int bx = (tx0 + tt % ntx) * 2 + (k & 1);
-            const int by = (ty0 + tt / ntx) * 4 + (k >> 1);
-            if (!tri_touches_block(r, bx, by)) continue;
-            const size_t bin = bin0 + size_t(by) * blocks_x + bx;
-            const int slot = atomicAdd(&b2.cursor[bin], 1);
-            if (slot < b2.cap) {
-                b2.list[bin * b2.cap + slot] = f;
-            } else {
-                const int sp = atomicAdd(b2.spill_n, 1);
-                if (sp < b2.spill_cap) b2.spill[sp] = make_int2(int(bin), f);
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += n;
             }
+            const int total = __shfl_sync(0xffffffffu, incl, 31);
+            int pos = incl - c;
+            while (m) {
+                const int k = __ffs(m) - 1;
+                m &= m - 1u;
+                blk[pos++] = uint16_t((lane << 3) | k);
+            }
+            __syncwarp();
+            for (int j = lane; j < total; j += 32) {
+                const int e = blk[j];
+                const int l = e >> 3, k = e & 7;
+                const int bx = (ox + (l & 7)) * 2 + (k & 1);
+                const int by = (oy + (l >> 3)) * 4 + (k >> 1);
+                if (!tri_touches_block(r, bx, by)) continue;
+                const size_t bin = bin0 + size_t(by) * blocks_x + bx;
+                const int slot = atomicAdd(&b2.cursor[bin], 1);
+                if (slot < b2.cap) {
+                    b2.list[bin * b2.cap + slot] = f;
+                } else {
+                    const int sp = atomicAdd(b2.spill_n, 1);
+                    if (sp < b2.spill_cap)
+                        b2.spill[sp] = make_int2(int(bin), f);
+                }
+            }
+            __syncwarp();  // blk reuse by the next round
         }
-        __syncwarp();  // blk reuse by the next round
     }
 }
 
@@ -1509,6 +1524,62 @@ __device__ __forceinline__ void rim_load_ids(const SweepArgs& a,
     __syncwarp();
 }
 
+// Front-to-back order of a rim block's list without a comparison sort: the
+// keys (block depth bound lbb | face word) are counted into kRimBuckets
+// buckets of lbb -- 0.5 + b/128 <= lbb < 0.5 + (b+1)/128 for b < 64, and
+// lbb == 1 in the last -- and scattered in bucket order through the scratch
+// `tmp` (n <= kRimSort keys). Each key's high word becomes its bucket's
+// lower edge, which is exact (a multiple of 2^-7 plus 0.5) and <= the
+// key's own bound, so the edges are ascending along the list and a pixel
+// whose survivor lies below an edge is done with every later entry, as
+// with sorted bounds. The face words are kept (the last bucket's stay
+// inverted). Order within a bucket is arbitrary: the fold is
+// order-independent.
+static __device__ __noinline__ void rim_bucket_order(unsigned long long* keys,
+                                                 int n,
+                                                 unsigned long long* tmp,
+                                                 int* cnt) {
+    const int lane = threadIdx.x & 31;
+    for (int i = lane; i < kRimBuckets; i += 32) cnt[i] = 0;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+        const unsigned long long k = keys[i];
+        tmp[i] = k;
+        const float lbb = __uint_as_float(uint32_t(k >> 32));
+        atomicAdd(&cnt[rim_bucket_of(lbb)], 1);
+    }
+    __syncwarp();
+    // exclusive scan of the counts (kRimBuckets = 65: lanes hold 0..31,
+    // 32..63, and lane 0 the last)
+    const int c0 = cnt[lane], c1 = cnt[lane + 32];
+    int s0 = c0, s1 = c1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u0 = __shfl_up_sync(0xffffffffu, s0, o);
+        const int u1 = __shfl_up_sync(0xffffffffu, s1, o);
+        if (lane >= o) {
+            s0 += u0;
+            s1 += u1;
+        }
+    }
+    const int t0 = __shfl_sync(0xffffffffu, s0, 31);
+    const int t1 = __shfl_sync(0xffffffffu, s1, 31);
+    __syncwarp();
+    cnt[lane] = s0 - c0;
+    cnt[lane + 32] = t0 + s1 - c1;
+    if (lane == 0) cnt[64] = t0 + t1;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+        const unsigned long long k = tmp[i];
+        const float lbb = __uint_as_float(uint32_t(k >> 32));
+        const int b = rim_bucket_of(lbb);
+        const float edge = b == 64 ? 1.f : 0.5f + float(b) * 0.0078125f;
+        keys[atomicAdd(&cnt[b], 1)] =
+                (uint64_t(__float_as_uint(edge)) << 32) | uint32_t(k);
+    }
+    __syncwarp();
+}
+
 // Rim phase for the open pixels of an open 8x4 block: folds every fragment
 // of the faces in the block's bin (records staged per warp in shared
 // memory, the next chunk's copy in flight while one is folded), pruned by
@@ -1530,7 +1601,7 @@ template <class Epi>
 static __device__ __forceinline__ void rim_block(const SweepArgs& a, FixedBins b2, int tile,
                                  int w, const int2* state, FaceRec* recs_w,
                                  int* ids_w, unsigned long long* keys_w,
-                                 Epi& epi) {
+                                 int* cnt_w, Epi& epi) {
     const int lane = threadIdx.x & 31;
     const int x = (tile % a.tiles_x) * kTile + (w & 1) * 8 + (lane & 7);
     const int y = (tile / a.tiles_x) * kTile + (w >> 1) * 4 + (lane >> 3);
@@ -1593,7 +1664,8 @@ static __device__ __forceinline__ void rim_block(const SweepArgs& a, FixedBins b
             keys_w[lane] = k;
             __syncwarp();
         } else {
-            warp_sort_smem(keys_w, end);
+            rim_bucket_order(keys_w, end, reinterpret_cast<unsigned long long*>(recs_w),
+                             cnt_w);
         }
     }
     bool done = !open;
@@ -1845,6 +1917,7 @@ __global__ void __launch_bounds__(kTileThreads)
     __shared__ FaceRec recs_sh[8][2 * kRimChunk];
     __shared__ int ids_sh[8][2 * kRimChunk];
     __shared__ unsigned long long keys_sh[8][kRimSort];
+    __shared__ int cnt_sh[8][kRimBuckets];
     const int wc = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_open = *b2.open_n;
     const int n_front = b2.order_n[0], n_back = b2.order_n[1];
@@ -1875,7 +1948,7 @@ __global__ void __launch_bounds__(kTileThreads)
         a.rim = a0.rim + a.v * view_stride_rim;
         if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
         rim_block(a, b2, tile, w, state, recs_sh[wc], ids_sh[wc], keys_sh[wc],
-                  epi);
+                  cnt_sh[wc], epi);
 #if DRESSI_RIM_PREFETCH
         item = __shfl_sync(0xffffffffu, next, 0);
 #endif
