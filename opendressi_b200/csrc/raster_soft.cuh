@@ -1109,31 +1109,43 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
 // is the value at the rectangle's centre plus |gradient| times the half
 // extents (3.5, 1.5); the margin (~80 float ulps of the largest magnitude
 // the products reach over the block) bounds the rounding of this float
-// evaluation and of soft_covers' own.
-__device__ __forceinline__ bool tri_touches_block(const FaceRec& r, int bx,
-                                                  int by) {
-    const float cx = float(bx * 8) + 4.f, cy = float(by * 4) + 2.f;
-    const float ia = fabsf(r.s_inv_area);
-    const float a0 = (r.s1x - cx) * (r.s2y - cy), b0 = (r.s1y - cy) * (r.s2x - cx);
-    const float a1 = (r.s2x - cx) * (r.s0y - cy), b1 = (r.s2y - cy) * (r.s0x - cx);
-    const float l0 = (a0 - b0) * r.s_inv_area;
-    const float l1 = (a1 - b1) * r.s_inv_area;
+// evaluation and of soft_covers' own. TriBlockTest holds the per-face
+// constants (the soft vertices, the gradients' half-extent terms), computed
+// once per face by tri_block_test_of with the same expressions.
+struct TriBlockTest {
+    float s0x, s0y, s1x, s1y, s2x, s2y, inv, ia, e0, e1, e2;
+};
+__device__ __forceinline__ TriBlockTest tri_block_test_of(const FaceRec& r) {
+    TriBlockTest t;
+    t.s0x = r.s0x; t.s0y = r.s0y; t.s1x = r.s1x; t.s1y = r.s1y;
+    t.s2x = r.s2x; t.s2y = r.s2y;
+    t.inv = r.s_inv_area;
+    t.ia = fabsf(r.s_inv_area);
     const float g0x = (r.s1y - r.s2y) * r.s_inv_area;
     const float g0y = (r.s2x - r.s1x) * r.s_inv_area;
     const float g1x = (r.s2y - r.s0y) * r.s_inv_area;
     const float g1y = (r.s0x - r.s2x) * r.s_inv_area;
-    const float e0 = fabsf(g0x) * 3.5f + fabsf(g0y) * 1.5f;
-    const float e1 = fabsf(g1x) * 3.5f + fabsf(g1y) * 1.5f;
-    const float e2 = fabsf(g0x + g1x) * 3.5f + fabsf(g0y + g1y) * 1.5f;
+    t.e0 = fabsf(g0x) * 3.5f + fabsf(g0y) * 1.5f;
+    t.e1 = fabsf(g1x) * 3.5f + fabsf(g1y) * 1.5f;
+    t.e2 = fabsf(g0x + g1x) * 3.5f + fabsf(g0y + g1y) * 1.5f;
+    return t;
+}
+__device__ __forceinline__ bool tri_touches_block(const TriBlockTest& t,
+                                                  int bx, int by) {
+    const float cx = float(bx * 8) + 4.f, cy = float(by * 4) + 2.f;
+    const float a0 = (t.s1x - cx) * (t.s2y - cy), b0 = (t.s1y - cy) * (t.s2x - cx);
+    const float a1 = (t.s2x - cx) * (t.s0y - cy), b1 = (t.s2y - cy) * (t.s0x - cx);
+    const float l0 = (a0 - b0) * t.inv;
+    const float l1 = (a1 - b1) * t.inv;
     // an upper bound of the products' magnitudes at every pixel centre of
     // the block (each factor widened by the half extent)
-    const float u0x = fabsf(r.s0x - cx) + 3.5f, u0y = fabsf(r.s0y - cy) + 1.5f;
-    const float u1x = fabsf(r.s1x - cx) + 3.5f, u1y = fabsf(r.s1y - cy) + 1.5f;
-    const float u2x = fabsf(r.s2x - cx) + 3.5f, u2y = fabsf(r.s2y - cy) + 1.5f;
-    const float mag = (u1x * u2y + u1y * u2x + u2x * u0y + u2y * u0x) * ia;
+    const float u0x = fabsf(t.s0x - cx) + 3.5f, u0y = fabsf(t.s0y - cy) + 1.5f;
+    const float u1x = fabsf(t.s1x - cx) + 3.5f, u1y = fabsf(t.s1y - cy) + 1.5f;
+    const float u2x = fabsf(t.s2x - cx) + 3.5f, u2y = fabsf(t.s2y - cy) + 1.5f;
+    const float mag = (u1x * u2y + u1y * u2x + u2x * u0y + u2y * u0x) * t.ia;
     const float margin = 1e-5f * (1.f + mag);
-    return !(l0 + e0 < -margin || l1 + e1 < -margin ||
-             (1.f - l0 - l1) + e2 < -margin);
+    return !(l0 + t.e0 < -margin || l1 + t.e1 < -margin ||
+             (1.f - l0 - l1) + t.e2 < -margin);
 }
 
 // Summed-area table of the open blocks per 16x16 tile of one view (block
@@ -1261,24 +1273,33 @@ __device__ __forceinline__ void rim_bin_face(int v, int i, int n_faces,
     const int by_lo = r.by0 >> 2, by_hi = r.by1 >> 2;
     const int tx0 = bx_lo >> 1, ty0 = by_lo >> 2;
     const int tx1 = bx_hi >> 1, ty1 = by_hi >> 2;
+    const TriBlockTest tb = tri_block_test_of(r);
     // rounds of 8 x 4 tiles (lane -> tile without integer division)
     for (int oy = ty0; oy <= ty1; oy += 4) {
         for (int ox = tx0; ox <= tx1; ox += 8) {
             // this lane's tile: its open blocks inside the bbox's range
+            // (block k of the tile: column k & 1, row k >> 1)
             const int tx = ox + (lane & 7), ty = oy + (lane >> 3);
             uint32_t m = 0;
             if (tx <= tx1 && ty <= ty1) {
                 const uint2 a8 = *reinterpret_cast<const uint2*>(
                         act + (size_t(ty) * tiles_x + tx) * 8);
-#pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    const uint32_t word = k < 4 ? a8.x : a8.y;
-                    const int bx = tx * 2 + (k & 1), by = ty * 4 + (k >> 1);
-                    if (((word >> (8 * (k & 3))) & 0xffu) != 0u &&
-                        bx >= bx_lo && bx <= bx_hi && by >= by_lo &&
-                        by <= by_hi)
-                        m |= 1u << k;
-                }
+                // the flags are 0 / 1 bytes: gather them into bits 0..7
+                const uint32_t lo = a8.x | (a8.x >> 7) | (a8.x >> 14) |
+                                    (a8.x >> 21);
+                const uint32_t hi = a8.y | (a8.y >> 7) | (a8.y >> 14) |
+                                    (a8.y >> 21);
+                m = (lo & 0xfu) | ((hi & 0xfu) << 4);
+                // columns and rows of the tile inside the block range
+                uint32_t cols = 0xffu;
+                if (tx * 2 < bx_lo) cols &= 0xaau;      // column 0 out
+                if (tx * 2 + 1 > bx_hi) cols &= 0x55u;  // column 1 out
+                const int r0 = imax_(by_lo - ty * 4, 0);
+                const int r1 = imin_(by_hi - ty * 4, 3);
+                const uint32_t rows =
+                        r0 > r1 ? 0u
+                                : ((0xffu << (2 * r0)) & (0xffu >> (6 - 2 * r1)));
+                m &= cols & rows;
             }
             // warp-exclusive scan of the counts, then the compacted list
             const int c = __popc(m);
@@ -1301,7 +1322,7 @@ __device__ __forceinline__ void rim_bin_face(int v, int i, int n_faces,
                 const int l = e >> 3, k = e & 7;
                 const int bx = (ox + (l & 7)) * 2 + (k & 1);
                 const int by = (oy + (l >> 3)) * 4 + (k >> 1);
-                if (!tri_touches_block(r, bx, by)) continue;
+                if (!tri_touches_block(tb, bx, by)) continue;
                 const size_t bin = bin0 + size_t(by) * blocks_x + bx;
                 const int slot = atomicAdd(&b2.cursor[bin], 1);
                 if (slot < b2.cap) {
@@ -1335,10 +1356,15 @@ static __global__ void __launch_bounds__(256)
 }
 
 // The rim work list with the longest lists first: blocks whose bins hold
-// more than kRimSort entries (too long to sort: no early stop) as kRimSplit
-// segments when the open blocks are few, then those above kRimHeavy whole,
-// then the others; within each class the order is arbitrary.
+// more than kRimSplitMin entries as kRimSplit segments when the open blocks
+// are few, then those above kRimHeavy whole, then the others; within each
+// class the order is arbitrary. Open blocks whose bins stayed empty go to
+// the epilogue-only list.
 constexpr int kRimHeavy = 96;
+// lists longer than this are split into segments when the open blocks are
+// few (below kRimSort, which bounds the ordered lists, so that at few views
+// the long lists run on several warps)
+constexpr int kRimSplitMin = 128;
 constexpr int kRimSplit = 4;  // segments of a heavy block (strided entries)
 // Splitting costs work (each segment prunes against its own survivor only)
 // and pays only when the open blocks are too few to fill the machine and
@@ -1362,7 +1388,8 @@ static __global__ void k_rim_order(FixedBins b2, int n_tiles, int tiles_x) {
         if (cnt == 0) {
             // nothing to fold (an empty bin spilled nothing either)
             b2.empty[atomicAdd(&b2.order_n[5], 1)] = e;
-        } else if (n < kRimSplitMaxOpen && cnt > kRimSort && cnt <= b2.cap) {
+        } else if (n < kRimSplitMaxOpen && cnt > kRimSplitMin &&
+                   cnt <= b2.cap) {
             // a list too long to sort (and not spilled): kRimSplit warps
             // fold a strided share each, k_rim_split_epi finishes the block
             const int slot = atomicAdd(&b2.order_n[2], kRimSplit);

@@ -190,7 +190,7 @@ void soft_rim_bins(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
     check_launch();
     // ... and one warp per kept face bins it (a resident grid strides over
     // the kept faces of all views)
-    k_rim_bin<<<148 * 8, 256, 0, s>>>(d.n_faces, d.n_tiles, d.tiles_x,
+    k_rim_bin<<<148 * 4, 256, 0, s>>>(d.n_faces, d.n_tiles, d.tiles_x,
                                       d.views, b.recs, b.active, b.kept,
                                       b.kept_n, b.bin2);
     check_launch();

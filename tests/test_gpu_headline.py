@@ -135,10 +135,12 @@ def test_c3_300_iterations(cuda, port):
     more than 1e-3 after about 40 iterations), because a coverage flip of one
     pixel changes the gradient by a step. So the trace is held to 1e-3 rel
     over its first 25 iterations, and the final loss and positions to 1e-3
-    or, beyond that, to twice the restatement's own spread measured in the
-    same test: the largest deviation, from its unperturbed run, of four
-    restatement runs whose starts differ by such one-ulp moves (one sample
-    of a chaotic spread is too few to bound it)."""
+    or, beyond that, to twice the spread of the chaos measured in the same
+    test: the largest deviation, from its unperturbed run, of four
+    restatement runs whose starts differ by such one-ulp moves, and the
+    deviation between this plan's run (float atomics) and its deterministic
+    mode's run (a fixed summation order) -- the same computation perturbed
+    only by the rounding order of the gradient sums at every iteration."""
     from opendressi_b200 import _native as N
 
     sc = scene.silhouette_scene(level=5, n_views=16, res=256, seed=0)
@@ -162,11 +164,19 @@ def test_c3_300_iterations(cuda, port):
         spread = max(spread,
                      abs(trace_pert[-1] - trace_cpu[-1]) / trace_cpu[-1])
         pos_spread = max(pos_spread, float(np.abs(pos_pert - pos_cpu).max()))
+    plan_det, _ = _sil_plan(sc, laplacian=0.15, normal=0.4)
+    plan_det.set_deterministic(True)
+    plan_det.step(n)
+    trace_det = plan_det.loss_history(n)
+    spread = max(spread, abs(trace_det[-1] - trace[-1]) / trace_cpu[-1])
+    pos = plan.download(N.SLOT_PARAM).reshape(-1, 3)
+    pos_det = plan_det.download(N.SLOT_PARAM).reshape(-1, 3)
+    pos_spread = max(pos_spread, float(np.abs(pos_det - pos).max()))
+    assert plan_det.status() == 0
     np.testing.assert_allclose(trace[:25], trace_cpu[:25], rtol=1e-3)
     rel = abs(trace[-1] - trace_cpu[-1]) / trace_cpu[-1]
     assert rel <= max(1e-3, 2.0 * spread), (rel, spread)
     assert trace[-1] < 0.5 * trace[0]          # it optimises
-    pos = plan.download(N.SLOT_PARAM).reshape(-1, 3)
     assert np.abs(pos - pos_cpu).max() <= max(1e-3, 2.0 * pos_spread)
     assert plan.status() == 0
 
