@@ -94,6 +94,10 @@ def parse():
     ap.add_argument("--deterministic", action="store_true",
                     help="c3: the plan's deterministic gradient mode "
                          "(ordered gathers instead of float atomics)")
+    ap.add_argument("--plain-iterations", type=int, default=0,
+                    help="run this many fused iterations after the set-up "
+                         "and exit without timing or a JSON line (a fixed "
+                         "launch sequence for an external profiler)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
@@ -442,6 +446,14 @@ def run_ours(args):
         plan.render_targets(sc.target_pos)
         param0, n_param = sc.pos0, sc.n_verts * 3
     stream = torch.cuda.current_stream()
+    if args.plain_iterations > 0:
+        torch.cuda.synchronize()
+        for _ in range(args.plain_iterations):
+            plan.step(1)
+        torch.cuda.synchronize()
+        print(f"{args.plain_iterations} iterations, status {plan.status()}")
+        plan.close()
+        return None
 
     # N > 1: phase 0, the NCCL all-reduce and phase 1 captured as one CUDA
     # graph, replayed once per iteration

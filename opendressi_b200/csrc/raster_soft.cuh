@@ -955,6 +955,11 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
         prevs[j] = (ins[j] && peel) ? a.prev[size_t(ys[j]) * a.W + xs[j]] : 0.f;
     }
     const size_t bin = size_t(a.v) * a.n_tiles + tile;
+    const unsigned long long* list = b1.list + bin * b1.cap;
+    // the list's first 32 slots are read together with its count (slots
+    // past the count hold stale entries and are masked below), so the two
+    // loads overlap instead of the list waiting on the count
+    const unsigned long long first = lane < b1.cap ? list[lane] : 0ull;
     const int nent = b1.cursor[bin];
     // overflow: the own list's entries are folded here, the tile is then
     // parked for k_sweep1_spill (spilled entries, or all faces)
@@ -965,14 +970,15 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
         b1.parked[atomicAdd(b1.parked_n, 1)] = int(bin);
     }
     const int end = over ? b1.cap : nent;
-    const unsigned long long* list = b1.list + bin * b1.cap;
     const unsigned lt = (1u << lane) - 1u;
     const uint32_t wmask = ((1u << kSweepPx) - 1u) << (kSweepPx * wq);
 
     // this warp's entries, in list order (first kWarpSort of them)
     int cnt = 0;
     for (int base = 0; base < end; base += 32) {
-        const unsigned long long k = base + lane < end ? list[base + lane] : 0ull;
+        const unsigned long long k =
+                base + lane < end ? (base == 0 ? first : list[base + lane])
+                                  : 0ull;
         const bool mine = (uint32_t(k) & wmask) != 0u;
         const unsigned bal = __ballot_sync(0xffffffffu, mine);
         const int slot = cnt + __popc(bal & lt);
@@ -1644,6 +1650,10 @@ static __device__ __forceinline__ void rim_block(const SweepArgs& a, FixedBins b
     const int by = (tile / a.tiles_x) * 4 + (w >> 1);
     const size_t bin = size_t(a.v) * a.n_tiles * 8 +
                        size_t(by) * (a.tiles_x * 2) + bx;
+    // the list's first 32 slots are read together with its count (slots
+    // past the count are never used)
+    const int* lst = b2.list + bin * b2.cap;
+    const int first = lane < b2.cap ? lst[lane] : 0;
     int n = 0, ns = 0;
     if (lane == 0) {
         n = b2.cursor[bin];
@@ -1659,7 +1669,6 @@ static __device__ __forceinline__ void rim_block(const SweepArgs& a, FixedBins b
         atomicOr(&a.status[1], 2u);  // this iteration: grow the rim bins
     }
     const int end = identity ? a.n_faces : (over ? b2.cap : n);
-    const int* lst = b2.list + bin * b2.cap;
     const float4* src = reinterpret_cast<const float4*>(a.recs);
     // Front-to-back order when the list fits the key buffer: per entry the
     // depth bound of the whole block (rim_depth_lb at the distance from the
@@ -1673,7 +1682,7 @@ static __device__ __forceinline__ void rim_block(const SweepArgs& a, FixedBins b
         const float xlo = float(bx * 8) + 0.5f, xhi = float(bx * 8) + 7.5f;
         const float ylo = float(by * 4) + 0.5f, yhi = float(by * 4) + 3.5f;
         for (int i = lane; i < end; i += 32) {
-            const int f = lst[i];
+            const int f = i < 32 ? first : lst[i];
             const float4 lbq = src[size_t(f) * kRecVec4 + kRecLbVec4];
             const float dx = fmaxf(fmaxf(lbq.x - xhi, xlo - lbq.y), 0.f);
             const float dy = fmaxf(fmaxf(lbq.z - yhi, ylo - lbq.w), 0.f);
