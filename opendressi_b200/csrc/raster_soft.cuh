@@ -539,12 +539,7 @@ static __global__ void k_bin_scan(BinSet b, int n_tiles, uint32_t* status) {
 constexpr int kRecChunk = 64;
 constexpr int kRimCell = 32;     // pixels per side of a rim-flag cell
 constexpr int kRimChunk = 8;     // records per rim staging buffer (2/warp)
-#ifndef DRESSI_RIM_LINE_LB
-#define DRESSI_RIM_LINE_LB 0  // 1: edge-line distance bounds in the rim fold
-#endif
-#ifndef DRESSI_RIM_PREFETCH
-#define DRESSI_RIM_PREFETCH 0  // 1: k_rim takes its next block ahead
-#endif
+
 
 // Fixed-capacity bins filled in one pass: entry i of bin k lives at
 // list[k * cap + i]; the bin's cursor counts every append. Appends past the
@@ -1488,40 +1483,7 @@ __device__ __forceinline__ void rim_fold_chunk(
             const float t = 2.f * s.depth - 1.f + 2.3841858e-7f;
             if (d2 > t * t * r2) continue;  // bound above the survivor
         }
-        bool far = d2 >= r2;  // depth exactly 1
-#if DRESSI_RIM_LINE_LB
-        if (!far && r.orient != 0.f) {
-            // The triangle lies in the inner half-plane of each edge, so the
-            // distance is >= the outward distance to any edge line, -o cr_k
-            // / |e_k|, whose rounding on a kFaceFast face is < 0.001 px
-            // (build_record). In squares: m_k = -o cr_k > 0 and m_k^2 >
-            // |e_k|^2 (0.001 + 1.001 D)^2 give a distance > D.
-            const float crs[3] = {
-                    r.ex0 * (py - r.h0y) - r.ey0 * (px - r.h0x),
-                    r.ex1 * (py - r.h1y) - r.ey1 * (px - r.h1x),
-                    r.ex2 * (py - r.h2y) - r.ey2 * (px - r.h2x)};
-            const float l2s[3] = {r.len2_0, r.len2_1, r.len2_2};
-            const float dr = 0.001f + 1.001f * a.radius;
-            const float kr = dr * dr;
-            float ks = kr;
-            if (s.depth < 1.f) {
-                const float ds = 0.001f + 1.001f * (2.f * s.depth - 1.f +
-                                                    2.3841858e-7f) * a.radius;
-                ks = ds * ds;
-            }
-            bool beyond = false;
-#pragma unroll
-            for (int k = 0; k < 3; k++) {
-                const float m = -r.orient * crs[k];
-                if (m > 0.f) {
-                    const float mm = m * m;
-                    beyond = beyond || mm > l2s[k] * ks;
-                    far = far || mm > l2s[k] * kr;
-                }
-            }
-            if (beyond && s.depth < 1.f) continue;  // above the survivor
-        }
-#endif
+        const bool far = d2 >= r2;  // depth exactly 1
         if (far && f < s.face) continue;  // 1.0 tie, older face
         if (!soft_covers(px, py, r)) continue;
         if (far) {
@@ -1957,22 +1919,11 @@ __global__ void __launch_bounds__(kTileThreads)
     const int wc = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_open = *b2.open_n;
     const int n_front = b2.order_n[0], n_back = b2.order_n[1];
-#if DRESSI_RIM_PREFETCH
-    // the next work item is taken while this one is folded, so the cursor's
-    // round trip leaves the chain of dependent loads of every block
-    int item = 0;
-    if (lane == 0) item = atomicAdd(b2.take, 1);
-    item = __shfl_sync(0xffffffffu, item, 0);
-    while (item < n_front + n_back) {
-        int next = 0;
-        if (lane == 0) next = atomicAdd(b2.take, 1);
-#else
     for (;;) {
         int item = 0;
         if (lane == 0) item = atomicAdd(b2.take, 1);
         item = __shfl_sync(0xffffffffu, item, 0);
         if (item >= n_front + n_back) break;
-#endif
         // the long lists first (the split blocks are not in this list)
         const int e = b2.order[item < n_front ? item
                                               : n_open - 1 - (item - n_front)];
@@ -1985,9 +1936,6 @@ __global__ void __launch_bounds__(kTileThreads)
         if (a0.prev) a.prev = a0.prev + a.v * view_stride_px;
         rim_block(a, b2, tile, w, state, recs_sh[wc], ids_sh[wc], keys_sh[wc],
                   cnt_sh[wc], epi);
-#if DRESSI_RIM_PREFETCH
-        item = __shfl_sync(0xffffffffu, next, 0);
-#endif
     }
 }
 
