@@ -746,6 +746,24 @@ __device__ __forceinline__ unsigned long long warp_sort_asc(
     return k;
 }
 
+// Ascending bitonic sort of one 32-bit key per lane across a full warp.
+__device__ __forceinline__ uint32_t warp_sort_asc32(uint32_t k) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            const uint32_t o = __shfl_xor_sync(0xffffffffu, k, j);
+            const bool up = (lane & size) == 0;
+            const bool lower = (lane & j) == 0;
+            const uint32_t lo = k < o ? k : o;
+            const uint32_t hi = k < o ? o : k;
+            k = (lower == up) ? lo : hi;
+        }
+    }
+    return k;
+}
+
 // Block-wide ascending bitonic sort of n <= kSortMax 64-bit keys in shared
 // memory (padded with ~0).
 __device__ __forceinline__ void block_sort_asc(unsigned long long* k, int n) {
@@ -984,10 +1002,16 @@ static __device__ void sweep1_tile(const SweepArgs& a, FixedBins1 b1,
     // front-to-back order when the warp's list fits the sort buffer
     const bool sorted = !over && cnt <= kWarpSort;
     if (sorted && cnt <= 32) {
-        unsigned long long k = lane < cnt ? keys[lane] : ~0ull;
-        k = warp_sort_asc(k);
+        // sorted as 32-bit keys: the bound's bits with the low five cleared
+        // (non-negative floats order as their bits, and the truncated value
+        // is still a lower bound) over the entry's slot; the entries are
+        // then rewritten in that order with the truncated bound
+        const uint32_t k = warp_sort_asc32(
+                lane < cnt ? ((uint32_t(keys[lane] >> 32) & ~31u) | uint32_t(lane))
+                           : 0xffffffffu);
+        const unsigned long long src = keys[k & 31u];  // lanes >= cnt: unused
         __syncwarp();
-        keys[lane] = k;
+        if (lane < cnt) keys[lane] = (uint64_t(k & ~31u) << 32) | uint32_t(src);
         __syncwarp();
     } else if (sorted) {
         warp_sort_smem(keys, cnt);
@@ -1252,107 +1276,41 @@ static __global__ void k_rim_filter(int n_faces, int n_tiles, int tiles_x,
 }
 
 // Rim-phase binning: a kept face enters the bin of every open 8x4 block its
-// soft triangle may touch. One warp per kept face: in rounds of 8 x 4 tiles
-// of the face's soft bbox, the lanes read the open flags of their tile's
-// eight blocks (one 8-byte word), compact the open blocks inside the bbox
-// into the warp's shared list (blk, 256 entries) and then test and append
-// those, one per lane.
-__device__ __forceinline__ void rim_bin_face(int v, int i, int n_faces,
-                                             int n_tiles, int tiles_x,
-                                             const FaceRec* recs_all,
-                                             const uint8_t* active,
-                                             const int* kept_all,
-                                             const FixedBins& b2,
-                                             uint16_t* blk) {
+// soft triangle may touch. One warp per kept face, lanes striding over the
+// blocks of its soft bbox (the face's test constants in registers).
+static __global__ void k_rim_bin(int n_faces, int n_tiles, int tiles_x,
+                                 const FaceRec* recs_all,
+                                 const uint8_t* active, const int* kept_all,
+                                 const int* kept_n, FixedBins b2) {
+    const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    const int v = blockIdx.y;
+    if (i >= kept_n[v]) return;
     const int f = kept_all[size_t(v) * n_faces + i];
     const FaceRec& r = recs_all[size_t(v) * n_faces + f];
+    const TriBlockTest tb = tri_block_test_of(r);
+    const int bx0 = r.bx0 >> 3, bx1 = r.bx1 >> 3;
+    const int by0 = r.by0 >> 2, by1 = r.by1 >> 2;
     const int blocks_x = tiles_x * 2;
     const uint8_t* act = active + size_t(v) * n_tiles * 8;
     const size_t bin0 = size_t(v) * n_tiles * 8;
-    const int bx_lo = r.bx0 >> 3, bx_hi = r.bx1 >> 3;
-    const int by_lo = r.by0 >> 2, by_hi = r.by1 >> 2;
-    const int tx0 = bx_lo >> 1, ty0 = by_lo >> 2;
-    const int tx1 = bx_hi >> 1, ty1 = by_hi >> 2;
-    const TriBlockTest tb = tri_block_test_of(r);
-    // rounds of 8 x 4 tiles (lane -> tile without integer division)
-    for (int oy = ty0; oy <= ty1; oy += 4) {
-        for (int ox = tx0; ox <= tx1; ox += 8) {
-            // this lane's tile: its open blocks inside the bbox's range
-            // (block k of the tile: column k & 1, row k >> 1)
-            const int tx = ox + (lane & 7), ty = oy + (lane >> 3);
-            uint32_t m = 0;
-            if (tx <= tx1 && ty <= ty1) {
-                const uint2 a8 = *reinterpret_cast<const uint2*>(
-                        act + (size_t(ty) * tiles_x + tx) * 8);
-                // the flags are 0 / 1 bytes: gather them into bits 0..7
-                const uint32_t lo = a8.x | (a8.x >> 7) | (a8.x >> 14) |
-                                    (a8.x >> 21);
-                const uint32_t hi = a8.y | (a8.y >> 7) | (a8.y >> 14) |
-                                    (a8.y >> 21);
-                m = (lo & 0xfu) | ((hi & 0xfu) << 4);
-                // columns and rows of the tile inside the block range
-                uint32_t cols = 0xffu;
-                if (tx * 2 < bx_lo) cols &= 0xaau;      // column 0 out
-                if (tx * 2 + 1 > bx_hi) cols &= 0x55u;  // column 1 out
-                const int r0 = imax_(by_lo - ty * 4, 0);
-                const int r1 = imin_(by_hi - ty * 4, 3);
-                const uint32_t rows =
-                        r0 > r1 ? 0u
-                                : ((0xffu << (2 * r0)) & (0xffu >> (6 - 2 * r1)));
-                m &= cols & rows;
+    // lanes tile the block range 8 wide x 4 tall (no integer division)
+    const int lx = lane & 7, ly = lane >> 3;
+    for (int by = by0 + ly; by <= by1; by += 4) {
+        for (int bx = bx0 + lx; bx <= bx1; bx += 8) {
+            if (!act[((by >> 2) * tiles_x + (bx >> 1)) * 8 + (by & 3) * 2 +
+                     (bx & 1)])
+                continue;
+            if (!tri_touches_block(tb, bx, by)) continue;
+            const size_t bin = bin0 + size_t(by) * blocks_x + bx;
+            const int slot = atomicAdd(&b2.cursor[bin], 1);
+            if (slot < b2.cap) {
+                b2.list[bin * b2.cap + slot] = f;
+            } else {
+                const int sp = atomicAdd(b2.spill_n, 1);
+                if (sp < b2.spill_cap) b2.spill[sp] = make_int2(int(bin), f);
             }
-            // warp-exclusive scan of the counts, then the compacted list
-            const int c = __popc(m);
-            int incl = c;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int n = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += n;
-            }
-            const int total = __shfl_sync(0xffffffffu, incl, 31);
-            int pos = incl - c;
-            while (m) {
-                const int k = __ffs(m) - 1;
-                m &= m - 1u;
-                blk[pos++] = uint16_t((lane << 3) | k);
-            }
-            __syncwarp();
-            for (int j = lane; j < total; j += 32) {
-                const int e = blk[j];
-                const int l = e >> 3, k = e & 7;
-                const int bx = (ox + (l & 7)) * 2 + (k & 1);
-                const int by = (oy + (l >> 3)) * 4 + (k >> 1);
-                if (!tri_touches_block(tb, bx, by)) continue;
-                const size_t bin = bin0 + size_t(by) * blocks_x + bx;
-                const int slot = atomicAdd(&b2.cursor[bin], 1);
-                if (slot < b2.cap) {
-                    b2.list[bin * b2.cap + slot] = f;
-                } else {
-                    const int sp = atomicAdd(b2.spill_n, 1);
-                    if (sp < b2.spill_cap)
-                        b2.spill[sp] = make_int2(int(bin), f);
-                }
-            }
-            __syncwarp();  // blk reuse by the next round
         }
-    }
-}
-
-// A persistent grid (whole warps) strides over the kept faces of every view.
-static __global__ void __launch_bounds__(256)
-        k_rim_bin(int n_faces, int n_tiles, int tiles_x, int views,
-                  const FaceRec* recs_all, const uint8_t* active,
-                  const int* kept_all, const int* kept_n, FixedBins b2) {
-    __shared__ uint16_t sh_blk[8][256];
-    const int wi = threadIdx.x >> 5;
-    const int gw = blockIdx.x * (blockDim.x >> 5) + wi;
-    const int nw = gridDim.x * (blockDim.x >> 5);
-    for (int v = 0; v < views; v++) {
-        const int nk = kept_n[v];
-        for (int i = gw; i < nk; i += nw)
-            rim_bin_face(v, i, n_faces, n_tiles, tiles_x, recs_all, active,
-                         kept_all, b2, sh_blk[wi]);
     }
 }
 

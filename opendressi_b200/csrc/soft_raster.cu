@@ -188,11 +188,10 @@ void soft_rim_bins(const SoftDims& d, const SoftBuffers& b, cudaStream_t s) {
                                     d.tiles_y, b.recs, b.sat, b.kept,
                                     b.kept_n, b.bin2, b.bin1);
     check_launch();
-    // ... and one warp per kept face bins it (a resident grid strides over
-    // the kept faces of all views)
-    k_rim_bin<<<148 * 4, 256, 0, s>>>(d.n_faces, d.n_tiles, d.tiles_x,
-                                      d.views, b.recs, b.active, b.kept,
-                                      b.kept_n, b.bin2);
+    // ... and one warp per kept face bins it (warps past the count exit)
+    const dim3 fg((d.n_faces + 7) / 8, d.views);
+    k_rim_bin<<<fg, 256, 0, s>>>(d.n_faces, d.n_tiles, d.tiles_x, b.recs,
+                                 b.active, b.kept, b.kept_n, b.bin2);
     check_launch();
 }
 
