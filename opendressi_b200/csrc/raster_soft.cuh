@@ -29,7 +29,7 @@
 // sin(theta/2) > kSafeSlope * L, L the largest pixel distance the face's
 // soft bbox reaches from a hard vertex (the rounding error of the edge
 // function is <= ~5u*|e|*L, its exact value outside the margin is >=
-// 2*sin(theta/2)*|e| * (kHardMargin + 1)/2 = 2*sin(theta/2)*|e|);
+// 2*sin(theta/2)*|e| * (kHardMargin + 1)/2 >= 2*sin(theta/2)*|e|);
 // faces failing it, or with huge coordinates, are evaluated exhaustively in
 // sweep 1.
 #pragma once
