@@ -56,7 +56,7 @@ GRAD_NAME = {"c2": "texture", "c3": "position", "c3p": "position",
              "c4": "position",
              "c5": "[albedo | metallic-roughness | environment]"}
 # bytes per view-pixel kept resident between the passes of an iteration
-PX_STATE = {"c2": 24, "c3": 16, "c3p": 16 + 64, "c4": 16, "c5": 92}
+PX_STATE = {"c2": 24, "c3": 16, "c3p": 16 + 64, "c4": 12, "c5": 76}
 
 
 def parse():
@@ -86,11 +86,14 @@ def parse():
     ap.add_argument("--normal", type=float, default=None)
     ap.add_argument("--level", type=int, default=5)
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--path", choices=["plan", "graph"], default="plan",
+    ap.add_argument("--path", choices=["plan", "graph", "eager"],
+                    default="plan",
                     help="plan: the hand-fused plan (default); graph: the "
                          "same workload built with the F:: graph API and run "
                          "by DressiAD (fusion planner + CUDA-graph executor); "
-                         "c1 and c3, one GPU")
+                         "c1 and c3, one GPU; eager: c3p through the eager "
+                         "ops composed with torch autograd (hsr_paper), one "
+                         "GPU")
     ap.add_argument("--deterministic", action="store_true",
                     help="c3: the plan's deterministic gradient mode "
                          "(ordered gathers instead of float atomics)")
@@ -690,6 +693,60 @@ def run_graph(args):
     }
 
 
+def run_eager(args):
+    """C3 on the paper path through the eager ops (opendressi_b200.
+    hsr_paper: this package's CUDA ops composed with torch autograd, a host
+    round trip per op and per step, as the reference's dressi.torch ops are
+    used) -- the cost the fused plan (`--config c3p`) removes. Each step
+    ends with the loss read back (the optimizer's API); the time is the wall
+    clock of `steps` steps after a synchronize."""
+    import time
+
+    import torch
+
+    from opendressi_b200 import _native as N
+    from opendressi_b200 import scene
+    from opendressi_b200.hsr_paper import PaperHsr, PaperSilhouetteOptimizer
+    from opendressi_b200.plans import SilhouettePlan
+
+    if args.config != "c3p" or args.gpus != 1:
+        raise SystemExit("--path eager: config c3p on one GPU")
+    torch.cuda.set_device(0)
+    N.load()
+    sc = scene.silhouette_scene(level=args.level, n_views=args.views,
+                                res=args.res, seed=args.seed)
+    tp = SilhouettePlan.from_scene(sc)
+    tp.upload(N.SLOT_PARAM, sc.pos0)
+    tp.render_targets(sc.target_pos)
+    targets = tp.download(N.SLOT_TARGET).reshape(args.views, args.res,
+                                                 args.res)
+    tp.close()
+    hsr = PaperHsr(sc.faces_f, sc.n_verts, args.res, sc.radius_px,
+                   n_samples=args.samples, peels=args.peels)
+    opt = PaperSilhouetteOptimizer(hsr, sc.pos0, sc.mvps, targets, lr=sc.lr,
+                                   laplacian=args.laplacian,
+                                   normal=args.normal)
+    for _ in range(args.warmup):
+        opt.step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    loss = 0.0
+    for _ in range(args.steps):
+        loss = opt.step()
+    torch.cuda.synchronize()
+    ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    return {
+        "metric": METRIC, "value": 1e3 / ms, "unit": "iterations/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": DATA[args.config],
+        "config": dict(workload(args), path="eager (hsr_paper: the package's "
+                                            "CUDA ops composed with torch "
+                                            "autograd, wall clock)"),
+        "loss_last": loss,
+    }
+
+
 # -------------------------------------------------------- CPU baselines
 
 class PbrCpuSample:
@@ -952,6 +1009,10 @@ def main():
         return
     if args.path == "graph":
         out = run_graph(args)
+        print(json.dumps(out), flush=True)
+        return
+    if args.path == "eager":
+        out = run_eager(args)
         print(json.dumps(out), flush=True)
         return
     out = run_ours(args)
