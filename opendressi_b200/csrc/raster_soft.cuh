@@ -764,31 +764,6 @@ __device__ __forceinline__ uint32_t warp_sort_asc32(uint32_t k) {
     return k;
 }
 
-// Block-wide ascending bitonic sort of n <= kSortMax 64-bit keys in shared
-// memory (padded with ~0).
-__device__ __forceinline__ void block_sort_asc(unsigned long long* k, int n) {
-    int p = 2;
-    while (p < n) p <<= 1;
-    for (int i = n + threadIdx.x; i < p; i += blockDim.x) k[i] = ~0ull;
-    __syncthreads();
-    for (int size = 2; size <= p; size <<= 1) {
-        for (int j = size >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < p; i += blockDim.x) {
-                const int ixj = i ^ j;
-                if (ixj > i) {
-                    const unsigned long long a = k[i], b = k[ixj];
-                    const bool up = (i & size) == 0;
-                    if (up ? a > b : a < b) {
-                        k[i] = b;
-                        k[ixj] = a;
-                    }
-                }
-            }
-            __syncthreads();
-        }
-    }
-}
-
 // Folds the spilled entries of an overflowed sweep-1 bin (gathered from the
 // spill list blockDim at a time) into the pixel's survivor -- or, when the
 // spill list itself overflowed (all_faces), every face. Faces already folded
